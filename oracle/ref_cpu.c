@@ -1,0 +1,652 @@
+/*
+ * ref_cpu.c -- CPU oracle for the jax4j FP32 hot path (test infrastructure).
+ *
+ * A plain-C restatement of the reference's pure-Java host implementation.
+ * Used only as the checker by tests/, __graft_entry__.smoke() and the CPU
+ * baseline leg of bench.py; never linked into or called by the product.
+ * Build with -O2 -ffp-contract=off -fno-fast-math (see oracle/build.py):
+ * Java evaluates float expressions without fused multiply-add.
+ *
+ * Citations are file:line in marmanis/jax4j, relative to
+ * src/main/java/com/marmanis/jax4j/.
+ */
+#include "ref_cpu.h"
+
+#include <math.h>
+#include <pthread.h>
+#include <stdlib.h>
+#include <string.h>
+
+/* ------------------------------------------------------------------ */
+/* Random.java:39-150 (SplitMix64 streams)                             */
+/* ------------------------------------------------------------------ */
+#define GOLDEN_GAMMA 0x9E3779B97F4A7C15ULL
+#define SPLIT_TAG 0xD1B54A32D192ED03ULL
+#define SAMPLE_TAG 0x2545F4914F6CDD1DULL
+
+/* api/Random.java:44-48 */
+uint64_t orc_mix64(uint64_t z) {
+    z = (z ^ (z >> 30)) * 0xbf58476d1ce4e5b9ULL;
+    z = (z ^ (z >> 27)) * 0x94d049bb133111ebULL;
+    return z ^ (z >> 31);
+}
+
+/* api/Random.java:56-58 */
+static uint64_t stream_value(uint64_t state, uint64_t tag, uint64_t index) {
+    return orc_mix64(state ^ tag ^ (GOLDEN_GAMMA * (index + 1)));
+}
+
+/* api/Random.java:61-65: top 24 bits / 2^24, an exact float division */
+static float raw_uniform01(uint64_t state, uint64_t i) {
+    uint64_t bits = stream_value(state, SAMPLE_TAG, i);
+    int32_t top24 = (int32_t)(bits >> 40);
+    return (float)top24 / (float)(1 << 24);
+}
+
+/* api/Random.java:70-76 */
+void orc_split(uint64_t state, int num, uint64_t *out) {
+    for (int i = 0; i < num; i++)
+        out[i] = orc_mix64(state ^ SPLIT_TAG ^ (GOLDEN_GAMMA * (uint64_t)(i + 1)));
+}
+
+/* api/Random.java:86-93: lo + u * (hi - lo), each step rounded to float */
+void orc_uniform(uint64_t state, int64_t n, float lo, float hi, float *out) {
+    float span = hi - lo;
+    for (int64_t i = 0; i < n; i++) {
+        float u = raw_uniform01(state, (uint64_t)i);
+        float scaled = u * span;
+        out[i] = lo + scaled;
+    }
+}
+
+/* api/Random.java:104-113: Box-Muller in double, narrowed to float */
+void orc_normal(uint64_t state, int64_t n, float *out) {
+    const double two_pi = 2.0 * 3.141592653589793;
+    for (int64_t i = 0; i < n; i++) {
+        float u1 = raw_uniform01(state, 2ULL * (uint64_t)i);
+        if (!(u1 >= 1e-7f)) u1 = 1e-7f; /* Math.max(u1, 1e-7f); u1 is never NaN */
+        float u2 = raw_uniform01(state, 2ULL * (uint64_t)i + 1ULL);
+        out[i] = (float)(sqrt(-2.0 * log((double)u1)) * cos(two_pi * (double)u2));
+    }
+}
+
+/* api/Random.java:147-150 */
+void orc_glorot_uniform(uint64_t state, int64_t n, int fan_in, int fan_out, float *out) {
+    float limit = (float)sqrt(6.0 / (double)(fan_in + fan_out));
+    orc_uniform(state, n, -limit, limit, out);
+}
+
+/* ------------------------------------------------------------------ */
+/* Shape.java:37-101                                                   */
+/* ------------------------------------------------------------------ */
+static int64_t shape_size(const int64_t *d, int r) {
+    int64_t s = 1;
+    for (int i = 0; i < r; i++) s *= d[i];
+    return s;
+}
+
+static int shape_equal(const int64_t *a, int ar, const int64_t *b, int br) {
+    if (ar != br) return 0;
+    for (int i = 0; i < ar; i++)
+        if (a[i] != b[i]) return 0;
+    return 1;
+}
+
+/* core/Shape.java:83-101 */
+int64_t orc_broadcast_index(const int64_t *dims, int rank, const int64_t *out_dims, int out_rank,
+                            int64_t flat) {
+    if (shape_equal(dims, rank, out_dims, out_rank)) return flat;
+    int64_t coords[16];
+    int64_t rem = flat;
+    for (int i = out_rank - 1; i >= 0; i--) {
+        coords[i] = rem % out_dims[i];
+        rem /= out_dims[i];
+    }
+    int offset = out_rank - rank;
+    int64_t f = 0;
+    for (int i = 0; i < rank; i++) {
+        int64_t dim = dims[i];
+        int64_t c = dim == 1 ? 0 : coords[i + offset];
+        f = f * dim + c;
+    }
+    return f;
+}
+
+/* ------------------------------------------------------------------ */
+/* java.lang.Math.max/min(double,double): NaN wins, max(-0,+0) = +0     */
+/* ------------------------------------------------------------------ */
+static double java_max(double a, double b) {
+    if (a != a) return a;
+    if (a == 0.0 && b == 0.0 && signbit(a)) return b;
+    return (a >= b) ? a : b;
+}
+
+static double java_min(double a, double b) {
+    if (a != a) return a;
+    if (a == 0.0 && b == 0.0 && signbit(b)) return b;
+    return (a <= b) ? a : b;
+}
+
+static double binary_op(int prim, double a, double b) {
+    switch (prim) {
+    case ORC_ADD: return a + b;
+    case ORC_SUB: return a - b;
+    case ORC_MUL: return a * b;
+    case ORC_DIV: return a / b;
+    case ORC_MAX: return java_max(a, b);
+    case ORC_MIN: return java_min(a, b);
+    default: return NAN;
+    }
+}
+
+/* core/ConcreteNDArray.java:274-292: op in double, narrowed to float */
+int orc_binary_f32(int prim, const float *a, const int64_t *ad, int ar, const float *b,
+                   const int64_t *bd, int br, float *out, const int64_t *od, int orank) {
+    if (prim != ORC_ADD && prim != ORC_SUB && prim != ORC_MUL && prim != ORC_DIV &&
+        prim != ORC_MAX && prim != ORC_MIN)
+        return -1;
+    int64_t n = shape_size(od, orank);
+    for (int64_t i = 0; i < n; i++) {
+        float v1 = a[orc_broadcast_index(ad, ar, od, orank, i)];
+        float v2 = b[orc_broadcast_index(bd, br, od, orank, i)];
+        out[i] = (float)binary_op(prim, (double)v1, (double)v2);
+    }
+    return 0;
+}
+
+static int compare_d(int prim, double a, double b) {
+    switch (prim) {
+    case ORC_GT: return a > b;
+    case ORC_GE: return a >= b;
+    case ORC_LT: return a < b;
+    case ORC_LE: return a <= b;
+    case ORC_EQ: return a == b;
+    case ORC_NE: return a != b;
+    default: return 0;
+    }
+}
+
+static int compare_l(int prim, int64_t a, int64_t b) {
+    switch (prim) {
+    case ORC_GT: return a > b;
+    case ORC_GE: return a >= b;
+    case ORC_LT: return a < b;
+    case ORC_LE: return a <= b;
+    case ORC_EQ: return a == b;
+    case ORC_NE: return a != b;
+    default: return 0;
+    }
+}
+
+/* core/ConcreteNDArray.java:343-396: F32/F64/I32 compare as double, I64 as long */
+int orc_compare(int prim, int dtype, const void *a, const int64_t *ad, int ar, const void *b,
+                const int64_t *bd, int br, uint8_t *out, const int64_t *od, int orank) {
+    if (prim < ORC_GT || prim > ORC_NE) return -1;
+    int64_t n = shape_size(od, orank);
+    for (int64_t i = 0; i < n; i++) {
+        int64_t ia = orc_broadcast_index(ad, ar, od, orank, i);
+        int64_t ib = orc_broadcast_index(bd, br, od, orank, i);
+        int r;
+        switch (dtype) {
+        case ORC_F32: r = compare_d(prim, ((const float *)a)[ia], ((const float *)b)[ib]); break;
+        case ORC_F64: r = compare_d(prim, ((const double *)a)[ia], ((const double *)b)[ib]); break;
+        case ORC_I32: r = compare_d(prim, ((const int32_t *)a)[ia], ((const int32_t *)b)[ib]); break;
+        case ORC_I64: r = compare_l(prim, ((const int64_t *)a)[ia], ((const int64_t *)b)[ib]); break;
+        default: return -1; /* BOOL is not comparable (ConcreteNDArray.java:393-394) */
+        }
+        out[i] = (uint8_t)r;
+    }
+    return 0;
+}
+
+/* core/ConcreteNDArray.java:648-664: (float) Math.f((double) x) */
+int orc_unary_f32(int prim, const float *in, int64_t n, float *out) {
+    for (int64_t i = 0; i < n; i++) {
+        double x = (double)in[i];
+        double r;
+        switch (prim) {
+        case ORC_EXP: r = exp(x); break;
+        case ORC_LOG: r = log(x); break;
+        case ORC_SIN: r = sin(x); break;
+        case ORC_COS: r = cos(x); break;
+        case ORC_TANH: r = tanh(x); break;
+        case ORC_RELU: r = java_max(0.0, x); break;
+        case ORC_SIGMOID: r = 1.0 / (1.0 + exp(-x)); break;
+        default: return -1;
+        }
+        out[i] = (float)r;
+    }
+    return 0;
+}
+
+/* JLS 5.1.3 narrowing of a floating value to int/long: NaN -> 0,
+ * out-of-range values saturate, otherwise truncation toward zero. */
+static int32_t java_d2i(double v) {
+    if (v != v) return 0;
+    if (v >= 2147483647.0) return INT32_MAX;
+    if (v <= -2147483648.0) return INT32_MIN;
+    return (int32_t)v;
+}
+
+static int64_t java_d2l(double v) {
+    if (v != v) return 0;
+    if (v >= 9223372036854775807.0) return INT64_MAX;
+    if (v <= -9223372036854775808.0) return INT64_MIN;
+    return (int64_t)v;
+}
+
+/* core/ConcreteNDArray.java:666-730 */
+int orc_cast(int src, int dst, const void *in, int64_t n, void *out) {
+    for (int64_t i = 0; i < n; i++) {
+        double dv = 0;
+        int64_t lv = 0;
+        int is_long = 0, truth = 0;
+        switch (src) {
+        case ORC_F32: dv = ((const float *)in)[i]; truth = ((const float *)in)[i] != 0.0f; break;
+        case ORC_F64: dv = ((const double *)in)[i]; truth = ((const double *)in)[i] != 0.0; break;
+        case ORC_I32: lv = ((const int32_t *)in)[i]; is_long = 1; truth = lv != 0; break;
+        case ORC_I64: lv = ((const int64_t *)in)[i]; is_long = 1; truth = lv != 0; break;
+        case ORC_BOOL: lv = ((const uint8_t *)in)[i] ? 1 : 0; is_long = 1; truth = lv != 0; break;
+        default: return -1;
+        }
+        switch (dst) {
+        case ORC_F32:
+            if (src == ORC_F32) ((float *)out)[i] = ((const float *)in)[i];
+            else if (is_long) ((float *)out)[i] = (float)lv; /* round to nearest */
+            else ((float *)out)[i] = (float)dv;
+            break;
+        case ORC_F64:
+            ((double *)out)[i] = is_long ? (double)lv : dv;
+            break;
+        case ORC_I32:
+            if (is_long) ((int32_t *)out)[i] = (int32_t)(uint32_t)(uint64_t)lv; /* narrows */
+            else ((int32_t *)out)[i] = java_d2i(dv);
+            break;
+        case ORC_I64:
+            ((int64_t *)out)[i] = is_long ? lv : java_d2l(dv);
+            break;
+        case ORC_BOOL:
+            ((uint8_t *)out)[i] = (uint8_t)truth;
+            break;
+        default: return -1;
+        }
+    }
+    return 0;
+}
+
+/* backend/HostBackend.java:117-124: sequential float sum from 0f; mean divides by (float) n */
+void orc_reduce_all_f32(int prim, const float *in, int64_t n, float *out) {
+    float sum = 0.0f;
+    for (int64_t i = 0; i < n; i++) sum += in[i];
+    if (prim == ORC_MEAN) sum = sum / (float)n;
+    out[0] = sum;
+}
+
+/* core/ConcreteNDArray.java:536-547 */
+void orc_reduce_axis_f32(int prim, const float *in, int64_t outer, int64_t axis, int64_t inner,
+                         float *out) {
+    for (int64_t o = 0; o < outer; o++) {
+        for (int64_t r = 0; r < inner; r++) {
+            float total = 0.0f;
+            for (int64_t a = 0; a < axis; a++) total += in[o * axis * inner + a * inner + r];
+            out[o * inner + r] = prim == ORC_MEAN_AXIS ? total / (float)axis : total;
+        }
+    }
+}
+
+/* core/ConcreteNDArray.java:602-617: first strict extremum wins */
+void orc_argreduce_f32(int prim, const float *in, int64_t outer, int64_t axis, int64_t inner,
+                       int32_t *out) {
+    int is_max = prim == ORC_ARGMAX;
+    for (int64_t o = 0; o < outer; o++) {
+        for (int64_t r = 0; r < inner; r++) {
+            int32_t best_idx = 0;
+            float best = in[o * axis * inner + r];
+            for (int64_t a = 1; a < axis; a++) {
+                float v = in[o * axis * inner + a * inner + r];
+                if (is_max ? v > best : v < best) {
+                    best = v;
+                    best_idx = (int32_t)a;
+                }
+            }
+            out[o * inner + r] = best_idx;
+        }
+    }
+}
+
+/* ------------------------------------------------------------------ */
+/* dot: core/ConcreteNDArray.java:452-459, backend/HostBackend.java:56-66 */
+/* For every (i, j) the k-sum is the same sequential float sum from 0f.  */
+/* The loops run i-k-j so the j lanes vectorise; each c[i][j] still sees  */
+/* its products in k order, so the result is bit-identical to i-j-k.     */
+/* ------------------------------------------------------------------ */
+typedef struct {
+    const float *a, *b;
+    float *c;
+    int64_t K, N, r0, r1;
+} dot_job;
+
+static void *dot_rows(void *arg) {
+    dot_job *j = (dot_job *)arg;
+    for (int64_t i = j->r0; i < j->r1; i++) {
+        float *crow = j->c + i * j->N;
+        for (int64_t n = 0; n < j->N; n++) crow[n] = 0.0f;
+        const float *arow = j->a + i * j->K;
+        for (int64_t k = 0; k < j->K; k++) {
+            float av = arow[k];
+            const float *brow = j->b + k * j->N;
+            for (int64_t n = 0; n < j->N; n++) {
+                float p = av * brow[n];
+                crow[n] = crow[n] + p;
+            }
+        }
+    }
+    return NULL;
+}
+
+void orc_dot_f32(const float *a, const float *b, float *c, int64_t M, int64_t K, int64_t N,
+                 int64_t row_begin, int64_t row_end, int threads) {
+    (void)M;
+    if (threads < 1) threads = 1;
+    int64_t rows = row_end - row_begin;
+    if (rows <= 0) return;
+    if (threads > rows) threads = (int)rows;
+    pthread_t tid[256];
+    dot_job jobs[256];
+    if (threads > 256) threads = 256;
+    int64_t per = (rows + threads - 1) / threads;
+    int started = 0;
+    for (int t = 0; t < threads; t++) {
+        int64_t r0 = row_begin + t * per;
+        int64_t r1 = r0 + per > row_end ? row_end : r0 + per;
+        if (r0 >= r1) break;
+        jobs[t].a = a; jobs[t].b = b; jobs[t].c = c;
+        jobs[t].K = K; jobs[t].N = N; jobs[t].r0 = r0; jobs[t].r1 = r1;
+        if (threads == 1) {
+            dot_rows(&jobs[t]);
+        } else {
+            pthread_create(&tid[t], NULL, dot_rows, &jobs[t]);
+            started++;
+        }
+    }
+    for (int t = 0; t < started; t++) pthread_join(tid[t], NULL);
+}
+
+/* ------------------------------------------------------------------ */
+/* Grad.java host helpers                                              */
+/* ------------------------------------------------------------------ */
+
+/* api/Grad.java:562-581 (FLOAT32 branch of broadcastLike) */
+void orc_broadcast_like_f32(const float *g, const int64_t *gd, int gr, float *out,
+                            const int64_t *td, int tr) {
+    int64_t gs = shape_size(gd, gr), ts = shape_size(td, tr);
+    if (gs == ts) { /* equal shapes or a pure reshape */
+        memcpy(out, g, (size_t)gs * sizeof(float));
+        return;
+    }
+    if (gs < ts) {
+        for (int64_t i = 0; i < ts; i++) out[i] = g[orc_broadcast_index(gd, gr, td, tr, i)];
+    } else {
+        for (int64_t i = 0; i < ts; i++) out[i] = 0.0f;
+        for (int64_t i = 0; i < gs; i++) out[orc_broadcast_index(td, tr, gd, gr, i)] += g[i];
+    }
+}
+
+/* api/Grad.java:593-597 */
+void orc_relu_grad_f32(const float *g, const float *x, int64_t n, float *out) {
+    for (int64_t i = 0; i < n; i++) out[i] = x[i] > 0 ? g[i] : 0.0f;
+}
+
+/* api/Grad.java:630-640 */
+void orc_axis_broadcast_like_f32(const float *g, const int64_t *dims, int rank, int axis,
+                                 float *out) {
+    int64_t axis_size = dims[axis], outer = 1, inner = 1;
+    for (int i = 0; i < axis; i++) outer *= dims[i];
+    for (int i = axis + 1; i < rank; i++) inner *= dims[i];
+    for (int64_t o = 0; o < outer; o++)
+        for (int64_t r = 0; r < inner; r++) {
+            float v = g[o * inner + r];
+            for (int64_t a = 0; a < axis_size; a++) out[o * axis_size * inner + a * inner + r] = v;
+        }
+}
+
+/* api/Grad.java:656-663 */
+void orc_transpose_f32(const float *in, int64_t rows, int64_t cols, float *out) {
+    for (int64_t i = 0; i < rows; i++)
+        for (int64_t j = 0; j < cols; j++) out[j * rows + i] = in[i * cols + j];
+}
+
+/* api/Grad.java:517-527: a wins ties; gA/gB are full output-shaped arrays
+ * (the caller applies broadcastLike to each, Grad.java:528-529) */
+void orc_maxmin_grad_f32(int is_max, const float *g, const int64_t *od, int orank, const float *a,
+                         const int64_t *ad, int ar, const float *b, const int64_t *bd, int br,
+                         float *ga_full, float *gb_full) {
+    int64_t n = shape_size(od, orank);
+    for (int64_t i = 0; i < n; i++) {
+        float va = a[orc_broadcast_index(ad, ar, od, orank, i)];
+        float vb = b[orc_broadcast_index(bd, br, od, orank, i)];
+        int a_wins = is_max ? va >= vb : va <= vb;
+        ga_full[i] = a_wins ? g[i] : 0.0f;
+        gb_full[i] = a_wins ? 0.0f : g[i];
+    }
+}
+
+/* api/SharedCollective.java:44-54: every shard sums slots d = 0..D-1 from 0f */
+void orc_psum_f32(const float *const *slots, int num_devices, int64_t n, float *out) {
+    for (int64_t i = 0; i < n; i++) out[i] = 0.0f;
+    for (int d = 0; d < num_devices; d++)
+        for (int64_t i = 0; i < n; i++) out[i] += slots[d][i];
+}
+
+/* ------------------------------------------------------------------ */
+/* MLP cross-entropy loss and its gradTree, in the order the Grad       */
+/* interpreter executes the traced equations of                          */
+/* examples/MNISTFromScratch.java:103-125 (predict + loss):              */
+/*   h = a.dot(w); z = h.add(b); a' = act(z)   (hidden layers)           */
+/*   e = exp(z_L); s = e.sum(-1, true); p = e.div(s); lp = p.log()        */
+/*   m = lp.mul(t); r = m.sum(-1); mu = r.mean(); L = mu.mul([-1])        */
+/* Backward follows Grad.computeVJPs (Grad.java:341-472) rule by rule.    */
+/* ------------------------------------------------------------------ */
+typedef struct {
+    int L;
+    int64_t B, C;
+    float **h;  /* pre-bias dot outputs (not needed after bias add) */
+    float **z;  /* z[l] = h[l] + b[l] */
+    float **a;  /* a[0] = x, a[l+1] = act(z[l]) */
+    float *e, *s, *p, *lp, *m, *r;
+    float mu, loss;
+} mlp_fwd;
+
+static float *fbuf(int64_t n) { return (float *)malloc((size_t)(n > 0 ? n : 1) * sizeof(float)); }
+
+/* z = h + b with b of shape [cols] broadcast over rows (ConcreteNDArray.java:286-290) */
+static void add_row_bias(const float *h, const float *b, int64_t rows, int64_t cols, float *z) {
+    for (int64_t i = 0; i < rows; i++)
+        for (int64_t j = 0; j < cols; j++)
+            z[i * cols + j] = (float)((double)h[i * cols + j] + (double)b[j]);
+}
+
+static void mlp_forward(mlp_fwd *f, int L, const int64_t *dims, int act, const float *const *w,
+                        const float *const *b, const float *x, const float *t, int64_t B,
+                        int threads) {
+    f->L = L;
+    f->B = B;
+    f->C = dims[L];
+    f->h = (float **)calloc((size_t)L, sizeof(float *));
+    f->z = (float **)calloc((size_t)L, sizeof(float *));
+    f->a = (float **)calloc((size_t)L + 1, sizeof(float *));
+    f->a[0] = (float *)x;
+    for (int l = 0; l < L; l++) {
+        int64_t din = dims[l], dout = dims[l + 1];
+        f->h[l] = fbuf(B * dout);
+        orc_dot_f32(f->a[l], w[l], f->h[l], B, din, dout, 0, B, threads);
+        f->z[l] = fbuf(B * dout);
+        add_row_bias(f->h[l], b[l], B, dout, f->z[l]);
+        free(f->h[l]);
+        f->h[l] = NULL;
+        if (l < L - 1) {
+            f->a[l + 1] = fbuf(B * dout);
+            orc_unary_f32(act == 0 ? ORC_TANH : ORC_RELU, f->z[l], B * dout, f->a[l + 1]);
+        }
+    }
+    int64_t C = f->C, n = B * C;
+    f->e = fbuf(n);
+    orc_unary_f32(ORC_EXP, f->z[L - 1], n, f->e);
+    f->s = fbuf(B);
+    orc_reduce_axis_f32(ORC_SUM_AXIS, f->e, B, C, 1, f->s);
+    f->p = fbuf(n);
+    for (int64_t i = 0; i < B; i++)
+        for (int64_t j = 0; j < C; j++) f->p[i * C + j] = f->e[i * C + j] / f->s[i];
+    f->lp = fbuf(n);
+    orc_unary_f32(ORC_LOG, f->p, n, f->lp);
+    f->m = fbuf(n);
+    for (int64_t i = 0; i < n; i++) f->m[i] = f->lp[i] * t[i];
+    f->r = fbuf(B);
+    orc_reduce_axis_f32(ORC_SUM_AXIS, f->m, B, C, 1, f->r);
+    orc_reduce_all_f32(ORC_MEAN, f->r, B, &f->mu);
+    f->loss = f->mu * -1.0f;
+}
+
+static void mlp_free(mlp_fwd *f) {
+    for (int l = 0; l < f->L; l++) {
+        free(f->z[l]);
+        if (l + 1 < f->L) free(f->a[l + 1]);
+    }
+    free(f->h); free(f->z); free(f->a);
+    free(f->e); free(f->s); free(f->p); free(f->lp); free(f->m); free(f->r);
+}
+
+int orc_mlp_loss_f32(int num_layers, const int64_t *dims, int act, const float *const *w,
+                     const float *const *b, const float *x, const float *onehot, int64_t batch,
+                     float *loss, int threads) {
+    mlp_fwd f;
+    mlp_forward(&f, num_layers, dims, act, w, b, x, onehot, batch, threads);
+    *loss = f.loss;
+    mlp_free(&f);
+    return 0;
+}
+
+int orc_mlp_loss_grad_f32(int num_layers, const int64_t *dims, int act, const float *const *w,
+                          const float *const *b, const float *x, const float *onehot,
+                          int64_t batch, float *loss, float *const *gw, float *const *gb,
+                          float *gx, int threads) {
+    int L = num_layers;
+    int64_t B = batch;
+    mlp_fwd f;
+    mlp_forward(&f, L, dims, act, w, b, x, onehot, B, threads);
+    *loss = f.loss;
+    int64_t C = f.C, n = B * C;
+
+    /* L = mu * [-1]: MUL VJP (Grad.java:345) with seed ones([1]) */
+    float g_mu = 1.0f * -1.0f;
+    /* MEAN VJP (Grad.java:354-358): g / (float) n, broadcast to [B] */
+    float g_r_val = g_mu / (float)B;
+    /* SUM_AXIS VJP (Grad.java:360-363): broadcast over the class axis;
+     * MUL VJP (Grad.java:345): g_lp = g_m * t; LOG VJP (Grad.java:371): g_p = g_lp / p */
+    float *g_p = fbuf(n);
+    for (int64_t i = 0; i < n; i++) {
+        float g_lp = g_r_val * onehot[i];
+        g_p[i] = g_lp / f.p[i];
+    }
+    /* DIV VJP (Grad.java:346-353) for p = e / s */
+    float *g_e = fbuf(n);
+    float *g_s = fbuf(B);
+    for (int64_t i = 0; i < B; i++) g_s[i] = 0.0f;
+    for (int64_t i = 0; i < B; i++)
+        for (int64_t j = 0; j < C; j++) {
+            int64_t k = i * C + j;
+            float s = f.s[i];
+            g_e[k] = g_p[k] / s;
+            float gb_ = g_p[k] * f.e[k];
+            gb_ = gb_ / s;
+            gb_ = gb_ / s;
+            gb_ = gb_ * -1.0f;
+            g_s[i] += gb_; /* broadcastLike sum-down, flat order (Grad.java:577-579) */
+        }
+    /* SUM_AXIS(e, keepDims) VJP merged into g_e by add (Grad.java:157, 180) */
+    for (int64_t i = 0; i < B; i++)
+        for (int64_t j = 0; j < C; j++) g_e[i * C + j] = g_e[i * C + j] + g_s[i];
+    /* EXP VJP (Grad.java:370): g * exp(z) with exp recomputed */
+    float *g_z = fbuf(n);
+    {
+        float *ez = fbuf(n);
+        orc_unary_f32(ORC_EXP, f.z[L - 1], n, ez);
+        for (int64_t i = 0; i < n; i++) g_z[i] = g_e[i] * ez[i];
+        free(ez);
+    }
+    free(g_p); free(g_e); free(g_s);
+
+    for (int l = L - 1; l >= 0; l--) {
+        int64_t din = dims[l], dout = dims[l + 1];
+        /* ADD VJP with bias broadcast: column sum-down in flat order (Grad.java:343, 577-579) */
+        for (int64_t j = 0; j < dout; j++) gb[l][j] = 0.0f;
+        for (int64_t i = 0; i < B; i++)
+            for (int64_t j = 0; j < dout; j++) gb[l][j] += g_z[i * dout + j];
+        /* DOT VJP (Grad.java:385-390): dW = transpose(a) . g, dA = g . transpose(W) */
+        float *aT = fbuf(din * B);
+        orc_transpose_f32(f.a[l], B, din, aT);
+        orc_dot_f32(aT, g_z, gw[l], din, B, dout, 0, din, threads);
+        free(aT);
+        if (l == 0 && !gx) break; /* x is a constant here: its cotangent is never read */
+        float *wT = fbuf(dout * din);
+        orc_transpose_f32(w[l], din, dout, wT);
+        float *g_a = l == 0 ? gx : fbuf(B * din);
+        orc_dot_f32(g_z, wT, g_a, B, dout, din, 0, B, threads);
+        free(wT);
+        if (l == 0) break;
+        free(g_z);
+        g_z = fbuf(B * din);
+        const float *zin = f.z[l - 1];
+        if (act == 0) {
+            /* TANH VJP (Grad.java:374-378): g * (1 - t*t), t recomputed */
+            for (int64_t i = 0; i < B * din; i++) {
+                float t = (float)tanh((double)zin[i]);
+                float tt = t * t;
+                float one_m = 1.0f - tt;
+                g_z[i] = g_a[i] * one_m;
+            }
+        } else {
+            orc_relu_grad_f32(g_a, zin, B * din, g_z); /* Grad.java:585-598 */
+        }
+        free(g_a);
+    }
+    free(g_z);
+    mlp_free(&f);
+    return 0;
+}
+
+/* ------------------------------------------------------------------ */
+/* Elementwise sweep: z = where(x.gt(0), tanh(x)*sigmoid(y),             */
+/* relu(y).clip(-1, 1)); z.sum(-1, true); z.argmax(-1).                  */
+/* where = c*x + (1-c)*y with c = BOOL->FLOAT32 (api/Numpy.java:39-44);   */
+/* clip = max(lo).min(hi) (core/NDArray.java:82).                         */
+/* ------------------------------------------------------------------ */
+void orc_sweep_f32(const float *x, const float *y, int64_t rows, int64_t cols, float *z,
+                   float *row_sum, int32_t *row_argmax) {
+    for (int64_t i = 0; i < rows; i++) {
+        float total = 0.0f;
+        int32_t best_idx = 0;
+        float best = 0.0f;
+        for (int64_t j = 0; j < cols; j++) {
+            int64_t k = i * cols + j;
+            float xv = x[k], yv = y[k];
+            float c = ((double)xv > 0.0) ? 1.0f : 0.0f;
+            float t = (float)tanh((double)xv);
+            float s = (float)(1.0 / (1.0 + exp(-(double)yv)));
+            float ts = t * s;
+            float r = (float)java_max(0.0, (double)yv);
+            float cl = (float)java_max((double)r, -1.0);
+            cl = (float)java_min((double)cl, 1.0);
+            float inv = 1.0f - c;
+            float zv = c * ts + inv * cl;
+            if (z) z[k] = zv;
+            total += zv;
+            if (j == 0 || zv > best) { /* ConcreteNDArray.java:606-613 */
+                best = zv;
+                best_idx = (int32_t)j;
+            }
+        }
+        row_sum[i] = total;
+        row_argmax[i] = best_idx;
+    }
+}
