@@ -1,0 +1,305 @@
+/*
+ * jax4j_cuda.h -- C ABI of libjax4j_cuda.so, the B200 (sm_100a) execution
+ * backend for jax4j.
+ *
+ * This header is the drop-in boundary.  Each entry point replaces one method
+ * of the reference's operator SPI (backend/ExecutionBackend.java), of its
+ * host array core (core/ConcreteNDArray.java), of the Grad interpreter's host
+ * helpers (api/Grad.java) or of its in-process collective
+ * (api/SharedCollective.java); the comment above each declaration cites the
+ * reference method it replaces (paths relative to
+ * src/main/java/com/marmanis/jax4j/).
+ *
+ * Conventions
+ *  - Plain pointers and sizes only.  Device pointers live on the calling
+ *    thread's current CUDA device (j4c_set_device); host pointers are
+ *    ordinary (preferably pinned) memory.
+ *  - Every function returns an int status: J4C_OK (0) or a J4C_E_* code.  The
+ *    calling thread's last error message is available from j4c_last_error().
+ *    No exception crosses the ABI and there is no host fallback: a request
+ *    the device path cannot serve fails with J4C_E_UNSUPPORTED.
+ *  - Work is enqueued on the given stream (a cudaStream_t; NULL = the legacy
+ *    default stream) and is asynchronous unless stated otherwise.
+ *  - Inputs are never modified; outputs are caller-allocated and must not
+ *    alias inputs unless stated.  The caller owns every buffer.
+ *  - prim is the ordinal of ir/Primitive.java and dtype the ordinal of
+ *    core/DType.java, so a Java caller passes Enum.ordinal() unchanged.
+ *  - Shapes are row-major int64 dimension arrays (dims, rank); rank 0 means
+ *    one element.  Broadcasting follows core/Shape.java:37-49 (align right,
+ *    size-1 dimensions stretch).
+ *  - Thread safety: calls from different host threads on different streams
+ *    (one pmap shard per thread) are safe.
+ */
+#ifndef JAX4J_CUDA_H
+#define JAX4J_CUDA_H
+
+#include <stddef.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+#define J4C_ABI_VERSION 1
+
+#if defined(__GNUC__)
+#define J4C_API __attribute__((visibility("default")))
+#else
+#define J4C_API
+#endif
+
+/* status codes */
+#define J4C_OK 0
+#define J4C_E_INVALID 1     /* bad argument: shape, dtype, op, size, pointer */
+#define J4C_E_UNSUPPORTED 2 /* valid request the device path does not implement */
+#define J4C_E_CUDA 3        /* CUDA runtime/driver error */
+#define J4C_E_OOM 4         /* device allocation failed */
+#define J4C_E_NCCL 5        /* NCCL error */
+#define J4C_E_TIMEOUT 6     /* a collective or a device-side wait exceeded its limit */
+#define J4C_E_DEVICE 7      /* a kernel reported an error through its status word */
+
+/* ir/Primitive.java:6-42 ordinals used by this ABI */
+#define J4C_ADD 0
+#define J4C_SUB 1
+#define J4C_MUL 2
+#define J4C_DIV 3
+#define J4C_DOT 4
+#define J4C_EXP 5
+#define J4C_LOG 6
+#define J4C_SIN 7
+#define J4C_COS 8
+#define J4C_SUM 9
+#define J4C_MEAN 10
+#define J4C_SUM_AXIS 11
+#define J4C_MEAN_AXIS 12
+#define J4C_TANH 13
+#define J4C_RELU 14
+#define J4C_SIGMOID 15
+#define J4C_GT 19
+#define J4C_GE 20
+#define J4C_LT 21
+#define J4C_LE 22
+#define J4C_EQ 23
+#define J4C_NE 24
+#define J4C_MAX 25
+#define J4C_MIN 26
+#define J4C_ARGMAX 27
+#define J4C_ARGMIN 28
+#define J4C_PSUM 30
+#define J4C_ALL_GATHER 31
+#define J4C_CAST 32
+
+/* core/DType.java:7-11 ordinals; BOOL is one byte holding 0 or 1 */
+#define J4C_FLOAT32 0
+#define J4C_FLOAT64 1
+#define J4C_INT32 2
+#define J4C_INT64 3
+#define J4C_BOOL 4
+
+typedef void *j4c_stream;           /* cudaStream_t */
+typedef struct j4c_comm_s *j4c_comm; /* one rank of a collective group */
+
+/* ------------------------------------------------------------------ */
+/* Runtime, devices, errors                                            */
+/* ------------------------------------------------------------------ */
+
+J4C_API int j4c_abi_version(void);
+/* Number of kernels this library has launched in the process (all devices). */
+J4C_API int j4c_kernel_launches(uint64_t *out);
+/* Message of the last failed call on this thread ("" if none). */
+J4C_API const char *j4c_last_error(void);
+/* Replaces Device.getDevices (core/Device.java:53-77): CUDA device count. */
+J4C_API int j4c_device_count(int *out);
+/* Binds the calling thread to a CUDA ordinal (pmap shard i -> GPU i). */
+J4C_API int j4c_set_device(int device);
+J4C_API int j4c_get_device(int *out);
+/* Enables peer access from `device` to `peer` (both directions when possible). */
+J4C_API int j4c_enable_peer_access(int device, int peer);
+/* Blocks until all work on the stream is done; returns any asynchronous
+ * kernel error, including device-side status words (J4C_E_DEVICE). */
+J4C_API int j4c_stream_synchronize(j4c_stream stream);
+J4C_API int j4c_stream_create(j4c_stream *out);
+J4C_API int j4c_stream_destroy(j4c_stream stream);
+/* Reads and clears the library's device status word on the current device:
+ * non-zero after a kernel gave up a bounded wait or rejected its input. */
+J4C_API int j4c_device_status(int *out_code);
+
+/* ------------------------------------------------------------------ */
+/* Storage: replaces ConcreteNDArray's host Storage records             */
+/* (core/ConcreteNDArray.java:47-87) and TornadoVM's per-call copies      */
+/* (backend/TornadoVMBackend.java:33-44) with resident device buffers.    */
+/* ------------------------------------------------------------------ */
+
+/* Stream-ordered allocation from the device's memory pool. */
+J4C_API int j4c_malloc(size_t bytes, void **out, j4c_stream stream);
+J4C_API int j4c_free(void *ptr, j4c_stream stream);
+J4C_API int j4c_memcpy_h2d(void *dst, const void *src, size_t bytes, j4c_stream stream);
+J4C_API int j4c_memcpy_d2h(void *dst, const void *src, size_t bytes, j4c_stream stream);
+J4C_API int j4c_memcpy_d2d(void *dst, const void *src, size_t bytes, j4c_stream stream);
+/* Fills n elements of dtype with value (Grad.java:847-903 ones/zeros/minusOne). */
+J4C_API int j4c_fill(int dtype, void *out, int64_t n, double value, j4c_stream stream);
+
+/* ------------------------------------------------------------------ */
+/* Elementwise                                                          */
+/* ------------------------------------------------------------------ */
+
+/* ExecutionBackend.binary (backend/ExecutionBackend.java:13) generalised to
+ * ConcreteNDArray.elementwise's broadcasting (core/ConcreteNDArray.java:219-316):
+ * prim in {ADD, SUB, MUL, DIV, MAX, MIN}; dtype FLOAT32 or FLOAT64; both
+ * operands share dtype.  out has the broadcast shape.  Results equal the
+ * reference's `(float) op((double) a, (double) b)`: correctly rounded
+ * IEEE arithmetic, Java Math.max/min NaN and signed-zero rules. */
+J4C_API int j4c_binary(int prim, int dtype, const void *a, const int64_t *a_dims, int a_rank,
+               const void *b, const int64_t *b_dims, int b_rank, void *out, j4c_stream stream);
+
+/* ConcreteNDArray.compareElementwise (core/ConcreteNDArray.java:328-404):
+ * prim in {GT, GE, LT, LE, EQ, NE}; dtype FLOAT32, FLOAT64, INT32 or INT64
+ * (BOOL operands are rejected, as in the reference); out is BOOL (uint8 0/1)
+ * with the broadcast shape.  Bit-exact. */
+J4C_API int j4c_compare(int prim, int dtype, const void *a, const int64_t *a_dims, int a_rank,
+                const void *b, const int64_t *b_dims, int b_rank, uint8_t *out,
+                j4c_stream stream);
+
+/* ExecutionBackend.unary (backend/ExecutionBackend.java:16) /
+ * ConcreteNDArray.unary (core/ConcreteNDArray.java:627-664): prim in {EXP,
+ * LOG, SIN, COS, TANH, RELU, SIGMOID}; dtype FLOAT32 or FLOAT64.  out may
+ * alias in. */
+J4C_API int j4c_unary(int prim, int dtype, const void *in, int64_t n, void *out, j4c_stream stream);
+
+/* ConcreteNDArray.astype (core/ConcreteNDArray.java:666-730): any pair of
+ * the five dtypes with Java's conversion rules (float->int truncates, NaN->0,
+ * saturates; long->int wraps; x->BOOL is "!= 0"; BOOL->x is 1/0).  Bit-exact. */
+J4C_API int j4c_cast(int src_dtype, int dst_dtype, const void *in, int64_t n, void *out,
+             j4c_stream stream);
+
+/* ------------------------------------------------------------------ */
+/* Reductions                                                           */
+/* ------------------------------------------------------------------ */
+
+/* ExecutionBackend.reduce (backend/ExecutionBackend.java:22) /
+ * HostBackend.reduce (backend/HostBackend.java:117-124): prim SUM or MEAN
+ * over n elements into out[0]; dtype FLOAT32 or FLOAT64.  Deterministic
+ * (fixed tree order); mean divides the sum by (T) n. */
+J4C_API int j4c_reduce_all(int prim, int dtype, const void *in, int64_t n, void *out,
+                   j4c_stream stream);
+
+/* ConcreteNDArray.reduceAxis (core/ConcreteNDArray.java:510-548): the input
+ * is viewed as [outer, axis_len, inner]; out is [outer, inner].  prim
+ * SUM_AXIS or MEAN_AXIS.  Deterministic. */
+J4C_API int j4c_reduce_axis(int prim, int dtype, const void *in, int64_t outer, int64_t axis_len,
+                    int64_t inner, void *out, j4c_stream stream);
+
+/* ConcreteNDArray.argReduceAxis (core/ConcreteNDArray.java:571-618): prim
+ * ARGMAX or ARGMIN over [outer, axis_len, inner] -> int32 [outer, inner];
+ * the first strict extremum wins, as the reference's sequential scan.
+ * Bit-exact. */
+J4C_API int j4c_argreduce(int prim, int dtype, const void *in, int64_t outer, int64_t axis_len,
+                  int64_t inner, int32_t *out, j4c_stream stream);
+
+/* ------------------------------------------------------------------ */
+/* Grad.java host helpers as device ops                                 */
+/* ------------------------------------------------------------------ */
+
+/* Grad.broadcastLike (api/Grad.java:539-582): reconciles g with the
+ * target shape -- equal size: copy (reshape); smaller g: broadcast it out;
+ * larger g: sum the broadcast contributions back down (deterministic).
+ * Also serves Grad.axisBroadcastLike (api/Grad.java:608-641) with g viewed as
+ * [outer, 1, inner] and the target as [outer, axis, inner]. */
+J4C_API int j4c_broadcast_like(int dtype, const void *g, const int64_t *g_dims, int g_rank, void *out,
+                       const int64_t *t_dims, int t_rank, j4c_stream stream);
+
+/* Grad.reluGrad (api/Grad.java:585-598): out = x > 0 ? g : 0. */
+J4C_API int j4c_relu_grad(int dtype, const void *g, const void *x, int64_t n, void *out,
+                  j4c_stream stream);
+
+/* Grad.maxMinGrad (api/Grad.java:500-530): routes g to the operand that won
+ * (ties go to a).  ga_full and gb_full have g's (broadcast) shape; apply
+ * j4c_broadcast_like to reduce them to the operand shapes. */
+J4C_API int j4c_maxmin_grad(int is_max, int dtype, const void *g, const int64_t *g_dims, int g_rank,
+                    const void *a, const int64_t *a_dims, int a_rank, const void *b,
+                    const int64_t *b_dims, int b_rank, void *ga_full, void *gb_full,
+                    j4c_stream stream);
+
+/* Grad.transpose (api/Grad.java:643-664): out[cols, rows] = in[rows, cols]. */
+J4C_API int j4c_transpose(int dtype, const void *in, int64_t rows, int64_t cols, void *out,
+                  j4c_stream stream);
+
+/* ------------------------------------------------------------------ */
+/* dot                                                                  */
+/* ------------------------------------------------------------------ */
+
+/* ExecutionBackend.matmul (backend/ExecutionBackend.java:19) /
+ * ConcreteNDArray.dot (core/ConcreteNDArray.java:406-461), with layout flags
+ * so the DOT VJP (api/Grad.java:385-390) needs no materialised transpose:
+ *   C[M,N] = op(A)[M,K] . op(B)[K,N]
+ *   op(A) = A stored [M,K] (trans_a = 0) or A stored [K,M] (trans_a = 1)
+ *   op(B) = B stored [K,N] (trans_b = 0) or B stored [N,K] (trans_b = 1)
+ * FLOAT32 runs on the 5th-generation tensor cores (tcgen05, TMA-fed) with a
+ * 3xTF32 split (a = hi + lo; a.b ~ hi.hi + hi.lo + lo.hi) so the result has
+ * FP32 accuracy; FLOAT64 runs a CUDA-core kernel.  Scratch for the split
+ * operands comes from the library's stream-ordered pool. */
+J4C_API int j4c_dot(int dtype, const void *a, const void *b, void *c, int64_t M, int64_t K, int64_t N,
+            int trans_a, int trans_b, j4c_stream stream);
+/* Same, with caller-provided scratch of at least j4c_dot_workspace_size bytes. */
+J4C_API int j4c_dot_ws(int dtype, const void *a, const void *b, void *c, int64_t M, int64_t K,
+               int64_t N, int trans_a, int trans_b, void *workspace, size_t workspace_bytes,
+               j4c_stream stream);
+J4C_API size_t j4c_dot_workspace_size(int dtype, int64_t M, int64_t K, int64_t N);
+
+/* ------------------------------------------------------------------ */
+/* Random (api/Random.java:39-150): SplitMix64 streams, bit-exact       */
+/* ------------------------------------------------------------------ */
+
+/* Random.uniform (api/Random.java:86-93): out[i] = lo + u(offset+i)*(hi-lo)
+ * in float.  offset lets each shard generate its slice of one global array. */
+J4C_API int j4c_random_uniform(uint64_t key, int64_t offset, int64_t n, float lo, float hi, float *out,
+                       j4c_stream stream);
+/* Random.normal (api/Random.java:104-113): Box-Muller in double. */
+J4C_API int j4c_random_normal(uint64_t key, int64_t offset, int64_t n, float *out, j4c_stream stream);
+
+/* ------------------------------------------------------------------ */
+/* Collectives: replace SharedCollective (api/SharedCollective.java)    */
+/* ------------------------------------------------------------------ */
+
+/* Number of bytes of a collective group id (the NCCL unique id). */
+#define J4C_COMM_ID_BYTES 128
+/* Creates a group id on rank 0; the caller distributes it to every rank. */
+J4C_API int j4c_comm_unique_id(void *out, size_t len);
+/* Joins rank `rank` of an nranks group on CUDA device `device`
+ * (one process per GPU).  Initialisation and every collective are bounded
+ * by timeout_ms: on expiry the communicator is aborted and the call returns
+ * J4C_E_TIMEOUT instead of hanging (the reference's barrier waits forever,
+ * api/SharedCollective.java:78-85). */
+J4C_API int j4c_comm_init_rank(const void *id, size_t len, int nranks, int rank, int device,
+                       int64_t timeout_ms, j4c_comm *out);
+/* One process driving ndev GPUs (the reference's thread-per-shard pmap,
+ * api/Pmap.java:135-166): out[i] is the rank bound to devices[i]. */
+J4C_API int j4c_comm_init_all(const int *devices, int ndev, int64_t timeout_ms, j4c_comm *out);
+J4C_API int j4c_comm_rank(j4c_comm comm, int *rank, int *nranks);
+J4C_API int j4c_comm_destroy(j4c_comm comm);
+J4C_API int j4c_comm_abort(j4c_comm comm);
+/* SharedCollective.psum (api/SharedCollective.java:44-54): all-reduce sum of
+ * n elements (FLOAT32/FLOAT64) enqueued on `stream`; in and out may alias.
+ * Asynchronous like every other op: j4c_comm_wait bounds the wait for it. */
+J4C_API int j4c_psum(j4c_comm comm, int dtype, const void *in, void *out, int64_t n, j4c_stream stream);
+/* SharedCollective.allGather (api/SharedCollective.java:61-76): out is
+ * [nranks, n] in rank order. */
+J4C_API int j4c_all_gather(j4c_comm comm, int dtype, const void *in, void *out, int64_t n,
+                   j4c_stream stream);
+/* Waits until the work enqueued on `stream` is done, bounded by the
+ * communicator's timeout; on expiry aborts the communicator and returns
+ * J4C_E_TIMEOUT (replaces the unbounded CyclicBarrier.await,
+ * api/SharedCollective.java:78-85). */
+J4C_API int j4c_comm_wait(j4c_comm comm, j4c_stream stream);
+/* In-process psum over shards that share one device (several pmap shards on
+ * one GPU, or peer-mapped slots): out[i] = 0 + slot0[i] + slot1[i] + ... in
+ * slot order, bit-identical to the reference's summation order
+ * (api/SharedCollective.java:47-51).  slots is a HOST array of nslots device
+ * pointers; out may alias any slot. */
+J4C_API int j4c_psum_slots(int dtype, const void *const *slots, int nslots, void *out, int64_t n,
+                   j4c_stream stream);
+
+#ifdef __cplusplus
+}
+#endif
+#endif /* JAX4J_CUDA_H */

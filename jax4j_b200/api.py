@@ -1,0 +1,321 @@
+"""Public transform and library API: JAX, Lax, Nn, Numpy, Random.
+
+Same entry points, argument meaning and error behaviour as the reference's
+api/JAX.java, api/Lax.java, api/Nn.java, api/Numpy.java and api/Random.java
+(paths relative to src/main/java/com/marmanis/jax4j/).  Python methods keep
+the Java names; where Java overloads on arity, the Python function accepts
+the extra argument (pmap of several sharded inputs, grad with argnum).
+"""
+from __future__ import annotations
+
+import math
+from typing import Callable, List, Sequence
+
+import numpy as np
+import torch
+
+from . import grad as _grad
+from . import pmap as _pm
+from ._lib import call
+from .core import (ConcreteNDArray, Device, DType, IllegalArgumentException, NDArray, PRNGKey,
+                   Primitive, Shape, stream_of)
+from .pytree import PyTree, PyTrees
+from .tracing import CheckpointMeta, Equation, PmapMeta, Tracer, TracedNDArray, to_var
+
+
+# ---------------------------------------------------------------------------
+# JAX (api/JAX.java)
+# ---------------------------------------------------------------------------
+class JAX:
+    @staticmethod
+    def make_jaxpr(fn: Callable, *args: NDArray):
+        """JAX.make_jaxpr (JAX.java:30-55)."""
+        return _grad.make_jaxpr(fn, *args)
+
+    @staticmethod
+    def grad(fn: Callable, argnum: int = None) -> Callable:
+        """JAX.grad (JAX.java:279-289)."""
+        return _grad.grad(fn, argnum)
+
+    @staticmethod
+    def gradBoth(fn: Callable) -> Callable:
+        return _grad.grad_both(fn)
+
+    @staticmethod
+    def gradTree(fn: Callable) -> Callable:
+        """JAX.gradTree (JAX.java:303-305)."""
+        return _grad.grad_tree(fn)
+
+    @staticmethod
+    def value_and_grad(fn: Callable) -> Callable:
+        """JAX.value_and_grad (JAX.java:243-245)."""
+        return _grad.value_and_grad(fn)
+
+    @staticmethod
+    def valueAndGradTree(fn: Callable) -> Callable:
+        """value_and_grad over a PyTree of parameters (one forward + backward)."""
+        return _grad.value_and_grad_tree(fn)
+
+    @staticmethod
+    def jit(fn: Callable) -> Callable:
+        """JAX.jit (JAX.java:92-125): traced once per input signature, then the
+        cached Jaxpr is executed; transparent inside another trace."""
+        cache = {}
+
+        def jitted(*args):
+            if Tracer.current() is not None:
+                return fn(*args)
+            key = tuple((a.shape(), a.dtype()) for a in args)
+            jaxpr = cache.get(key)
+            if jaxpr is None:
+                jaxpr = _grad.make_jaxpr(fn, *args)
+                cache[key] = jaxpr
+            return _grad.forward_interpret(jaxpr, list(args))[0]
+
+        jitted.cache = cache
+        return jitted
+
+    @staticmethod
+    def jitGrad(fn: Callable) -> Callable:
+        """JAX.jitGrad (JAX.java:137-151)."""
+        cache = {}
+
+        def g(arg):
+            if Tracer.current() is not None:
+                return _grad.grad(fn)(arg)
+            key = (arg.shape(), arg.dtype())
+            jaxpr = cache.get(key)
+            if jaxpr is None:
+                jaxpr = _grad.make_jaxpr(fn, arg)
+                cache[key] = jaxpr
+            return _grad._backward(jaxpr, [arg])[0]
+
+        g.cache = cache
+        return g
+
+    @staticmethod
+    def jitGradTree(fn: Callable) -> Callable:
+        """JAX.jitGradTree (JAX.java:168-183)."""
+        cache = {}
+
+        def g(tree):
+            if Tracer.current() is not None:
+                return _grad.grad_tree(fn)(tree)
+            leaves = PyTrees.flatten(tree)
+            key = tuple((l.shape(), l.dtype()) for l in leaves)
+            jaxpr = cache.get(key)
+            if jaxpr is None:
+                jaxpr = _grad._trace_tree(fn, tree, leaves)
+                cache[key] = jaxpr
+            return PyTrees.unflatten(tree, _grad._backward(jaxpr, leaves))
+
+        g.cache = cache
+        return g
+
+    @staticmethod
+    def checkpoint(fn: Callable) -> Callable:
+        """JAX.checkpoint (JAX.java:258-274): a CHECKPOINT equation under a trace."""
+        def c(arg):
+            if Tracer.current() is not None:
+                sub = _trace_body(fn, [(arg.shape(), arg.dtype())])
+                tracer = Tracer.current()
+                in_var = to_var(arg)
+                ov = sub.outVars[0]
+                out = tracer.nextVar(ov.shape, ov.dtype)
+                tracer.addEquation(Equation([in_var], [out], Primitive.CHECKPOINT, CheckpointMeta(sub)))
+                return TracedNDArray(out)
+            return fn(arg)
+        return c
+
+    @staticmethod
+    def pmap(fn: Callable, devices: Sequence[Device]) -> Callable:
+        """JAX.pmap (JAX.java:356-377): every argument is sharded along axis 0
+        (its leading dim must equal len(devices)); results are stacked to
+        [D, *out].  Under a trace a PMAP equation is emitted so grad composes
+        with the collectives in the body."""
+        devices = tuple(devices)
+        D = len(devices)
+
+        def mapped(*inputs: NDArray):
+            if not inputs:
+                raise IllegalArgumentException("pmap needs at least one input")
+            if Tracer.current() is not None:
+                specs = []
+                for x in inputs:
+                    d = x.shape().dimensions()
+                    if not d or d[0] != D:
+                        raise IllegalArgumentException(
+                            f"pmap: input leading dim {d[0] if d else 0} must equal numDevices {D}")
+                    specs.append((Shape(d[1:]), x.dtype()))
+                body = _trace_body(fn, specs)
+                tracer = Tracer.current()
+                in_vars = [to_var(x) for x in inputs]
+                ov = body.outVars[0]
+                out = tracer.nextVar(Shape((D,) + ov.shape.dimensions()), ov.dtype)
+                tracer.addEquation(Equation(in_vars, [out], Primitive.PMAP, PmapMeta(body, devices)))
+                return TracedNDArray(out)
+            return _pm.run_forward(fn, inputs, devices)
+
+        return mapped
+
+
+def _trace_body(fn: Callable, specs) -> "Jaxpr":
+    """JAX.traceBody (JAX.java:379-391) for any number of inputs."""
+    Tracer.start()
+    try:
+        t = Tracer.current()
+        in_vars = [t.nextVar(s, d) for s, d in specs]
+        result = fn(*[TracedNDArray(v) for v in in_vars])
+        if not isinstance(result, TracedNDArray):
+            result = TracedNDArray(t.nextConstant(result))
+        return Tracer.stop(in_vars, [result.getVar()])
+    except BaseException:
+        Tracer.abort()
+        raise
+
+
+# ---------------------------------------------------------------------------
+# Lax collectives (api/Lax.java:166-217)
+# ---------------------------------------------------------------------------
+class Lax:
+    @staticmethod
+    def psum(x: NDArray) -> NDArray:
+        """Lax.psum (Lax.java:176-187): PSUM equation under a trace, all-reduce
+        sum inside pmap, identity outside."""
+        if Tracer.current() is not None:
+            tracer = Tracer.current()
+            v = to_var(x)
+            out = tracer.nextVar(x.shape(), x.dtype())
+            tracer.addEquation(Equation([v], [out], Primitive.PSUM, None))
+            return TracedNDArray(out)
+        return _pm.psum_value(x)
+
+    @staticmethod
+    def allGather(x: NDArray, numDevices: int) -> NDArray:
+        """Lax.allGather (Lax.java:202-217)."""
+        if Tracer.current() is not None:
+            tracer = Tracer.current()
+            v = to_var(x)
+            out = tracer.nextVar(Shape((numDevices,) + x.shape().dimensions()), x.dtype())
+            tracer.addEquation(Equation([v], [out], Primitive.ALL_GATHER, numDevices))
+            return TracedNDArray(out)
+        return _pm.all_gather_value(x)
+
+    @staticmethod
+    def psumTree(tree: PyTree) -> PyTree:
+        """PyTrees.map(Lax::psum, tree) as ONE all-reduce: the leaves are packed
+        into a single buffer (one NCCL call instead of one per leaf); every
+        element's sum is the same as leaf-by-leaf psum."""
+        ctx = _pm.PmapContext.current()
+        leaves = PyTrees.flatten(tree)
+        if ctx is None or Tracer.current() is not None or not leaves:
+            return PyTrees.map(Lax.psum, tree)
+        first = leaves[0]
+        if any(l.dtype() != first.dtype() or l.tensor().device != first.tensor().device for l in leaves):
+            return PyTrees.map(Lax.psum, tree)
+        total = sum(l.shape().size() for l in leaves)
+        flat = torch.empty(total, dtype=first.dtype().torch, device=first.tensor().device)
+        s = first._stream()
+        off = 0
+        es = first.dtype().byteSize()
+        for l in leaves:
+            n = l.shape().size()
+            call("j4c_memcpy_d2d", flat.data_ptr() + off * es, l.data_ptr(), n * es, s)
+            off += n
+        packed = ConcreteNDArray._wrap(flat, Shape(total), first.dtype(), first.device())
+        summed = ctx.collective.psum(ctx.deviceIndex, packed)
+        out, off = [], 0
+        for l in leaves:
+            n = l.shape().size()
+            out.append(ConcreteNDArray._wrap(summed.tensor()[off:off + n], l.shape(), l.dtype(),
+                                             summed.device()))
+            off += n
+        return PyTrees.unflatten(tree, out)
+
+
+# ---------------------------------------------------------------------------
+# Nn / Numpy (api/Nn.java:21-25, api/Numpy.java:39-44)
+# ---------------------------------------------------------------------------
+class Nn:
+    @staticmethod
+    def softmax(x: NDArray) -> NDArray:
+        """Nn.softmax: exp(x) / sum(exp(x), -1, keepDims) -- no max subtraction,
+        as in the reference."""
+        e = x.exp()
+        return e.div(e.sum(-1, True))
+
+
+class Numpy:
+    @staticmethod
+    def where(cond: NDArray, x: NDArray, y: NDArray) -> NDArray:
+        """Numpy.where: c*x + (1-c)*y with c = cond as FLOAT32 (an arithmetic
+        blend, not a select, exactly as the reference computes it)."""
+        c = cond.astype(DType.FLOAT32) if cond.dtype() == DType.BOOL else cond
+        one = ConcreteNDArray.scalar(1.0, DType.FLOAT32, _dev_of(c))
+        inv = one.sub(c)
+        return c.mul(x).add(inv.mul(y))
+
+
+def _dev_of(x: NDArray):
+    return x.device() if isinstance(x, ConcreteNDArray) else None
+
+
+# ---------------------------------------------------------------------------
+# Random (api/Random.java): SplitMix64 streams, generated on the device
+# ---------------------------------------------------------------------------
+_GAMMA = 0x9E3779B97F4A7C15
+_SPLIT = 0xD1B54A32D192ED03
+_M64 = 0xFFFFFFFFFFFFFFFF
+
+
+def _mix64(z: int) -> int:
+    z &= _M64
+    z = ((z ^ (z >> 30)) * 0xBF58476D1CE4E5B9) & _M64
+    z = ((z ^ (z >> 27)) * 0x94D049BB133111EB) & _M64
+    return z ^ (z >> 31)
+
+
+class Random:
+    @staticmethod
+    def split(key: PRNGKey, num: int = 2) -> List[PRNGKey]:
+        """Random.split (Random.java:70-81)."""
+        return [PRNGKey(_mix64(key.state() ^ _SPLIT ^ ((_GAMMA * (i + 1)) & _M64))) for i in range(num)]
+
+    @staticmethod
+    def uniform(key: PRNGKey, shape, lo: float = 0.0, hi: float = 1.0, device: Device = None,
+                offset: int = 0, count: int = None) -> ConcreteNDArray:
+        """Random.uniform (Random.java:86-98).  offset/count select elements
+        [offset, offset+count) of the full array (a shard's rows)."""
+        shape = shape if isinstance(shape, Shape) else Shape(shape)
+        n = shape.size() if count is None else count
+        device = device or Device.defaultDevice()
+        t = torch.empty(n, dtype=torch.float32, device=device.torch_device())
+        call("j4c_random_uniform", key.state(), offset, n, float(np.float32(lo)), float(np.float32(hi)),
+             t.data_ptr(), stream_of(device.ordinal()))
+        out_shape = shape if count is None else Shape(n)
+        return ConcreteNDArray._wrap(t, out_shape, DType.FLOAT32, device)
+
+    @staticmethod
+    def normal(key: PRNGKey, shape, device: Device = None, offset: int = 0,
+               count: int = None) -> ConcreteNDArray:
+        """Random.normal (Random.java:104-113): Box-Muller."""
+        shape = shape if isinstance(shape, Shape) else Shape(shape)
+        n = shape.size() if count is None else count
+        device = device or Device.defaultDevice()
+        t = torch.empty(n, dtype=torch.float32, device=device.torch_device())
+        call("j4c_random_normal", key.state(), offset, n, t.data_ptr(), stream_of(device.ordinal()))
+        out_shape = shape if count is None else Shape(n)
+        return ConcreteNDArray._wrap(t, out_shape, DType.FLOAT32, device)
+
+    @staticmethod
+    def bernoulli(key: PRNGKey, p: float, shape, device: Device = None) -> ConcreteNDArray:
+        """Random.bernoulli (Random.java:116-123): uniform < p."""
+        u = Random.uniform(key, shape, 0.0, 1.0, device)
+        return u.lt(ConcreteNDArray.scalar(float(np.float32(p)), DType.FLOAT32, u.device()))
+
+    @staticmethod
+    def glorotUniform(key: PRNGKey, shape, fanIn: int, fanOut: int, device: Device = None,
+                      offset: int = 0, count: int = None) -> ConcreteNDArray:
+        """Random.glorotUniform (Random.java:147-150)."""
+        limit = float(np.float32(math.sqrt(6.0 / (fanIn + fanOut))))
+        return Random.uniform(key, shape, -limit, limit, device, offset, count)

@@ -1,0 +1,62 @@
+// dot.cu -- the j4c_dot entry points (ConcreteNDArray.dot,
+// core/ConcreteNDArray.java:406-461; ExecutionBackend.matmul,
+// backend/ExecutionBackend.java:19).  Chooses the kernel for a shape/dtype.
+#include "common.cuh"
+
+namespace j4c {
+int simt_gemm(int dtype, const void *a, const void *b, void *c, int64_t M, int64_t K, int64_t N,
+              int trans_a, int trans_b, cudaStream_t s);
+int tc_gemm_workspace(int64_t M, int64_t K, int64_t N, size_t *bytes);
+int tc_gemm_f32(const float *a, const float *b, float *c, int64_t M, int64_t K, int64_t N,
+                int trans_a, int trans_b, void *ws, size_t ws_bytes, cudaStream_t s);
+bool tc_gemm_supported(int64_t M, int64_t K, int64_t N);
+}  // namespace j4c
+
+using namespace j4c;
+
+extern "C" {
+
+size_t j4c_dot_workspace_size(int dtype, int64_t M, int64_t K, int64_t N) {
+    if (dtype != J4C_FLOAT32 || !tc_gemm_supported(M, K, N)) return 0;
+    size_t bytes = 0;
+    tc_gemm_workspace(M, K, N, &bytes);
+    return bytes;
+}
+
+int j4c_dot_ws(int dtype, const void *a, const void *b, void *c, int64_t M, int64_t K, int64_t N,
+               int trans_a, int trans_b, void *workspace, size_t workspace_bytes,
+               j4c_stream stream) {
+    J4C_REQUIRE(M >= 0 && K >= 0 && N >= 0, "j4c_dot: negative dimension");
+    J4C_REQUIRE(dtype == J4C_FLOAT32 || dtype == J4C_FLOAT64,
+                "dot requires FLOAT32 or FLOAT64 operands, got %s", dtype_name(dtype));
+    cudaStream_t s = as_stream(stream);
+    if (M == 0 || N == 0) return J4C_OK;
+    J4C_REQUIRE(a && b && c, "j4c_dot: NULL pointer");
+    if (K == 0) return j4c_fill(dtype, c, M * N, 0.0, stream);
+    if (dtype == J4C_FLOAT32 && tc_gemm_supported(M, K, N)) {
+        size_t need = 0;
+        tc_gemm_workspace(M, K, N, &need);
+        J4C_REQUIRE(workspace_bytes >= need && (need == 0 || workspace),
+                    "j4c_dot_ws: workspace of %zu bytes is smaller than the %zu required",
+                    workspace_bytes, need);
+        return tc_gemm_f32((const float *)a, (const float *)b, (float *)c, M, K, N, trans_a,
+                           trans_b, workspace, workspace_bytes, s);
+    }
+    return simt_gemm(dtype, a, b, c, M, K, N, trans_a, trans_b, s);
+}
+
+int j4c_dot(int dtype, const void *a, const void *b, void *c, int64_t M, int64_t K, int64_t N,
+            int trans_a, int trans_b, j4c_stream stream) {
+    size_t need = j4c_dot_workspace_size(dtype, M, K, N);
+    void *ws = nullptr;
+    cudaStream_t s = as_stream(stream);
+    if (need) {
+        int rc = scratch_alloc(need, &ws, s);
+        if (rc) return rc;
+    }
+    int rc = j4c_dot_ws(dtype, a, b, c, M, K, N, trans_a, trans_b, ws, need, stream);
+    if (ws) scratch_free(ws, s);
+    return rc;
+}
+
+}  // extern "C"

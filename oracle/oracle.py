@@ -42,35 +42,35 @@ def lib() -> C.CDLL:
 
 
 P = C.c_void_p
-I64 = C.c_int64
+CI64 = C.c_int64
 
 
 def _declare(L):
     L.orc_mix64.restype = C.c_uint64
     L.orc_mix64.argtypes = [C.c_uint64]
     L.orc_split.argtypes = [C.c_uint64, C.c_int, P]
-    L.orc_uniform.argtypes = [C.c_uint64, I64, C.c_float, C.c_float, P]
-    L.orc_normal.argtypes = [C.c_uint64, I64, P]
-    L.orc_glorot_uniform.argtypes = [C.c_uint64, I64, C.c_int, C.c_int, P]
-    L.orc_broadcast_index.restype = I64
-    L.orc_broadcast_index.argtypes = [P, C.c_int, P, C.c_int, I64]
+    L.orc_uniform.argtypes = [C.c_uint64, CI64, C.c_float, C.c_float, P]
+    L.orc_normal.argtypes = [C.c_uint64, CI64, P]
+    L.orc_glorot_uniform.argtypes = [C.c_uint64, CI64, C.c_int, C.c_int, P]
+    L.orc_broadcast_index.restype = CI64
+    L.orc_broadcast_index.argtypes = [P, C.c_int, P, C.c_int, CI64]
     L.orc_binary_f32.argtypes = [C.c_int, P, P, C.c_int, P, P, C.c_int, P, P, C.c_int]
     L.orc_compare.argtypes = [C.c_int, C.c_int, P, P, C.c_int, P, P, C.c_int, P, P, C.c_int]
-    L.orc_unary_f32.argtypes = [C.c_int, P, I64, P]
-    L.orc_cast.argtypes = [C.c_int, C.c_int, P, I64, P]
-    L.orc_reduce_all_f32.argtypes = [C.c_int, P, I64, P]
-    L.orc_reduce_axis_f32.argtypes = [C.c_int, P, I64, I64, I64, P]
-    L.orc_argreduce_f32.argtypes = [C.c_int, P, I64, I64, I64, P]
-    L.orc_dot_f32.argtypes = [P, P, P, I64, I64, I64, I64, I64, C.c_int]
+    L.orc_unary_f32.argtypes = [C.c_int, P, CI64, P]
+    L.orc_cast.argtypes = [C.c_int, C.c_int, P, CI64, P]
+    L.orc_reduce_all_f32.argtypes = [C.c_int, P, CI64, P]
+    L.orc_reduce_axis_f32.argtypes = [C.c_int, P, CI64, CI64, CI64, P]
+    L.orc_argreduce_f32.argtypes = [C.c_int, P, CI64, CI64, CI64, P]
+    L.orc_dot_f32.argtypes = [P, P, P, CI64, CI64, CI64, CI64, CI64, C.c_int]
     L.orc_broadcast_like_f32.argtypes = [P, P, C.c_int, P, P, C.c_int]
-    L.orc_relu_grad_f32.argtypes = [P, P, I64, P]
+    L.orc_relu_grad_f32.argtypes = [P, P, CI64, P]
     L.orc_axis_broadcast_like_f32.argtypes = [P, P, C.c_int, C.c_int, P]
-    L.orc_transpose_f32.argtypes = [P, I64, I64, P]
+    L.orc_transpose_f32.argtypes = [P, CI64, CI64, P]
     L.orc_maxmin_grad_f32.argtypes = [C.c_int, P, P, C.c_int, P, P, C.c_int, P, P, C.c_int, P, P]
-    L.orc_psum_f32.argtypes = [P, C.c_int, I64, P]
-    L.orc_mlp_loss_grad_f32.argtypes = [C.c_int, P, C.c_int, P, P, P, P, I64, P, P, P, P, C.c_int]
-    L.orc_mlp_loss_f32.argtypes = [C.c_int, P, C.c_int, P, P, P, P, I64, P, C.c_int]
-    L.orc_sweep_f32.argtypes = [P, P, I64, I64, P, P, P]
+    L.orc_psum_f32.argtypes = [P, C.c_int, CI64, P]
+    L.orc_mlp_loss_grad_f32.argtypes = [C.c_int, P, C.c_int, P, P, P, P, CI64, P, P, P, P, P, C.c_int]
+    L.orc_mlp_loss_f32.argtypes = [C.c_int, P, C.c_int, P, P, P, P, CI64, P, C.c_int]
+    L.orc_sweep_f32.argtypes = [P, P, CI64, CI64, P, P, P]
 
 
 def _p(a: np.ndarray):
@@ -286,7 +286,20 @@ def psum(slots):
 
 
 # ---- MLP cross-entropy (examples/MNISTFromScratch.java:103-125) ----
-def mlp_loss_grad(ws, bs, x, onehot, act: str = "tanh", want_gx: bool = False, threads: int = 1):
+def mlp_hidden_preacts(ws, bs, x, act: str = "relu", threads: int = 1):
+    """Pre-activations z_l = a_l.W_l + b_l of the hidden layers, computed with
+    the same restated ops (dot, broadcast add, activation) as the MLP oracle."""
+    a = _c(x)
+    zs = []
+    for l in range(len(ws) - 1):
+        z = binary(ADD, dot(a, ws[l], threads=threads), bs[l])
+        zs.append(z)
+        a = unary(TANH if act == "tanh" else RELU, z)
+    return zs
+
+
+def mlp_loss_grad(ws, bs, x, onehot, act: str = "tanh", want_gx: bool = False, threads: int = 1,
+                  relu_masks=None):
     L = len(ws)
     ws = [_c(w) for w in ws]
     bs = [_c(b) for b in bs]
@@ -301,9 +314,13 @@ def mlp_loss_grad(ws, bs, x, onehot, act: str = "tanh", want_gx: bool = False, t
     gbp = (C.c_void_p * L)(*[g.ctypes.data for g in gbs])
     gx = np.empty_like(x) if want_gx else None
     loss = np.zeros(1, np.float32)
+    mp = None
+    if relu_masks is not None:
+        masks = [np.ascontiguousarray(m, dtype=np.uint8) for m in relu_masks]
+        mp = (C.c_void_p * len(masks))(*[m.ctypes.data for m in masks])
     lib().orc_mlp_loss_grad_f32(L, _p(dims), 0 if act == "tanh" else 1, wp, bp, _p(x), _p(onehot),
                                 x.shape[0], _p(loss), gwp, gbp,
-                                _p(gx) if gx is not None else None, threads)
+                                _p(gx) if gx is not None else None, mp, threads)
     return float(loss[0]), gws, gbs, gx
 
 

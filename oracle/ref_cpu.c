@@ -529,7 +529,7 @@ int orc_mlp_loss_f32(int num_layers, const int64_t *dims, int act, const float *
 int orc_mlp_loss_grad_f32(int num_layers, const int64_t *dims, int act, const float *const *w,
                           const float *const *b, const float *x, const float *onehot,
                           int64_t batch, float *loss, float *const *gw, float *const *gb,
-                          float *gx, int threads) {
+                          float *gx, const uint8_t *const *relu_masks, int threads) {
     int L = num_layers;
     int64_t B = batch;
     mlp_fwd f;
@@ -605,6 +605,10 @@ int orc_mlp_loss_grad_f32(int num_layers, const int64_t *dims, int act, const fl
                 float one_m = 1.0f - tt;
                 g_z[i] = g_a[i] * one_m;
             }
+        } else if (relu_masks && relu_masks[l - 1]) {
+            /* relu'(z) from a caller-supplied sign pattern of z (see header) */
+            const uint8_t *mk = relu_masks[l - 1];
+            for (int64_t i = 0; i < B * din; i++) g_z[i] = mk[i] ? g_a[i] : 0.0f;
         } else {
             orc_relu_grad_f32(g_a, zin, B * din, g_z); /* Grad.java:585-598 */
         }

@@ -95,12 +95,18 @@ void orc_psum_f32(const float *const *slots, int num_devices, int64_t n, float *
  * layers: L weight matrices w[l] of [dims[l], dims[l+1]] and biases b[l];
  * act: 0 = tanh (MNISTFromScratch.java:103-115), 1 = relu.
  * Writes the loss (scalar) and the gradient of every w/b leaf, and, when gx
- * is not NULL, the gradient with respect to x (the DOT VJP's first output). */
+ * is not NULL, the gradient with respect to x (the DOT VJP's first output).
+ * relu_masks (optional, relu only): one [batch, dims[l+1]] byte array per
+ * hidden layer giving the sign pattern z > 0 to use in relu's VJP.  relu' is
+ * discontinuous at 0, so an element whose pre-activation is within rounding
+ * of 0 can take the other branch under a different (equally valid) summation
+ * order; a checker passes the device's pattern after verifying every
+ * disagreement is such a near-tie. */
 int orc_mlp_loss_grad_f32(int num_layers, const int64_t *dims, int act,
                           const float *const *w, const float *const *b,
                           const float *x, const float *onehot, int64_t batch,
                           float *loss, float *const *gw, float *const *gb, float *gx,
-                          int threads);
+                          const uint8_t *const *relu_masks, int threads);
 /* Loss-only forward (same equation order). */
 int orc_mlp_loss_f32(int num_layers, const int64_t *dims, int act,
                      const float *const *w, const float *const *b,

@@ -1,0 +1,160 @@
+"""The workloads of the path, end to end through the public API, against the
+oracle: the MLP cross-entropy grad steps (tanh 2-layer and relu 4-layer, at
+reduced sizes the oracle finishes in seconds), grad-of-pmap w.r.t. the input,
+and the elementwise where/tanh/sigmoid/clip sweep with sum and argmax."""
+import numpy as np
+import pytest
+
+from oracle import oracle as orc
+from tests.util import TOL_ELEMENTWISE, TOL_REDUCTION, assert_rel
+
+pytestmark = pytest.mark.gpu
+
+
+@pytest.fixture(scope="module")
+def J():
+    import jax4j_b200 as j
+    return j
+
+
+def make_mlp(J, dims, seed):
+    """Glorot weights and zero biases from split keys (seeded like the configs)."""
+    keys = J.Random.split(J.PRNGKey.key(seed), len(dims) - 1)
+    tree = {}
+    for i in range(len(dims) - 1):
+        tree[f"w{i + 1}"] = J.Random.glorotUniform(keys[i], J.Shape(dims[i], dims[i + 1]), dims[i], dims[i + 1])
+        tree[f"b{i + 1}"] = J.ConcreteNDArray.full(J.Shape(dims[i + 1]), 0.0)
+    return J.PyTree.dictOf(tree)
+
+
+def mlp_loss(J, act):
+    def loss(p, x, t):
+        c = p.children
+        L = len(c) // 2
+        a = x
+        for i in range(1, L):
+            z = a.dot(c[f"w{i}"].value).add(c[f"b{i}"].value)
+            a = z.tanh() if act == "tanh" else z.relu()
+        logits = a.dot(c[f"w{L}"].value).add(c[f"b{L}"].value)
+        neg = J.ConcreteNDArray.scalar(-1.0, device=x.device())
+        return J.Nn.softmax(logits).log().mul(t).sum(-1).mean().mul(neg)
+    return loss
+
+
+def onehot(labels, C):
+    t = np.zeros((len(labels), C), np.float32)
+    t[np.arange(len(labels)), labels] = 1
+    return t
+
+
+def host_params(tree):
+    c = tree.children
+    L = len(c) // 2
+    return ([c[f"w{i}"].value.numpy() for i in range(1, L + 1)],
+            [c[f"b{i}"].value.numpy() for i in range(1, L + 1)])
+
+
+def relu_masks(J, params, x_dev, xh, act):
+    """Device sign patterns of the hidden pre-activations, after checking
+    every element where they disagree with the oracle's is a near-tie:
+    |z| within the reduction tolerance of 0 (relu' is discontinuous there and
+    either branch is a correct rounding of the reference's arithmetic)."""
+    if act != "relu":
+        return None
+    c = params.children
+    L = len(c) // 2
+    ws, bs = host_params(params)
+    z_ref = orc.mlp_hidden_preacts(ws, bs, xh, act, threads=8)
+    a = x_dev
+    masks = []
+    for i in range(1, L):
+        z = a.dot(c[f"w{i}"].value.to(a.device())).add(c[f"b{i}"].value.to(a.device()))
+        a = z.relu()
+        zg = z.numpy()
+        zr = z_ref[i - 1]
+        m = zg > 0
+        dis = m != (zr > 0)
+        rms = float(np.sqrt(np.mean(zr.astype(np.float64) ** 2)))
+        assert np.all(np.abs(zr[dis]) <= TOL_REDUCTION * rms), "relu sign flip away from a tie"
+        masks.append(m)
+    return masks
+
+
+@pytest.mark.parametrize("dims,act,B,D", [([784, 512, 10], "tanh", 64, 2),
+                                          ([256, 512, 512, 512, 100], "relu", 96, 2),
+                                          ([1024, 4096, 4096, 4096, 1000], "relu", 64, 1)])
+def test_dp_grad_step_matches_oracle(J, dims, act, B, D):
+    """pmap-of-valueAndGradTree with psum-averaged grads (configs 0 and 4 shape)."""
+    params = make_mlp(J, dims, 3)
+    x = J.Random.normal(J.PRNGKey.key(1), J.Shape(D, B, dims[0]))
+    labels = (orc.uniform(J.PRNGKey.key(2).state(), (D * B,)) * dims[-1]).astype(np.int64)
+    t_host = onehot(labels, dims[-1]).reshape(D, B, dims[-1])
+    t = J.ConcreteNDArray.of(t_host)
+    devices = [J.Device(None) for _ in range(D)]
+    loss = mlp_loss(J, act)
+    Dn = J.ConcreteNDArray.scalar(float(D))
+    out = {}
+
+    def body(xs, ts):
+        ploc = J.PyTrees.map(lambda a: a.to(xs.device()), params)
+        v, g = J.JAX.valueAndGradTree(lambda p: loss(p, xs, ts))(ploc)
+        g = J.Lax.psumTree(g)
+        out[id(xs.device())] = J.PyTrees.map(lambda a: a.div(Dn.to(a.device())), g)
+        return v
+
+    losses = J.JAX.pmap(body, devices)(x, t).toFloatArray()
+    ws, bs = host_params(params)
+    xh = x.numpy()
+    shards = [J.ConcreteNDArray.of(xh[i]) for i in range(D)]
+    per = [orc.mlp_loss_grad(ws, bs, xh[i], t_host[i], act=act, threads=8,
+                             relu_masks=relu_masks(J, params, shards[i], xh[i], act)) for i in range(D)]
+    for i in range(D):
+        assert abs(losses[i] - per[i][0]) <= TOL_REDUCTION * abs(per[i][0])
+    g = next(iter(out.values())).children
+    L = len(ws)
+    for l in range(L):
+        ref_w = orc.binary(orc.DIV, orc.psum([per[i][1][l] for i in range(D)]), np.float32([D]))
+        ref_b = orc.binary(orc.DIV, orc.psum([per[i][2][l] for i in range(D)]), np.float32([D]))
+        assert_rel(g[f"w{l + 1}"].value.numpy(), ref_w, TOL_REDUCTION, f"dW{l + 1}")
+        assert_rel(g[f"b{l + 1}"].value.numpy(), ref_b, TOL_REDUCTION, f"db{l + 1}")
+
+
+def test_grad_of_pmap_wrt_input(J):
+    """JAX.grad(x -> pmap(loss(params, .)).sum()) -- the PMAP VJP path."""
+    dims = [784, 512, 10]
+    params = make_mlp(J, dims, 0)
+    B, D = 32, 2
+    x = J.Random.normal(J.PRNGKey.key(0), J.Shape(D, B, dims[0]))
+    labels = (orc.uniform(7, (D * B,)) * 10).astype(np.int64)
+    t_host = onehot(labels, 10)
+    t_dev = [J.ConcreteNDArray.of(t_host[i * B:(i + 1) * B]) for i in range(D)]
+    devices = [J.Device(None) for _ in range(D)]
+    loss = mlp_loss(J, "tanh")
+    # each shard's labels selected by its position: a 2-input pmap body
+    t = J.ConcreteNDArray.of(t_host.reshape(D, B, 10))
+
+    def f(xx):
+        return J.JAX.pmap(lambda xs, ts: loss(params, xs, ts), devices)(xx, t).sum()
+
+    gx = J.JAX.grad(f)(x).numpy()
+    ws, bs = host_params(params)
+    xh = x.numpy()
+    for i in range(D):
+        _, _, _, ref_gx = orc.mlp_loss_grad(ws, bs, xh[i], t_host[i * B:(i + 1) * B], act="tanh",
+                                            want_gx=True, threads=8)
+        assert_rel(gx[i], ref_gx, TOL_REDUCTION, f"gx shard {i}")
+
+
+@pytest.mark.parametrize("rows,cols", [(8, 16384), (33, 1000), (4, 7)])
+def test_elementwise_sweep(J, rows, cols):
+    x = J.Random.normal(J.PRNGKey.key(1), J.Shape(rows, cols))
+    y = J.Random.uniform(J.PRNGKey.key(11), J.Shape(rows, cols), -3.0, 3.0)
+    zero = J.ConcreteNDArray.scalar(0.0)
+    lo, hi = J.ConcreteNDArray.scalar(-1.0), J.ConcreteNDArray.scalar(1.0)
+    z = J.Numpy.where(x.gt(zero), x.tanh().mul(y.sigmoid()), y.relu().clip(lo, hi))
+    s = z.sum(-1, True)
+    am = z.argmax(-1)
+    rz, rs, ram = orc.sweep(x.numpy(), y.numpy(), want_z=True)
+    assert_rel(z.numpy(), rz, TOL_ELEMENTWISE, "z")
+    assert_rel(s.numpy(), rs, TOL_REDUCTION, "row sums")
+    np.testing.assert_array_equal(am.numpy(), ram)

@@ -1,0 +1,279 @@
+"""Parity of every device op with the CPU oracle on seeded inputs.
+
+Bit-exact for BOOL/INT32/index results, the RNG streams and the IEEE
+add/sub/mul/div/max/min; FP32 transcendental unary ops within 1e-5 and
+reductions/dot within 1e-4 (relative per tensor, tests/util.py).
+"""
+import numpy as np
+import pytest
+
+from oracle import oracle as orc
+from tests.util import TOL_ELEMENTWISE, TOL_REDUCTION, assert_rel
+
+pytestmark = pytest.mark.gpu
+
+
+@pytest.fixture(scope="module")
+def J():
+    import jax4j_b200 as j
+    return j
+
+
+def dev(J, a, dtype=None):
+    a = np.asarray(a)
+    dt = dtype or {np.dtype(np.float32): J.DType.FLOAT32, np.dtype(np.int32): J.DType.INT32,
+                   np.dtype(np.bool_): J.DType.BOOL, np.dtype(np.float64): J.DType.FLOAT64,
+                   np.dtype(np.int64): J.DType.INT64}[a.dtype]
+    shape = list(a.shape) if a.ndim else [1]
+    return J.ConcreteNDArray.of(a.reshape(shape), J.Shape(shape), dt)
+
+
+def rng(seed=0):
+    return np.random.default_rng(seed)
+
+
+BIN = ["add", "sub", "mul", "div", "max", "min"]
+SHAPES = [((4097,), (4097,)), ((3,), (1,)), ((64, 130), (130,)), ((64, 130), (64, 1)),
+          ((5, 1, 7), (1, 6, 1)), ((2, 3, 4, 5), (3, 1, 5)), ((1,), (33, 17)), ((256, 1024), (256, 1024))]
+
+
+@pytest.mark.parametrize("op", BIN)
+@pytest.mark.parametrize("sa,sb", SHAPES)
+def test_binary_bit_exact(J, op, sa, sb):
+    r = rng(hash((op, sa, sb)) % 2**32)
+    a = r.standard_normal(sa).astype(np.float32)
+    b = r.standard_normal(sb).astype(np.float32)
+    if op == "div":
+        b[np.abs(b) < 1e-3] = 0.5
+    got = getattr(dev(J, a), op)(dev(J, b)).numpy()
+    ref = orc.binary(getattr(orc, op.upper()), a, b)
+    np.testing.assert_array_equal(got, ref)
+
+
+def test_binary_java_special_values(J):
+    a = np.float32([np.nan, 1, -0.0, 0.0, np.inf, -np.inf, 3, 0])
+    b = np.float32([1, np.nan, 0.0, -0.0, np.inf, 2, 0, 0])
+    for op in BIN:
+        got = getattr(dev(J, a), op)(dev(J, b)).numpy()
+        ref = orc.binary(getattr(orc, op.upper()), a, b)
+        assert np.array_equal(got, ref, equal_nan=True), op
+        real = ~np.isnan(ref)  # a NaN's sign is not observable in Java
+        assert np.array_equal(np.signbit(got[real]), np.signbit(ref[real])), op
+
+
+@pytest.mark.parametrize("op", ["gt", "ge", "lt", "le", "eq", "ne"])
+def test_compare_bit_exact(J, op):
+    r = rng(1)
+    a = r.integers(-3, 4, (64, 129)).astype(np.float32)
+    b = r.integers(-3, 4, (129,)).astype(np.float32)
+    a[0, :4] = [np.nan, 0.0, -0.0, np.inf]
+    got = getattr(dev(J, a), op)(dev(J, b)).toBoolArray().reshape(a.shape)
+    ref = orc.compare(getattr(orc, op.upper()), orc.F32, a, b).astype(bool)
+    np.testing.assert_array_equal(got, ref)
+    ai = a[1:].astype(np.int32)
+    bi = b.astype(np.int32)
+    got = getattr(dev(J, ai), op)(dev(J, bi)).toBoolArray().reshape(ai.shape)
+    np.testing.assert_array_equal(got, orc.compare(getattr(orc, op.upper()), orc.I32, ai, bi).astype(bool))
+
+
+@pytest.mark.parametrize("op", ["exp", "log", "sin", "cos", "tanh", "relu", "sigmoid"])
+@pytest.mark.parametrize("n", [1, 3, 4097, 1 << 20])
+def test_unary(J, op, n):
+    r = rng(n)
+    x = (r.standard_normal(n) * 3).astype(np.float32)
+    if op == "log":
+        x = np.abs(x) + 1e-3
+    got = getattr(dev(J, x), op)().toFloatArray()
+    ref = orc.unary(getattr(orc, op.upper()), x)
+    if op == "relu":
+        np.testing.assert_array_equal(got, ref)
+    else:
+        assert_rel(got, ref, TOL_ELEMENTWISE, op)
+
+
+CASTS = [("float32", "int32"), ("float32", "bool"), ("float32", "float64"), ("float32", "int64"),
+         ("int32", "float32"), ("int32", "bool"), ("bool", "float32"), ("bool", "int32"),
+         ("float64", "float32"), ("float64", "int32"), ("int64", "int32"), ("int64", "float32")]
+
+
+@pytest.mark.parametrize("src,dst", CASTS)
+def test_cast_bit_exact(J, src, dst):
+    r = rng(7)
+    base = np.concatenate([r.standard_normal(1000) * 1e3,
+                           [np.nan, np.inf, -np.inf, 3e10, -3e10, -0.0, 0.0, 2.5, -2.5, 1.0]])
+    np_src = {"float32": np.float32, "float64": np.float64, "int32": np.int32, "int64": np.int64,
+              "bool": np.bool_}[src]
+    if src in ("int32", "int64", "bool"):
+        base = np.nan_to_num(base, nan=0, posinf=0, neginf=0)
+        if src == "int64":
+            base = np.concatenate([base, [2**40 + 3, -(2**40) - 7]])
+        elif src == "int32":
+            base = np.clip(base, -2**31, 2**31 - 1)
+    x = base.astype(np_src)
+    D = {"float32": J.DType.FLOAT32, "float64": J.DType.FLOAT64, "int32": J.DType.INT32,
+         "int64": J.DType.INT64, "bool": J.DType.BOOL}
+    got = dev(J, x, D[src]).astype(D[dst]).numpy()
+    O = {"float32": orc.F32, "float64": orc.F64, "int32": orc.I32, "int64": orc.I64, "bool": orc.BOOL}
+    ref = orc.cast(O[src], O[dst], x.astype(np.uint8) if src == "bool" else x)
+    if dst == "bool":
+        ref = ref.astype(bool)
+    assert np.array_equal(got, ref, equal_nan=True), (src, dst)
+
+
+@pytest.mark.parametrize("n", [1, 5, 4096, 1 << 20, 3 * 1048576 + 7])
+@pytest.mark.parametrize("mean", [False, True])
+def test_reduce_all(J, n, mean):
+    x = rng(n).standard_normal(n).astype(np.float32)
+    a = dev(J, x)
+    got = (a.mean() if mean else a.sum()).toFloatArray()
+    ref = orc.reduce_all(orc.MEAN if mean else orc.SUM, x)
+    # relative to the sum of magnitudes: the order of a float sum is free
+    scale = float(np.abs(x).sum()) / (n if mean else 1)
+    assert abs(float(got[0]) - float(ref[0])) <= TOL_REDUCTION * max(scale, 1e-30)
+
+
+@pytest.mark.parametrize("shape,axis", [((4, 16384), -1), ((7, 33), 1), ((4096, 10), 1), ((8192, 64), 0),
+                                        ((3, 1000, 5), 1), ((2, 3), 0), ((1, 1), 0), ((600, 2048), 1)])
+@pytest.mark.parametrize("keep", [False, True])
+@pytest.mark.parametrize("mean", [False, True])
+def test_reduce_axis(J, shape, axis, keep, mean):
+    x = rng(sum(shape)).standard_normal(shape).astype(np.float32)
+    a = dev(J, x)
+    got = (a.mean(axis, keep) if mean else a.sum(axis, keep)).numpy()
+    ref = orc.reduce_axis(orc.MEAN_AXIS if mean else orc.SUM_AXIS, x, axis, keep)
+    assert got.shape == ref.shape
+    n = shape[axis]
+    scale = np.abs(x).sum(axis=axis, keepdims=keep) / (n if mean else 1)
+    assert np.all(np.abs(got - ref) <= TOL_REDUCTION * np.maximum(scale, 1e-30))
+
+
+@pytest.mark.parametrize("shape,axis", [((4, 16384), -1), ((100, 7), 1), ((9, 3000), 1), ((64, 5), 0),
+                                        ((3, 50, 4), 1)])
+@pytest.mark.parametrize("op", ["argmax", "argmin"])
+def test_argreduce_bit_exact(J, shape, axis, op):
+    r = rng(3)
+    x = r.integers(-5, 6, shape).astype(np.float32)  # many ties: the first must win
+    if len(shape) == 2 and shape[1] > 3:
+        x[0, 0] = np.nan          # NaN first: index 0 wins
+        x[1, 2] = np.nan          # NaN later: skipped
+        x[2, :] = -np.inf         # all equal: index 0
+    got = getattr(dev(J, x), op)(axis).numpy()
+    ref = orc.argreduce(getattr(orc, op.upper()), x, axis)
+    np.testing.assert_array_equal(got, ref)
+
+
+@pytest.mark.parametrize("gshape,tshape", [((64, 130), (130,)), ((64, 130), (64, 1)), ((64, 130), (1,)),
+                                            ((4, 5, 6), (5, 1)), ((4, 5, 6), (4, 1, 6)),
+                                            ((8192, 16), (16,)), ((3,), (2, 3)), ((6,), (2, 3)),
+                                            ((2, 3, 4, 5), (3, 1, 5))])
+def test_broadcast_like(J, gshape, tshape):
+    from jax4j_b200 import grad as G
+    g = rng(5).standard_normal(gshape).astype(np.float32)
+    got = G.broadcast_like(dev(J, g), J.Shape(tshape)).numpy()
+    ref = orc.broadcast_like(g, tshape)
+    assert_rel(got, ref, TOL_REDUCTION, f"{gshape}->{tshape}")
+
+
+def test_relu_and_maxmin_grad(J):
+    from jax4j_b200 import grad as G
+    r = rng(9)
+    g = r.standard_normal((40, 50)).astype(np.float32)
+    x = r.integers(-2, 3, (40, 50)).astype(np.float32)
+    np.testing.assert_array_equal(G.relu_grad(dev(J, g), dev(J, x)).numpy(), orc.relu_grad(g, x))
+    b = r.integers(-2, 3, (50,)).astype(np.float32)
+    for is_max in (True, False):
+        ga, gb = G.maxmin_grad(dev(J, g), dev(J, x), dev(J, b), is_max)
+        ra, rb = orc.maxmin_grad(is_max, g, x, b)
+        np.testing.assert_array_equal(ga.numpy(), ra)
+        assert_rel(gb.numpy(), rb, TOL_REDUCTION)
+
+
+@pytest.mark.parametrize("M,K,N", [(1, 1, 1), (2, 3, 4), (37, 53, 29), (128, 128, 128), (256, 784, 512),
+                                   (256, 512, 10), (300, 1000, 257), (1024, 1024, 1024)])
+@pytest.mark.parametrize("ta,tb", [(0, 0), (1, 0), (0, 1), (1, 1)])
+def test_dot(J, M, K, N, ta, tb):
+    from jax4j_b200.core import _dot_raw
+    r = rng(M * 7 + K * 3 + N)
+    A = r.uniform(-1, 1, (M, K)).astype(np.float32)
+    B = r.uniform(-1, 1, (K, N)).astype(np.float32)
+    a = dev(J, A.T.copy() if ta else A)
+    b = dev(J, B.T.copy() if tb else B)
+    got = _dot_raw(a, b, bool(ta), bool(tb), a.device()).numpy()
+    ref = orc.dot(A, B, threads=8)
+    assert_rel(got, ref, TOL_REDUCTION, f"dot {M}x{K}x{N} ta={ta} tb={tb}")
+
+
+def test_dot_public_api_and_f64(J):
+    r = rng(11)
+    A = r.uniform(-1, 1, (65, 33)).astype(np.float32)
+    B = r.uniform(-1, 1, (33, 17)).astype(np.float32)
+    got = dev(J, A).dot(dev(J, B)).toFloatArray().reshape(65, 17)
+    assert_rel(got, orc.dot(A, B), TOL_REDUCTION)
+    got64 = dev(J, A.astype(np.float64)).dot(dev(J, B.astype(np.float64))).numpy()
+    np.testing.assert_allclose(got64, A.astype(np.float64) @ B.astype(np.float64), rtol=1e-12, atol=1e-12)
+
+
+def test_transpose(J):
+    from jax4j_b200 import _lib
+    import torch
+    x = rng(1).standard_normal((37, 70)).astype(np.float32)
+    a = dev(J, x)
+    out = torch.empty(x.size, dtype=torch.float32, device="cuda")
+    _lib.call("j4c_transpose", 0, a.data_ptr(), 37, 70, out.data_ptr(), a._stream())
+    np.testing.assert_array_equal(out.cpu().numpy().reshape(70, 37), orc.transpose(x))
+
+
+@pytest.mark.parametrize("n", [1, 17, 100003])
+def test_random_streams_bit_exact(J, n):
+    key = J.PRNGKey.key(12345)
+    u = J.Random.uniform(key, J.Shape(n), -3.0, 3.0).toFloatArray()
+    np.testing.assert_array_equal(u, orc.uniform(key.state(), (n,), -3.0, 3.0))
+    g = J.Random.glorotUniform(key, J.Shape(n), 1024, 4096).toFloatArray()
+    np.testing.assert_array_equal(g, orc.glorot_uniform(key.state(), (n,), 1024, 4096))
+    z = J.Random.normal(key, J.Shape(n)).toFloatArray()
+    # Box-Muller runs in double: libm and CUDA's double log/cos may differ in
+    # the last double ulp, which can move the float by one ulp
+    assert_rel(z, orc.normal(key.state(), (n,)), 1e-6)
+    # a shard of the stream equals the same slice of the whole array
+    part = J.Random.uniform(key, J.Shape(n), -3.0, 3.0, offset=n // 3, count=n - n // 3).toFloatArray()
+    np.testing.assert_array_equal(part, u[n // 3:])
+    assert [k.state() for k in J.Random.split(key, 5)] == orc.split(key.state(), 5)
+
+
+def test_psum_slots_order(J):
+    import ctypes as C
+    from jax4j_b200 import _lib
+    r = rng(2)
+    slots = [r.standard_normal(10001).astype(np.float32) * 10 ** i for i in range(5)]
+    arrs = [dev(J, s) for s in slots]
+    import torch
+    out = torch.empty(10001, dtype=torch.float32, device="cuda")
+    ptrs = (C.c_void_p * 5)(*[a.data_ptr() for a in arrs])
+    _lib.call("j4c_psum_slots", 0, ptrs, 5, out.data_ptr(), 10001, arrs[0]._stream())
+    np.testing.assert_array_equal(out.cpu().numpy(), orc.psum(slots))
+
+
+def test_device_placement_rules(J):
+    # DevicePlacementTest.java:28-111
+    g0, g1 = J.Device(None), J.Device(None)
+    a = dev(J, np.float32([1, 2, 3])).to(g0)
+    b = dev(J, np.float32([4, 5, 6])).to(g1)
+    with pytest.raises(J.IllegalStateException, match="different devices"):
+        a.add(b)
+    c = dev(J, np.float32([4, 5, 6])).to(g0)
+    r = a.mul(c)
+    assert r.device() is g0
+    np.testing.assert_allclose(r.toFloatArray(), [4, 10, 18])
+    row = dev(J, np.float32([[1, 2, 3], [4, 5, 6]])).to(g0)
+    assert row.add(dev(J, np.float32([10, 20, 30])).to(g0)).device() is g0
+    h = J.Device.host()
+    assert dev(J, np.float32([1, 2])).to(h).add(dev(J, np.float32([1, 1])).to(h)).device() is h
+
+
+def test_empty_and_single_element(J):
+    x = dev(J, np.float32([2.0]))
+    assert x.sum().toFloatArray()[0] == 2.0
+    assert x.argmax(0).toIntArray()[0] == 0
+    e = J.ConcreteNDArray(np.zeros(0, np.float32), J.Shape(0, 3), J.DType.FLOAT32)
+    assert e.add(e).shape() == J.Shape(0, 3)
+    assert e.exp().shape() == J.Shape(0, 3)
