@@ -56,6 +56,14 @@ def parse():
     p.add_argument("--batch", type=int, default=BATCH, help="samples per GPU (profiling runs only)")
     p.add_argument("--no-cpu-baseline", action="store_true")
     p.add_argument("--no-e2e", action="store_true")
+    p.add_argument("--workload", default="dp_step", choices=["dp_step", "gemm", "sweep"],
+                   help="dp_step is the headline; gemm/sweep are single-kernel measurements "
+                        "used for profiling")
+    p.add_argument("--m", type=int, default=8192)
+    p.add_argument("--k", type=int, default=4096)
+    p.add_argument("--n", type=int, default=4096)
+    p.add_argument("--rows", type=int, default=4096)
+    p.add_argument("--cols", type=int, default=16384)
     return p.parse_args()
 
 
@@ -355,10 +363,71 @@ def run_reference(args):
     print(json.dumps(line), flush=True)
 
 
+def run_gemm(args):
+    """One FP32 dot C[M,N] = A[M,K].B[K,N] (split + tcgen05 GEMM) per step."""
+    import torch
+    import jax4j_b200 as J
+    from jax4j_b200 import core
+    torch.cuda.set_device(0)
+    M, K, N = args.m, args.k, args.n
+    dev = J.Device.defaultDevice()
+    A = J.Random.uniform(J.PRNGKey.key(2), J.Shape(M, K), -1.0, 1.0)
+    B = J.Random.uniform(J.PRNGKey.key(3), J.Shape(K, N), -1.0, 1.0)
+    for _ in range(args.warmup):
+        core._dot_raw(A, B, False, False, dev)
+    torch.cuda.synchronize()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record()
+    for _ in range(args.steps):
+        core._dot_raw(A, B, False, False, dev)
+    e1.record()
+    torch.cuda.synchronize()
+    ms = e0.elapsed_time(e1) / args.steps
+    tf = 2.0 * M * N * K / (ms / 1e3) / 1e12
+    print(json.dumps({"metric": "dot TFLOP/s (FP32 accuracy, 3xTF32)", "value": tf, "unit": "TFLOP/s",
+                      "ms_per_step": ms, "config": {"workload": f"dot {M}x{K}x{N}"},
+                      "algorithmic_bytes": 4 * (M * K + K * N + M * N)}), flush=True)
+
+
+def run_sweep(args):
+    """where(x.gt(0), tanh(x)*sigmoid(y), relu(y).clip(-1,1)), sum(-1,keep), argmax(-1)."""
+    import torch
+    import jax4j_b200 as J
+    torch.cuda.set_device(0)
+    R, Cc = args.rows, args.cols
+    x = J.Random.normal(J.PRNGKey.key(1), J.Shape(R, Cc))
+    y = J.Random.uniform(J.PRNGKey.key(11), J.Shape(R, Cc), -3.0, 3.0)
+    zero, lo, hi = (J.ConcreteNDArray.scalar(v) for v in (0.0, -1.0, 1.0))
+
+    def step():
+        z = J.Numpy.where(x.gt(zero), x.tanh().mul(y.sigmoid()), y.relu().clip(lo, hi))
+        return z.sum(-1, True), z.argmax(-1)
+
+    for _ in range(args.warmup):
+        step()
+    torch.cuda.synchronize()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record()
+    for _ in range(args.steps):
+        step()
+    e1.record()
+    torch.cuda.synchronize()
+    ms = e0.elapsed_time(e1) / args.steps
+    n = R * Cc
+    print(json.dumps({"metric": "elements/s", "value": n / (ms / 1e3), "unit": "elements/s",
+                      "ms_per_step": ms, "config": {"workload": f"sweep {R}x{Cc}"},
+                      "min_bytes_per_step": 8 * n + 8 * R,
+                      "effective_GBps": (8 * n + 8 * R) / (ms / 1e3) / 1e9}), flush=True)
+
+
 def main():
     args = parse()
     if args.impl == "reference":
         run_reference(args)
+    elif args.workload == "gemm":
+        run_gemm(args)
+    elif args.workload == "sweep":
+        run_sweep(args)
     else:
         run_ours(args)
 
