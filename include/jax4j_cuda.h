@@ -189,6 +189,24 @@ J4C_API int j4c_reduce_all(int prim, int dtype, const void *in, int64_t n, void 
 J4C_API int j4c_reduce_axis(int prim, int dtype, const void *in, int64_t outer, int64_t axis_len,
                     int64_t inner, void *out, j4c_stream stream);
 
+/* No counterpart in the reference.  The same per-axis sum/mean as
+ * j4c_reduce_axis (same kernels, same bits), for callers that cannot allocate
+ * device memory: a host runtime that hands all of the GPU's memory to its own
+ * arena at start-up and lets native code take no more, or code that must not
+ * block, since cudaFree synchronises the device and a pool allocation may
+ * stall while the pool grows.  Its only scratch -- the partial sums when the
+ * axis is split across CTAs -- lives in a static device array of
+ * J4C_REDUCE_NOALLOC_SCRATCH_BYTES that every GPU loading the library holds
+ * until the process exits; a reduction needing more is rejected with
+ * J4C_E_INVALID (use j4c_reduce_axis).  The first call on each device looks
+ * the array's address up (cudaGetSymbolAddress) and should come before any
+ * stream capture on that device.  All calls share the one array: calls
+ * whose work overlaps on the GPU (other streams, other threads) race on it;
+ * nothing needs clearing between calls. */
+#define J4C_REDUCE_NOALLOC_SCRATCH_BYTES (256 * 1024)
+J4C_API int j4c_reduce_axis_noalloc(int prim, int dtype, const void *in, int64_t outer,
+                                    int64_t axis_len, int64_t inner, void *out, j4c_stream stream);
+
 /* ConcreteNDArray.argReduceAxis (core/ConcreteNDArray.java:571-618): prim
  * ARGMAX or ARGMIN over [outer, axis_len, inner] -> int32 [outer, inner];
  * the first strict extremum wins, as the reference's sequential scan.

@@ -65,6 +65,7 @@ SIGNATURES = {
     "j4c_cast": [I32, I32, P, I64, P, P],
     "j4c_reduce_all": [I32, I32, P, I64, P, P],
     "j4c_reduce_axis": [I32, I32, P, I64, I64, I64, P, P],
+    "j4c_reduce_axis_noalloc": [I32, I32, P, I64, I64, I64, P, P],
     "j4c_argreduce": [I32, I32, P, I64, I64, I64, P, P],
     "j4c_broadcast_like": [I32, P, PI64, I32, P, PI64, I32, P],
     "j4c_relu_grad": [I32, P, P, I64, P, P],

@@ -8,6 +8,7 @@
 // adjacent columns (coalesced) and split long axes across CTAs, combining the
 // partials in a second deterministic pass.
 #include <algorithm>
+#include <mutex>
 #include <vector>
 
 #include "common.cuh"
@@ -336,6 +337,69 @@ int reduce_all_any(int dtype, const void *in, int64_t n, void *out, int mean, cu
                      dtype_name(dtype));
 }
 
+// ---- j4c_reduce_axis_noalloc: the same reduction with static scratch ----------------
+// The only scratch a per-axis reduction needs is the partial sums of a split
+// axis (splits x outer x inner values).  This array holds them for the
+// allocation-free entry point.  It lives in the library's device image, so
+// every GPU that loads the library keeps these bytes until the process
+// exits.  Host code must not pass the symbol itself to a kernel: on the host
+// it is only a stand-in, not a device address.
+static __device__ __align__(256) unsigned char g_reduce_noalloc_scratch[J4C_REDUCE_NOALLOC_SCRATCH_BYTES];
+
+// Device address of the array on the current device, looked up once per
+// device (the first call on a device does this; no allocation happens).
+static int noalloc_scratch(void **out) {
+    static std::mutex mu;
+    static std::vector<void *> ptrs;
+    int dev = 0;
+    J4C_CUDA(cudaGetDevice(&dev));
+    std::lock_guard<std::mutex> lock(mu);
+    if ((int)ptrs.size() <= dev) ptrs.resize(dev + 1, nullptr);
+    if (!ptrs[dev]) {
+        void *p = nullptr;
+        cudaError_t e = cudaGetSymbolAddress(&p, g_reduce_noalloc_scratch);
+        if (e != cudaSuccess) return cuda_status(e, "cudaGetSymbolAddress(g_reduce_noalloc_scratch)");
+        ptrs[dev] = p;
+    }
+    *out = ptrs[dev];
+    return J4C_OK;
+}
+
+// Same kernels and the same split of the axis as reduce_axis_t, so the result
+// is bit-identical to j4c_reduce_axis; only the partial-sum buffer differs.
+template <typename T>
+static int reduce_axis_noalloc_t(const T *in, int64_t outer, int64_t axis, int64_t inner, T *out,
+                                 int mean, cudaStream_t s) {
+    if (inner == 1) return reduce_axis_t<T>(in, outer, axis, inner, out, mean, s);  // no scratch
+    int64_t gx = ceil_div(inner, 256);
+    int64_t gy = std::min<int64_t>(outer, 65535);
+    int64_t ctas = gx * gy;
+    int64_t want = (int64_t)sm_count() * 4;
+    int64_t splits = 1;
+    if (ctas < want && axis >= 64) splits = std::min<int64_t>({ceil_div(want, ctas), axis / 32, 64});
+    int64_t chunk = ceil_div(axis, splits);
+    splits = ceil_div(axis, chunk);
+    if (splits == 1) return reduce_axis_t<T>(in, outer, axis, inner, out, mean, s);  // no scratch
+    const size_t need = sizeof(T) * (size_t)(splits * outer * inner);
+    if (need > (size_t)J4C_REDUCE_NOALLOC_SCRATCH_BYTES)
+        return set_error(J4C_E_INVALID,
+                         "j4c_reduce_axis_noalloc: this reduction needs %zu bytes of scratch, more "
+                         "than the %d-byte static maximum; call j4c_reduce_axis instead",
+                         need, (int)J4C_REDUCE_NOALLOC_SCRATCH_BYTES);
+    void *part = nullptr;
+    int rc = noalloc_scratch(&part);
+    if (rc) return rc;
+    // Every partial is written before it is read, so the array's previous
+    // contents never matter and nothing is cleared.
+    dim3 grid((unsigned)gx, (unsigned)gy, (unsigned)splits);
+    col_reduce_kernel<T><<<grid, 256, 0, s>>>(in, outer, axis, inner, chunk, out, (T *)part, mean);
+    J4C_LAUNCH_CHECK("col_reduce_kernel");
+    int64_t n = outer * inner;
+    combine_parts_kernel<T><<<grid_for(n, 256), 256, 0, s>>>((const T *)part, (int)splits, n, axis, out, mean);
+    J4C_LAUNCH_CHECK("combine_parts_kernel");
+    return J4C_OK;
+}
+
 }  // namespace j4c
 
 using namespace j4c;
@@ -360,6 +424,26 @@ int j4c_reduce_axis(int prim, int dtype, const void *in, int64_t outer, int64_t 
         return j4c_fill(dtype, out, outer * inner, prim == J4C_MEAN_AXIS ? NAN : 0.0, stream);
     return reduce_axis_any(dtype, in, outer, axis_len, inner, out, prim == J4C_MEAN_AXIS,
                            as_stream(stream));
+}
+
+// See include/jax4j_cuda.h: allocation-free variant of j4c_reduce_axis.
+int j4c_reduce_axis_noalloc(int prim, int dtype, const void *in, int64_t outer, int64_t axis_len,
+                            int64_t inner, void *out, j4c_stream stream) {
+    J4C_REQUIRE(prim == J4C_SUM_AXIS || prim == J4C_MEAN_AXIS, "j4c_reduce_axis_noalloc: primitive %d",
+                prim);
+    J4C_REQUIRE(in && out && outer >= 0 && axis_len >= 0 && inner >= 0,
+                "j4c_reduce_axis_noalloc: bad arguments");
+    if (outer * inner == 0) return J4C_OK;
+    if (axis_len == 0)
+        return j4c_fill(dtype, out, outer * inner, prim == J4C_MEAN_AXIS ? NAN : 0.0, stream);
+    cudaStream_t s = as_stream(stream);
+    const int mean = prim == J4C_MEAN_AXIS;
+    if (dtype == J4C_FLOAT32)
+        return reduce_axis_noalloc_t<float>((const float *)in, outer, axis_len, inner, (float *)out, mean, s);
+    if (dtype == J4C_FLOAT64)
+        return reduce_axis_noalloc_t<double>((const double *)in, outer, axis_len, inner, (double *)out, mean, s);
+    return set_error(J4C_E_INVALID, "reduction requires FLOAT32 or FLOAT64 operands, got %s",
+                     dtype_name(dtype));
 }
 
 int j4c_argreduce(int prim, int dtype, const void *in, int64_t outer, int64_t axis_len,
