@@ -251,7 +251,9 @@ def run_ours(args):
                "ms_per_step": e2e_ms / args.steps, "loss": float(losses[0])}
 
     if rank != 0:
-        distributed.barrier() if world > 1 else None
+        if world > 1:
+            distributed.barrier()
+            distributed.shutdown()
         return
     peaks = _measured_peaks()
     peak = peaks.get("bf16_tflops_sustained") or peaks.get("bf16_tflops")
@@ -281,6 +283,7 @@ def run_ours(args):
     print(json.dumps(line), flush=True)
     if world > 1:
         distributed.barrier()
+        distributed.shutdown()
 
 
 def _measured_peaks() -> dict:

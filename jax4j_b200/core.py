@@ -468,7 +468,7 @@ class ConcreteNDArray(NDArray):
         """core/ConcreteNDArray.java:148-151: re-tags; moves the buffer only if the
         target is another physical GPU."""
         t = self._t
-        if t.device.index != device.ordinal():
+        if t.device.type == "cuda" and t.device.index != device.ordinal():
             t = t.to(device.torch_device())
         return ConcreteNDArray._wrap(t, self._shape, self._dtype, device)
 

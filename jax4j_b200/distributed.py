@@ -44,15 +44,19 @@ def state() -> Optional[SpmdState]:
     return _state
 
 
-def initialize(timeout_s: float = 120.0) -> SpmdState:
-    """Joins the job described by RANK/WORLD_SIZE/LOCAL_RANK/MASTER_ADDR/MASTER_PORT."""
+def initialize(timeout_s: float = 120.0, collective_factory=None) -> SpmdState:
+    """Joins the job described by RANK/WORLD_SIZE/LOCAL_RANK/MASTER_ADDR/MASTER_PORT.
+
+    collective_factory(rank, world) -> collective replaces the NCCL group
+    (used to run the executor's host logic on CPU processes in tests)."""
     global _state
     if _state is not None:
         return _state
     rank = int(os.environ.get("RANK", "0"))
     world = int(os.environ.get("WORLD_SIZE", "1"))
     local_rank = int(os.environ.get("LOCAL_RANK", str(rank)))
-    torch.cuda.set_device(local_rank)
+    if collective_factory is None:
+        torch.cuda.set_device(local_rank)
     local = Device.cuda(local_rank)
     Device.setDefault(local)
     if not dist.is_initialized():
@@ -60,6 +64,10 @@ def initialize(timeout_s: float = 120.0) -> SpmdState:
         os.environ.setdefault("MASTER_PORT", "29533")
         dist.init_process_group("gloo", rank=rank, world_size=world,
                                 timeout=datetime.timedelta(seconds=timeout_s))
+    devices = [local if r == rank else Device(None, f"rank{r}") for r in range(world)]
+    if collective_factory is not None:
+        _state = SpmdState(rank, world, local_rank, 0, collective_factory(rank, world), devices)
+        return _state
     uid = bytearray(128)
     if rank == 0:
         buf = (C.c_char * 128)()
@@ -71,14 +79,28 @@ def initialize(timeout_s: float = 120.0) -> SpmdState:
     comm = C.c_void_p()
     call("j4c_comm_init_rank", C.cast(raw, C.c_void_p), 128, world, rank, local_rank,
          int(timeout_s * 1000) if timeout_s else COMM_TIMEOUT_MS, C.byref(comm))
-    comms = [None] * world
-    comms[0] = comm.value
     # The collective object is indexed by PmapContext.deviceIndex (= rank);
     # every index resolves to this process's own communicator.
     coll = NcclCollective([comm.value] * world)
-    devices = [local if r == rank else Device(None, f"rank{r}") for r in range(world)]
     _state = SpmdState(rank, world, local_rank, comm.value, coll, devices)
     return _state
+
+
+HEARTBEAT_S = float(os.environ.get("J4C_HEARTBEAT_S", "30"))
+
+
+def heartbeat() -> None:
+    """Host-side liveness check run before a pmap call enqueues any
+    collective: every rank must reach it within HEARTBEAT_S.  A rank that has
+    left (between steps) is reported here, on the host, before this rank
+    launches a kernel that would wait for it on the GPU."""
+    from .pmap import CollectiveError
+    if _state is None or _state.world_size == 1 or not dist.is_initialized():
+        return
+    try:
+        dist.monitored_barrier(timeout=datetime.timedelta(seconds=HEARTBEAT_S))
+    except RuntimeError as e:
+        raise CollectiveError(f"pmap: a peer rank did not reach the step within {HEARTBEAT_S} s: {e}") from e
 
 
 def global_devices() -> List[Device]:
@@ -96,7 +118,8 @@ def shutdown() -> None:
     """Destroys the communicator and the process group."""
     global _state
     if _state is not None:
-        call("j4c_comm_destroy", _state.comm)
+        if _state.comm:
+            call("j4c_comm_destroy", _state.comm)
         _state = None
     if dist.is_initialized():
         dist.destroy_process_group()

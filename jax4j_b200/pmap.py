@@ -293,6 +293,11 @@ def run_parallel(D: int, task: Callable[[int], object], collective) -> list:
     return results
 
 
+def _heartbeat():
+    from . import distributed
+    distributed.heartbeat()
+
+
 def _bind(device: Device):
     return torch.cuda.device(device.ordinal())
 
@@ -320,6 +325,7 @@ def run_forward(fn: Callable, inputs: Sequence[NDArray], devices: Sequence[Devic
     mode, obj = _placement(devices)
     if mode == "spmd":
         st = obj
+        _heartbeat()
         shards = _local_inputs(inputs, D, st.rank)
         PmapContext.set(PmapContext(st.rank, D, st.collective))
         try:
@@ -365,6 +371,7 @@ def run_forward_jaxpr(body, devices: Sequence[Device], shards: List[List[Concret
     mode, obj = _placement(devices)
     if mode == "spmd":
         st = obj
+        _heartbeat()
         PmapContext.set(PmapContext(st.rank, D, st.collective))
         try:
             res = forward_interpret(_body_on(body, devices[st.rank]),
@@ -396,6 +403,7 @@ def run_backward_jaxpr(body, devices: Sequence[Device], in_shards: List[List[Con
     mode, obj = _placement(devices)
     if mode == "spmd":
         st = obj
+        _heartbeat()
         r = st.rank
         PmapContext.set(PmapContext(r, D, st.collective))
         try:

@@ -1,0 +1,73 @@
+"""pmap across GPUs: in-process (one host thread per GPU, NCCL communicators
+from ncclCommInitAll) and one process per GPU (torchrun, NCCL group with a
+host heartbeat).  Skipped when fewer than two GPUs are visible."""
+import os
+import subprocess
+import sys
+
+import numpy as np
+import pytest
+
+from oracle import oracle as orc
+from tests.util import TOL_REDUCTION, assert_rel
+
+ROOT = os.path.dirname(os.path.dirname(os.path.abspath(__file__)))
+pytestmark = pytest.mark.gpu
+
+
+def _ngpus():
+    import torch
+    return torch.cuda.device_count()
+
+
+needs2 = pytest.mark.skipif("_ngpus() < 2", reason="needs two GPUs")
+
+
+@needs2
+def test_in_process_pmap_over_two_gpus():
+    import jax4j_b200 as J
+    devices = [J.Device.cuda(0), J.Device.cuda(1)]
+    # PmapTest.java:68-76 / :92-100 / :118-138 with one shard per GPU
+    x = J.ConcreteNDArray.of(np.float32([[10, 20], [10, 20]]))
+    r = J.JAX.pmap(lambda s: J.Lax.psum(s), devices)(x)
+    np.testing.assert_allclose(r.toFloatArray(), [20, 40, 20, 40], atol=1e-5)
+    x = J.ConcreteNDArray.of(np.float32([[1, 2], [3, 4]]))
+    r = J.JAX.pmap(lambda s: J.Lax.allGather(s, 2).sum(), devices)(x)
+    np.testing.assert_allclose(r.toFloatArray(), [10, 10], atol=1e-5)
+    two = J.ConcreteNDArray.scalar(2.0)
+    fn = lambda v: J.JAX.pmap(lambda s: J.Lax.psum(s.mul(s).sum()).div(two), devices)(v).sum()
+    np.testing.assert_allclose(J.JAX.grad(fn)(x).toFloatArray(), [2, 4, 6, 8], atol=1e-3)
+
+
+def _torchrun(scenario, out, env_extra=None, timeout=240):
+    env = dict(os.environ)
+    env.update(env_extra or {})
+    cmd = [sys.executable, "-m", "torch.distributed.run", "--nnodes=1", "--nproc-per-node", "2",
+           "--master-addr", "127.0.0.1", "--master-port", str(29600 + os.getpid() % 300),
+           os.path.join(ROOT, "tests", "spmd_gpu_worker.py"), "--scenario", scenario, "--out", out]
+    return subprocess.run(cmd, env=env, capture_output=True, text=True, timeout=timeout)
+
+
+@needs2
+def test_one_process_per_gpu_dp_step_matches_oracle(tmp_path):
+    out = str(tmp_path / "dp.npz")
+    r = _torchrun("dp_step", out)
+    assert r.returncode == 0, r.stderr[-2000:]
+    z = np.load(out)
+    z1 = np.load(out + ".rank1.npz")
+    ws, bs = [z["w1"], z["w2"]], [z["b1"], z["b2"]]
+    per = [orc.mlp_loss_grad(ws, bs, z["x"], z["t"], act="tanh", threads=8),
+           orc.mlp_loss_grad(ws, bs, z1["x"], z1["t"], act="tanh", threads=8)]
+    np.testing.assert_allclose(z["losses"], [per[0][0], per[1][0]], rtol=TOL_REDUCTION)
+    for i, k in enumerate(["w1", "w2"]):
+        assert_rel(z["g_" + k], orc.psum([per[0][1][i], per[1][1][i]]), TOL_REDUCTION, k)
+    for i, k in enumerate(["b1", "b2"]):
+        assert_rel(z["g_" + k], orc.psum([per[0][2][i], per[1][2][i]]), TOL_REDUCTION, k)
+
+
+@needs2
+def test_rank_leaving_between_steps_is_reported_on_the_host(tmp_path):
+    out = str(tmp_path / "leave.txt")
+    r = _torchrun("leave", out, {"J4C_HEARTBEAT_S": "5", "NCCL_NVLS_ENABLE": "0"})
+    assert os.path.exists(out), r.stderr[-2000:]
+    assert open(out).read().startswith("CollectiveError")
