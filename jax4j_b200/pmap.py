@@ -25,6 +25,7 @@ import ctypes as C
 import os
 import threading
 from concurrent.futures import ThreadPoolExecutor
+from concurrent.futures import wait as wait_futures
 from typing import Callable, List, Optional, Sequence
 
 import torch
@@ -171,9 +172,18 @@ class NcclCollective:
     def __init__(self, comms: List[int]):
         self.comms = comms
         self.num_devices = len(comms)
+        self.aborted = False
 
     def abort(self):
-        pass  # each rank's wait is bounded by the communicator's own deadline
+        """Aborts every rank's communicator, which ends NCCL kernels waiting on
+        a peer; the communicators cannot be used afterwards."""
+        for c in self.comms:
+            _lib.lib().j4c_comm_abort(c)
+        self.aborted = True
+        with _comm_lock:
+            for k, v in list(_comm_cache.items()):
+                if v is self:
+                    del _comm_cache[k]
 
     def psum(self, index: int, x: ConcreteNDArray) -> ConcreteNDArray:
         out = torch.empty_like(x.tensor())
@@ -266,9 +276,14 @@ def _placement(devices: Sequence[Device]):
         f"{list(ordinals)}")
 
 
+RUN_TIMEOUT_S = float(os.environ.get("J4C_PMAP_TIMEOUT_S", "600"))
+
+
 def run_parallel(D: int, task: Callable[[int], object], collective) -> list:
     """Pmap.runParallel (Pmap.java:135-166): one thread per shard; the first
-    failure aborts the collective so no peer blocks, and is re-raised."""
+    failure aborts the collective so no peer blocks, and is re-raised.  The
+    wait for the shards is bounded: past RUN_TIMEOUT_S the collective is
+    aborted (which also ends device-side waits) and CollectiveError raised."""
     results = [None] * D
     errors: List[Optional[BaseException]] = [None] * D
 
@@ -283,8 +298,17 @@ def run_parallel(D: int, task: Callable[[int], object], collective) -> list:
     if D == 1:
         run(0)
     else:
-        with ThreadPoolExecutor(max_workers=D) as ex:
-            list(ex.map(run, range(D)))
+        ex = ThreadPoolExecutor(max_workers=D)
+        futs = [ex.submit(run, i) for i in range(D)]
+        done, pending = wait_futures(futs, timeout=RUN_TIMEOUT_S)
+        if pending:
+            if collective is not None:
+                collective.abort()
+            wait_futures(pending, timeout=30)
+            ex.shutdown(wait=False, cancel_futures=True)
+            raise CollectiveError(f"pmap: shards did not finish within {RUN_TIMEOUT_S} s; "
+                                  "the collective was aborted")
+        ex.shutdown(wait=True)
     first = next((e for e in errors if e is not None and not isinstance(e, CollectiveError)), None)
     if first is None:
         first = next((e for e in errors if e is not None), None)
@@ -335,12 +359,16 @@ def run_forward(fn: Callable, inputs: Sequence[NDArray], devices: Sequence[Devic
         return _gather_stack(st, res)
     shards = [split(x, D) for x in inputs]
     coll = SlotCollective(D) if mode == "slots" else obj
+    # Every shard reaches its device before any shard thread starts: a copy
+    # issued from a shard thread could queue behind a peer's collective
+    # kernel on the source GPU and wait for itself.
+    placed = [[s[i].to(devices[i]) for s in shards] for i in range(D)]
 
     def task(i):
         with _bind(devices[i]):
             PmapContext.set(PmapContext(i, D, coll))
             try:
-                return fn(*[s[i].to(devices[i]) for s in shards])
+                return fn(*placed[i])
             finally:
                 PmapContext.set(None)
 
@@ -380,13 +408,14 @@ def run_forward_jaxpr(body, devices: Sequence[Device], shards: List[List[Concret
             PmapContext.set(None)
         return _gather_stack(st, res)
     coll = SlotCollective(D) if mode == "slots" else obj
+    bodies = [_body_on(body, devices[i]) for i in range(D)]  # placed before any thread starts
+    placed = [[s[i].to(devices[i]) for s in shards] for i in range(D)]
 
     def task(i):
         with _bind(devices[i]):
             PmapContext.set(PmapContext(i, D, coll))
             try:
-                return forward_interpret(_body_on(body, devices[i]),
-                                         [s[i].to(devices[i]) for s in shards])[0]
+                return forward_interpret(bodies[i], placed[i])[0]
             finally:
                 PmapContext.set(None)
 
@@ -415,14 +444,15 @@ def run_backward_jaxpr(body, devices: Sequence[Device], in_shards: List[List[Con
         stacked = [split(_gather_stack(st, g), D) for g in g_local]
         return [[stacked[k][i] for k in range(len(g_local))] for i in range(D)]
     coll = SlotCollective(D) if mode == "slots" else obj
+    bodies = [_body_on(body, devices[i]) for i in range(D)]  # placed before any thread starts
+    placed = [[s[i].to(devices[i]) for s in in_shards] for i in range(D)]
+    seeds = [g_shards[i].to(devices[i]) for i in range(D)]
 
     def task(i):
         with _bind(devices[i]):
             PmapContext.set(PmapContext(i, D, coll))
             try:
-                return backward_interpret(_body_on(body, devices[i]),
-                                          [s[i].to(devices[i]) for s in in_shards],
-                                          [g_shards[i].to(devices[i])])
+                return backward_interpret(bodies[i], placed[i], [seeds[i]])
             finally:
                 PmapContext.set(None)
 
