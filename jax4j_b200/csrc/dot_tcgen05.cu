@@ -32,6 +32,7 @@
 #include <cuda.h>
 #include <cudaTypedefs.h>
 
+#include <cstdlib>
 #include <mutex>
 #include <vector>
 
@@ -41,16 +42,20 @@ namespace j4c {
 namespace tc {
 
 constexpr int BM = 128;           // rows of a CTA tile (TMEM lanes)
-constexpr int BK = 32;            // FP32 elements per 128-byte swizzled smem row
+constexpr int KPAD = 32;          // K is zero-padded to a multiple of this in the split
 constexpr int UMMA_K = 8;         // K of one tf32 MMA instruction (32 bytes)
+constexpr int CHUNK_K = 256;      // K accumulated in TMEM before promotion to registers
 constexpr int kEpiWarps = 8;      // two warps per TMEM lane quadrant
 constexpr int kThreads = 64 + 32 * kEpiWarps;
-constexpr int CHUNK_KB = 8;       // k-blocks (of BK) accumulated in TMEM before promotion
 constexpr int kStatusTimeout = 0x7C05;
 constexpr uint64_t kWaitLimitNs = 2000000000ull;  // 2 s without progress
 
-template <int BN, int STAGES>
+// BK = FP32 elements per smem row of a stage: 32 (128-byte swizzle) or 16
+// (64-byte swizzle, half the bytes per stage, so twice the stages fit).
+template <int BN, int STAGES, int BK>
 struct Cfg {
+    static_assert(BK == 32 || BK == 16, "BK is 32 (SW128) or 16 (SW64)");
+    static constexpr int CHUNK_KB = CHUNK_K / BK;
     static constexpr int A_BYTES = BM * BK * 4;
     static constexpr int B_BYTES = BN * BK * 4;
     static constexpr int STAGE_BYTES = 2 * A_BYTES + 2 * B_BYTES;
@@ -138,15 +143,19 @@ __device__ __forceinline__ void tc_fence_after() {
     asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
 }
 
-// K-major operand tile, 128-byte swizzle: 8-row core-matrix groups are 1024 B
-// apart (SBO); the leading-dimension offset is unused for swizzled K-major.
-__device__ __forceinline__ uint64_t smem_desc_sw128(uint32_t addr) {
+// K-major operand tile with a BK*4-byte swizzle: 8-row core-matrix groups are
+// 8 rows * row bytes apart (SBO); the leading-dimension offset is unused for
+// swizzled K-major.  Layout type 2 = 128-byte swizzle, 4 = 64-byte swizzle.
+template <int BK>
+__device__ __forceinline__ uint64_t smem_desc(uint32_t addr) {
+    constexpr uint64_t row_bytes = BK * 4;
+    constexpr uint64_t layout = BK == 32 ? 2 : 4;
     uint64_t d = 0;
     d |= (uint64_t)((addr & 0x3FFFF) >> 4);
-    d |= (uint64_t)1 << 16;             // LBO (unused here)
-    d |= (uint64_t)(1024 >> 4) << 32;   // SBO
-    d |= (uint64_t)1 << 46;             // descriptor version for sm_100
-    d |= (uint64_t)2 << 61;             // SWIZZLE_128B
+    d |= (uint64_t)1 << 16;                      // LBO (unused here)
+    d |= (uint64_t)((8 * row_bytes) >> 4) << 32; // SBO
+    d |= (uint64_t)1 << 46;                      // descriptor version for sm_100
+    d |= layout << 61;
     return d;
 }
 
@@ -196,12 +205,13 @@ __device__ __forceinline__ void tile_coords(int t, int num_m, int num_n, int &mt
     nt = r / gsize;
 }
 
-template <int BN, int STAGES>
+template <int BN, int STAGES, int BK>
 __global__ void __launch_bounds__(kThreads, 1)
 gemm_3xtf32_kernel(const __grid_constant__ CUtensorMap tAh, const __grid_constant__ CUtensorMap tAl,
                    const __grid_constant__ CUtensorMap tBh, const __grid_constant__ CUtensorMap tBl,
                    float *__restrict__ C, int M, int N, int num_kb, int vec_store, int *status) {
-    using Q = Cfg<BN, STAGES>;
+    using Q = Cfg<BN, STAGES, BK>;
+    constexpr int CHUNK_KB = Q::CHUNK_KB;
     extern __shared__ uint8_t smem_raw[];
     uint8_t *smem = reinterpret_cast<uint8_t *>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
     Ctl<STAGES> *ctl = reinterpret_cast<Ctl<STAGES> *>(smem + STAGES * Q::STAGE_BYTES);
@@ -308,8 +318,8 @@ gemm_3xtf32_kernel(const __grid_constant__ CUtensorMap tAh, const __grid_constan
 #pragma unroll
                         for (int kk = 0; kk < BK / UMMA_K; kk++) {
                             const uint32_t off = kk * UMMA_K * 4;
-                            const uint64_t ah = smem_desc_sw128(sa_hi + off), al = smem_desc_sw128(sa_lo + off);
-                            const uint64_t bh = smem_desc_sw128(sb_hi + off), bl = smem_desc_sw128(sb_lo + off);
+                            const uint64_t ah = smem_desc<BK>(sa_hi + off), al = smem_desc<BK>(sa_lo + off);
+                            const uint64_t bh = smem_desc<BK>(sb_hi + off), bl = smem_desc<BK>(sb_lo + off);
                             mma_tf32(dcol, al, bh, idesc, (kb > kb0 || kk > 0) ? 1u : 0u);
                             mma_tf32(dcol, ah, bl, idesc, 1u);
                             mma_tf32(dcol, ah, bh, idesc, 1u);
@@ -398,33 +408,65 @@ __device__ __forceinline__ float tf32_round(float x) {
     return __uint_as_float(r & 0xFFFFE000u);
 }
 
-// src is [rows, K] row-major (kr = 0) or [K, rows] row-major (kr = 1).
-__global__ void __launch_bounds__(256) split_tf32_kernel(const float *__restrict__ src, int64_t rows,
-                                                         int64_t K, int64_t Kp, int kr,
-                                                         float *__restrict__ hi,
-                                                         float *__restrict__ lo) {
-    __shared__ float tile[32][33];
-    const int64_t k0 = (int64_t)blockIdx.x * 32, r0 = (int64_t)blockIdx.y * 32;
-    const int tx = threadIdx.x, ty = threadIdx.y;  // 32 x 8
-    if (!kr) {
-        for (int j = ty; j < 32; j += 8) {
-            const int64_t r = r0 + j, k = k0 + tx;
-            tile[j][tx] = (r < rows && k < K) ? src[r * K + k] : 0.0f;
+// Direct operand ([rows, K] row-major): 4 consecutive k per thread step,
+// 16-byte loads when K allows, 16-byte stores of hi and lo (Kp % 4 == 0).
+__global__ void __launch_bounds__(256) split_direct_kernel(const float *__restrict__ src, int64_t rows,
+                                                           int64_t K, int64_t Kp, int vec,
+                                                           float *__restrict__ hi,
+                                                           float *__restrict__ lo) {
+    const int64_t q = Kp / 4;
+    const int64_t n = rows * q;
+    for (int64_t v = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; v < n;
+         v += (int64_t)gridDim.x * blockDim.x) {
+        const int64_t r = v / q, k = (v - r * q) * 4;
+        float x[4];
+        const float *p = src + r * K + k;
+        if (vec && k + 4 <= K) {
+            const float4 t = __ldg(reinterpret_cast<const float4 *>(p));
+            x[0] = t.x; x[1] = t.y; x[2] = t.z; x[3] = t.w;
+        } else {
+#pragma unroll
+            for (int j = 0; j < 4; j++) x[j] = (k + j < K) ? p[j] : 0.0f;
         }
-    } else {
-        for (int j = ty; j < 32; j += 8) {
-            const int64_t k = k0 + j, r = r0 + tx;
-            tile[tx][j] = (r < rows && k < K) ? src[k * rows + r] : 0.0f;
+        float h[4], l[4];
+#pragma unroll
+        for (int j = 0; j < 4; j++) {
+            h[j] = tf32_round(x[j]);
+            l[j] = tf32_round(x[j] - h[j]);
+        }
+        *reinterpret_cast<float4 *>(hi + r * Kp + k) = make_float4(h[0], h[1], h[2], h[3]);
+        *reinterpret_cast<float4 *>(lo + r * Kp + k) = make_float4(l[0], l[1], l[2], l[3]);
+    }
+}
+
+// Transposed operand (stored [K, rows] row-major): 64 x 64 tiles through
+// shared memory, reads coalesced along rows, writes coalesced along k.
+__global__ void __launch_bounds__(256) split_transpose_kernel(const float *__restrict__ src, int64_t rows,
+                                                              int64_t K, int64_t Kp,
+                                                              float *__restrict__ hi,
+                                                              float *__restrict__ lo) {
+    __shared__ float tile[64][65];
+    const int64_t k0 = (int64_t)blockIdx.x * 64, r0 = (int64_t)blockIdx.y * 64;
+    const int tx = threadIdx.x & 31, ty = threadIdx.x >> 5;  // 32 x 8
+    for (int j = ty; j < 64; j += 8) {  // tile[r][k] <- src[k][r]
+        const int64_t k = k0 + j;
+        for (int i = tx; i < 64; i += 32) {
+            const int64_t r = r0 + i;
+            tile[i][j] = (r < rows && k < K) ? src[k * rows + r] : 0.0f;
         }
     }
     __syncthreads();
-    for (int j = ty; j < 32; j += 8) {
-        const int64_t r = r0 + j, k = k0 + tx;
-        if (r < rows) {
-            const float x = tile[j][tx];
-            const float h = tf32_round(x);
-            hi[r * Kp + k] = h;
-            lo[r * Kp + k] = tf32_round(x - h);
+    for (int j = ty; j < 64; j += 8) {
+        const int64_t r = r0 + j;
+        if (r >= rows) continue;
+        for (int i = tx; i < 64; i += 32) {
+            const int64_t k = k0 + i;
+            if (k < Kp) {
+                const float x = tile[j][i];
+                const float h = tf32_round(x);
+                hi[r * Kp + k] = h;
+                lo[r * Kp + k] = tf32_round(x - h);
+            }
         }
     }
 }
@@ -443,24 +485,25 @@ static PFN_cuTensorMapEncodeTiled_v12000 encode_fn() {
     return fn;
 }
 
-static int make_map(CUtensorMap *map, const float *base, int64_t rows, int64_t Kp, int box_rows) {
+static int make_map(CUtensorMap *map, const float *base, int64_t rows, int64_t Kp, int box_rows, int bk) {
     auto fn = encode_fn();
     if (!fn) return set_error(J4C_E_CUDA, "cuTensorMapEncodeTiled is unavailable");
     cuuint64_t dims[2] = {(cuuint64_t)Kp, (cuuint64_t)rows};
     cuuint64_t strides[1] = {(cuuint64_t)Kp * 4};
-    cuuint32_t box[2] = {(cuuint32_t)BK, (cuuint32_t)box_rows};
+    cuuint32_t box[2] = {(cuuint32_t)bk, (cuuint32_t)box_rows};
     cuuint32_t estr[2] = {1, 1};
     CUresult r = fn(map, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 2, const_cast<float *>(base), dims, strides, box,
-                    estr, CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
+                    estr, CU_TENSOR_MAP_INTERLEAVE_NONE,
+                    bk == 32 ? CU_TENSOR_MAP_SWIZZLE_128B : CU_TENSOR_MAP_SWIZZLE_64B,
                     CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
     if (r != CUDA_SUCCESS) return set_error(J4C_E_CUDA, "cuTensorMapEncodeTiled failed (%d)", (int)r);
     return J4C_OK;
 }
 
-template <int BN, int STAGES>
+template <int BN, int STAGES, int BK>
 static int launch_gemm(const float *ah, const float *al, const float *bh, const float *bl, float *c,
                        int64_t M, int64_t N, int64_t Kp, cudaStream_t s) {
-    using Q = Cfg<BN, STAGES>;
+    using Q = Cfg<BN, STAGES, BK>;
     static std::mutex mu;
     static std::vector<char> configured;
     int dev = 0;
@@ -469,22 +512,22 @@ static int launch_gemm(const float *ah, const float *al, const float *bh, const 
         std::lock_guard<std::mutex> lock(mu);
         if ((int)configured.size() <= dev) configured.resize(dev + 1, 0);
         if (!configured[dev]) {
-            J4C_CUDA(cudaFuncSetAttribute(gemm_3xtf32_kernel<BN, STAGES>,
+            J4C_CUDA(cudaFuncSetAttribute(gemm_3xtf32_kernel<BN, STAGES, BK>,
                                           cudaFuncAttributeMaxDynamicSharedMemorySize, Q::SMEM_BYTES));
             configured[dev] = 1;
         }
     }
     CUtensorMap mAh, mAl, mBh, mBl;
     int rc;
-    if ((rc = make_map(&mAh, ah, M, Kp, BM)) || (rc = make_map(&mAl, al, M, Kp, BM)) ||
-        (rc = make_map(&mBh, bh, N, Kp, BN)) || (rc = make_map(&mBl, bl, N, Kp, BN)))
+    if ((rc = make_map(&mAh, ah, M, Kp, BM, BK)) || (rc = make_map(&mAl, al, M, Kp, BM, BK)) ||
+        (rc = make_map(&mBh, bh, N, Kp, BN, BK)) || (rc = make_map(&mBl, bl, N, Kp, BN, BK)))
         return rc;
     int *status = device_status_ptr();
     if (!status) return set_error(J4C_E_OOM, "no device status word");
     const int64_t tiles = ceil_div(M, BM) * ceil_div(N, BN);
     const int grid = (int)std::min<int64_t>(tiles, sm_count());
     const int vec = (N % 4 == 0) && aligned16(c);
-    gemm_3xtf32_kernel<BN, STAGES><<<grid, kThreads, Q::SMEM_BYTES, s>>>(
+    gemm_3xtf32_kernel<BN, STAGES, BK><<<grid, kThreads, Q::SMEM_BYTES, s>>>(
         mAh, mAl, mBh, mBl, c, (int)M, (int)N, (int)(Kp / BK), vec, status);
     J4C_LAUNCH_CHECK("gemm_3xtf32_kernel");
     return J4C_OK;
@@ -492,9 +535,15 @@ static int launch_gemm(const float *ah, const float *al, const float *bh, const 
 
 static int launch_split(const float *src, int64_t rows, int64_t K, int64_t Kp, int kr, float *hi,
                         float *lo, cudaStream_t s) {
-    dim3 grid((unsigned)(Kp / 32), (unsigned)ceil_div(rows, 32));
-    split_tf32_kernel<<<grid, dim3(32, 8), 0, s>>>(src, rows, K, Kp, kr, hi, lo);
-    J4C_LAUNCH_CHECK("split_tf32_kernel");
+    if (!kr) {
+        const int vec = (K % 4 == 0) && aligned16(src);
+        split_direct_kernel<<<grid_for(rows * (Kp / 4), 256), 256, 0, s>>>(src, rows, K, Kp, vec, hi, lo);
+        J4C_LAUNCH_CHECK("split_direct_kernel");
+    } else {
+        dim3 grid((unsigned)ceil_div(Kp, 64), (unsigned)ceil_div(rows, 64));
+        split_transpose_kernel<<<grid, 256, 0, s>>>(src, rows, K, Kp, hi, lo);
+        J4C_LAUNCH_CHECK("split_transpose_kernel");
+    }
     return J4C_OK;
 }
 
@@ -503,18 +552,18 @@ static int launch_split(const float *src, int64_t rows, int64_t K, int64_t Kp, i
 bool tc_gemm_supported(int64_t M, int64_t K, int64_t N) {
     // int32 coordinates/extents in the kernel and the split grid's y limit
     return M >= 1 && N >= 1 && K >= 1 && M < (1ll << 31) && N < (1ll << 31) &&
-           ceil_div(M, 32) < 65536 && ceil_div(N, 32) < 65536 && K < (1ll << 30);
+           ceil_div(M, 64) < 65536 && ceil_div(N, 64) < 65536 && K < (1ll << 30);
 }
 
 int tc_gemm_workspace(int64_t M, int64_t K, int64_t N, size_t *bytes) {
-    const int64_t Kp = ceil_div(K, tc::BK) * tc::BK;
+    const int64_t Kp = ceil_div(K, tc::KPAD) * tc::KPAD;
     *bytes = (size_t)(M + N) * (size_t)Kp * 2 * sizeof(float);
     return J4C_OK;
 }
 
 int tc_gemm_f32(const float *a, const float *b, float *c, int64_t M, int64_t K, int64_t N,
                 int trans_a, int trans_b, void *ws, size_t ws_bytes, cudaStream_t s) {
-    const int64_t Kp = ceil_div(K, tc::BK) * tc::BK;
+    const int64_t Kp = ceil_div(K, tc::KPAD) * tc::KPAD;
     float *ah = static_cast<float *>(ws);
     float *al = ah + M * Kp;
     float *bh = al + M * Kp;
@@ -525,7 +574,12 @@ int tc_gemm_f32(const float *a, const float *b, float *c, int64_t M, int64_t K, 
     if ((rc = tc::launch_split(a, M, K, Kp, trans_a ? 1 : 0, ah, al, s))) return rc;
     // op(B) = B [K,N]: the GEMM wants it K-major [N,K]
     if ((rc = tc::launch_split(b, N, K, Kp, trans_b ? 0 : 1, bh, bl, s))) return rc;
-    return tc::launch_gemm<256, 2>(ah, al, bh, bl, c, M, N, Kp, s);
+    static const int variant = [] {
+        const char *v = getenv("J4C_GEMM_VARIANT");
+        return v ? atoi(v) : 1;
+    }();
+    if (variant == 0) return tc::launch_gemm<256, 2, 32>(ah, al, bh, bl, c, M, N, Kp, s);
+    return tc::launch_gemm<256, 4, 16>(ah, al, bh, bl, c, M, N, Kp, s);
 }
 
 }  // namespace j4c
