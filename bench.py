@@ -402,23 +402,36 @@ def run_sweep(args):
     y = J.Random.uniform(J.PRNGKey.key(11), J.Shape(R, Cc), -3.0, 3.0)
     zero, lo, hi = (J.ConcreteNDArray.scalar(v) for v in (0.0, -1.0, 1.0))
 
-    def step():
-        z = J.Numpy.where(x.gt(zero), x.tanh().mul(y.sigmoid()), y.relu().clip(lo, hi))
+    def sweep(xx, yy):
+        z = J.Numpy.where(xx.gt(zero), xx.tanh().mul(yy.sigmoid()), yy.relu().clip(lo, hi))
         return z.sum(-1, True), z.argmax(-1)
 
-    for _ in range(args.warmup):
-        step()
-    torch.cuda.synchronize()
-    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-    e0.record()
-    for _ in range(args.steps):
-        step()
-    e1.record()
-    torch.cuda.synchronize()
-    ms = e0.elapsed_time(e1) / args.steps
+    jitted = J.JAX.jit(sweep)
+
+    def step():
+        return jitted(x, y)
+
+    from jax4j_b200 import grad as _g
+
+    def timed(fused: bool) -> float:
+        _g.FUSION = fused
+        for _ in range(args.warmup):
+            step()
+        torch.cuda.synchronize()
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0.record()
+        for _ in range(args.steps):
+            step()
+        e1.record()
+        torch.cuda.synchronize()
+        return e0.elapsed_time(e1) / args.steps
+
+    ms_unfused = timed(False)
+    ms = timed(True)
     n = R * Cc
     print(json.dumps({"metric": "elements/s", "value": n / (ms / 1e3), "unit": "elements/s",
-                      "ms_per_step": ms, "config": {"workload": f"sweep {R}x{Cc}"},
+                      "ms_per_step": ms, "ms_per_step_unfused": ms_unfused,
+                      "config": {"workload": f"sweep {R}x{Cc} via JAX.jit"},
                       "min_bytes_per_step": 8 * n + 8 * R,
                       "effective_GBps": (8 * n + 8 * R) / (ms / 1e3) / 1e9}), flush=True)
 

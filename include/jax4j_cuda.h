@@ -265,6 +265,54 @@ J4C_API int j4c_dot_ws(int dtype, const void *a, const void *b, void *c, int64_t
 J4C_API size_t j4c_dot_workspace_size(int dtype, int64_t M, int64_t K, int64_t N);
 
 /* ------------------------------------------------------------------ */
+/* Fused elementwise programs: replace TornadoJitCompiler.compile       */
+/* (backend/TornadoJitCompiler.java:82-246), which runs one kernel per   */
+/* Jaxpr equation, with one generated kernel per chain.                  */
+/* ------------------------------------------------------------------ */
+
+/* A program works on a [rows, cols] view of the chain's shape (cols = the
+ * last dimension).  Each input is read with one of four broadcast patterns. */
+#define J4C_BCAST_FULL 0   /* [rows, cols] */
+#define J4C_BCAST_ROW 1    /* [cols]: one value per column, shared by all rows */
+#define J4C_BCAST_COL 2    /* [rows, 1]: one value per row */
+#define J4C_BCAST_SCALAR 3 /* a single value */
+
+/* Instruction opcodes beyond the primitive ordinals. */
+#define J4C_OP_INPUT (-1)     /* the value of input slot `a` */
+#define J4C_OP_CONST (-2)     /* the constant `value` */
+#define J4C_OP_RELU_GRAD (-3) /* Grad.reluGrad (api/Grad.java:593-597): b > 0 ? a : 0 */
+
+typedef struct {
+    int32_t op;    /* primitive ordinal (ADD..MIN, EXP..SIGMOID, GT..NE, CAST) or J4C_OP_* */
+    int32_t dtype; /* dtype of the result (FLOAT32, FLOAT64, INT32 or BOOL) */
+    int32_t a, b;  /* operand instruction indices (-1 unused); for INPUT, a = input slot */
+    double value;  /* for CONST */
+} j4c_insn;
+
+typedef struct {
+    int32_t n_insns;
+    const j4c_insn *insns; /* in dependency order */
+    int32_t n_inputs;      /* <= 16 */
+    const int32_t *input_dtype;
+    const int32_t *input_bcast;
+    int32_t n_outputs;         /* <= 16; each written as a [rows, cols] array */
+    const int32_t *output_insn;
+    int32_t n_tails;           /* <= 8; one value per row */
+    const int32_t *tail_op;    /* SUM_AXIS, MEAN_AXIS (-> insn dtype), ARGMAX, ARGMIN (-> INT32) */
+    const int32_t *tail_insn;
+} j4c_program;
+
+/* Generates, compiles (NVRTC, sm_100a) and caches the program's kernels on
+ * the current device; *handle stays valid for the process lifetime.  Calls
+ * with an identical program return the same handle. */
+J4C_API int j4c_fused_compile(const j4c_program *prog, void **handle);
+/* Runs a compiled program: inputs/outputs/tails are arrays of device
+ * pointers in slot order.  Elementwise results equal the unfused kernels'
+ * bit for bit; tails are deterministic tree reductions of each row. */
+J4C_API int j4c_fused_launch(void *handle, int64_t rows, int64_t cols, const void *const *inputs,
+                             void *const *outputs, void *const *tails, j4c_stream stream);
+
+/* ------------------------------------------------------------------ */
 /* Random (api/Random.java:39-150): SplitMix64 streams, bit-exact       */
 /* ------------------------------------------------------------------ */
 

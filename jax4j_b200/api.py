@@ -59,7 +59,9 @@ class JAX:
     @staticmethod
     def jit(fn: Callable) -> Callable:
         """JAX.jit (JAX.java:92-125): traced once per input signature, then the
-        cached Jaxpr is executed; transparent inside another trace."""
+        cached Jaxpr is executed -- its elementwise chains as fused generated
+        kernels (jax4j_b200/fusion.py) -- and transparent inside another
+        trace.  A function may return a tuple of arrays."""
         cache = {}
 
         def jitted(*args):
@@ -70,7 +72,8 @@ class JAX:
             if jaxpr is None:
                 jaxpr = _grad.make_jaxpr(fn, *args)
                 cache[key] = jaxpr
-            return _grad.forward_interpret(jaxpr, list(args))[0]
+            outs = _grad.forward_interpret(jaxpr, list(args))
+            return tuple(outs) if jaxpr.__dict__.get("_tuple_out") else outs[0]
 
         jitted.cache = cache
         return jitted

@@ -1,0 +1,446 @@
+// fused.cu -- generated kernels for fused elementwise chains with row-reduction
+// tails (j4c_fused_compile / j4c_fused_launch).
+//
+// The reference's "JIT" (backend/TornadoJitCompiler.java:82-246) compiles a
+// Jaxpr into one TornadoVM task per equation, so a chain of k elementwise
+// ops streams its arrays through memory k times.  Here the host side groups a
+// chain into a small SSA program; this file turns the program into CUDA C++,
+// compiles it once per device with NVRTC for sm_100a, and launches it: every
+// input is read once, only the values needed later are written, and
+// reductions over the last axis (sum/mean/argmax/argmin) are computed in the
+// same pass.  Elementwise arithmetic uses the same rounding rules as the
+// unfused kernels (explicit round-to-nearest ops, no FMA contraction, Java's
+// max/min and cast rules), so fused and unfused elementwise results agree bit
+// for bit.
+#include <nvrtc.h>
+
+#include <algorithm>
+#include <cinttypes>
+#include <cstring>
+#include <map>
+#include <memory>
+#include <mutex>
+#include <sstream>
+#include <string>
+#include <vector>
+
+#include "common.cuh"
+
+namespace j4c {
+namespace fused {
+
+constexpr int kMaxIn = 16, kMaxOut = 16, kMaxTail = 8;
+
+struct Args {
+    const void *in[kMaxIn];
+    void *out[kMaxOut];
+    void *tail[kMaxTail];
+};
+
+struct Entry {
+    cudaLibrary_t library = nullptr;
+    cudaKernel_t flat = nullptr, rows_warp = nullptr, rows_block = nullptr;
+    bool needs_rows = false;  // tails or row/column-broadcast inputs
+    int n_in = 0, n_out = 0, n_tail = 0;
+};
+
+static const char *kPreamble = R"(
+typedef long long i64;
+#define J_INF __longlong_as_double(0x7ff0000000000000LL)
+struct Args { const void *in[16]; void *out[16]; void *tail[8]; };
+__device__ __forceinline__ float j_add(float a, float b) { return __fadd_rn(a, b); }
+__device__ __forceinline__ float j_sub(float a, float b) { return __fsub_rn(a, b); }
+__device__ __forceinline__ float j_mul(float a, float b) { return __fmul_rn(a, b); }
+__device__ __forceinline__ float j_div(float a, float b) { return __fdiv_rn(a, b); }
+__device__ __forceinline__ double j_add(double a, double b) { return __dadd_rn(a, b); }
+__device__ __forceinline__ double j_sub(double a, double b) { return __dsub_rn(a, b); }
+__device__ __forceinline__ double j_mul(double a, double b) { return __dmul_rn(a, b); }
+__device__ __forceinline__ double j_div(double a, double b) { return __ddiv_rn(a, b); }
+__device__ __forceinline__ bool j_neg(float a) { return __float_as_int(a) < 0; }
+__device__ __forceinline__ bool j_neg(double a) { return __double_as_longlong(a) < 0; }
+template <class T> __device__ __forceinline__ T j_max(T a, T b) {
+    if (a != a) return a;
+    if (a == T(0) && b == T(0) && j_neg(a)) return b;
+    return (a >= b) ? a : b;
+}
+template <class T> __device__ __forceinline__ T j_min(T a, T b) {
+    if (a != a) return a;
+    if (a == T(0) && b == T(0) && j_neg(b)) return b;
+    return (a <= b) ? a : b;
+}
+__device__ __forceinline__ int j_d2i(double v) {
+    if (v != v) return 0;
+    if (v >= 2147483647.0) return 2147483647;
+    if (v <= -2147483648.0) return (-2147483647 - 1);
+    return (int)v;
+}
+__device__ __forceinline__ i64 j_d2l(double v) {
+    if (v != v) return 0;
+    if (v >= 9223372036854775807.0) return 9223372036854775807LL;
+    if (v <= -9223372036854775808.0) return (-9223372036854775807LL - 1);
+    return (i64)v;
+}
+template <class T> __device__ __forceinline__ T j_warp_sum(T v) {
+    for (int o = 16; o > 0; o >>= 1) v = j_add(v, __shfl_xor_sync(0xffffffffu, v, o));
+    return v;
+}
+template <class T, bool MAX> __device__ __forceinline__ void j_warp_arg(T &best, int &bi) {
+    for (int o = 16; o > 0; o >>= 1) {
+        T v = __shfl_xor_sync(0xffffffffu, best, o);
+        int i = __shfl_xor_sync(0xffffffffu, bi, o);
+        if ((MAX ? v > best : v < best) || (v == best && i < bi)) { best = v; bi = i; }
+    }
+}
+)";
+
+static const char *ctype(int dt) {
+    switch (dt) {
+    case J4C_FLOAT32: return "float";
+    case J4C_FLOAT64: return "double";
+    case J4C_INT32: return "int";
+    case J4C_INT64: return "i64";
+    case J4C_BOOL: return "unsigned char";
+    default: return nullptr;
+    }
+}
+
+static bool is_float(int dt) { return dt == J4C_FLOAT32 || dt == J4C_FLOAT64; }
+
+static std::string const_literal(int dt, double v) {
+    char buf[96];
+    if (dt == J4C_FLOAT32) {
+        float f = (float)v;
+        uint32_t u;
+        memcpy(&u, &f, 4);
+        snprintf(buf, sizeof(buf), "__int_as_float(0x%08x)", u);
+    } else if (dt == J4C_FLOAT64) {
+        uint64_t u;
+        memcpy(&u, &v, 8);
+        snprintf(buf, sizeof(buf), "__longlong_as_double(0x%016" PRIx64 "LL)", u);
+    } else if (dt == J4C_INT32) {
+        snprintf(buf, sizeof(buf), "(int)%lld", (long long)v);
+    } else if (dt == J4C_INT64) {
+        snprintf(buf, sizeof(buf), "(i64)%lldLL", (long long)v);
+    } else {
+        snprintf(buf, sizeof(buf), "(unsigned char)%d", v != 0.0 ? 1 : 0);
+    }
+    return buf;
+}
+
+// Validates the program; returns an error code or J4C_OK.
+static int validate(const j4c_program *p) {
+    J4C_REQUIRE(p && p->insns && p->n_insns > 0, "fused program: no instructions");
+    J4C_REQUIRE(p->n_inputs >= 0 && p->n_inputs <= kMaxIn, "fused program: at most %d inputs", kMaxIn);
+    J4C_REQUIRE(p->n_outputs >= 0 && p->n_outputs <= kMaxOut, "fused program: at most %d outputs", kMaxOut);
+    J4C_REQUIRE(p->n_tails >= 0 && p->n_tails <= kMaxTail, "fused program: at most %d tails", kMaxTail);
+    J4C_REQUIRE(p->n_outputs + p->n_tails > 0, "fused program: nothing to write");
+    for (int i = 0; i < p->n_inputs; i++) {
+        J4C_REQUIRE(ctype(p->input_dtype[i]) && p->input_bcast[i] >= 0 && p->input_bcast[i] <= 3,
+                    "fused program: bad input %d", i);
+    }
+    for (int i = 0; i < p->n_insns; i++) {
+        const j4c_insn &q = p->insns[i];
+        J4C_REQUIRE(ctype(q.dtype), "fused program: insn %d has bad dtype %d", i, q.dtype);
+        auto opnd = [&](int k) { return k >= 0 && k < i; };
+        switch (q.op) {
+        case J4C_OP_INPUT:
+            J4C_REQUIRE(q.a >= 0 && q.a < p->n_inputs && p->input_dtype[q.a] == q.dtype,
+                        "fused program: insn %d reads a bad input", i);
+            break;
+        case J4C_OP_CONST: break;
+        case J4C_OP_RELU_GRAD:
+            J4C_REQUIRE(opnd(q.a) && opnd(q.b) && is_float(q.dtype) && p->insns[q.a].dtype == q.dtype &&
+                            p->insns[q.b].dtype == q.dtype,
+                        "fused program: bad relu_grad at %d", i);
+            break;
+        case J4C_ADD: case J4C_SUB: case J4C_MUL: case J4C_DIV: case J4C_MAX: case J4C_MIN:
+            J4C_REQUIRE(opnd(q.a) && opnd(q.b) && is_float(q.dtype) && p->insns[q.a].dtype == q.dtype &&
+                            p->insns[q.b].dtype == q.dtype,
+                        "fused program: bad binary op at %d", i);
+            break;
+        case J4C_EXP: case J4C_LOG: case J4C_SIN: case J4C_COS: case J4C_TANH: case J4C_RELU:
+        case J4C_SIGMOID:
+            J4C_REQUIRE(opnd(q.a) && is_float(q.dtype) && p->insns[q.a].dtype == q.dtype,
+                        "fused program: bad unary op at %d", i);
+            break;
+        case J4C_GT: case J4C_GE: case J4C_LT: case J4C_LE: case J4C_EQ: case J4C_NE:
+            J4C_REQUIRE(opnd(q.a) && opnd(q.b) && q.dtype == J4C_BOOL &&
+                            p->insns[q.a].dtype == p->insns[q.b].dtype && p->insns[q.a].dtype != J4C_BOOL,
+                        "fused program: bad comparison at %d", i);
+            break;
+        case J4C_CAST: J4C_REQUIRE(opnd(q.a), "fused program: bad cast at %d", i); break;
+        default: return set_error(J4C_E_INVALID, "fused program: unsupported op %d at %d", q.op, i);
+        }
+    }
+    for (int k = 0; k < p->n_outputs; k++)
+        J4C_REQUIRE(p->output_insn[k] >= 0 && p->output_insn[k] < p->n_insns, "fused program: bad output");
+    for (int k = 0; k < p->n_tails; k++) {
+        int t = p->tail_insn[k], op = p->tail_op[k];
+        J4C_REQUIRE(t >= 0 && t < p->n_insns && is_float(p->insns[t].dtype), "fused program: bad tail");
+        J4C_REQUIRE(op == J4C_SUM_AXIS || op == J4C_MEAN_AXIS || op == J4C_ARGMAX || op == J4C_ARGMIN,
+                    "fused program: bad tail op %d", op);
+    }
+    return J4C_OK;
+}
+
+// Per-element body: computes every instruction for element (r, j) / idx.
+static std::string gen_body(const j4c_program *p, bool flat) {
+    std::ostringstream o;
+    for (int i = 0; i < p->n_insns; i++) {
+        const j4c_insn &q = p->insns[i];
+        const char *T = ctype(q.dtype);
+        o << "        " << T << " v" << i << " = ";
+        switch (q.op) {
+        case J4C_OP_INPUT: {
+            int b = p->input_bcast[q.a];
+            const char *idx = flat ? (b == J4C_BCAST_SCALAR ? "0" : "idx")
+                                   : (b == J4C_BCAST_FULL ? "(r * C + j)"
+                                      : b == J4C_BCAST_ROW ? "j" : b == J4C_BCAST_COL ? "r" : "0");
+            o << "((const " << T << " *)a.in[" << q.a << "])[" << idx << "];\n";
+            continue;
+        }
+        case J4C_OP_CONST: o << const_literal(q.dtype, q.value) << ";\n"; continue;
+        case J4C_OP_RELU_GRAD: o << "(v" << q.b << " > (" << T << ")0) ? v" << q.a << " : (" << T << ")0;\n"; continue;
+        case J4C_ADD: o << "j_add(v" << q.a << ", v" << q.b << ");\n"; continue;
+        case J4C_SUB: o << "j_sub(v" << q.a << ", v" << q.b << ");\n"; continue;
+        case J4C_MUL: o << "j_mul(v" << q.a << ", v" << q.b << ");\n"; continue;
+        case J4C_DIV: o << "j_div(v" << q.a << ", v" << q.b << ");\n"; continue;
+        case J4C_MAX: o << "j_max(v" << q.a << ", v" << q.b << ");\n"; continue;
+        case J4C_MIN: o << "j_min(v" << q.a << ", v" << q.b << ");\n"; continue;
+        case J4C_GT: o << "(unsigned char)(v" << q.a << " > v" << q.b << ");\n"; continue;
+        case J4C_GE: o << "(unsigned char)(v" << q.a << " >= v" << q.b << ");\n"; continue;
+        case J4C_LT: o << "(unsigned char)(v" << q.a << " < v" << q.b << ");\n"; continue;
+        case J4C_LE: o << "(unsigned char)(v" << q.a << " <= v" << q.b << ");\n"; continue;
+        case J4C_EQ: o << "(unsigned char)(v" << q.a << " == v" << q.b << ");\n"; continue;
+        case J4C_NE: o << "(unsigned char)(v" << q.a << " != v" << q.b << ");\n"; continue;
+        default: break;
+        }
+        const bool f = q.dtype == J4C_FLOAT32;
+        std::string x = "v" + std::to_string(q.a);
+        switch (q.op) {
+        case J4C_EXP: o << (f ? "expf(" : "exp(") << x << ");\n"; break;
+        case J4C_LOG: o << (f ? "logf(" : "log(") << x << ");\n"; break;
+        case J4C_SIN: o << (f ? "sinf(" : "sin(") << x << ");\n"; break;
+        case J4C_COS: o << (f ? "cosf(" : "cos(") << x << ");\n"; break;
+        case J4C_TANH: o << (f ? "tanhf(" : "tanh(") << x << ");\n"; break;
+        case J4C_RELU: o << "j_max((" << T << ")0, " << x << ");\n"; break;
+        case J4C_SIGMOID:
+            o << (f ? "__fdiv_rn(1.0f, __fadd_rn(1.0f, expf(-" : "__ddiv_rn(1.0, __dadd_rn(1.0, exp(-") << x
+              << ")));\n";
+            break;
+        case J4C_CAST: {
+            int src = p->insns[q.a].dtype, dst = q.dtype;
+            if (dst == J4C_BOOL) o << "(unsigned char)(" << x << " != 0);\n";
+            else if (src == J4C_BOOL) o << "(" << T << ")(" << x << " ? 1 : 0);\n";
+            else if (dst == J4C_INT32 && is_float(src)) o << "j_d2i((double)" << x << ");\n";
+            else if (dst == J4C_INT32) o << "(int)(unsigned int)(unsigned long long)(i64)" << x << ";\n";
+            else if (dst == J4C_INT64 && is_float(src)) o << "j_d2l((double)" << x << ");\n";
+            else o << "(" << T << ")" << x << ";\n";
+            break;
+        }
+        default: o << "0;\n"; break;
+        }
+    }
+    for (int k = 0; k < p->n_outputs; k++) {
+        int i = p->output_insn[k];
+        o << "        ((" << ctype(p->insns[i].dtype) << " *)a.out[" << k << "])[" << (flat ? "idx" : "(r * C + j)")
+          << "] = v" << i << ";\n";
+    }
+    return o.str();
+}
+
+static std::string gen_source(const j4c_program *p, bool *needs_rows) {
+    bool rows = p->n_tails > 0;
+    for (int i = 0; i < p->n_inputs; i++)
+        if (p->input_bcast[i] == J4C_BCAST_ROW || p->input_bcast[i] == J4C_BCAST_COL) rows = true;
+    *needs_rows = rows;
+    std::ostringstream o;
+    o << kPreamble;
+    if (!rows) {
+        o << "extern \"C\" __global__ void __launch_bounds__(256) k_flat(i64 N, Args a) {\n"
+             "    for (i64 idx = blockIdx.x * (i64)blockDim.x + threadIdx.x; idx < N;\n"
+             "         idx += (i64)gridDim.x * blockDim.x) {\n"
+          << gen_body(p, true) << "    }\n}\n";
+        return o.str();
+    }
+    // Row kernels: TPR threads per row (32: a warp per row, 256: a CTA per row).
+    for (int tpr : {32, 256}) {
+        const char *name = tpr == 32 ? "k_rows_warp" : "k_rows_block";
+        o << "extern \"C\" __global__ void __launch_bounds__(256) " << name << "(i64 R, i64 C, Args a) {\n";
+        if (tpr == 256) o << "    __shared__ double s_d[8]; __shared__ float s_f[8]; __shared__ int s_i[8];\n";
+        o << "    const int sub = threadIdx.x % " << tpr << ";\n"
+          << "    const int rows_per_cta = 256 / " << tpr << ";\n"
+          << "    for (i64 r0 = (i64)blockIdx.x * rows_per_cta; r0 < R; r0 += (i64)gridDim.x * rows_per_cta) {\n"
+          << "      const i64 r = r0 + threadIdx.x / " << tpr << ";\n";
+        for (int k = 0; k < p->n_tails; k++) {
+            const char *T = ctype(p->insns[p->tail_insn[k]].dtype);
+            int op = p->tail_op[k];
+            if (op == J4C_SUM_AXIS || op == J4C_MEAN_AXIS) {
+                o << "      " << T << " acc" << k << " = (" << T << ")0;\n";
+            } else {
+                bool mx = op == J4C_ARGMAX;
+                o << "      " << T << " best" << k << " = (" << T << ")(" << (mx ? "-" : "") << "J_INF);\n"
+                  << "      int bi" << k << " = 2147483647; int nan" << k << " = 0;\n";
+            }
+        }
+        o << "      if (r < R) {\n"
+          << "      for (i64 j = sub; j < C; j += " << tpr << ") {\n"
+          << gen_body(p, false);
+        for (int k = 0; k < p->n_tails; k++) {
+            int op = p->tail_op[k], t = p->tail_insn[k];
+            if (op == J4C_SUM_AXIS || op == J4C_MEAN_AXIS) {
+                o << "        acc" << k << " = j_add(acc" << k << ", v" << t << ");\n";
+            } else {
+                bool mx = op == J4C_ARGMAX;
+                // first strict extremum wins; a NaN in the first slot wins; later NaNs are skipped
+                o << "        if (j == 0 && v" << t << " != v" << t << ") nan" << k << " = 1;\n"
+                  << "        if (v" << t << " == v" << t << " && (v" << t << (mx ? " > " : " < ") << "best" << k
+                  << " || (v" << t << " == best" << k << " && (int)j < bi" << k << "))) { best" << k << " = v" << t
+                  << "; bi" << k << " = (int)j; }\n";
+            }
+        }
+        o << "      }\n      }\n";
+        // reductions
+        for (int k = 0; k < p->n_tails; k++) {
+            int op = p->tail_op[k];
+            const char *T = ctype(p->insns[p->tail_insn[k]].dtype);
+            const bool dbl = p->insns[p->tail_insn[k]].dtype == J4C_FLOAT64;
+            const char *S = dbl ? "s_d" : "s_f";
+            if (op == J4C_SUM_AXIS || op == J4C_MEAN_AXIS) {
+                o << "      acc" << k << " = j_warp_sum(acc" << k << ");\n";
+                if (tpr == 256) {
+                    o << "      if ((threadIdx.x & 31) == 0) " << S << "[threadIdx.x >> 5] = acc" << k << ";\n"
+                      << "      __syncthreads();\n"
+                      << "      if (threadIdx.x < 32) { " << T << " t = threadIdx.x < 8 ? " << S
+                      << "[threadIdx.x] : (" << T << ")0; acc" << k << " = j_warp_sum(t); }\n"
+                      << "      __syncthreads();\n";
+                }
+                o << "      if (sub == 0 && r < R) ((" << T << " *)a.tail[" << k << "])[r] = "
+                  << (op == J4C_MEAN_AXIS ? "j_div(acc" + std::to_string(k) + ", (" + T + ")C)"
+                                          : "acc" + std::to_string(k))
+                  << ";\n";
+            } else {
+                const char *mx = op == J4C_ARGMAX ? "true" : "false";
+                o << "      j_warp_arg<" << T << ", " << mx << ">(best" << k << ", bi" << k << ");\n";
+                if (tpr == 256) {
+                    o << "      if ((threadIdx.x & 31) == 0) { " << S << "[threadIdx.x >> 5] = best" << k
+                      << "; s_i[threadIdx.x >> 5] = bi" << k << "; }\n"
+                      << "      __syncthreads();\n"
+                      << "      if (threadIdx.x < 32) { best" << k << " = threadIdx.x < 8 ? " << S
+                      << "[threadIdx.x] : (" << T << ")(" << (op == J4C_ARGMAX ? "-" : "") << "J_INF); bi" << k
+                      << " = threadIdx.x < 8 ? s_i[threadIdx.x] : 2147483647; j_warp_arg<" << T << ", " << mx
+                      << ">(best" << k << ", bi" << k << "); }\n"
+                      << "      __syncthreads();\n";
+                }
+                o << "      if (sub == 0 && r < R) ((int *)a.tail[" << k << "])[r] = (nan" << k << " || bi" << k
+                  << " == 2147483647) ? 0 : bi" << k << ";\n";
+            }
+        }
+        o << "    }\n}\n";
+    }
+    return o.str();
+}
+
+static std::mutex g_mu;
+static std::map<std::string, std::unique_ptr<Entry>> g_cache;  // key: device + source
+
+static int compile(const std::string &src, Entry *e) {
+    nvrtcProgram prog;
+    nvrtcResult nr = nvrtcCreateProgram(&prog, src.c_str(), "j4c_fused.cu", 0, nullptr, nullptr);
+    if (nr != NVRTC_SUCCESS) return set_error(J4C_E_CUDA, "nvrtcCreateProgram: %s", nvrtcGetErrorString(nr));
+    // Same contraction setting as the library's own nvcc build, so the CUDA
+    // math functions (expf, tanhf, ...) compile to the same code; the chain's
+    // own arithmetic uses explicit round-to-nearest ops that never contract.
+    const char *opts[] = {"--gpu-architecture=sm_100a", "-std=c++17", "--fmad=true"};
+    nr = nvrtcCompileProgram(prog, 3, opts);
+    if (nr != NVRTC_SUCCESS) {
+        size_t n = 0;
+        nvrtcGetProgramLogSize(prog, &n);
+        std::string log(n, '\0');
+        nvrtcGetProgramLog(prog, &log[0]);
+        nvrtcDestroyProgram(&prog);
+        return set_error(J4C_E_CUDA, "fused kernel compilation failed: %s", log.c_str());
+    }
+    size_t n = 0;
+    nvrtcGetCUBINSize(prog, &n);
+    std::vector<char> cubin(n);
+    nvrtcGetCUBIN(prog, cubin.data());
+    nvrtcDestroyProgram(&prog);
+    J4C_CUDA(cudaLibraryLoadData(&e->library, cubin.data(), nullptr, nullptr, 0, nullptr, nullptr, 0));
+    if (e->needs_rows) {
+        J4C_CUDA(cudaLibraryGetKernel(&e->rows_warp, e->library, "k_rows_warp"));
+        J4C_CUDA(cudaLibraryGetKernel(&e->rows_block, e->library, "k_rows_block"));
+    } else {
+        J4C_CUDA(cudaLibraryGetKernel(&e->flat, e->library, "k_flat"));
+    }
+    return J4C_OK;
+}
+
+}  // namespace fused
+}  // namespace j4c
+
+using namespace j4c;
+using namespace j4c::fused;
+
+extern "C" {
+
+int j4c_fused_compile(const j4c_program *prog, void **handle) {
+    J4C_REQUIRE(handle, "j4c_fused_compile: handle is NULL");
+    int rc = validate(prog);
+    if (rc) return rc;
+    int dev = 0;
+    J4C_CUDA(cudaGetDevice(&dev));
+    J4C_CUDA(cudaSetDevice(dev));  // makes the device's primary context current for the driver API
+    bool needs_rows = false;
+    std::string src = gen_source(prog, &needs_rows);
+    std::string key = std::to_string(dev) + "\n" + src;
+    std::lock_guard<std::mutex> lock(g_mu);
+    auto it = g_cache.find(key);
+    if (it != g_cache.end()) {
+        *handle = it->second.get();
+        return J4C_OK;
+    }
+    auto e = std::make_unique<Entry>();
+    e->needs_rows = needs_rows;
+    e->n_in = prog->n_inputs;
+    e->n_out = prog->n_outputs;
+    e->n_tail = prog->n_tails;
+    rc = compile(src, e.get());
+    if (rc) return rc;
+    *handle = e.get();
+    g_cache.emplace(key, std::move(e));
+    return J4C_OK;
+}
+
+int j4c_fused_launch(void *handle, int64_t rows, int64_t cols, const void *const *inputs,
+                     void *const *outputs, void *const *tails, j4c_stream stream) {
+    J4C_REQUIRE(handle, "j4c_fused_launch: NULL handle");
+    J4C_REQUIRE(rows >= 0 && cols >= 0, "j4c_fused_launch: negative extent");
+    const Entry *e = static_cast<const Entry *>(handle);
+    if (rows == 0 || cols == 0) return J4C_OK;
+    Args a;
+    memset(&a, 0, sizeof(a));
+    for (int i = 0; i < e->n_in; i++) a.in[i] = inputs[i];
+    for (int i = 0; i < e->n_out; i++) a.out[i] = outputs[i];
+    for (int i = 0; i < e->n_tail; i++) a.tail[i] = tails[i];
+    cudaStream_t s = as_stream(stream);
+    cudaError_t r;
+    if (!e->needs_rows) {
+        int64_t N = rows * cols;
+        void *params[] = {&N, &a};
+        r = cudaLaunchKernel((const void *)e->flat, dim3(grid_for(N, 256)), dim3(256), params, 0, s);
+    } else if (cols >= 512) {
+        void *params[] = {&rows, &cols, &a};
+        unsigned g = (unsigned)std::min<int64_t>(rows, (int64_t)sm_count() * 8);
+        r = cudaLaunchKernel((const void *)e->rows_block, dim3(g), dim3(256), params, 0, s);
+    } else {
+        void *params[] = {&rows, &cols, &a};
+        unsigned g = (unsigned)std::min<int64_t>(ceil_div(rows, 8), (int64_t)sm_count() * 8);
+        r = cudaLaunchKernel((const void *)e->rows_warp, dim3(g), dim3(256), params, 0, s);
+    }
+    count_launch();
+    if (r != cudaSuccess) return cuda_status(r, "cudaLaunchKernel(fused)");
+    return J4C_OK;
+}
+
+}  // extern "C"

@@ -19,6 +19,7 @@ rules while doing less work:
 """
 from __future__ import annotations
 
+import os
 from typing import Callable, Dict, List
 
 import torch
@@ -50,6 +51,11 @@ def zeros(shape: Shape, dtype: DType, device=None) -> ConcreteNDArray:
 
 def zeros_like(x: NDArray) -> ConcreteNDArray:
     return zeros(x.shape(), x.dtype(), x.device())
+
+
+def _zeros_for(var: Var, like: ConcreteNDArray) -> ConcreteNDArray:
+    """Zero cotangent of a Var (Grad.zerosLike, Grad.java:884-887) next to `like`."""
+    return zeros(var.shape, var.dtype, like.device())
 
 
 # ---------------------------------------------------------------------------
@@ -133,22 +139,41 @@ def _needs_grad(jaxpr: Jaxpr) -> set:
     return need
 
 
-def fill_forward_values(jaxpr: Jaxpr, args: List[NDArray]) -> Dict[int, NDArray]:
-    """Grad.fillForwardValues (Grad.java:192-211)."""
+# Elementwise chains of an interpreted Jaxpr run as fused generated kernels
+# (jax4j_b200/fusion.py); J4C_FUSION=0 runs every equation on its own.
+FUSION = os.environ.get("J4C_FUSION", "1") != "0"
+
+
+def _evaluate(jaxpr: Jaxpr, args: List[NDArray], keep_for_vjp: bool) -> Dict[int, NDArray]:
     values: Dict[int, NDArray] = dict(jaxpr.consts)
     if len(args) != len(jaxpr.inVars):
         raise IllegalArgumentException(f"expected {len(jaxpr.inVars)} arguments, got {len(args)}")
     for v, a in zip(jaxpr.inVars, args):
         values[v.id] = a
+    if FUSION and all(isinstance(a, ConcreteNDArray) for a in values.values()):
+        from . import fusion
+        for kind, item in fusion.plan_for(jaxpr, keep_for_vjp).steps:
+            if kind == "eq":
+                inputs = [values[v.id] for v in item.inputs]
+                values[item.outputs[0].id] = execute_primitive(item.primitive, item, inputs)
+            else:
+                fusion.run_group(item, values)
+        return values
     for eq in jaxpr.equations:
         inputs = [values[v.id] for v in eq.inputs]
         values[eq.outputs[0].id] = execute_primitive(eq.primitive, eq, inputs)
     return values
 
 
+def fill_forward_values(jaxpr: Jaxpr, args: List[NDArray]) -> Dict[int, NDArray]:
+    """Grad.fillForwardValues (Grad.java:192-211): every value a VJP rule
+    reads is kept; values only used inside a fused chain are not written."""
+    return _evaluate(jaxpr, args, True)
+
+
 def forward_interpret(jaxpr: Jaxpr, args: List[NDArray]) -> List[NDArray]:
     """Grad.forwardInterpret (Grad.java:135-138)."""
-    values = fill_forward_values(jaxpr, args)
+    values = _evaluate(jaxpr, args, False)
     return [values[v.id] for v in jaxpr.outVars]
 
 
@@ -175,7 +200,7 @@ def do_backward(jaxpr: Jaxpr, values: Dict[int, NDArray], seeds: List[NDArray]) 
         wanted = [v.id in need for v in eq.inputs]
         if not any(wanted):
             continue
-        inputs = [values[v.id] for v in eq.inputs]
+        inputs = [values.get(v.id) for v in eq.inputs]
         out_value = values.get(eq.outputs[0].id)
         g_ins = compute_vjps(eq.primitive, eq, g_out, inputs, out_value, wanted)
         for v, w, g in zip(eq.inputs, wanted, g_ins):
@@ -246,34 +271,35 @@ def compute_vjps(p: Primitive, eq, g: ConcreteNDArray, inputs: List[NDArray], ou
     from . import pmap as _pm
     want_a = wanted[0]
     want_b = len(wanted) > 1 and wanted[1]
+    shapes = [v.shape for v in eq.inputs]  # rules that need only shapes read them from the Vars
     if p == Primitive.ADD:
-        return [broadcast_like(g, inputs[0].shape()) if want_a else None,
-                broadcast_like(g, inputs[1].shape()) if want_b else None]
+        return [broadcast_like(g, shapes[0]) if want_a else None,
+                broadcast_like(g, shapes[1]) if want_b else None]
     if p == Primitive.SUB:
-        return [broadcast_like(g, inputs[0].shape()) if want_a else None,
-                broadcast_like(_neg(g), inputs[1].shape()) if want_b else None]
+        return [broadcast_like(g, shapes[0]) if want_a else None,
+                broadcast_like(_neg(g), shapes[1]) if want_b else None]
     if p == Primitive.MUL:
-        return [broadcast_like(_bin(g, inputs[1], Primitive.MUL), inputs[0].shape()) if want_a else None,
-                broadcast_like(_bin(g, inputs[0], Primitive.MUL), inputs[1].shape()) if want_b else None]
+        return [broadcast_like(_bin(g, inputs[1], Primitive.MUL), shapes[0]) if want_a else None,
+                broadcast_like(_bin(g, inputs[0], Primitive.MUL), shapes[1]) if want_b else None]
     if p == Primitive.DIV:
         a, b = inputs
-        ga = broadcast_like(_bin(g, b, Primitive.DIV), a.shape()) if want_a else None
+        ga = broadcast_like(_bin(g, b, Primitive.DIV), shapes[0]) if want_a else None
         gb = None
         if want_b:
             t = _bin(_bin(_bin(g, a, Primitive.MUL), b, Primitive.DIV), b, Primitive.DIV)
-            gb = broadcast_like(_neg(t), b.shape())
+            gb = broadcast_like(_neg(t), shapes[1])
         return [ga, gb]
     if p == Primitive.MEAN:
-        n = float(inputs[0].shape().size())
-        return [broadcast_like(_bin(g, _scalar_like(n, g), Primitive.DIV), inputs[0].shape())]
+        n = float(shapes[0].size())
+        return [broadcast_like(_bin(g, _scalar_like(n, g), Primitive.DIV), shapes[0])]
     if p == Primitive.SUM:
-        return [broadcast_like(g, inputs[0].shape())]
+        return [broadcast_like(g, shapes[0])]
     if p == Primitive.SUM_AXIS:
-        return [axis_broadcast_like(g, inputs[0].shape(), eq.metadata.axis)]
+        return [axis_broadcast_like(g, shapes[0], eq.metadata.axis)]
     if p == Primitive.MEAN_AXIS:
         m = eq.metadata
-        n = float(inputs[0].shape()[m.axis])
-        return [axis_broadcast_like(_bin(g, _scalar_like(n, g), Primitive.DIV), inputs[0].shape(), m.axis)]
+        n = float(shapes[0][m.axis])
+        return [axis_broadcast_like(_bin(g, _scalar_like(n, g), Primitive.DIV), shapes[0], m.axis)]
     if p == Primitive.EXP:
         e = out_value if out_value is not None else inputs[0].exp()
         return [_bin(g, e, Primitive.MUL)]
@@ -300,13 +326,14 @@ def compute_vjps(p: Primitive, eq, g: ConcreteNDArray, inputs: List[NDArray], ou
         gb = _dot_raw(a, g, True, False, g.device()) if want_b else None
         return [ga, gb]
     if p in (Primitive.GT, Primitive.GE, Primitive.LT, Primitive.LE, Primitive.EQ, Primitive.NE):
-        return [zeros_like(inputs[0]) if want_a else None, zeros_like(inputs[1]) if want_b else None]
+        return [_zeros_for(eq.inputs[0], g) if want_a else None,
+                _zeros_for(eq.inputs[1], g) if want_b else None]
     if p == Primitive.MAX:
         return maxmin_grad(g, inputs[0], inputs[1], True)
     if p == Primitive.MIN:
         return maxmin_grad(g, inputs[0], inputs[1], False)
     if p in (Primitive.ARGMAX, Primitive.ARGMIN):
-        return [zeros_like(inputs[0])]
+        return [_zeros_for(eq.inputs[0], g)]
     if p == Primitive.PMAP:
         m: PmapMeta = eq.metadata
         D = m.numDevices()
@@ -321,8 +348,8 @@ def compute_vjps(p: Primitive, eq, g: ConcreteNDArray, inputs: List[NDArray], ou
         return [_pm.all_gather_vjp(g)]
     if p == Primitive.CAST:
         target = eq.metadata
-        identity = inputs[0].dtype() == target and target.is_floating()
-        return [broadcast_like(g, inputs[0].shape()) if identity else zeros_like(inputs[0])]
+        identity = eq.inputs[0].dtype == target and target.is_floating()
+        return [broadcast_like(g, shapes[0]) if identity else _zeros_for(eq.inputs[0], g)]
     if p == Primitive.CHECKPOINT:
         return [backward_interpret(eq.metadata.subJaxpr, [inputs[0]], [g])[0]]
     if p == Primitive.WHILE:
@@ -335,15 +362,22 @@ def compute_vjps(p: Primitive, eq, g: ConcreteNDArray, inputs: List[NDArray], ou
 # public transforms (Grad.java:37-119)
 # ---------------------------------------------------------------------------
 def make_jaxpr(fn: Callable, *args: NDArray) -> Jaxpr:
-    """JAX.make_jaxpr (JAX.java:30-55), any number of arguments."""
+    """JAX.make_jaxpr (JAX.java:30-55), any number of arguments; a function
+    returning a tuple or list of arrays gives a Jaxpr with that many outputs."""
     Tracer.start()
     try:
         t = Tracer.current()
         in_vars = [t.nextVar(a.shape(), a.dtype()) for a in args]
         result = fn(*[TracedNDArray(v) for v in in_vars])
-        if not isinstance(result, TracedNDArray):
-            result = TracedNDArray(t.nextConstant(result))
-        return Tracer.stop(in_vars, [result.getVar()])
+        results = list(result) if isinstance(result, (tuple, list)) else [result]
+        out_vars = []
+        for r in results:
+            if not isinstance(r, TracedNDArray):
+                r = TracedNDArray(t.nextConstant(r))
+            out_vars.append(r.getVar())
+        jaxpr = Tracer.stop(in_vars, out_vars)
+        jaxpr.__dict__["_tuple_out"] = isinstance(result, (tuple, list))
+        return jaxpr
     except BaseException:
         Tracer.abort()
         raise

@@ -1,0 +1,88 @@
+"""Host-side tests of the fusion planner (no GPU): which equations form a
+group, which values a group writes, and the program limits."""
+import pytest
+
+from jax4j_b200 import fusion
+from jax4j_b200 import grad as G
+from jax4j_b200.core import DType, Primitive as P, Shape
+from jax4j_b200.tracing import Tracer, TracedNDArray
+
+
+class Spec:
+    """Shape and dtype only: enough to trace a function."""
+    def __init__(self, *dims, dtype=DType.FLOAT32):
+        self._s, self._d = Shape(*dims), dtype
+
+    def shape(self):
+        return self._s
+
+    def dtype(self):
+        return self._d
+
+
+def test_select_chain_is_one_group_with_two_tails():
+    def f(x, y, zero, lo, hi):
+        m = x.gt(zero).astype(DType.FLOAT32)
+        z = m.mul(x.tanh().mul(y.sigmoid())).add(y.relu().clip(lo, hi))
+        return z.sum(-1, True), z.argmax(-1)
+
+    jp = G.make_jaxpr(f, Spec(64, 128), Spec(64, 128), Spec(), Spec(), Spec())
+    plan = fusion.plan(jp, keep_for_vjp=False)
+    groups = plan.groups
+    assert len(groups) == 1
+    g = groups[0]
+    assert [e.primitive for e in g.tails] == [P.SUM_AXIS, P.ARGMAX]
+    assert g.outputs == []                         # z is never written
+    assert all(kind == "group" for kind, _ in plan.steps)
+
+
+def test_keep_for_vjp_writes_values_the_backward_reads():
+    def f(x, w):
+        return x.mul(w).tanh().relu()
+
+    jp = G.make_jaxpr(f, Spec(8, 16), Spec(8, 16))
+    p0 = fusion.plan(jp, keep_for_vjp=False)
+    p1 = fusion.plan(jp, keep_for_vjp=True)
+    assert len(p0.groups) == len(p1.groups) == 1
+    assert [v.id for v in p0.groups[0].outputs] == [jp.outVars[0].id]
+    # tanh' reads its output, relu' reads its input (the tanh value)
+    assert len(p1.groups[0].outputs) >= 2
+
+
+def test_dot_splits_groups():
+    def f(x, w, b):
+        return x.dot(w).add(b).relu().mul(x.dot(w))
+
+    jp = G.make_jaxpr(f, Spec(8, 16), Spec(16, 16), Spec(16))
+    plan = fusion.plan(jp, keep_for_vjp=False)
+    kinds = [k for k, _ in plan.steps]
+    assert kinds.count("eq") == 2 and kinds.count("group") == 1
+
+
+def test_group_limits():
+    n = 40
+
+    def f(*xs):
+        acc = xs[0]
+        for x in xs[1:]:
+            acc = acc.add(x)
+        return acc
+
+    jp = G.make_jaxpr(f, *[Spec(4, 4) for _ in range(n)])
+    plan = fusion.plan(jp, keep_for_vjp=False)
+    assert len(plan.groups) >= 3
+    for g in plan.groups:
+        assert len(g.inputs) <= fusion.MAX_INPUTS and len(g.eqs) <= fusion.MAX_EQS
+    # every equation is in exactly one group
+    assert sum(len(g.eqs) for g in plan.groups) == n - 1
+
+
+def test_mismatched_shapes_and_bool_compare_not_fused():
+    def f(x, y):
+        return x.sum(0).add(y).gt(y).eq(y.gt(y))
+
+    jp = G.make_jaxpr(f, Spec(8, 16), Spec(16))
+    plan = fusion.plan(jp, keep_for_vjp=False)
+    fused = [e.primitive for g in plan.groups for e in g.eqs]
+    assert P.EQ not in fused                      # comparison of two booleans stays unfused
+    assert P.SUM_AXIS not in fused

@@ -1,0 +1,92 @@
+"""Fused elementwise chains (JAX.jit / the grad interpreter's forward pass)
+against the unfused kernels and the oracle: elementwise results bit for bit,
+row-reduction tails within the reduction tolerance, argmax exact."""
+import numpy as np
+import pytest
+
+from oracle import oracle as orc
+from tests.util import TOL_ELEMENTWISE, TOL_REDUCTION, assert_rel
+
+pytestmark = pytest.mark.gpu
+
+
+@pytest.fixture(scope="module")
+def J():
+    import jax4j_b200 as j
+    return j
+
+
+def _unfused(J, monkeypatch_fn):
+    from jax4j_b200 import grad
+    old = grad.FUSION
+    grad.FUSION = False
+    try:
+        return monkeypatch_fn()
+    finally:
+        grad.FUSION = old
+
+
+@pytest.mark.parametrize("rows,cols", [(4096, 16384), (33, 1000), (3, 7), (1, 5000), (700, 300)])
+def test_fused_sweep_matches_oracle(J, rows, cols):
+    x = J.Random.normal(J.PRNGKey.key(1), J.Shape(rows, cols))
+    y = J.Random.uniform(J.PRNGKey.key(11), J.Shape(rows, cols), -3.0, 3.0)
+    zero, lo, hi = (J.ConcreteNDArray.scalar(v) for v in (0.0, -1.0, 1.0))
+
+    def sweep(xx, yy):
+        z = J.Numpy.where(xx.gt(zero), xx.tanh().mul(yy.sigmoid()), yy.relu().clip(lo, hi))
+        return z, z.sum(-1, True), z.argmax(-1)
+
+    jitted = J.JAX.jit(sweep)
+    z, s, am = jitted(x, y)
+    groups = [g for g in next(iter(jitted.cache.values())).__dict__["_fusion_plan"].groups]
+    assert len(groups) == 1 and len(groups[0].tails) == 2  # one pass: chain + both tails
+    rz, rs, ram = orc.sweep(x.numpy(), y.numpy(), want_z=True)
+    assert_rel(z.numpy(), rz, TOL_ELEMENTWISE, "z")
+    assert_rel(s.numpy(), rs, TOL_REDUCTION, "row sums")
+    np.testing.assert_array_equal(am.numpy(), ram)
+    # fused elementwise values equal the unfused kernels' bit for bit
+    z2, _, am2 = _unfused(J, lambda: J.JAX.jit(sweep)(x, y))
+    np.testing.assert_array_equal(z.numpy(), z2.numpy())
+    np.testing.assert_array_equal(am.numpy(), am2.numpy())
+
+
+def test_fused_broadcast_patterns_and_casts(J):
+    r = np.random.default_rng(4)
+    a = J.ConcreteNDArray.of(r.standard_normal((64, 96)).astype(np.float32))
+    row = J.ConcreteNDArray.of(r.standard_normal(96).astype(np.float32))
+    col = J.ConcreteNDArray.of(r.standard_normal((64, 1)).astype(np.float32))
+    sc = J.ConcreteNDArray.scalar(0.25)
+
+    def f(x, rv, cv):
+        t = x.mul(rv).sub(cv).max(sc).exp().log().sin().cos()
+        m = t.gt(cv).astype(J.DType.FLOAT32).add(t.div(rv)).min(x)
+        i = m.astype(J.DType.INT32).astype(J.DType.FLOAT32)
+        return m.add(i), m.mean(-1, False), m.argmin(-1), t.sum(-1, True)
+
+    got = J.JAX.jit(f)(a, row, col)
+    ref = _unfused(J, lambda: f(a, row, col))
+    np.testing.assert_array_equal(got[0].numpy(), ref[0].numpy())
+    assert_rel(got[1].numpy(), ref[1].numpy(), TOL_REDUCTION)
+    np.testing.assert_array_equal(got[2].numpy(), ref[2].numpy())
+    assert_rel(got[3].numpy(), ref[3].numpy(), TOL_REDUCTION)
+
+
+def test_fused_argmax_nan_and_tie_rules(J):
+    x = np.float32([[np.nan, 5, 5, 1], [1, 7, 7, np.nan], [-np.inf] * 4, [3, 3, 9, 9]])
+    a = J.ConcreteNDArray.of(x)
+    one = J.ConcreteNDArray.scalar(1.0)
+    got = J.JAX.jit(lambda v: (v.mul(one).argmax(-1), v.mul(one).argmin(-1)))(a)
+    np.testing.assert_array_equal(got[0].numpy(), orc.argreduce(orc.ARGMAX, x, -1))
+    np.testing.assert_array_equal(got[1].numpy(), orc.argreduce(orc.ARGMIN, x, -1))
+
+
+def test_fusion_keeps_values_the_backward_reads(J):
+    # grad through a fused forward: the relu VJP reads z, the MUL VJP reads both inputs
+    r = np.random.default_rng(2)
+    x = J.ConcreteNDArray.of(r.standard_normal((32, 48)).astype(np.float32))
+    b = J.ConcreteNDArray.of(r.standard_normal(48).astype(np.float32))
+    w = J.ConcreteNDArray.of(r.standard_normal((32, 48)).astype(np.float32))
+    fn = lambda v: v.add(b).relu().mul(w).tanh().sum(-1).mean()
+    g = J.JAX.grad(fn)(x).numpy()
+    g_ref = _unfused(J, lambda: J.JAX.grad(fn)(x).numpy())
+    assert_rel(g, g_ref, TOL_REDUCTION)
