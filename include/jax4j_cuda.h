@@ -309,6 +309,13 @@ J4C_API int j4c_fused_compile(const j4c_program *prog, void **handle);
 /* Runs a compiled program: inputs/outputs/tails are arrays of device
  * pointers in slot order.  Elementwise results equal the unfused kernels'
  * bit for bit; tails are deterministic tree reductions of each row. */
+/* Diagnostics: the CUDA C++ source j4c_fused_compile would generate for
+ * `prog` (NUL-terminated, truncated to cap bytes; *len = full size + 1), and
+ * when `compile` is nonzero its NVRTC compilation for sm_100a, which needs no
+ * GPU.  Returns J4C_E_INVALID for a malformed program and J4C_E_CUDA with the
+ * compiler log in j4c_last_error() when compilation fails. */
+J4C_API int j4c_fused_source(const j4c_program *prog, int compile, char *buf, size_t cap, size_t *len);
+
 J4C_API int j4c_fused_launch(void *handle, int64_t rows, int64_t cols, const void *const *inputs,
                              void *const *outputs, void *const *tails, j4c_stream stream);
 

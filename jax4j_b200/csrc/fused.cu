@@ -39,9 +39,10 @@ struct Args {
 
 struct Entry {
     cudaLibrary_t library = nullptr;
-    cudaKernel_t flat = nullptr, rows_warp = nullptr, rows_block = nullptr;
+    cudaKernel_t flat[2] = {}, rows_warp[2] = {}, rows_block[2] = {};  // [0]: 1 element, [1]: 4 per thread
     bool needs_rows = false;  // tails or row/column-broadcast inputs
     int n_in = 0, n_out = 0, n_tail = 0;
+    int in_size[kMaxIn] = {}, in_bcast[kMaxIn] = {}, out_size[kMaxOut] = {};
 };
 
 static const char *kPreamble = R"(
@@ -68,6 +69,21 @@ template <class T> __device__ __forceinline__ T j_min(T a, T b) {
     if (a == T(0) && b == T(0) && j_neg(b)) return b;
     return (a <= b) ? a : b;
 }
+// float Math.max / Math.min in four instructions: equal operands (this
+// includes +0 / -0) combine their bit patterns, which gives +0 for max and
+// -0 for min; otherwise max.NaN / min.NaN return the larger / smaller value
+// or NaN when either operand is NaN (as the canonical NaN).
+template <> __device__ __forceinline__ float j_max<float>(float a, float b) {
+    float m;
+    asm("max.NaN.f32 %0, %1, %2;" : "=f"(m) : "f"(a), "f"(b));
+    return a == b ? __int_as_float(__float_as_int(a) & __float_as_int(b)) : m;
+}
+template <> __device__ __forceinline__ float j_min<float>(float a, float b) {
+    float m;
+    asm("min.NaN.f32 %0, %1, %2;" : "=f"(m) : "f"(a), "f"(b));
+    return a == b ? __int_as_float(__float_as_int(a) | __float_as_int(b)) : m;
+}
+template <class T> __device__ __forceinline__ T j_relu(T x) { return (T(0) >= x) ? T(0) : x; }
 __device__ __forceinline__ int j_d2i(double v) {
     if (v != v) return 0;
     if (v >= 2147483647.0) return 2147483647;
@@ -84,11 +100,14 @@ template <class T> __device__ __forceinline__ T j_warp_sum(T v) {
     for (int o = 16; o > 0; o >>= 1) v = j_add(v, __shfl_xor_sync(0xffffffffu, v, o));
     return v;
 }
+// (best, bi): a lane's first strict extremum, bi < 0 when the lane saw
+// none.  Combines lanes: any candidate beats none, then the larger
+// (smaller) value, then the smaller index.
 template <class T, bool MAX> __device__ __forceinline__ void j_warp_arg(T &best, int &bi) {
     for (int o = 16; o > 0; o >>= 1) {
         T v = __shfl_xor_sync(0xffffffffu, best, o);
         int i = __shfl_xor_sync(0xffffffffu, bi, o);
-        if ((MAX ? v > best : v < best) || (v == best && i < bi)) { best = v; bi = i; }
+        if (i >= 0 && (bi < 0 || (MAX ? v > best : v < best) || (v == best && i < bi))) { best = v; bi = i; }
     }
 }
 )";
@@ -183,22 +202,17 @@ static int validate(const j4c_program *p) {
     return J4C_OK;
 }
 
-// Per-element body: computes every instruction for element (r, j) / idx.
-static std::string gen_body(const j4c_program *p, bool flat) {
+// Code for one element.  The element's inputs are read from `ld<k>` (a
+// register array filled before the lane loop) and its outputs go to
+// `st<k>`; lane `l` is the element's position inside the thread's group of V.
+static std::string gen_element(const j4c_program *p) {
     std::ostringstream o;
     for (int i = 0; i < p->n_insns; i++) {
         const j4c_insn &q = p->insns[i];
         const char *T = ctype(q.dtype);
-        o << "        " << T << " v" << i << " = ";
+        o << "        const " << T << " v" << i << " = ";
         switch (q.op) {
-        case J4C_OP_INPUT: {
-            int b = p->input_bcast[q.a];
-            const char *idx = flat ? (b == J4C_BCAST_SCALAR ? "0" : "idx")
-                                   : (b == J4C_BCAST_FULL ? "(r * C + j)"
-                                      : b == J4C_BCAST_ROW ? "j" : b == J4C_BCAST_COL ? "r" : "0");
-            o << "((const " << T << " *)a.in[" << q.a << "])[" << idx << "];\n";
-            continue;
-        }
+        case J4C_OP_INPUT: o << "ld" << q.a << "[l];\n"; continue;
         case J4C_OP_CONST: o << const_literal(q.dtype, q.value) << ";\n"; continue;
         case J4C_OP_RELU_GRAD: o << "(v" << q.b << " > (" << T << ")0) ? v" << q.a << " : (" << T << ")0;\n"; continue;
         case J4C_ADD: o << "j_add(v" << q.a << ", v" << q.b << ");\n"; continue;
@@ -223,15 +237,14 @@ static std::string gen_body(const j4c_program *p, bool flat) {
         case J4C_SIN: o << (f ? "sinf(" : "sin(") << x << ");\n"; break;
         case J4C_COS: o << (f ? "cosf(" : "cos(") << x << ");\n"; break;
         case J4C_TANH: o << (f ? "tanhf(" : "tanh(") << x << ");\n"; break;
-        case J4C_RELU: o << "j_max((" << T << ")0, " << x << ");\n"; break;
-        case J4C_SIGMOID:
-            o << (f ? "__fdiv_rn(1.0f, __fadd_rn(1.0f, expf(-" : "__ddiv_rn(1.0, __dadd_rn(1.0, exp(-") << x
-              << ")));\n";
+        case J4C_RELU: o << "j_relu(" << x << ");\n"; break;
+        case J4C_SIGMOID:  // 1 / (1 + e^-x); a correctly rounded reciprocal equals the correctly rounded 1.0 / d
+            o << (f ? "__frcp_rn(__fadd_rn(1.0f, expf(-" : "__drcp_rn(__dadd_rn(1.0, exp(-") << x << ")));\n";
             break;
         case J4C_CAST: {
             int src = p->insns[q.a].dtype, dst = q.dtype;
             if (dst == J4C_BOOL) o << "(unsigned char)(" << x << " != 0);\n";
-            else if (src == J4C_BOOL) o << "(" << T << ")(" << x << " ? 1 : 0);\n";
+            else if (src == J4C_BOOL) o << "(" << x << " ? (" << T << ")1 : (" << T << ")0);\n";
             else if (dst == J4C_INT32 && is_float(src)) o << "j_d2i((double)" << x << ");\n";
             else if (dst == J4C_INT32) o << "(int)(unsigned int)(unsigned long long)(i64)" << x << ";\n";
             else if (dst == J4C_INT64 && is_float(src)) o << "j_d2l((double)" << x << ");\n";
@@ -241,10 +254,61 @@ static std::string gen_body(const j4c_program *p, bool flat) {
         default: o << "0;\n"; break;
         }
     }
+    for (int k = 0; k < p->n_outputs; k++) o << "        st" << k << "[l] = v" << p->output_insn[k] << ";\n";
+    return o.str();
+}
+
+static int dsize(int dt) { return dt == J4C_FLOAT64 || dt == J4C_INT64 ? 8 : dt == J4C_BOOL ? 1 : 4; }
+
+// Loads the V consecutive elements starting at element `base` (row/flat
+// position) into ld<k>, and declares st<k>.  4-byte types move as one
+// 128-bit access when V == 4; the launcher only picks V == 4 when every
+// such pointer is 16-byte aligned and the extent is a multiple of 4.
+static std::string gen_loads(const j4c_program *p, bool flat, int V) {
+    std::ostringstream o;
+    for (int i = 0; i < p->n_inputs; i++) {
+        const char *T = ctype(p->input_dtype[i]);
+        const int b = p->input_bcast[i];
+        o << "      " << T << " ld" << i << "[" << V << "];\n";
+        std::string ptr = std::string("((const ") + T + " *)a.in[" + std::to_string(i) + "])";
+        if (b == J4C_BCAST_SCALAR || b == J4C_BCAST_COL) {
+            const char *at = b == J4C_BCAST_SCALAR ? "0" : "r";
+            o << "      { const " << T << " t = " << ptr << "[" << at << "];";
+            for (int l = 0; l < V; l++) o << " ld" << i << "[" << l << "] = t;";
+            o << " }\n";
+            continue;
+        }
+        std::string idx = flat ? "e" : (b == J4C_BCAST_ROW ? "j" : "(r * C + j)");
+        if (V == 4 && dsize(p->input_dtype[i]) == 4) {
+            const char *T4 = p->input_dtype[i] == J4C_FLOAT32 ? "float4" : "int4";
+            o << "      { const " << T4 << " t = *(const " << T4 << " *)(" << ptr << " + " << idx << ");"
+              << " ld" << i << "[0] = t.x; ld" << i << "[1] = t.y; ld" << i << "[2] = t.z; ld" << i
+              << "[3] = t.w; }\n";
+        } else {
+            for (int l = 0; l < V; l++)
+                o << "      ld" << i << "[" << l << "] = " << ptr << "[" << idx << " + " << l << "];\n";
+        }
+    }
+    for (int k = 0; k < p->n_outputs; k++)
+        o << "      " << ctype(p->insns[p->output_insn[k]].dtype) << " st" << k << "[" << V << "];\n";
+    return o.str();
+}
+
+static std::string gen_stores(const j4c_program *p, bool flat, int V) {
+    std::ostringstream o;
+    std::string idx = flat ? "e" : "(r * C + j)";
     for (int k = 0; k < p->n_outputs; k++) {
-        int i = p->output_insn[k];
-        o << "        ((" << ctype(p->insns[i].dtype) << " *)a.out[" << k << "])[" << (flat ? "idx" : "(r * C + j)")
-          << "] = v" << i << ";\n";
+        const int dt = p->insns[p->output_insn[k]].dtype;
+        const char *T = ctype(dt);
+        std::string ptr = std::string("((") + T + " *)a.out[" + std::to_string(k) + "])";
+        if (V == 4 && dsize(dt) == 4) {
+            const char *T4 = dt == J4C_FLOAT32 ? "float4" : "int4";
+            o << "      *(" << T4 << " *)(" << ptr << " + " << idx << ") = make_" << T4 << "(st" << k << "[0], st"
+              << k << "[1], st" << k << "[2], st" << k << "[3]);\n";
+        } else {
+            for (int l = 0; l < V; l++)
+                o << "      " << ptr << "[" << idx << " + " << l << "] = st" << k << "[" << l << "];\n";
+        }
     }
     return o.str();
 }
@@ -254,18 +318,27 @@ static std::string gen_source(const j4c_program *p, bool *needs_rows) {
     for (int i = 0; i < p->n_inputs; i++)
         if (p->input_bcast[i] == J4C_BCAST_ROW || p->input_bcast[i] == J4C_BCAST_COL) rows = true;
     *needs_rows = rows;
+    const std::string element = gen_element(p);
     std::ostringstream o;
     o << kPreamble;
     if (!rows) {
-        o << "extern \"C\" __global__ void __launch_bounds__(256) k_flat(i64 N, Args a) {\n"
-             "    for (i64 idx = blockIdx.x * (i64)blockDim.x + threadIdx.x; idx < N;\n"
-             "         idx += (i64)gridDim.x * blockDim.x) {\n"
-          << gen_body(p, true) << "    }\n}\n";
+        for (int V : {1, 4}) {
+            o << "extern \"C\" __global__ void __launch_bounds__(256) k_flat" << (V == 4 ? "4" : "")
+              << "(i64 N, Args a) {\n"
+              << "    for (i64 e = (blockIdx.x * (i64)blockDim.x + threadIdx.x) * " << V << "; e < N;\n"
+              << "         e += (i64)gridDim.x * blockDim.x * " << V << ") {\n"
+              << gen_loads(p, true, V) << "      #pragma unroll\n      for (int l = 0; l < " << V
+              << "; l++) {\n"
+              << element << "      }\n"
+              << gen_stores(p, true, V) << "    }\n}\n";
+        }
         return o.str();
     }
-    // Row kernels: TPR threads per row (32: a warp per row, 256: a CTA per row).
+    // Row kernels: TPR threads per row (32: a warp per row, 256: a CTA per
+    // row), each thread taking V consecutive elements per iteration.
+    for (int V : {1, 4})
     for (int tpr : {32, 256}) {
-        const char *name = tpr == 32 ? "k_rows_warp" : "k_rows_block";
+        std::string name = std::string(tpr == 32 ? "k_rows_warp" : "k_rows_block") + (V == 4 ? "4" : "");
         o << "extern \"C\" __global__ void __launch_bounds__(256) " << name << "(i64 R, i64 C, Args a) {\n";
         if (tpr == 256) o << "    __shared__ double s_d[8]; __shared__ float s_f[8]; __shared__ int s_i[8];\n";
         o << "    const int sub = threadIdx.x % " << tpr << ";\n"
@@ -280,26 +353,30 @@ static std::string gen_source(const j4c_program *p, bool *needs_rows) {
             } else {
                 bool mx = op == J4C_ARGMAX;
                 o << "      " << T << " best" << k << " = (" << T << ")(" << (mx ? "-" : "") << "J_INF);\n"
-                  << "      int bi" << k << " = 2147483647; int nan" << k << " = 0;\n";
+                  << "      int bi" << k << " = -1; int nan" << k << " = 0;\n";
             }
         }
         o << "      if (r < R) {\n"
-          << "      for (i64 j = sub; j < C; j += " << tpr << ") {\n"
-          << gen_body(p, false);
+          << "      for (i64 j = (i64)sub * " << V << "; j < C; j += " << tpr * V << ") {\n"
+          << gen_loads(p, false, V) << "      #pragma unroll\n      for (int l = 0; l < " << V << "; l++) {\n"
+          << element;
         for (int k = 0; k < p->n_tails; k++) {
             int op = p->tail_op[k], t = p->tail_insn[k];
             if (op == J4C_SUM_AXIS || op == J4C_MEAN_AXIS) {
                 o << "        acc" << k << " = j_add(acc" << k << ", v" << t << ");\n";
             } else {
                 bool mx = op == J4C_ARGMAX;
-                // first strict extremum wins; a NaN in the first slot wins; later NaNs are skipped
-                o << "        if (j == 0 && v" << t << " != v" << t << ") nan" << k << " = 1;\n"
-                  << "        if (v" << t << " == v" << t << " && (v" << t << (mx ? " > " : " < ") << "best" << k
-                  << " || (v" << t << " == best" << k << " && (int)j < bi" << k << "))) { best" << k << " = v" << t
-                  << "; bi" << k << " = (int)j; }\n";
+                // The reference keeps the first strict extremum, starting from
+                // element 0: a NaN there wins, later NaNs never compare
+                // greater.  A lane sees its elements in increasing order, so a
+                // strict comparison keeps its first extremum; a row of only
+                // -inf (+inf for argmin) or NaN leaves no candidate and gives 0.
+                o << "        if (l == 0 && j == 0 && v" << t << " != v" << t << ") nan" << k << " = 1;\n"
+                  << "        if (v" << t << (mx ? " > " : " < ") << "best" << k << ") { best" << k << " = v" << t
+                  << "; bi" << k << " = (int)(j + l); }\n";
             }
         }
-        o << "      }\n      }\n";
+        o << "      }\n" << gen_stores(p, false, V) << "      }\n      }\n";
         // reductions
         for (int k = 0; k < p->n_tails; k++) {
             int op = p->tail_op[k];
@@ -328,12 +405,12 @@ static std::string gen_source(const j4c_program *p, bool *needs_rows) {
                       << "      __syncthreads();\n"
                       << "      if (threadIdx.x < 32) { best" << k << " = threadIdx.x < 8 ? " << S
                       << "[threadIdx.x] : (" << T << ")(" << (op == J4C_ARGMAX ? "-" : "") << "J_INF); bi" << k
-                      << " = threadIdx.x < 8 ? s_i[threadIdx.x] : 2147483647; j_warp_arg<" << T << ", " << mx
+                      << " = threadIdx.x < 8 ? s_i[threadIdx.x] : -1; j_warp_arg<" << T << ", " << mx
                       << ">(best" << k << ", bi" << k << "); }\n"
                       << "      __syncthreads();\n";
                 }
                 o << "      if (sub == 0 && r < R) ((int *)a.tail[" << k << "])[r] = (nan" << k << " || bi" << k
-                  << " == 2147483647) ? 0 : bi" << k << ";\n";
+                  << " < 0) ? 0 : bi" << k << ";\n";
             }
         }
         o << "    }\n}\n";
@@ -344,7 +421,7 @@ static std::string gen_source(const j4c_program *p, bool *needs_rows) {
 static std::mutex g_mu;
 static std::map<std::string, std::unique_ptr<Entry>> g_cache;  // key: device + source
 
-static int compile(const std::string &src, Entry *e) {
+static int nvrtc_cubin(const std::string &src, std::vector<char> *cubin) {
     nvrtcProgram prog;
     nvrtcResult nr = nvrtcCreateProgram(&prog, src.c_str(), "j4c_fused.cu", 0, nullptr, nullptr);
     if (nr != NVRTC_SUCCESS) return set_error(J4C_E_CUDA, "nvrtcCreateProgram: %s", nvrtcGetErrorString(nr));
@@ -363,15 +440,25 @@ static int compile(const std::string &src, Entry *e) {
     }
     size_t n = 0;
     nvrtcGetCUBINSize(prog, &n);
-    std::vector<char> cubin(n);
-    nvrtcGetCUBIN(prog, cubin.data());
+    cubin->resize(n);
+    nvrtcGetCUBIN(prog, cubin->data());
     nvrtcDestroyProgram(&prog);
+    return J4C_OK;
+}
+
+static int compile(const std::string &src, Entry *e) {
+    std::vector<char> cubin;
+    int rc = nvrtc_cubin(src, &cubin);
+    if (rc) return rc;
     J4C_CUDA(cudaLibraryLoadData(&e->library, cubin.data(), nullptr, nullptr, 0, nullptr, nullptr, 0));
     if (e->needs_rows) {
-        J4C_CUDA(cudaLibraryGetKernel(&e->rows_warp, e->library, "k_rows_warp"));
-        J4C_CUDA(cudaLibraryGetKernel(&e->rows_block, e->library, "k_rows_block"));
+        J4C_CUDA(cudaLibraryGetKernel(&e->rows_warp[0], e->library, "k_rows_warp"));
+        J4C_CUDA(cudaLibraryGetKernel(&e->rows_block[0], e->library, "k_rows_block"));
+        J4C_CUDA(cudaLibraryGetKernel(&e->rows_warp[1], e->library, "k_rows_warp4"));
+        J4C_CUDA(cudaLibraryGetKernel(&e->rows_block[1], e->library, "k_rows_block4"));
     } else {
-        J4C_CUDA(cudaLibraryGetKernel(&e->flat, e->library, "k_flat"));
+        J4C_CUDA(cudaLibraryGetKernel(&e->flat[0], e->library, "k_flat"));
+        J4C_CUDA(cudaLibraryGetKernel(&e->flat[1], e->library, "k_flat4"));
     }
     return J4C_OK;
 }
@@ -405,10 +492,33 @@ int j4c_fused_compile(const j4c_program *prog, void **handle) {
     e->n_in = prog->n_inputs;
     e->n_out = prog->n_outputs;
     e->n_tail = prog->n_tails;
+    for (int i = 0; i < prog->n_inputs; i++) {
+        e->in_size[i] = dsize(prog->input_dtype[i]);
+        e->in_bcast[i] = prog->input_bcast[i];
+    }
+    for (int k = 0; k < prog->n_outputs; k++) e->out_size[k] = dsize(prog->insns[prog->output_insn[k]].dtype);
     rc = compile(src, e.get());
     if (rc) return rc;
     *handle = e.get();
     g_cache.emplace(key, std::move(e));
+    return J4C_OK;
+}
+
+int j4c_fused_source(const j4c_program *prog, int compile, char *buf, size_t cap, size_t *len) {
+    int rc = validate(prog);
+    if (rc) return rc;
+    bool needs_rows = false;
+    std::string src = gen_source(prog, &needs_rows);
+    if (len) *len = src.size() + 1;
+    if (buf && cap) {
+        size_t n = std::min(cap - 1, src.size());
+        memcpy(buf, src.data(), n);
+        buf[n] = '\0';
+    }
+    if (compile) {
+        std::vector<char> cubin;
+        return nvrtc_cubin(src, &cubin);
+    }
     return J4C_OK;
 }
 
@@ -423,20 +533,33 @@ int j4c_fused_launch(void *handle, int64_t rows, int64_t cols, const void *const
     for (int i = 0; i < e->n_in; i++) a.in[i] = inputs[i];
     for (int i = 0; i < e->n_out; i++) a.out[i] = outputs[i];
     for (int i = 0; i < e->n_tail; i++) a.tail[i] = tails[i];
+    // 4 elements per thread when the extent allows it and every 128-bit
+    // access is aligned (4-byte types; wider and narrower types are read
+    // element by element inside the 4-wide loop).
+    const int64_t extent = e->needs_rows ? cols : rows * cols;
+    bool v4 = extent % 4 == 0;
+    for (int i = 0; i < e->n_in && v4; i++)
+        if (e->in_size[i] == 4 && (e->in_bcast[i] == J4C_BCAST_FULL || e->in_bcast[i] == J4C_BCAST_ROW) &&
+            reinterpret_cast<uintptr_t>(a.in[i]) % 16 != 0)
+            v4 = false;
+    for (int k = 0; k < e->n_out && v4; k++)
+        if (e->out_size[k] == 4 && reinterpret_cast<uintptr_t>(a.out[k]) % 16 != 0) v4 = false;
+    const int V = v4 ? 4 : 1;
     cudaStream_t s = as_stream(stream);
     cudaError_t r;
     if (!e->needs_rows) {
         int64_t N = rows * cols;
         void *params[] = {&N, &a};
-        r = cudaLaunchKernel((const void *)e->flat, dim3(grid_for(N, 256)), dim3(256), params, 0, s);
-    } else if (cols >= 512) {
+        r = cudaLaunchKernel((const void *)e->flat[v4], dim3(grid_for(ceil_div(N, (int64_t)V), 256)), dim3(256),
+                             params, 0, s);
+    } else if (cols >= 512 * V) {  // a CTA per row once each thread gets two or more iterations
         void *params[] = {&rows, &cols, &a};
         unsigned g = (unsigned)std::min<int64_t>(rows, (int64_t)sm_count() * 8);
-        r = cudaLaunchKernel((const void *)e->rows_block, dim3(g), dim3(256), params, 0, s);
+        r = cudaLaunchKernel((const void *)e->rows_block[v4], dim3(g), dim3(256), params, 0, s);
     } else {
         void *params[] = {&rows, &cols, &a};
-        unsigned g = (unsigned)std::min<int64_t>(ceil_div(rows, 8), (int64_t)sm_count() * 8);
-        r = cudaLaunchKernel((const void *)e->rows_warp, dim3(g), dim3(256), params, 0, s);
+        unsigned g = (unsigned)std::min<int64_t>(ceil_div(rows, (int64_t)8), (int64_t)sm_count() * 8);
+        r = cudaLaunchKernel((const void *)e->rows_warp[v4], dim3(g), dim3(256), params, 0, s);
     }
     count_launch();
     if (r != cudaSuccess) return cuda_status(r, "cudaLaunchKernel(fused)");

@@ -254,7 +254,8 @@ def _program(g: Group):
     return insns, outs, tail_ops, tail_insn
 
 
-def compile_group(g: Group) -> None:
+def _c_program(g: Group):
+    """The group as a j4c_program struct (with the arrays it points to)."""
     insns, outs, tail_ops, tail_insn = _program(g)
     arr = (_Insn * len(insns))(*[_Insn(*t) for t in insns])
     in_dt = (C.c_int32 * max(1, len(g.inputs)))(*[v.dtype.ordinal for v, _ in g.inputs])
@@ -263,10 +264,28 @@ def compile_group(g: Group) -> None:
     t_op = (C.c_int32 * max(1, len(tail_ops)))(*tail_ops)
     t_in = (C.c_int32 * max(1, len(tail_insn)))(*tail_insn)
     prog = _Program(len(insns), arr, len(g.inputs), in_dt, in_bc, len(outs), out_i, len(tail_ops), t_op, t_in)
+    return prog, (arr, in_dt, in_bc, out_i, t_op, t_in)
+
+
+def compile_group(g: Group) -> None:
+    prog, _keep = _c_program(g)
     handle = C.c_void_p()
     _lib.check(_lib.lib().j4c_fused_compile(C.cast(C.pointer(prog), C.c_void_p), C.byref(handle)),
                "j4c_fused_compile")
     g.handle = handle.value
+
+
+def group_source(g: Group, compile: bool = False) -> str:
+    """The CUDA source generated for a group; with compile=True it is also
+    compiled by NVRTC for sm_100a (no GPU needed)."""
+    prog, _keep = _c_program(g)
+    n = C.c_size_t()
+    pp = C.cast(C.pointer(prog), C.c_void_p)
+    _lib.check(_lib.lib().j4c_fused_source(pp, 0, None, 0, C.byref(n)), "j4c_fused_source")
+    buf = C.create_string_buffer(n.value)
+    _lib.check(_lib.lib().j4c_fused_source(pp, 1 if compile else 0, buf, n.value, C.byref(n)),
+               "j4c_fused_source")
+    return buf.value.decode()
 
 
 def run_group(g: Group, values: Dict[int, NDArray]) -> None:

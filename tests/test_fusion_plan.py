@@ -86,3 +86,51 @@ def test_mismatched_shapes_and_bool_compare_not_fused():
     fused = [e.primitive for g in plan.groups for e in g.eqs]
     assert P.EQ not in fused                      # comparison of two booleans stays unfused
     assert P.SUM_AXIS not in fused
+
+
+def _compile_all(jp, keep=False):
+    plan = fusion.plan(jp, keep_for_vjp=keep)
+    srcs = [fusion.group_source(g, compile=True) for g in plan.groups]
+    assert srcs
+    return srcs
+
+
+def test_generated_kernels_compile_for_sm100a():
+    # sweep-like chain with two tails: row kernels, 1- and 4-wide variants
+    def f(x, y, zero, lo, hi):
+        m = x.gt(zero).astype(DType.FLOAT32)
+        z = m.mul(x.tanh().mul(y.sigmoid())).add(y.relu().clip(lo, hi))
+        return z.sum(-1, True), z.argmax(-1), z.mean(-1, False), z.argmin(-1)
+
+    srcs = _compile_all(G.make_jaxpr(f, Spec(16, 64), Spec(16, 64), Spec(), Spec(), Spec()))
+    assert "k_rows_block4" in srcs[0] and "float4" in srcs[0]
+
+
+def test_generated_kernels_compile_for_mixed_dtypes_and_broadcasts():
+    def f(x, row, col, d, i):
+        t = x.mul(row).sub(col).exp().log()
+        b = t.gt(col)
+        k = t.astype(DType.INT32).astype(DType.INT64).astype(DType.FLOAT64).add(d)
+        return b.astype(DType.FLOAT32).add(t), k.sin().cos(), i.astype(DType.FLOAT32).div(t)
+
+    srcs = _compile_all(G.make_jaxpr(f, Spec(8, 12), Spec(12), Spec(8, 1), Spec(8, 12, dtype=DType.FLOAT64),
+                                     Spec(8, 12, dtype=DType.INT32)), keep=True)
+    assert any("double" in s for s in srcs)
+
+
+def test_generated_flat_kernel_compiles():
+    def f(x, y):
+        return x.mul(y).tanh().max(y).min(x).div(y)
+
+    srcs = _compile_all(G.make_jaxpr(f, Spec(3, 5, 7), Spec(3, 5, 7)))
+    assert "k_flat4" in srcs[0] and "k_rows" not in srcs[0]
+
+
+def test_invalid_program_rejected():
+    import ctypes as C
+    from jax4j_b200 import _lib
+    insn = (fusion._Insn * 1)(fusion._Insn(int(P.ADD), DType.FLOAT32.ordinal, 0, 0, 0.0))  # reads itself
+    z = (C.c_int32 * 1)(0)
+    prog = fusion._Program(1, insn, 0, z, z, 1, z, 0, z, z)
+    rc = _lib.lib().j4c_fused_source(C.cast(C.pointer(prog), C.c_void_p), 0, None, 0, None)
+    assert rc == _lib.E_INVALID

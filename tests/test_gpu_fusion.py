@@ -72,12 +72,52 @@ def test_fused_broadcast_patterns_and_casts(J):
 
 
 def test_fused_argmax_nan_and_tie_rules(J):
-    x = np.float32([[np.nan, 5, 5, 1], [1, 7, 7, np.nan], [-np.inf] * 4, [3, 3, 9, 9]])
+    x = np.float32([[np.nan, 5, 5, 1], [1, 7, 7, np.nan], [-np.inf] * 4, [3, 3, 9, 9],
+                    [-np.inf, np.nan, -np.inf, 2], [np.nan] * 4, [-np.inf, -np.inf, np.nan, np.nan],
+                    [np.inf, np.inf, -np.inf, np.nan], [0.0, -0.0, 0.0, -0.0], [-0.0, 0.0, -1, -1]])
     a = J.ConcreteNDArray.of(x)
     one = J.ConcreteNDArray.scalar(1.0)
     got = J.JAX.jit(lambda v: (v.mul(one).argmax(-1), v.mul(one).argmin(-1)))(a)
     np.testing.assert_array_equal(got[0].numpy(), orc.argreduce(orc.ARGMAX, x, -1))
     np.testing.assert_array_equal(got[1].numpy(), orc.argreduce(orc.ARGMIN, x, -1))
+
+
+@pytest.mark.parametrize("cols", [33, 1000, 1001, 4096, 16384])
+def test_fused_argmax_ties_across_lanes(J, cols):
+    # few distinct values so every row has many ties, spread over lanes and
+    # CTA warps; some rows carry NaN / inf; exercises 1- and 4-wide kernels
+    r = np.random.default_rng(cols)
+    x = r.integers(-3, 4, size=(64, cols)).astype(np.float32)
+    x[5, :] = -np.inf
+    x[6, 0] = np.nan
+    x[7, r.integers(1, cols, 20)] = np.nan
+    x[8, :] = np.nan
+    x[9, r.integers(0, cols, 5)] = np.inf
+    a = J.ConcreteNDArray.of(x)
+    one = J.ConcreteNDArray.scalar(1.0)
+    got = J.JAX.jit(lambda v: (v.mul(one).argmax(-1), v.mul(one).argmin(-1), v.mul(one).max(one)))(a)
+    np.testing.assert_array_equal(got[0].numpy(), orc.argreduce(orc.ARGMAX, x, -1))
+    np.testing.assert_array_equal(got[1].numpy(), orc.argreduce(orc.ARGMIN, x, -1))
+    np.testing.assert_array_equal(got[2].numpy(), orc.binary(orc.MAX, x, np.float32(1.0)))
+
+
+def test_fused_max_min_signed_zero_and_nan(J):
+    vals = np.float32([0.0, -0.0, 1.0, -1.0, np.inf, -np.inf, np.nan, 3.0e38, -1e-45])
+    x = np.repeat(vals, len(vals)).reshape(len(vals), len(vals))
+    y = np.tile(vals, len(vals)).reshape(len(vals), len(vals))
+    a, b = J.ConcreteNDArray.of(x), J.ConcreteNDArray.of(y)
+    one = J.ConcreteNDArray.scalar(1.0)
+    got = J.JAX.jit(lambda u, v: (u.mul(one).max(v), u.mul(one).min(v), u.mul(one).relu()))(a, b)
+    for k, (g, prim) in enumerate([(got[0], orc.MAX), (got[1], orc.MIN)]):
+        ref = orc.binary(prim, x, y)
+        gb = g.numpy()
+        assert np.array_equal(np.isnan(gb), np.isnan(ref))
+        ok = ~np.isnan(ref)
+        np.testing.assert_array_equal(gb[ok].view(np.uint32), ref[ok].view(np.uint32))
+    relu_ref = orc.unary(orc.RELU, x)
+    rb = got[2].numpy()
+    ok = ~np.isnan(relu_ref)
+    np.testing.assert_array_equal(rb[ok].view(np.uint32), relu_ref[ok].view(np.uint32))
 
 
 def test_fusion_keeps_values_the_backward_reads(J):
