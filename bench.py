@@ -62,6 +62,8 @@ def parse():
     p.add_argument("--m", type=int, default=8192)
     p.add_argument("--k", type=int, default=4096)
     p.add_argument("--n", type=int, default=4096)
+    p.add_argument("--trans", default="nn", choices=["nn", "tn", "nt", "tt"],
+                   help="gemm workload: whether A and B are stored transposed")
     p.add_argument("--rows", type=int, default=4096)
     p.add_argument("--cols", type=int, default=16384)
     return p.parse_args()
@@ -367,28 +369,50 @@ def run_reference(args):
 
 
 def run_gemm(args):
-    """One FP32 dot C[M,N] = A[M,K].B[K,N] (split + tcgen05 GEMM) per step."""
+    """One FP32 dot C[M,N] = op(A)[M,K].op(B)[K,N] per step through j4c_dot_ws
+    (both operand splits + the tcgen05 GEMM); the GEMM kernel alone is timed
+    too, from cached splits."""
     import torch
     import jax4j_b200 as J
     from jax4j_b200 import core
+    from jax4j_b200._lib import call, lib
     torch.cuda.set_device(0)
     M, K, N = args.m, args.k, args.n
+    ta, tb = args.trans[0] == "t", args.trans[1] == "t"
     dev = J.Device.defaultDevice()
-    A = J.Random.uniform(J.PRNGKey.key(2), J.Shape(M, K), -1.0, 1.0)
-    B = J.Random.uniform(J.PRNGKey.key(3), J.Shape(K, N), -1.0, 1.0)
-    for _ in range(args.warmup):
-        core._dot_raw(A, B, False, False, dev)
-    torch.cuda.synchronize()
-    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-    e0.record()
-    for _ in range(args.steps):
-        core._dot_raw(A, B, False, False, dev)
-    e1.record()
-    torch.cuda.synchronize()
-    ms = e0.elapsed_time(e1) / args.steps
-    tf = 2.0 * M * N * K / (ms / 1e3) / 1e12
-    print(json.dumps({"metric": "dot TFLOP/s (FP32 accuracy, 3xTF32)", "value": tf, "unit": "TFLOP/s",
-                      "ms_per_step": ms, "config": {"workload": f"dot {M}x{K}x{N}"},
+    A = J.Random.uniform(J.PRNGKey.key(2), J.Shape(*((K, M) if ta else (M, K))), -1.0, 1.0)
+    B = J.Random.uniform(J.PRNGKey.key(3), J.Shape(*((N, K) if tb else (K, N))), -1.0, 1.0)
+    ws_bytes = lib().j4c_dot_workspace_size(0, M, K, N)
+    ws = torch.empty(ws_bytes, dtype=torch.uint8, device="cuda")
+    out = torch.empty(M * N, dtype=torch.float32, device="cuda")
+    stream = torch.cuda.current_stream().cuda_stream
+
+    def full():
+        call("j4c_dot_ws", 0, A.data_ptr(), B.data_ptr(), out.data_ptr(), M, K, N, int(ta), int(tb),
+             ws.data_ptr(), ws_bytes, stream)
+
+    def gemm_only():
+        core._dot_raw(A, B, ta, tb, dev)
+
+    def timed(fn):
+        for _ in range(args.warmup):
+            fn()
+        torch.cuda.synchronize()
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0.record()
+        for _ in range(args.steps):
+            fn()
+        e1.record()
+        torch.cuda.synchronize()
+        return e0.elapsed_time(e1) / args.steps
+
+    ms = timed(full)
+    gemm_ms = timed(gemm_only)
+    flop = 2.0 * M * N * K
+    print(json.dumps({"metric": "dot TFLOP/s (FP32 accuracy, 3xTF32)", "value": flop / (ms / 1e3) / 1e12,
+                      "unit": "TFLOP/s", "ms_per_step": ms, "gemm_ms": gemm_ms,
+                      "gemm_tflops": flop / (gemm_ms / 1e3) / 1e12,
+                      "config": {"workload": f"dot {M}x{K}x{N} op(A){'T' if ta else ''} op(B){'T' if tb else ''}"},
                       "algorithmic_bytes": 4 * (M * K + K * N + M * N)}), flush=True)
 
 

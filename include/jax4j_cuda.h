@@ -264,6 +264,26 @@ J4C_API int j4c_dot_ws(int dtype, const void *a, const void *b, void *c, int64_t
                j4c_stream stream);
 J4C_API size_t j4c_dot_workspace_size(int dtype, int64_t M, int64_t K, int64_t N);
 
+/* The FLOAT32 dot in two steps, so a tensor that takes part in several
+ * products (a layer's input, weight and output gradient each appear in two
+ * of the forward/VJP dots) is split once.  j4c_split_f32 writes
+ * hi = tf32(x) and lo = tf32(x - hi) of x stored [rows, cols] as two arrays
+ * [rows, j4c_split_pitch(cols)] (16-byte aligned, padding columns zero);
+ * j4c_dot_split then computes C = op(A) . op(B) as j4c_dot does, from the
+ * split arrays of A and B in their stored layouts (trans flags as for
+ * j4c_dot).  The split of an unchanged tensor may be reused by any number of
+ * j4c_dot_split calls. */
+J4C_API int64_t j4c_split_pitch(int64_t cols);
+J4C_API int j4c_split_f32(const float *x, int64_t rows, int64_t cols, float *hi, float *lo, j4c_stream stream);
+/* The split of x^T: hi/lo arrays [cols, j4c_split_pitch(rows)].  A product
+ * whose A and B are both stored with K as the leading (slow) dimension, such
+ * as the weight gradient x^T . dy, runs fastest with one of them given in
+ * this form (and its trans flag flipped). */
+J4C_API int j4c_split_f32_transposed(const float *x, int64_t rows, int64_t cols, float *hi, float *lo,
+                                     j4c_stream stream);
+J4C_API int j4c_dot_split(const float *a_hi, const float *a_lo, const float *b_hi, const float *b_lo, float *c,
+                          int64_t M, int64_t K, int64_t N, int trans_a, int trans_b, j4c_stream stream);
+
 /* ------------------------------------------------------------------ */
 /* Fused elementwise programs: replace TornadoJitCompiler.compile       */
 /* (backend/TornadoJitCompiler.java:82-246), which runs one kernel per   */

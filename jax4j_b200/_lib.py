@@ -74,6 +74,10 @@ SIGNATURES = {
     "j4c_dot": [I32, P, P, P, I64, I64, I64, I32, I32, P],
     "j4c_dot_ws": [I32, P, P, P, I64, I64, I64, I32, I32, P, C.c_size_t, P],
     "j4c_dot_workspace_size": [I32, I64, I64, I64],
+    "j4c_split_pitch": [I64],
+    "j4c_split_f32": [P, I64, I64, P, P, P],
+    "j4c_split_f32_transposed": [P, I64, I64, P, P, P],
+    "j4c_dot_split": [P, P, P, P, P, I64, I64, I64, I32, I32, P],
     "j4c_fused_compile": [P, C.POINTER(P)],
     "j4c_fused_source": [P, I32, P, C.c_size_t, C.POINTER(C.c_size_t)],
     "j4c_fused_launch": [P, I64, I64, C.POINTER(P), C.POINTER(P), C.POINTER(P), P],
@@ -90,7 +94,8 @@ SIGNATURES = {
     "j4c_comm_wait": [P, P],
     "j4c_psum_slots": [I32, C.POINTER(P), I32, P, I64, P],
 }
-_RESTYPES = {"j4c_last_error": C.c_char_p, "j4c_dot_workspace_size": C.c_size_t}
+_RESTYPES = {"j4c_last_error": C.c_char_p, "j4c_dot_workspace_size": C.c_size_t,
+             "j4c_split_pitch": C.c_int64}
 
 
 def lib() -> C.CDLL:

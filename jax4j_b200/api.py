@@ -213,6 +213,8 @@ class Lax:
         leaves = PyTrees.flatten(tree)
         if ctx is None or Tracer.current() is not None or not leaves:
             return PyTrees.map(Lax.psum, tree)
+        if ctx.numDevices == 1:
+            return tree  # the sum over one shard is the shard (arrays are immutable)
         first = leaves[0]
         if any(l.dtype() != first.dtype() or l.tensor().device != first.tensor().device for l in leaves):
             return PyTrees.map(Lax.psum, tree)

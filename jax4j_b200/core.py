@@ -374,10 +374,12 @@ class ConcreteNDArray(NDArray):
     """A device-resident array (core/ConcreteNDArray.java).
 
     Storage is a flat, contiguous HBM buffer of shape.size() elements of the
-    dtype (BOOL as one byte 0/1).  Instances are immutable.
+    dtype (BOOL as one byte 0/1).  Instances are immutable, which is what
+    lets a FLOAT32 array keep the hi/lo split of its values (`_split`) once
+    it has been a dot operand, for the other dots it takes part in.
     """
 
-    __slots__ = ("_t", "_shape", "_dtype", "_device")
+    __slots__ = ("_t", "_shape", "_dtype", "_device", "_split", "_split_t")
 
     def __init__(self, data, shape=None, dtype: DType = None, device: Device = None):
         if device is None:
@@ -411,6 +413,8 @@ class ConcreteNDArray(NDArray):
         self._shape = shape
         self._dtype = dtype
         self._device = device
+        self._split = None
+        self._split_t = None
 
     # ---- construction helpers ----
     @staticmethod
@@ -439,6 +443,8 @@ class ConcreteNDArray(NDArray):
         obj._shape = shape
         obj._dtype = dtype
         obj._device = device
+        obj._split = None
+        obj._split_t = None
         return obj
 
     def _new(self, shape: Shape, dtype: DType) -> torch.Tensor:
@@ -726,6 +732,25 @@ def _dtype_of_numpy(arr: np.ndarray) -> DType:
 DOT_TIMING = None
 
 
+def _tf32_split(x: "ConcreteNDArray", transposed: bool = False):
+    """hi/lo split of a 2-D FLOAT32 array -- in its stored layout, or of its
+    transpose -- made on first use and kept on the (immutable) array."""
+    s = x._split_t if transposed else x._split
+    if s is None:
+        rows, cols = x._shape.dimensions()
+        n = (cols if transposed else rows) * _lib.lib().j4c_split_pitch(rows if transposed else cols)
+        hi = torch.empty(max(n, 4), dtype=torch.float32, device=x._t.device)
+        lo = torch.empty(max(n, 4), dtype=torch.float32, device=x._t.device)
+        call("j4c_split_f32_transposed" if transposed else "j4c_split_f32", x._t.data_ptr(), rows, cols,
+             hi.data_ptr(), lo.data_ptr(), x._stream())
+        s = (hi, lo)
+        if transposed:
+            x._split_t = s
+        else:
+            x._split = s
+    return s
+
+
 def _dot_raw(a: "ConcreteNDArray", b: "ConcreteNDArray", trans_a: bool, trans_b: bool,
              device: Device) -> "ConcreteNDArray":
     """C = op(A) . op(B) on the tensor cores; op = transpose when flagged."""
@@ -737,16 +762,39 @@ def _dot_raw(a: "ConcreteNDArray", b: "ConcreteNDArray", trans_a: bool, trans_b:
     if K != K2:
         raise IllegalArgumentException(f"dot: inner dimensions differ ({a._shape} . {b._shape})")
     out = torch.empty(M * N, dtype=a._dtype.torch, device=a._t.device)
-    ws_bytes = _lib.lib().j4c_dot_workspace_size(a._dtype.ordinal, M, K, N)
-    ws = torch.empty(max(ws_bytes, 1), dtype=torch.uint8, device=a._t.device) if ws_bytes else None
     timing = DOT_TIMING
-    if timing is not None:
-        ev0 = torch.cuda.Event(enable_timing=True)
-        ev1 = torch.cuda.Event(enable_timing=True)
-        ev0.record()
-    call("j4c_dot_ws", a._dtype.ordinal, a._t.data_ptr(), b._t.data_ptr(), out.data_ptr(), M, K, N,
-         int(trans_a), int(trans_b), ws.data_ptr() if ws is not None else None, ws_bytes,
-         a._stream())
+    if a._dtype == DType.FLOAT32 and M and N and K:
+        # tensor-core path: each operand's 3xTF32 split is made once per array.
+        # With K the leading dimension of both stored operands (A^T . B, the
+        # weight gradient) one of them goes in transposed (K-major) form: the
+        # smaller one, so the extra split pass is as short as possible.
+        ta, tb = trans_a, trans_b
+        if ta and not tb:
+            if a._shape.size() < b._shape.size():
+                (ah, al), ta = _tf32_split(a, True), False
+                bh, bl = _tf32_split(b)
+            else:
+                ah, al = _tf32_split(a)
+                (bh, bl), tb = _tf32_split(b, True), True
+        else:
+            ah, al = _tf32_split(a)
+            bh, bl = _tf32_split(b)
+        if timing is not None:
+            ev0 = torch.cuda.Event(enable_timing=True)
+            ev1 = torch.cuda.Event(enable_timing=True)
+            ev0.record()
+        call("j4c_dot_split", ah.data_ptr(), al.data_ptr(), bh.data_ptr(), bl.data_ptr(), out.data_ptr(),
+             M, K, N, int(ta), int(tb), a._stream())
+    else:
+        ws_bytes = _lib.lib().j4c_dot_workspace_size(a._dtype.ordinal, M, K, N)
+        ws = torch.empty(max(ws_bytes, 1), dtype=torch.uint8, device=a._t.device) if ws_bytes else None
+        if timing is not None:
+            ev0 = torch.cuda.Event(enable_timing=True)
+            ev1 = torch.cuda.Event(enable_timing=True)
+            ev0.record()
+        call("j4c_dot_ws", a._dtype.ordinal, a._t.data_ptr(), b._t.data_ptr(), out.data_ptr(), M, K, N,
+             int(trans_a), int(trans_b), ws.data_ptr() if ws is not None else None, ws_bytes,
+             a._stream())
     if timing is not None:
         ev1.record()
         timing.append((ev0, ev1, 2.0 * M * N * K))

@@ -10,6 +10,10 @@ int tc_gemm_workspace(int64_t M, int64_t K, int64_t N, size_t *bytes);
 int tc_gemm_f32(const float *a, const float *b, float *c, int64_t M, int64_t K, int64_t N,
                 int trans_a, int trans_b, void *ws, size_t ws_bytes, cudaStream_t s);
 bool tc_gemm_supported(int64_t M, int64_t K, int64_t N);
+int tc_split_f32(const float *x, int64_t rows, int64_t cols, float *hi, float *lo, cudaStream_t s);
+int tc_split_f32_t(const float *x, int64_t rows, int64_t cols, float *hi, float *lo, cudaStream_t s);
+int tc_gemm_presplit(const float *ah, const float *al, const float *bh, const float *bl, float *c, int64_t M,
+                     int64_t K, int64_t N, int trans_a, int trans_b, cudaStream_t s);
 }  // namespace j4c
 
 using namespace j4c;
@@ -57,6 +61,36 @@ int j4c_dot(int dtype, const void *a, const void *b, void *c, int64_t M, int64_t
     int rc = j4c_dot_ws(dtype, a, b, c, M, K, N, trans_a, trans_b, ws, need, stream);
     if (ws) scratch_free(ws, s);
     return rc;
+}
+
+int64_t j4c_split_pitch(int64_t cols) { return cols < 0 ? -1 : (cols + 3) / 4 * 4; }
+
+int j4c_split_f32(const float *x, int64_t rows, int64_t cols, float *hi, float *lo, j4c_stream stream) {
+    J4C_REQUIRE(rows >= 0 && cols >= 0, "j4c_split_f32: negative extent");
+    if (rows == 0 || cols == 0) return J4C_OK;
+    J4C_REQUIRE(x && hi && lo, "j4c_split_f32: NULL pointer");
+    return tc_split_f32(x, rows, cols, hi, lo, as_stream(stream));
+}
+
+int j4c_split_f32_transposed(const float *x, int64_t rows, int64_t cols, float *hi, float *lo,
+                             j4c_stream stream) {
+    J4C_REQUIRE(rows >= 0 && cols >= 0, "j4c_split_f32_transposed: negative extent");
+    if (rows == 0 || cols == 0) return J4C_OK;
+    J4C_REQUIRE(x && hi && lo, "j4c_split_f32_transposed: NULL pointer");
+    return tc_split_f32_t(x, rows, cols, hi, lo, as_stream(stream));
+}
+
+int j4c_dot_split(const float *a_hi, const float *a_lo, const float *b_hi, const float *b_lo, float *c,
+                  int64_t M, int64_t K, int64_t N, int trans_a, int trans_b, j4c_stream stream) {
+    J4C_REQUIRE(M >= 0 && K >= 0 && N >= 0, "j4c_dot_split: negative dimension");
+    if (M == 0 || N == 0) return J4C_OK;
+    J4C_REQUIRE(c, "j4c_dot_split: NULL output");
+    if (K == 0) return j4c_fill(J4C_FLOAT32, c, M * N, 0.0, stream);
+    J4C_REQUIRE(a_hi && a_lo && b_hi && b_lo, "j4c_dot_split: NULL operand");
+    if (!tc_gemm_supported(M, K, N))
+        return set_error(J4C_E_UNSUPPORTED, "j4c_dot_split: shape %lld x %lld x %lld is too large", (long long)M,
+                         (long long)K, (long long)N);
+    return tc_gemm_presplit(a_hi, a_lo, b_hi, b_lo, c, M, K, N, trans_a, trans_b, as_stream(stream));
 }
 
 }  // extern "C"

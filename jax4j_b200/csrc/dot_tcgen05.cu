@@ -10,13 +10,17 @@
 // core/ConcreteNDArray.java:452-459; backend/HostBackend.java:56-66).
 //
 // Pipeline:
-//  1. split pass (HBM-bound): op(A) and op(B) are written K-major as hi/lo
-//     pairs [rows, Kp] (Kp = K rounded up to 32, zero padded); a transposed
-//     operand (the DOT VJP's A^T / B^T, api/Grad.java:385-390) is transposed
-//     on the way through shared memory, so the GEMM sees one layout.
+//  1. split pass (HBM-bound): each operand is split elementwise in its own
+//     row-major layout into hi/lo arrays whose rows are padded to a multiple
+//     of 4 floats (16-byte TMA strides).  No transpose is needed: the GEMM
+//     reads an operand K-major (K contiguous) or MN-major (M or N
+//     contiguous, the DOT VJP's A^T / B^T, api/Grad.java:385-390) as it lies,
+//     so one split of a tensor serves all the products it takes part in.
 //  2. GEMM: a persistent kernel, one CTA per SM, three warp roles:
-//     warp 0 lane 0 issues TMA loads (cp.async.bulk.tensor, 128B swizzle)
-//     into a STAGES-deep shared-memory ring; warp 1 lane 0 issues
+//     warp 0 lane 0 issues TMA loads (cp.async.bulk.tensor; K-major tiles
+//     with a BK*4-byte swizzle, MN-major tiles as 32-float-wide column
+//     blocks in the 128-byte/32-byte-atom swizzle) into a STAGES-deep
+//     shared-memory ring; warp 1 lane 0 issues
 //     tcgen05.mma.kind::tf32 (M=128, N=BN, K=8) and tcgen05.commit's the
 //     ring slots back; warps 2..9 accumulate and store C.
 //  Promotion: the tensor core's FP32 accumulation does not round to nearest,
@@ -32,6 +36,7 @@
 #include <cuda.h>
 #include <cudaTypedefs.h>
 
+#include <algorithm>
 #include <cstdlib>
 #include <mutex>
 #include <vector>
@@ -42,7 +47,7 @@ namespace j4c {
 namespace tc {
 
 constexpr int BM = 128;           // rows of a CTA tile (TMEM lanes)
-constexpr int KPAD = 32;          // K is zero-padded to a multiple of this in the split
+constexpr int MNW = 32;           // MN-major tiles: floats per 128-byte swizzle row
 constexpr int UMMA_K = 8;         // K of one tf32 MMA instruction (32 bytes)
 constexpr int CHUNK_K = 256;      // K accumulated in TMEM before promotion to registers
 constexpr int kEpiWarps = 8;      // two warps per TMEM lane quadrant
@@ -58,6 +63,7 @@ struct Cfg {
     static constexpr int CHUNK_KB = CHUNK_K / BK;
     static constexpr int A_BYTES = BM * BK * 4;
     static constexpr int B_BYTES = BN * BK * 4;
+    static constexpr int MN_BOX_BYTES = MNW * BK * 4;  // one MN-major column block (BK rows x 128 B)
     static constexpr int STAGE_BYTES = 2 * A_BYTES + 2 * B_BYTES;
     static constexpr int TMEM_COLS = 2 * BN;  // two partial-sum buffers
     static constexpr int COLS_PER_WARP = BN / 2;  // each epilogue warp owns half the columns
@@ -159,9 +165,31 @@ __device__ __forceinline__ uint64_t smem_desc(uint32_t addr) {
     return d;
 }
 
-// kind::tf32 instruction descriptor: D f32, A/B tf32, both K-major.
-__host__ __device__ constexpr uint32_t idesc_tf32(int m, int n) {
-    return (1u << 4) | (2u << 7) | (2u << 10) | ((uint32_t)(n >> 3) << 17) | ((uint32_t)(m >> 4) << 24);
+// MN-major operand tile.  For 32-bit (tf32) operands the tensor core reads
+// MN-major data only in the "128-byte swizzle with 32-byte atoms" layout
+// (descriptor layout type 1; the TMA writes it with
+// CU_TENSOR_MAP_SWIZZLE_128B_ATOM_32B): 128-byte rows of 32 floats along M/N,
+// one row per k, whose four 32-byte pieces are permuted by (row mod 4).
+// Column blocks of 32 floats are stacked BK rows deep, MN_BOX_BYTES apart:
+// LBO = the distance between column blocks along M/N, SBO = the distance
+// between groups of 4 k-rows (one MMA's K = 8 reads two groups).
+template <int BK>
+__device__ __forceinline__ uint64_t smem_desc_mn(uint32_t addr) {
+    constexpr uint64_t box_bytes = MNW * BK * 4;
+    uint64_t d = 0;
+    d |= (uint64_t)((addr & 0x3FFFF) >> 4);
+    d |= (uint64_t)(box_bytes >> 4) << 16;       // LBO: next 32-float column block
+    d |= (uint64_t)((4 * 128) >> 4) << 32;       // SBO: next 4 k-rows
+    d |= (uint64_t)1 << 46;                      // descriptor version for sm_100
+    d |= (uint64_t)1 << 61;                      // 128-byte swizzle, 32-byte atoms
+    return d;
+}
+
+// kind::tf32 instruction descriptor: D f32, A/B tf32; a_mn / b_mn select the
+// MN-major operand layout (bits 15 / 16).
+__host__ __device__ constexpr uint32_t idesc_tf32(int m, int n, bool a_mn, bool b_mn) {
+    return (1u << 4) | (2u << 7) | (2u << 10) | ((a_mn ? 1u : 0u) << 15) | ((b_mn ? 1u : 0u) << 16) |
+           ((uint32_t)(n >> 3) << 17) | ((uint32_t)(m >> 4) << 24);
 }
 
 __device__ __forceinline__ void mma_tf32(uint32_t d_tmem, uint64_t a, uint64_t b, uint32_t idesc,
@@ -205,11 +233,25 @@ __device__ __forceinline__ void tile_coords(int t, int num_m, int num_n, int &mt
     nt = r / gsize;
 }
 
-template <int BN, int STAGES, int BK>
+// Loads one operand's hi or lo tile (ROWS of M or N, BK of K) into smem.
+template <int ROWS, int BK, bool MN>
+__device__ __forceinline__ void load_operand(uint32_t dst, const CUtensorMap *map, int kx, int row0,
+                                             uint32_t bar) {
+    if constexpr (!MN) {
+        tma_load_2d(dst, map, kx, row0, bar);  // box {BK, ROWS} of a [rows, K] array
+    } else {
+#pragma unroll
+        for (int i = 0; i < ROWS / MNW; i++)   // boxes {32, BK} of a [K, rows] array
+            tma_load_2d(dst + i * (MNW * BK * 4), map, row0 + i * MNW, kx, bar);
+    }
+}
+
+template <int BN, int STAGES, int BK, bool A_MN, bool B_MN>
 __global__ void __launch_bounds__(kThreads, 1)
 gemm_3xtf32_kernel(const __grid_constant__ CUtensorMap tAh, const __grid_constant__ CUtensorMap tAl,
                    const __grid_constant__ CUtensorMap tBh, const __grid_constant__ CUtensorMap tBl,
-                   float *__restrict__ C, int M, int N, int num_kb, int vec_store, int *status) {
+                   float *__restrict__ C, int M, int N, int num_kb, int vec_store, int store_t,
+                   int *status) {
     using Q = Cfg<BN, STAGES, BK>;
     constexpr int CHUNK_KB = Q::CHUNK_KB;
     extern __shared__ uint8_t smem_raw[];
@@ -265,10 +307,10 @@ gemm_3xtf32_kernel(const __grid_constant__ CUtensorMap tAh, const __grid_constan
                     const uint32_t fb = smem_u32(&ctl->full[stage]);
                     mbar_expect_tx(fb, Q::STAGE_BYTES);
                     const int kx = kb * BK;
-                    tma_load_2d(sb, &tAh, kx, mt * BM, fb);
-                    tma_load_2d(sb + Q::A_BYTES, &tAl, kx, mt * BM, fb);
-                    tma_load_2d(sb + 2 * Q::A_BYTES, &tBh, kx, nt * BN, fb);
-                    tma_load_2d(sb + 2 * Q::A_BYTES + Q::B_BYTES, &tBl, kx, nt * BN, fb);
+                    load_operand<BM, BK, A_MN>(sb, &tAh, kx, mt * BM, fb);
+                    load_operand<BM, BK, A_MN>(sb + Q::A_BYTES, &tAl, kx, mt * BM, fb);
+                    load_operand<BN, BK, B_MN>(sb + 2 * Q::A_BYTES, &tBh, kx, nt * BN, fb);
+                    load_operand<BN, BK, B_MN>(sb + 2 * Q::A_BYTES + Q::B_BYTES, &tBl, kx, nt * BN, fb);
                     issued++;
                     if (++stage == STAGES) {
                         stage = 0;
@@ -289,7 +331,7 @@ gemm_3xtf32_kernel(const __grid_constant__ CUtensorMap tAh, const __grid_constan
     } else if (warp == 1) {
         // ---------------- MMA issuer ----------------
         if (lane == 0) {
-            constexpr uint32_t idesc = idesc_tf32(BM, BN);
+            constexpr uint32_t idesc = idesc_tf32(BM, BN, A_MN, B_MN);
             int stage = 0;
             uint32_t phase = 0;
             int ci = 0;  // chunk counter across tiles: selects the TMEM buffer
@@ -317,9 +359,13 @@ gemm_3xtf32_kernel(const __grid_constant__ CUtensorMap tAh, const __grid_constan
                         const uint32_t sb_lo = sb_hi + Q::B_BYTES;
 #pragma unroll
                         for (int kk = 0; kk < BK / UMMA_K; kk++) {
-                            const uint32_t off = kk * UMMA_K * 4;
-                            const uint64_t ah = smem_desc<BK>(sa_hi + off), al = smem_desc<BK>(sa_lo + off);
-                            const uint64_t bh = smem_desc<BK>(sb_hi + off), bl = smem_desc<BK>(sb_lo + off);
+                            // next K = 8: 32 bytes along a K-major row, 8 rows of 128 B in an MN-major block
+                            const uint32_t oa = A_MN ? kk * UMMA_K * 128 : kk * UMMA_K * 4;
+                            const uint32_t ob = B_MN ? kk * UMMA_K * 128 : kk * UMMA_K * 4;
+                            const uint64_t ah = A_MN ? smem_desc_mn<BK>(sa_hi + oa) : smem_desc<BK>(sa_hi + oa);
+                            const uint64_t al = A_MN ? smem_desc_mn<BK>(sa_lo + oa) : smem_desc<BK>(sa_lo + oa);
+                            const uint64_t bh = B_MN ? smem_desc_mn<BK>(sb_hi + ob) : smem_desc<BK>(sb_hi + ob);
+                            const uint64_t bl = B_MN ? smem_desc_mn<BK>(sb_lo + ob) : smem_desc<BK>(sb_lo + ob);
                             mma_tf32(dcol, al, bh, idesc, (kb > kb0 || kk > 0) ? 1u : 0u);
                             mma_tf32(dcol, ah, bl, idesc, 1u);
                             mma_tf32(dcol, ah, bh, idesc, 1u);
@@ -375,7 +421,15 @@ gemm_3xtf32_kernel(const __grid_constant__ CUtensorMap tAh, const __grid_constan
             if (!ok) break;
             const int row = mt * BM + q * 32 + lane;
             const int col0 = nt * BN + cbase;
-            if (row < M && col0 < N) {
+            if (store_t) {
+                // C holds the transpose of this product ([N, M]): for each
+                // column the warp's 32 lanes write 32 consecutive floats.
+                if (row < M) {
+#pragma unroll
+                    for (int j = 0; j < Q::COLS_PER_WARP; j++)
+                        if (col0 + j < N) C[(size_t)(col0 + j) * (size_t)M + row] = acc[j];
+                }
+            } else if (row < M && col0 < N) {
                 float *crow = C + (size_t)row * (size_t)N + col0;
                 if (vec_store && col0 + Q::COLS_PER_WARP <= N) {
                     float4 *dst = reinterpret_cast<float4 *>(crow);
@@ -401,32 +455,31 @@ gemm_3xtf32_kernel(const __grid_constant__ CUtensorMap tAh, const __grid_constan
     }
 }
 
-// ---- operand split: op(X) -> K-major hi/lo pairs [rows, Kp] ---------------------------
+// ---- operand split: X [rows, cols] -> hi/lo [rows, pitch], pitch = cols rounded up to 4 ----
 __device__ __forceinline__ float tf32_round(float x) {
     uint32_t r;
     asm("cvt.rna.tf32.f32 %0, %1;" : "=r"(r) : "f"(x));
     return __uint_as_float(r & 0xFFFFE000u);
 }
 
-// Direct operand ([rows, K] row-major): 4 consecutive k per thread step,
-// 16-byte loads when K allows, 16-byte stores of hi and lo (Kp % 4 == 0).
-__global__ void __launch_bounds__(256) split_direct_kernel(const float *__restrict__ src, int64_t rows,
-                                                           int64_t K, int64_t Kp, int vec,
-                                                           float *__restrict__ hi,
-                                                           float *__restrict__ lo) {
-    const int64_t q = Kp / 4;
+// 4 consecutive columns per thread step: 16-byte loads when the source
+// allows, 16-byte stores of hi and lo; padding columns are written as zero.
+__global__ void __launch_bounds__(256) split_kernel(const float *__restrict__ src, int64_t rows, int64_t cols,
+                                                    int64_t pitch, int vec, float *__restrict__ hi,
+                                                    float *__restrict__ lo) {
+    const int64_t q = pitch / 4;
     const int64_t n = rows * q;
     for (int64_t v = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; v < n;
          v += (int64_t)gridDim.x * blockDim.x) {
         const int64_t r = v / q, k = (v - r * q) * 4;
         float x[4];
-        const float *p = src + r * K + k;
-        if (vec && k + 4 <= K) {
+        const float *p = src + r * cols + k;
+        if (vec && k + 4 <= cols) {
             const float4 t = __ldg(reinterpret_cast<const float4 *>(p));
             x[0] = t.x; x[1] = t.y; x[2] = t.z; x[3] = t.w;
         } else {
 #pragma unroll
-            for (int j = 0; j < 4; j++) x[j] = (k + j < K) ? p[j] : 0.0f;
+            for (int j = 0; j < 4; j++) x[j] = (k + j < cols) ? p[j] : 0.0f;
         }
         float h[4], l[4];
 #pragma unroll
@@ -434,38 +487,38 @@ __global__ void __launch_bounds__(256) split_direct_kernel(const float *__restri
             h[j] = tf32_round(x[j]);
             l[j] = tf32_round(x[j] - h[j]);
         }
-        *reinterpret_cast<float4 *>(hi + r * Kp + k) = make_float4(h[0], h[1], h[2], h[3]);
-        *reinterpret_cast<float4 *>(lo + r * Kp + k) = make_float4(l[0], l[1], l[2], l[3]);
+        *reinterpret_cast<float4 *>(hi + r * pitch + k) = make_float4(h[0], h[1], h[2], h[3]);
+        *reinterpret_cast<float4 *>(lo + r * pitch + k) = make_float4(l[0], l[1], l[2], l[3]);
     }
 }
 
-// Transposed operand (stored [K, rows] row-major): 64 x 64 tiles through
-// shared memory, reads coalesced along rows, writes coalesced along k.
-__global__ void __launch_bounds__(256) split_transpose_kernel(const float *__restrict__ src, int64_t rows,
-                                                              int64_t K, int64_t Kp,
-                                                              float *__restrict__ hi,
-                                                              float *__restrict__ lo) {
+// Transposed split: X [rows, cols] -> hi/lo of X^T, [cols, pitch] with
+// pitch = rows rounded up to 4.  64 x 64 tiles through shared memory: reads
+// coalesced along X's rows, writes coalesced along X^T's rows.
+__global__ void __launch_bounds__(256) split_t_kernel(const float *__restrict__ src, int64_t rows, int64_t cols,
+                                                      int64_t pitch, int64_t tiles_c, float *__restrict__ hi,
+                                                      float *__restrict__ lo) {
     __shared__ float tile[64][65];
-    const int64_t k0 = (int64_t)blockIdx.x * 64, r0 = (int64_t)blockIdx.y * 64;
+    const int64_t c0 = (blockIdx.x % tiles_c) * 64, r0 = (blockIdx.x / tiles_c) * 64;
     const int tx = threadIdx.x & 31, ty = threadIdx.x >> 5;  // 32 x 8
-    for (int j = ty; j < 64; j += 8) {  // tile[r][k] <- src[k][r]
-        const int64_t k = k0 + j;
-        for (int i = tx; i < 64; i += 32) {
-            const int64_t r = r0 + i;
-            tile[i][j] = (r < rows && k < K) ? src[k * rows + r] : 0.0f;
+    for (int i = ty; i < 64; i += 8) {  // tile[i][j] = X[r0 + i][c0 + j]
+        const int64_t r = r0 + i;
+        for (int j = tx; j < 64; j += 32) {
+            const int64_t c = c0 + j;
+            tile[i][j] = (r < rows && c < cols) ? src[r * cols + c] : 0.0f;
         }
     }
     __syncthreads();
-    for (int j = ty; j < 64; j += 8) {
-        const int64_t r = r0 + j;
-        if (r >= rows) continue;
+    for (int j = ty; j < 64; j += 8) {  // X^T[c0 + j][r0 + i] = tile[i][j]
+        const int64_t c = c0 + j;
+        if (c >= cols) continue;
         for (int i = tx; i < 64; i += 32) {
-            const int64_t k = k0 + i;
-            if (k < Kp) {
-                const float x = tile[j][i];
+            const int64_t r = r0 + i;
+            if (r < pitch) {
+                const float x = tile[i][j];
                 const float h = tf32_round(x);
-                hi[r * Kp + k] = h;
-                lo[r * Kp + k] = tf32_round(x - h);
+                hi[c * pitch + r] = h;
+                lo[c * pitch + r] = tf32_round(x - h);
             }
         }
     }
@@ -485,25 +538,42 @@ static PFN_cuTensorMapEncodeTiled_v12000 encode_fn() {
     return fn;
 }
 
-static int make_map(CUtensorMap *map, const float *base, int64_t rows, int64_t Kp, int box_rows, int bk) {
+inline int64_t split_pitch(int64_t cols) { return ceil_div(cols, 4) * 4; }
+
+// Tensor map of a hi or lo array [rows, pitch] (pitch * 4 bytes per row).
+//   K-major use (rows = M or N, cols = K): box {BK, box_rows}, BK*4-byte swizzle.
+//   MN-major use (rows = K, cols = M or N): box {32, BK}, 128-byte swizzle of 32-byte atoms.
+// Columns past `cols` and rows past `rows` read as zero (TMA fill).
+static int make_map(CUtensorMap *map, const float *base, int64_t rows, int64_t cols, bool mn, int box_rows,
+                    int bk) {
     auto fn = encode_fn();
     if (!fn) return set_error(J4C_E_CUDA, "cuTensorMapEncodeTiled is unavailable");
-    cuuint64_t dims[2] = {(cuuint64_t)Kp, (cuuint64_t)rows};
-    cuuint64_t strides[1] = {(cuuint64_t)Kp * 4};
-    cuuint32_t box[2] = {(cuuint32_t)bk, (cuuint32_t)box_rows};
+    cuuint64_t dims[2] = {(cuuint64_t)cols, (cuuint64_t)rows};
+    cuuint64_t strides[1] = {(cuuint64_t)split_pitch(cols) * 4};
+    cuuint32_t box[2];
+    CUtensorMapSwizzle sw;
+    if (mn) {
+        box[0] = MNW;
+        box[1] = (cuuint32_t)bk;
+        sw = CU_TENSOR_MAP_SWIZZLE_128B_ATOM_32B;
+    } else {
+        box[0] = (cuuint32_t)bk;
+        box[1] = (cuuint32_t)box_rows;
+        sw = bk == 32 ? CU_TENSOR_MAP_SWIZZLE_128B : CU_TENSOR_MAP_SWIZZLE_64B;
+    }
     cuuint32_t estr[2] = {1, 1};
     CUresult r = fn(map, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 2, const_cast<float *>(base), dims, strides, box,
-                    estr, CU_TENSOR_MAP_INTERLEAVE_NONE,
-                    bk == 32 ? CU_TENSOR_MAP_SWIZZLE_128B : CU_TENSOR_MAP_SWIZZLE_64B,
-                    CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+                    estr, CU_TENSOR_MAP_INTERLEAVE_NONE, sw, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+                    CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
     if (r != CUDA_SUCCESS) return set_error(J4C_E_CUDA, "cuTensorMapEncodeTiled failed (%d)", (int)r);
     return J4C_OK;
 }
 
-template <int BN, int STAGES, int BK>
+template <int BN, int STAGES, int BK, bool A_MN, bool B_MN>
 static int launch_gemm(const float *ah, const float *al, const float *bh, const float *bl, float *c,
-                       int64_t M, int64_t N, int64_t Kp, cudaStream_t s) {
+                       int64_t M, int64_t N, int64_t K, bool store_t, cudaStream_t s) {
     using Q = Cfg<BN, STAGES, BK>;
+    auto kernel = gemm_3xtf32_kernel<BN, STAGES, BK, A_MN, B_MN>;
     static std::mutex mu;
     static std::vector<char> configured;
     int dev = 0;
@@ -512,74 +582,123 @@ static int launch_gemm(const float *ah, const float *al, const float *bh, const 
         std::lock_guard<std::mutex> lock(mu);
         if ((int)configured.size() <= dev) configured.resize(dev + 1, 0);
         if (!configured[dev]) {
-            J4C_CUDA(cudaFuncSetAttribute(gemm_3xtf32_kernel<BN, STAGES, BK>,
-                                          cudaFuncAttributeMaxDynamicSharedMemorySize, Q::SMEM_BYTES));
+            J4C_CUDA(cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, Q::SMEM_BYTES));
             configured[dev] = 1;
         }
     }
     CUtensorMap mAh, mAl, mBh, mBl;
     int rc;
-    if ((rc = make_map(&mAh, ah, M, Kp, BM, BK)) || (rc = make_map(&mAl, al, M, Kp, BM, BK)) ||
-        (rc = make_map(&mBh, bh, N, Kp, BN, BK)) || (rc = make_map(&mBl, bl, N, Kp, BN, BK)))
+    // op(A) [M, K]: stored [M, K] (K-major) or [K, M] (MN-major); likewise op(B)^T [N, K].
+    const int64_t ar = A_MN ? K : M, ac = A_MN ? M : K;
+    const int64_t br = B_MN ? K : N, bc = B_MN ? N : K;
+    if ((rc = make_map(&mAh, ah, ar, ac, A_MN, BM, BK)) || (rc = make_map(&mAl, al, ar, ac, A_MN, BM, BK)) ||
+        (rc = make_map(&mBh, bh, br, bc, B_MN, BN, BK)) || (rc = make_map(&mBl, bl, br, bc, B_MN, BN, BK)))
         return rc;
     int *status = device_status_ptr();
     if (!status) return set_error(J4C_E_OOM, "no device status word");
     const int64_t tiles = ceil_div(M, BM) * ceil_div(N, BN);
     const int grid = (int)std::min<int64_t>(tiles, sm_count());
     const int vec = (N % 4 == 0) && aligned16(c);
-    gemm_3xtf32_kernel<BN, STAGES, BK><<<grid, kThreads, Q::SMEM_BYTES, s>>>(
-        mAh, mAl, mBh, mBl, c, (int)M, (int)N, (int)(Kp / BK), vec, status);
+    kernel<<<grid, kThreads, Q::SMEM_BYTES, s>>>(mAh, mAl, mBh, mBl, c, (int)M, (int)N, (int)ceil_div(K, BK),
+                                                 store_t ? 0 : vec, store_t ? 1 : 0, status);
     J4C_LAUNCH_CHECK("gemm_3xtf32_kernel");
     return J4C_OK;
 }
 
-static int launch_split(const float *src, int64_t rows, int64_t K, int64_t Kp, int kr, float *hi,
-                        float *lo, cudaStream_t s) {
-    if (!kr) {
-        const int vec = (K % 4 == 0) && aligned16(src);
-        split_direct_kernel<<<grid_for(rows * (Kp / 4), 256), 256, 0, s>>>(src, rows, K, Kp, vec, hi, lo);
-        J4C_LAUNCH_CHECK("split_direct_kernel");
-    } else {
-        dim3 grid((unsigned)ceil_div(Kp, 64), (unsigned)ceil_div(rows, 64));
-        split_transpose_kernel<<<grid, 256, 0, s>>>(src, rows, K, Kp, hi, lo);
-        J4C_LAUNCH_CHECK("split_transpose_kernel");
-    }
+template <int BN, int STAGES, int BK>
+static int launch_gemm_any(const float *ah, const float *al, const float *bh, const float *bl, float *c,
+                           int64_t M, int64_t N, int64_t K, bool a_mn, bool b_mn, cudaStream_t s) {
+    if (!a_mn && !b_mn) return launch_gemm<BN, STAGES, BK, false, false>(ah, al, bh, bl, c, M, N, K, false, s);
+    if (a_mn && !b_mn) return launch_gemm<BN, STAGES, BK, true, false>(ah, al, bh, bl, c, M, N, K, false, s);
+    // The wide (BN = 256) operand is read MN-major at a smem cost that
+    // throttles the tensor pipe, so a K-major A with an MN-major B runs as
+    // C^T = op(B)^T . op(A)^T: B's split becomes the (MN-major) A operand,
+    // A's the (K-major) B operand, and the epilogue stores transposed.
+    if (!a_mn && b_mn) return launch_gemm<BN, STAGES, BK, true, false>(bh, bl, ah, al, c, N, M, K, true, s);
+    return launch_gemm<BN, STAGES, BK, true, true>(ah, al, bh, bl, c, M, N, K, false, s);
+}
+
+int split_t(const float *src, int64_t rows, int64_t cols, float *hi, float *lo, cudaStream_t s) {
+    if (rows == 0 || cols == 0) return J4C_OK;
+    J4C_REQUIRE(aligned16(hi) && aligned16(lo), "split: hi/lo must be 16-byte aligned");
+    const int64_t pitch = split_pitch(rows);
+    const int64_t tiles_c = ceil_div(cols, 64), tiles_r = ceil_div(pitch, 64);
+    J4C_REQUIRE(tiles_c * tiles_r < (1ll << 31), "split: array too large");
+    split_t_kernel<<<(unsigned)(tiles_c * tiles_r), 256, 0, s>>>(src, rows, cols, pitch, tiles_c, hi, lo);
+    J4C_LAUNCH_CHECK("split_t_kernel");
+    return J4C_OK;
+}
+
+int split(const float *src, int64_t rows, int64_t cols, float *hi, float *lo, cudaStream_t s) {
+    if (rows == 0 || cols == 0) return J4C_OK;
+    J4C_REQUIRE(aligned16(hi) && aligned16(lo), "split: hi/lo must be 16-byte aligned");
+    const int64_t pitch = split_pitch(cols);
+    const int vec = (cols % 4 == 0) && aligned16(src);
+    split_kernel<<<grid_for(rows * (pitch / 4), 256), 256, 0, s>>>(src, rows, cols, pitch, vec, hi, lo);
+    J4C_LAUNCH_CHECK("split_kernel");
     return J4C_OK;
 }
 
 }  // namespace tc
 
 bool tc_gemm_supported(int64_t M, int64_t K, int64_t N) {
-    // int32 coordinates/extents in the kernel and the split grid's y limit
-    return M >= 1 && N >= 1 && K >= 1 && M < (1ll << 31) && N < (1ll << 31) &&
-           ceil_div(M, 64) < 65536 && ceil_div(N, 64) < 65536 && K < (1ll << 30);
+    // int32 coordinates and extents in the kernel and the tensor maps
+    return M >= 1 && N >= 1 && K >= 1 && M < (1ll << 31) && N < (1ll << 31) && K < (1ll << 31);
 }
 
+// hi + lo floats of one operand stored [rows, cols]
+static int64_t split_floats(int64_t rows, int64_t cols) { return 2 * rows * tc::split_pitch(cols); }
+
 int tc_gemm_workspace(int64_t M, int64_t K, int64_t N, size_t *bytes) {
-    const int64_t Kp = ceil_div(K, tc::KPAD) * tc::KPAD;
-    *bytes = (size_t)(M + N) * (size_t)Kp * 2 * sizeof(float);
+    // the larger of the two storage orders of each operand
+    const int64_t a = std::max(split_floats(M, K), split_floats(K, M));
+    const int64_t b = std::max(split_floats(K, N), split_floats(N, K));
+    *bytes = (size_t)(a + b) * sizeof(float);
     return J4C_OK;
 }
 
-int tc_gemm_f32(const float *a, const float *b, float *c, int64_t M, int64_t K, int64_t N,
-                int trans_a, int trans_b, void *ws, size_t ws_bytes, cudaStream_t s) {
-    const int64_t Kp = ceil_div(K, tc::KPAD) * tc::KPAD;
-    float *ah = static_cast<float *>(ws);
-    float *al = ah + M * Kp;
-    float *bh = al + M * Kp;
-    float *bl = bh + N * Kp;
-    J4C_REQUIRE(aligned16(ws), "dot: workspace must be 16-byte aligned");
-    int rc;
-    // op(A) = A [M,K] (trans_a = 0) or A^T with A stored [K,M]
-    if ((rc = tc::launch_split(a, M, K, Kp, trans_a ? 1 : 0, ah, al, s))) return rc;
-    // op(B) = B [K,N]: the GEMM wants it K-major [N,K]
-    if ((rc = tc::launch_split(b, N, K, Kp, trans_b ? 0 : 1, bh, bl, s))) return rc;
+int tc_split_f32(const float *x, int64_t rows, int64_t cols, float *hi, float *lo, cudaStream_t s) {
+    return tc::split(x, rows, cols, hi, lo, s);
+}
+
+int tc_split_f32_t(const float *x, int64_t rows, int64_t cols, float *hi, float *lo, cudaStream_t s) {
+    return tc::split_t(x, rows, cols, hi, lo, s);
+}
+
+int tc_gemm_presplit(const float *ah, const float *al, const float *bh, const float *bl, float *c, int64_t M,
+                     int64_t K, int64_t N, int trans_a, int trans_b, cudaStream_t s) {
+    J4C_REQUIRE(aligned16(ah) && aligned16(al) && aligned16(bh) && aligned16(bl),
+                "dot: split operands must be 16-byte aligned");
+    // op(A) = A [M,K] is read K-major; A^T (A stored [K,M]) MN-major.
+    // op(B) = B [K,N] is read MN-major; B^T (B stored [N,K]) K-major.
+    const bool a_mn = trans_a != 0, b_mn = trans_b == 0;
     static const int variant = [] {
         const char *v = getenv("J4C_GEMM_VARIANT");
         return v ? atoi(v) : 1;
     }();
-    if (variant == 0) return tc::launch_gemm<256, 2, 32>(ah, al, bh, bl, c, M, N, Kp, s);
-    return tc::launch_gemm<256, 4, 16>(ah, al, bh, bl, c, M, N, Kp, s);
+    if (variant == 0) return tc::launch_gemm_any<256, 2, 32>(ah, al, bh, bl, c, M, N, K, a_mn, b_mn, s);
+    return tc::launch_gemm_any<256, 4, 16>(ah, al, bh, bl, c, M, N, K, a_mn, b_mn, s);
+}
+
+int tc_gemm_f32(const float *a, const float *b, float *c, int64_t M, int64_t K, int64_t N,
+                int trans_a, int trans_b, void *ws, size_t ws_bytes, cudaStream_t s) {
+    J4C_REQUIRE(aligned16(ws), "dot: workspace must be 16-byte aligned");
+    const int64_t ar = trans_a ? K : M, ac = trans_a ? M : K;  // A as stored
+    const int64_t br = trans_b ? N : K, bc = trans_b ? K : N;  // B as stored
+    float *ah = static_cast<float *>(ws);
+    float *al = ah + ar * tc::split_pitch(ac);
+    float *bh = al + ar * tc::split_pitch(ac);
+    const bool b_transposed = trans_a && !trans_b;  // B is split as B^T: [bc, pitch(br)]
+    float *bl = bh + (b_transposed ? bc * tc::split_pitch(br) : br * tc::split_pitch(bc));
+    int rc;
+    if ((rc = tc::split(a, ar, ac, ah, al, s))) return rc;
+    if (b_transposed) {
+        // both stored K-leading: B goes in as the split of B^T (K-major)
+        if ((rc = tc::split_t(b, br, bc, bh, bl, s))) return rc;
+        return tc_gemm_presplit(ah, al, bh, bl, c, M, K, N, trans_a, 1, s);
+    }
+    if ((rc = tc::split(b, br, bc, bh, bl, s))) return rc;
+    return tc_gemm_presplit(ah, al, bh, bl, c, M, K, N, trans_a, trans_b, s);
 }
 
 }  // namespace j4c

@@ -230,8 +230,8 @@ def _nccl_for(ordinals: tuple) -> NcclCollective:
 def psum_value(x: NDArray) -> NDArray:
     """Lax.psum eager branch (Lax.java:184-186): identity outside pmap."""
     ctx = PmapContext.current()
-    if ctx is None:
-        return x
+    if ctx is None or ctx.numDevices == 1:
+        return x  # a sum over one shard is the shard itself (arrays are immutable)
     return ctx.collective.psum(ctx.deviceIndex, x)
 
 

@@ -7,6 +7,7 @@ reductions/dot within 1e-4 (relative per tensor, tests/util.py).
 import numpy as np
 import pytest
 
+from jax4j_b200 import _lib
 from oracle import oracle as orc
 from tests.util import TOL_ELEMENTWISE, TOL_REDUCTION, assert_rel
 
@@ -277,3 +278,81 @@ def test_empty_and_single_element(J):
     e = J.ConcreteNDArray(np.zeros(0, np.float32), J.Shape(0, 3), J.DType.FLOAT32)
     assert e.add(e).shape() == J.Shape(0, 3)
     assert e.exp().shape() == J.Shape(0, 3)
+
+
+@pytest.mark.parametrize("rows,cols", [(1, 1), (3, 5), (37, 53), (64, 1000), (129, 4097)])
+def test_split_f32_layout(J, rows, cols):
+    """j4c_split_f32: hi is TF32 (low 13 mantissa bits clear), lo = tf32(x - hi),
+    rows padded to j4c_split_pitch(cols) with zeros."""
+    import torch
+    r = rng(rows * 31 + cols)
+    x = (r.standard_normal((rows, cols)) * np.exp(r.uniform(-20, 20, (rows, cols)))).astype(np.float32)
+    a = dev(J, x)
+    pitch = _lib.lib().j4c_split_pitch(cols)
+    assert pitch % 4 == 0 and cols <= pitch < cols + 4
+    hi = torch.full((rows * pitch,), 7.0, dtype=torch.float32, device=a.tensor().device)
+    lo = torch.full((rows * pitch,), 7.0, dtype=torch.float32, device=a.tensor().device)
+    _lib.call("j4c_split_f32", a.data_ptr(), rows, cols, hi.data_ptr(), lo.data_ptr(), a._stream())
+    h = hi.cpu().numpy().reshape(rows, pitch)
+    l = lo.cpu().numpy().reshape(rows, pitch)
+    assert np.all(h[:, cols:] == 0) and np.all(l[:, cols:] == 0)
+    h, l = h[:, :cols], l[:, :cols]
+    assert np.all(h.view(np.uint32) & 0x1FFF == 0) and np.all(l.view(np.uint32) & 0x1FFF == 0)
+    err = np.abs(h.astype(np.float64) + l - x)
+    assert np.all(err <= np.abs(x) * 2.0 ** -21)
+
+
+@pytest.mark.parametrize("ta,tb", [(0, 0), (1, 0), (0, 1), (1, 1)])
+def test_dot_ws_and_split_reuse(J, ta, tb):
+    """j4c_dot_ws (split inside) and j4c_dot_split reusing one split of A
+    for two products with different layouts of A."""
+    import torch
+    M, K, N = 200, 300, 150
+    r = rng(ta * 2 + tb + 5)
+    A = r.uniform(-1, 1, (M, K)).astype(np.float32)
+    B = r.uniform(-1, 1, (K, N)).astype(np.float32)
+    a = dev(J, A.T.copy() if ta else A)
+    b = dev(J, B.T.copy() if tb else B)
+    ws_bytes = _lib.lib().j4c_dot_workspace_size(0, M, K, N)
+    ws = torch.empty(ws_bytes, dtype=torch.uint8, device=a.tensor().device)
+    out = torch.empty(M * N, dtype=torch.float32, device=a.tensor().device)
+    _lib.call("j4c_dot_ws", 0, a.data_ptr(), b.data_ptr(), out.data_ptr(), M, K, N, ta, tb, ws.data_ptr(),
+              ws_bytes, a._stream())
+    ref = orc.dot(A, B, threads=8)
+    assert_rel(out.cpu().numpy().reshape(M, N), ref, TOL_REDUCTION, "dot_ws")
+    # the split of `a` used again, now as the transposed operand of a second product
+    from jax4j_b200.core import _tf32_split
+    ah, al = _tf32_split(a)
+    C2 = r.uniform(-1, 1, (M, 70)).astype(np.float32) if not ta else r.uniform(-1, 1, (K, 70)).astype(np.float32)
+    c2 = dev(J, C2)
+    ch, cl = _tf32_split(c2)
+    out2 = torch.empty(K * 70 if not ta else M * 70, dtype=torch.float32, device=a.tensor().device)
+    if not ta:   # a stored [M, K]: a^T . c2 = [K, M] . [M, 70]
+        _lib.call("j4c_dot_split", ah.data_ptr(), al.data_ptr(), ch.data_ptr(), cl.data_ptr(), out2.data_ptr(),
+                  K, M, 70, 1, 0, a._stream())
+        ref2 = orc.dot(np.ascontiguousarray(A.T), C2, threads=8)
+    else:        # a stored [K, M]: a^T . c2 = [M, K] . [K, 70]
+        _lib.call("j4c_dot_split", ah.data_ptr(), al.data_ptr(), ch.data_ptr(), cl.data_ptr(), out2.data_ptr(),
+                  M, K, 70, 1, 0, a._stream())
+        ref2 = orc.dot(A, C2, threads=8)
+    assert_rel(out2.cpu().numpy().reshape(ref2.shape), ref2, TOL_REDUCTION, "split reuse")
+
+
+@pytest.mark.parametrize("rows,cols", [(1, 1), (3, 5), (37, 53), (64, 1000), (130, 67)])
+def test_split_f32_transposed_layout(J, rows, cols):
+    """j4c_split_f32_transposed: the split of x^T as [cols, pitch(rows)], padding zero."""
+    import torch
+    r = rng(rows * 17 + cols)
+    x = r.standard_normal((rows, cols)).astype(np.float32)
+    a = dev(J, x)
+    pitch = _lib.lib().j4c_split_pitch(rows)
+    hi = torch.full((cols * pitch,), 7.0, dtype=torch.float32, device=a.tensor().device)
+    lo = torch.full((cols * pitch,), 7.0, dtype=torch.float32, device=a.tensor().device)
+    _lib.call("j4c_split_f32_transposed", a.data_ptr(), rows, cols, hi.data_ptr(), lo.data_ptr(), a._stream())
+    h = hi.cpu().numpy().reshape(cols, pitch)
+    l = lo.cpu().numpy().reshape(cols, pitch)
+    assert np.all(h[:, rows:] == 0) and np.all(l[:, rows:] == 0)
+    h, l = h[:, :rows], l[:, :rows]
+    assert np.all(h.view(np.uint32) & 0x1FFF == 0)
+    err = np.abs(h.astype(np.float64) + l - x.T)
+    assert np.all(err <= np.abs(x.T) * 2.0 ** -21)
