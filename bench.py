@@ -56,7 +56,7 @@ def parse():
     p.add_argument("--batch", type=int, default=BATCH, help="samples per GPU (profiling runs only)")
     p.add_argument("--no-cpu-baseline", action="store_true")
     p.add_argument("--no-e2e", action="store_true")
-    p.add_argument("--workload", default="dp_step", choices=["dp_step", "gemm", "sweep"],
+    p.add_argument("--workload", default="dp_step", choices=["dp_step", "gemm", "sweep", "cfg0", "cfg2", "collectives"],
                    help="dp_step is the headline; gemm/sweep are single-kernel measurements "
                         "used for profiling")
     p.add_argument("--m", type=int, default=8192)
@@ -64,6 +64,7 @@ def parse():
     p.add_argument("--n", type=int, default=4096)
     p.add_argument("--trans", default="nn", choices=["nn", "tn", "nt", "tt"],
                    help="gemm workload: whether A and B are stored transposed")
+    p.add_argument("--max-bytes", type=int, default=1 << 30, help="collectives: largest message per rank")
     p.add_argument("--rows", type=int, default=4096)
     p.add_argument("--cols", type=int, default=16384)
     return p.parse_args()
@@ -476,6 +477,227 @@ def run_sweep(args):
                       "effective_GBps": (8 * n + 8 * R) / (ms / 1e3) / 1e9}), flush=True)
 
 
+# ---------------------------------------------------------------------------
+# the other configurations: their own measurements (parity is in tests/)
+# ---------------------------------------------------------------------------
+def _spmd_setup():
+    """(rank, world, devices) for this process: torchrun ranks or one GPU."""
+    import torch
+    import jax4j_b200 as J
+    from jax4j_b200 import distributed
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    if world > 1:
+        st = distributed.initialize(timeout_s=120.0)
+        return st.rank, world, distributed.global_devices()
+    torch.cuda.set_device(0)
+    return 0, 1, [J.Device.defaultDevice()]
+
+
+def _max_over_ranks(v: float, world: int) -> float:
+    if world == 1:
+        return v
+    import torch
+    import torch.distributed as dist
+    t = torch.tensor([v], dtype=torch.float64)
+    dist.all_reduce(t, op=dist.ReduceOp.MAX)
+    return float(t.item())
+
+
+def _timed(fn, steps: int, warmup: int, world: int) -> float:
+    """ms per call: device-timed on this rank's stream, max over ranks."""
+    import torch
+    from jax4j_b200 import distributed
+    for _ in range(warmup):
+        fn()
+    torch.cuda.synchronize()
+    distributed.barrier()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record()
+    for _ in range(steps):
+        fn()
+    e1.record()
+    torch.cuda.synchronize()
+    return _max_over_ranks(e0.elapsed_time(e1) / steps, world)
+
+
+def _finish(world: int):
+    from jax4j_b200 import distributed
+    if world > 1:
+        distributed.barrier()
+        distributed.shutdown()
+
+
+def run_cfg0(args):
+    """Config 0: 2-layer tanh MLP 784-512-10, x [2,256,784] ~ N(0,1) sharded
+    over D = 2 pmap devices (two ranks, or two shards on one GPU).  (i) grad of
+    pmap w.r.t. x; (ii) pmap of gradTree over {W1,b1,W2,b2} + psumTree."""
+    import torch
+    import jax4j_b200 as J
+    rank, world, devices = _spmd_setup()
+    if world == 1:
+        devices = [J.Device.defaultDevice(), J.Device(None, "shard1")]
+    D = len(devices)
+    dims, B = [784, 512, 10], 256
+    keys = J.Random.split(J.PRNGKey.key(0), 3)
+    params = {"w1": J.Random.glorotUniform(keys[0], J.Shape(784, 512), 784, 512),
+              "b1": J.ConcreteNDArray.full(J.Shape(512), 0.0),
+              "w2": J.Random.glorotUniform(keys[1], J.Shape(512, 10), 512, 10),
+              "b2": J.ConcreteNDArray.full(J.Shape(10), 0.0)}
+    x_all = J.Random.normal(J.PRNGKey.key(0), J.Shape(2, B, 784))
+    lab = torch.clamp((J.Random.uniform(keys[2], J.Shape(2 * B)).tensor() * 10).to(torch.int64), max=9)
+    t_t = torch.zeros(2 * B * 10, dtype=torch.float32, device="cuda")
+    t_t.view(2 * B, 10).scatter_(1, lab.view(-1, 1), 1.0)
+    t_all = J.ConcreteNDArray._wrap(t_t, J.Shape(2, B, 10), J.DType.FLOAT32, J.Device.defaultDevice())
+    if world > 1:
+        x_in = J.LocalShard(J.ConcreteNDArray._wrap(x_all.tensor().view(2, -1)[rank].clone(),
+                                                    J.Shape(B, 784), J.DType.FLOAT32, J.Device.defaultDevice()), D)
+        t_in = J.LocalShard(J.ConcreteNDArray._wrap(t_t.view(2, -1)[rank].clone(), J.Shape(B, 10),
+                                                    J.DType.FLOAT32, J.Device.defaultDevice()), D)
+    else:
+        x_in, t_in = x_all, t_all
+    neg = J.ConcreteNDArray.scalar(-1.0)
+
+    def loss_fn(p, xs, ts):
+        h = xs.dot(p["w1"]).add(p["b1"]).tanh()
+        logits = h.dot(p["w2"]).add(p["b2"])
+        return J.Nn.softmax(logits).log().mul(ts).sum(-1).mean().mul(neg)
+
+    def part_i():
+        return J.JAX.grad(lambda xx: J.JAX.pmap(lambda xs, ts: loss_fn(params, xs, ts), devices)(xx, t_in).sum())(
+            x_in)
+
+    def body_ii(xs, ts):
+        v, g = J.JAX.valueAndGradTree(
+            lambda tr: loss_fn({k: tr.children[k].value for k in params}, xs, ts))(J.PyTree.dictOf(params))
+        J.Lax.psumTree(g)
+        return v
+
+    pm = J.JAX.pmap(body_ii, devices)
+
+    def part_ii():
+        return pm(x_in, t_in)
+
+    ms_i = _timed(part_i, args.steps, args.warmup, world)
+    ms_ii = _timed(part_ii, args.steps, args.warmup, world)
+    if rank == 0:
+        samples = 2 * B
+        line = {"metric": "config-0 grad-step samples/s", "unit": "samples/s", "n_gpus": world,
+                "config": {"workload": "2-layer tanh MLP 784-512-10, x [2,256,784], D=2 pmap devices"},
+                "grad_wrt_x": {"value": samples / (ms_i / 1e3), "ms_per_step": ms_i,
+                               "flop_per_sample": 1626112},
+                "grad_tree_psum": {"value": samples / (ms_ii / 1e3), "ms_per_step": ms_ii,
+                                   "flop_per_sample": 1636352, "psum_floats": 407050},
+                "bound": "latency (launch and host dispatch)"}
+        if world == 1 and not args.no_cpu_baseline:
+            line["cpu_baseline"] = _cfg0_cpu()
+        print(json.dumps(line), flush=True)
+    _finish(world)
+
+
+def _cfg0_cpu() -> dict:
+    import numpy as np
+    from oracle import oracle as orc
+    keys = orc.split(0, 3)
+    ws = [orc.glorot_uniform(keys[0], (784, 512), 784, 512), orc.glorot_uniform(keys[1], (512, 10), 512, 10)]
+    bs = [np.zeros(512, np.float32), np.zeros(10, np.float32)]
+    x = orc.normal(0, (2 * 256 * 784,)).reshape(2, 256, 784)
+    lab = np.minimum((orc.uniform(keys[2], (512,)) * 10).astype(np.int64), 9)
+    t = np.zeros((512, 10), np.float32)
+    t[np.arange(512), lab] = 1
+    t = t.reshape(2, 256, 10)
+    threads = orc.nproc()
+    reps = 0
+    t0 = time.perf_counter()
+    while time.perf_counter() - t0 < 10.0:
+        for d in range(2):  # the two shards, as the reference's pmap runs them
+            orc.mlp_loss_grad(ws, bs, x[d], t[d], act="tanh", threads=threads)
+        reps += 1
+    dt = time.perf_counter() - t0
+    return {"value": 512 * reps / dt, "unit": "samples/s", "cores": threads, "kind": "port",
+            "sample": f"{reps} full steps (both shards, grad over the params)"}
+
+
+def run_cfg2(args):
+    """Config 2: each shard computes A_i [4096,8192] . B [8192,4096]
+    (A ~ U(-1,1) sharded on the leading axis, B replicated, seed 2) and the
+    results are gathered with Lax.allGather."""
+    import jax4j_b200 as J
+    rank, world, devices = _spmd_setup()
+    D = len(devices)
+    M, K, N = 4096, 8192, 4096
+    A = J.Random.uniform(J.PRNGKey.key(2), J.Shape(D * M, K), -1.0, 1.0, offset=rank * M * K,
+                         count=M * K).reshape(J.Shape(M, K))
+    B = J.Random.uniform(J.Random.split(J.PRNGKey.key(2), 2)[1], J.Shape(K, N), -1.0, 1.0)
+    a_in = J.LocalShard(A, D) if world > 1 else A.reshape(J.Shape(1, M, K))
+    pm = J.JAX.pmap(lambda a: J.Lax.allGather(a.dot(B), D), devices)
+
+    def step():
+        return pm(a_in)
+
+    ms = _timed(step, args.steps, args.warmup, world)
+    if rank == 0:
+        flop = 2.0 * M * K * N * D
+        print(json.dumps({"metric": "config-2 pmap dot + allGather TFLOP/s", "unit": "TFLOP/s",
+                          "value": flop / (ms / 1e3) / 1e12, "ms_per_step": ms, "n_gpus": world,
+                          "config": {"workload": "per shard [4096,8192].[8192,4096] FP32 (3xTF32), "
+                                                 "allGather of the [4096,4096] results"},
+                          "allgather_bytes_per_rank": 4 * M * N}), flush=True)
+    _finish(world)
+
+
+def run_collectives(args):
+    """Config 3: Lax.psum / Lax.allGather of float32 vectors ~ N(0,1), 4 KB to
+    1 GB per rank.  Reports NCCL-convention bus GB/s for the raw device
+    collective (back-to-back on the stream) and per call through JAX.pmap,
+    plus grad through psum (its VJP is a psum) at 64 MB."""
+    import torch
+    import jax4j_b200 as J
+    from jax4j_b200 import _lib, distributed
+    rank, world, devices = _spmd_setup()
+    D = len(devices)
+    if D == 1:
+        if rank == 0:
+            print(json.dumps({"metric": "psum bus GB/s", "n_gpus": 1,
+                              "note": "a collective over one device moves no data; run with --gpus >= 2"}))
+        return
+    comm = distributed.state().comm
+    stream = torch.cuda.current_stream().cuda_stream
+    rows = []
+    size = 4096
+    while size <= args.max_bytes:
+        n = size // 4
+        x = J.Random.normal(J.PRNGKey.key(4), J.Shape(n), offset=rank * n, count=n)
+        out = torch.empty(n, dtype=torch.float32, device="cuda")
+        gat = torch.empty(n * D, dtype=torch.float32, device="cuda")
+        iters = max(5, min(200, int(2e9 / max(size, 1) / 10)))
+        ar_ms = _timed(lambda: _lib.call("j4c_psum", comm, 0, x.data_ptr(), out.data_ptr(), n, stream),
+                       iters, 3, world)
+        ag_ms = _timed(lambda: _lib.call("j4c_all_gather", comm, 0, x.data_ptr(), gat.data_ptr(), n, stream),
+                       iters, 3, world)
+        pm = J.JAX.pmap(lambda s: J.Lax.psum(s), devices)
+        api_ms = _timed(lambda: pm(J.LocalShard(x, D)), max(3, iters // 10), 2, world)
+        rows.append({"bytes": size, "allreduce_ms": ar_ms,
+                     "allreduce_busbw_GBps": size / (ar_ms / 1e3) * 2 * (D - 1) / D / 1e9,
+                     "allgather_ms": ag_ms,
+                     "allgather_busbw_GBps": size * D / (ag_ms / 1e3) * (D - 1) / D / 1e9,
+                     "pmap_psum_ms": api_ms})
+        del x, out, gat
+        size *= 4
+    n = (64 << 20) // 4
+    x = J.Random.normal(J.PRNGKey.key(5), J.Shape(n), offset=rank * n, count=n)
+    gpm = J.JAX.pmap(lambda s: J.JAX.grad(lambda v: J.Lax.psum(v.mul(v)).sum())(s), devices)
+    grad_ms = _timed(lambda: gpm(J.LocalShard(x, D)), 5, 2, world)
+    if rank == 0:
+        peak = max(r["allreduce_busbw_GBps"] for r in rows)
+        print(json.dumps({"metric": "psum bus GB/s", "value": peak, "unit": "GB/s", "n_gpus": D,
+                          "config": {"workload": "Lax.psum / Lax.allGather, float32, 4 KB..%d MB per rank"
+                                                 % (args.max_bytes >> 20)},
+                          "sizes": rows, "grad_through_psum_64MB_ms": grad_ms,
+                          "peak_source": "NCCL busBW convention: allreduce (S/t)*2(D-1)/D, "
+                                         "allgather (D*S/t)*(D-1)/D"}), flush=True)
+    _finish(world)
+
+
 def main():
     args = parse()
     if args.impl == "reference":
@@ -484,6 +706,12 @@ def main():
         run_gemm(args)
     elif args.workload == "sweep":
         run_sweep(args)
+    elif args.workload == "cfg0":
+        run_cfg0(args)
+    elif args.workload == "cfg2":
+        run_cfg2(args)
+    elif args.workload == "collectives":
+        run_collectives(args)
     else:
         run_ours(args)
 

@@ -32,9 +32,14 @@ static int nccl_status(ncclResult_t r, const char *what) {
 using Clock = std::chrono::steady_clock;
 
 // Polls the communicator until no operation is in progress or the deadline
-// passes (then aborts it).
+// passes (then aborts it).  A collective on a non-blocking communicator
+// usually finishes enqueueing within microseconds, so the first 2 ms are a
+// busy poll; only a longer wait (communicator setup, a slow peer) sleeps
+// between polls.
 static int wait_comm_ready(j4c_comm c, const char *what) {
-    auto deadline = Clock::now() + std::chrono::milliseconds(c->timeout_ms);
+    const auto start = Clock::now();
+    const auto spin_until = start + std::chrono::milliseconds(2);
+    auto deadline = start + std::chrono::milliseconds(c->timeout_ms);
     while (true) {
         ncclResult_t st = ncclSuccess;
         ncclResult_t r = ncclCommGetAsyncError(c->nccl, &st);
@@ -47,7 +52,8 @@ static int wait_comm_ready(j4c_comm c, const char *what) {
             return set_error(J4C_E_TIMEOUT, "%s: timed out after %lld ms; communicator aborted", what,
                              (long long)c->timeout_ms);
         }
-        std::this_thread::sleep_for(std::chrono::microseconds(50));
+        if (Clock::now() < spin_until) std::this_thread::yield();
+        else std::this_thread::sleep_for(std::chrono::microseconds(50));
     }
 }
 

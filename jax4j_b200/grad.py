@@ -252,7 +252,7 @@ def execute_primitive(p: Primitive, eq, inputs: List[NDArray]) -> NDArray:
     if p == Primitive.CAST: return inputs[0].astype(eq.metadata)
     if p == Primitive.PMAP:
         m: PmapMeta = eq.metadata
-        shards = [_pm.split(x, m.numDevices()) for x in inputs]
+        shards = [_pm.shards_of(x, m.numDevices()) for x in inputs]
         return _pm.run_forward_jaxpr(m.bodyJaxpr, m.devices, shards)
     if p == Primitive.PSUM:
         return _pm.psum_value(inputs[0])
@@ -337,8 +337,8 @@ def compute_vjps(p: Primitive, eq, g: ConcreteNDArray, inputs: List[NDArray], ou
     if p == Primitive.PMAP:
         m: PmapMeta = eq.metadata
         D = m.numDevices()
-        in_shards = [_pm.split(x, D) for x in inputs]
-        g_shards = _pm.split(g, D)
+        in_shards = [_pm.shards_of(x, D) for x in inputs]
+        g_shards = _pm.shards_of(g, D)
         g_in = _pm.run_backward_jaxpr(m.bodyJaxpr, m.devices, in_shards, g_shards)
         return [_pm.stack([gi[k] for gi in g_in]) for k in range(len(inputs))]
     if p == Primitive.PSUM:

@@ -326,6 +326,22 @@ def _bind(device: Device):
     return torch.cuda.device(device.ordinal())
 
 
+def shards_of(x: NDArray, D: int) -> List[Optional[ConcreteNDArray]]:
+    """split(x, D), except that a LocalShard yields only this rank's shard
+    (the other slots are None; one-process-per-GPU runs read only their own)."""
+    if isinstance(x, LocalShard):
+        st = _spmd()
+        if st is None:
+            raise IllegalArgumentException("a LocalShard input needs a one-process-per-GPU run "
+                                           "(distributed.initialize)")
+        if x.num_devices != D:
+            raise IllegalArgumentException("LocalShard built for a different device count")
+        out: List[Optional[ConcreteNDArray]] = [None] * D
+        out[st.rank] = x.local
+        return out
+    return split(x, D)
+
+
 def _local_inputs(inputs: Sequence[NDArray], D: int, rank: int) -> List[ConcreteNDArray]:
     out = []
     for x in inputs:

@@ -56,6 +56,31 @@ def main():
                      **{"g_" + k: g[k].value.numpy() for k in params})
         else:
             np.savez(args.out + f".rank{rank}", x=x.numpy(), t=t)
+    elif args.scenario == "grad_x":
+        # grad of a pmap'd loss w.r.t. its sharded input, with LocalShard inputs
+        keys = J.Random.split(J.PRNGKey.key(3), 2)
+        params = {"w1": J.Random.glorotUniform(keys[0], J.Shape(64, 32), 64, 32),
+                  "b1": J.ConcreteNDArray.full(J.Shape(32), 0.0),
+                  "w2": J.Random.glorotUniform(keys[1], J.Shape(32, 10), 32, 10),
+                  "b2": J.ConcreteNDArray.full(J.Shape(10), 0.0)}
+        B = 16
+        x = J.Random.normal(J.PRNGKey.key(1), J.Shape(D * B, 64), offset=rank * B * 64,
+                            count=B * 64).reshape(J.Shape(B, 64))
+        lab = (np.arange(D * B) * 31 % 10)[rank * B:(rank + 1) * B]
+        t = np.zeros((B, 10), np.float32)
+        t[np.arange(B), lab] = 1
+        tt = J.ConcreteNDArray.of(t)
+        neg = J.ConcreteNDArray.scalar(-1.0)
+
+        def loss(xs, ts):
+            h = xs.dot(params["w1"]).add(params["b1"]).tanh()
+            logits = h.dot(params["w2"]).add(params["b2"])
+            return J.Nn.softmax(logits).log().mul(ts).sum(-1).mean().mul(neg)
+
+        tl = J.LocalShard(tt, D)
+        gx = J.JAX.grad(lambda xx: J.JAX.pmap(loss, devices)(xx, tl).sum())(J.LocalShard(x, D))
+        np.savez(args.out + f".rank{rank}", gx=gx.numpy(), x=x.numpy(), t=t,
+                 **{k: params[k].numpy() for k in params})
     elif args.scenario == "leave":
         x = J.ConcreteNDArray.of(np.ones((D, 8), np.float32))
         J.JAX.pmap(lambda s: J.Lax.psum(s), devices)(x).toFloatArray()

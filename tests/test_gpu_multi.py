@@ -43,7 +43,7 @@ def _torchrun(scenario, out, env_extra=None, timeout=240):
     env = dict(os.environ)
     env.update(env_extra or {})
     cmd = [sys.executable, "-m", "torch.distributed.run", "--nnodes=1", "--nproc-per-node", "2",
-           "--master-addr", "127.0.0.1", "--master-port", str(29600 + os.getpid() % 300),
+           "--master-addr", "127.0.0.1", "--master-port", str(29600 + (os.getpid() + 37 * len(scenario)) % 300),
            os.path.join(ROOT, "tests", "spmd_gpu_worker.py"), "--scenario", scenario, "--out", out]
     return subprocess.run(cmd, env=env, capture_output=True, text=True, timeout=timeout)
 
@@ -63,6 +63,22 @@ def test_one_process_per_gpu_dp_step_matches_oracle(tmp_path):
         assert_rel(z["g_" + k], orc.psum([per[0][1][i], per[1][1][i]]), TOL_REDUCTION, k)
     for i, k in enumerate(["b1", "b2"]):
         assert_rel(z["g_" + k], orc.psum([per[0][2][i], per[1][2][i]]), TOL_REDUCTION, k)
+
+
+@needs2
+def test_one_process_per_gpu_grad_wrt_sharded_input(tmp_path):
+    """JAX.grad of a pmap'd loss w.r.t. a LocalShard input: every rank gets
+    the full [D, B, 64] cotangent, each slice equal to that shard's own gx."""
+    out = str(tmp_path / "gx")
+    r = _torchrun("grad_x", out)
+    assert r.returncode == 0, r.stderr[-2000:]
+    z = [np.load(out + f".rank{k}.npz") for k in range(2)]
+    ws, bs = [z[0]["w1"], z[0]["w2"]], [z[0]["b1"], z[0]["b2"]]
+    for k in range(2):
+        for shard in range(2):
+            ref = orc.mlp_loss_grad(ws, bs, z[shard]["x"], z[shard]["t"], act="tanh", want_gx=True,
+                                    threads=4)[3]
+            assert_rel(z[k]["gx"][shard], ref, TOL_REDUCTION, f"rank {k} shard {shard}")
 
 
 @needs2
