@@ -464,7 +464,10 @@ class ConcreteNDArray(NDArray):
         return self._device
 
     def tensor(self) -> torch.Tensor:
-        """The backing HBM buffer (flat)."""
+        """The backing HBM buffer (flat).  Arrays are immutable: a caller that
+        refills this buffer in place (an input slot reused across steps) wraps
+        it in a new array afterwards, since this one may keep a split of its
+        old values for dot."""
         return self._t
 
     def data_ptr(self) -> int:

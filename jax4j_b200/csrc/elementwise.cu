@@ -42,7 +42,7 @@ __device__ __forceinline__ float unary_op(float x) {
     else if constexpr (OP == J4C_COS) return cosf(x);
     else if constexpr (OP == J4C_TANH) return tanhf(x);
     else if constexpr (OP == J4C_RELU) return java_max(0.0f, x);
-    else return __fdiv_rn(1.0f, __fadd_rn(1.0f, expf(-x)));  // SIGMOID
+    else return __frcp_rn(__fadd_rn(1.0f, expf(-x)));  // SIGMOID: correctly rounded 1 / (1 + e^-x)
 }
 template <int OP>
 __device__ __forceinline__ double unary_op(double x) {
@@ -52,43 +52,37 @@ __device__ __forceinline__ double unary_op(double x) {
     else if constexpr (OP == J4C_COS) return cos(x);
     else if constexpr (OP == J4C_TANH) return tanh(x);
     else if constexpr (OP == J4C_RELU) return java_max(0.0, x);
-    else return __ddiv_rn(1.0, __dadd_rn(1.0, exp(-x)));
+    else return __drcp_rn(__dadd_rn(1.0, exp(-x)));
 }
 
 // ---- vector helpers ------------------------------------------------------------
-template <typename T>
-struct Vec;  // 16-byte vector of T
-template <>
-struct Vec<float> {
-    using type = float4;
-    static constexpr int N = 4;
-};
-template <>
-struct Vec<double> {
-    using type = double2;
-    static constexpr int N = 2;
-};
-template <>
-struct Vec<int32_t> {
-    using type = int4;
-    static constexpr int N = 4;
-};
-
+// A lane moves VEC consecutive elements as one 16-byte (or 8- / 4-byte)
+// access, so each warp-wide access is contiguous; the streaming kernels below
+// keep U such accesses per operand in flight per thread (grid-stride steps
+// u * stride apart, all loads issued before any result is stored).
 template <typename T, int N>
-struct Pack {
+struct alignas(16) Pack {
     T v[N];
 };
 
+// N elements at p: consecutive (stride 1; p aligned to min(16, N*sizeof(T))
+// bytes), N copies of p[0] (stride 0), or a strided gather.
 template <typename T, int N>
 __device__ __forceinline__ Pack<T, N> load_pack(const T *p, int64_t stride) {
+    constexpr int BYTES = N * (int)sizeof(T);
     Pack<T, N> r;
     if (stride == 0) {
-        T x = p[0];
+        const T x = p[0];
 #pragma unroll
         for (int i = 0; i < N; i++) r.v[i] = x;
-    } else if (N * sizeof(T) == 16 && stride == 1) {
-        *reinterpret_cast<typename Vec<T>::type *>(r.v) =
-            __ldg(reinterpret_cast<const typename Vec<T>::type *>(p));
+    } else if (stride == 1 && BYTES % 16 == 0) {
+#pragma unroll
+        for (int c = 0; c < BYTES / 16; c++)
+            reinterpret_cast<uint4 *>(r.v)[c] = __ldg(reinterpret_cast<const uint4 *>(p) + c);
+    } else if (stride == 1 && BYTES == 8) {
+        *reinterpret_cast<uint2 *>(r.v) = __ldg(reinterpret_cast<const uint2 *>(p));
+    } else if (stride == 1 && BYTES == 4) {
+        *reinterpret_cast<unsigned int *>(r.v) = __ldg(reinterpret_cast<const unsigned int *>(p));
     } else {
 #pragma unroll
         for (int i = 0; i < N; i++) r.v[i] = p[i * stride];
@@ -98,56 +92,85 @@ __device__ __forceinline__ Pack<T, N> load_pack(const T *p, int64_t stride) {
 
 template <typename T, int N>
 __device__ __forceinline__ void store_pack(T *p, const Pack<T, N> &r) {
-    if constexpr (N * sizeof(T) == 16) {
-        *reinterpret_cast<typename Vec<T>::type *>(p) =
-            *reinterpret_cast<const typename Vec<T>::type *>(r.v);
+    constexpr int BYTES = N * (int)sizeof(T);
+    if constexpr (BYTES % 16 == 0) {
+#pragma unroll
+        for (int c = 0; c < BYTES / 16; c++)
+            reinterpret_cast<uint4 *>(p)[c] = reinterpret_cast<const uint4 *>(r.v)[c];
+    } else if constexpr (BYTES == 8) {
+        *reinterpret_cast<uint2 *>(p) = *reinterpret_cast<const uint2 *>(r.v);
+    } else if constexpr (BYTES == 4) {
+        *reinterpret_cast<unsigned int *>(p) = *reinterpret_cast<const unsigned int *>(r.v);
     } else {
 #pragma unroll
         for (int i = 0; i < N; i++) p[i] = r.v[i];
     }
 }
 
+// Offsets of output element i in each operand (rank-1 shapes need no division).
+__device__ __forceinline__ void elem_offsets(const Indexer &ix, int64_t i, int64_t (&off)[3]) {
+    if (ix.rank == 1) {
+        off[0] = i * ix.stride[0][0];
+        off[1] = i * ix.stride[1][0];
+        off[2] = i * ix.stride[2][0];
+    } else {
+        index_offsets(ix, i, off);
+    }
+}
+
+// Whether VEC consecutive outputs per thread step may use vector accesses:
+// the innermost collapsed dim is a multiple of VEC and every contiguous
+// operand (and the output) is 16-byte aligned.
+inline bool vec_ok(const Indexer &ix, int vec, const void *a, const void *b, const void *out,
+                   int out_align = 16) {
+    const int last = ix.rank - 1;
+    return ix.size[last] % vec == 0 && (reinterpret_cast<uintptr_t>(out) % out_align == 0) &&
+           (ix.stride[0][last] != 1 || aligned16(a)) && (ix.stride[1][last] != 1 || aligned16(b));
+}
+
 // ---- binary -----------------------------------------------------------------
-// VEC consecutive outputs per thread step; VEC > 1 requires the innermost
-// collapsed dim to be a multiple of VEC and 16-byte aligned pointers.
-template <typename T, int OP, int VEC>
+// VEC consecutive outputs per lane access (see vec_ok), U accesses in flight.
+template <typename T, int OP, int VEC, int U>
 __global__ void __launch_bounds__(256) binary_kernel(Indexer ix, const T *__restrict__ a,
                                                      const T *__restrict__ b, T *__restrict__ out,
                                                      int64_t n) {
-    const int64_t nvec = n / VEC;
+    const int64_t nvec = n / VEC, stride = (int64_t)gridDim.x * blockDim.x;
     const int64_t sa0 = ix.stride[0][ix.rank - 1], sb0 = ix.stride[1][ix.rank - 1];
-    for (int64_t v = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; v < nvec;
-         v += (int64_t)gridDim.x * blockDim.x) {
-        int64_t i = v * VEC;
-        int64_t off[3];
-        if (ix.rank == 1) {
-            off[0] = i * ix.stride[0][0];
-            off[1] = i * ix.stride[1][0];
-        } else {
-            index_offsets(ix, i, off);
-        }
-        Pack<T, VEC> pa = load_pack<T, VEC>(a + off[0], sa0);
-        Pack<T, VEC> pb = load_pack<T, VEC>(b + off[1], sb0);
-        Pack<T, VEC> r;
+    for (int64_t v0 = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; v0 < nvec; v0 += U * stride) {
+        Pack<T, VEC> pa[U], pb[U];
 #pragma unroll
-        for (int k = 0; k < VEC; k++) r.v[k] = binary_op<OP, T>(pa.v[k], pb.v[k]);
-        store_pack<T, VEC>(out + i, r);
+        for (int u = 0; u < U; u++) {
+            const int64_t v = v0 + u * stride;
+            if (v < nvec) {
+                int64_t off[3];
+                elem_offsets(ix, v * VEC, off);
+                pa[u] = load_pack<T, VEC>(a + off[0], sa0);
+                pb[u] = load_pack<T, VEC>(b + off[1], sb0);
+            }
+        }
+#pragma unroll
+        for (int u = 0; u < U; u++) {
+            const int64_t v = v0 + u * stride;
+            if (v < nvec) {
+                Pack<T, VEC> r;
+#pragma unroll
+                for (int k = 0; k < VEC; k++) r.v[k] = binary_op<OP, T>(pa[u].v[k], pb[u].v[k]);
+                store_pack<T, VEC>(out + v * VEC, r);
+            }
+        }
     }
 }
 
 template <typename T, int OP>
 static int launch_binary(const Indexer &ix, const void *a, const void *b, void *out, int64_t n,
                          cudaStream_t s) {
-    constexpr int V = Vec<T>::N;
-    bool vec_ok = (ix.size[ix.rank - 1] % V == 0) && aligned16(out) &&
-                  (ix.stride[0][ix.rank - 1] != 1 || aligned16(a)) &&
-                  (ix.stride[1][ix.rank - 1] != 1 || aligned16(b));
-    if (vec_ok) {
-        binary_kernel<T, OP, V><<<grid_for(n / V, 256), 256, 0, s>>>(
+    constexpr int V = 16 / sizeof(T), U = 1;  // U = 2 measured slower for a scalar operand
+    if (vec_ok(ix, V, a, b, out)) {
+        binary_kernel<T, OP, V, U><<<grid_for(ceil_div(n / V, U), 256), 256, 0, s>>>(
             ix, (const T *)a, (const T *)b, (T *)out, n);
     } else {
-        binary_kernel<T, OP, 1><<<grid_for(n, 256), 256, 0, s>>>(ix, (const T *)a, (const T *)b,
-                                                                 (T *)out, n);
+        binary_kernel<T, OP, 1, U><<<grid_for(ceil_div(n, U), 256), 256, 0, s>>>(ix, (const T *)a, (const T *)b,
+                                                                                  (T *)out, n);
     }
     J4C_LAUNCH_CHECK("binary_kernel");
     return J4C_OK;
@@ -168,80 +191,101 @@ static int dispatch_binary(int prim, const Indexer &ix, const void *a, const voi
 }
 
 // ---- compare ----------------------------------------------------------------
-template <typename T, int OP>
+// VEC outputs per lane access; 16 (one 16-byte store of BOOLs per lane, the
+// operands read as 4 (8) consecutive 16-byte pieces) measured fastest.
+template <typename T, int OP, int VEC, int U>
 __global__ void __launch_bounds__(256) compare_kernel(Indexer ix, const T *__restrict__ a,
                                                       const T *__restrict__ b,
                                                       uint8_t *__restrict__ out, int64_t n) {
-    // 4 outputs per step so each thread stores one 32-bit word.
-    const int64_t nvec = n / 4;
+    const int64_t nvec = n / VEC, stride = (int64_t)gridDim.x * blockDim.x;
     const int64_t sa0 = ix.stride[0][ix.rank - 1], sb0 = ix.stride[1][ix.rank - 1];
-    const bool vec = (ix.size[ix.rank - 1] % 4 == 0) && ((reinterpret_cast<uintptr_t>(out) & 3) == 0);
-    const int64_t steps = vec ? nvec : n;
-    for (int64_t v = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; v < steps;
-         v += (int64_t)gridDim.x * blockDim.x) {
-        if (vec) {
-            int64_t i = v * 4;
-            int64_t off[3];
-            index_offsets(ix, i, off);
-            uint32_t word = 0;
+    for (int64_t v0 = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; v0 < nvec; v0 += U * stride) {
+        Pack<T, VEC> pa[U], pb[U];
 #pragma unroll
-            for (int k = 0; k < 4; k++)
-                word |= (uint32_t)compare_op<OP, T>(a[off[0] + k * sa0], b[off[1] + k * sb0]) << (8 * k);
-            *reinterpret_cast<uint32_t *>(out + i) = word;
-        } else {
-            int64_t off[3];
-            index_offsets(ix, v, off);
-            out[v] = compare_op<OP, T>(a[off[0]], b[off[1]]);
+        for (int u = 0; u < U; u++) {
+            const int64_t v = v0 + u * stride;
+            if (v < nvec) {
+                int64_t off[3];
+                elem_offsets(ix, v * VEC, off);
+                pa[u] = load_pack<T, VEC>(a + off[0], sa0);
+                pb[u] = load_pack<T, VEC>(b + off[1], sb0);
+            }
+        }
+#pragma unroll
+        for (int u = 0; u < U; u++) {
+            const int64_t v = v0 + u * stride;
+            if (v < nvec) {
+                Pack<uint8_t, VEC> r;
+#pragma unroll
+                for (int k = 0; k < VEC; k++) r.v[k] = compare_op<OP, T>(pa[u].v[k], pb[u].v[k]);
+                store_pack<uint8_t, VEC>(out + v * VEC, r);
+            }
         }
     }
+}
+
+template <typename T, int OP>
+static void launch_compare(const Indexer &ix, const void *a, const void *b, uint8_t *out, int64_t n,
+                           cudaStream_t s) {
+    constexpr int U = 1;
+    if (vec_ok(ix, 16, a, b, out, 16))
+        compare_kernel<T, OP, 16, U><<<grid_for(n / 16, 256), 256, 0, s>>>(ix, (const T *)a, (const T *)b, out, n);
+    else if (vec_ok(ix, 4, a, b, out, 4))
+        compare_kernel<T, OP, 4, U><<<grid_for(n / 4, 256), 256, 0, s>>>(ix, (const T *)a, (const T *)b, out, n);
+    else
+        compare_kernel<T, OP, 1, U><<<grid_for(ceil_div(n, U), 256), 256, 0, s>>>(ix, (const T *)a,
+                                                                                   (const T *)b, out, n);
 }
 
 template <typename T>
 static int dispatch_compare(int prim, const Indexer &ix, const void *a, const void *b, uint8_t *out,
                             int64_t n, cudaStream_t s) {
-    unsigned g = grid_for(ceil_div(n, 4), 256);
-#define J4C_CMP(P)                                                                            \
-    case P:                                                                                   \
-        compare_kernel<T, P><<<g, 256, 0, s>>>(ix, (const T *)a, (const T *)b, out, n); \
-        break;
     switch (prim) {
-        J4C_CMP(J4C_GT)
-        J4C_CMP(J4C_GE)
-        J4C_CMP(J4C_LT)
-        J4C_CMP(J4C_LE)
-        J4C_CMP(J4C_EQ)
-        J4C_CMP(J4C_NE)
+    case J4C_GT: launch_compare<T, J4C_GT>(ix, a, b, out, n, s); break;
+    case J4C_GE: launch_compare<T, J4C_GE>(ix, a, b, out, n, s); break;
+    case J4C_LT: launch_compare<T, J4C_LT>(ix, a, b, out, n, s); break;
+    case J4C_LE: launch_compare<T, J4C_LE>(ix, a, b, out, n, s); break;
+    case J4C_EQ: launch_compare<T, J4C_EQ>(ix, a, b, out, n, s); break;
+    case J4C_NE: launch_compare<T, J4C_NE>(ix, a, b, out, n, s); break;
     default: return set_error(J4C_E_INVALID, "j4c_compare: primitive %d is not a comparison", prim);
     }
-#undef J4C_CMP
     J4C_LAUNCH_CHECK("compare_kernel");
     return J4C_OK;
 }
 
 // ---- unary ------------------------------------------------------------------
-template <typename T, int OP, int VEC>
+// VEC consecutive elements per lane access, U accesses in flight, then a
+// scalar tail (fewer than VEC elements).
+template <typename T, int OP, int VEC, int U>
 __global__ void __launch_bounds__(256) unary_kernel(const T *__restrict__ in, T *__restrict__ out,
                                                     int64_t n) {
-    const int64_t nvec = n / VEC;
-    for (int64_t v = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; v < nvec;
-         v += (int64_t)gridDim.x * blockDim.x) {
-        Pack<T, VEC> p = load_pack<T, VEC>(in + v * VEC, 1);
+    const int64_t nvec = n / VEC, stride = (int64_t)gridDim.x * blockDim.x;
+    for (int64_t v0 = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; v0 < nvec; v0 += U * stride) {
+        Pack<T, VEC> p[U];
 #pragma unroll
-        for (int k = 0; k < VEC; k++) p.v[k] = unary_op<OP>(p.v[k]);
-        store_pack<T, VEC>(out + v * VEC, p);
+        for (int u = 0; u < U; u++)
+            if (v0 + u * stride < nvec) p[u] = load_pack<T, VEC>(in + (v0 + u * stride) * VEC, 1);
+#pragma unroll
+        for (int u = 0; u < U; u++) {
+            if (v0 + u * stride < nvec) {
+#pragma unroll
+                for (int k = 0; k < VEC; k++) p[u].v[k] = unary_op<OP>(p[u].v[k]);
+                store_pack<T, VEC>(out + (v0 + u * stride) * VEC, p[u]);
+            }
+        }
     }
-    // tail
-    int64_t t = nvec * VEC + blockIdx.x * (int64_t)blockDim.x + threadIdx.x;
-    if (VEC > 1 && t < n && t < nvec * VEC + VEC) out[t] = unary_op<OP>(in[t]);
+    const int64_t t = nvec * VEC + blockIdx.x * (int64_t)blockDim.x + threadIdx.x;
+    if (VEC > 1 && t < n) out[t] = unary_op<OP>(in[t]);  // n - nvec*VEC < VEC <= threads
 }
 
 template <typename T, int OP>
 static int launch_unary(const void *in, void *out, int64_t n, cudaStream_t s) {
-    constexpr int V = Vec<T>::N;
+    constexpr int V = 16 / sizeof(T), U = 4;
     if (aligned16(in) && aligned16(out) && n >= V)
-        unary_kernel<T, OP, V><<<grid_for(ceil_div(n, V), 256), 256, 0, s>>>((const T *)in, (T *)out, n);
+        unary_kernel<T, OP, V, U><<<grid_for(ceil_div(ceil_div(n, V), U), 256), 256, 0, s>>>((const T *)in,
+                                                                                            (T *)out, n);
     else
-        unary_kernel<T, OP, 1><<<grid_for(n, 256), 256, 0, s>>>((const T *)in, (T *)out, n);
+        unary_kernel<T, OP, 1, U><<<grid_for(ceil_div(n, U), 256), 256, 0, s>>>((const T *)in, (T *)out, n);
     J4C_LAUNCH_CHECK("unary_kernel");
     return J4C_OK;
 }
@@ -281,23 +325,48 @@ __device__ __forceinline__ D java_cast(S v) {
     }
 }
 
-template <typename S, typename D>
+template <typename S, typename D, int VEC, int U>
 __global__ void __launch_bounds__(256) cast_kernel(const S *__restrict__ in, D *__restrict__ out,
                                                    int64_t n) {
-    for (int64_t i = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; i < n;
-         i += (int64_t)gridDim.x * blockDim.x)
-        out[i] = java_cast<S, D>(in[i]);
+    const int64_t nvec = n / VEC, stride = (int64_t)gridDim.x * blockDim.x;
+    for (int64_t v0 = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; v0 < nvec; v0 += U * stride) {
+        Pack<S, VEC> p[U];
+#pragma unroll
+        for (int u = 0; u < U; u++)
+            if (v0 + u * stride < nvec) p[u] = load_pack<S, VEC>(in + (v0 + u * stride) * VEC, 1);
+#pragma unroll
+        for (int u = 0; u < U; u++) {
+            if (v0 + u * stride < nvec) {
+                Pack<D, VEC> r;
+#pragma unroll
+                for (int k = 0; k < VEC; k++) r.v[k] = java_cast<S, D>(p[u].v[k]);
+                store_pack<D, VEC>(out + (v0 + u * stride) * VEC, r);
+            }
+        }
+    }
+    const int64_t t = nvec * VEC + blockIdx.x * (int64_t)blockDim.x + threadIdx.x;
+    if (VEC > 1 && t < n) out[t] = java_cast<S, D>(in[t]);
+}
+
+template <typename S, typename D>
+static void launch_cast(const void *in, void *out, int64_t n, cudaStream_t s) {
+    // 4 elements per lane access: 4 B (bool) .. 32 B (8-byte types) per side
+    constexpr int U = 4;
+    if (aligned16(in) && aligned16(out) && n >= 4)
+        cast_kernel<S, D, 4, U><<<grid_for(ceil_div(ceil_div(n, 4), U), 256), 256, 0, s>>>((const S *)in,
+                                                                                           (D *)out, n);
+    else
+        cast_kernel<S, D, 1, U><<<grid_for(ceil_div(n, U), 256), 256, 0, s>>>((const S *)in, (D *)out, n);
 }
 
 template <typename S>
 static int cast_from(int dst, const void *in, void *out, int64_t n, cudaStream_t s) {
-    unsigned g = grid_for(n, 256);
     switch (dst) {
-    case J4C_FLOAT32: cast_kernel<S, float><<<g, 256, 0, s>>>((const S *)in, (float *)out, n); break;
-    case J4C_FLOAT64: cast_kernel<S, double><<<g, 256, 0, s>>>((const S *)in, (double *)out, n); break;
-    case J4C_INT32: cast_kernel<S, int32_t><<<g, 256, 0, s>>>((const S *)in, (int32_t *)out, n); break;
-    case J4C_INT64: cast_kernel<S, int64_t><<<g, 256, 0, s>>>((const S *)in, (int64_t *)out, n); break;
-    case J4C_BOOL: cast_kernel<S, uint8_t><<<g, 256, 0, s>>>((const S *)in, (uint8_t *)out, n); break;
+    case J4C_FLOAT32: launch_cast<S, float>(in, out, n, s); break;
+    case J4C_FLOAT64: launch_cast<S, double>(in, out, n, s); break;
+    case J4C_INT32: launch_cast<S, int32_t>(in, out, n, s); break;
+    case J4C_INT64: launch_cast<S, int64_t>(in, out, n, s); break;
+    case J4C_BOOL: launch_cast<S, uint8_t>(in, out, n, s); break;
     default: return set_error(J4C_E_INVALID, "j4c_cast: bad target dtype %d", dst);
     }
     J4C_LAUNCH_CHECK("cast_kernel");
@@ -312,13 +381,31 @@ __global__ void fill_kernel(T *out, int64_t n, T v) {
         out[i] = v;
 }
 
-template <typename T>
+template <typename T, int VEC, int U>
 __global__ void __launch_bounds__(256) relu_grad_kernel(const T *__restrict__ g,
                                                         const T *__restrict__ x,
                                                         T *__restrict__ out, int64_t n) {
-    for (int64_t i = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; i < n;
-         i += (int64_t)gridDim.x * blockDim.x)
-        out[i] = x[i] > T(0) ? g[i] : T(0);
+    const int64_t nvec = n / VEC, stride = (int64_t)gridDim.x * blockDim.x;
+    for (int64_t v0 = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; v0 < nvec; v0 += U * stride) {
+        Pack<T, VEC> pg[U], px[U];
+#pragma unroll
+        for (int u = 0; u < U; u++) {
+            if (v0 + u * stride < nvec) {
+                pg[u] = load_pack<T, VEC>(g + (v0 + u * stride) * VEC, 1);
+                px[u] = load_pack<T, VEC>(x + (v0 + u * stride) * VEC, 1);
+            }
+        }
+#pragma unroll
+        for (int u = 0; u < U; u++) {
+            if (v0 + u * stride < nvec) {
+#pragma unroll
+                for (int k = 0; k < VEC; k++) pg[u].v[k] = px[u].v[k] > T(0) ? pg[u].v[k] : T(0);
+                store_pack<T, VEC>(out + (v0 + u * stride) * VEC, pg[u]);
+            }
+        }
+    }
+    const int64_t t = nvec * VEC + blockIdx.x * (int64_t)blockDim.x + threadIdx.x;
+    if (VEC > 1 && t < n) out[t] = x[t] > T(0) ? g[t] : T(0);
 }
 
 template <typename T>
@@ -531,13 +618,24 @@ int j4c_relu_grad(int dtype, const void *g, const void *x, int64_t n, void *out,
     if (n == 0) return J4C_OK;
     J4C_REQUIRE(g && x && out, "j4c_relu_grad: NULL pointer");
     cudaStream_t s = as_stream(stream);
-    unsigned gr = grid_for(n, 256);
-    if (dtype == J4C_FLOAT32)
-        relu_grad_kernel<float><<<gr, 256, 0, s>>>((const float *)g, (const float *)x, (float *)out, n);
-    else if (dtype == J4C_FLOAT64)
-        relu_grad_kernel<double><<<gr, 256, 0, s>>>((const double *)g, (const double *)x, (double *)out, n);
-    else
+    const bool vec = aligned16(g) && aligned16(x) && aligned16(out) && n >= 4;
+    if (dtype == J4C_FLOAT32) {
+        if (vec)
+            relu_grad_kernel<float, 4, 2><<<grid_for(ceil_div(ceil_div(n, 4), 2), 256), 256, 0, s>>>(
+                (const float *)g, (const float *)x, (float *)out, n);
+        else
+            relu_grad_kernel<float, 1, 2><<<grid_for(ceil_div(n, 2), 256), 256, 0, s>>>(
+                (const float *)g, (const float *)x, (float *)out, n);
+    } else if (dtype == J4C_FLOAT64) {
+        if (vec)
+            relu_grad_kernel<double, 2, 2><<<grid_for(ceil_div(ceil_div(n, 2), 2), 256), 256, 0, s>>>(
+                (const double *)g, (const double *)x, (double *)out, n);
+        else
+            relu_grad_kernel<double, 1, 2><<<grid_for(ceil_div(n, 2), 256), 256, 0, s>>>(
+                (const double *)g, (const double *)x, (double *)out, n);
+    } else {
         return set_error(J4C_E_INVALID, "j4c_relu_grad: dtype %s", dtype_name(dtype));
+    }
     J4C_LAUNCH_CHECK("relu_grad_kernel");
     return J4C_OK;
 }

@@ -174,7 +174,7 @@ __device__ __forceinline__ void arg_warp(T &best, int32_t &bi) {
     }
 }
 
-template <typename T, bool MAX, int TPR>
+template <typename T, bool MAX, int TPR, int VEC>
 __global__ void __launch_bounds__(256) row_arg_kernel(const T *__restrict__ in, int64_t rows,
                                                       int64_t len, int32_t *__restrict__ out) {
     constexpr int ROWS_PER_CTA = 256 / TPR;
@@ -191,11 +191,23 @@ __global__ void __launch_bounds__(256) row_arg_kernel(const T *__restrict__ in, 
         if (row < rows) {
             const T *p = in + row * len;
             first_nan = p[0] != p[0];
-            for (int64_t j = sub; j < len; j += TPR) {
-                T v = p[j];
-                if (v == v && arg_better<T, MAX>(v, (int32_t)j, best, bi)) {
-                    best = v;
-                    bi = (int32_t)j;
+            // VEC consecutive elements per step (one 16-byte load when VEC > 1;
+            // the launcher checks alignment and len % VEC); each lane still
+            // visits its elements in increasing index order.
+            for (int64_t j0 = (int64_t)sub * VEC; j0 < len; j0 += (int64_t)TPR * VEC) {
+                T v[VEC];
+                if constexpr (VEC == 4 && sizeof(T) == 4) {
+                    const float4 q = __ldg(reinterpret_cast<const float4 *>(p + j0));
+                    v[0] = q.x; v[1] = q.y; v[2] = q.z; v[3] = q.w;
+                } else {
+                    v[0] = p[j0];
+                }
+#pragma unroll
+                for (int k = 0; k < VEC; k++) {
+                    if (v[k] == v[k] && arg_better<T, MAX>(v[k], (int32_t)(j0 + k), best, bi)) {
+                        best = v[k];
+                        bi = (int32_t)(j0 + k);
+                    }
                 }
             }
         }
@@ -305,12 +317,16 @@ template <typename T, bool MAX>
 static int argreduce_t(const T *in, int64_t outer, int64_t axis, int64_t inner, int32_t *out,
                        cudaStream_t s) {
     if (inner == 1) {
+        constexpr int V = sizeof(T) == 4 ? 4 : 1;  // 16-byte loads for FLOAT32
+        const bool v4 = V == 4 && axis % 4 == 0 && aligned16(in);
         if (axis >= 2048) {
             unsigned g = (unsigned)std::min<int64_t>(outer, (int64_t)sm_count() * 16);
-            row_arg_kernel<T, MAX, 256><<<g, 256, 0, s>>>(in, outer, axis, out);
+            if (v4) row_arg_kernel<T, MAX, 256, V><<<g, 256, 0, s>>>(in, outer, axis, out);
+            else row_arg_kernel<T, MAX, 256, 1><<<g, 256, 0, s>>>(in, outer, axis, out);
         } else {
             unsigned g = (unsigned)std::min<int64_t>(ceil_div(outer, 8), (int64_t)sm_count() * 16);
-            row_arg_kernel<T, MAX, 32><<<g, 256, 0, s>>>(in, outer, axis, out);
+            if (v4) row_arg_kernel<T, MAX, 32, V><<<g, 256, 0, s>>>(in, outer, axis, out);
+            else row_arg_kernel<T, MAX, 32, 1><<<g, 256, 0, s>>>(in, outer, axis, out);
         }
     } else {
         col_arg_kernel<T, MAX><<<grid_for(outer * inner, 256), 256, 0, s>>>(in, outer, axis, inner, out);
