@@ -16,6 +16,7 @@
 
 #include <algorithm>
 #include <cinttypes>
+#include <cstddef>
 #include <cstring>
 #include <map>
 #include <memory>
@@ -30,6 +31,12 @@ namespace j4c {
 namespace fused {
 
 constexpr int kMaxIn = 16, kMaxOut = 16, kMaxTail = 8;
+
+// The ABI structs' layout is what foreign callers (ctypes, Java FFM) mirror.
+static_assert(sizeof(j4c_insn) == 24 && offsetof(j4c_insn, value) == 16, "j4c_insn layout");
+static_assert(offsetof(j4c_program, insns) == 8 && offsetof(j4c_program, input_bcast) == 32 &&
+                  offsetof(j4c_program, tail_insn) == 72 && sizeof(j4c_program) == 80,
+              "j4c_program layout");
 
 struct Args {
     const void *in[kMaxIn];

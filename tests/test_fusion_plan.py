@@ -134,3 +134,15 @@ def test_invalid_program_rejected():
     prog = fusion._Program(1, insn, 0, z, z, 1, z, 0, z, z)
     rc = _lib.lib().j4c_fused_source(C.cast(C.pointer(prog), C.c_void_p), 0, None, 0, None)
     assert rc == _lib.E_INVALID
+
+
+def test_program_struct_layout_matches_the_c_abi():
+    """j4c_insn is 24 bytes; j4c_program has pointers at 8-byte offsets (the
+    layout a Java FFM StructLayout of the header reproduces)."""
+    import ctypes as C
+    assert C.sizeof(fusion._Insn) == 24
+    assert fusion._Insn.value.offset == 16
+    P = fusion._Program
+    assert [getattr(P, f).offset for f in ("n_insns", "insns", "n_inputs", "input_dtype", "input_bcast",
+                                            "n_outputs", "output_insn", "n_tails", "tail_op", "tail_insn")] == \
+        [0, 8, 16, 24, 32, 40, 48, 56, 64, 72]

@@ -158,3 +158,30 @@ def test_elementwise_sweep(J, rows, cols):
     assert_rel(z.numpy(), rz, TOL_ELEMENTWISE, "z")
     assert_rel(s.numpy(), rs, TOL_REDUCTION, "row sums")
     np.testing.assert_array_equal(am.numpy(), ram)
+
+
+def test_config2_pmap_dot_allgather_full_size(J):
+    """Config 2 at full size: two shards of A [4096,8192] (U(-1,1), seed 2)
+    times a replicated B [8192,4096], gathered with Lax.allGather.  The
+    oracle recomputes sampled rows of every shard (a full FP32 host dot of
+    this size takes minutes); the rest is checked through a size-independent
+    identity: (A_i . B) . 1 = A_i . (B . 1) on every row."""
+    M, K, N, D = 4096, 8192, 4096, 2
+    devices = [J.Device(None) for _ in range(D)]
+    A = J.Random.uniform(J.PRNGKey.key(2), J.Shape(D, M, K), -1.0, 1.0)
+    B = J.Random.uniform(J.Random.split(J.PRNGKey.key(2), 2)[1], J.Shape(K, N), -1.0, 1.0)
+    out = J.JAX.pmap(lambda a: J.Lax.allGather(a.dot(B), D), devices)(A)
+    assert out.shape().dimensions() == (D, D, M, N)
+    c = out.numpy()
+    np.testing.assert_array_equal(c[0], c[1])  # every shard holds the same gather
+    ah, bh = A.numpy(), B.numpy()
+    for i in range(D):
+        for r0 in (0, 1733, M - 8):
+            ref = orc.dot(ah[i], bh, rows=(r0, r0 + 8), threads=8)
+            assert_rel(c[0, i, r0:r0 + 8], ref, TOL_REDUCTION, f"shard {i} rows {r0}..")
+    ones = np.ones(N, np.float64)
+    b1 = bh.astype(np.float64) @ ones
+    for i in range(D):
+        lhs = c[0, i].astype(np.float64) @ ones
+        rhs = ah[i].astype(np.float64) @ b1
+        assert_rel(lhs, rhs, TOL_REDUCTION, f"row-sum identity, shard {i}")
