@@ -56,6 +56,7 @@ def parse():
     p.add_argument("--batch", type=int, default=BATCH, help="samples per GPU (profiling runs only)")
     p.add_argument("--no-cpu-baseline", action="store_true")
     p.add_argument("--no-e2e", action="store_true")
+    p.add_argument("--no-graph", action="store_true", help="time the eager step only (no CUDA graph)")
     p.add_argument("--workload", default="dp_step", choices=["dp_step", "gemm", "sweep", "cfg0", "cfg2", "collectives"],
                    help="dp_step is the headline; gemm/sweep are single-kernel measurements "
                         "used for profiling")
@@ -172,23 +173,32 @@ def run_ours(args):
         logits = a.dot(c[f"w{L}"].value).add(c[f"b{L}"].value)
         return J.Nn.softmax(logits).log().mul(t).sum(-1).mean().mul(neg)
 
-    def body(xs, ts):
-        tree = J.PyTree.dictOf(params)
-        value, grads = J.JAX.valueAndGradTree(lambda p: loss(p, xs, ts))(tree)
-        grads = J.Lax.psumTree(grads)
-        g = grads.children
-        for k in names:  # psum-averaged gradient, SGD update
-            params[k] = params[k].sub(g[k].value.mul(inv_d).mul(lr))
-        return value
+    def step_fn(xs_arr, ts_arr, *ps):
+        """One training step as a function of its buffers:
+        (x, one-hot targets, *params) -> [per-shard losses, *updated params]."""
+        p = dict(zip(names, ps))
+        new = {}
 
-    pm = J.JAX.pmap(body, devices)
-    if world > 1:
-        inputs = (J.LocalShard(x_loc, D), J.LocalShard(t_loc, D))
-    else:
-        inputs = (x_loc.reshape(J.Shape(1, B, DIMS[0])), t_loc.reshape(J.Shape(1, B, DIMS[-1])))
+        def body(xs, ts):
+            value, grads = J.JAX.valueAndGradTree(lambda tr: loss(tr, xs, ts))(J.PyTree.dictOf(p))
+            g = J.Lax.psumTree(grads).children
+            for k in names:  # psum-averaged gradient, SGD update
+                new[k] = p[k].sub(g[k].value.mul(inv_d).mul(lr))
+            return value
+
+        if world > 1:
+            ins = (J.LocalShard(xs_arr, D), J.LocalShard(ts_arr, D))
+        else:
+            ins = (xs_arr.reshape(J.Shape(1, B, DIMS[0])), ts_arr.reshape(J.Shape(1, B, DIMS[-1])))
+        losses = J.JAX.pmap(body, devices)(*ins)
+        return [losses] + [new[k] for k in names]
+
+    state = {"params": [params[k] for k in names]}
 
     def step():
-        return pm(*inputs)
+        outs = step_fn(x_loc, t_loc, *state["params"])
+        state["params"] = outs[1:]
+        return outs[0]
 
     def sync_all():
         torch.cuda.synchronize()
@@ -207,10 +217,7 @@ def run_ours(args):
         step()
     sync_all()
 
-    # ---- device-timed region (inputs resident in HBM) ----
-    clocks = ClockSampler(ordinal)
-    clocks.start()
-    time.sleep(0.3)
+    # ---- eager steps, timed (per-dot CUDA events for the roofline) ----
     launches0 = _lib.kernel_launches()
     core.DOT_TIMING = []
     sync_all()
@@ -222,15 +229,53 @@ def run_ours(args):
     host_ms = (time.perf_counter() - h0) * 1e3 / args.steps  # enqueue time per step (no sync inside)
     ev1.record()
     torch.cuda.synchronize()
-    ms_local = ev0.elapsed_time(ev1)
-    launches = _lib.kernel_launches() - launches0
+    eager_ms_local = ev0.elapsed_time(ev1)
+    eager_launches = _lib.kernel_launches() - launches0
     dots = core.DOT_TIMING
     core.DOT_TIMING = None
+    eager_ms = max_over_ranks(eager_ms_local)
+    dot_ms = sum(a.elapsed_time(b) for a, b, _ in dots)
+    dot_flop = sum(f for _, _, f in dots)
+
+    # ---- the same step recorded once as a CUDA graph and replayed ----
+    graphs, graph_note, per_replay = [], None, None
+    if not args.no_graph:
+        try:
+            from jax4j_b200.graphs import CapturedStep
+            nparam = len(names)
+            donate = {1 + j: 2 + j for j in range(nparam)}
+            l0 = _lib.kernel_launches()
+            graphs.append(CapturedStep(step_fn, [x_loc, t_loc] + state["params"], donate, warmup=1))
+            # kernels recorded by the capture (the warm-up's are counted with it)
+            per_replay = (_lib.kernel_launches() - l0) // 2
+            state["params"] = graphs[0].inputs[2:]
+        except Exception as e:  # noqa: BLE001 - reported in the line, eager numbers stand
+            graph_note = f"capture failed: {type(e).__name__}: {str(e)[:200]}"
+            graphs = []
+
+    def replay():
+        return graphs[0]()[0]
+
+    timed_step = replay if graphs else step
+    for _ in range(args.warmup):
+        timed_step()
+    sync_all()
+
+    # ---- device-timed region (inputs resident in HBM) ----
+    clocks = ClockSampler(ordinal)
+    clocks.start()
+    time.sleep(0.3)
+    sync_all()
+    ev0.record()
+    for _ in range(args.steps):
+        timed_step()
+    ev1.record()
+    torch.cuda.synchronize()
+    ms_local = ev0.elapsed_time(ev1)
     clk = clocks.stop()
     ms = max_over_ranks(ms_local)
     value = D * B * args.steps / (ms / 1e3)
-    dot_ms = sum(a.elapsed_time(b) for a, b, _ in dots)
-    dot_flop = sum(f for _, _, f in dots)
+    launches = per_replay * args.steps if graphs else eager_launches
 
     # ---- end to end: host inputs copied in, loss read back, every step ----
     e2e = None
@@ -248,9 +293,16 @@ def run_ours(args):
         h2d = (x_host.numel() + t_host.numel()) * 4
         slots = []
         for _ in range(2):
-            xs = J.ConcreteNDArray._wrap(torch.empty_like(x_loc.tensor()), J.Shape(B, DIMS[0]), J.DType.FLOAT32, dev)
-            ts = J.ConcreteNDArray._wrap(torch.empty_like(t_loc.tensor()), J.Shape(B, DIMS[-1]), J.DType.FLOAT32, dev)
+            xs = J.ConcreteNDArray._wrap(x_loc.tensor().clone(), J.Shape(B, DIMS[0]), J.DType.FLOAT32, dev)
+            ts = J.ConcreteNDArray._wrap(t_loc.tensor().clone(), J.Shape(B, DIMS[-1]), J.DType.FLOAT32, dev)
             slots.append((xs, ts))
+        slot_graphs = []
+        if graphs:
+            # one recorded step per input slot, both on the shared parameter buffers
+            slot_graphs = [None, None]
+            for k in range(2):
+                slot_graphs[k] = CapturedStep(step_fn, [slots[k][0], slots[k][1]] + state["params"], donate,
+                                              warmup=1)
         copy_stream = torch.cuda.Stream()
         compute = torch.cuda.current_stream()
         ready = [torch.cuda.Event() for _ in range(2)]
@@ -270,10 +322,7 @@ def run_ours(args):
 
         def inputs_of(k):
             # fresh wrappers each step: the slot buffers are rewritten in place
-            xs, ts = (J.ConcreteNDArray._wrap(a.tensor(), a.shape(), a.dtype(), dev) for a in slots[k])
-            if world > 1:
-                return (J.LocalShard(xs, D), J.LocalShard(ts, D))
-            return (xs.reshape(J.Shape(1, B, DIMS[0])), ts.reshape(J.Shape(1, B, DIMS[-1])))
+            return [J.ConcreteNDArray._wrap(a.tensor(), a.shape(), a.dtype(), dev) for a in slots[k]]
 
         losses = []
         sync_all()
@@ -283,7 +332,12 @@ def run_ours(args):
         for i in range(args.steps):
             k = i % 2
             compute.wait_event(ready[k])
-            res = pm(*inputs_of(k))
+            if slot_graphs:
+                res = slot_graphs[k]()[0]
+            else:
+                res = step_fn(*inputs_of(k), *state["params"])
+                state["params"] = res[1:]
+                res = res[0]
             free[k].record(compute)
             used[k] = True
             if i + 1 < args.steps:
@@ -303,7 +357,11 @@ def run_ours(args):
                "ms_per_step": e2e_ms / args.steps, "loss": losses[-1],
                "pipeline": "inputs of step i+1 copied on a second stream during step i; "
                            "loss of step i read after step i+1 is launched"}
+        for g in slot_graphs:
+            g.release()
 
+    for g in graphs:
+        g.release()  # before the process group goes away (a graph may hold NCCL work)
     if rank != 0:
         if world > 1:
             distributed.barrier()
@@ -324,13 +382,19 @@ def run_ours(args):
                      "achieved": achieved, "peak": peak, "unit": "TFLOP/s",
                      "frac": (achieved / peak) if (achieved and peak) else None,
                      "peak_source": "MEASURED_PEAKS.json bf16 (sustained); TF32 dense rate is half of bf16",
-                     "dot_share_of_step": dot_ms / ms_local if ms_local else None,
+                     "dot_share_of_step": dot_ms / eager_ms_local if eager_ms_local else None,
                      "traffic": None},
         "gpu_launches": launches,
+        "execution": ("CUDA graph replay of the recorded step (%d kernels per step)" % per_replay) if graphs
+                     else "eager",
+        "eager": {"ms_per_step": eager_ms / args.steps, "value": D * B * args.steps / (eager_ms / 1e3),
+                  "gpu_launches": eager_launches},
         "host_enqueue_ms_per_step": host_ms,
         "clocks": clk,
         "flops_per_sample": flops_per_sample(),
     }
+    if graph_note:
+        line["graph_note"] = graph_note
     if e2e:
         line["e2e"] = e2e
     if D == 1 and not args.no_cpu_baseline:
@@ -631,15 +695,48 @@ def run_cfg0(args):
 
     ms_i = _timed(part_i, args.steps, args.warmup, world)
     ms_ii = _timed(part_ii, args.steps, args.warmup, world)
+
+    # the same two computations recorded as CUDA graphs and replayed
+    from jax4j_b200.graphs import CapturedStep
+    xa = x_in.local if world > 1 else x_in
+    ta = t_in.local if world > 1 else t_in
+
+    def wrap(a, b):
+        return (J.LocalShard(a, D), J.LocalShard(b, D)) if world > 1 else (a, b)
+
+    def fn_i(xx, tt):
+        xi, ti = wrap(xx, tt)
+        return [J.JAX.grad(lambda v: J.JAX.pmap(lambda xs, ts: loss_fn(params, xs, ts), devices)(v, ti).sum())(xi)]
+
+    def fn_ii(xx, tt):
+        xi, ti = wrap(xx, tt)
+        outs = []
+
+        def body(xs, ts):
+            v, g = J.JAX.valueAndGradTree(
+                lambda tr: loss_fn({k: tr.children[k].value for k in params}, xs, ts))(J.PyTree.dictOf(params))
+            outs.extend(J.PyTrees.flatten(J.Lax.psumTree(g)))
+            return v
+
+        return [J.JAX.pmap(body, devices)(xi, ti)] + outs
+
+    cs_i = CapturedStep(fn_i, [xa, ta])
+    gms_i = _timed(cs_i, args.steps * 10, args.warmup, world)
+    cs_i.release()
+    cs_ii = CapturedStep(fn_ii, [xa, ta])
+    gms_ii = _timed(cs_ii, args.steps * 10, args.warmup, world)
+    cs_ii.release()
     if rank == 0:
         samples = 2 * B
         line = {"metric": "config-0 grad-step samples/s", "unit": "samples/s", "n_gpus": world,
                 "config": {"workload": "2-layer tanh MLP 784-512-10, x [2,256,784], D=2 pmap devices"},
-                "grad_wrt_x": {"value": samples / (ms_i / 1e3), "ms_per_step": ms_i,
-                               "flop_per_sample": 1626112},
-                "grad_tree_psum": {"value": samples / (ms_ii / 1e3), "ms_per_step": ms_ii,
-                                   "flop_per_sample": 1636352, "psum_floats": 407050},
-                "bound": "latency (launch and host dispatch)"}
+                "grad_wrt_x": {"value": samples / (gms_i / 1e3), "ms_per_step": gms_i,
+                               "eager_ms_per_step": ms_i, "flop_per_sample": 1626112},
+                "grad_tree_psum": {"value": samples / (gms_ii / 1e3), "ms_per_step": gms_ii,
+                                   "eager_ms_per_step": ms_ii, "flop_per_sample": 1636352,
+                                   "psum_floats": 407050},
+                "execution": "CUDA graph replay of the recorded step (eager times beside)",
+                "bound": "latency (launches); eager: host dispatch"}
         if world == 1 and not args.no_cpu_baseline:
             line["cpu_baseline"] = _cfg0_cpu()
         print(json.dumps(line), flush=True)

@@ -322,8 +322,30 @@ def _heartbeat():
     distributed.heartbeat()
 
 
-def _bind(device: Device):
-    return torch.cuda.device(device.ordinal())
+class _Bound:
+    """Makes a shard thread use its device and the stream the pmap caller had
+    current on that device (so shards sharing a GPU stay ordered with the
+    caller's work, and a CUDA-graph capture on the caller's stream sees them)."""
+
+    def __init__(self, ordinal: int, stream):
+        self.ordinal, self.stream = ordinal, stream
+
+    def __enter__(self):
+        self._dev = torch.cuda.device(self.ordinal)
+        self._dev.__enter__()
+        self._st = torch.cuda.stream(self.stream)
+        self._st.__enter__()
+
+    def __exit__(self, *exc):
+        self._st.__exit__(*exc)
+        self._dev.__exit__(*exc)
+        return False
+
+
+def _binder(devices: Sequence[Device]):
+    """Called on the pmap caller's thread: records each device's current stream."""
+    streams = {o: torch.cuda.current_stream(o) for o in {d.ordinal() for d in devices}}
+    return lambda device: _Bound(device.ordinal(), streams[device.ordinal()])
 
 
 def shards_of(x: NDArray, D: int) -> List[Optional[ConcreteNDArray]]:
@@ -375,13 +397,14 @@ def run_forward(fn: Callable, inputs: Sequence[NDArray], devices: Sequence[Devic
         return _gather_stack(st, res)
     shards = [split(x, D) for x in inputs]
     coll = SlotCollective(D) if mode == "slots" else obj
+    bind = _binder(devices)
     # Every shard reaches its device before any shard thread starts: a copy
     # issued from a shard thread could queue behind a peer's collective
     # kernel on the source GPU and wait for itself.
     placed = [[s[i].to(devices[i]) for s in shards] for i in range(D)]
 
     def task(i):
-        with _bind(devices[i]):
+        with bind(devices[i]):
             PmapContext.set(PmapContext(i, D, coll))
             try:
                 return fn(*placed[i])
@@ -424,11 +447,12 @@ def run_forward_jaxpr(body, devices: Sequence[Device], shards: List[List[Concret
             PmapContext.set(None)
         return _gather_stack(st, res)
     coll = SlotCollective(D) if mode == "slots" else obj
+    bind = _binder(devices)
     bodies = [_body_on(body, devices[i]) for i in range(D)]  # placed before any thread starts
     placed = [[s[i].to(devices[i]) for s in shards] for i in range(D)]
 
     def task(i):
-        with _bind(devices[i]):
+        with bind(devices[i]):
             PmapContext.set(PmapContext(i, D, coll))
             try:
                 return forward_interpret(bodies[i], placed[i])[0]
@@ -460,12 +484,13 @@ def run_backward_jaxpr(body, devices: Sequence[Device], in_shards: List[List[Con
         stacked = [split(_gather_stack(st, g), D) for g in g_local]
         return [[stacked[k][i] for k in range(len(g_local))] for i in range(D)]
     coll = SlotCollective(D) if mode == "slots" else obj
+    bind = _binder(devices)
     bodies = [_body_on(body, devices[i]) for i in range(D)]  # placed before any thread starts
     placed = [[s[i].to(devices[i]) for s in in_shards] for i in range(D)]
     seeds = [g_shards[i].to(devices[i]) for i in range(D)]
 
     def task(i):
-        with _bind(devices[i]):
+        with bind(devices[i]):
             PmapContext.set(PmapContext(i, D, coll))
             try:
                 return backward_interpret(bodies[i], placed[i], [seeds[i]])
