@@ -173,6 +173,9 @@ def run_ours(args):
         logits = a.dot(c[f"w{L}"].value).add(c[f"b{L}"].value)
         return J.Nn.softmax(logits).log().mul(t).sum(-1).mean().mul(neg)
 
+    # SGD update, jitted: one fused kernel per parameter (w - g * (1/D) * lr)
+    sgd = J.JAX.jit(lambda w, g: w.sub(g.mul(inv_d).mul(lr)))
+
     def step_fn(xs_arr, ts_arr, *ps):
         """One training step as a function of its buffers:
         (x, one-hot targets, *params) -> [per-shard losses, *updated params]."""
@@ -183,7 +186,7 @@ def run_ours(args):
             value, grads = J.JAX.valueAndGradTree(lambda tr: loss(tr, xs, ts))(J.PyTree.dictOf(p))
             g = J.Lax.psumTree(grads).children
             for k in names:  # psum-averaged gradient, SGD update
-                new[k] = p[k].sub(g[k].value.mul(inv_d).mul(lr))
+                new[k] = sgd(p[k], g[k].value)
             return value
 
         if world > 1:

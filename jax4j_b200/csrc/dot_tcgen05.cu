@@ -493,34 +493,48 @@ __global__ void __launch_bounds__(256) split_kernel(const float *__restrict__ sr
 }
 
 // Transposed split: X [rows, cols] -> hi/lo of X^T, [cols, pitch] with
-// pitch = rows rounded up to 4.  64 x 64 tiles through shared memory: reads
-// coalesced along X's rows, writes coalesced along X^T's rows.
+// pitch = rows rounded up to 4.  64 x 64 tiles through shared memory; each
+// lane reads 4 consecutive floats of an X row (16 bytes when X's rows allow)
+// and writes 4 consecutive floats of an X^T row to hi and to lo (16 bytes;
+// pitch is a multiple of 4 and the tile origin a multiple of 64).
 __global__ void __launch_bounds__(256) split_t_kernel(const float *__restrict__ src, int64_t rows, int64_t cols,
-                                                      int64_t pitch, int64_t tiles_c, float *__restrict__ hi,
-                                                      float *__restrict__ lo) {
+                                                      int64_t pitch, int64_t tiles_c, int vec_in,
+                                                      float *__restrict__ hi, float *__restrict__ lo) {
     __shared__ float tile[64][65];
     const int64_t c0 = (blockIdx.x % tiles_c) * 64, r0 = (blockIdx.x / tiles_c) * 64;
-    const int tx = threadIdx.x & 31, ty = threadIdx.x >> 5;  // 32 x 8
-    for (int i = ty; i < 64; i += 8) {  // tile[i][j] = X[r0 + i][c0 + j]
-        const int64_t r = r0 + i;
-        for (int j = tx; j < 64; j += 32) {
-            const int64_t c = c0 + j;
-            tile[i][j] = (r < rows && c < cols) ? src[r * cols + c] : 0.0f;
-        }
-    }
-    __syncthreads();
-    for (int j = ty; j < 64; j += 8) {  // X^T[c0 + j][r0 + i] = tile[i][j]
-        const int64_t c = c0 + j;
-        if (c >= cols) continue;
-        for (int i = tx; i < 64; i += 32) {
-            const int64_t r = r0 + i;
-            if (r < pitch) {
-                const float x = tile[i][j];
-                const float h = tf32_round(x);
-                hi[c * pitch + r] = h;
-                lo[c * pitch + r] = tf32_round(x - h);
+    const int q = threadIdx.x & 15, w = threadIdx.x >> 4;  // 16 lanes per 64-float row, 16 rows per pass
+#pragma unroll
+    for (int pass = 0; pass < 4; pass++) {  // tile[i][4q..4q+3] = X[r0 + i][c0 + 4q ..]
+        const int i = pass * 16 + w;
+        const int64_t r = r0 + i, c = c0 + 4 * q;
+        float v[4] = {0.0f, 0.0f, 0.0f, 0.0f};
+        if (r < rows) {
+            if (vec_in && c + 4 <= cols) {
+                const float4 t = __ldg(reinterpret_cast<const float4 *>(src + r * cols + c));
+                v[0] = t.x; v[1] = t.y; v[2] = t.z; v[3] = t.w;
+            } else {
+#pragma unroll
+                for (int k = 0; k < 4; k++) v[k] = (c + k < cols) ? src[r * cols + c + k] : 0.0f;
             }
         }
+#pragma unroll
+        for (int k = 0; k < 4; k++) tile[i][4 * q + k] = v[k];
+    }
+    __syncthreads();
+#pragma unroll
+    for (int pass = 0; pass < 4; pass++) {  // X^T[c0 + j][r0 + 4q ..] = tile[4q..4q+3][j]
+        const int j = pass * 16 + w;
+        const int64_t c = c0 + j, r = r0 + 4 * q;
+        if (c >= cols || r >= pitch) continue;
+        float h[4], l[4];
+#pragma unroll
+        for (int k = 0; k < 4; k++) {
+            const float x = tile[4 * q + k][j];  // rows >= `rows` were loaded as zero
+            h[k] = tf32_round(x);
+            l[k] = tf32_round(x - h[k]);
+        }
+        *reinterpret_cast<float4 *>(hi + c * pitch + r) = make_float4(h[0], h[1], h[2], h[3]);
+        *reinterpret_cast<float4 *>(lo + c * pitch + r) = make_float4(l[0], l[1], l[2], l[3]);
     }
 }
 
@@ -624,7 +638,8 @@ int split_t(const float *src, int64_t rows, int64_t cols, float *hi, float *lo, 
     const int64_t pitch = split_pitch(rows);
     const int64_t tiles_c = ceil_div(cols, 64), tiles_r = ceil_div(pitch, 64);
     J4C_REQUIRE(tiles_c * tiles_r < (1ll << 31), "split: array too large");
-    split_t_kernel<<<(unsigned)(tiles_c * tiles_r), 256, 0, s>>>(src, rows, cols, pitch, tiles_c, hi, lo);
+    const int vec_in = (cols % 4 == 0) && aligned16(src);
+    split_t_kernel<<<(unsigned)(tiles_c * tiles_r), 256, 0, s>>>(src, rows, cols, pitch, tiles_c, vec_in, hi, lo);
     J4C_LAUNCH_CHECK("split_t_kernel");
     return J4C_OK;
 }

@@ -86,21 +86,80 @@ __global__ void __launch_bounds__(256) row_reduce_kernel(const T *__restrict__ i
 // ---- column reduction: [outer, axis, inner] -> [outer, inner] ------------------
 // grid: x over column groups, y over outer, z over axis splits.  With
 // splits > 1 the partial sums go to part[z][outer*inner].
-template <typename T>
+// Column reduction (inner > 1): each thread owns VEC adjacent columns (one
+// 16-byte load per row for FLOAT32) of one outer slice and sums a chunk of
+// the axis with four independent accumulators per column (rows a, a+1, a+2,
+// a+3), combined at the end; with more than one chunk the partial sums go to
+// `part` and combine_parts_kernel adds them in chunk order.
+template <typename T, int VEC>
 __global__ void __launch_bounds__(256) col_reduce_kernel(const T *__restrict__ in, int64_t outer,
                                                          int64_t axis, int64_t inner,
                                                          int64_t chunk, T *__restrict__ out,
                                                          T *__restrict__ part, int mean) {
-    int64_t i = blockIdx.x * (int64_t)blockDim.x + threadIdx.x;
+    const int64_t i = (blockIdx.x * (int64_t)blockDim.x + threadIdx.x) * VEC;
     if (i >= inner) return;
     for (int64_t o = blockIdx.y; o < outer; o += gridDim.y) {
-        int64_t a0 = blockIdx.z * chunk, a1 = std::min<int64_t>(axis, a0 + chunk);
+        const int64_t a0 = blockIdx.z * chunk, a1 = std::min<int64_t>(axis, a0 + chunk);
         const T *p = in + o * axis * inner + i;
-        T acc = T(0);
-        for (int64_t a = a0; a < a1; a++) acc = r_add(acc, p[a * inner]);
-        if (gridDim.z == 1) out[o * inner + i] = mean ? to_mean(acc, axis) : acc;
-        else part[(int64_t)blockIdx.z * outer * inner + o * inner + i] = acc;
+        T acc[4][VEC];
+#pragma unroll
+        for (int u = 0; u < 4; u++)
+#pragma unroll
+            for (int k = 0; k < VEC; k++) acc[u][k] = T(0);
+        int64_t a = a0;
+        for (; a + 4 <= a1; a += 4) {
+#pragma unroll
+            for (int u = 0; u < 4; u++) {
+                T v[VEC];
+                if constexpr (VEC == 4 && sizeof(T) == 4) {
+                    const float4 q = __ldg(reinterpret_cast<const float4 *>(p + (a + u) * inner));
+                    v[0] = q.x; v[1] = q.y; v[2] = q.z; v[3] = q.w;
+                } else {
+#pragma unroll
+                    for (int k = 0; k < VEC; k++) v[k] = p[(a + u) * inner + k];
+                }
+#pragma unroll
+                for (int k = 0; k < VEC; k++) acc[u][k] = r_add(acc[u][k], v[k]);
+            }
+        }
+        for (; a < a1; a++)
+#pragma unroll
+            for (int k = 0; k < VEC; k++) acc[0][k] = r_add(acc[0][k], p[a * inner + k]);
+#pragma unroll
+        for (int k = 0; k < VEC; k++) {
+            const T r = r_add(r_add(acc[0][k], acc[1][k]), r_add(acc[2][k], acc[3][k]));
+            if (gridDim.z == 1) out[o * inner + i + k] = mean ? to_mean(r, axis) : r;
+            else part[(int64_t)blockIdx.z * outer * inner + o * inner + i + k] = r;
+        }
     }
+}
+
+// The launch shape of a column reduction, shared by j4c_reduce_axis and
+// j4c_reduce_axis_noalloc so both add in the same order.
+struct ColPlan {
+    int vec;
+    int64_t gx, gy, splits, chunk;
+};
+template <typename T>
+static ColPlan col_plan(const T *in, int64_t outer, int64_t axis, int64_t inner) {
+    ColPlan c;
+    c.vec = (sizeof(T) == 4 && inner % 4 == 0 && aligned16(in)) ? 4 : 1;
+    c.gx = ceil_div(inner, 256 * c.vec);
+    c.gy = std::min<int64_t>(outer, 65535);
+    const int64_t ctas = c.gx * c.gy, want = (int64_t)sm_count() * 4;
+    c.splits = 1;
+    if (ctas < want && axis >= 64) c.splits = std::min<int64_t>({ceil_div(want, ctas), axis / 32, 64});
+    c.chunk = ceil_div(axis, c.splits);
+    c.splits = ceil_div(axis, c.chunk);
+    return c;
+}
+
+template <typename T>
+static void launch_col_reduce(const ColPlan &c, const T *in, int64_t outer, int64_t axis, int64_t inner, T *out,
+                              T *part, int mean, cudaStream_t s) {
+    dim3 grid((unsigned)c.gx, (unsigned)c.gy, (unsigned)c.splits);
+    if (c.vec == 4) col_reduce_kernel<T, 4><<<grid, 256, 0, s>>>(in, outer, axis, inner, c.chunk, out, part, mean);
+    else col_reduce_kernel<T, 1><<<grid, 256, 0, s>>>(in, outer, axis, inner, c.chunk, out, part, mean);
 }
 
 template <typename T>
@@ -274,25 +333,17 @@ static int reduce_axis_t(const T *in, int64_t outer, int64_t axis, int64_t inner
         return J4C_OK;
     }
     // columns
-    int64_t gx = ceil_div(inner, 256);
-    int64_t gy = std::min<int64_t>(outer, 65535);
-    int64_t ctas = gx * gy;
-    int64_t want = (int64_t)sm_count() * 4;
-    int64_t splits = 1;
-    if (ctas < want && axis >= 64) splits = std::min<int64_t>({ceil_div(want, ctas), axis / 32, 64});
-    int64_t chunk = ceil_div(axis, splits);
-    splits = ceil_div(axis, chunk);
+    const ColPlan c = col_plan<T>(in, outer, axis, inner);
     T *part = nullptr;
-    if (splits > 1) {
-        int rc = scratch_alloc(sizeof(T) * (size_t)(splits * outer * inner), (void **)&part, s);
+    if (c.splits > 1) {
+        int rc = scratch_alloc(sizeof(T) * (size_t)(c.splits * outer * inner), (void **)&part, s);
         if (rc) return rc;
     }
-    dim3 grid((unsigned)gx, (unsigned)gy, (unsigned)splits);
-    col_reduce_kernel<T><<<grid, 256, 0, s>>>(in, outer, axis, inner, chunk, out, part, mean);
+    launch_col_reduce<T>(c, in, outer, axis, inner, out, part, mean, s);
     J4C_LAUNCH_CHECK("col_reduce_kernel");
-    if (splits > 1) {
+    if (c.splits > 1) {
         int64_t n = outer * inner;
-        combine_parts_kernel<T><<<grid_for(n, 256), 256, 0, s>>>(part, (int)splits, n, axis, out, mean);
+        combine_parts_kernel<T><<<grid_for(n, 256), 256, 0, s>>>(part, (int)c.splits, n, axis, out, mean);
         J4C_LAUNCH_CHECK("combine_parts_kernel");
         return scratch_free(part, s);
     }
@@ -387,15 +438,9 @@ template <typename T>
 static int reduce_axis_noalloc_t(const T *in, int64_t outer, int64_t axis, int64_t inner, T *out,
                                  int mean, cudaStream_t s) {
     if (inner == 1) return reduce_axis_t<T>(in, outer, axis, inner, out, mean, s);  // no scratch
-    int64_t gx = ceil_div(inner, 256);
-    int64_t gy = std::min<int64_t>(outer, 65535);
-    int64_t ctas = gx * gy;
-    int64_t want = (int64_t)sm_count() * 4;
-    int64_t splits = 1;
-    if (ctas < want && axis >= 64) splits = std::min<int64_t>({ceil_div(want, ctas), axis / 32, 64});
-    int64_t chunk = ceil_div(axis, splits);
-    splits = ceil_div(axis, chunk);
-    if (splits == 1) return reduce_axis_t<T>(in, outer, axis, inner, out, mean, s);  // no scratch
+    const ColPlan c = col_plan<T>(in, outer, axis, inner);
+    if (c.splits == 1) return reduce_axis_t<T>(in, outer, axis, inner, out, mean, s);  // no scratch
+    const int64_t splits = c.splits;
     const size_t need = sizeof(T) * (size_t)(splits * outer * inner);
     if (need > (size_t)J4C_REDUCE_NOALLOC_SCRATCH_BYTES)
         return set_error(J4C_E_INVALID,
@@ -407,8 +452,7 @@ static int reduce_axis_noalloc_t(const T *in, int64_t outer, int64_t axis, int64
     if (rc) return rc;
     // Every partial is written before it is read, so the array's previous
     // contents never matter and nothing is cleared.
-    dim3 grid((unsigned)gx, (unsigned)gy, (unsigned)splits);
-    col_reduce_kernel<T><<<grid, 256, 0, s>>>(in, outer, axis, inner, chunk, out, (T *)part, mean);
+    launch_col_reduce<T>(c, in, outer, axis, inner, out, (T *)part, mean, s);
     J4C_LAUNCH_CHECK("col_reduce_kernel");
     int64_t n = outer * inner;
     combine_parts_kernel<T><<<grid_for(n, 256), 256, 0, s>>>((const T *)part, (int)splits, n, axis, out, mean);

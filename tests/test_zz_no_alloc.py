@@ -57,8 +57,8 @@ def test_noalloc_rejects_reductions_beyond_its_scratch():
     import torch
     from jax4j_b200 import _lib
     torch.cuda.set_device(0)
-    # a [8192, 4096] column sum splits its axis ~37 ways: 37 x 4096 floats of
-    # partials is more than the 256 KiB static array
+    # a [8192, 4096] column sum splits its axis across CTAs: its partial sums
+    # (splits x 4096 floats) are more than the 256 KiB static array
     x = torch.zeros(8192 * 4096, dtype=torch.float32, device="cuda")
     rc, _ = _reduce("j4c_reduce_axis_noalloc", SUM_AXIS, FLOAT32, x, 1, 8192, 4096)
     assert rc == _lib.E_INVALID
