@@ -283,6 +283,18 @@ J4C_API int j4c_split_f32_transposed(const float *x, int64_t rows, int64_t cols,
                                      j4c_stream stream);
 J4C_API int j4c_dot_split(const float *a_hi, const float *a_lo, const float *b_hi, const float *b_lo, float *c,
                           int64_t M, int64_t K, int64_t N, int trans_a, int trans_b, j4c_stream stream);
+/* j4c_dot_split with elementwise work fused into the store of C [M, N] (each
+ * pointer may be NULL; none may alias C):
+ *   C = op(A).op(B) + bias        bias [N], broadcast over rows -- the bias
+ *                                 add of a dense layer (ConcreteNDArray.add)
+ *   C = mask > 0 ? C : 0          mask [M, N] -- relu' (api/Grad.java:585-598)
+ *                                 applied to an input gradient
+ *   act = max(0, C)               act [M, N] -- the layer's relu output
+ * Each value is rounded exactly as the separate add / relu / relu' kernels
+ * round it, so results equal the unfused sequence bit for bit. */
+J4C_API int j4c_dot_split_ep(const float *a_hi, const float *a_lo, const float *b_hi, const float *b_lo,
+                             float *c, int64_t M, int64_t K, int64_t N, int trans_a, int trans_b,
+                             const float *bias, const float *mask, float *act, j4c_stream stream);
 
 /* ------------------------------------------------------------------ */
 /* Fused elementwise programs: replace TornadoJitCompiler.compile       */

@@ -754,9 +754,19 @@ def _tf32_split(x: "ConcreteNDArray", transposed: bool = False):
     return s
 
 
+def dot_supports_epilogue(a: "ConcreteNDArray") -> bool:
+    """Whether _dot_raw can fuse a bias / relu' / relu into the product's store."""
+    return a._dtype == DType.FLOAT32
+
+
 def _dot_raw(a: "ConcreteNDArray", b: "ConcreteNDArray", trans_a: bool, trans_b: bool,
-             device: Device) -> "ConcreteNDArray":
-    """C = op(A) . op(B) on the tensor cores; op = transpose when flagged."""
+             device: Device, bias: "ConcreteNDArray" = None, mask: "ConcreteNDArray" = None,
+             act: bool = False):
+    """C = op(A) . op(B) on the tensor cores; op = transpose when flagged.
+
+    FLOAT32 only, optional epilogue (j4c_dot_split_ep): C += bias (a [N]
+    vector), C = mask > 0 ? C : 0 (mask [M, N]), and with act=True also
+    returns relu(C); the result is then (C, relu(C))."""
     ad, bd = a._shape.dimensions(), b._shape.dimensions()
     if len(ad) != 2 or len(bd) != 2:
         raise IllegalArgumentException(f"dot requires 2-D operands, got {a._shape} and {b._shape}")
@@ -764,7 +774,16 @@ def _dot_raw(a: "ConcreteNDArray", b: "ConcreteNDArray", trans_a: bool, trans_b:
     K2, N = (bd[1], bd[0]) if trans_b else (bd[0], bd[1])
     if K != K2:
         raise IllegalArgumentException(f"dot: inner dimensions differ ({a._shape} . {b._shape})")
+    epilogue = bias is not None or mask is not None or act
+    if epilogue:
+        if a._dtype != DType.FLOAT32 or not (M and N and K):
+            raise IllegalArgumentException("dot epilogue needs a non-empty FLOAT32 product")
+        if bias is not None and (bias._dtype != DType.FLOAT32 or bias._shape.size() != N):
+            raise IllegalArgumentException(f"dot epilogue: bias {bias._shape} does not match N = {N}")
+        if mask is not None and (mask._dtype != DType.FLOAT32 or mask._shape.size() != M * N):
+            raise IllegalArgumentException(f"dot epilogue: mask {mask._shape} does not match [{M}, {N}]")
     out = torch.empty(M * N, dtype=a._dtype.torch, device=a._t.device)
+    act_out = torch.empty(M * N, dtype=a._dtype.torch, device=a._t.device) if act else None
     timing = DOT_TIMING
     if a._dtype == DType.FLOAT32 and M and N and K:
         # tensor-core path: each operand's 3xTF32 split is made once per array.
@@ -786,8 +805,14 @@ def _dot_raw(a: "ConcreteNDArray", b: "ConcreteNDArray", trans_a: bool, trans_b:
             ev0 = torch.cuda.Event(enable_timing=True)
             ev1 = torch.cuda.Event(enable_timing=True)
             ev0.record()
-        call("j4c_dot_split", ah.data_ptr(), al.data_ptr(), bh.data_ptr(), bl.data_ptr(), out.data_ptr(),
-             M, K, N, int(ta), int(tb), a._stream())
+        if epilogue:
+            call("j4c_dot_split_ep", ah.data_ptr(), al.data_ptr(), bh.data_ptr(), bl.data_ptr(), out.data_ptr(),
+                 M, K, N, int(ta), int(tb), bias.data_ptr() if bias is not None else None,
+                 mask.data_ptr() if mask is not None else None,
+                 act_out.data_ptr() if act_out is not None else None, a._stream())
+        else:
+            call("j4c_dot_split", ah.data_ptr(), al.data_ptr(), bh.data_ptr(), bl.data_ptr(), out.data_ptr(),
+                 M, K, N, int(ta), int(tb), a._stream())
     else:
         ws_bytes = _lib.lib().j4c_dot_workspace_size(a._dtype.ordinal, M, K, N)
         ws = torch.empty(max(ws_bytes, 1), dtype=torch.uint8, device=a._t.device) if ws_bytes else None
@@ -801,7 +826,10 @@ def _dot_raw(a: "ConcreteNDArray", b: "ConcreteNDArray", trans_a: bool, trans_b:
     if timing is not None:
         ev1.record()
         timing.append((ev0, ev1, 2.0 * M * N * K))
-    return ConcreteNDArray._wrap(out, Shape(M, N), a._dtype, device)
+    c = ConcreteNDArray._wrap(out, Shape(M, N), a._dtype, device)
+    if act:
+        return c, ConcreteNDArray._wrap(act_out, Shape(M, N), a._dtype, device)
+    return c
 
 
 from .tracing import TracedNDArray, Tracer  # noqa: E402  (late import: tracing imports core)

@@ -13,7 +13,8 @@ bool tc_gemm_supported(int64_t M, int64_t K, int64_t N);
 int tc_split_f32(const float *x, int64_t rows, int64_t cols, float *hi, float *lo, cudaStream_t s);
 int tc_split_f32_t(const float *x, int64_t rows, int64_t cols, float *hi, float *lo, cudaStream_t s);
 int tc_gemm_presplit(const float *ah, const float *al, const float *bh, const float *bl, float *c, int64_t M,
-                     int64_t K, int64_t N, int trans_a, int trans_b, cudaStream_t s);
+                     int64_t K, int64_t N, int trans_a, int trans_b, const float *bias, const float *mask,
+                     float *act, cudaStream_t s);
 }  // namespace j4c
 
 using namespace j4c;
@@ -80,17 +81,26 @@ int j4c_split_f32_transposed(const float *x, int64_t rows, int64_t cols, float *
     return tc_split_f32_t(x, rows, cols, hi, lo, as_stream(stream));
 }
 
-int j4c_dot_split(const float *a_hi, const float *a_lo, const float *b_hi, const float *b_lo, float *c,
-                  int64_t M, int64_t K, int64_t N, int trans_a, int trans_b, j4c_stream stream) {
+int j4c_dot_split_ep(const float *a_hi, const float *a_lo, const float *b_hi, const float *b_lo, float *c,
+                     int64_t M, int64_t K, int64_t N, int trans_a, int trans_b, const float *bias,
+                     const float *mask, float *act, j4c_stream stream) {
     J4C_REQUIRE(M >= 0 && K >= 0 && N >= 0, "j4c_dot_split: negative dimension");
     if (M == 0 || N == 0) return J4C_OK;
     J4C_REQUIRE(c, "j4c_dot_split: NULL output");
+    J4C_REQUIRE(K > 0 || (!bias && !mask && !act), "j4c_dot_split_ep: K = 0 with an epilogue");
     if (K == 0) return j4c_fill(J4C_FLOAT32, c, M * N, 0.0, stream);
     J4C_REQUIRE(a_hi && a_lo && b_hi && b_lo, "j4c_dot_split: NULL operand");
     if (!tc_gemm_supported(M, K, N))
         return set_error(J4C_E_UNSUPPORTED, "j4c_dot_split: shape %lld x %lld x %lld is too large", (long long)M,
                          (long long)K, (long long)N);
-    return tc_gemm_presplit(a_hi, a_lo, b_hi, b_lo, c, M, K, N, trans_a, trans_b, as_stream(stream));
+    return tc_gemm_presplit(a_hi, a_lo, b_hi, b_lo, c, M, K, N, trans_a, trans_b, bias, mask, act,
+                            as_stream(stream));
+}
+
+int j4c_dot_split(const float *a_hi, const float *a_lo, const float *b_hi, const float *b_lo, float *c,
+                  int64_t M, int64_t K, int64_t N, int trans_a, int trans_b, j4c_stream stream) {
+    return j4c_dot_split_ep(a_hi, a_lo, b_hi, b_lo, c, M, K, N, trans_a, trans_b, nullptr, nullptr, nullptr,
+                            stream);
 }
 
 }  // extern "C"

@@ -233,6 +233,19 @@ __device__ __forceinline__ void tile_coords(int t, int num_m, int num_n, int &mt
     nt = r / gsize;
 }
 
+// Elementwise work fused into the GEMM's store (each part optional), in the
+// coordinates of the stored C [rows, cols]:
+//   v = acc + bias[col]            (a bias add broadcast along rows)
+//   v = mask[row][col] > 0 ? v : 0 (relu' given the saved pre-activation)
+//   C[row][col] = v,  act[row][col] = max(0, v)  (Java Math.max rules)
+struct Epilogue {
+    const float *bias;
+    const float *mask;
+    float *act;
+};
+
+__device__ __forceinline__ float ep_relu(float v) { return (0.0f >= v) ? 0.0f : v; }
+
 // Loads one operand's hi or lo tile (ROWS of M or N, BK of K) into smem.
 template <int ROWS, int BK, bool MN>
 __device__ __forceinline__ void load_operand(uint32_t dst, const CUtensorMap *map, int kx, int row0,
@@ -251,7 +264,7 @@ __global__ void __launch_bounds__(kThreads, 1)
 gemm_3xtf32_kernel(const __grid_constant__ CUtensorMap tAh, const __grid_constant__ CUtensorMap tAl,
                    const __grid_constant__ CUtensorMap tBh, const __grid_constant__ CUtensorMap tBl,
                    float *__restrict__ C, int M, int N, int num_kb, int vec_store, int store_t,
-                   int *status) {
+                   Epilogue ep, int *status) {
     using Q = Cfg<BN, STAGES, BK>;
     constexpr int CHUNK_KB = Q::CHUNK_KB;
     extern __shared__ uint8_t smem_raw[];
@@ -424,22 +437,51 @@ gemm_3xtf32_kernel(const __grid_constant__ CUtensorMap tAh, const __grid_constan
             if (store_t) {
                 // C holds the transpose of this product ([N, M]): for each
                 // column the warp's 32 lanes write 32 consecutive floats.
+                // Stored C's column index is `row`, so the bias is one value.
                 if (row < M) {
+                    const float b = ep.bias ? __ldg(ep.bias + row) : 0.0f;
 #pragma unroll
-                    for (int j = 0; j < Q::COLS_PER_WARP; j++)
-                        if (col0 + j < N) C[(size_t)(col0 + j) * (size_t)M + row] = acc[j];
+                    for (int j = 0; j < Q::COLS_PER_WARP; j++) {
+                        if (col0 + j < N) {
+                            const size_t idx = (size_t)(col0 + j) * (size_t)M + row;
+                            float v = ep.bias ? __fadd_rn(acc[j], b) : acc[j];
+                            if (ep.mask) v = __ldg(ep.mask + idx) > 0.0f ? v : 0.0f;
+                            C[idx] = v;
+                            if (ep.act) ep.act[idx] = ep_relu(v);
+                        }
+                    }
                 }
             } else if (row < M && col0 < N) {
-                float *crow = C + (size_t)row * (size_t)N + col0;
+                const size_t base = (size_t)row * (size_t)N + col0;
                 if (vec_store && col0 + Q::COLS_PER_WARP <= N) {
-                    float4 *dst = reinterpret_cast<float4 *>(crow);
 #pragma unroll
-                    for (int v = 0; v < Q::COLS_PER_WARP / 4; v++)
-                        dst[v] = make_float4(acc[4 * v], acc[4 * v + 1], acc[4 * v + 2], acc[4 * v + 3]);
+                    for (int v4 = 0; v4 < Q::COLS_PER_WARP / 4; v4++) {
+                        float x[4] = {acc[4 * v4], acc[4 * v4 + 1], acc[4 * v4 + 2], acc[4 * v4 + 3]};
+                        if (ep.bias) {
+                            const float4 b = __ldg(reinterpret_cast<const float4 *>(ep.bias + col0) + v4);
+                            x[0] = __fadd_rn(x[0], b.x); x[1] = __fadd_rn(x[1], b.y);
+                            x[2] = __fadd_rn(x[2], b.z); x[3] = __fadd_rn(x[3], b.w);
+                        }
+                        if (ep.mask) {
+                            const float4 m = __ldg(reinterpret_cast<const float4 *>(ep.mask + base) + v4);
+                            x[0] = m.x > 0.0f ? x[0] : 0.0f; x[1] = m.y > 0.0f ? x[1] : 0.0f;
+                            x[2] = m.z > 0.0f ? x[2] : 0.0f; x[3] = m.w > 0.0f ? x[3] : 0.0f;
+                        }
+                        reinterpret_cast<float4 *>(C + base)[v4] = make_float4(x[0], x[1], x[2], x[3]);
+                        if (ep.act)
+                            reinterpret_cast<float4 *>(ep.act + base)[v4] =
+                                make_float4(ep_relu(x[0]), ep_relu(x[1]), ep_relu(x[2]), ep_relu(x[3]));
+                    }
                 } else {
 #pragma unroll
-                    for (int j = 0; j < Q::COLS_PER_WARP; j++)
-                        if (col0 + j < N) crow[j] = acc[j];
+                    for (int j = 0; j < Q::COLS_PER_WARP; j++) {
+                        if (col0 + j < N) {
+                            float v = ep.bias ? __fadd_rn(acc[j], __ldg(ep.bias + col0 + j)) : acc[j];
+                            if (ep.mask) v = __ldg(ep.mask + base + j) > 0.0f ? v : 0.0f;
+                            C[base + j] = v;
+                            if (ep.act) ep.act[base + j] = ep_relu(v);
+                        }
+                    }
                 }
             }
         }
@@ -585,7 +627,7 @@ static int make_map(CUtensorMap *map, const float *base, int64_t rows, int64_t c
 
 template <int BN, int STAGES, int BK, bool A_MN, bool B_MN>
 static int launch_gemm(const float *ah, const float *al, const float *bh, const float *bl, float *c,
-                       int64_t M, int64_t N, int64_t K, bool store_t, cudaStream_t s) {
+                       int64_t M, int64_t N, int64_t K, bool store_t, const Epilogue &ep, cudaStream_t s) {
     using Q = Cfg<BN, STAGES, BK>;
     auto kernel = gemm_3xtf32_kernel<BN, STAGES, BK, A_MN, B_MN>;
     static std::mutex mu;
@@ -612,24 +654,26 @@ static int launch_gemm(const float *ah, const float *al, const float *bh, const 
     if (!status) return set_error(J4C_E_OOM, "no device status word");
     const int64_t tiles = ceil_div(M, BM) * ceil_div(N, BN);
     const int grid = (int)std::min<int64_t>(tiles, sm_count());
-    const int vec = (N % 4 == 0) && aligned16(c);
+    const int vec = (N % 4 == 0) && aligned16(c) && (!ep.bias || aligned16(ep.bias)) &&
+                    (!ep.mask || aligned16(ep.mask)) && (!ep.act || aligned16(ep.act));
     kernel<<<grid, kThreads, Q::SMEM_BYTES, s>>>(mAh, mAl, mBh, mBl, c, (int)M, (int)N, (int)ceil_div(K, BK),
-                                                 store_t ? 0 : vec, store_t ? 1 : 0, status);
+                                                 store_t ? 0 : vec, store_t ? 1 : 0, ep, status);
     J4C_LAUNCH_CHECK("gemm_3xtf32_kernel");
     return J4C_OK;
 }
 
 template <int BN, int STAGES, int BK>
 static int launch_gemm_any(const float *ah, const float *al, const float *bh, const float *bl, float *c,
-                           int64_t M, int64_t N, int64_t K, bool a_mn, bool b_mn, cudaStream_t s) {
-    if (!a_mn && !b_mn) return launch_gemm<BN, STAGES, BK, false, false>(ah, al, bh, bl, c, M, N, K, false, s);
-    if (a_mn && !b_mn) return launch_gemm<BN, STAGES, BK, true, false>(ah, al, bh, bl, c, M, N, K, false, s);
+                           int64_t M, int64_t N, int64_t K, bool a_mn, bool b_mn, const Epilogue &ep,
+                           cudaStream_t s) {
+    if (!a_mn && !b_mn) return launch_gemm<BN, STAGES, BK, false, false>(ah, al, bh, bl, c, M, N, K, false, ep, s);
+    if (a_mn && !b_mn) return launch_gemm<BN, STAGES, BK, true, false>(ah, al, bh, bl, c, M, N, K, false, ep, s);
     // The wide (BN = 256) operand is read MN-major at a smem cost that
     // throttles the tensor pipe, so a K-major A with an MN-major B runs as
     // C^T = op(B)^T . op(A)^T: B's split becomes the (MN-major) A operand,
     // A's the (K-major) B operand, and the epilogue stores transposed.
-    if (!a_mn && b_mn) return launch_gemm<BN, STAGES, BK, true, false>(bh, bl, ah, al, c, N, M, K, true, s);
-    return launch_gemm<BN, STAGES, BK, true, true>(ah, al, bh, bl, c, M, N, K, false, s);
+    if (!a_mn && b_mn) return launch_gemm<BN, STAGES, BK, true, false>(bh, bl, ah, al, c, N, M, K, true, ep, s);
+    return launch_gemm<BN, STAGES, BK, true, true>(ah, al, bh, bl, c, M, N, K, false, ep, s);
 }
 
 int split_t(const float *src, int64_t rows, int64_t cols, float *hi, float *lo, cudaStream_t s) {
@@ -681,7 +725,8 @@ int tc_split_f32_t(const float *x, int64_t rows, int64_t cols, float *hi, float 
 }
 
 int tc_gemm_presplit(const float *ah, const float *al, const float *bh, const float *bl, float *c, int64_t M,
-                     int64_t K, int64_t N, int trans_a, int trans_b, cudaStream_t s) {
+                     int64_t K, int64_t N, int trans_a, int trans_b, const float *bias, const float *mask,
+                     float *act, cudaStream_t s) {
     J4C_REQUIRE(aligned16(ah) && aligned16(al) && aligned16(bh) && aligned16(bl),
                 "dot: split operands must be 16-byte aligned");
     // op(A) = A [M,K] is read K-major; A^T (A stored [K,M]) MN-major.
@@ -691,8 +736,9 @@ int tc_gemm_presplit(const float *ah, const float *al, const float *bh, const fl
         const char *v = getenv("J4C_GEMM_VARIANT");
         return v ? atoi(v) : 1;
     }();
-    if (variant == 0) return tc::launch_gemm_any<256, 2, 32>(ah, al, bh, bl, c, M, N, K, a_mn, b_mn, s);
-    return tc::launch_gemm_any<256, 4, 16>(ah, al, bh, bl, c, M, N, K, a_mn, b_mn, s);
+    const tc::Epilogue ep{bias, mask, act};
+    if (variant == 0) return tc::launch_gemm_any<256, 2, 32>(ah, al, bh, bl, c, M, N, K, a_mn, b_mn, ep, s);
+    return tc::launch_gemm_any<256, 4, 16>(ah, al, bh, bl, c, M, N, K, a_mn, b_mn, ep, s);
 }
 
 int tc_gemm_f32(const float *a, const float *b, float *c, int64_t M, int64_t K, int64_t N,
@@ -710,10 +756,10 @@ int tc_gemm_f32(const float *a, const float *b, float *c, int64_t M, int64_t K, 
     if (b_transposed) {
         // both stored K-leading: B goes in as the split of B^T (K-major)
         if ((rc = tc::split_t(b, br, bc, bh, bl, s))) return rc;
-        return tc_gemm_presplit(ah, al, bh, bl, c, M, K, N, trans_a, 1, s);
+        return tc_gemm_presplit(ah, al, bh, bl, c, M, K, N, trans_a, 1, nullptr, nullptr, nullptr, s);
     }
     if ((rc = tc::split(b, br, bc, bh, bl, s))) return rc;
-    return tc_gemm_presplit(ah, al, bh, bl, c, M, K, N, trans_a, trans_b, s);
+    return tc_gemm_presplit(ah, al, bh, bl, c, M, K, N, trans_a, trans_b, nullptr, nullptr, nullptr, s);
 }
 
 }  // namespace j4c

@@ -127,6 +127,46 @@ def _is_fusible(eq) -> bool:
     return eq.outputs[0].shape.rank() >= 1
 
 
+class DotEpilogue:
+    """DOT -> ADD(bias [N]) [-> RELU]: the bias add and the relu run in the
+    GEMM's store (j4c_dot_split_ep); the DOT's own output is never written."""
+
+    def __init__(self, dot, add, relu, bias):
+        self.dot, self.add, self.relu, self.bias = dot, add, relu, bias
+        self.inputs = [dot.inputs[0], dot.inputs[1], bias]
+
+
+def _dot_epilogues(jaxpr: Jaxpr) -> Dict[int, DotEpilogue]:
+    """Finds DOT -> ADD(bias) [-> RELU] chains whose DOT output feeds only the
+    ADD and whose bias exists before the DOT.  Keyed by id(dot equation)."""
+    eqs = jaxpr.equations
+    uses: Dict[int, list] = {}
+    pos: Dict[int, int] = {}
+    for i, eq in enumerate(eqs):
+        for v in eq.inputs:
+            uses.setdefault(v.id, []).append(eq)
+        for o in eq.outputs:
+            pos[o.id] = i
+    outs = {v.id for v in jaxpr.outVars}
+    found: Dict[int, DotEpilogue] = {}
+    for i, eq in enumerate(eqs):
+        if eq.primitive != P.DOT:
+            continue
+        z0 = eq.outputs[0]
+        if z0.dtype != DType.FLOAT32 or z0.shape.rank() != 2 or z0.id in outs or len(uses.get(z0.id, [])) != 1:
+            continue
+        add = uses[z0.id][0]
+        if add.primitive != P.ADD or add.inputs[0].id == add.inputs[1].id:
+            continue
+        bias = add.inputs[1] if add.inputs[0].id == z0.id else add.inputs[0]
+        if (bias.dtype != DType.FLOAT32 or bcast_kind(bias.shape, z0.shape) != BCAST_ROW
+                or add.outputs[0].shape != z0.shape or pos.get(bias.id, -1) >= i):
+            continue
+        relu = next((e for e in uses.get(add.outputs[0].id, []) if e.primitive == P.RELU), None)
+        found[id(eq)] = DotEpilogue(eq, add, relu, bias)
+    return found
+
+
 def plan(jaxpr: Jaxpr, keep_for_vjp: bool) -> Plan:
     """Groups the Jaxpr's equations.  keep_for_vjp: also write every value a
     VJP rule will read (the grad interpreter's forward pass)."""
@@ -162,7 +202,17 @@ def plan(jaxpr: Jaxpr, keep_for_vjp: bool) -> Plan:
         return all(v.id in g.values or (v.id not in g.tail_values and bcast_kind(v.shape, S) is not None)
                    for v in eq.inputs)
 
+    epilogues = _dot_epilogues(jaxpr)
+    folded = {id(e.add) for e in epilogues.values()} | {id(e.relu) for e in epilogues.values() if e.relu}
+
     for eq in eqs:
+        if id(eq) in folded:
+            continue  # computed by its DOT's epilogue step
+        ep = epilogues.get(id(eq))
+        if ep is not None:
+            close_producers(ep)
+            steps.append(("dot_ep", ep))
+            continue
         if _is_fusible(eq):
             S = eq.outputs[0].shape
             target = None
@@ -322,6 +372,29 @@ def run_group(g: Group, values: Dict[int, NDArray]) -> None:
     ptail = (C.c_void_p * max(1, len(tails)))(*[t.data_ptr() for t in tails])
     stream = torch.cuda.current_stream(tdev).cuda_stream
     call("j4c_fused_launch", g.handle, R, Cc, pin, pout, ptail, stream)
+
+
+def run_dot_epilogue(ep: DotEpilogue, values: Dict[int, NDArray]) -> None:
+    """One GEMM for DOT + bias add (+ relu); falls back to the three
+    equations when the operands do not take the fused path."""
+    from .core import _dot_raw, dot_supports_epilogue
+    from .grad import execute_primitive
+    a, w, b = (values[v.id] for v in ep.inputs)
+    if (all(isinstance(x, ConcreteNDArray) for x in (a, w, b)) and dot_supports_epilogue(a)
+            and a.dtype() == w.dtype() == b.dtype() and b.tensor().device == a.tensor().device):
+        dev = a._check_devices(w)
+        res = _dot_raw(a, w, False, False, dev, bias=b, act=ep.relu is not None)
+        if ep.relu is not None:
+            values[ep.add.outputs[0].id], values[ep.relu.outputs[0].id] = res
+        else:
+            values[ep.add.outputs[0].id] = res
+        return
+    z0 = execute_primitive(P.DOT, ep.dot, [a, w])
+    z = execute_primitive(P.ADD, ep.add, [z0, b] if ep.add.inputs[0].id == ep.dot.outputs[0].id else [b, z0])
+    values[ep.dot.outputs[0].id] = z0
+    values[ep.add.outputs[0].id] = z
+    if ep.relu is not None:
+        values[ep.relu.outputs[0].id] = execute_primitive(P.RELU, ep.relu, [z])
 
 
 def plan_for(jaxpr: Jaxpr, keep_for_vjp: bool) -> Plan:

@@ -156,6 +156,8 @@ def _evaluate(jaxpr: Jaxpr, args: List[NDArray], keep_for_vjp: bool) -> Dict[int
             if kind == "eq":
                 inputs = [values[v.id] for v in item.inputs]
                 values[item.outputs[0].id] = execute_primitive(item.primitive, item, inputs)
+            elif kind == "dot_ep":
+                fusion.run_dot_epilogue(item, values)
             else:
                 fusion.run_group(item, values)
         return values
@@ -187,9 +189,36 @@ def _merge(grads: Dict[int, NDArray], vid: int, g: NDArray) -> None:
     grads[vid] = g if prev is None else prev.add(g)
 
 
+def _relu_fed_dots(jaxpr: Jaxpr, need) -> Dict[int, object]:
+    """DOT equations whose first input h = relu(z) feeds nothing else: the
+    input gradient g . W^T is masked by z > 0 in the GEMM's store and
+    credited to z, so relu's own VJP (relu_grad, Grad.java:585-598) has
+    nothing left to do.  Keyed by id(dot equation) -> z."""
+    uses: Dict[int, int] = {}
+    producer = {}
+    for eq in jaxpr.equations:
+        for v in eq.inputs:
+            uses[v.id] = uses.get(v.id, 0) + 1
+        for o in eq.outputs:
+            producer[o.id] = eq
+    outs = {v.id for v in jaxpr.outVars}
+    found = {}
+    for eq in jaxpr.equations:
+        if eq.primitive != Primitive.DOT:
+            continue
+        h = eq.inputs[0]
+        r = producer.get(h.id)
+        if (r is None or r.primitive != Primitive.RELU or uses.get(h.id) != 1 or h.id in outs
+                or h.dtype != DType.FLOAT32 or r.inputs[0].id not in need):
+            continue
+        found[id(eq)] = r.inputs[0]
+    return found
+
+
 def do_backward(jaxpr: Jaxpr, values: Dict[int, NDArray], seeds: List[NDArray]) -> List[NDArray]:
     """Grad.doBackward (Grad.java:154-189)."""
     need = _needs_grad(jaxpr)
+    fused_relu = _relu_fed_dots(jaxpr, need) if FUSION else {}
     grads: Dict[int, NDArray] = {}
     for v, s in zip(jaxpr.outVars, seeds):
         _merge(grads, v.id, s)
@@ -200,6 +229,17 @@ def do_backward(jaxpr: Jaxpr, values: Dict[int, NDArray], seeds: List[NDArray]) 
         wanted = [v.id in need for v in eq.inputs]
         if not any(wanted):
             continue
+        z = fused_relu.get(id(eq))
+        if z is not None and wanted[0]:
+            a, b = values.get(eq.inputs[0].id), values.get(eq.inputs[1].id)
+            zv = values.get(z.id)
+            if (isinstance(g_out, ConcreteNDArray) and isinstance(b, ConcreteNDArray) and
+                    isinstance(zv, ConcreteNDArray) and g_out.dtype() == b.dtype() == zv.dtype() == DType.FLOAT32):
+                # dz = (g . W^T) masked by z > 0 in one GEMM; dW as usual
+                _merge(grads, z.id, _dot_raw(g_out, b, False, True, g_out.device(), mask=zv))
+                if wanted[1]:
+                    _merge(grads, eq.inputs[1].id, _dot_raw(a, g_out, True, False, g_out.device()))
+                continue
         inputs = [values.get(v.id) for v in eq.inputs]
         out_value = values.get(eq.outputs[0].id)
         g_ins = compute_vjps(eq.primitive, eq, g_out, inputs, out_value, wanted)

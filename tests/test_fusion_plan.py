@@ -51,12 +51,41 @@ def test_keep_for_vjp_writes_values_the_backward_reads():
 
 def test_dot_splits_groups():
     def f(x, w, b):
-        return x.dot(w).add(b).relu().mul(x.dot(w))
+        return x.dot(w).mul(b).relu().mul(x.dot(w))
 
     jp = G.make_jaxpr(f, Spec(8, 16), Spec(16, 16), Spec(16))
     plan = fusion.plan(jp, keep_for_vjp=False)
     kinds = [k for k, _ in plan.steps]
     assert kinds.count("eq") == 2 and kinds.count("group") == 1
+
+
+def test_dot_bias_relu_runs_in_the_gemm_epilogue():
+    def f(x, w1, b1, w2, b2):
+        h = x.dot(w1).add(b1).relu()
+        return h.dot(w2).add(b2).exp().sum(-1, True)
+
+    jp = G.make_jaxpr(f, Spec(8, 16), Spec(16, 32), Spec(32), Spec(32, 4), Spec(4))
+    plan = fusion.plan(jp, keep_for_vjp=True)
+    kinds = [k for k, _ in plan.steps]
+    assert kinds == ["dot_ep", "dot_ep", "group"]
+    first, second = plan.steps[0][1], plan.steps[1][1]
+    assert first.relu is not None and second.relu is None
+    # the second epilogue's output (the logits) feeds the exp + row-sum group
+    assert plan.steps[2][1].inputs[0][0].id == second.add.outputs[0].id
+
+
+def test_dot_epilogue_needs_a_private_dot_output_and_an_earlier_bias():
+    def used_twice(x, w, b):
+        z = x.dot(w)
+        return z.add(b).relu().add(z)
+
+    def bias_after_dot(x, w, b):
+        z = x.dot(w)
+        return z.add(b.mul(b)).relu()  # b*b is computed after the DOT
+
+    for f in (used_twice, bias_after_dot):
+        jp = G.make_jaxpr(f, Spec(8, 16), Spec(16, 16), Spec(16))
+        assert "dot_ep" not in [k for k, _ in fusion.plan(jp, keep_for_vjp=False).steps]
 
 
 def test_group_limits():

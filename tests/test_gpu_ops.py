@@ -356,3 +356,61 @@ def test_split_f32_transposed_layout(J, rows, cols):
     assert np.all(h.view(np.uint32) & 0x1FFF == 0)
     err = np.abs(h.astype(np.float64) + l - x.T)
     assert np.all(err <= np.abs(x.T) * 2.0 ** -21)
+
+
+@pytest.mark.parametrize("ta,tb", [(0, 0), (1, 0), (0, 1), (1, 1)])
+@pytest.mark.parametrize("M,K,N", [(200, 96, 130), (37, 53, 29)])
+def test_dot_epilogue_equals_unfused_sequence(J, ta, tb, M, K, N):
+    """j4c_dot_split_ep: bias add, relu output and relu' mask in the GEMM's
+    store give exactly what the separate kernels give."""
+    from jax4j_b200 import grad as G
+    from jax4j_b200.core import _dot_raw
+    r = rng(M + 3 * N + 7 * ta + 11 * tb)
+    A = r.uniform(-1, 1, (M, K)).astype(np.float32)
+    B = r.uniform(-1, 1, (K, N)).astype(np.float32)
+    a = dev(J, A.T.copy() if ta else A)
+    b = dev(J, B.T.copy() if tb else B)
+    bias = dev(J, r.uniform(-1, 1, N).astype(np.float32))
+    mask = dev(J, r.integers(-1, 2, (M, N)).astype(np.float32))
+    plain = _dot_raw(a, b, bool(ta), bool(tb), a.device())
+    z, h = _dot_raw(a, b, bool(ta), bool(tb), a.device(), bias=bias, act=True)
+    np.testing.assert_array_equal(z.numpy(), plain.add(bias).numpy())
+    np.testing.assert_array_equal(h.numpy(), plain.add(bias).relu().numpy())
+    masked = _dot_raw(a, b, bool(ta), bool(tb), a.device(), mask=mask)
+    np.testing.assert_array_equal(masked.numpy(), G.relu_grad(plain, mask).numpy())
+
+
+def test_mlp_grads_with_gemm_epilogues_equal_the_unfused_interpreter(J):
+    """The forward's DOT+bias+relu epilogues and the backward's relu'-masked
+    input gradients change no bit of the loss or of any gradient."""
+    from jax4j_b200 import grad as G
+    r = rng(5)
+    dims = [64, 96, 96, 10]
+    ws = [dev(J, r.uniform(-0.3, 0.3, (dims[i], dims[i + 1])).astype(np.float32)) for i in range(3)]
+    bs = [dev(J, r.uniform(-0.1, 0.1, dims[i + 1]).astype(np.float32)) for i in range(3)]
+    x = dev(J, r.standard_normal((48, 64)).astype(np.float32))
+    t = np.zeros((48, 10), np.float32)
+    t[np.arange(48), np.arange(48) % 10] = 1
+    tt = dev(J, t)
+    neg = J.ConcreteNDArray.scalar(-1.0)
+    names = ["w1", "b1", "w2", "b2", "w3", "b3"]
+    params = dict(zip(names, [ws[0], bs[0], ws[1], bs[1], ws[2], bs[2]]))
+
+    def loss(tr):
+        c = tr.children
+        a = x
+        for i in (1, 2):
+            a = a.dot(c[f"w{i}"].value).add(c[f"b{i}"].value).relu()
+        logits = a.dot(c["w3"].value).add(c["b3"].value)
+        return J.Nn.softmax(logits).log().mul(tt).sum(-1).mean().mul(neg)
+
+    v1, g1 = J.JAX.valueAndGradTree(loss)(J.PyTree.dictOf(params))
+    old = G.FUSION
+    G.FUSION = False
+    try:
+        v0, g0 = J.JAX.valueAndGradTree(loss)(J.PyTree.dictOf(params))
+    finally:
+        G.FUSION = old
+    np.testing.assert_array_equal(v1.numpy(), v0.numpy())
+    for k in names:
+        np.testing.assert_array_equal(g1.children[k].value.numpy(), g0.children[k].value.numpy())
