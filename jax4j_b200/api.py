@@ -116,6 +116,15 @@ class JAX:
         return g
 
     @staticmethod
+    def vmap(fn: Callable, in_axes: Sequence[int] = None, out_axis: int = 0) -> Callable:
+        """JAX.vmap (JAX.java:311-337, api/Vmap.java): batches fn over the
+        leading axis of its one or two arguments.  in_axes[i] = -1 leaves
+        argument i unbatched; axis 1 of a 2-D argument (and out_axis 1 of a
+        2-D result) is moved by a transpose."""
+        from .vmap import vmap as _vmap
+        return _vmap(fn, in_axes, out_axis)
+
+    @staticmethod
     def checkpoint(fn: Callable) -> Callable:
         """JAX.checkpoint (JAX.java:258-274): a CHECKPOINT equation under a trace."""
         def c(arg):
