@@ -292,6 +292,15 @@ J4C_API int j4c_dot_split(const float *a_hi, const float *a_lo, const float *b_h
  *   act = max(0, C)               act [M, N] -- the layer's relu output
  * Each value is rounded exactly as the separate add / relu / relu' kernels
  * round it, so results equal the unfused sequence bit for bit. */
+/* Strided-batched j4c_dot_split (vmap's batched dot, api/Vmap.java:269-297):
+ * for b < batch, C[b] = op(A[b]) . op(B[b]) with C [batch, M, N].  An operand
+ * flagged batched holds `batch` split matrices back to back (the split of its
+ * [batch * rows, cols] storage); an unbatched one is shared by every b.  One
+ * persistent launch covers every (b, tile).  trans_a && !trans_b is rejected
+ * (pass one operand's transposed split instead, as for j4c_dot_split). */
+J4C_API int j4c_dot_split_batched(const float *a_hi, const float *a_lo, const float *b_hi, const float *b_lo,
+                                  float *c, int64_t batch, int64_t M, int64_t K, int64_t N, int trans_a,
+                                  int trans_b, int a_batched, int b_batched, j4c_stream stream);
 J4C_API int j4c_dot_split_ep(const float *a_hi, const float *a_lo, const float *b_hi, const float *b_lo,
                              float *c, int64_t M, int64_t K, int64_t N, int trans_a, int trans_b,
                              const float *bias, const float *mask, float *act, j4c_stream stream);

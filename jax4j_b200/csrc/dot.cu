@@ -14,7 +14,7 @@ int tc_split_f32(const float *x, int64_t rows, int64_t cols, float *hi, float *l
 int tc_split_f32_t(const float *x, int64_t rows, int64_t cols, float *hi, float *lo, cudaStream_t s);
 int tc_gemm_presplit(const float *ah, const float *al, const float *bh, const float *bl, float *c, int64_t M,
                      int64_t K, int64_t N, int trans_a, int trans_b, const float *bias, const float *mask,
-                     float *act, cudaStream_t s);
+                     float *act, int64_t batch, int a_batched, int b_batched, cudaStream_t s);
 }  // namespace j4c
 
 using namespace j4c;
@@ -93,8 +93,26 @@ int j4c_dot_split_ep(const float *a_hi, const float *a_lo, const float *b_hi, co
     if (!tc_gemm_supported(M, K, N))
         return set_error(J4C_E_UNSUPPORTED, "j4c_dot_split: shape %lld x %lld x %lld is too large", (long long)M,
                          (long long)K, (long long)N);
-    return tc_gemm_presplit(a_hi, a_lo, b_hi, b_lo, c, M, K, N, trans_a, trans_b, bias, mask, act,
+    return tc_gemm_presplit(a_hi, a_lo, b_hi, b_lo, c, M, K, N, trans_a, trans_b, bias, mask, act, 1, 0, 0,
                             as_stream(stream));
+}
+
+int j4c_dot_split_batched(const float *a_hi, const float *a_lo, const float *b_hi, const float *b_lo, float *c,
+                          int64_t batch, int64_t M, int64_t K, int64_t N, int trans_a, int trans_b,
+                          int a_batched, int b_batched, j4c_stream stream) {
+    J4C_REQUIRE(batch >= 0 && M >= 0 && K >= 0 && N >= 0, "j4c_dot_split_batched: negative dimension");
+    if (batch == 0 || M == 0 || N == 0) return J4C_OK;
+    J4C_REQUIRE(c, "j4c_dot_split_batched: NULL output");
+    if (K == 0) return j4c_fill(J4C_FLOAT32, c, batch * M * N, 0.0, stream);
+    J4C_REQUIRE(a_hi && a_lo && b_hi && b_lo, "j4c_dot_split_batched: NULL operand");
+    J4C_REQUIRE(batch < (1ll << 31), "j4c_dot_split_batched: batch too large");
+    if (!tc_gemm_supported(M, K, N))
+        return set_error(J4C_E_UNSUPPORTED, "j4c_dot_split_batched: shape %lld x %lld x %lld is too large",
+                         (long long)M, (long long)K, (long long)N);
+    J4C_REQUIRE(!(trans_a && !trans_b),
+                "j4c_dot_split_batched: A^T . B takes one operand's transposed split (flip its flag)");
+    return tc_gemm_presplit(a_hi, a_lo, b_hi, b_lo, c, M, K, N, trans_a, trans_b, nullptr, nullptr, nullptr,
+                            batch, a_batched, b_batched, as_stream(stream));
 }
 
 int j4c_dot_split(const float *a_hi, const float *a_lo, const float *b_hi, const float *b_lo, float *c,

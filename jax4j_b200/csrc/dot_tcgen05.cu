@@ -133,12 +133,13 @@ __device__ __forceinline__ bool wait_bar(uint32_t bar, uint32_t parity, volatile
     }
 }
 
-__device__ __forceinline__ void tma_load_2d(uint32_t dst, const CUtensorMap *map, int x, int y,
+// 3-D tile load {x, y, z}: z selects the batch entry (0 for an unbatched operand).
+__device__ __forceinline__ void tma_load_3d(uint32_t dst, const CUtensorMap *map, int x, int y, int z,
                                             uint32_t bar) {
     asm volatile(
-        "cp.async.bulk.tensor.2d.shared::cluster.global.mbarrier::complete_tx::bytes"
-        " [%0], [%1, {%2, %3}], [%4];" ::"r"(dst),
-        "l"(reinterpret_cast<uint64_t>(map)), "r"(x), "r"(y), "r"(bar)
+        "cp.async.bulk.tensor.3d.shared::cluster.global.mbarrier::complete_tx::bytes"
+        " [%0], [%1, {%2, %3, %4}], [%5];" ::"r"(dst),
+        "l"(reinterpret_cast<uint64_t>(map)), "r"(x), "r"(y), "r"(z), "r"(bar)
         : "memory");
 }
 
@@ -248,14 +249,14 @@ __device__ __forceinline__ float ep_relu(float v) { return (0.0f >= v) ? 0.0f : 
 
 // Loads one operand's hi or lo tile (ROWS of M or N, BK of K) into smem.
 template <int ROWS, int BK, bool MN>
-__device__ __forceinline__ void load_operand(uint32_t dst, const CUtensorMap *map, int kx, int row0,
+__device__ __forceinline__ void load_operand(uint32_t dst, const CUtensorMap *map, int kx, int row0, int z,
                                              uint32_t bar) {
     if constexpr (!MN) {
-        tma_load_2d(dst, map, kx, row0, bar);  // box {BK, ROWS} of a [rows, K] array
+        tma_load_3d(dst, map, kx, row0, z, bar);  // box {BK, ROWS, 1} of a [batch][rows, K] array
     } else {
 #pragma unroll
-        for (int i = 0; i < ROWS / MNW; i++)   // boxes {32, BK} of a [K, rows] array
-            tma_load_2d(dst + i * (MNW * BK * 4), map, row0 + i * MNW, kx, bar);
+        for (int i = 0; i < ROWS / MNW; i++)      // boxes {32, BK, 1} of a [batch][K, rows] array
+            tma_load_3d(dst + i * (MNW * BK * 4), map, row0 + i * MNW, kx, z, bar);
     }
 }
 
@@ -264,7 +265,7 @@ __global__ void __launch_bounds__(kThreads, 1)
 gemm_3xtf32_kernel(const __grid_constant__ CUtensorMap tAh, const __grid_constant__ CUtensorMap tAl,
                    const __grid_constant__ CUtensorMap tBh, const __grid_constant__ CUtensorMap tBl,
                    float *__restrict__ C, int M, int N, int num_kb, int vec_store, int store_t,
-                   Epilogue ep, int *status) {
+                   Epilogue ep, int batch, int a_batched, int b_batched, int *status) {
     using Q = Cfg<BN, STAGES, BK>;
     constexpr int CHUNK_KB = Q::CHUNK_KB;
     extern __shared__ uint8_t smem_raw[];
@@ -273,7 +274,8 @@ gemm_3xtf32_kernel(const __grid_constant__ CUtensorMap tAh, const __grid_constan
     volatile int *abort = &ctl->abort;
     const int warp = threadIdx.x / 32, lane = threadIdx.x % 32;
     const int num_m = (M + BM - 1) / BM, num_n = (N + BN - 1) / BN;
-    const int num_tiles = num_m * num_n;
+    const int tiles_per_batch = num_m * num_n;
+    const int num_tiles = tiles_per_batch * batch;  // batch entries one after another
 
     if (threadIdx.x == 0) {
         for (int s = 0; s < STAGES; s++) {
@@ -310,7 +312,9 @@ gemm_3xtf32_kernel(const __grid_constant__ CUtensorMap tAh, const __grid_constan
             bool ok = true;
             for (int t = blockIdx.x; ok && t < num_tiles; t += gridDim.x) {
                 int mt, nt;
-                tile_coords(t, num_m, num_n, mt, nt);
+                const int bidx = t / tiles_per_batch;
+                tile_coords(t - bidx * tiles_per_batch, num_m, num_n, mt, nt);
+                const int za = a_batched ? bidx : 0, zb = b_batched ? bidx : 0;
                 for (int kb = 0; kb < num_kb; kb++) {
                     if (!wait_bar(smem_u32(&ctl->empty[stage]), phase ^ 1, abort, status)) {
                         ok = false;
@@ -320,10 +324,10 @@ gemm_3xtf32_kernel(const __grid_constant__ CUtensorMap tAh, const __grid_constan
                     const uint32_t fb = smem_u32(&ctl->full[stage]);
                     mbar_expect_tx(fb, Q::STAGE_BYTES);
                     const int kx = kb * BK;
-                    load_operand<BM, BK, A_MN>(sb, &tAh, kx, mt * BM, fb);
-                    load_operand<BM, BK, A_MN>(sb + Q::A_BYTES, &tAl, kx, mt * BM, fb);
-                    load_operand<BN, BK, B_MN>(sb + 2 * Q::A_BYTES, &tBh, kx, nt * BN, fb);
-                    load_operand<BN, BK, B_MN>(sb + 2 * Q::A_BYTES + Q::B_BYTES, &tBl, kx, nt * BN, fb);
+                    load_operand<BM, BK, A_MN>(sb, &tAh, kx, mt * BM, za, fb);
+                    load_operand<BM, BK, A_MN>(sb + Q::A_BYTES, &tAl, kx, mt * BM, za, fb);
+                    load_operand<BN, BK, B_MN>(sb + 2 * Q::A_BYTES, &tBh, kx, nt * BN, zb, fb);
+                    load_operand<BN, BK, B_MN>(sb + 2 * Q::A_BYTES + Q::B_BYTES, &tBl, kx, nt * BN, zb, fb);
                     issued++;
                     if (++stage == STAGES) {
                         stage = 0;
@@ -408,7 +412,13 @@ gemm_3xtf32_kernel(const __grid_constant__ CUtensorMap tAh, const __grid_constan
         bool ok = true;
         for (int t = blockIdx.x; ok && t < num_tiles; t += gridDim.x) {
             int mt, nt;
-            tile_coords(t, num_m, num_n, mt, nt);
+            const int bidx = t / tiles_per_batch;
+            tile_coords(t - bidx * tiles_per_batch, num_m, num_n, mt, nt);
+            // this batch entry's C (and mask / act): [M, N], or [N, M] when stored transposed
+            const size_t boff = (size_t)bidx * (size_t)M * (size_t)N;
+            float *const Cb = C + boff;
+            const float *const mask_b = ep.mask ? ep.mask + boff : nullptr;
+            float *const act_b = ep.act ? ep.act + boff : nullptr;
             float acc[Q::COLS_PER_WARP];
 #pragma unroll
             for (int j = 0; j < Q::COLS_PER_WARP; j++) acc[j] = 0.0f;
@@ -445,9 +455,9 @@ gemm_3xtf32_kernel(const __grid_constant__ CUtensorMap tAh, const __grid_constan
                         if (col0 + j < N) {
                             const size_t idx = (size_t)(col0 + j) * (size_t)M + row;
                             float v = ep.bias ? __fadd_rn(acc[j], b) : acc[j];
-                            if (ep.mask) v = __ldg(ep.mask + idx) > 0.0f ? v : 0.0f;
-                            C[idx] = v;
-                            if (ep.act) ep.act[idx] = ep_relu(v);
+                            if (mask_b) v = __ldg(mask_b + idx) > 0.0f ? v : 0.0f;
+                            Cb[idx] = v;
+                            if (act_b) act_b[idx] = ep_relu(v);
                         }
                     }
                 }
@@ -462,14 +472,14 @@ gemm_3xtf32_kernel(const __grid_constant__ CUtensorMap tAh, const __grid_constan
                             x[0] = __fadd_rn(x[0], b.x); x[1] = __fadd_rn(x[1], b.y);
                             x[2] = __fadd_rn(x[2], b.z); x[3] = __fadd_rn(x[3], b.w);
                         }
-                        if (ep.mask) {
-                            const float4 m = __ldg(reinterpret_cast<const float4 *>(ep.mask + base) + v4);
+                        if (mask_b) {
+                            const float4 m = __ldg(reinterpret_cast<const float4 *>(mask_b + base) + v4);
                             x[0] = m.x > 0.0f ? x[0] : 0.0f; x[1] = m.y > 0.0f ? x[1] : 0.0f;
                             x[2] = m.z > 0.0f ? x[2] : 0.0f; x[3] = m.w > 0.0f ? x[3] : 0.0f;
                         }
-                        reinterpret_cast<float4 *>(C + base)[v4] = make_float4(x[0], x[1], x[2], x[3]);
-                        if (ep.act)
-                            reinterpret_cast<float4 *>(ep.act + base)[v4] =
+                        reinterpret_cast<float4 *>(Cb + base)[v4] = make_float4(x[0], x[1], x[2], x[3]);
+                        if (act_b)
+                            reinterpret_cast<float4 *>(act_b + base)[v4] =
                                 make_float4(ep_relu(x[0]), ep_relu(x[1]), ep_relu(x[2]), ep_relu(x[3]));
                     }
                 } else {
@@ -477,9 +487,9 @@ gemm_3xtf32_kernel(const __grid_constant__ CUtensorMap tAh, const __grid_constan
                     for (int j = 0; j < Q::COLS_PER_WARP; j++) {
                         if (col0 + j < N) {
                             float v = ep.bias ? __fadd_rn(acc[j], __ldg(ep.bias + col0 + j)) : acc[j];
-                            if (ep.mask) v = __ldg(ep.mask + base + j) > 0.0f ? v : 0.0f;
-                            C[base + j] = v;
-                            if (ep.act) ep.act[base + j] = ep_relu(v);
+                            if (mask_b) v = __ldg(mask_b + base + j) > 0.0f ? v : 0.0f;
+                            Cb[base + j] = v;
+                            if (act_b) act_b[base + j] = ep_relu(v);
                         }
                     }
                 }
@@ -601,12 +611,13 @@ inline int64_t split_pitch(int64_t cols) { return ceil_div(cols, 4) * 4; }
 //   MN-major use (rows = K, cols = M or N): box {32, BK}, 128-byte swizzle of 32-byte atoms.
 // Columns past `cols` and rows past `rows` read as zero (TMA fill).
 static int make_map(CUtensorMap *map, const float *base, int64_t rows, int64_t cols, bool mn, int box_rows,
-                    int bk) {
+                    int bk, int64_t batch) {
     auto fn = encode_fn();
     if (!fn) return set_error(J4C_E_CUDA, "cuTensorMapEncodeTiled is unavailable");
-    cuuint64_t dims[2] = {(cuuint64_t)cols, (cuuint64_t)rows};
-    cuuint64_t strides[1] = {(cuuint64_t)split_pitch(cols) * 4};
-    cuuint32_t box[2];
+    // [batch][rows, pitch]: batch entries back to back (batch = 1 for an operand shared by all)
+    cuuint64_t dims[3] = {(cuuint64_t)cols, (cuuint64_t)rows, (cuuint64_t)batch};
+    cuuint64_t strides[2] = {(cuuint64_t)split_pitch(cols) * 4, (cuuint64_t)(rows * split_pitch(cols) * 4)};
+    cuuint32_t box[3];
     CUtensorMapSwizzle sw;
     if (mn) {
         box[0] = MNW;
@@ -617,8 +628,9 @@ static int make_map(CUtensorMap *map, const float *base, int64_t rows, int64_t c
         box[1] = (cuuint32_t)box_rows;
         sw = bk == 32 ? CU_TENSOR_MAP_SWIZZLE_128B : CU_TENSOR_MAP_SWIZZLE_64B;
     }
-    cuuint32_t estr[2] = {1, 1};
-    CUresult r = fn(map, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 2, const_cast<float *>(base), dims, strides, box,
+    box[2] = 1;
+    cuuint32_t estr[3] = {1, 1, 1};
+    CUresult r = fn(map, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 3, const_cast<float *>(base), dims, strides, box,
                     estr, CU_TENSOR_MAP_INTERLEAVE_NONE, sw, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
                     CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
     if (r != CUDA_SUCCESS) return set_error(J4C_E_CUDA, "cuTensorMapEncodeTiled failed (%d)", (int)r);
@@ -627,7 +639,8 @@ static int make_map(CUtensorMap *map, const float *base, int64_t rows, int64_t c
 
 template <int BN, int STAGES, int BK, bool A_MN, bool B_MN>
 static int launch_gemm(const float *ah, const float *al, const float *bh, const float *bl, float *c,
-                       int64_t M, int64_t N, int64_t K, bool store_t, const Epilogue &ep, cudaStream_t s) {
+                       int64_t M, int64_t N, int64_t K, bool store_t, const Epilogue &ep, int64_t batch,
+                       bool a_bat, bool b_bat, cudaStream_t s) {
     using Q = Cfg<BN, STAGES, BK>;
     auto kernel = gemm_3xtf32_kernel<BN, STAGES, BK, A_MN, B_MN>;
     static std::mutex mu;
@@ -647,17 +660,20 @@ static int launch_gemm(const float *ah, const float *al, const float *bh, const 
     // op(A) [M, K]: stored [M, K] (K-major) or [K, M] (MN-major); likewise op(B)^T [N, K].
     const int64_t ar = A_MN ? K : M, ac = A_MN ? M : K;
     const int64_t br = B_MN ? K : N, bc = B_MN ? N : K;
-    if ((rc = make_map(&mAh, ah, ar, ac, A_MN, BM, BK)) || (rc = make_map(&mAl, al, ar, ac, A_MN, BM, BK)) ||
-        (rc = make_map(&mBh, bh, br, bc, B_MN, BN, BK)) || (rc = make_map(&mBl, bl, br, bc, B_MN, BN, BK)))
+    const int64_t ab = a_bat ? batch : 1, bb = b_bat ? batch : 1;
+    if ((rc = make_map(&mAh, ah, ar, ac, A_MN, BM, BK, ab)) || (rc = make_map(&mAl, al, ar, ac, A_MN, BM, BK, ab)) ||
+        (rc = make_map(&mBh, bh, br, bc, B_MN, BN, BK, bb)) || (rc = make_map(&mBl, bl, br, bc, B_MN, BN, BK, bb)))
         return rc;
     int *status = device_status_ptr();
     if (!status) return set_error(J4C_E_OOM, "no device status word");
-    const int64_t tiles = ceil_div(M, BM) * ceil_div(N, BN);
+    const int64_t tiles = ceil_div(M, BM) * ceil_div(N, BN) * batch;
+    if (tiles >= (1ll << 31)) return set_error(J4C_E_UNSUPPORTED, "dot: too many output tiles");
     const int grid = (int)std::min<int64_t>(tiles, sm_count());
     const int vec = (N % 4 == 0) && aligned16(c) && (!ep.bias || aligned16(ep.bias)) &&
                     (!ep.mask || aligned16(ep.mask)) && (!ep.act || aligned16(ep.act));
     kernel<<<grid, kThreads, Q::SMEM_BYTES, s>>>(mAh, mAl, mBh, mBl, c, (int)M, (int)N, (int)ceil_div(K, BK),
-                                                 store_t ? 0 : vec, store_t ? 1 : 0, ep, status);
+                                                 store_t ? 0 : vec, store_t ? 1 : 0, ep, (int)batch, a_bat ? 1 : 0,
+                                                 b_bat ? 1 : 0, status);
     J4C_LAUNCH_CHECK("gemm_3xtf32_kernel");
     return J4C_OK;
 }
@@ -665,15 +681,18 @@ static int launch_gemm(const float *ah, const float *al, const float *bh, const 
 template <int BN, int STAGES, int BK>
 static int launch_gemm_any(const float *ah, const float *al, const float *bh, const float *bl, float *c,
                            int64_t M, int64_t N, int64_t K, bool a_mn, bool b_mn, const Epilogue &ep,
-                           cudaStream_t s) {
-    if (!a_mn && !b_mn) return launch_gemm<BN, STAGES, BK, false, false>(ah, al, bh, bl, c, M, N, K, false, ep, s);
-    if (a_mn && !b_mn) return launch_gemm<BN, STAGES, BK, true, false>(ah, al, bh, bl, c, M, N, K, false, ep, s);
+                           int64_t batch, bool a_bat, bool b_bat, cudaStream_t s) {
+    if (!a_mn && !b_mn)
+        return launch_gemm<BN, STAGES, BK, false, false>(ah, al, bh, bl, c, M, N, K, false, ep, batch, a_bat, b_bat, s);
+    if (a_mn && !b_mn)
+        return launch_gemm<BN, STAGES, BK, true, false>(ah, al, bh, bl, c, M, N, K, false, ep, batch, a_bat, b_bat, s);
     // The wide (BN = 256) operand is read MN-major at a smem cost that
     // throttles the tensor pipe, so a K-major A with an MN-major B runs as
     // C^T = op(B)^T . op(A)^T: B's split becomes the (MN-major) A operand,
     // A's the (K-major) B operand, and the epilogue stores transposed.
-    if (!a_mn && b_mn) return launch_gemm<BN, STAGES, BK, true, false>(bh, bl, ah, al, c, N, M, K, true, ep, s);
-    return launch_gemm<BN, STAGES, BK, true, true>(ah, al, bh, bl, c, M, N, K, false, ep, s);
+    if (!a_mn && b_mn)
+        return launch_gemm<BN, STAGES, BK, true, false>(bh, bl, ah, al, c, N, M, K, true, ep, batch, b_bat, a_bat, s);
+    return launch_gemm<BN, STAGES, BK, true, true>(ah, al, bh, bl, c, M, N, K, false, ep, batch, a_bat, b_bat, s);
 }
 
 int split_t(const float *src, int64_t rows, int64_t cols, float *hi, float *lo, cudaStream_t s) {
@@ -726,7 +745,7 @@ int tc_split_f32_t(const float *x, int64_t rows, int64_t cols, float *hi, float 
 
 int tc_gemm_presplit(const float *ah, const float *al, const float *bh, const float *bl, float *c, int64_t M,
                      int64_t K, int64_t N, int trans_a, int trans_b, const float *bias, const float *mask,
-                     float *act, cudaStream_t s) {
+                     float *act, int64_t batch, int a_batched, int b_batched, cudaStream_t s) {
     J4C_REQUIRE(aligned16(ah) && aligned16(al) && aligned16(bh) && aligned16(bl),
                 "dot: split operands must be 16-byte aligned");
     // op(A) = A [M,K] is read K-major; A^T (A stored [K,M]) MN-major.
@@ -737,8 +756,10 @@ int tc_gemm_presplit(const float *ah, const float *al, const float *bh, const fl
         return v ? atoi(v) : 1;
     }();
     const tc::Epilogue ep{bias, mask, act};
-    if (variant == 0) return tc::launch_gemm_any<256, 2, 32>(ah, al, bh, bl, c, M, N, K, a_mn, b_mn, ep, s);
-    return tc::launch_gemm_any<256, 4, 16>(ah, al, bh, bl, c, M, N, K, a_mn, b_mn, ep, s);
+    const bool ab = a_batched != 0, bb = b_batched != 0;
+    if (variant == 0)
+        return tc::launch_gemm_any<256, 2, 32>(ah, al, bh, bl, c, M, N, K, a_mn, b_mn, ep, batch, ab, bb, s);
+    return tc::launch_gemm_any<256, 4, 16>(ah, al, bh, bl, c, M, N, K, a_mn, b_mn, ep, batch, ab, bb, s);
 }
 
 int tc_gemm_f32(const float *a, const float *b, float *c, int64_t M, int64_t K, int64_t N,
@@ -756,10 +777,10 @@ int tc_gemm_f32(const float *a, const float *b, float *c, int64_t M, int64_t K, 
     if (b_transposed) {
         // both stored K-leading: B goes in as the split of B^T (K-major)
         if ((rc = tc::split_t(b, br, bc, bh, bl, s))) return rc;
-        return tc_gemm_presplit(ah, al, bh, bl, c, M, K, N, trans_a, 1, nullptr, nullptr, nullptr, s);
+        return tc_gemm_presplit(ah, al, bh, bl, c, M, K, N, trans_a, 1, nullptr, nullptr, nullptr, 1, 0, 0, s);
     }
     if ((rc = tc::split(b, br, bc, bh, bl, s))) return rc;
-    return tc_gemm_presplit(ah, al, bh, bl, c, M, K, N, trans_a, trans_b, nullptr, nullptr, nullptr, s);
+    return tc_gemm_presplit(ah, al, bh, bl, c, M, K, N, trans_a, trans_b, nullptr, nullptr, nullptr, 1, 0, 0, s);
 }
 
 }  // namespace j4c

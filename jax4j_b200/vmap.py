@@ -13,8 +13,9 @@ batch axis leads the output (out_axis 1 moves it back for 2-D outputs), and
 eager execution -- vmap does not compose with further tracing.
 
 Device mapping: a DOT with only its left operand batched is one GEMM over
-[B*M, K]; other batched DOTs run one GEMM per example; per-example SUM/MEAN is
-one row reduction over [B, rest].
+[B*M, K]; other batched FLOAT32 DOTs are one strided-batched GEMM launch
+(j4c_dot_split_batched); per-example SUM/MEAN is one row reduction over
+[B, rest].
 """
 from __future__ import annotations
 
@@ -85,8 +86,26 @@ def batched_dot(a: ConcreteNDArray, a_batched: bool, b: ConcreteNDArray, b_batch
     if a_batched and not b_batched:
         # every example shares B: one product over the stacked rows
         return a.reshape(Shape(batch * M, K)).dot(b).reshape(Shape(batch, M, N))
+    if a.dtype() == b.dtype() == DType.FLOAT32 and M and K and N:
+        return _strided_batched_dot(a, a_batched, b, b_batched, batch, M, K, N)
     outs = [(_leading(a, i) if a_batched else a).dot(_leading(b, i) if b_batched else b) for i in range(batch)]
     return _pm.stack(outs).reshape(Shape(batch, M, N))
+
+
+def _strided_batched_dot(a, a_batched, b, b_batched, batch, M, K, N) -> ConcreteNDArray:
+    """One launch of the strided-batched tcgen05 GEMM (j4c_dot_split_batched):
+    each operand is split once as its [entries * rows, cols] storage."""
+    import torch
+    from .core import _tf32_split
+    dev = a._check_devices(b)
+    a2 = a.reshape(Shape(batch * M, K)) if a_batched else a
+    b2 = b.reshape(Shape(batch * K, N)) if b_batched else b
+    ah, al = _tf32_split(a2)
+    bh, bl = _tf32_split(b2)
+    out = torch.empty(batch * M * N, dtype=torch.float32, device=a.tensor().device)
+    call("j4c_dot_split_batched", ah.data_ptr(), al.data_ptr(), bh.data_ptr(), bl.data_ptr(), out.data_ptr(),
+         batch, M, K, N, 0, 0, int(a_batched), int(b_batched), a._stream())
+    return ConcreteNDArray._wrap(out, Shape(batch, M, N), DType.FLOAT32, dev)
 
 
 def broadcast_to_batch(x: NDArray, batch: int) -> ConcreteNDArray:

@@ -126,3 +126,21 @@ def test_vmap_mlp_forward_per_example_against_oracle(J):
 def test_vmap_rejects_unbatched_psum(J):
     with pytest.raises(J.UnsupportedOperationException):
         J.JAX.vmap(lambda x: J.Lax.psum(x))(arr(J, [1, 2, 3, 4], (2, 2)))
+
+
+@pytest.mark.parametrize("a_b,b_b,B,M,K,N", [(False, True, 5, 130, 200, 70), (True, True, 3, 256, 96, 300),
+                                               (True, True, 7, 1, 33, 9)])
+def test_strided_batched_gemm_one_launch(J, a_b, b_b, B, M, K, N):
+    """j4c_dot_split_batched covers every (example, tile) in one launch."""
+    from jax4j_b200 import _lib
+    r = np.random.default_rng(B * 100 + M)
+    A = r.uniform(-1, 1, (B, M, K) if a_b else (M, K)).astype(np.float32)
+    W = r.uniform(-1, 1, (B, K, N) if b_b else (K, N)).astype(np.float32)
+    f = J.JAX.vmap(lambda a, w: a.dot(w), in_axes=[0 if a_b else -1, 0 if b_b else -1])
+    n0 = _lib.kernel_launches()
+    out = f(J.ConcreteNDArray.of(A), J.ConcreteNDArray.of(W))
+    launched = _lib.kernel_launches() - n0
+    assert launched <= 3, launched  # two operand splits and one GEMM
+    o = out.numpy()
+    for i in range(B):
+        assert_rel(o[i], orc.dot(A[i] if a_b else A, W[i] if b_b else W), TOL_REDUCTION, f"example {i}")
