@@ -400,6 +400,12 @@ J4C_API int j4c_psum(j4c_comm comm, int dtype, const void *in, void *out, int64_
  * [nranks, n] in rank order. */
 J4C_API int j4c_all_gather(j4c_comm comm, int dtype, const void *in, void *out, int64_t n,
                    j4c_stream stream);
+/* Reduce-scatter: in [nranks * n] on every rank; out [n] on rank r = the sum
+ * over ranks of their slice r (the transpose of all-gather, used by the
+ * optional reduce-scatter ALL_GATHER VJP; the reference's VJP,
+ * api/Grad.java:437-441, takes the local slice without communication). */
+J4C_API int j4c_reduce_scatter(j4c_comm comm, int dtype, const void *in, void *out, int64_t n,
+                               j4c_stream stream);
 /* Waits until the work enqueued on `stream` is done, bounded by the
  * communicator's timeout; on expiry aborts the communicator and returns
  * J4C_E_TIMEOUT (replaces the unbounded CyclicBarrier.await,

@@ -93,6 +93,7 @@ SIGNATURES = {
     "j4c_comm_abort": [P],
     "j4c_psum": [P, I32, P, P, I64, P],
     "j4c_all_gather": [P, I32, P, P, I64, P],
+    "j4c_reduce_scatter": [P, I32, P, P, I64, P],
     "j4c_comm_wait": [P, P],
     "j4c_psum_slots": [I32, C.POINTER(P), I32, P, I64, P],
 }

@@ -20,7 +20,8 @@ from ._lib import call
 from .core import (ConcreteNDArray, Device, DType, IllegalArgumentException, NDArray, PRNGKey,
                    Primitive, Shape, stream_of)
 from .pytree import PyTree, PyTrees
-from .tracing import CheckpointMeta, Equation, PmapMeta, Tracer, TracedNDArray, to_var
+from .tracing import (CheckpointMeta, CondMeta, Equation, PmapMeta, ScanMeta, Tracer, TracedNDArray, WhileMeta,
+                      to_var)
 
 
 # ---------------------------------------------------------------------------
@@ -171,6 +172,37 @@ class JAX:
         return mapped
 
 
+class ScanResult:
+    """Lax.ScanResult (Lax.java:127): the final carry and the stacked ys
+    (record accessors carry() and ys(); also unpacks as (carry, ys))."""
+
+    def __init__(self, carry: NDArray, ys: NDArray):
+        self._carry, self._ys = carry, ys
+
+    def carry(self) -> NDArray:
+        return self._carry
+
+    def ys(self) -> NDArray:
+        return self._ys
+
+    def __iter__(self):
+        return iter((self._carry, self._ys))
+
+
+def _trace_step(step_fn: Callable, carry_shape, carry_dtype, x_shape, x_dtype):
+    """Lax.traceStep (Lax.java:219-233)."""
+    Tracer.start()
+    try:
+        t = Tracer.current()
+        cv = t.nextVar(carry_shape, carry_dtype)
+        xv = t.nextVar(x_shape, x_dtype)
+        outs = step_fn(TracedNDArray(cv), TracedNDArray(xv))
+        return Tracer.stop([cv, xv], [to_var(outs[0]), to_var(outs[1])])
+    except BaseException:
+        Tracer.abort()
+        raise
+
+
 def _trace_body(fn: Callable, specs) -> "Jaxpr":
     """JAX.traceBody (JAX.java:379-391) for any number of inputs."""
     Tracer.start()
@@ -212,6 +244,76 @@ class Lax:
             tracer.addEquation(Equation([v], [out], Primitive.ALL_GATHER, numDevices))
             return TracedNDArray(out)
         return _pm.all_gather_value(x)
+
+    # ---- control flow (Lax.java:69-217) ----
+    @staticmethod
+    def cond(pred: NDArray, trueFn: Callable, falseFn: Callable, operand: NDArray) -> NDArray:
+        """Lax.cond (Lax.java:72-88): eager -> the taken branch; traced -> one
+        COND equation holding both branches (its VJP flows through the taken
+        branch, pred gets zero)."""
+        if Tracer.current() is None:
+            return trueFn(operand) if _grad.is_true(pred) else falseFn(operand)
+        t_br = _grad.make_jaxpr(trueFn, operand)
+        f_br = _grad.make_jaxpr(falseFn, operand)
+        tracer = Tracer.current()
+        pv, ov = to_var(pred), to_var(operand)
+        out = tracer.nextVar(t_br.outVars[0].shape, operand.dtype())
+        tracer.addEquation(Equation([pv, ov], [out], Primitive.COND, CondMeta(t_br, f_br)))
+        return TracedNDArray(out)
+
+    @staticmethod
+    def whileLoop(condFn: Callable, bodyFn: Callable, init: NDArray) -> NDArray:
+        """Lax.whileLoop (Lax.java:92-110): not reverse-mode differentiable."""
+        if Tracer.current() is None:
+            state = init
+            while _grad.is_true(condFn(state)):
+                state = bodyFn(state)
+            return state
+        c = _grad.make_jaxpr(condFn, init)
+        b = _grad.make_jaxpr(bodyFn, init)
+        tracer = Tracer.current()
+        iv = to_var(init)
+        out = tracer.nextVar(b.outVars[0].shape, init.dtype())
+        tracer.addEquation(Equation([iv], [out], Primitive.WHILE, WhileMeta(c, b)))
+        return TracedNDArray(out)
+
+    @staticmethod
+    def foriLoop(lower: int, upper: int, bodyFn: Callable, init: NDArray) -> NDArray:
+        """Lax.foriLoop (Lax.java:119-125): a host loop; under a trace each call
+        appends its equations, so it is differentiable with no new primitive."""
+        state = init
+        for i in range(lower, upper):
+            state = bodyFn(i, state)
+        return state
+
+    @staticmethod
+    def scan(stepFn: Callable, initCarry: NDArray, xs: NDArray) -> "ScanResult":
+        """Lax.scan (Lax.java:135-163): stepFn(carry, x_t) -> [new carry, y_t]
+        for each leading slice of xs; returns (final carry, stacked ys)."""
+        d = xs.shape().dimensions()
+        steps = d[0]
+        x_step = Shape(d[1:])
+        if Tracer.current() is None:
+            carry, ys = initCarry, []
+            for t in range(steps):
+                carry, y = stepFn(carry, _grad.slice_leading(xs, t))
+                ys.append(y)
+            return ScanResult(carry, _grad.stack_leading(ys))
+        step = _trace_step(stepFn, initCarry.shape(), initCarry.dtype(), x_step, xs.dtype())
+        tracer = Tracer.current()
+        cv, xv = to_var(initCarry), to_var(xs)
+        y_shape = step.outVars[1].shape
+        c_out = tracer.nextVar(step.outVars[0].shape, initCarry.dtype())
+        ys_out = tracer.nextVar(Shape((steps,) + y_shape.dimensions()), xs.dtype())
+        tracer.addEquation(Equation([cv, xv], [c_out, ys_out], Primitive.SCAN, ScanMeta(step)))
+        return ScanResult(TracedNDArray(c_out), TracedNDArray(ys_out))
+
+    @staticmethod
+    def setAllGatherVjp(mode: str) -> None:
+        """'slice' (default, the reference's ALL_GATHER VJP: the local slice of
+        the cotangent) or 'reduce_scatter' (the transpose of all-gather: the
+        cotangents' slices for this shard summed over shards)."""
+        _pm.set_all_gather_vjp(mode)
 
     @staticmethod
     def psumTree(tree: PyTree) -> PyTree:

@@ -175,6 +175,19 @@ int j4c_all_gather(j4c_comm comm, int dtype, const void *in, void *out, int64_t 
     return J4C_OK;
 }
 
+int j4c_reduce_scatter(j4c_comm comm, int dtype, const void *in, void *out, int64_t n, j4c_stream stream) {
+    J4C_REQUIRE(comm && !comm->aborted, "j4c_reduce_scatter: communicator is NULL or aborted");
+    J4C_REQUIRE(dtype == J4C_FLOAT32 || dtype == J4C_FLOAT64, "j4c_reduce_scatter: dtype %s",
+                dtype_name(dtype));
+    if (n == 0) return J4C_OK;
+    J4C_REQUIRE(in && out, "j4c_reduce_scatter: NULL pointer");
+    ncclResult_t r = ncclReduceScatter(in, out, (size_t)n, nccl_type(dtype), ncclSum, comm->nccl,
+                                       as_stream(stream));
+    if (r != ncclSuccess && r != ncclInProgress) return nccl_status(r, "ncclReduceScatter");
+    if (r == ncclInProgress) return wait_comm_ready(comm, "ncclReduceScatter");
+    return J4C_OK;
+}
+
 // Waits (bounded by the communicator's timeout) until all work enqueued on
 // `stream` has finished, checking the communicator for asynchronous errors.
 int j4c_comm_wait(j4c_comm comm, j4c_stream stream) {

@@ -44,7 +44,7 @@ OP_INPUT = -1
 _VJP_READS = {
     P.MUL: ("in",), P.DIV: ("in",), P.EXP: ("out",), P.LOG: ("in",), P.SIN: ("in",),
     P.COS: ("in",), P.TANH: ("out",), P.RELU: ("in",), P.SIGMOID: ("out",), P.DOT: ("in",),
-    P.MAX: ("in",), P.MIN: ("in",),
+    P.MAX: ("in",), P.MIN: ("in",), P.COND: ("in",), P.SCAN: ("in",),
 }
 
 

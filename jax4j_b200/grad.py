@@ -27,7 +27,8 @@ import torch
 from ._lib import call, dims as _dims
 from .core import (ConcreteNDArray, DType, IllegalArgumentException, NDArray, Primitive, Shape,
                    UnsupportedOperationException, _dot_raw)
-from .tracing import AxisMeta, CheckpointMeta, Jaxpr, PmapMeta, Tracer, TracedNDArray, Var
+from .tracing import (AxisMeta, CheckpointMeta, CondMeta, Jaxpr, PmapMeta, ScanMeta, Tracer, TracedNDArray, Var,
+                      WhileMeta)
 
 
 # ---------------------------------------------------------------------------
@@ -154,17 +155,77 @@ def _evaluate(jaxpr: Jaxpr, args: List[NDArray], keep_for_vjp: bool) -> Dict[int
         from . import fusion
         for kind, item in fusion.plan_for(jaxpr, keep_for_vjp).steps:
             if kind == "eq":
-                inputs = [values[v.id] for v in item.inputs]
-                values[item.outputs[0].id] = execute_primitive(item.primitive, item, inputs)
+                _run_equation(item, values)
             elif kind == "dot_ep":
                 fusion.run_dot_epilogue(item, values)
             else:
                 fusion.run_group(item, values)
         return values
     for eq in jaxpr.equations:
-        inputs = [values[v.id] for v in eq.inputs]
-        values[eq.outputs[0].id] = execute_primitive(eq.primitive, eq, inputs)
+        _run_equation(eq, values)
     return values
+
+
+def _run_equation(eq, values: Dict[int, NDArray]) -> None:
+    inputs = [values[v.id] for v in eq.inputs]
+    if eq.primitive == Primitive.SCAN:  # the one two-output primitive
+        carry, ys = scan_forward(eq, inputs)
+        values[eq.outputs[0].id] = carry
+        values[eq.outputs[1].id] = ys
+    else:
+        values[eq.outputs[0].id] = execute_primitive(eq.primitive, eq, inputs)
+
+
+# ---- control flow (api/Lax.java:69-217, Grad.java:213-265) ----------------------------
+def is_true(pred: NDArray) -> bool:
+    """Lax.isTrue (Lax.java:60-62): the first element, nonzero."""
+    return float(pred.numpy().reshape(-1)[0]) != 0.0
+
+
+def slice_leading(a: ConcreteNDArray, t: int) -> ConcreteNDArray:
+    """ScanUtil.sliceLeading: step t of a [T, *step] array (a view)."""
+    step = Shape(a.shape().dimensions()[1:])
+    n = step.size()
+    return ConcreteNDArray._wrap(a.tensor()[t * n:(t + 1) * n], step, a.dtype(), a.device())
+
+
+def stack_leading(items: List[ConcreteNDArray]) -> ConcreteNDArray:
+    """ScanUtil.stackLeading: [T, *step]."""
+    from . import pmap as _pm
+    return _pm.stack(items)
+
+
+def scan_forward(eq, inputs: List[NDArray]):
+    """Grad.scanForward (Grad.java:213-230): the step once per leading slice."""
+    m: ScanMeta = eq.metadata
+    carry, xs = inputs
+    ys = []
+    for t in range(xs.shape().dimensions()[0]):
+        carry, y = forward_interpret(m.stepFn, [carry, slice_leading(xs, t)])
+        ys.append(y)
+    return carry, stack_leading(ys)
+
+
+def scan_backward(eq, inputs: List[NDArray], g_carry_final, g_ys):
+    """Grad.scanBackward (Grad.java:232-265): re-runs the forward to record
+    every step's (carry, x), then backward-interprets the step in reverse."""
+    m: ScanMeta = eq.metadata
+    init, xs = inputs
+    steps = xs.shape().dimensions()[0]
+    y_shape = m.stepFn.outVars[1].shape
+    carry_in, x_in = [], []
+    carry = init
+    for t in range(steps):
+        carry_in.append(carry)
+        x_in.append(slice_leading(xs, t))
+        carry = forward_interpret(m.stepFn, [carry, x_in[t]])[0]
+    dev = init.device()
+    g_carry = g_carry_final if g_carry_final is not None else zeros(init.shape(), init.dtype(), dev)
+    g_xs = [None] * steps
+    for t in range(steps - 1, -1, -1):
+        g_y = slice_leading(g_ys, t) if g_ys is not None else zeros(y_shape, m.stepFn.outVars[1].dtype, dev)
+        g_carry, g_xs[t] = backward_interpret(m.stepFn, [carry_in[t], x_in[t]], [g_carry, g_y])
+    return g_carry, stack_leading(g_xs)
 
 
 def fill_forward_values(jaxpr: Jaxpr, args: List[NDArray]) -> Dict[int, NDArray]:
@@ -223,6 +284,15 @@ def do_backward(jaxpr: Jaxpr, values: Dict[int, NDArray], seeds: List[NDArray]) 
     for v, s in zip(jaxpr.outVars, seeds):
         _merge(grads, v.id, s)
     for eq in reversed(jaxpr.equations):
+        if eq.primitive == Primitive.SCAN:
+            g_c, g_y = grads.get(eq.outputs[0].id), grads.get(eq.outputs[1].id)
+            if (g_c is None and g_y is None) or not any(v.id in need for v in eq.inputs):
+                continue
+            gi = scan_backward(eq, [values.get(v.id) for v in eq.inputs], g_c, g_y)
+            for v, g in zip(eq.inputs, gi):
+                if v.id in need:
+                    _merge(grads, v.id, g)
+            continue
         g_out = grads.get(eq.outputs[0].id)
         if g_out is None:
             continue
@@ -290,6 +360,15 @@ def execute_primitive(p: Primitive, eq, inputs: List[NDArray]) -> NDArray:
         m = eq.metadata
         return inputs[0].argmax(m.axis) if p == Primitive.ARGMAX else inputs[0].argmin(m.axis)
     if p == Primitive.CAST: return inputs[0].astype(eq.metadata)
+    if p == Primitive.COND:
+        m: CondMeta = eq.metadata
+        return forward_interpret(m.trueBranch if is_true(inputs[0]) else m.falseBranch, [inputs[1]])[0]
+    if p == Primitive.WHILE:
+        m: WhileMeta = eq.metadata
+        state = inputs[0]
+        while is_true(forward_interpret(m.condFn, [state])[0]):
+            state = forward_interpret(m.bodyFn, [state])[0]
+        return state
     if p == Primitive.PMAP:
         m: PmapMeta = eq.metadata
         shards = [_pm.shards_of(x, m.numDevices()) for x in inputs]
@@ -374,6 +453,16 @@ def compute_vjps(p: Primitive, eq, g: ConcreteNDArray, inputs: List[NDArray], ou
         return maxmin_grad(g, inputs[0], inputs[1], False)
     if p in (Primitive.ARGMAX, Primitive.ARGMIN):
         return [_zeros_for(eq.inputs[0], g)]
+    if p == Primitive.COND:
+        # pred is not differentiable (Grad.java:391-397)
+        m: CondMeta = eq.metadata
+        branch = m.trueBranch if is_true(inputs[0]) else m.falseBranch
+        g_operand = backward_interpret(branch, [inputs[1]], [g])[0] if want_b else None
+        return [_zeros_for(eq.inputs[0], g) if want_a else None, g_operand]
+    if p == Primitive.WHILE:
+        raise UnsupportedOperationException(
+            "Lax.whileLoop is not reverse-mode differentiable (mirrors jax.lax.while_loop, whose iteration "
+            "count is itself data-dependent); use Lax.scan or Lax.foriLoop for a differentiable loop.")
     if p == Primitive.PMAP:
         m: PmapMeta = eq.metadata
         D = m.numDevices()

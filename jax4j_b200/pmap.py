@@ -153,6 +153,21 @@ class SlotCollective:
         self._await()
         return ConcreteNDArray._wrap(out, x.shape(), x.dtype(), _result_device(x))
 
+    def reduceScatter(self, index: int, x: ConcreteNDArray) -> ConcreteNDArray:
+        """Sum over shards of slice `index` of every shard's [D, *shard] value."""
+        self.slots[index] = x
+        self._await()
+        n = x.shape().size() // self.num_devices
+        for s in self.slots:
+            if s.shape().size() != x.shape().size() or s.dtype() != x.dtype():
+                raise CollectiveError("reduceScatter: shards deposited different sizes or dtypes")
+        es = x.dtype().byteSize()
+        out = torch.empty(n, dtype=x.dtype().torch, device=x.tensor().device)
+        ptrs = (C.c_void_p * self.num_devices)(*[s.data_ptr() + index * n * es for s in self.slots])
+        call("j4c_psum_slots", x.dtype().ordinal, ptrs, self.num_devices, out.data_ptr(), n, x._stream())
+        self._await()
+        return ConcreteNDArray._wrap(out, Shape(x.shape().dimensions()[1:]), x.dtype(), _result_device(x))
+
     def allGather(self, index: int, x: ConcreteNDArray) -> ConcreteNDArray:
         self.slots[index] = x
         self._await()
@@ -204,6 +219,14 @@ class NcclCollective:
         shape = Shape((self.num_devices,) + x.shape().dimensions())
         return ConcreteNDArray._wrap(out, shape, x.dtype(), _result_device(x))
 
+    def reduceScatter(self, index: int, x: ConcreteNDArray) -> ConcreteNDArray:
+        """Sum over ranks of slice `index` of every rank's [D, *shard] value."""
+        n = x.shape().size() // self.num_devices
+        out = torch.empty(n, dtype=x.dtype().torch, device=x.tensor().device)
+        call("j4c_reduce_scatter", self.comms[index], x.dtype().ordinal, x.data_ptr(), out.data_ptr(), n,
+             x._stream())
+        return ConcreteNDArray._wrap(out, Shape(x.shape().dimensions()[1:]), x.dtype(), _result_device(x))
+
     def wait(self, index: int, stream: int) -> None:
         call("j4c_comm_wait", self.comms[index], stream)
 
@@ -243,12 +266,28 @@ def all_gather_value(x: NDArray) -> NDArray:
     return ctx.collective.allGather(ctx.deviceIndex, x)
 
 
+# The ALL_GATHER VJP.  "slice" (default): the reference's rule
+# (Grad.java:437-441), the local slice of gOut with no communication.
+# "reduce_scatter": the transpose of all-gather -- every shard's gOut slice
+# for this shard, summed over shards -- which is what a loss that each shard
+# computes from the gathered value needs.
+ALLGATHER_VJP = os.environ.get("J4C_ALLGATHER_VJP", "slice")
+
+
+def set_all_gather_vjp(mode: str) -> None:
+    global ALLGATHER_VJP
+    if mode not in ("slice", "reduce_scatter"):
+        raise IllegalArgumentException(f"allGather VJP must be 'slice' or 'reduce_scatter', got {mode!r}")
+    ALLGATHER_VJP = mode
+
+
 def all_gather_vjp(g: ConcreteNDArray) -> ConcreteNDArray:
-    """ALL_GATHER VJP (Grad.java:437-441): the local slice of gOut, with no
-    communication -- the reference's rule, kept for parity."""
+    """ALL_GATHER VJP: see ALLGATHER_VJP."""
     ctx = PmapContext.current()
     if ctx is None:
         return g
+    if ALLGATHER_VJP == "reduce_scatter" and ctx.numDevices > 1:
+        return ctx.collective.reduceScatter(ctx.deviceIndex, g)
     return split(g, ctx.numDevices)[ctx.deviceIndex]
 
 

@@ -48,6 +48,26 @@ class CheckpointMeta:
     subJaxpr: "Jaxpr"
 
 
+@dataclass(frozen=True)
+class CondMeta:
+    """ir/CondMeta: the two branches of a COND, each one operand -> one result."""
+    trueBranch: "Jaxpr"
+    falseBranch: "Jaxpr"
+
+
+@dataclass(frozen=True)
+class WhileMeta:
+    """ir/WhileMeta: condition (state -> BOOL/number [1]) and body (state -> state)."""
+    condFn: "Jaxpr"
+    bodyFn: "Jaxpr"
+
+
+@dataclass(frozen=True)
+class ScanMeta:
+    """ir/ScanMeta: the step (carry, x_t) -> (new carry, y_t)."""
+    stepFn: "Jaxpr"
+
+
 @dataclass
 class Equation:
     inputs: List[Var]

@@ -185,3 +185,23 @@ def test_config2_pmap_dot_allgather_full_size(J):
         lhs = c[0, i].astype(np.float64) @ ones
         rhs = ah[i].astype(np.float64) @ b1
         assert_rel(lhs, rhs, TOL_REDUCTION, f"row-sum identity, shard {i}")
+
+
+@pytest.mark.parametrize("mode,factor", [("slice", 1.0), ("reduce_scatter", 2.0)])
+def test_all_gather_vjp_modes(J, mode, factor):
+    """L = sum over 2 shards of sum(allGather(x) * c): dL/dx = 2c.  The
+    reference's VJP (the local slice, Grad.java:437-441) gives c; the
+    reduce-scatter VJP gives the true 2c."""
+    from jax4j_b200 import pmap as P
+    c = np.float32([[1, 2, 3], [4, 5, 6]])
+    cc = J.ConcreteNDArray.of(c)
+    x = J.ConcreteNDArray.of(np.float32([[0.5, -1, 2], [3, 0.25, -4]]))
+    devices = [J.Device(None), J.Device(None)]
+    old = P.ALLGATHER_VJP
+    try:
+        J.Lax.setAllGatherVjp(mode)
+        fn = lambda v: J.JAX.pmap(lambda s: J.Lax.allGather(s, 2).mul(cc).sum(), devices)(v).sum()
+        g = J.JAX.grad(fn)(x).numpy()
+    finally:
+        P.ALLGATHER_VJP = old
+    np.testing.assert_allclose(g, factor * c, rtol=1e-6)

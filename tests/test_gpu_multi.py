@@ -37,6 +37,16 @@ def test_in_process_pmap_over_two_gpus():
     two = J.ConcreteNDArray.scalar(2.0)
     fn = lambda v: J.JAX.pmap(lambda s: J.Lax.psum(s.mul(s).sum()).div(two), devices)(v).sum()
     np.testing.assert_allclose(J.JAX.grad(fn)(x).toFloatArray(), [2, 4, 6, 8], atol=1e-3)
+    # the reduce-scatter ALL_GATHER VJP over NCCL (ncclReduceScatter)
+    from jax4j_b200 import pmap as P
+    c = J.ConcreteNDArray.of(np.float32([[1, 2], [3, 4]]))
+    old = P.ALLGATHER_VJP
+    try:
+        J.Lax.setAllGatherVjp("reduce_scatter")
+        fn = lambda v: J.JAX.pmap(lambda s: J.Lax.allGather(s, 2).mul(c).sum(), devices)(v).sum()
+        np.testing.assert_allclose(J.JAX.grad(fn)(x).toFloatArray(), [2, 4, 6, 8], atol=1e-5)
+    finally:
+        P.ALLGATHER_VJP = old
 
 
 def _torchrun(scenario, out, env_extra=None, timeout=240):
