@@ -34,6 +34,13 @@ class JAX:
         return _grad.make_jaxpr(fn, *args)
 
     @staticmethod
+    def jvp(fn: Callable, arg: NDArray, tangent: NDArray) -> List[NDArray]:
+        """JAX.jvp (JAX.java:62-66): forward mode; returns [primal out, tangent out]."""
+        jaxpr = _grad.make_jaxpr(fn, arg)
+        primals, tangents = _grad.forward_ad(jaxpr, [arg], [tangent])
+        return [primals[0], tangents[0]]
+
+    @staticmethod
     def grad(fn: Callable, argnum: int = None) -> Callable:
         """JAX.grad (JAX.java:279-289)."""
         return _grad.grad(fn, argnum)

@@ -176,6 +176,96 @@ def _run_equation(eq, values: Dict[int, NDArray]) -> None:
         values[eq.outputs[0].id] = execute_primitive(eq.primitive, eq, inputs)
 
 
+# ---- forward mode (Grad.forwardAd, Grad.java:668-835) -----------------------------------
+def forward_ad(jaxpr: Jaxpr, args: List[NDArray], tangents_in: List[NDArray]):
+    """Grad.forwardAd: primals and tangents pushed forward together; returns
+    (output primals, output tangents)."""
+    primals: Dict[int, NDArray] = dict(jaxpr.consts)
+    tangents: Dict[int, NDArray] = {k: zeros_like(v) for k, v in jaxpr.consts.items()}
+    for v, a, t in zip(jaxpr.inVars, args, tangents_in):
+        primals[v.id] = a
+        tangents[v.id] = t
+    for eq in jaxpr.equations:
+        ins = [primals[v.id] for v in eq.inputs]
+        tins = [tangents[v.id] for v in eq.inputs]
+        if eq.primitive == Primitive.SCAN:
+            c, ys, ct, yst = _scan_jvp(eq, ins, tins)
+            primals[eq.outputs[0].id], primals[eq.outputs[1].id] = c, ys
+            tangents[eq.outputs[0].id], tangents[eq.outputs[1].id] = ct, yst
+            continue
+        out = execute_primitive(eq.primitive, eq, ins)
+        primals[eq.outputs[0].id] = out
+        tangents[eq.outputs[0].id] = compute_jvp(eq.primitive, eq, out, ins, tins)
+    return [primals[v.id] for v in jaxpr.outVars], [tangents[v.id] for v in jaxpr.outVars]
+
+
+def _scan_jvp(eq, primals: List[NDArray], tangents: List[NDArray]):
+    """Grad.scanJVP (Grad.java:707-731)."""
+    m: ScanMeta = eq.metadata
+    carry, xs = primals
+    carry_t, xs_t = tangents
+    ys, ys_t = [], []
+    for t in range(xs.shape().dimensions()[0]):
+        (carry, y), (carry_t, y_t) = forward_ad(m.stepFn, [carry, slice_leading(xs, t)],
+                                                [carry_t, slice_leading(xs_t, t)])
+        ys.append(y)
+        ys_t.append(y_t)
+    return carry, stack_leading(ys), carry_t, stack_leading(ys_t)
+
+
+def compute_jvp(p: Primitive, eq, out: ConcreteNDArray, x: List[NDArray], t: List[NDArray]) -> NDArray:
+    """Grad.computeJVP (Grad.java:733-835), op for op."""
+    from . import pmap as _pm
+    dtype, shape, dev = out.dtype(), out.shape(), out.device()
+
+    def full(v):
+        return ConcreteNDArray.full(shape, v, dtype, dev)
+
+    if p == Primitive.ADD: return t[0].add(t[1])
+    if p == Primitive.SUB: return t[0].sub(t[1])
+    if p == Primitive.MUL: return t[0].mul(x[1]).add(x[0].mul(t[1]))
+    if p == Primitive.DIV:
+        b = x[1]
+        return t[0].mul(b).sub(x[0].mul(t[1])).div(b.mul(b))
+    if p == Primitive.MEAN: return t[0].mean()
+    if p == Primitive.SUM: return t[0].sum()
+    if p in (Primitive.SUM_AXIS, Primitive.MEAN_AXIS):
+        m: AxisMeta = eq.metadata
+        return t[0].sum(m.axis, m.keepDims) if p == Primitive.SUM_AXIS else t[0].mean(m.axis, m.keepDims)
+    if p == Primitive.EXP: return t[0].mul(out)
+    if p == Primitive.LOG: return t[0].div(x[0])
+    if p == Primitive.SIN: return t[0].mul(x[0].cos())
+    if p == Primitive.COS: return t[0].mul(x[0].sin()).mul(full(-1.0))
+    if p == Primitive.TANH: return t[0].mul(full(1.0).sub(out.mul(out)))
+    if p == Primitive.RELU:
+        zero = ConcreteNDArray.full(x[0].shape(), 0.0, x[0].dtype(), x[0].device())
+        return t[0].mul(x[0].gt(zero).astype(x[0].dtype()))
+    if p == Primitive.SIGMOID: return t[0].mul(out.mul(full(1.0).sub(out)))
+    if p == Primitive.DOT: return t[0].dot(x[1]).add(x[0].dot(t[1]))
+    if p == Primitive.COND:
+        m: CondMeta = eq.metadata
+        branch = m.trueBranch if is_true(x[0]) else m.falseBranch
+        return forward_ad(branch, [x[1]], [t[1]])[1][0]
+    if p == Primitive.WHILE:
+        raise UnsupportedOperationException("Lax.whileLoop is not forward-mode differentiable")
+    if p == Primitive.CAST: return t[0].astype(eq.metadata)
+    if p in (Primitive.GT, Primitive.GE, Primitive.LT, Primitive.LE, Primitive.EQ, Primitive.NE,
+             Primitive.ARGMAX, Primitive.ARGMIN):
+        return zeros(shape, dtype, dev)
+    if p == Primitive.CHECKPOINT:
+        m: CheckpointMeta = eq.metadata
+        return forward_ad(m.subJaxpr, [x[0]], [t[0]])[1][0]
+    if p == Primitive.PMAP:
+        # each shard's body pushed forward in turn, as the reference does (its
+        # collectives see no pmap context there, so they act as identities)
+        m: PmapMeta = eq.metadata
+        ps, ts = _pm.split(x[0], m.numDevices()), _pm.split(t[0], m.numDevices())
+        return _pm.stack([forward_ad(m.bodyJaxpr, [ps[i]], [ts[i]])[1][0] for i in range(m.numDevices())])
+    if p == Primitive.PSUM: return _pm.psum_value(t[0])
+    if p == Primitive.ALL_GATHER: return _pm.all_gather_value(t[0])
+    raise UnsupportedOperationException(f"No JVP rule defined for primitive: {p.name}")
+
+
 # ---- control flow (api/Lax.java:69-217, Grad.java:213-265) ----------------------------
 def is_true(pred: NDArray) -> bool:
     """Lax.isTrue (Lax.java:60-62): the first element, nonzero."""
