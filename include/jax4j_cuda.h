@@ -242,6 +242,18 @@ J4C_API int j4c_maxmin_grad(int is_max, int dtype, const void *g, const int64_t 
 J4C_API int j4c_transpose(int dtype, const void *in, int64_t rows, int64_t cols, void *out,
                   j4c_stream stream);
 
+/* Numpy.take (api/Numpy.java:54-76, primitive GATHER): out[p, :] =
+ * table[idx[p], :] for a [rows, dim] table and n INT32/INT64 indices (out is
+ * [n, dim]); an index outside [0, rows) yields a zero row (callers validate
+ * indices first, as the reference's array copy would throw).  Its VJP
+ * (Grad.gatherBackward, api/Grad.java:474-493): gtable (zeroed by the
+ * caller, [rows, dim]) += g rows scattered to their indices; repeated indices
+ * accumulate (atomic adds, so their order is unspecified). */
+J4C_API int j4c_gather_rows(int dtype, const void *table, int64_t rows, int64_t dim, int idx_dtype,
+                            const void *idx, int64_t n, void *out, j4c_stream stream);
+J4C_API int j4c_scatter_add_rows(int dtype, const void *g, int64_t rows, int64_t dim, int idx_dtype,
+                                 const void *idx, int64_t n, void *gtable, j4c_stream stream);
+
 /* ------------------------------------------------------------------ */
 /* dot                                                                  */
 /* ------------------------------------------------------------------ */

@@ -71,6 +71,8 @@ SIGNATURES = {
     "j4c_relu_grad": [I32, P, P, I64, P, P],
     "j4c_maxmin_grad": [I32, I32, P, PI64, I32, P, PI64, I32, P, PI64, I32, P, P, P],
     "j4c_transpose": [I32, P, I64, I64, P, P],
+    "j4c_gather_rows": [I32, P, I64, I64, I32, P, I64, P, P],
+    "j4c_scatter_add_rows": [I32, P, I64, I64, I32, P, I64, P, P],
     "j4c_dot": [I32, P, P, P, I64, I64, I64, I32, I32, P],
     "j4c_dot_ws": [I32, P, P, P, I64, I64, I64, I32, I32, P, C.c_size_t, P],
     "j4c_dot_workspace_size": [I32, I64, I64, I64],

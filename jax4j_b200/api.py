@@ -370,6 +370,20 @@ class Nn:
 
 class Numpy:
     @staticmethod
+    def take(table: NDArray, indices: NDArray) -> NDArray:
+        """Numpy.take (Numpy.java:54-66): embedding lookup, rows of a
+        [rows, dim] table -> [*indices.shape, dim]; a GATHER equation under a
+        trace (its VJP scatter-adds into the table)."""
+        if Tracer.current() is not None:
+            tracer = Tracer.current()
+            tv, iv = to_var(table), to_var(indices)
+            out = tracer.nextVar(Shape(indices.shape().dimensions() + (table.shape().dimensions()[1],)),
+                                 table.dtype())
+            tracer.addEquation(Equation([tv, iv], [out], Primitive.GATHER, None))
+            return TracedNDArray(out)
+        return _grad.take_eager(table, indices)
+
+    @staticmethod
     def where(cond: NDArray, x: NDArray, y: NDArray) -> NDArray:
         """Numpy.where: c*x + (1-c)*y with c = cond as FLOAT32 (an arithmetic
         blend, not a select, exactly as the reference computes it)."""

@@ -456,6 +456,37 @@ __global__ void __launch_bounds__(256) expand_kernel(Indexer ix, const T *__rest
     }
 }
 
+// ---- Numpy.take (GATHER) and its VJP -----------------------------------------------
+// out[p, :] = table[idx[p], :]; rows are copied 16 bytes at a time when aligned.
+// Indices outside [0, rows) write zeros (the host validates them first).
+template <typename T, typename I>
+__global__ void __launch_bounds__(256) gather_rows_kernel(const T *__restrict__ table, int64_t rows, int64_t dim,
+                                                          const I *__restrict__ idx, int64_t n,
+                                                          T *__restrict__ out) {
+    const int64_t total = n * dim;
+    for (int64_t e = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; e < total;
+         e += (int64_t)gridDim.x * blockDim.x) {
+        const int64_t p = e / dim, d = e - p * dim;
+        const int64_t r = (int64_t)idx[p];
+        out[e] = (r >= 0 && r < rows) ? table[r * dim + d] : T(0);
+    }
+}
+
+// gtable[idx[p], :] += g[p, :] (gtable zeroed by the caller); repeated
+// indices accumulate with atomic adds.
+template <typename T, typename I>
+__global__ void __launch_bounds__(256) scatter_add_rows_kernel(const T *__restrict__ g, int64_t rows, int64_t dim,
+                                                               const I *__restrict__ idx, int64_t n,
+                                                               T *__restrict__ gtable) {
+    const int64_t total = n * dim;
+    for (int64_t e = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; e < total;
+         e += (int64_t)gridDim.x * blockDim.x) {
+        const int64_t p = e / dim, d = e - p * dim;
+        const int64_t r = (int64_t)idx[p];
+        if (r >= 0 && r < rows) atomicAdd(gtable + r * dim + d, g[e]);
+    }
+}
+
 // ---- Random (api/Random.java:39-113) ----------------------------------------------
 __device__ __forceinline__ uint64_t mix64(uint64_t z) {
     z = (z ^ (z >> 30)) * 0xbf58476d1ce4e5b9ULL;
@@ -684,6 +715,61 @@ int j4c_transpose(int dtype, const void *in, int64_t rows, int64_t cols, void *o
     default: return set_error(J4C_E_INVALID, "j4c_transpose: bad dtype %d", dtype);
     }
     J4C_LAUNCH_CHECK("transpose_kernel");
+    return J4C_OK;
+}
+
+int j4c_gather_rows(int dtype, const void *table, int64_t rows, int64_t dim, int idx_dtype, const void *idx,
+                    int64_t n, void *out, j4c_stream stream) {
+    J4C_REQUIRE(rows >= 0 && dim >= 0 && n >= 0, "j4c_gather_rows: negative size");
+    if (n == 0 || dim == 0) return J4C_OK;
+    J4C_REQUIRE(table && idx && out, "j4c_gather_rows: NULL pointer");
+    J4C_REQUIRE(idx_dtype == J4C_INT32 || idx_dtype == J4C_INT64, "j4c_gather_rows: indices must be INT32 or INT64");
+    cudaStream_t s = as_stream(stream);
+    const unsigned g = grid_for(n * dim, 256);
+#define J4C_GATHER(T)                                                                                          \
+    if (idx_dtype == J4C_INT32)                                                                              \
+        gather_rows_kernel<T, int32_t><<<g, 256, 0, s>>>((const T *)table, rows, dim, (const int32_t *)idx, n, \
+                                                        (T *)out);                                            \
+    else                                                                                                       \
+        gather_rows_kernel<T, int64_t><<<g, 256, 0, s>>>((const T *)table, rows, dim, (const int64_t *)idx, n, \
+                                                        (T *)out);
+    switch (dtype_size(dtype)) {
+    case 4: J4C_GATHER(float) break;
+    case 8: J4C_GATHER(double) break;
+    case 1: J4C_GATHER(uint8_t) break;
+    default: return set_error(J4C_E_INVALID, "j4c_gather_rows: bad dtype %d", dtype);
+    }
+#undef J4C_GATHER
+    J4C_LAUNCH_CHECK("gather_rows_kernel");
+    return J4C_OK;
+}
+
+int j4c_scatter_add_rows(int dtype, const void *g, int64_t rows, int64_t dim, int idx_dtype, const void *idx,
+                         int64_t n, void *gtable, j4c_stream stream) {
+    J4C_REQUIRE(rows >= 0 && dim >= 0 && n >= 0, "j4c_scatter_add_rows: negative size");
+    if (n == 0 || dim == 0) return J4C_OK;
+    J4C_REQUIRE(g && idx && gtable, "j4c_scatter_add_rows: NULL pointer");
+    J4C_REQUIRE(idx_dtype == J4C_INT32 || idx_dtype == J4C_INT64,
+                "j4c_scatter_add_rows: indices must be INT32 or INT64");
+    J4C_REQUIRE(dtype == J4C_FLOAT32 || dtype == J4C_FLOAT64, "j4c_scatter_add_rows: dtype %s", dtype_name(dtype));
+    cudaStream_t s = as_stream(stream);
+    const unsigned gr = grid_for(n * dim, 256);
+    if (dtype == J4C_FLOAT32) {
+        if (idx_dtype == J4C_INT32)
+            scatter_add_rows_kernel<float, int32_t><<<gr, 256, 0, s>>>((const float *)g, rows, dim,
+                                                                       (const int32_t *)idx, n, (float *)gtable);
+        else
+            scatter_add_rows_kernel<float, int64_t><<<gr, 256, 0, s>>>((const float *)g, rows, dim,
+                                                                       (const int64_t *)idx, n, (float *)gtable);
+    } else {
+        if (idx_dtype == J4C_INT32)
+            scatter_add_rows_kernel<double, int32_t><<<gr, 256, 0, s>>>((const double *)g, rows, dim,
+                                                                        (const int32_t *)idx, n, (double *)gtable);
+        else
+            scatter_add_rows_kernel<double, int64_t><<<gr, 256, 0, s>>>((const double *)g, rows, dim,
+                                                                        (const int64_t *)idx, n, (double *)gtable);
+    }
+    J4C_LAUNCH_CHECK("scatter_add_rows_kernel");
     return J4C_OK;
 }
 

@@ -176,6 +176,38 @@ def _run_equation(eq, values: Dict[int, NDArray]) -> None:
         values[eq.outputs[0].id] = execute_primitive(eq.primitive, eq, inputs)
 
 
+# ---- Numpy.take (GATHER) ------------------------------------------------------------------
+def take_eager(table: ConcreteNDArray, indices: ConcreteNDArray) -> ConcreteNDArray:
+    """Numpy.takeEager (Numpy.java:68-76): rows of a [rows, dim] table at
+    integer indices -> [*indices.shape, dim]."""
+    td = table.shape().dimensions()
+    if len(td) != 2:
+        raise IllegalArgumentException(f"take: table must be [rows, dim], got {table.shape()}")
+    if indices.dtype() not in (DType.INT32, DType.INT64):
+        raise IllegalArgumentException(f"take: indices must be INT32 or INT64, got {indices.dtype()}")
+    rows, dim = td
+    n = indices.shape().size()
+    if n:
+        host = indices.numpy()
+        lo, hi = int(host.min()), int(host.max())
+        if lo < 0 or hi >= rows:
+            raise IllegalArgumentException(f"take: index {lo if lo < 0 else hi} out of range for {rows} rows")
+    import torch
+    out = torch.empty(n * dim, dtype=table.dtype().torch, device=table.tensor().device)
+    call("j4c_gather_rows", table.dtype().ordinal, table.data_ptr(), rows, dim, indices.dtype().ordinal,
+         indices.data_ptr(), n, out.data_ptr(), table._stream())
+    return ConcreteNDArray._wrap(out, Shape(indices.shape().dimensions() + (dim,)), table.dtype(), table.device())
+
+
+def gather_backward(g: ConcreteNDArray, table_shape: Shape, indices: ConcreteNDArray) -> ConcreteNDArray:
+    """Grad.gatherBackward (Grad.java:474-493): scatter-add of g's rows."""
+    rows, dim = table_shape.dimensions()
+    out = zeros(table_shape, g.dtype(), g.device())
+    call("j4c_scatter_add_rows", g.dtype().ordinal, g.data_ptr(), rows, dim, indices.dtype().ordinal,
+         indices.data_ptr(), indices.shape().size(), out.data_ptr(), g._stream())
+    return out
+
+
 # ---- forward mode (Grad.forwardAd, Grad.java:668-835) -----------------------------------
 def forward_ad(jaxpr: Jaxpr, args: List[NDArray], tangents_in: List[NDArray]):
     """Grad.forwardAd: primals and tangents pushed forward together; returns
@@ -249,6 +281,7 @@ def compute_jvp(p: Primitive, eq, out: ConcreteNDArray, x: List[NDArray], t: Lis
     if p == Primitive.WHILE:
         raise UnsupportedOperationException("Lax.whileLoop is not forward-mode differentiable")
     if p == Primitive.CAST: return t[0].astype(eq.metadata)
+    if p == Primitive.GATHER: return take_eager(t[0], x[1])
     if p in (Primitive.GT, Primitive.GE, Primitive.LT, Primitive.LE, Primitive.EQ, Primitive.NE,
              Primitive.ARGMAX, Primitive.ARGMIN):
         return zeros(shape, dtype, dev)
@@ -450,6 +483,8 @@ def execute_primitive(p: Primitive, eq, inputs: List[NDArray]) -> NDArray:
         m = eq.metadata
         return inputs[0].argmax(m.axis) if p == Primitive.ARGMAX else inputs[0].argmin(m.axis)
     if p == Primitive.CAST: return inputs[0].astype(eq.metadata)
+    if p == Primitive.GATHER:
+        return take_eager(inputs[0], inputs[1])
     if p == Primitive.COND:
         m: CondMeta = eq.metadata
         return forward_interpret(m.trueBranch if is_true(inputs[0]) else m.falseBranch, [inputs[1]])[0]
@@ -543,6 +578,10 @@ def compute_vjps(p: Primitive, eq, g: ConcreteNDArray, inputs: List[NDArray], ou
         return maxmin_grad(g, inputs[0], inputs[1], False)
     if p in (Primitive.ARGMAX, Primitive.ARGMIN):
         return [_zeros_for(eq.inputs[0], g)]
+    if p == Primitive.GATHER:
+        # embedding backward: scatter-add into a table-shaped zero gradient
+        return [gather_backward(g, shapes[0], inputs[1]) if want_a else None,
+                _zeros_for(eq.inputs[1], g) if want_b else None]
     if p == Primitive.COND:
         # pred is not differentiable (Grad.java:391-397)
         m: CondMeta = eq.metadata

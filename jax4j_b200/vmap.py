@@ -146,6 +146,10 @@ def _rule(eq, inputs: List[NDArray], batched: List[bool], batch: int) -> NDArray
         axis = m.axis + 1 if batched[0] else m.axis
         return inputs[0].argmax(axis) if p == P.ARGMAX else inputs[0].argmin(axis)
     if p == P.CAST: return inputs[0].astype(m)
+    if p == P.GATHER:
+        # batched indices already carry the batch axis in their shape
+        from .grad import take_eager
+        return take_eager(inputs[0], inputs[1])
     if p == P.CHECKPOINT:
         # the rematerialisation hint is a no-op under vmap: batch the body inline
         return run(m.subJaxpr, [inputs[0]], [batched[0]], batch)

@@ -144,3 +144,55 @@ def test_strided_batched_gemm_one_launch(J, a_b, b_b, B, M, K, N):
     o = out.numpy()
     for i in range(B):
         assert_rel(o[i], orc.dot(A[i] if a_b else A, W[i] if b_b else W), TOL_REDUCTION, f"example {i}")
+
+
+def _ints(J, v, shape):
+    return J.ConcreteNDArray.of(np.asarray(v, np.int32).reshape(shape), dtype=J.DType.INT32)
+
+
+def test_take_looks_up_rows(J):  # DTypeTest.java:172-181
+    table = arr(J, [10, 11, 20, 21, 30, 31, 40, 41], (4, 2))
+    out = J.Numpy.take(table, _ints(J, [2, 0, 3], (3,)))
+    assert out.shape().dimensions() == (3, 2)
+    np.testing.assert_allclose(out.toFloatArray(), [30, 31, 10, 11, 40, 41], atol=1e-6)
+
+
+def test_take_multi_dim_indices(J):  # DTypeTest.java:183-191
+    out = J.Numpy.take(arr(J, [1, 1, 2, 2, 3, 3], (3, 2)), _ints(J, [0, 1, 2, 0], (2, 2)))
+    assert out.shape().dimensions() == (2, 2, 2)
+    np.testing.assert_allclose(out.toFloatArray(), [1, 1, 2, 2, 3, 3, 1, 1], atol=1e-6)
+
+
+def test_take_gradient_scatter_adds(J):  # DTypeTest.java:193-204
+    idx = _ints(J, [0, 0, 1], (3,))
+    g = J.JAX.grad(lambda t: J.Numpy.take(t, idx).sum())(arr(J, [0, 0, 0], (3, 1)))
+    np.testing.assert_allclose(g.toFloatArray(), [2, 1, 0], atol=1e-6)
+
+
+def test_take_composes_with_vmap(J):  # DTypeTest.java:206-214
+    table = arr(J, [1, 2, 3, 4], (2, 2))
+    out = J.JAX.vmap(lambda idx: J.Numpy.take(table, idx))(_ints(J, [0, 1], (2, 1)))
+    assert out.shape().dimensions() == (2, 1, 2)
+    np.testing.assert_allclose(out.toFloatArray(), [1, 2, 3, 4], atol=1e-6)
+
+
+def test_take_embedding_bag_grad_at_size(J):
+    """A 50k x 64 embedding table, 20k lookups with many repeats: forward rows
+    exact, gradient equal to numpy's scatter-add (within the reduction
+    tolerance: repeated rows accumulate in an unspecified order)."""
+    r = np.random.default_rng(2)
+    T = r.standard_normal((50000, 64)).astype(np.float32)
+    I = r.integers(0, 50000, 20000).astype(np.int64)
+    I[:5000] = r.integers(0, 100, 5000)
+    table, idx = J.ConcreteNDArray.of(T), J.ConcreteNDArray.of(I, dtype=J.DType.INT64)
+    np.testing.assert_array_equal(J.Numpy.take(table, idx).numpy(), T[I])
+    w = J.ConcreteNDArray.of(r.standard_normal((20000, 64)).astype(np.float32))
+    g = J.JAX.grad(lambda t: J.Numpy.take(t, idx).mul(w).sum())(table).numpy()
+    ref = np.zeros_like(T, dtype=np.float64)
+    np.add.at(ref, I, w.numpy().astype(np.float64))
+    assert_rel(g, ref.astype(np.float32), TOL_REDUCTION)
+
+
+def test_take_rejects_out_of_range(J):
+    with pytest.raises(J.IllegalArgumentException):
+        J.Numpy.take(arr(J, [1, 2, 3, 4], (2, 2)), _ints(J, [0, 2], (2,)))
