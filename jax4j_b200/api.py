@@ -9,7 +9,8 @@ the extra argument (pmap of several sharded inputs, grad with argnum).
 from __future__ import annotations
 
 import math
-from typing import Callable, List, Sequence
+import os
+from typing import Callable, List, Optional, Sequence
 
 import numpy as np
 import torch
@@ -324,9 +325,12 @@ class Lax:
 
     @staticmethod
     def psumTree(tree: PyTree) -> PyTree:
-        """PyTrees.map(Lax::psum, tree) as ONE all-reduce: the leaves are packed
-        into a single buffer (one NCCL call instead of one per leaf); every
-        element's sum is the same as leaf-by-leaf psum."""
+        """PyTrees.map(Lax::psum, tree) with few collectives: over NCCL the
+        leaves go in buckets of ~J4C_PSUM_BUCKET_MB, each all-reduced on a side
+        stream as soon as the backward pass has produced its gradients
+        (overlapping communication with the rest of the backward); shards
+        sharing a GPU pack every leaf into one slot sum.  Each element's sum is
+        the same as a leaf-by-leaf psum."""
         ctx = _pm.PmapContext.current()
         leaves = PyTrees.flatten(tree)
         if ctx is None or Tracer.current() is not None or not leaves:
@@ -336,6 +340,8 @@ class Lax:
         first = leaves[0]
         if any(l.dtype() != first.dtype() or l.tensor().device != first.tensor().device for l in leaves):
             return PyTrees.map(Lax.psum, tree)
+        if isinstance(ctx.collective, _pm.NcclCollective) and PSUM_BUCKET_BYTES > 0:
+            return PyTrees.unflatten(tree, _psum_overlapped(ctx, leaves))
         total = sum(l.shape().size() for l in leaves)
         flat = torch.empty(total, dtype=first.dtype().torch, device=first.tensor().device)
         s = first._stream()
@@ -354,6 +360,68 @@ class Lax:
                                              summed.device()))
             off += n
         return PyTrees.unflatten(tree, out)
+
+
+# Gradient all-reduce overlapped with the backward pass.  The backward records
+# a CUDA event on each gradient when it is complete; psumTree groups the leaves
+# into buckets (last leaves first, the order the backward completes them) and
+# all-reduces each bucket on a side stream as soon as its gradients exist, so
+# the NCCL traffic of the last layers runs while the first layers' backward is
+# still computing.  J4C_PSUM_BUCKET_MB=0 restores the single packed all-reduce.
+PSUM_BUCKET_BYTES = int(float(os.environ.get("J4C_PSUM_BUCKET_MB", "32")) * (1 << 20))
+_comm_streams = {}
+
+
+def _comm_stream(device) -> "torch.cuda.Stream":
+    s = _comm_streams.get(device)
+    if s is None:
+        s = _comm_streams[device] = torch.cuda.Stream(device=device)
+    return s
+
+
+def _psum_overlapped(ctx, leaves: List[ConcreteNDArray]) -> List[ConcreteNDArray]:
+    dev = leaves[0].tensor().device
+    dt = leaves[0].dtype()
+    es = dt.byteSize()
+    compute = torch.cuda.current_stream(dev)
+    comm = _comm_stream(dev)
+    capturing = torch.cuda.is_current_stream_capturing()
+    # buckets of consecutive leaves, walked from the last leaf (ready first)
+    buckets, cur, size = [], [], 0
+    for i in reversed(range(len(leaves))):
+        cur.append(i)
+        size += leaves[i].shape().size() * es
+        if size >= PSUM_BUCKET_BYTES:
+            buckets.append(cur)
+            cur, size = [], 0
+    if cur:
+        buckets.append(cur)
+    out: List[Optional[ConcreteNDArray]] = [None] * len(leaves)
+    done = []
+    entry = torch.cuda.Event()
+    entry.record(compute)  # work before psumTree (for leaves without a ready event)
+    for b in buckets:
+        with torch.cuda.stream(comm):
+            for i in b:
+                comm.wait_event(leaves[i]._ready if leaves[i]._ready is not None else entry)
+            total = sum(leaves[i].shape().size() for i in b)
+            buf = torch.empty(total, dtype=dt.torch, device=dev)  # allocated on the side stream
+            off = 0
+            for i in b:
+                n = leaves[i].shape().size()
+                call("j4c_memcpy_d2d", buf.data_ptr() + off * es, leaves[i].data_ptr(), n * es, comm.cuda_stream)
+                out[i] = ConcreteNDArray._wrap(buf[off:off + n], leaves[i].shape(), dt, _pm._result_device(leaves[i]))
+                off += n
+            call("j4c_psum", ctx.collective.comms[ctx.deviceIndex], dt.ordinal, buf.data_ptr(), buf.data_ptr(),
+                 total, comm.cuda_stream)
+            ev = torch.cuda.Event()
+            ev.record(comm)
+            done.append(ev)
+        if not capturing:
+            buf.record_stream(compute)  # read on the compute stream after the wait below
+    for ev in done:
+        compute.wait_event(ev)
+    return out
 
 
 # ---------------------------------------------------------------------------

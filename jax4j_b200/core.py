@@ -379,7 +379,7 @@ class ConcreteNDArray(NDArray):
     it has been a dot operand, for the other dots it takes part in.
     """
 
-    __slots__ = ("_t", "_shape", "_dtype", "_device", "_split", "_split_t")
+    __slots__ = ("_t", "_shape", "_dtype", "_device", "_split", "_split_t", "_ready")
 
     def __init__(self, data, shape=None, dtype: DType = None, device: Device = None):
         if device is None:
@@ -415,6 +415,7 @@ class ConcreteNDArray(NDArray):
         self._device = device
         self._split = None
         self._split_t = None
+        self._ready = None  # CUDA event recorded once the value was produced, when tracked
 
     # ---- construction helpers ----
     @staticmethod
@@ -445,6 +446,7 @@ class ConcreteNDArray(NDArray):
         obj._device = device
         obj._split = None
         obj._split_t = None
+        obj._ready = None
         return obj
 
     def _new(self, shape: Shape, dtype: DType) -> torch.Tensor:

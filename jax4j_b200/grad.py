@@ -406,44 +406,69 @@ def do_backward(jaxpr: Jaxpr, values: Dict[int, NDArray], seeds: List[NDArray]) 
     grads: Dict[int, NDArray] = {}
     for v, s in zip(jaxpr.outVars, seeds):
         _merge(grads, v.id, s)
-    for eq in reversed(jaxpr.equations):
-        if eq.primitive == Primitive.SCAN:
-            g_c, g_y = grads.get(eq.outputs[0].id), grads.get(eq.outputs[1].id)
-            if (g_c is None and g_y is None) or not any(v.id in need for v in eq.inputs):
-                continue
-            gi = scan_backward(eq, [values.get(v.id) for v in eq.inputs], g_c, g_y)
-            for v, g in zip(eq.inputs, gi):
-                if v.id in need:
-                    _merge(grads, v.id, g)
-            continue
-        g_out = grads.get(eq.outputs[0].id)
-        if g_out is None:
-            continue
-        wanted = [v.id in need for v in eq.inputs]
-        if not any(wanted):
-            continue
-        z = fused_relu.get(id(eq))
-        if z is not None and wanted[0]:
-            a, b = values.get(eq.inputs[0].id), values.get(eq.inputs[1].id)
-            zv = values.get(z.id)
-            if (isinstance(g_out, ConcreteNDArray) and isinstance(b, ConcreteNDArray) and
-                    isinstance(zv, ConcreteNDArray) and g_out.dtype() == b.dtype() == zv.dtype() == DType.FLOAT32):
-                # dz = (g . W^T) masked by z > 0 in one GEMM; dW as usual
-                _merge(grads, z.id, _dot_raw(g_out, b, False, True, g_out.device(), mask=zv))
-                if wanted[1]:
-                    _merge(grads, eq.inputs[1].id, _dot_raw(a, g_out, True, False, g_out.device()))
-                continue
-        inputs = [values.get(v.id) for v in eq.inputs]
-        out_value = values.get(eq.outputs[0].id)
-        g_ins = compute_vjps(eq.primitive, eq, g_out, inputs, out_value, wanted)
-        for v, w, g in zip(eq.inputs, wanted, g_ins):
-            if w and g is not None:
-                _merge(grads, v.id, g)
+    # The equation after which each input's cotangent is complete (its first
+    # consumer): there a CUDA event is recorded on the gradient, so a
+    # collective over it (Lax.psumTree) can start while the rest of the
+    # backward pass still runs.
+    in_ids = {v.id for v in jaxpr.inVars}
+    last_use = {}
+    for i, e in enumerate(jaxpr.equations):
+        for v in e.inputs:
+            if v.id in in_ids and v.id not in last_use:
+                last_use[v.id] = i
+    done_at: Dict[int, list] = {}
+    for vid, i in last_use.items():
+        done_at.setdefault(i, []).append(vid)
+    for i_eq, eq in reversed(list(enumerate(jaxpr.equations))):
+        _process_backward_eq(eq, values, grads, need, fused_relu)
+        for vid in done_at.get(i_eq, ()):
+            g = grads.get(vid)
+            if isinstance(g, ConcreteNDArray) and g.tensor().is_cuda:
+                import torch
+                ev = torch.cuda.Event()
+                ev.record(torch.cuda.current_stream(g.tensor().device))
+                g._ready = ev
     result = []
     for v in jaxpr.inVars:
         g = grads.get(v.id)
         result.append(g if g is not None else zeros(v.shape, v.dtype, _device_of(values.get(v.id))))
     return result
+
+
+def _process_backward_eq(eq, values, grads, need, fused_relu) -> None:
+    """One equation of Grad.doBackward's reverse walk (Grad.java:162-185)."""
+    if eq.primitive == Primitive.SCAN:
+        g_c, g_y = grads.get(eq.outputs[0].id), grads.get(eq.outputs[1].id)
+        if (g_c is None and g_y is None) or not any(v.id in need for v in eq.inputs):
+            return
+        gi = scan_backward(eq, [values.get(v.id) for v in eq.inputs], g_c, g_y)
+        for v, g in zip(eq.inputs, gi):
+            if v.id in need:
+                _merge(grads, v.id, g)
+        return
+    g_out = grads.get(eq.outputs[0].id)
+    if g_out is None:
+        return
+    wanted = [v.id in need for v in eq.inputs]
+    if not any(wanted):
+        return
+    z = fused_relu.get(id(eq))
+    if z is not None and wanted[0]:
+        a, b = values.get(eq.inputs[0].id), values.get(eq.inputs[1].id)
+        zv = values.get(z.id)
+        if (isinstance(g_out, ConcreteNDArray) and isinstance(b, ConcreteNDArray) and
+                isinstance(zv, ConcreteNDArray) and g_out.dtype() == b.dtype() == zv.dtype() == DType.FLOAT32):
+            # dz = (g . W^T) masked by z > 0 in one GEMM; dW as usual
+            _merge(grads, z.id, _dot_raw(g_out, b, False, True, g_out.device(), mask=zv))
+            if wanted[1]:
+                _merge(grads, eq.inputs[1].id, _dot_raw(a, g_out, True, False, g_out.device()))
+            return
+    inputs = [values.get(v.id) for v in eq.inputs]
+    out_value = values.get(eq.outputs[0].id)
+    g_ins = compute_vjps(eq.primitive, eq, g_out, inputs, out_value, wanted)
+    for v, w, g in zip(eq.inputs, wanted, g_ins):
+        if w and g is not None:
+            _merge(grads, v.id, g)
 
 
 def _device_of(x):
