@@ -378,6 +378,10 @@ J4C_API int j4c_fused_launch(void *handle, int64_t rows, int64_t cols, const voi
 
 /* Random.uniform (api/Random.java:86-93): out[i] = lo + u(offset+i)*(hi-lo)
  * in float.  offset lets each shard generate its slice of one global array. */
+/* Random.permutation (api/Random.java:130-140): a permutation of 0..n-1 as
+ * INT32, the reference's Fisher-Yates over the key's uniform stream
+ * (bit-identical; the swaps run sequentially on one GPU thread). */
+J4C_API int j4c_random_permutation(uint64_t key, int64_t n, int32_t *out, j4c_stream stream);
 J4C_API int j4c_random_uniform(uint64_t key, int64_t offset, int64_t n, float lo, float hi, float *out,
                        j4c_stream stream);
 /* Random.normal (api/Random.java:104-113): Box-Muller in double. */

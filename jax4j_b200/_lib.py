@@ -85,6 +85,7 @@ SIGNATURES = {
     "j4c_fused_compile": [P, C.POINTER(P)],
     "j4c_fused_source": [P, I32, P, C.c_size_t, C.POINTER(C.c_size_t)],
     "j4c_fused_launch": [P, I64, I64, C.POINTER(P), C.POINTER(P), C.POINTER(P), P],
+    "j4c_random_permutation": [C.c_uint64, I64, P, P],
     "j4c_random_uniform": [C.c_uint64, I64, I64, C.c_float, C.c_float, P, P],
     "j4c_random_normal": [C.c_uint64, I64, I64, P, P],
     "j4c_comm_unique_id": [P, C.c_size_t],

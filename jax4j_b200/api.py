@@ -436,6 +436,19 @@ class Nn:
         return e.div(e.sum(-1, True))
 
 
+def _dropout(x: NDArray, key: PRNGKey, rate: float, training: bool) -> NDArray:
+    """Nn.dropout (Nn.java:42-47): keep with probability 1 - rate, rescale by
+    1 / (1 - rate); a pass-through when not training."""
+    if not training:
+        return x
+    p = float(np.float32(1.0) - np.float32(rate))  # 1f - rate in float, as the reference
+    keep = Random.bernoulli(key, p, x.shape()).astype(DType.FLOAT32)
+    return x.mul(keep).div(ConcreteNDArray.scalar(p))
+
+
+Nn.dropout = staticmethod(_dropout)
+
+
 class Numpy:
     @staticmethod
     def take(table: NDArray, indices: NDArray) -> NDArray:
@@ -517,6 +530,21 @@ class Random:
         """Random.bernoulli (Random.java:116-123): uniform < p."""
         u = Random.uniform(key, shape, 0.0, 1.0, device)
         return u.lt(ConcreteNDArray.scalar(float(np.float32(p)), DType.FLOAT32, u.device()))
+
+    @staticmethod
+    def permutation(key: PRNGKey, n: int, device: Device = None) -> ConcreteNDArray:
+        """Random.permutation (Random.java:130-140): INT32 permutation of 0..n-1."""
+        device = device or Device.defaultDevice()
+        t = torch.empty(max(n, 1), dtype=torch.int32, device=device.torch_device())
+        call("j4c_random_permutation", key.state(), n, t.data_ptr(), stream_of(device.ordinal()))
+        return ConcreteNDArray._wrap(t[:n], Shape(n), DType.INT32, device)
+
+    @staticmethod
+    def heNormal(key: PRNGKey, shape, fanIn: int, device: Device = None) -> ConcreteNDArray:
+        """Random.heNormal (Random.java:153-157): N(0, 1) * sqrt(2 / fanIn)."""
+        std = float(np.float32(math.sqrt(2.0 / fanIn)))
+        x = Random.normal(key, shape, device)
+        return x.mul(ConcreteNDArray.scalar(std, DType.FLOAT32, x.device()))
 
     @staticmethod
     def glorotUniform(key: PRNGKey, shape, fanIn: int, fanOut: int, device: Device = None,

@@ -522,6 +522,25 @@ __global__ void normal_kernel(uint64_t key, int64_t offset, int64_t n, float *ou
     }
 }
 
+// Random.permutation (Random.java:130-140): Fisher-Yates from the top, swap
+// index j = min((int)(u_i * (i + 1)), i) with u_i the i-th uniform draw.  The
+// swaps are sequential, so one thread performs them after a parallel fill.
+__global__ void iota_kernel(int32_t *out, int64_t n) {
+    for (int64_t i = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; i < n; i += (int64_t)gridDim.x * blockDim.x)
+        out[i] = (int32_t)i;
+}
+
+__global__ void fisher_yates_kernel(uint64_t key, int64_t n, int32_t *out) {
+    for (int64_t i = n - 1; i > 0; i--) {
+        const float u = raw_uniform01(key, (uint64_t)i);
+        int64_t j = (int64_t)(int32_t)__fmul_rn(u, (float)(i + 1));  // Java: (int) (u * (i + 1)), float product
+        if (j > i) j = i;
+        const int32_t t = out[i];
+        out[i] = out[j];
+        out[j] = t;
+    }
+}
+
 // ---- in-process psum over slots (api/SharedCollective.java:44-54) -----------------
 struct SlotPtrs {
     const void *p[16];
@@ -770,6 +789,18 @@ int j4c_scatter_add_rows(int dtype, const void *g, int64_t rows, int64_t dim, in
                                                                         (const int64_t *)idx, n, (double *)gtable);
     }
     J4C_LAUNCH_CHECK("scatter_add_rows_kernel");
+    return J4C_OK;
+}
+
+int j4c_random_permutation(uint64_t key, int64_t n, int32_t *out, j4c_stream stream) {
+    J4C_REQUIRE(n >= 0 && n < (1ll << 31), "j4c_random_permutation: n out of range");
+    if (n == 0) return J4C_OK;
+    J4C_REQUIRE(out, "j4c_random_permutation: NULL pointer");
+    cudaStream_t s = as_stream(stream);
+    iota_kernel<<<grid_for(n, 256), 256, 0, s>>>(out, n);
+    J4C_LAUNCH_CHECK("iota_kernel");
+    fisher_yates_kernel<<<1, 1, 0, s>>>(key, n, out);
+    J4C_LAUNCH_CHECK("fisher_yates_kernel");
     return J4C_OK;
 }
 

@@ -50,6 +50,7 @@ def _declare(L):
     L.orc_mix64.argtypes = [C.c_uint64]
     L.orc_split.argtypes = [C.c_uint64, C.c_int, P]
     L.orc_uniform.argtypes = [C.c_uint64, CI64, C.c_float, C.c_float, P]
+    L.orc_permutation.argtypes = [C.c_uint64, CI64, P]
     L.orc_normal.argtypes = [C.c_uint64, CI64, P]
     L.orc_glorot_uniform.argtypes = [C.c_uint64, CI64, C.c_int, C.c_int, P]
     L.orc_broadcast_index.restype = CI64
@@ -115,6 +116,13 @@ def uniform(state: int, shape, lo=0.0, hi=1.0):
     out = np.empty(n, dtype=np.float32)
     lib().orc_uniform(state & 0xFFFFFFFFFFFFFFFF, n, lo, hi, _p(out))
     return out.reshape(shape)
+
+
+def permutation(state: int, n: int):
+    """Random.permutation (Random.java:130-140)."""
+    out = np.empty(max(n, 1), dtype=np.int32)
+    lib().orc_permutation(state & 0xFFFFFFFFFFFFFFFF, n, _p(out))
+    return out[:n]
 
 
 def normal(state: int, shape):

@@ -50,6 +50,20 @@ void orc_split(uint64_t state, int num, uint64_t *out) {
 }
 
 /* api/Random.java:86-93: lo + u * (hi - lo), each step rounded to float */
+/* Random.permutation (api/Random.java:130-140): Fisher-Yates from the top. */
+void orc_permutation(uint64_t state, int64_t n, int32_t *out) {
+    for (int64_t i = 0; i < n; i++) out[i] = (int32_t)i;
+    for (int64_t i = n - 1; i > 0; i--) {
+        float u = raw_uniform01(state, (uint64_t)i);
+        float prod = u * (float)(i + 1);
+        int64_t j = (int64_t)(int32_t)prod;
+        if (j > i) j = i;
+        int32_t t = out[i];
+        out[i] = out[j];
+        out[j] = t;
+    }
+}
+
 void orc_uniform(uint64_t state, int64_t n, float lo, float hi, float *out) {
     float span = hi - lo;
     for (int64_t i = 0; i < n; i++) {

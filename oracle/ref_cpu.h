@@ -48,6 +48,7 @@ enum { ORC_F32 = 0, ORC_F64 = 1, ORC_I32 = 2, ORC_I64 = 3, ORC_BOOL = 4 };
 uint64_t orc_mix64(uint64_t z);
 void orc_split(uint64_t state, int num, uint64_t *out);
 void orc_uniform(uint64_t state, int64_t n, float lo, float hi, float *out);
+void orc_permutation(uint64_t state, int64_t n, int32_t *out);
 void orc_normal(uint64_t state, int64_t n, float *out);
 void orc_glorot_uniform(uint64_t state, int64_t n, int fan_in, int fan_out, float *out);
 

@@ -414,3 +414,26 @@ def test_mlp_grads_with_gemm_epilogues_equal_the_unfused_interpreter(J):
     np.testing.assert_array_equal(v1.numpy(), v0.numpy())
     for k in names:
         np.testing.assert_array_equal(g1.children[k].value.numpy(), g0.children[k].value.numpy())
+
+
+@pytest.mark.parametrize("n", [1, 2, 17, 1000, 100000])
+def test_random_permutation_bit_exact(J, n):
+    from oracle import oracle as orc
+    key = J.Random.split(J.PRNGKey.key(42), 3)[1]
+    got = J.Random.permutation(key, n)
+    assert got.dtype() == J.DType.INT32
+    np.testing.assert_array_equal(got.numpy(), orc.permutation(key.state(), n))
+
+
+def test_he_normal_and_dropout(J):
+    from oracle import oracle as orc
+    key = J.PRNGKey.key(3)
+    h = J.Random.heNormal(key, J.Shape(64, 32), 64).numpy()
+    std = np.float32(np.sqrt(2.0 / 64))
+    assert_rel(h, (orc.normal(key.state(), (64, 32)).astype(np.float64) * std).astype(np.float32), TOL_ELEMENTWISE)
+    x = J.ConcreteNDArray.of(np.arange(1, 2049, dtype=np.float32).reshape(32, 64))
+    d = J.Nn.dropout(x, key, 0.25, True).numpy()
+    keep = orc.uniform(key.state(), (32, 64)) < np.float32(0.75)
+    ref = (x.numpy() * keep.astype(np.float32)).astype(np.float64) / np.float64(np.float32(0.75))
+    np.testing.assert_array_equal(d, ref.astype(np.float32))
+    np.testing.assert_array_equal(J.Nn.dropout(x, key, 0.25, False).numpy(), x.numpy())

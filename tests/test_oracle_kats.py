@@ -201,3 +201,13 @@ def test_oracle_sweep_matches_composed_ops():
     assert np.array_equal(z, zz)
     assert np.array_equal(s, o.reduce_axis(o.SUM_AXIS, zz, -1, True))
     assert np.array_equal(am, o.argreduce(o.ARGMAX, zz, -1))
+
+
+def test_oracle_permutation_is_a_permutation():
+    """Random.permutation (Random.java:130-140) restated: a permutation of 0..n-1,
+    deterministic per key, different across keys."""
+    from oracle import oracle as orc
+    p = orc.permutation(orc.split(7)[0], 1000)
+    assert sorted(p.tolist()) == list(range(1000))
+    assert np.array_equal(p, orc.permutation(orc.split(7)[0], 1000))
+    assert not np.array_equal(p, orc.permutation(orc.split(8)[0], 1000))
