@@ -83,16 +83,28 @@ class ClockSampler:
         self.index = index
         self.proc = None
         self.file = None
+        self.skip = 0
 
     def start(self):
         try:
             self.file = tempfile.NamedTemporaryFile("w+", suffix=".csv", delete=False)
             self.proc = subprocess.Popen(
                 ["nvidia-smi", f"--id={self.index}", f"--query-gpu={self.QUERY}",
-                 "--format=csv,noheader,nounits", "-lms", "200"],
+                 "--format=csv,noheader,nounits", "-lms", "20"],
                 stdout=self.file, stderr=subprocess.DEVNULL)
         except OSError:
             self.proc = None
+            return
+        # wait for the first sample, then count only the samples taken from here on
+        deadline = time.time() + 3.0
+        while time.time() < deadline and self.proc.poll() is None:
+            self.file.flush()
+            with open(self.file.name) as f:
+                n = sum(1 for l in f if l.strip())
+            if n:
+                self.skip = n
+                break
+            time.sleep(0.02)
 
     def stop(self) -> dict:
         if self.proc is None:
@@ -104,7 +116,7 @@ class ClockSampler:
             self.proc.kill()
         self.file.flush()
         with open(self.file.name) as f:
-            rows = [l.strip().split(", ") for l in f if l.strip()]
+            rows = [l.strip().split(", ") for l in f if l.strip()][self.skip:]
         os.unlink(self.file.name)
         sm, smax, reasons = [], None, set()
         names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
@@ -237,8 +249,9 @@ def run_ours(args):
     dots = core.DOT_TIMING
     core.DOT_TIMING = None
     eager_ms = max_over_ranks(eager_ms_local)
-    dot_ms = sum(a.elapsed_time(b) for a, b, _ in dots)
-    dot_flop = sum(f for _, _, f in dots)
+    dot_ms = sum(a.elapsed_time(b) for a, b, _, _ in dots)
+    dot_flop = sum(f for _, _, f, _ in dots)
+    dot_bytes_per_launch = sum(n for _, _, _, n in dots) / len(dots) if dots else None
 
     # ---- the same step recorded once as a CUDA graph and replayed ----
     graphs, graph_note, per_replay = [], None, None
@@ -267,7 +280,6 @@ def run_ours(args):
     # ---- device-timed region (inputs resident in HBM) ----
     clocks = ClockSampler(ordinal)
     clocks.start()
-    time.sleep(0.3)
     sync_all()
     ev0.record()
     for _ in range(args.steps):
@@ -371,7 +383,7 @@ def run_ours(args):
             distributed.shutdown()
         return
     peaks = _measured_peaks()
-    peak = peaks.get("bf16_tflops_sustained") or peaks.get("bf16_tflops")
+    peak, peak_source = _tensor_peak(peaks, clk)
     achieved = (dot_flop / (dot_ms / 1e3)) / 1e12 if dot_ms > 0 else None
     line = {
         "metric": METRIC, "value": value, "unit": "samples/s", "n_gpus": D, "steps": args.steps,
@@ -384,9 +396,17 @@ def run_ours(args):
         "roofline": {"bound": "tensor", "kernel": "dot (FP32 via 3xTF32 split)",
                      "achieved": achieved, "peak": peak, "unit": "TFLOP/s",
                      "frac": (achieved / peak) if (achieved and peak) else None,
-                     "peak_source": "MEASURED_PEAKS.json bf16 (sustained); TF32 dense rate is half of bf16",
+                     "peak_source": peak_source,
                      "dot_share_of_step": dot_ms / eager_ms_local if eager_ms_local else None,
-                     "traffic": None},
+                     # the three TF32 products each FP32 product issues, against the dense TF32 rate
+                     "tf32_issued": {"achieved": 3 * achieved if achieved else None,
+                                     "peak": peak / 2 if peak else None,
+                                     "frac": (6 * achieved / peak) if (achieved and peak) else None},
+                     "algorithmic_bytes_per_launch": dot_bytes_per_launch,
+                     "traffic": GEMM_DRAM_BYTES_PER_LAUNCH if B == BATCH else None,
+                     "traffic_source": "ncu dram__bytes_read.sum + dram__bytes_write.sum over the 11 GEMM "
+                                       "launches of one step at batch 8192, averaged per launch "
+                                       "(single-pass capture, cold L2)"},
         "gpu_launches": launches,
         "execution": ("CUDA graph replay of the recorded step (%d kernels per step)" % per_replay) if graphs
                      else "eager",
@@ -406,6 +426,24 @@ def run_ours(args):
     if world > 1:
         distributed.barrier()
         distributed.shutdown()
+
+
+# DRAM bytes per GEMM launch of the batch-8192 step, from an ncu capture of its
+# 11 GEMM launches (dram__bytes_read.sum + dram__bytes_write.sum, averaged).
+GEMM_DRAM_BYTES_PER_LAUNCH = 1.0654e9
+
+
+def _tensor_peak(peaks: dict, clk: dict):
+    """The bf16 denominator for a tensor-bound kernel: the sustained (power
+    capped) figure when the sampled SM clock sat below its maximum, else the
+    burst figure (the kernel ran at full clock, as the burst GEMM did)."""
+    burst, sustained = peaks.get("bf16_tflops"), peaks.get("bf16_tflops_sustained")
+    sm, smax = (clk or {}).get("sm_mhz"), (clk or {}).get("sm_max_mhz")
+    at_max = sm is not None and smax and sm >= 0.97 * smax
+    src = peaks.get("source", "MEASURED_PEAKS.json")
+    if sustained and not at_max:
+        return sustained, f"{src} bf16 sustained (SM clock below max during the run); TF32 dense rate is half"
+    return burst, f"{src} bf16 burst (SM clock at max during the run); TF32 dense rate is half"
 
 
 def _measured_peaks() -> dict:

@@ -334,6 +334,12 @@ class PRNGKey:
 # Streams: one per (thread, GPU) via torch's thread-local current stream.
 # ---------------------------------------------------------------------------
 def stream_of(ordinal: int) -> int:
+    """Handle of the device's current torch stream, with that device made the
+    calling thread's current device first: the library launches on the current
+    device, and the default stream's handle (0) does not name one, so an op on
+    another GPU's array must not run with a different device current."""
+    if torch.cuda.current_device() != ordinal:
+        torch.cuda.set_device(ordinal)
     return torch.cuda.current_stream(ordinal).cuda_stream
 
 
@@ -453,7 +459,7 @@ class ConcreteNDArray(NDArray):
         return torch.empty(shape.size(), dtype=dtype.torch, device=self._t.device)
 
     def _stream(self) -> int:
-        return torch.cuda.current_stream(self._t.device).cuda_stream
+        return stream_of(self._t.device.index)
 
     # ---- accessors ----
     def shape(self) -> Shape:
@@ -731,9 +737,11 @@ def _dtype_of_numpy(arr: np.ndarray) -> DType:
     return DType.FLOAT32
 
 
-# When a list, every dot launch appends (start_event, end_event, flops):
+# When a list, every dot launch appends (start_event, end_event, flops, bytes):
 # CUDA events recorded on the launching stream around the kernel (used by the
-# benchmark to time the GEMM kernels inside its timed region).
+# benchmark to time the GEMM kernels inside its timed region) and the launch's
+# algorithmic HBM bytes: each FP32 operand read once as its hi/lo split (8 B per
+# element), every output written once, the epilogue's bias and mask read once.
 DOT_TIMING = None
 
 
@@ -827,7 +835,12 @@ def _dot_raw(a: "ConcreteNDArray", b: "ConcreteNDArray", trans_a: bool, trans_b:
              a._stream())
     if timing is not None:
         ev1.record()
-        timing.append((ev0, ev1, 2.0 * M * N * K))
+        if a._dtype == DType.FLOAT32:
+            nbytes = 8 * (M * K + K * N) + 4 * M * N * (1 + int(act) + int(mask is not None)) \
+                + (4 * N if bias is not None else 0)
+        else:
+            nbytes = a._dtype.byteSize() * (M * K + K * N + M * N)
+        timing.append((ev0, ev1, 2.0 * M * N * K, nbytes))
     c = ConcreteNDArray._wrap(out, Shape(M, N), a._dtype, device)
     if act:
         return c, ConcreteNDArray._wrap(act_out, Shape(M, N), a._dtype, device)

@@ -29,7 +29,7 @@ import torch
 
 from . import _lib
 from ._lib import call
-from .core import ConcreteNDArray, DType, NDArray, Primitive as P, Shape
+from .core import ConcreteNDArray, DType, NDArray, Primitive as P, Shape, stream_of
 from .tracing import AxisMeta, Jaxpr
 
 ELEMENTWISE = {P.ADD, P.SUB, P.MUL, P.DIV, P.MAX, P.MIN, P.EXP, P.LOG, P.SIN, P.COS, P.TANH,
@@ -370,7 +370,7 @@ def run_group(g: Group, values: Dict[int, NDArray]) -> None:
     pin = (C.c_void_p * max(1, len(ins)))(*[x.data_ptr() for x in ins])
     pout = (C.c_void_p * max(1, len(outs)))(*[t.data_ptr() for t in outs])
     ptail = (C.c_void_p * max(1, len(tails)))(*[t.data_ptr() for t in tails])
-    stream = torch.cuda.current_stream(tdev).cuda_stream
+    stream = stream_of(tdev.index)
     call("j4c_fused_launch", g.handle, R, Cc, pin, pout, ptail, stream)
 
 

@@ -25,7 +25,7 @@ from typing import Callable, Dict, List, Optional, Sequence
 import torch
 
 from ._lib import call
-from .core import ConcreteNDArray
+from .core import ConcreteNDArray, stream_of
 
 
 class CapturedStep:
@@ -92,7 +92,7 @@ class CapturedStep:
             raise ValueError(f"CapturedStep.set_input: {src.shape()} {src.dtype()} does not fit input {index}")
         if src.data_ptr() == dst.data_ptr():
             return
-        s = stream if stream is not None else torch.cuda.current_stream(self.device).cuda_stream
+        s = stream if stream is not None else stream_of(self.device.index)
         call("j4c_memcpy_d2d", dst.data_ptr(), src.data_ptr(), dst.tensor().numel() * dst.tensor().element_size(), s)
 
     def __call__(self) -> List[ConcreteNDArray]:

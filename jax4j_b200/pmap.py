@@ -33,7 +33,7 @@ import torch
 from . import _lib
 from ._lib import call
 from .core import (ConcreteNDArray, Device, DType, IllegalArgumentException,
-                   IllegalStateException, NDArray, Shape)
+                   IllegalStateException, NDArray, Shape, stream_of)
 
 BARRIER_TIMEOUT_S = float(os.environ.get("J4C_BARRIER_TIMEOUT_S", "120"))
 COMM_TIMEOUT_MS = int(os.environ.get("J4C_COMM_TIMEOUT_MS", "120000"))
@@ -209,7 +209,7 @@ class NcclCollective:
 
     def psum_inplace(self, index: int, t: torch.Tensor, dtype: DType) -> None:
         call("j4c_psum", self.comms[index], dtype.ordinal, t.data_ptr(), t.data_ptr(), t.numel(),
-             torch.cuda.current_stream(t.device).cuda_stream)
+             stream_of(t.device.index))
 
     def allGather(self, index: int, x: ConcreteNDArray) -> ConcreteNDArray:
         out = torch.empty(self.num_devices * x.shape().size(), dtype=x.dtype().torch,
