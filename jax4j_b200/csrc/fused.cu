@@ -48,6 +48,7 @@ struct Entry {
     cudaLibrary_t library = nullptr;
     cudaKernel_t flat[2] = {}, rows_warp[2] = {}, rows_block[2] = {};  // [0]: 1 element, [1]: 4 per thread
     bool needs_rows = false;  // tails or row/column-broadcast inputs
+    bool wide_sum = false;    // an 8-byte SUM/MEAN tail: summed element by element, as the row reduction does
     int n_in = 0, n_out = 0, n_tail = 0;
     int in_size[kMaxIn] = {}, in_bcast[kMaxIn] = {}, out_size[kMaxOut] = {};
 };
@@ -365,12 +366,18 @@ static std::string gen_source(const j4c_program *p, bool *needs_rows) {
         }
         o << "      if (r < R) {\n"
           << "      for (i64 j = (i64)sub * " << V << "; j < C; j += " << tpr * V << ") {\n"
-          << gen_loads(p, false, V) << "      #pragma unroll\n      for (int l = 0; l < " << V << "; l++) {\n"
-          << element;
+          << gen_loads(p, false, V);
+        // a lane's sum takes its V consecutive elements as ((x0 + x1) + (x2 + x3)),
+        // the order of the row reduction kernel, so fused and eager sums agree
+        for (int k = 0; k < p->n_tails; k++)
+            if (V == 4 && (p->tail_op[k] == J4C_SUM_AXIS || p->tail_op[k] == J4C_MEAN_AXIS))
+                o << "      " << ctype(p->insns[p->tail_insn[k]].dtype) << " tv" << k << "[4];\n";
+        o << "      #pragma unroll\n      for (int l = 0; l < " << V << "; l++) {\n" << element;
         for (int k = 0; k < p->n_tails; k++) {
             int op = p->tail_op[k], t = p->tail_insn[k];
             if (op == J4C_SUM_AXIS || op == J4C_MEAN_AXIS) {
-                o << "        acc" << k << " = j_add(acc" << k << ", v" << t << ");\n";
+                if (V == 4) o << "        tv" << k << "[l] = v" << t << ";\n";
+                else o << "        acc" << k << " = j_add(acc" << k << ", v" << t << ");\n";
             } else {
                 bool mx = op == J4C_ARGMAX;
                 // The reference keeps the first strict extremum, starting from
@@ -383,7 +390,13 @@ static std::string gen_source(const j4c_program *p, bool *needs_rows) {
                   << "; bi" << k << " = (int)(j + l); }\n";
             }
         }
-        o << "      }\n" << gen_stores(p, false, V) << "      }\n      }\n";
+        o << "      }\n";
+        if (V == 4)
+            for (int k = 0; k < p->n_tails; k++)
+                if (p->tail_op[k] == J4C_SUM_AXIS || p->tail_op[k] == J4C_MEAN_AXIS)
+                    o << "      acc" << k << " = j_add(acc" << k << ", j_add(j_add(tv" << k << "[0], tv" << k
+                      << "[1]), j_add(tv" << k << "[2], tv" << k << "[3])));\n";
+        o << gen_stores(p, false, V) << "      }\n      }\n";
         // reductions
         for (int k = 0; k < p->n_tails; k++) {
             int op = p->tail_op[k];
@@ -496,6 +509,10 @@ int j4c_fused_compile(const j4c_program *prog, void **handle) {
     }
     auto e = std::make_unique<Entry>();
     e->needs_rows = needs_rows;
+    for (int k = 0; k < prog->n_tails; k++)
+        if ((prog->tail_op[k] == J4C_SUM_AXIS || prog->tail_op[k] == J4C_MEAN_AXIS) &&
+            dsize(prog->insns[prog->tail_insn[k]].dtype) == 8)
+            e->wide_sum = true;
     e->n_in = prog->n_inputs;
     e->n_out = prog->n_outputs;
     e->n_tail = prog->n_tails;
@@ -544,7 +561,7 @@ int j4c_fused_launch(void *handle, int64_t rows, int64_t cols, const void *const
     // access is aligned (4-byte types; wider and narrower types are read
     // element by element inside the 4-wide loop).
     const int64_t extent = e->needs_rows ? cols : rows * cols;
-    bool v4 = extent % 4 == 0;
+    bool v4 = extent % 4 == 0 && !(e->needs_rows && e->wide_sum);
     for (int i = 0; i < e->n_in && v4; i++)
         if (e->in_size[i] == 4 && (e->in_bcast[i] == J4C_BCAST_FULL || e->in_bcast[i] == J4C_BCAST_ROW) &&
             reinterpret_cast<uintptr_t>(a.in[i]) % 16 != 0)
@@ -559,7 +576,7 @@ int j4c_fused_launch(void *handle, int64_t rows, int64_t cols, const void *const
         void *params[] = {&N, &a};
         r = cudaLaunchKernel((const void *)e->flat[v4], dim3(grid_for(ceil_div(N, (int64_t)V), 256)), dim3(256),
                              params, 0, s);
-    } else if (cols >= 512 * V) {  // a CTA per row once each thread gets two or more iterations
+    } else if (cols >= 2048) {  // a CTA per row from 2048 columns, as the row reduction kernel
         void *params[] = {&rows, &cols, &a};
         unsigned g = (unsigned)std::min<int64_t>(rows, (int64_t)sm_count() * 8);
         r = cudaLaunchKernel((const void *)e->rows_block[v4], dim3(g), dim3(256), params, 0, s);

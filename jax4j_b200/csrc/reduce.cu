@@ -107,6 +107,25 @@ __global__ void __launch_bounds__(256) col_reduce_kernel(const T *__restrict__ i
 #pragma unroll
             for (int k = 0; k < VEC; k++) acc[u][k] = T(0);
         int64_t a = a0;
+        // eight rows' loads in flight before their adds; row a+u still goes
+        // to accumulator u % 4 in row order, so the sums are unchanged
+        for (; a + 8 <= a1; a += 8) {
+            T v[8][VEC];
+#pragma unroll
+            for (int u = 0; u < 8; u++) {
+                if constexpr (VEC == 4 && sizeof(T) == 4) {
+                    const float4 q = __ldg(reinterpret_cast<const float4 *>(p + (a + u) * inner));
+                    v[u][0] = q.x; v[u][1] = q.y; v[u][2] = q.z; v[u][3] = q.w;
+                } else {
+#pragma unroll
+                    for (int k = 0; k < VEC; k++) v[u][k] = p[(a + u) * inner + k];
+                }
+            }
+#pragma unroll
+            for (int u = 0; u < 8; u++)
+#pragma unroll
+                for (int k = 0; k < VEC; k++) acc[u & 3][k] = r_add(acc[u & 3][k], v[u][k]);
+        }
         for (; a + 4 <= a1; a += 4) {
 #pragma unroll
             for (int u = 0; u < 4; u++) {
@@ -136,6 +155,8 @@ __global__ void __launch_bounds__(256) col_reduce_kernel(const T *__restrict__ i
 
 // The launch shape of a column reduction, shared by j4c_reduce_axis and
 // j4c_reduce_axis_noalloc so both add in the same order.
+constexpr int kMaxColSplits = 64;  // most chunks col_plan cuts an axis into
+
 struct ColPlan {
     int vec;
     int64_t gx, gy, splits, chunk;
@@ -148,7 +169,8 @@ static ColPlan col_plan(const T *in, int64_t outer, int64_t axis, int64_t inner)
     c.gy = std::min<int64_t>(outer, 65535);
     const int64_t ctas = c.gx * c.gy, want = (int64_t)sm_count() * 4;
     c.splits = 1;
-    if (ctas < want && axis >= 64) c.splits = std::min<int64_t>({ceil_div(want, ctas), axis / 32, 64});
+    if (ctas < want && axis >= 64)
+        c.splits = std::min<int64_t>({ceil_div(want, ctas), axis / 32, (int64_t)kMaxColSplits});
     c.chunk = ceil_div(axis, c.splits);
     c.splits = ceil_div(axis, c.chunk);
     return c;
@@ -169,7 +191,18 @@ __global__ void __launch_bounds__(256) combine_parts_kernel(const T *__restrict_
     for (int64_t i = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; i < n;
          i += (int64_t)gridDim.x * blockDim.x) {
         T acc = T(0);
-        for (int s = 0; s < splits; s++) acc = r_add(acc, part[(int64_t)s * n + i]);
+        if (splits <= kMaxColSplits) {
+            // all the loads first (independent), then the adds in chunk order
+            T v[kMaxColSplits];
+#pragma unroll
+            for (int s = 0; s < kMaxColSplits; s++)
+                if (s < splits) v[s] = part[(int64_t)s * n + i];
+#pragma unroll
+            for (int s = 0; s < kMaxColSplits; s++)
+                if (s < splits) acc = r_add(acc, v[s]);
+        } else {
+            for (int s = 0; s < splits; s++) acc = r_add(acc, part[(int64_t)s * n + i]);
+        }
         out[i] = mean ? to_mean(acc, axis) : acc;
     }
 }

@@ -16,13 +16,19 @@ rules while doing less work:
     rest, e.g. the DOT VJP w.r.t. a constant data batch);
   * TANH/SIGMOID/EXP VJPs reuse the forward output instead of recomputing
     the same deterministic kernel on the same input.
+With fusion on, the elementwise parts of the rules are deferred inside the
+backward walk and evaluated as generated kernels (lazy.py).
 """
 from __future__ import annotations
 
 import os
+import threading
 from typing import Callable, Dict, List
 
 import torch
+
+from . import lazy
+from .lazy import Deferred, materialize
 
 from ._lib import call, dims as _dims
 from .core import (ConcreteNDArray, DType, IllegalArgumentException, NDArray, Primitive, Shape,
@@ -38,8 +44,32 @@ def _float_or_default(dtype: DType) -> DType:
     return dtype if dtype.is_floating() else DType.FLOAT32
 
 
-def _scalar_like(v: float, like: ConcreteNDArray, dtype: DType = None) -> ConcreteNDArray:
-    return ConcreteNDArray.scalar(v, dtype or like.dtype(), like.device())
+_CONSTS: Dict[tuple, ConcreteNDArray] = {}
+
+
+def _scalar_like(v: float, like: NDArray, dtype: DType = None) -> ConcreteNDArray:
+    """A [1] constant next to `like`.  Constants are immutable, so each
+    (value, dtype, device) is made once -- outside a stream capture, where
+    making it waits for its fill -- and reused."""
+    dtype = dtype or like.dtype()
+    dev = like.device()
+    key = (float(v), dtype, dev.ordinal() if dev is not None else None)
+    c = _CONSTS.get(key)
+    if c is not None:
+        return c
+    c = ConcreteNDArray.scalar(v, dtype, dev)
+    if not torch.cuda.is_current_stream_capturing():
+        torch.cuda.current_stream(c.tensor().device).synchronize()
+        _CONSTS[key] = c
+    return c
+
+
+# Deferred (fused) cotangents are built only inside the backward walk, per thread.
+_lazy_scope = threading.local()
+
+
+def _lazy_on() -> bool:
+    return FUSION and lazy.ENABLED and getattr(_lazy_scope, "depth", 0) > 0
 
 
 def ones(shape: Shape, dtype: DType, device=None) -> ConcreteNDArray:
@@ -62,11 +92,17 @@ def _zeros_for(var: Var, like: ConcreteNDArray) -> ConcreteNDArray:
 # ---------------------------------------------------------------------------
 # device versions of the Grad.java host helpers
 # ---------------------------------------------------------------------------
-def broadcast_like(g: ConcreteNDArray, target_shape: Shape) -> ConcreteNDArray:
+def broadcast_like(g: NDArray, target_shape: Shape) -> NDArray:
     """Grad.broadcastLike (Grad.java:539-582): copy/reshape, expand, or sum down."""
     gs = g.shape()
     if gs == target_shape:
         return g
+    if _lazy_on() and gs.size() != target_shape.size():
+        d = (lazy.expand(g, target_shape) if target_shape.size() > gs.size()
+             else lazy.row_sum(g, target_shape))
+        if d is not None:
+            return d
+    g = materialize(g)
     if gs.size() == target_shape.size():
         return g.reshape(target_shape)
     out = torch.empty(target_shape.size(), dtype=g.dtype().torch, device=g.tensor().device)
@@ -79,6 +115,14 @@ def axis_broadcast_like(g: ConcreteNDArray, original: Shape, axis: int) -> Concr
     """Grad.axisBroadcastLike (Grad.java:608-641): g (with or without the
     reduced dim) viewed as [outer, 1, inner], broadcast to [outer, axis, inner]."""
     outer, n, inner = original.axis_split(axis)
+    if _lazy_on() and inner == 1:
+        # the last axis: g as [..., 1] broadcasts over it as a column
+        col = Shape(original.dimensions()[:-1] + (1,))
+        gv = g if g.shape() == col else materialize(g).reshape(col)
+        d = lazy.expand(gv, original)
+        if d is not None:
+            return d
+    g = materialize(g)
     src = Shape(outer, 1, inner)
     dst = Shape(outer, n, inner)
     out = torch.empty(dst.size(), dtype=g.dtype().torch, device=g.tensor().device)
@@ -89,6 +133,7 @@ def axis_broadcast_like(g: ConcreteNDArray, original: Shape, axis: int) -> Concr
 
 def relu_grad(g: ConcreteNDArray, x: ConcreteNDArray) -> ConcreteNDArray:
     """Grad.reluGrad (Grad.java:585-598)."""
+    g = materialize(g)
     out = torch.empty_like(x.tensor())
     call("j4c_relu_grad", x.dtype().ordinal, g.data_ptr(), x.data_ptr(), x.shape().size(),
          out.data_ptr(), x._stream())
@@ -97,6 +142,7 @@ def relu_grad(g: ConcreteNDArray, x: ConcreteNDArray) -> ConcreteNDArray:
 
 def maxmin_grad(g: ConcreteNDArray, a: ConcreteNDArray, b: ConcreteNDArray, is_max: bool):
     """Grad.maxMinGrad (Grad.java:500-530): ties go to a."""
+    g = materialize(g)
     gs = g.shape()
     ga = torch.empty_like(g.tensor())
     gb = torch.empty_like(g.tensor())
@@ -115,7 +161,13 @@ def _neg(x: ConcreteNDArray) -> ConcreteNDArray:
 
 def _bin(a: ConcreteNDArray, b: ConcreteNDArray, prim: Primitive) -> ConcreteNDArray:
     """A binary kernel without the public method's device-tag rules (the
-    interpreter's helper constants are created next to their operands)."""
+    interpreter's helper constants are created next to their operands);
+    deferred inside the backward walk when it fits a generated kernel."""
+    if _lazy_on():
+        d = lazy.binary(a, b, prim)
+        if d is not None:
+            return d
+    a, b = materialize(a), materialize(b)
     out_shape = Shape.broadcast(a.shape(), b.shape())
     out = torch.empty(out_shape.size(), dtype=a.dtype().torch, device=a.tensor().device)
     call("j4c_binary", int(prim), a.dtype().ordinal, a.data_ptr(), _dims(a.shape()), a.shape().rank(),
@@ -370,7 +422,12 @@ def backward_interpret(jaxpr: Jaxpr, args: List[NDArray], seeds: List[NDArray]) 
 
 def _merge(grads: Dict[int, NDArray], vid: int, g: NDArray) -> None:
     prev = grads.get(vid)
-    grads[vid] = g if prev is None else prev.add(g)
+    if prev is None:
+        grads[vid] = g
+    elif isinstance(prev, Deferred) or isinstance(g, Deferred):
+        grads[vid] = _bin(prev, g, Primitive.ADD)
+    else:
+        grads[vid] = prev.add(g)
 
 
 def _relu_fed_dots(jaxpr: Jaxpr, need) -> Dict[int, object]:
@@ -401,6 +458,14 @@ def _relu_fed_dots(jaxpr: Jaxpr, need) -> Dict[int, object]:
 
 def do_backward(jaxpr: Jaxpr, values: Dict[int, NDArray], seeds: List[NDArray]) -> List[NDArray]:
     """Grad.doBackward (Grad.java:154-189)."""
+    _lazy_scope.depth = getattr(_lazy_scope, "depth", 0) + 1
+    try:
+        return _do_backward(jaxpr, values, seeds)
+    finally:
+        _lazy_scope.depth -= 1
+
+
+def _do_backward(jaxpr: Jaxpr, values: Dict[int, NDArray], seeds: List[NDArray]) -> List[NDArray]:
     need = _needs_grad(jaxpr)
     fused_relu = _relu_fed_dots(jaxpr, need) if FUSION else {}
     grads: Dict[int, NDArray] = {}
@@ -423,6 +488,8 @@ def do_backward(jaxpr: Jaxpr, values: Dict[int, NDArray], seeds: List[NDArray]) 
         _process_backward_eq(eq, values, grads, need, fused_relu)
         for vid in done_at.get(i_eq, ()):
             g = grads.get(vid)
+            if isinstance(g, Deferred):
+                g = grads[vid] = materialize(g)
             if isinstance(g, ConcreteNDArray) and g.tensor().is_cuda:
                 import torch
                 ev = torch.cuda.Event()
@@ -430,7 +497,7 @@ def do_backward(jaxpr: Jaxpr, values: Dict[int, NDArray], seeds: List[NDArray]) 
                 g._ready = ev
     result = []
     for v in jaxpr.inVars:
-        g = grads.get(v.id)
+        g = materialize(grads.get(v.id))
         result.append(g if g is not None else zeros(v.shape, v.dtype, _device_of(values.get(v.id))))
     return result
 
@@ -438,7 +505,7 @@ def do_backward(jaxpr: Jaxpr, values: Dict[int, NDArray], seeds: List[NDArray]) 
 def _process_backward_eq(eq, values, grads, need, fused_relu) -> None:
     """One equation of Grad.doBackward's reverse walk (Grad.java:162-185)."""
     if eq.primitive == Primitive.SCAN:
-        g_c, g_y = grads.get(eq.outputs[0].id), grads.get(eq.outputs[1].id)
+        g_c, g_y = materialize(grads.get(eq.outputs[0].id)), materialize(grads.get(eq.outputs[1].id))
         if (g_c is None and g_y is None) or not any(v.id in need for v in eq.inputs):
             return
         gi = scan_backward(eq, [values.get(v.id) for v in eq.inputs], g_c, g_y)
@@ -454,6 +521,7 @@ def _process_backward_eq(eq, values, grads, need, fused_relu) -> None:
         return
     z = fused_relu.get(id(eq))
     if z is not None and wanted[0]:
+        g_out = materialize(g_out)
         a, b = values.get(eq.inputs[0].id), values.get(eq.inputs[1].id)
         zv = values.get(z.id)
         if (isinstance(g_out, ConcreteNDArray) and isinstance(b, ConcreteNDArray) and
@@ -533,11 +601,22 @@ def execute_primitive(p: Primitive, eq, inputs: List[NDArray]) -> NDArray:
     raise UnsupportedOperationException(str(p))
 
 
+# rules built only from _bin / broadcasts, whose cotangent may stay deferred
+_DEFERRABLE_RULES = {Primitive.ADD, Primitive.SUB, Primitive.MUL, Primitive.DIV, Primitive.MEAN, Primitive.SUM,
+                     Primitive.SUM_AXIS, Primitive.MEAN_AXIS, Primitive.EXP, Primitive.LOG, Primitive.SIN,
+                     Primitive.COS, Primitive.TANH, Primitive.SIGMOID, Primitive.CAST,
+                     # zero cotangents: g is not read
+                     Primitive.GT, Primitive.GE, Primitive.LT, Primitive.LE, Primitive.EQ, Primitive.NE,
+                     Primitive.ARGMAX, Primitive.ARGMIN}
+
+
 def compute_vjps(p: Primitive, eq, g: ConcreteNDArray, inputs: List[NDArray], out_value,
                  wanted: List[bool]) -> List:
     """Grad.computeVJPs (Grad.java:341-472).  Entries of inputs whose cotangent is
     not wanted may come back as None."""
     from . import pmap as _pm
+    if p not in _DEFERRABLE_RULES:
+        g = materialize(g)
     want_a = wanted[0]
     want_b = len(wanted) > 1 and wanted[1]
     shapes = [v.shape for v in eq.inputs]  # rules that need only shapes read them from the Vars

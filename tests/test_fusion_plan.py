@@ -175,3 +175,69 @@ def test_program_struct_layout_matches_the_c_abi():
     assert [getattr(P, f).offset for f in ("n_insns", "insns", "n_inputs", "input_dtype", "input_bcast",
                                             "n_outputs", "output_insn", "n_tails", "tail_op", "tail_insn")] == \
         [0, 8, 16, 24, 32, 40, 48, 56, 64, 72]
+
+
+def _leaf(*dims):
+    """A host-memory FLOAT32 array standing in for a forward value (planning only)."""
+    import torch
+    from jax4j_b200.core import ConcreteNDArray
+    s = Shape(*dims)
+    return ConcreteNDArray._wrap(torch.empty(s.size()), s, DType.FLOAT32, None)
+
+
+def _softmax_ce_backward(B=64, C=40):
+    """The deferred cotangent of the logits for loss = -mean(sum(log(e / sum(e)) * t, -1)),
+    built with the rules of Grad.computeVJPs (MEAN, SUM_AXIS, MUL, LOG, DIV, SUM_AXIS, EXP)."""
+    from jax4j_b200 import lazy
+    g_r = _leaf(B, 1)                     # the mean's cotangent, already spread over the rows
+    onehot, p, e = _leaf(B, C), _leaf(B, C), _leaf(B, C)
+    s, minus1 = _leaf(B, 1), _leaf(1)
+    g_t = lazy.expand(g_r, Shape(B, C))                        # SUM_AXIS VJP
+    g_p = lazy.binary(lazy.binary(g_t, onehot, P.MUL), p, P.DIV)  # MUL, then LOG VJP (g / p)
+    ga = lazy.binary(g_p, s, P.DIV)                              # DIV VJP w.r.t. e
+    t = lazy.binary(lazy.binary(lazy.binary(g_p, e, P.MUL), s, P.DIV), s, P.DIV)
+    g_s = lazy.row_sum(lazy.binary(t, minus1, P.MUL), Shape(B, 1))  # DIV VJP w.r.t. s, summed down
+    g_e = lazy.binary(ga, lazy.expand(g_s, Shape(B, C)), P.ADD)   # + SUM_AXIS VJP of s = sum(e)
+    return lazy.binary(g_e, e, P.MUL)                            # EXP VJP
+
+
+def test_deferred_softmax_ce_backward_is_two_kernels():
+    from jax4j_b200 import lazy
+    x = _softmax_ce_backward()
+    assert isinstance(x, lazy.Deferred)
+    # the planning half of lazy.materialize
+    leaves, nodes = [], []
+    seen = {}
+
+    def walk(n):
+        if not isinstance(n, lazy.Deferred):
+            if id(n) not in seen:
+                seen[id(n)] = ("in", len(leaves))
+                leaves.append(n)
+            return seen[id(n)]
+        if id(n) not in seen:
+            refs = [walk(a) for a in n.args]
+            seen[id(n)] = ("eq", len(nodes))
+            nodes.append((n, refs))
+        return seen[id(n)]
+
+    walk(x)
+    jaxpr, plan = lazy._build(leaves, nodes)
+    kinds = [k for k, _ in plan.steps]
+    assert kinds == ["group", "group"]
+    g1, g2 = plan.groups
+    assert [e.primitive for e in g1.tails] == [P.SUM_AXIS]
+    assert len(g1.outputs) == 1 and len(g2.outputs) == 1   # ga, then the logits' cotangent
+    assert g2.outputs[0].id == jaxpr.outVars[0].id
+    for g in plan.groups:
+        assert "extern \"C\"" in fusion.group_source(g, compile=True)
+
+
+def test_deferred_values_refuse_what_a_kernel_cannot_broadcast():
+    from jax4j_b200 import lazy
+    a, b = _leaf(8, 16), _leaf(16, 1)
+    assert lazy.binary(a, b, P.ADD) is None              # [16, 1] is no row, column or scalar of [8, 16]
+    assert lazy.expand(_leaf(8), Shape(8, 16)) is None    # needs the [8, 1] view first
+    assert lazy.row_sum(a, Shape(16)) is None             # a column sum: not a last-axis tail
+    assert lazy.row_sum(a, Shape(8)).meta.keepDims is False
+    assert lazy.row_sum(a, Shape(8, 1)).meta.keepDims is True

@@ -1,6 +1,8 @@
-"""Fused elementwise chains (JAX.jit / the grad interpreter's forward pass)
-against the unfused kernels and the oracle: elementwise results bit for bit,
-row-reduction tails within the reduction tolerance, argmax exact."""
+"""Fused elementwise chains (JAX.jit, the grad interpreter's forward pass and
+its deferred backward) against the unfused kernels and the oracle: fused and
+unfused results bit for bit (row-reduction tails add in the row reduction
+kernel's order), the oracle within the elementwise / reduction tolerances,
+argmax exact."""
 import numpy as np
 import pytest
 
@@ -44,9 +46,11 @@ def test_fused_sweep_matches_oracle(J, rows, cols):
     assert_rel(z.numpy(), rz, TOL_ELEMENTWISE, "z")
     assert_rel(s.numpy(), rs, TOL_REDUCTION, "row sums")
     np.testing.assert_array_equal(am.numpy(), ram)
-    # fused elementwise values equal the unfused kernels' bit for bit
-    z2, _, am2 = _unfused(J, lambda: J.JAX.jit(sweep)(x, y))
+    # fused values equal the unfused kernels' bit for bit -- the row sums too:
+    # the generated tail adds in the row reduction kernel's order
+    z2, s2, am2 = _unfused(J, lambda: J.JAX.jit(sweep)(x, y))
     np.testing.assert_array_equal(z.numpy(), z2.numpy())
+    np.testing.assert_array_equal(s.numpy(), s2.numpy())
     np.testing.assert_array_equal(am.numpy(), am2.numpy())
 
 
@@ -130,3 +134,69 @@ def test_fusion_keeps_values_the_backward_reads(J):
     g = J.JAX.grad(fn)(x).numpy()
     g_ref = _unfused(J, lambda: J.JAX.grad(fn)(x).numpy())
     assert_rel(g, g_ref, TOL_REDUCTION)
+
+
+def _eager_backward(fn):
+    """fn() with the backward's cotangents computed op by op (no deferral)."""
+    from jax4j_b200 import lazy
+    old = lazy.ENABLED
+    lazy.ENABLED = False
+    try:
+        return fn()
+    finally:
+        lazy.ENABLED = old
+
+
+def test_deferred_backward_softmax_ce_fewer_launches_same_bits(J):
+    from jax4j_b200 import _lib
+    r = np.random.default_rng(9)
+    x = J.ConcreteNDArray.of(r.standard_normal((96, 50)).astype(np.float32))
+    w = J.ConcreteNDArray.of((0.1 * r.standard_normal((50, 30))).astype(np.float32))
+    b = J.ConcreteNDArray.of((0.1 * r.standard_normal(30)).astype(np.float32))
+    t = np.zeros((96, 30), np.float32)
+    t[np.arange(96), r.integers(0, 30, 96)] = 1.0
+    tt = J.ConcreteNDArray.of(t)
+    neg = J.ConcreteNDArray.scalar(-1.0)
+
+    def loss(tree):
+        c = tree.children
+        logits = x.dot(c["w"].value).add(c["b"].value)
+        return J.Nn.softmax(logits).log().mul(tt).sum(-1).mean().mul(neg)
+
+    vg = J.JAX.valueAndGradTree(loss)
+    tree = J.PyTree.dictOf({"w": w, "b": b})
+    vg(tree)  # plans and kernels compiled once
+    n0 = _lib.kernel_launches()
+    v1, g1 = vg(tree)
+    n1 = _lib.kernel_launches()
+    v0, g0 = _eager_backward(lambda: vg(tree))
+    n2 = _lib.kernel_launches()
+    assert (n1 - n0) + 8 <= (n2 - n1), (n1 - n0, n2 - n1)
+    np.testing.assert_array_equal(v1.numpy(), v0.numpy())
+    for k in ("w", "b"):
+        np.testing.assert_array_equal(g1.children[k].value.numpy(), g0.children[k].value.numpy())
+
+
+@pytest.mark.parametrize("shape", [(64, 48), (5, 3), (1, 700), (300, 1)])
+def test_deferred_backward_rules_match_eager(J, shape):
+    """TANH, SIGMOID, EXP, LOG, SIN, COS, DIV with row / column / scalar
+    broadcasts, MEAN_AXIS over the last axis and SUM: the deferred VJPs give
+    the eager kernels' bits."""
+    r = np.random.default_rng(sum(shape))
+    x = J.ConcreteNDArray.of(r.standard_normal(shape).astype(np.float32))
+    y = J.ConcreteNDArray.of((r.random(shape) + 0.5).astype(np.float32))
+    row = J.ConcreteNDArray.of((r.random(shape[-1]) + 0.5).astype(np.float32))
+    col = J.ConcreteNDArray.of((r.random((shape[0], 1)) + 0.5).astype(np.float32))
+    two = J.ConcreteNDArray.scalar(2.0)
+
+    def f(a, c):
+        u = a.tanh().mul(c.sigmoid()).div(row).add(a.exp().div(col))
+        v = c.log().mul(a.sin()).sub(a.cos().div(two))
+        m = u.mul(v).mean(-1, True)
+        return u.div(m.add(two)).sum()
+
+    g = J.JAX.gradBoth(f)
+    ga, gc = g(x, y)
+    ea, ec = _eager_backward(lambda: g(x, y))
+    np.testing.assert_array_equal(ga.numpy(), ea.numpy())
+    np.testing.assert_array_equal(gc.numpy(), ec.numpy())
