@@ -437,3 +437,37 @@ def test_he_normal_and_dropout(J):
     ref = (x.numpy() * keep.astype(np.float32)).astype(np.float64) / np.float64(np.float32(0.75))
     np.testing.assert_array_equal(d, ref.astype(np.float32))
     np.testing.assert_array_equal(J.Nn.dropout(x, key, 0.25, False).numpy(), x.numpy())
+
+
+# ---- RandomTest.java:104-183: permutation, heNormal and dropout, as the reference tests them ----
+def test_reference_permutation_is_a_valid_permutation(J):
+    perm = J.Random.permutation(J.PRNGKey.key(4), 200)
+    assert perm.dtype() == J.DType.INT32
+    assert sorted(perm.numpy().tolist()) == list(range(200))
+
+
+def test_reference_he_normal_scales_by_expected_std(J):
+    fan_in, n = 256, 20000
+    expected = float(np.float32(np.sqrt(2.0 / fan_in)))
+    w = J.Random.heNormal(J.PRNGKey.key(6), J.Shape(n), fan_in).numpy().astype(np.float64)
+    assert abs(np.sqrt((w * w).sum() / n) - expected) <= expected * 0.15
+
+
+def test_reference_dropout_modes(J):
+    x = J.ConcreteNDArray.of(np.array([1, 2, 3, 4], np.float32))
+    np.testing.assert_array_equal(J.Nn.dropout(x, J.PRNGKey.key(1), 0.5, False).numpy(), [1, 2, 3, 4])
+    ones = J.ConcreteNDArray.of(np.ones(20000, np.float32))
+    out = J.Nn.dropout(ones, J.PRNGKey.key(8), 0.4, True).numpy()
+    kept = out[out != 0]
+    np.testing.assert_allclose(kept, np.float32(1.0) / np.float32(0.6), atol=1e-4)
+    assert abs((out == 0).mean() - 0.4) <= 0.02
+
+
+def test_reference_dropout_gradient(J):
+    """Zero at dropped positions, 1 / (1 - rate) at kept ones, through JAX.grad."""
+    x = J.ConcreteNDArray.of(np.ones(8, np.float32))
+    key, rate = J.PRNGKey.key(123), 0.5
+    m = J.Random.bernoulli(key, 1.0 - rate, x.shape()).numpy().astype(bool)
+    g = J.JAX.grad(lambda v: J.Nn.dropout(v, key, rate, True).sum())(x).numpy()
+    np.testing.assert_array_equal(g[~m], 0.0)
+    np.testing.assert_allclose(g[m], 1.0 / (1.0 - rate), atol=1e-4)
