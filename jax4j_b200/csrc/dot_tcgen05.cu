@@ -54,6 +54,7 @@ constexpr int kEpiWarps = 8;      // two warps per TMEM lane quadrant
 constexpr int kThreads = 64 + 32 * kEpiWarps;
 constexpr int kStatusTimeout = 0x7C05;
 constexpr uint64_t kWaitLimitNs = 2000000000ull;  // 2 s without progress
+constexpr int kMaxTailSplits = 4; // parts along K of a tile of the last wave
 
 // BK = FP32 elements per smem row of a stage: 32 (128-byte swizzle) or 16
 // (64-byte swizzle, half the bytes per stage, so twice the stages fit).
@@ -234,6 +235,22 @@ __device__ __forceinline__ void tile_coords(int t, int num_m, int num_n, int &mt
     nt = r / gsize;
 }
 
+// Work units.  The tiles of the full waves are units of their own; the tiles
+// of a last, partial wave are cut into `splits` parts along K (k-blocks
+// [num_kb*p/splits, num_kb*(p+1)/splits)), so that wave takes 1/splits of a
+// tile's time.  Each part leaves its FP32 partial in `part`; the last part of
+// a tile to finish adds the partials in part order and stores the tile.
+struct Unit {
+    int tile, kb0, kb1, part;  // part < 0: a whole tile
+};
+
+__device__ __forceinline__ Unit unit_of(int u, int full_tiles, int splits, int num_kb) {
+    if (u < full_tiles) return Unit{u, 0, num_kb, -1};
+    const int r = u - full_tiles, part = r % splits;
+    return Unit{full_tiles + r / splits, (int)((int64_t)num_kb * part / splits),
+                (int)((int64_t)num_kb * (part + 1) / splits), part};
+}
+
 // Elementwise work fused into the GEMM's store (each part optional), in the
 // coordinates of the stored C [rows, cols]:
 //   v = acc + bias[col]            (a bias add broadcast along rows)
@@ -265,7 +282,8 @@ __global__ void __launch_bounds__(kThreads, 1)
 gemm_3xtf32_kernel(const __grid_constant__ CUtensorMap tAh, const __grid_constant__ CUtensorMap tAl,
                    const __grid_constant__ CUtensorMap tBh, const __grid_constant__ CUtensorMap tBl,
                    float *__restrict__ C, int M, int N, int num_kb, int vec_store, int store_t,
-                   Epilogue ep, int batch, int a_batched, int b_batched, int *status) {
+                   Epilogue ep, int batch, int a_batched, int b_batched, int *status, int full_tiles,
+                   int splits, float *__restrict__ part, int *__restrict__ arrivals) {
     using Q = Cfg<BN, STAGES, BK>;
     constexpr int CHUNK_KB = Q::CHUNK_KB;
     extern __shared__ uint8_t smem_raw[];
@@ -276,6 +294,7 @@ gemm_3xtf32_kernel(const __grid_constant__ CUtensorMap tAh, const __grid_constan
     const int num_m = (M + BM - 1) / BM, num_n = (N + BN - 1) / BN;
     const int tiles_per_batch = num_m * num_n;
     const int num_tiles = tiles_per_batch * batch;  // batch entries one after another
+    const int num_units = full_tiles + (num_tiles - full_tiles) * splits;
 
     if (threadIdx.x == 0) {
         for (int s = 0; s < STAGES; s++) {
@@ -310,12 +329,14 @@ gemm_3xtf32_kernel(const __grid_constant__ CUtensorMap tAh, const __grid_constan
             uint32_t phase = 0;
             int issued = 0;
             bool ok = true;
-            for (int t = blockIdx.x; ok && t < num_tiles; t += gridDim.x) {
+            for (int u = blockIdx.x; ok && u < num_units; u += gridDim.x) {
+                const Unit w = unit_of(u, full_tiles, splits, num_kb);
+                const int t = w.tile;
                 int mt, nt;
                 const int bidx = t / tiles_per_batch;
                 tile_coords(t - bidx * tiles_per_batch, num_m, num_n, mt, nt);
                 const int za = a_batched ? bidx : 0, zb = b_batched ? bidx : 0;
-                for (int kb = 0; kb < num_kb; kb++) {
+                for (int kb = w.kb0; kb < w.kb1; kb++) {
                     if (!wait_bar(smem_u32(&ctl->empty[stage]), phase ^ 1, abort, status)) {
                         ok = false;
                         break;
@@ -353,8 +374,9 @@ gemm_3xtf32_kernel(const __grid_constant__ CUtensorMap tAh, const __grid_constan
             uint32_t phase = 0;
             int ci = 0;  // chunk counter across tiles: selects the TMEM buffer
             bool ok = true;
-            for (int t = blockIdx.x; ok && t < num_tiles; t += gridDim.x) {
-                for (int kb0 = 0; ok && kb0 < num_kb; kb0 += CHUNK_KB, ci++) {
+            for (int u = blockIdx.x; ok && u < num_units; u += gridDim.x) {
+                const Unit w = unit_of(u, full_tiles, splits, num_kb);
+                for (int kb0 = w.kb0; ok && kb0 < w.kb1; kb0 += CHUNK_KB, ci++) {
                     const int buf = ci & 1;
                     const uint32_t bph = (ci >> 1) & 1;
                     if (!wait_bar(smem_u32(&ctl->tempty[buf]), bph ^ 1, abort, status)) {
@@ -363,7 +385,7 @@ gemm_3xtf32_kernel(const __grid_constant__ CUtensorMap tAh, const __grid_constan
                     }
                     tc_fence_after();
                     const uint32_t dcol = tmem + buf * BN;
-                    const int kb1 = min(num_kb, kb0 + CHUNK_KB);
+                    const int kb1 = min(w.kb1, kb0 + CHUNK_KB);
                     for (int kb = kb0; kb < kb1; kb++) {
                         if (!wait_bar(smem_u32(&ctl->full[stage]), phase, abort, status)) {
                             ok = false;
@@ -410,7 +432,9 @@ gemm_3xtf32_kernel(const __grid_constant__ CUtensorMap tAh, const __grid_constan
         const uint32_t lane_off = (uint32_t)(q * 32) << 16;
         int ci = 0;
         bool ok = true;
-        for (int t = blockIdx.x; ok && t < num_tiles; t += gridDim.x) {
+        for (int u = blockIdx.x; ok && u < num_units; u += gridDim.x) {
+            const Unit w = unit_of(u, full_tiles, splits, num_kb);
+            const int t = w.tile;
             int mt, nt;
             const int bidx = t / tiles_per_batch;
             tile_coords(t - bidx * tiles_per_batch, num_m, num_n, mt, nt);
@@ -422,7 +446,7 @@ gemm_3xtf32_kernel(const __grid_constant__ CUtensorMap tAh, const __grid_constan
             float acc[Q::COLS_PER_WARP];
 #pragma unroll
             for (int j = 0; j < Q::COLS_PER_WARP; j++) acc[j] = 0.0f;
-            for (int kb0 = 0; kb0 < num_kb; kb0 += CHUNK_KB, ci++) {
+            for (int kb0 = w.kb0; kb0 < w.kb1; kb0 += CHUNK_KB, ci++) {
                 const int buf = ci & 1;
                 const uint32_t bph = (ci >> 1) & 1;
                 if (!wait_bar(smem_u32(&ctl->tfull[buf]), bph, abort, status)) {
@@ -442,6 +466,35 @@ gemm_3xtf32_kernel(const __grid_constant__ CUtensorMap tAh, const __grid_constan
                 if (lane == 0) mbar_arrive(smem_u32(&ctl->tempty[buf]));
             }
             if (!ok) break;
+            if (w.part >= 0) {
+                // A part of a split tile.  Each epilogue warp owns 32 rows x
+                // COLS_PER_WARP columns of the tile and settles them alone (no
+                // wait on other warps): it leaves its partial (a column j of the
+                // region is 32 consecutive floats), counts its arrival, and the
+                // warp of the last part to arrive adds all partials in part order.
+                constexpr int RF = 32 * Q::COLS_PER_WARP;  // floats of one warp's region
+                const size_t tix = (size_t)(t - full_tiles);
+                float *mine = part + ((tix * splits + w.part) * kEpiWarps + ew) * (size_t)RF + lane;
+#pragma unroll
+                for (int j = 0; j < Q::COLS_PER_WARP; j++) mine[(size_t)j * 32] = acc[j];
+                __threadfence();
+                __syncwarp();
+                int before = 0;
+                if (lane == 0) before = atomicAdd(arrivals + tix * kEpiWarps + ew, 1);
+                before = __shfl_sync(0xffffffffu, before, 0);
+                if (before != splits - 1) continue;  // a later part settles the region
+                __threadfence();
+                // every partial (this part's too) is read back through L2
+                const float *rp = part + (tix * splits * kEpiWarps + ew) * (size_t)RF + lane;
+#pragma unroll
+                for (int j = 0; j < Q::COLS_PER_WARP; j++) {
+                    float v = __ldcg(rp + (size_t)j * 32);
+#pragma unroll
+                    for (int p = 1; p < kMaxTailSplits; p++)
+                        if (p < splits) v = __fadd_rn(v, __ldcg(rp + (size_t)p * kEpiWarps * RF + (size_t)j * 32));
+                    acc[j] = v;
+                }
+            }
             const int row = mt * BM + q * 32 + lane;
             const int col0 = nt * BN + cbase;
             if (store_t) {
@@ -637,10 +690,45 @@ static int make_map(CUtensorMap *map, const float *base, int64_t rows, int64_t c
     return J4C_OK;
 }
 
+// The tail split of a GEMM (Unit): the tiles of the full waves stay whole;
+// the rest are cut into as many parts along K (up to 4) as still fit one
+// wave, each part keeping at least one promotion chunk of k-blocks.
+struct TailPlan {
+    int64_t full_tiles;
+    int splits;
+};
+
+static TailPlan tail_plan(int64_t tiles, int64_t num_kb, int64_t chunk_kb, int64_t sms) {
+    const int64_t full = tiles / sms * sms, rem = tiles - full;
+    if (rem == 0) return TailPlan{tiles, 1};
+    int64_t sp = std::min<int64_t>(kMaxTailSplits, sms / rem);
+    while (sp > 1 && num_kb / sp < chunk_kb) sp--;
+    return sp < 2 ? TailPlan{tiles, 1} : TailPlan{full, (int)sp};
+}
+
+// Scratch of a tail split: the parts' FP32 partial tiles, then one arrival
+// counter per (split tile, epilogue warp).
+static size_t tail_scratch_bytes(int64_t tiles, const TailPlan &p, int bn) {
+    if (p.splits < 2) return 0;
+    const int64_t rem = tiles - p.full_tiles;
+    return (size_t)(rem * p.splits * BM * bn) * sizeof(float) + (size_t)(rem * kEpiWarps) * sizeof(int);
+}
+
+// An upper bound of tail_scratch_bytes for an [m, n] product in either
+// orientation (the K condition only lowers the number of parts).
+size_t tail_scratch_bound(int64_t m, int64_t n, int64_t batch) {
+    size_t most = 0;
+    for (int o = 0; o < 2; o++) {
+        const int64_t tiles = ceil_div(o ? n : m, BM) * ceil_div(o ? m : n, 256) * batch;
+        most = std::max(most, tail_scratch_bytes(tiles, tail_plan(tiles, 1ll << 40, 1, sm_count()), 256));
+    }
+    return most;
+}
+
 template <int BN, int STAGES, int BK, bool A_MN, bool B_MN>
 static int launch_gemm(const float *ah, const float *al, const float *bh, const float *bl, float *c,
                        int64_t M, int64_t N, int64_t K, bool store_t, const Epilogue &ep, int64_t batch,
-                       bool a_bat, bool b_bat, cudaStream_t s) {
+                       bool a_bat, bool b_bat, void *tail_ws, cudaStream_t s) {
     using Q = Cfg<BN, STAGES, BK>;
     auto kernel = gemm_3xtf32_kernel<BN, STAGES, BK, A_MN, B_MN>;
     static std::mutex mu;
@@ -667,32 +755,49 @@ static int launch_gemm(const float *ah, const float *al, const float *bh, const 
     int *status = device_status_ptr();
     if (!status) return set_error(J4C_E_OOM, "no device status word");
     const int64_t tiles = ceil_div(M, BM) * ceil_div(N, BN) * batch;
-    if (tiles >= (1ll << 31)) return set_error(J4C_E_UNSUPPORTED, "dot: too many output tiles");
-    const int grid = (int)std::min<int64_t>(tiles, sm_count());
+    if (tiles >= (1ll << 30)) return set_error(J4C_E_UNSUPPORTED, "dot: too many output tiles");
+    const int64_t num_kb = ceil_div(K, BK);
+    const TailPlan tp = tail_plan(tiles, num_kb, Q::CHUNK_KB, sm_count());
+    const int64_t units = tp.full_tiles + (tiles - tp.full_tiles) * tp.splits;
+    const int grid = (int)std::min<int64_t>(units, sm_count());
     const int vec = (N % 4 == 0) && aligned16(c) && (!ep.bias || aligned16(ep.bias)) &&
                     (!ep.mask || aligned16(ep.mask)) && (!ep.act || aligned16(ep.act));
-    kernel<<<grid, kThreads, Q::SMEM_BYTES, s>>>(mAh, mAl, mBh, mBl, c, (int)M, (int)N, (int)ceil_div(K, BK),
+    float *part = nullptr;
+    int *arrivals = nullptr;
+    void *owned = nullptr;
+    if (tp.splits > 1) {
+        const size_t bytes = tail_scratch_bytes(tiles, tp, BN);
+        if (!tail_ws) {
+            if ((rc = scratch_alloc(bytes, &owned, s))) return rc;
+            tail_ws = owned;
+        }
+        part = static_cast<float *>(tail_ws);
+        arrivals = reinterpret_cast<int *>(part + (tiles - tp.full_tiles) * tp.splits * BM * BN);
+        J4C_CUDA(cudaMemsetAsync(arrivals, 0, (size_t)((tiles - tp.full_tiles) * kEpiWarps) * sizeof(int), s));
+    }
+    kernel<<<grid, kThreads, Q::SMEM_BYTES, s>>>(mAh, mAl, mBh, mBl, c, (int)M, (int)N, (int)num_kb,
                                                  store_t ? 0 : vec, store_t ? 1 : 0, ep, (int)batch, a_bat ? 1 : 0,
-                                                 b_bat ? 1 : 0, status);
+                                                 b_bat ? 1 : 0, status, (int)tp.full_tiles, tp.splits, part, arrivals);
     J4C_LAUNCH_CHECK("gemm_3xtf32_kernel");
+    if (owned) return scratch_free(owned, s);
     return J4C_OK;
 }
 
 template <int BN, int STAGES, int BK>
 static int launch_gemm_any(const float *ah, const float *al, const float *bh, const float *bl, float *c,
                            int64_t M, int64_t N, int64_t K, bool a_mn, bool b_mn, const Epilogue &ep,
-                           int64_t batch, bool a_bat, bool b_bat, cudaStream_t s) {
+                           int64_t batch, bool a_bat, bool b_bat, void *tail_ws, cudaStream_t s) {
     if (!a_mn && !b_mn)
-        return launch_gemm<BN, STAGES, BK, false, false>(ah, al, bh, bl, c, M, N, K, false, ep, batch, a_bat, b_bat, s);
+        return launch_gemm<BN, STAGES, BK, false, false>(ah, al, bh, bl, c, M, N, K, false, ep, batch, a_bat, b_bat, tail_ws, s);
     if (a_mn && !b_mn)
-        return launch_gemm<BN, STAGES, BK, true, false>(ah, al, bh, bl, c, M, N, K, false, ep, batch, a_bat, b_bat, s);
+        return launch_gemm<BN, STAGES, BK, true, false>(ah, al, bh, bl, c, M, N, K, false, ep, batch, a_bat, b_bat, tail_ws, s);
     // The wide (BN = 256) operand is read MN-major at a smem cost that
     // throttles the tensor pipe, so a K-major A with an MN-major B runs as
     // C^T = op(B)^T . op(A)^T: B's split becomes the (MN-major) A operand,
     // A's the (K-major) B operand, and the epilogue stores transposed.
     if (!a_mn && b_mn)
-        return launch_gemm<BN, STAGES, BK, true, false>(bh, bl, ah, al, c, N, M, K, true, ep, batch, b_bat, a_bat, s);
-    return launch_gemm<BN, STAGES, BK, true, true>(ah, al, bh, bl, c, M, N, K, false, ep, batch, a_bat, b_bat, s);
+        return launch_gemm<BN, STAGES, BK, true, false>(bh, bl, ah, al, c, N, M, K, true, ep, batch, b_bat, a_bat, tail_ws, s);
+    return launch_gemm<BN, STAGES, BK, true, true>(ah, al, bh, bl, c, M, N, K, false, ep, batch, a_bat, b_bat, tail_ws, s);
 }
 
 int split_t(const float *src, int64_t rows, int64_t cols, float *hi, float *lo, cudaStream_t s) {
@@ -728,10 +833,11 @@ bool tc_gemm_supported(int64_t M, int64_t K, int64_t N) {
 static int64_t split_floats(int64_t rows, int64_t cols) { return 2 * rows * tc::split_pitch(cols); }
 
 int tc_gemm_workspace(int64_t M, int64_t K, int64_t N, size_t *bytes) {
-    // the larger of the two storage orders of each operand
+    // the larger of the two storage orders of each operand, then the scratch
+    // of a tail split (256-byte aligned)
     const int64_t a = std::max(split_floats(M, K), split_floats(K, M));
     const int64_t b = std::max(split_floats(K, N), split_floats(N, K));
-    *bytes = (size_t)(a + b) * sizeof(float);
+    *bytes = ceil_div((int64_t)((a + b) * sizeof(float)), 256) * 256 + tc::tail_scratch_bound(M, N, 1);
     return J4C_OK;
 }
 
@@ -743,9 +849,12 @@ int tc_split_f32_t(const float *x, int64_t rows, int64_t cols, float *hi, float 
     return tc::split_t(x, rows, cols, hi, lo, s);
 }
 
-int tc_gemm_presplit(const float *ah, const float *al, const float *bh, const float *bl, float *c, int64_t M,
-                     int64_t K, int64_t N, int trans_a, int trans_b, const float *bias, const float *mask,
-                     float *act, int64_t batch, int a_batched, int b_batched, cudaStream_t s) {
+// tail_ws: scratch of at least tc::tail_scratch_bound bytes, or NULL to take it
+// from the library's pool when the product splits its last wave.
+static int gemm_presplit_ws(const float *ah, const float *al, const float *bh, const float *bl, float *c, int64_t M,
+                            int64_t K, int64_t N, int trans_a, int trans_b, const float *bias, const float *mask,
+                            float *act, int64_t batch, int a_batched, int b_batched, void *tail_ws,
+                            cudaStream_t s) {
     J4C_REQUIRE(aligned16(ah) && aligned16(al) && aligned16(bh) && aligned16(bl),
                 "dot: split operands must be 16-byte aligned");
     // op(A) = A [M,K] is read K-major; A^T (A stored [K,M]) MN-major.
@@ -758,8 +867,15 @@ int tc_gemm_presplit(const float *ah, const float *al, const float *bh, const fl
     const tc::Epilogue ep{bias, mask, act};
     const bool ab = a_batched != 0, bb = b_batched != 0;
     if (variant == 0)
-        return tc::launch_gemm_any<256, 2, 32>(ah, al, bh, bl, c, M, N, K, a_mn, b_mn, ep, batch, ab, bb, s);
-    return tc::launch_gemm_any<256, 4, 16>(ah, al, bh, bl, c, M, N, K, a_mn, b_mn, ep, batch, ab, bb, s);
+        return tc::launch_gemm_any<256, 2, 32>(ah, al, bh, bl, c, M, N, K, a_mn, b_mn, ep, batch, ab, bb, tail_ws, s);
+    return tc::launch_gemm_any<256, 4, 16>(ah, al, bh, bl, c, M, N, K, a_mn, b_mn, ep, batch, ab, bb, tail_ws, s);
+}
+
+int tc_gemm_presplit(const float *ah, const float *al, const float *bh, const float *bl, float *c, int64_t M,
+                     int64_t K, int64_t N, int trans_a, int trans_b, const float *bias, const float *mask,
+                     float *act, int64_t batch, int a_batched, int b_batched, cudaStream_t s) {
+    return gemm_presplit_ws(ah, al, bh, bl, c, M, K, N, trans_a, trans_b, bias, mask, act, batch, a_batched,
+                            b_batched, nullptr, s);
 }
 
 int tc_gemm_f32(const float *a, const float *b, float *c, int64_t M, int64_t K, int64_t N,
@@ -772,15 +888,20 @@ int tc_gemm_f32(const float *a, const float *b, float *c, int64_t M, int64_t K, 
     float *bh = al + ar * tc::split_pitch(ac);
     const bool b_transposed = trans_a && !trans_b;  // B is split as B^T: [bc, pitch(br)]
     float *bl = bh + (b_transposed ? bc * tc::split_pitch(br) : br * tc::split_pitch(bc));
+    // the tail-split scratch follows the largest layout of both splits
+    const int64_t a_fl = std::max(split_floats(M, K), split_floats(K, M));
+    const int64_t b_fl = std::max(split_floats(K, N), split_floats(N, K));
+    void *tail_ws = static_cast<char *>(ws) + ceil_div((int64_t)((a_fl + b_fl) * sizeof(float)), 256) * 256;
     int rc;
     if ((rc = tc::split(a, ar, ac, ah, al, s))) return rc;
     if (b_transposed) {
         // both stored K-leading: B goes in as the split of B^T (K-major)
         if ((rc = tc::split_t(b, br, bc, bh, bl, s))) return rc;
-        return tc_gemm_presplit(ah, al, bh, bl, c, M, K, N, trans_a, 1, nullptr, nullptr, nullptr, 1, 0, 0, s);
+        return gemm_presplit_ws(ah, al, bh, bl, c, M, K, N, trans_a, 1, nullptr, nullptr, nullptr, 1, 0, 0, tail_ws, s);
     }
     if ((rc = tc::split(b, br, bc, bh, bl, s))) return rc;
-    return tc_gemm_presplit(ah, al, bh, bl, c, M, K, N, trans_a, trans_b, nullptr, nullptr, nullptr, 1, 0, 0, s);
+    return gemm_presplit_ws(ah, al, bh, bl, c, M, K, N, trans_a, trans_b, nullptr, nullptr, nullptr, 1, 0, 0, tail_ws,
+                            s);
 }
 
 }  // namespace j4c
