@@ -771,12 +771,13 @@ def dot_supports_epilogue(a: "ConcreteNDArray") -> bool:
 
 def _dot_raw(a: "ConcreteNDArray", b: "ConcreteNDArray", trans_a: bool, trans_b: bool,
              device: Device, bias: "ConcreteNDArray" = None, mask: "ConcreteNDArray" = None,
-             act: bool = False):
+             act: bool = False, store_c: bool = True):
     """C = op(A) . op(B) on the tensor cores; op = transpose when flagged.
 
     FLOAT32 only, optional epilogue (j4c_dot_split_ep): C += bias (a [N]
     vector), C = mask > 0 ? C : 0 (mask [M, N]), and with act=True also
-    returns relu(C); the result is then (C, relu(C))."""
+    returns relu(C); the result is then (C, relu(C)), or (None, relu(C)) with
+    store_c=False (C itself is not written)."""
     ad, bd = a._shape.dimensions(), b._shape.dimensions()
     if len(ad) != 2 or len(bd) != 2:
         raise IllegalArgumentException(f"dot requires 2-D operands, got {a._shape} and {b._shape}")
@@ -792,7 +793,9 @@ def _dot_raw(a: "ConcreteNDArray", b: "ConcreteNDArray", trans_a: bool, trans_b:
             raise IllegalArgumentException(f"dot epilogue: bias {bias._shape} does not match N = {N}")
         if mask is not None and (mask._dtype != DType.FLOAT32 or mask._shape.size() != M * N):
             raise IllegalArgumentException(f"dot epilogue: mask {mask._shape} does not match [{M}, {N}]")
-    out = torch.empty(M * N, dtype=a._dtype.torch, device=a._t.device)
+    if not store_c and not (act and a._dtype == DType.FLOAT32 and M and N and K):
+        raise IllegalArgumentException("dot: C may only be skipped when the relu output is written")
+    out = torch.empty(M * N if store_c else 0, dtype=a._dtype.torch, device=a._t.device)
     act_out = torch.empty(M * N, dtype=a._dtype.torch, device=a._t.device) if act else None
     timing = DOT_TIMING
     if a._dtype == DType.FLOAT32 and M and N and K:
@@ -816,7 +819,8 @@ def _dot_raw(a: "ConcreteNDArray", b: "ConcreteNDArray", trans_a: bool, trans_b:
             ev1 = torch.cuda.Event(enable_timing=True)
             ev0.record()
         if epilogue:
-            call("j4c_dot_split_ep", ah.data_ptr(), al.data_ptr(), bh.data_ptr(), bl.data_ptr(), out.data_ptr(),
+            call("j4c_dot_split_ep", ah.data_ptr(), al.data_ptr(), bh.data_ptr(), bl.data_ptr(),
+                 out.data_ptr() if store_c else None,
                  M, K, N, int(ta), int(tb), bias.data_ptr() if bias is not None else None,
                  mask.data_ptr() if mask is not None else None,
                  act_out.data_ptr() if act_out is not None else None, a._stream())
@@ -841,7 +845,7 @@ def _dot_raw(a: "ConcreteNDArray", b: "ConcreteNDArray", trans_a: bool, trans_b:
         else:
             nbytes = a._dtype.byteSize() * (M * K + K * N + M * N)
         timing.append((ev0, ev1, 2.0 * M * N * K, nbytes))
-    c = ConcreteNDArray._wrap(out, Shape(M, N), a._dtype, device)
+    c = ConcreteNDArray._wrap(out, Shape(M, N), a._dtype, device) if store_c else None
     if act:
         return c, ConcreteNDArray._wrap(act_out, Shape(M, N), a._dtype, device)
     return c

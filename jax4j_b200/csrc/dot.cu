@@ -86,7 +86,7 @@ int j4c_dot_split_ep(const float *a_hi, const float *a_lo, const float *b_hi, co
                      const float *mask, float *act, j4c_stream stream) {
     J4C_REQUIRE(M >= 0 && K >= 0 && N >= 0, "j4c_dot_split: negative dimension");
     if (M == 0 || N == 0) return J4C_OK;
-    J4C_REQUIRE(c, "j4c_dot_split: NULL output");
+    J4C_REQUIRE(c || act, "j4c_dot_split: NULL output");
     J4C_REQUIRE(K > 0 || (!bias && !mask && !act), "j4c_dot_split_ep: K = 0 with an epilogue");
     if (K == 0) return j4c_fill(J4C_FLOAT32, c, M * N, 0.0, stream);
     J4C_REQUIRE(a_hi && a_lo && b_hi && b_lo, "j4c_dot_split: NULL operand");

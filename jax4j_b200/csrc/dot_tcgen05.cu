@@ -440,7 +440,7 @@ gemm_3xtf32_kernel(const __grid_constant__ CUtensorMap tAh, const __grid_constan
             tile_coords(t - bidx * tiles_per_batch, num_m, num_n, mt, nt);
             // this batch entry's C (and mask / act): [M, N], or [N, M] when stored transposed
             const size_t boff = (size_t)bidx * (size_t)M * (size_t)N;
-            float *const Cb = C + boff;
+            float *const Cb = C ? C + boff : nullptr;  // NULL: only the relu output is stored
             const float *const mask_b = ep.mask ? ep.mask + boff : nullptr;
             float *const act_b = ep.act ? ep.act + boff : nullptr;
             float acc[Q::COLS_PER_WARP];
@@ -509,7 +509,7 @@ gemm_3xtf32_kernel(const __grid_constant__ CUtensorMap tAh, const __grid_constan
                             const size_t idx = (size_t)(col0 + j) * (size_t)M + row;
                             float v = ep.bias ? __fadd_rn(acc[j], b) : acc[j];
                             if (mask_b) v = __ldg(mask_b + idx) > 0.0f ? v : 0.0f;
-                            Cb[idx] = v;
+                            if (Cb) Cb[idx] = v;
                             if (act_b) act_b[idx] = ep_relu(v);
                         }
                     }
@@ -530,7 +530,7 @@ gemm_3xtf32_kernel(const __grid_constant__ CUtensorMap tAh, const __grid_constan
                             x[0] = m.x > 0.0f ? x[0] : 0.0f; x[1] = m.y > 0.0f ? x[1] : 0.0f;
                             x[2] = m.z > 0.0f ? x[2] : 0.0f; x[3] = m.w > 0.0f ? x[3] : 0.0f;
                         }
-                        reinterpret_cast<float4 *>(Cb + base)[v4] = make_float4(x[0], x[1], x[2], x[3]);
+                        if (Cb) reinterpret_cast<float4 *>(Cb + base)[v4] = make_float4(x[0], x[1], x[2], x[3]);
                         if (act_b)
                             reinterpret_cast<float4 *>(act_b + base)[v4] =
                                 make_float4(ep_relu(x[0]), ep_relu(x[1]), ep_relu(x[2]), ep_relu(x[3]));
@@ -541,7 +541,7 @@ gemm_3xtf32_kernel(const __grid_constant__ CUtensorMap tAh, const __grid_constan
                         if (col0 + j < N) {
                             float v = ep.bias ? __fadd_rn(acc[j], __ldg(ep.bias + col0 + j)) : acc[j];
                             if (mask_b) v = __ldg(mask_b + base + j) > 0.0f ? v : 0.0f;
-                            Cb[base + j] = v;
+                            if (Cb) Cb[base + j] = v;
                             if (act_b) act_b[base + j] = ep_relu(v);
                         }
                     }

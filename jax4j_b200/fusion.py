@@ -43,7 +43,7 @@ OP_INPUT = -1
 # "out" = the equation's own output
 _VJP_READS = {
     P.MUL: ("in",), P.DIV: ("in",), P.EXP: ("out",), P.LOG: ("in",), P.SIN: ("in",),
-    P.COS: ("in",), P.TANH: ("out",), P.RELU: ("in",), P.SIGMOID: ("out",), P.DOT: ("in",),
+    P.COS: ("in",), P.TANH: ("out",), P.RELU: ("out",), P.SIGMOID: ("out",), P.DOT: ("in",),
     P.MAX: ("in",), P.MIN: ("in",), P.COND: ("in",), P.SCAN: ("in",),
 }
 
@@ -131,9 +131,12 @@ class DotEpilogue:
     """DOT -> ADD(bias [N]) [-> RELU]: the bias add and the relu run in the
     GEMM's store (j4c_dot_split_ep); the DOT's own output is never written."""
 
-    def __init__(self, dot, add, relu, bias):
+    def __init__(self, dot, add, relu, bias, store_sum=True):
         self.dot, self.add, self.relu, self.bias = dot, add, relu, bias
         self.inputs = [dot.inputs[0], dot.inputs[1], bias]
+        # with a relu whose input z = dot + bias is read by nothing else (relu's
+        # VJP reads its output), only the relu output is written
+        self.store_sum = store_sum
 
 
 def _dot_epilogues(jaxpr: Jaxpr) -> Dict[int, DotEpilogue]:
@@ -163,7 +166,9 @@ def _dot_epilogues(jaxpr: Jaxpr) -> Dict[int, DotEpilogue]:
                 or add.outputs[0].shape != z0.shape or pos.get(bias.id, -1) >= i):
             continue
         relu = next((e for e in uses.get(add.outputs[0].id, []) if e.primitive == P.RELU), None)
-        found[id(eq)] = DotEpilogue(eq, add, relu, bias)
+        z = add.outputs[0]
+        store_sum = relu is None or z.id in outs or len(uses.get(z.id, [])) != 1
+        found[id(eq)] = DotEpilogue(eq, add, relu, bias, store_sum)
     return found
 
 
@@ -383,9 +388,12 @@ def run_dot_epilogue(ep: DotEpilogue, values: Dict[int, NDArray]) -> None:
     if (all(isinstance(x, ConcreteNDArray) for x in (a, w, b)) and dot_supports_epilogue(a)
             and a.dtype() == w.dtype() == b.dtype() and b.tensor().device == a.tensor().device):
         dev = a._check_devices(w)
-        res = _dot_raw(a, w, False, False, dev, bias=b, act=ep.relu is not None)
+        res = _dot_raw(a, w, False, False, dev, bias=b, act=ep.relu is not None, store_c=ep.store_sum)
         if ep.relu is not None:
-            values[ep.add.outputs[0].id], values[ep.relu.outputs[0].id] = res
+            z, h = res
+            if ep.store_sum:
+                values[ep.add.outputs[0].id] = z
+            values[ep.relu.outputs[0].id] = h
         else:
             values[ep.add.outputs[0].id] = res
         return

@@ -432,9 +432,11 @@ def _merge(grads: Dict[int, NDArray], vid: int, g: NDArray) -> None:
 
 def _relu_fed_dots(jaxpr: Jaxpr, need) -> Dict[int, object]:
     """DOT equations whose first input h = relu(z) feeds nothing else: the
-    input gradient g . W^T is masked by z > 0 in the GEMM's store and
-    credited to z, so relu's own VJP (relu_grad, Grad.java:585-598) has
-    nothing left to do.  Keyed by id(dot equation) -> z."""
+    input gradient g . W^T is masked by h > 0 (the same elements as z > 0:
+    relu keeps a positive z and maps every other z, NaN included, to 0 or
+    NaN) in the GEMM's store and credited to z, so relu's own VJP
+    (relu_grad, Grad.java:585-598) has nothing left to do.  Keyed by
+    id(dot equation) -> (z, h)."""
     uses: Dict[int, int] = {}
     producer = {}
     for eq in jaxpr.equations:
@@ -452,7 +454,7 @@ def _relu_fed_dots(jaxpr: Jaxpr, need) -> Dict[int, object]:
         if (r is None or r.primitive != Primitive.RELU or uses.get(h.id) != 1 or h.id in outs
                 or h.dtype != DType.FLOAT32 or r.inputs[0].id not in need):
             continue
-        found[id(eq)] = r.inputs[0]
+        found[id(eq)] = (r.inputs[0], h)
     return found
 
 
@@ -519,11 +521,12 @@ def _process_backward_eq(eq, values, grads, need, fused_relu) -> None:
     wanted = [v.id in need for v in eq.inputs]
     if not any(wanted):
         return
-    z = fused_relu.get(id(eq))
-    if z is not None and wanted[0]:
+    zh = fused_relu.get(id(eq))
+    if zh is not None and wanted[0]:
+        z, h = zh
         g_out = materialize(g_out)
         a, b = values.get(eq.inputs[0].id), values.get(eq.inputs[1].id)
-        zv = values.get(z.id)
+        zv = values.get(h.id)  # the mask: h > 0 where z > 0
         if (isinstance(g_out, ConcreteNDArray) and isinstance(b, ConcreteNDArray) and
                 isinstance(zv, ConcreteNDArray) and g_out.dtype() == b.dtype() == zv.dtype() == DType.FLOAT32):
             # dz = (g . W^T) masked by z > 0 in one GEMM; dW as usual
@@ -662,7 +665,8 @@ def compute_vjps(p: Primitive, eq, g: ConcreteNDArray, inputs: List[NDArray], ou
         one_m = _bin(_scalar_like(1.0, t), _bin(t, t, Primitive.MUL), Primitive.SUB)
         return [_bin(g, one_m, Primitive.MUL)]
     if p == Primitive.RELU:
-        return [relu_grad(g, inputs[0])]
+        # h = relu(z) > 0 exactly where z > 0, so the output serves as the mask
+        return [relu_grad(g, out_value if out_value is not None else inputs[0])]
     if p == Primitive.SIGMOID:
         s = out_value if out_value is not None else inputs[0].sigmoid()
         one_m = _bin(_scalar_like(1.0, s), s, Primitive.SUB)
