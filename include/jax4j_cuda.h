@@ -293,6 +293,11 @@ J4C_API int j4c_split_f32(const float *x, int64_t rows, int64_t cols, float *hi,
  * this form (and its trans flag flipped). */
 J4C_API int j4c_split_f32_transposed(const float *x, int64_t rows, int64_t cols, float *hi, float *lo,
                                      j4c_stream stream);
+/* Both splits of x in one pass over it: hi/lo exactly as j4c_split_f32 and
+ * hi_t/lo_t exactly as j4c_split_f32_transposed (an output gradient that is
+ * the left operand of g . W^T and the right one of x^T . g). */
+J4C_API int j4c_split_f32_both(const float *x, int64_t rows, int64_t cols, float *hi, float *lo, float *hi_t,
+                               float *lo_t, j4c_stream stream);
 J4C_API int j4c_dot_split(const float *a_hi, const float *a_lo, const float *b_hi, const float *b_lo, float *c,
                           int64_t M, int64_t K, int64_t N, int trans_a, int trans_b, j4c_stream stream);
 /* j4c_dot_split with elementwise work fused into the store of C [M, N] (each

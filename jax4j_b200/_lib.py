@@ -81,6 +81,7 @@ SIGNATURES = {
     "j4c_split_f32_transposed": [P, I64, I64, P, P, P],
     "j4c_dot_split": [P, P, P, P, P, I64, I64, I64, I32, I32, P],
     "j4c_dot_split_ep": [P, P, P, P, P, I64, I64, I64, I32, I32, P, P, P, P],
+    "j4c_split_f32_both": [P, I64, I64, P, P, P, P, P],
     "j4c_dot_split_batched": [P, P, P, P, P, I64, I64, I64, I64, I32, I32, I32, I32, P],
     "j4c_fused_compile": [P, C.POINTER(P)],
     "j4c_fused_source": [P, I32, P, C.c_size_t, C.POINTER(C.c_size_t)],

@@ -764,6 +764,23 @@ def _tf32_split(x: "ConcreteNDArray", transposed: bool = False):
     return s
 
 
+def _tf32_split_both(x: "ConcreteNDArray") -> None:
+    """Both splits of a 2-D FLOAT32 array (stored layout and transpose) in one
+    pass over it, kept on the array; for an output gradient that is the left
+    operand of g . W^T and, transposed, the right operand of x^T . g."""
+    if x._dtype != DType.FLOAT32 or x._shape.rank() != 2 or x._split is not None or x._split_t is not None:
+        return
+    rows, cols = x._shape.dimensions()
+    if not rows or not cols:
+        return
+    n, n_t = rows * _lib.lib().j4c_split_pitch(cols), cols * _lib.lib().j4c_split_pitch(rows)
+    hi, lo = (torch.empty(max(n, 4), dtype=torch.float32, device=x._t.device) for _ in range(2))
+    hi_t, lo_t = (torch.empty(max(n_t, 4), dtype=torch.float32, device=x._t.device) for _ in range(2))
+    call("j4c_split_f32_both", x._t.data_ptr(), rows, cols, hi.data_ptr(), lo.data_ptr(), hi_t.data_ptr(),
+         lo_t.data_ptr(), x._stream())
+    x._split, x._split_t = (hi, lo), (hi_t, lo_t)
+
+
 def dot_supports_epilogue(a: "ConcreteNDArray") -> bool:
     """Whether _dot_raw can fuse a bias / relu' / relu into the product's store."""
     return a._dtype == DType.FLOAT32

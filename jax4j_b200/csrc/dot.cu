@@ -12,6 +12,8 @@ int tc_gemm_f32(const float *a, const float *b, float *c, int64_t M, int64_t K, 
 bool tc_gemm_supported(int64_t M, int64_t K, int64_t N);
 int tc_split_f32(const float *x, int64_t rows, int64_t cols, float *hi, float *lo, cudaStream_t s);
 int tc_split_f32_t(const float *x, int64_t rows, int64_t cols, float *hi, float *lo, cudaStream_t s);
+int tc_split_f32_both(const float *x, int64_t rows, int64_t cols, float *hi, float *lo, float *hi_t, float *lo_t,
+                      cudaStream_t s);
 int tc_gemm_presplit(const float *ah, const float *al, const float *bh, const float *bl, float *c, int64_t M,
                      int64_t K, int64_t N, int trans_a, int trans_b, const float *bias, const float *mask,
                      float *act, int64_t batch, int a_batched, int b_batched, cudaStream_t s);
@@ -71,6 +73,14 @@ int j4c_split_f32(const float *x, int64_t rows, int64_t cols, float *hi, float *
     if (rows == 0 || cols == 0) return J4C_OK;
     J4C_REQUIRE(x && hi && lo, "j4c_split_f32: NULL pointer");
     return tc_split_f32(x, rows, cols, hi, lo, as_stream(stream));
+}
+
+int j4c_split_f32_both(const float *x, int64_t rows, int64_t cols, float *hi, float *lo, float *hi_t,
+                       float *lo_t, j4c_stream stream) {
+    J4C_REQUIRE(rows >= 0 && cols >= 0, "j4c_split_f32_both: negative extent");
+    if (rows == 0 || cols == 0) return J4C_OK;
+    J4C_REQUIRE(x && hi && lo && hi_t && lo_t, "j4c_split_f32_both: NULL pointer");
+    return tc_split_f32_both(x, rows, cols, hi, lo, hi_t, lo_t, as_stream(stream));
 }
 
 int j4c_split_f32_transposed(const float *x, int64_t rows, int64_t cols, float *hi, float *lo,

@@ -602,9 +602,14 @@ __global__ void __launch_bounds__(256) split_kernel(const float *__restrict__ sr
 // lane reads 4 consecutive floats of an X row (16 bytes when X's rows allow)
 // and writes 4 consecutive floats of an X^T row to hi and to lo (16 bytes;
 // pitch is a multiple of 4 and the tile origin a multiple of 64).
+// With phi / plo set it also writes the split in the stored layout
+// ([rows, ppitch], zero padding), from the values it loads: both splits of
+// an operand for one read of it.
 __global__ void __launch_bounds__(256) split_t_kernel(const float *__restrict__ src, int64_t rows, int64_t cols,
                                                       int64_t pitch, int64_t tiles_c, int vec_in,
-                                                      float *__restrict__ hi, float *__restrict__ lo) {
+                                                      float *__restrict__ hi, float *__restrict__ lo,
+                                                      float *__restrict__ phi, float *__restrict__ plo,
+                                                      int64_t ppitch) {
     __shared__ float tile[64][65];
     const int64_t c0 = (blockIdx.x % tiles_c) * 64, r0 = (blockIdx.x / tiles_c) * 64;
     const int q = threadIdx.x & 15, w = threadIdx.x >> 4;  // 16 lanes per 64-float row, 16 rows per pass
@@ -624,6 +629,16 @@ __global__ void __launch_bounds__(256) split_t_kernel(const float *__restrict__ 
         }
 #pragma unroll
         for (int k = 0; k < 4; k++) tile[i][4 * q + k] = v[k];
+        if (phi && r < rows && c < ppitch) {  // columns past `cols` were loaded as zero
+            float h[4], l[4];
+#pragma unroll
+            for (int k = 0; k < 4; k++) {
+                h[k] = tf32_round(v[k]);
+                l[k] = tf32_round(v[k] - h[k]);
+            }
+            *reinterpret_cast<float4 *>(phi + r * ppitch + c) = make_float4(h[0], h[1], h[2], h[3]);
+            *reinterpret_cast<float4 *>(plo + r * ppitch + c) = make_float4(l[0], l[1], l[2], l[3]);
+        }
     }
     __syncthreads();
 #pragma unroll
@@ -800,14 +815,19 @@ static int launch_gemm_any(const float *ah, const float *al, const float *bh, co
     return launch_gemm<BN, STAGES, BK, true, true>(ah, al, bh, bl, c, M, N, K, false, ep, batch, a_bat, b_bat, tail_ws, s);
 }
 
-int split_t(const float *src, int64_t rows, int64_t cols, float *hi, float *lo, cudaStream_t s) {
+// The split of X^T, and with phi / plo also X's own split, in one pass.
+int split_t(const float *src, int64_t rows, int64_t cols, float *hi, float *lo, cudaStream_t s,
+            float *phi = nullptr, float *plo = nullptr) {
     if (rows == 0 || cols == 0) return J4C_OK;
     J4C_REQUIRE(aligned16(hi) && aligned16(lo), "split: hi/lo must be 16-byte aligned");
+    J4C_REQUIRE(!phi == !plo && (!phi || (aligned16(phi) && aligned16(plo))),
+                "split: both stored-layout outputs, 16-byte aligned");
     const int64_t pitch = split_pitch(rows);
     const int64_t tiles_c = ceil_div(cols, 64), tiles_r = ceil_div(pitch, 64);
     J4C_REQUIRE(tiles_c * tiles_r < (1ll << 31), "split: array too large");
     const int vec_in = (cols % 4 == 0) && aligned16(src);
-    split_t_kernel<<<(unsigned)(tiles_c * tiles_r), 256, 0, s>>>(src, rows, cols, pitch, tiles_c, vec_in, hi, lo);
+    split_t_kernel<<<(unsigned)(tiles_c * tiles_r), 256, 0, s>>>(src, rows, cols, pitch, tiles_c, vec_in, hi, lo,
+                                                                 phi, plo, split_pitch(cols));
     J4C_LAUNCH_CHECK("split_t_kernel");
     return J4C_OK;
 }
@@ -847,6 +867,11 @@ int tc_split_f32(const float *x, int64_t rows, int64_t cols, float *hi, float *l
 
 int tc_split_f32_t(const float *x, int64_t rows, int64_t cols, float *hi, float *lo, cudaStream_t s) {
     return tc::split_t(x, rows, cols, hi, lo, s);
+}
+
+int tc_split_f32_both(const float *x, int64_t rows, int64_t cols, float *hi, float *lo, float *hi_t, float *lo_t,
+                      cudaStream_t s) {
+    return tc::split_t(x, rows, cols, hi_t, lo_t, s, hi, lo);
 }
 
 // tail_ws: scratch of at least tc::tail_scratch_bound bytes, or NULL to take it

@@ -430,6 +430,17 @@ def _merge(grads: Dict[int, NDArray], vid: int, g: NDArray) -> None:
         grads[vid] = prev.add(g)
 
 
+def _split_g_both(g, a, want_a: bool, want_b: bool) -> None:
+    """A DOT VJP reads its output gradient g in the stored layout (g . B^T)
+    and, when A is at least as large as g, transposed (A^T . g takes the
+    smaller operand's transposed split): then both splits of g are made in
+    one pass."""
+    from .core import _tf32_split_both
+    if (want_a and want_b and isinstance(g, ConcreteNDArray) and isinstance(a, ConcreteNDArray)
+            and a.shape().size() >= g.shape().size()):
+        _tf32_split_both(g)
+
+
 def _relu_fed_dots(jaxpr: Jaxpr, need) -> Dict[int, object]:
     """DOT equations whose first input h = relu(z) feeds nothing else: the
     input gradient g . W^T is masked by h > 0 (the same elements as z > 0:
@@ -530,6 +541,7 @@ def _process_backward_eq(eq, values, grads, need, fused_relu) -> None:
         if (isinstance(g_out, ConcreteNDArray) and isinstance(b, ConcreteNDArray) and
                 isinstance(zv, ConcreteNDArray) and g_out.dtype() == b.dtype() == zv.dtype() == DType.FLOAT32):
             # dz = (g . W^T) masked by z > 0 in one GEMM; dW as usual
+            _split_g_both(g_out, a, True, wanted[1])
             _merge(grads, z.id, _dot_raw(g_out, b, False, True, g_out.device(), mask=zv))
             if wanted[1]:
                 _merge(grads, eq.inputs[1].id, _dot_raw(a, g_out, True, False, g_out.device()))
@@ -673,6 +685,7 @@ def compute_vjps(p: Primitive, eq, g: ConcreteNDArray, inputs: List[NDArray], ou
         return [_bin(g, _bin(s, one_m, Primitive.MUL), Primitive.MUL)]
     if p == Primitive.DOT:
         a, b = inputs
+        _split_g_both(g, a, want_a, want_b)
         # dA = gOut . B^T, dB = A^T . gOut (Grad.java:385-390), transposes as layout flags
         ga = _dot_raw(g, b, False, True, g.device()) if want_a else None
         gb = _dot_raw(a, g, True, False, g.device()) if want_b else None

@@ -471,3 +471,52 @@ def test_reference_dropout_gradient(J):
     g = J.JAX.grad(lambda v: J.Nn.dropout(v, key, rate, True).sum())(x).numpy()
     np.testing.assert_array_equal(g[~m], 0.0)
     np.testing.assert_allclose(g[m], 1.0 / (1.0 - rate), atol=1e-4)
+
+
+@pytest.mark.parametrize("ta,tb", [(0, 0), (1, 0), (0, 1), (1, 1)])
+@pytest.mark.parametrize("M,K,N", [(512, 1024, 1024), (4096, 1024, 4096), (300, 1100, 257)])
+def test_dot_tail_split_shapes(J, ta, tb, M, K, N):
+    """Products whose last wave of output tiles is cut along K (16 tiles into
+    4 parts, 512 tiles' last 68 into 2, a ragged 6-tile product into 4):
+    within the dot tolerance of the float64 product, and the bias / relu /
+    relu' epilogues, applied once the parts are added, equal the unfused
+    sequence bit for bit."""
+    from jax4j_b200 import grad as G
+    from jax4j_b200.core import _dot_raw
+    r = rng(M + K + N + 5 * ta + 7 * tb)
+    A = r.uniform(-1, 1, (M, K)).astype(np.float32)
+    B = r.uniform(-1, 1, (K, N)).astype(np.float32)
+    a = dev(J, A.T.copy() if ta else A)
+    b = dev(J, B.T.copy() if tb else B)
+    bias = dev(J, r.uniform(-1, 1, N).astype(np.float32))
+    mask = dev(J, r.integers(-1, 2, (M, N)).astype(np.float32))
+    plain = _dot_raw(a, b, bool(ta), bool(tb), a.device())
+    assert_rel(plain.numpy(), (A.astype(np.float64) @ B.astype(np.float64)).astype(np.float32), TOL_REDUCTION)
+    again = _dot_raw(a, b, bool(ta), bool(tb), a.device())
+    np.testing.assert_array_equal(again.numpy(), plain.numpy())  # deterministic
+    z, h = _dot_raw(a, b, bool(ta), bool(tb), a.device(), bias=bias, act=True)
+    np.testing.assert_array_equal(z.numpy(), plain.add(bias).numpy())
+    np.testing.assert_array_equal(h.numpy(), plain.add(bias).relu().numpy())
+    _, h_only = _dot_raw(a, b, bool(ta), bool(tb), a.device(), bias=bias, act=True, store_c=False)
+    np.testing.assert_array_equal(h_only.numpy(), h.numpy())
+    masked = _dot_raw(a, b, bool(ta), bool(tb), a.device(), mask=mask)
+    np.testing.assert_array_equal(masked.numpy(), G.relu_grad(plain, mask).numpy())
+
+
+@pytest.mark.parametrize("rows,cols", [(1, 1), (3, 5), (64, 64), (130, 257), (8192, 1000), (1000, 4096)])
+def test_split_f32_both_equals_the_two_passes(J, rows, cols):
+    """j4c_split_f32_both writes exactly what j4c_split_f32 and
+    j4c_split_f32_transposed write, padding included."""
+    import torch
+    r = rng(rows * 5 + cols)
+    a = dev(J, r.standard_normal((rows, cols)).astype(np.float32))
+    pc, pr = _lib.lib().j4c_split_pitch(cols), _lib.lib().j4c_split_pitch(rows)
+    d = a.tensor().device
+    out = [torch.full((n,), 7.0, dtype=torch.float32, device=d) for n in (rows * pc, rows * pc, cols * pr, cols * pr)]
+    ref = [torch.full((n,), 9.0, dtype=torch.float32, device=d) for n in (rows * pc, rows * pc, cols * pr, cols * pr)]
+    _lib.call("j4c_split_f32_both", a.data_ptr(), rows, cols, *[t.data_ptr() for t in out], a._stream())
+    _lib.call("j4c_split_f32", a.data_ptr(), rows, cols, ref[0].data_ptr(), ref[1].data_ptr(), a._stream())
+    _lib.call("j4c_split_f32_transposed", a.data_ptr(), rows, cols, ref[2].data_ptr(), ref[3].data_ptr(),
+              a._stream())
+    for o, e in zip(out, ref):
+        assert torch.equal(o, e)
