@@ -307,6 +307,7 @@ J4C_API int j4c_dot_split(const float *a_hi, const float *a_lo, const float *b_h
  *   C = mask > 0 ? C : 0          mask [M, N] -- relu' (api/Grad.java:585-598)
  *                                 applied to an input gradient
  *   act = max(0, C)               act [M, N] -- the layer's relu output
+ * c may be NULL when act is given (only the relu output is stored).
  * Each value is rounded exactly as the separate add / relu / relu' kernels
  * round it, so results equal the unfused sequence bit for bit. */
 /* Strided-batched j4c_dot_split (vmap's batched dot, api/Vmap.java:269-297):
