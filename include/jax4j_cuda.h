@@ -324,6 +324,32 @@ J4C_API int j4c_dot_split_ep(const float *a_hi, const float *a_lo, const float *
                              const float *bias, const float *mask, float *act, j4c_stream stream);
 
 /* ------------------------------------------------------------------ */
+/* Discrete Fourier transforms: replace api/Fft.java's radix-2 host     */
+/* transforms (Fft.java:292-371) and its per-call TornadoVM cuFFT path  */
+/* (Fft.java:760-1100).  A complex signal is two arrays (real, imag)    */
+/* as in the reference; rank 1 (a vector) or 3 (an N0 x N1 x N2 grid);  */
+/* every extent a power of two (J4C_E_INVALID otherwise); FLOAT32 or    */
+/* FLOAT64, outputs of the input's dtype, caller-allocated.             */
+/* ------------------------------------------------------------------ */
+/* Fft.fft / ifft / fft3 / ifft3 (Fft.java:64-80, 405-418): every axis;
+ * the inverse scales by 1/N. */
+J4C_API int j4c_fft(int dtype, int rank, const int64_t *dims, const void *re, const void *im, void *out_re,
+                    void *out_im, int inverse, j4c_stream stream);
+/* Fft.rfft / rfft3 (Fft.java:93-127, 423-492): real x with extents `dims`
+ * -> the half spectrum [.., dims[rank-1]/2 + 1] (real and imaginary parts). */
+J4C_API int j4c_rfft(int dtype, int rank, const int64_t *dims, const void *x, void *out_re, void *out_im,
+                     j4c_stream stream);
+/* Fft.irfft / irfft3 (Fft.java:130-186, 494-568): half spectrum
+ * [.., dims[rank-1]/2 + 1] -> real signal with extents `dims`
+ * (dims[rank-1] >= 2); the imaginary parts of the DC and Nyquist bins are
+ * ignored, as the reference's Hermitian mirror ignores them. */
+J4C_API int j4c_irfft(int dtype, int rank, const int64_t *dims, const void *re, const void *im, void *out,
+                      j4c_stream stream);
+/* Fft.dctI (Fft.java:200-227): unnormalised DCT-I of n values, n = 1 or
+ * n - 1 a power of two, computed in FP64 for both dtypes. */
+J4C_API int j4c_dct1(int dtype, int64_t n, const void *x, void *out, j4c_stream stream);
+
+/* ------------------------------------------------------------------ */
 /* Fused elementwise programs: replace TornadoJitCompiler.compile       */
 /* (backend/TornadoJitCompiler.java:82-246), which runs one kernel per   */
 /* Jaxpr equation, with one generated kernel per chain.                  */

@@ -8,12 +8,12 @@ from .core import (ConcreteNDArray, Device, DType, IllegalArgumentException, Ill
                    NDArray, PRNGKey, Primitive, Shape, UnsupportedOperationException)
 from .tracing import Equation, Jaxpr, Tracer, TracedNDArray, Var
 from .pytree import PyTree, PyTrees
-from .api import JAX, Lax, Nn, Numpy, Random
+from .api import Fft, JAX, Lax, Nn, Numpy, Random
 from .pmap import CollectiveError, LocalShard, PmapContext
 from ._lib import J4CError, J4CTimeout
 
 __all__ = ["ConcreteNDArray", "Device", "DType", "NDArray", "PRNGKey", "Primitive", "Shape",
            "IllegalArgumentException", "IllegalStateException", "UnsupportedOperationException",
            "Equation", "Jaxpr", "Tracer", "TracedNDArray", "Var", "PyTree", "PyTrees", "JAX", "Lax",
-           "Nn", "Numpy", "Random", "CollectiveError", "LocalShard", "PmapContext", "J4CError",
+           "Nn", "Numpy", "Random", "Fft", "CollectiveError", "LocalShard", "PmapContext", "J4CError",
            "J4CTimeout"]

@@ -17,7 +17,7 @@ import torch
 
 from . import grad as _grad
 from . import pmap as _pm
-from ._lib import call
+from ._lib import call, dims as _dims
 from .core import (ConcreteNDArray, Device, DType, IllegalArgumentException, NDArray, PRNGKey,
                    Primitive, Shape, stream_of)
 from .pytree import PyTree, PyTrees
@@ -552,3 +552,184 @@ class Random:
         """Random.glorotUniform (Random.java:147-150)."""
         limit = float(np.float32(math.sqrt(6.0 / (fanIn + fanOut))))
         return Random.uniform(key, shape, -limit, limit, device, offset, count)
+
+
+# ---------------------------------------------------------------------------
+# Fft (api/Fft.java)
+# ---------------------------------------------------------------------------
+def _pow2(n: int) -> bool:
+    return n >= 1 and (n & (n - 1)) == 0
+
+
+def _fft_operand(x, who: str) -> ConcreteNDArray:
+    if not isinstance(x, ConcreteNDArray):
+        raise IllegalArgumentException(f"{who}: a concrete array is required (FFTs are not traced primitives)")
+    if x.dtype() not in (DType.FLOAT32, DType.FLOAT64):
+        raise IllegalArgumentException(f"{who} requires FLOAT32 or FLOAT64 input, got {x.dtype()}")
+    return x
+
+
+def _fft_pair(re, im, rank: int, who: str):
+    re, im = _fft_operand(re, who), _fft_operand(im, who)
+    if re.shape().rank() != rank or im.shape().rank() != rank:
+        kind = "1-D vectors" if rank == 1 else "3-D inputs"
+        raise IllegalArgumentException(f"{who} require {kind}, got shapes {re.shape()}, {im.shape()}")
+    if re.shape() != im.shape():
+        raise IllegalArgumentException(f"{who} real and imaginary parts must have the same shape: "
+                                       f"{re.shape()} vs {im.shape()}")
+    if re.dtype() != im.dtype():
+        raise IllegalArgumentException(f"{who} real and imaginary parts must share dtype: "
+                                       f"{re.dtype()} vs {im.dtype()}")
+    re._check_devices(im)
+    return re, im
+
+
+def _fft_new(like: ConcreteNDArray, shape: Shape) -> ConcreteNDArray:
+    t = torch.empty(shape.size(), dtype=like.dtype().torch, device=like.tensor().device)
+    return ConcreteNDArray._wrap(t, shape, like.dtype(), like.device())
+
+
+def _fft_complex(re, im, inverse: bool, rank: int) -> List[ConcreteNDArray]:
+    who = "fft/ifft" if rank == 1 else "fft3/ifft3"
+    re, im = _fft_pair(re, im, rank, who)
+    d = re.shape().dimensions()
+    if not all(_pow2(n) for n in d):
+        what = "length" if rank == 1 else "dimensions"
+        raise IllegalArgumentException(f"{who} {what} must be {'a power' if rank == 1 else 'powers'} of two, "
+                                       f"got {re.shape()}")
+    ore, oim = _fft_new(re, re.shape()), _fft_new(re, re.shape())
+    call("j4c_fft", re.dtype().ordinal, rank, _dims(d), re.data_ptr(), im.data_ptr(), ore.data_ptr(),
+         oim.data_ptr(), int(inverse), re._stream())
+    return [ore, oim]
+
+
+def _rfft(x, rank: int) -> List[ConcreteNDArray]:
+    who = "rfft" if rank == 1 else "rfft3"
+    x = _fft_operand(x, who)
+    if x.shape().rank() != rank:
+        raise IllegalArgumentException(f"{who} requires a {rank}-D input, got shape {x.shape()}")
+    d = x.shape().dimensions()
+    if not all(_pow2(n) for n in d):
+        what = "length must be a power" if rank == 1 else "dimensions must be powers"
+        raise IllegalArgumentException(f"{who} {what} of two, got {d[0] if rank == 1 else x.shape()}")
+    out_shape = Shape(d[:-1] + (d[-1] // 2 + 1,))
+    ore, oim = _fft_new(x, out_shape), _fft_new(x, out_shape)
+    call("j4c_rfft", x.dtype().ordinal, rank, _dims(d), x.data_ptr(), ore.data_ptr(), oim.data_ptr(), x._stream())
+    return [ore, oim]
+
+
+def _irfft(re, im, rank: int, n_last: Optional[int] = None) -> ConcreteNDArray:
+    who = "irfft" if rank == 1 else "irfft3"
+    re, im = _fft_pair(re, im, rank, who)
+    d = re.shape().dimensions()
+    n = 2 * (d[-1] - 1) if n_last is None else n_last
+    if n < 2 or not _pow2(n) or n // 2 + 1 != d[-1]:
+        last = "N" if rank == 1 else "N3"
+        raise IllegalArgumentException(f"{who} input length implies {last} = {n}, which must be a power of two >= 2")
+    if not all(_pow2(k) for k in d[:-1]):
+        raise IllegalArgumentException(f"{who} leading dimensions must be powers of two, got {re.shape()}")
+    out_shape = Shape(d[:-1] + (n,))
+    out = _fft_new(re, out_shape)
+    call("j4c_irfft", re.dtype().ordinal, rank, _dims(out_shape.dimensions()), re.data_ptr(), im.data_ptr(),
+         out.data_ptr(), re._stream())
+    return out
+
+
+class Fft:
+    """api/Fft.java: discrete Fourier transforms, resident on the device
+    (cuFFT through j4c_fft / j4c_rfft / j4c_irfft / j4c_dct1).  A complex
+    signal is a pair (real, imaginary) of equal-shape arrays; 1-D vectors or
+    3-D grids with power-of-two extents; FLOAT32 or FLOAT64, outputs of the
+    input's dtype.  As in the reference, FFTs are numerical primitives with
+    no VJP or vmap rule.  The reference's *OnDevice entry points are the same
+    calls here (every array already lives on a GPU)."""
+
+    @staticmethod
+    def fft(re: NDArray, im: NDArray) -> List[ConcreteNDArray]:
+        """Fft.fft (Fft.java:64-67): y_k = sum_j (re_j + i im_j) exp(-2 pi i j k / N)."""
+        return _fft_complex(re, im, False, 1)
+
+    @staticmethod
+    def ifft(re: NDArray, im: NDArray) -> List[ConcreteNDArray]:
+        """Fft.ifft (Fft.java:75-78): the inverse, scaled by 1/N."""
+        return _fft_complex(re, im, True, 1)
+
+    @staticmethod
+    def rfft(x: NDArray) -> List[ConcreteNDArray]:
+        """Fft.rfft (Fft.java:93-127): the N/2 + 1 independent bins of a real signal."""
+        return _rfft(x, 1)
+
+    @staticmethod
+    def irfft(re: NDArray, im: NDArray) -> ConcreteNDArray:
+        """Fft.irfft (Fft.java:130-186): the real signal of length 2 (len(re) - 1)."""
+        return _irfft(re, im, 1)
+
+    @staticmethod
+    def dctI(x: NDArray) -> NDArray:
+        """Fft.dctI (Fft.java:200-227): unnormalised DCT-I, n = 1 or n - 1 a power of two."""
+        x = _fft_operand(x, "dctI")
+        if x.shape().rank() != 1:
+            raise IllegalArgumentException(f"dctI requires a 1-D input, got shape {x.shape()}")
+        n = x.shape().dimensions()[0]
+        if n == 1:
+            return x
+        if n < 2 or not _pow2(n - 1):
+            raise IllegalArgumentException(f"dctI requires (N - 1) to be a power of two, got N = {n}")
+        out = _fft_new(x, x.shape())
+        call("j4c_dct1", x.dtype().ordinal, n, x.data_ptr(), out.data_ptr(), x._stream())
+        return out
+
+    @staticmethod
+    def dctIRaw(x) -> np.ndarray:
+        """Fft.dctIRaw (Fft.java:237-247): host doubles in, a fresh host array
+        out (the input is never aliased nor changed)."""
+        a = np.array(x, dtype=np.float64, copy=True).reshape(-1)
+        n = a.shape[0]
+        if n == 0:
+            raise IllegalArgumentException("dctIRaw: input must be non-empty")
+        if n == 1:
+            return a
+        if not _pow2(n - 1):
+            raise IllegalArgumentException(f"dctIRaw requires (N - 1) to be a power of two, got N = {n}")
+        arr = ConcreteNDArray.of(a, Shape(n), DType.FLOAT64)
+        return Fft.dctI(arr).numpy().astype(np.float64).copy()
+
+    @staticmethod
+    def fft3(re: NDArray, im: NDArray) -> List[ConcreteNDArray]:
+        """Fft.fft3 (Fft.java:405-408): every axis of an (N1, N2, N3) grid."""
+        return _fft_complex(re, im, False, 3)
+
+    @staticmethod
+    def ifft3(re: NDArray, im: NDArray) -> List[ConcreteNDArray]:
+        """Fft.ifft3 (Fft.java:414-417)."""
+        return _fft_complex(re, im, True, 3)
+
+    @staticmethod
+    def rfft3(x: NDArray) -> List[ConcreteNDArray]:
+        """Fft.rfft3 (Fft.java:423-492): (N1, N2, N3) real -> (N1, N2, N3/2 + 1) complex."""
+        return _rfft(x, 3)
+
+    @staticmethod
+    def irfft3(re: NDArray, im: NDArray) -> ConcreteNDArray:
+        """Fft.irfft3 (Fft.java:494-568)."""
+        return _irfft(re, im, 3)
+
+    @staticmethod
+    def fftOnDevice(re: NDArray, im: NDArray, inverse: bool) -> List[ConcreteNDArray]:
+        """Fft.fftOnDevice (Fft.java:812-835)."""
+        return _fft_complex(re, im, inverse, 1)
+
+    @staticmethod
+    def fft3OnDevice(re: NDArray, im: NDArray, inverse: bool) -> List[ConcreteNDArray]:
+        """Fft.fft3OnDevice (Fft.java:1018-1036)."""
+        return _fft_complex(re, im, inverse, 3)
+
+    @staticmethod
+    def rfft3OnDevice(x: NDArray) -> List[ConcreteNDArray]:
+        """Fft.rfft3OnDevice (Fft.java:1045-1063)."""
+        return _rfft(x, 3)
+
+    @staticmethod
+    def irfft3OnDevice(re: NDArray, im: NDArray, fullN2: int) -> ConcreteNDArray:
+        """Fft.irfft3OnDevice (Fft.java:1072-1100): fullN2 is the last extent of the signal."""
+        return _irfft(re, im, 3, fullN2)

@@ -51,6 +51,10 @@ def _declare(L):
     L.orc_split.argtypes = [C.c_uint64, C.c_int, P]
     L.orc_uniform.argtypes = [C.c_uint64, CI64, C.c_float, C.c_float, P]
     L.orc_permutation.argtypes = [C.c_uint64, CI64, P]
+    L.orc_fft.argtypes = [C.c_int, C.c_int, P, P, P, C.c_int]
+    L.orc_rfft.argtypes = [C.c_int, C.c_int, P, P, P, P]
+    L.orc_irfft.argtypes = [C.c_int, C.c_int, P, P, P, P]
+    L.orc_dct1.argtypes = [C.c_int, CI64, P, P]
     L.orc_normal.argtypes = [C.c_uint64, CI64, P]
     L.orc_glorot_uniform.argtypes = [C.c_uint64, CI64, C.c_int, C.c_int, P]
     L.orc_broadcast_index.restype = CI64
@@ -361,3 +365,54 @@ def sweep(x, y, want_z: bool = False):
 
 def nproc() -> int:
     return len(os.sched_getaffinity(0))
+
+
+# ---- Fft (api/Fft.java) -------------------------------------------------------
+def _fft_dtype(a: np.ndarray) -> int:
+    if a.dtype == np.float64:
+        return F64
+    if a.dtype == np.float32:
+        return F32
+    raise TypeError(f"fft oracle: float32 or float64, got {a.dtype}")
+
+
+def _fft_dims(shape):
+    return np.asarray(shape, dtype=np.int64)
+
+
+def fft(re, im, inverse=False):
+    """Fft.fft / ifft / fft3 / ifft3 (Fft.java:64-80, 292-371, 405-418, 571-612)."""
+    re = np.ascontiguousarray(re).copy()
+    im = np.ascontiguousarray(im, dtype=re.dtype).copy()
+    d = _fft_dims(re.shape)
+    lib().orc_fft(_fft_dtype(re), re.ndim, _p(d), _p(re), _p(im), int(bool(inverse)))
+    return re, im
+
+
+def rfft(x):
+    """Fft.rfft / rfft3 (Fft.java:93-127, 423-492): the half spectrum along the last axis."""
+    x = np.ascontiguousarray(x)
+    out_shape = x.shape[:-1] + (x.shape[-1] // 2 + 1,)
+    ore, oim = np.empty(out_shape, x.dtype), np.empty(out_shape, x.dtype)
+    d = _fft_dims(x.shape)
+    lib().orc_rfft(_fft_dtype(x), x.ndim, _p(d), _p(x), _p(ore), _p(oim))
+    return ore, oim
+
+
+def irfft(re, im):
+    """Fft.irfft / irfft3 (Fft.java:130-186, 494-568): the real signal of length 2 (h - 1) on the last axis."""
+    re = np.ascontiguousarray(re)
+    im = np.ascontiguousarray(im, dtype=re.dtype)
+    shape = re.shape[:-1] + (2 * (re.shape[-1] - 1),)
+    out = np.empty(shape, re.dtype)
+    d = _fft_dims(shape)
+    lib().orc_irfft(_fft_dtype(re), re.ndim, _p(d), _p(re), _p(im), _p(out))
+    return out
+
+
+def dct1(x):
+    """Fft.dctI (Fft.java:200-227, 373-398)."""
+    x = np.ascontiguousarray(x)
+    out = np.empty_like(x)
+    lib().orc_dct1(_fft_dtype(x), x.shape[0], _p(x), _p(out))
+    return out

@@ -668,3 +668,215 @@ void orc_sweep_f32(const float *x, const float *y, int64_t rows, int64_t cols, f
         row_argmax[i] = best_idx;
     }
 }
+
+#define ORC_PI 3.14159265358979323846 /* the double nearest pi, Java's Math.PI */
+
+/* ---- Fft (api/Fft.java) ------------------------------------------------------------
+ * The reference's iterative radix-2 Cooley-Tukey, restated: a bit-reversal
+ * permutation, then stages of butterflies whose twiddle advances by the
+ * rotation w <- w * w_step, w_step = (cos, sin)(sign * 2 pi / len)
+ * (Fft.java:292-331 in FP64).  The FP32 form (Fft.java:333-371) keeps the
+ * twiddle and each butterfly's product in double and rounds every result to
+ * float; the inverse then multiplies by the float 1/n.  3-D transforms run
+ * the line transform along axis 2, then 1, then 0 (Fft.java:571-612), a
+ * line at a time. */
+static void fft_line_f64(double *re, double *im, int64_t n, int inverse) {
+    for (int64_t i = 1, j = 0; i < n; i++) {
+        int64_t bit = n >> 1;
+        for (; (j & bit) != 0; bit >>= 1) j ^= bit;
+        j ^= bit;
+        if (i < j) {
+            double t = re[i]; re[i] = re[j]; re[j] = t;
+            t = im[i]; im[i] = im[j]; im[j] = t;
+        }
+    }
+    const double sign = inverse ? 1.0 : -1.0;
+    for (int64_t len = 2; len <= n; len <<= 1) {
+        const double theta = sign * 2.0 * ORC_PI / (double)len;
+        const double sr = cos(theta), si = sin(theta);
+        const int64_t half = len >> 1;
+        for (int64_t i = 0; i < n; i += len) {
+            double wr = 1.0, wi = 0.0;
+            for (int64_t k = 0; k < half; k++) {
+                const int64_t a = i + k, b = a + half;
+                const double tr = wr * re[b] - wi * im[b];
+                const double ti = wr * im[b] + wi * re[b];
+                re[b] = re[a] - tr;
+                im[b] = im[a] - ti;
+                re[a] += tr;
+                im[a] += ti;
+                const double nr = wr * sr - wi * si, ni = wr * si + wi * sr;
+                wr = nr;
+                wi = ni;
+            }
+        }
+    }
+    if (inverse) {
+        const double inv = 1.0 / (double)n;
+        for (int64_t i = 0; i < n; i++) { re[i] *= inv; im[i] *= inv; }
+    }
+}
+
+static void fft_line_f32(float *re, float *im, int64_t n, int inverse) {
+    for (int64_t i = 1, j = 0; i < n; i++) {
+        int64_t bit = n >> 1;
+        for (; (j & bit) != 0; bit >>= 1) j ^= bit;
+        j ^= bit;
+        if (i < j) {
+            float t = re[i]; re[i] = re[j]; re[j] = t;
+            t = im[i]; im[i] = im[j]; im[j] = t;
+        }
+    }
+    const double sign = inverse ? 1.0 : -1.0;
+    for (int64_t len = 2; len <= n; len <<= 1) {
+        const double theta = sign * 2.0 * ORC_PI / (double)len;
+        const double sr = cos(theta), si = sin(theta);
+        const int64_t half = len >> 1;
+        for (int64_t i = 0; i < n; i += len) {
+            double wr = 1.0, wi = 0.0;
+            for (int64_t k = 0; k < half; k++) {
+                const int64_t a = i + k, b = a + half;
+                const double tr = wr * (double)re[b] - wi * (double)im[b];
+                const double ti = wr * (double)im[b] + wi * (double)re[b];
+                re[b] = (float)((double)re[a] - tr);
+                im[b] = (float)((double)im[a] - ti);
+                re[a] = (float)((double)re[a] + tr);
+                im[a] = (float)((double)im[a] + ti);
+                const double nr = wr * sr - wi * si, ni = wr * si + wi * sr;
+                wr = nr;
+                wi = ni;
+            }
+        }
+    }
+    if (inverse) {
+        const float inv = 1.0f / (float)n;
+        for (int64_t i = 0; i < n; i++) { re[i] *= inv; im[i] *= inv; }
+    }
+}
+
+/* One axis of a [n0, n1, n2] grid: gather each line, transform, scatter. */
+static void fft_axis(int dtype, void *re, void *im, const int64_t *d, int axis, int inverse) {
+    const int64_t n = d[axis];
+    const int64_t stride = axis == 0 ? d[1] * d[2] : axis == 1 ? d[2] : 1;
+    const int64_t lines = d[0] * d[1] * d[2] / n;
+    const size_t es = dtype == ORC_F64 ? sizeof(double) : sizeof(float);
+    char *tr = malloc(es * (size_t)n), *ti = malloc(es * (size_t)n);
+    for (int64_t l = 0; l < lines; l++) {
+        /* line l: the base index with the transformed axis at 0 */
+        int64_t base;
+        if (axis == 0) base = l;                                       /* (j, k) -> j * n2 + k */
+        else if (axis == 1) base = (l / d[2]) * d[1] * d[2] + l % d[2]; /* (i, k) */
+        else base = l * d[2];                                          /* (i, j) */
+        for (int64_t t = 0; t < n; t++) {
+            memcpy(tr + es * t, (char *)re + es * (base + t * stride), es);
+            memcpy(ti + es * t, (char *)im + es * (base + t * stride), es);
+        }
+        if (dtype == ORC_F64) fft_line_f64((double *)tr, (double *)ti, n, inverse);
+        else fft_line_f32((float *)tr, (float *)ti, n, inverse);
+        for (int64_t t = 0; t < n; t++) {
+            memcpy((char *)re + es * (base + t * stride), tr + es * t, es);
+            memcpy((char *)im + es * (base + t * stride), ti + es * t, es);
+        }
+    }
+    free(tr);
+    free(ti);
+}
+
+static void dims3(int rank, const int64_t *dims, int64_t *d) {
+    if (rank == 1) { d[0] = 1; d[1] = 1; d[2] = dims[0]; }
+    else { d[0] = dims[0]; d[1] = dims[1]; d[2] = dims[2]; }
+}
+
+void orc_fft(int dtype, int rank, const int64_t *dims, void *re, void *im, int inverse) {
+    int64_t d[3];
+    dims3(rank, dims, d);
+    for (int axis = 2; axis >= 0; axis--)
+        if (rank == 3 || axis == 2) fft_axis(dtype, re, im, d, axis, inverse);
+}
+
+/* rfft / rfft3 (Fft.java:93-127, 423-492): each row of the last axis as the
+ * complex transform of (x, 0) cut to n/2 + 1 bins, then axes 1 and 0 of the
+ * half spectrum. */
+void orc_rfft(int dtype, int rank, const int64_t *dims, const void *x, void *ore, void *oim) {
+    int64_t d[3];
+    dims3(rank, dims, d);
+    const int64_t n = d[2], h = n / 2 + 1, rows = d[0] * d[1];
+    const size_t es = dtype == ORC_F64 ? sizeof(double) : sizeof(float);
+    char *tr = calloc((size_t)n, es), *ti = calloc((size_t)n, es);
+    for (int64_t r = 0; r < rows; r++) {
+        memcpy(tr, (const char *)x + es * r * n, es * (size_t)n);
+        memset(ti, 0, es * (size_t)n);
+        if (dtype == ORC_F64) fft_line_f64((double *)tr, (double *)ti, n, 0);
+        else fft_line_f32((float *)tr, (float *)ti, n, 0);
+        memcpy((char *)ore + es * r * h, tr, es * (size_t)h);
+        memcpy((char *)oim + es * r * h, ti, es * (size_t)h);
+    }
+    free(tr);
+    free(ti);
+    if (rank == 3) {
+        const int64_t dh[3] = {d[0], d[1], h};
+        fft_axis(dtype, ore, oim, dh, 1, 0);
+        fft_axis(dtype, ore, oim, dh, 0, 0);
+    }
+}
+
+/* irfft / irfft3 (Fft.java:130-186, 494-568): inverse transforms of axes 0
+ * and 1 of the half spectrum, then per row the Hermitian mirror
+ * X[n-k] = conj(X[k]) (k = 1 .. h-2), the inverse transform and its real part. */
+void orc_irfft(int dtype, int rank, const int64_t *dims, const void *re, const void *im, void *out) {
+    int64_t d[3];
+    dims3(rank, dims, d);
+    const int64_t n = d[2], h = n / 2 + 1, rows = d[0] * d[1];
+    const size_t es = dtype == ORC_F64 ? sizeof(double) : sizeof(float);
+    char *wr = malloc(es * (size_t)(rows * h)), *wi = malloc(es * (size_t)(rows * h));
+    memcpy(wr, re, es * (size_t)(rows * h));
+    memcpy(wi, im, es * (size_t)(rows * h));
+    if (rank == 3) {
+        const int64_t dh[3] = {d[0], d[1], h};
+        fft_axis(dtype, wr, wi, dh, 0, 1);
+        fft_axis(dtype, wr, wi, dh, 1, 1);
+    }
+    char *tr = calloc((size_t)n, es), *ti = calloc((size_t)n, es);
+    for (int64_t r = 0; r < rows; r++) {
+        memset(tr, 0, es * (size_t)n);
+        memset(ti, 0, es * (size_t)n);
+        memcpy(tr, wr + es * r * h, es * (size_t)h);
+        memcpy(ti, wi + es * r * h, es * (size_t)h);
+        if (dtype == ORC_F64) {
+            double *a = (double *)tr, *b = (double *)ti;
+            for (int64_t k = 1; k < h - 1; k++) { a[n - k] = a[k]; b[n - k] = -b[k]; }
+            fft_line_f64(a, b, n, 1);
+        } else {
+            float *a = (float *)tr, *b = (float *)ti;
+            for (int64_t k = 1; k < h - 1; k++) { a[n - k] = a[k]; b[n - k] = -b[k]; }
+            fft_line_f32(a, b, n, 1);
+        }
+        memcpy((char *)out + es * r * n, tr, es * (size_t)n);
+    }
+    free(tr);
+    free(ti);
+    free(wr);
+    free(wi);
+}
+
+/* dctI (Fft.java:200-227, 373-398): the real part of the FP64 transform of
+ * [x0 .. x_{n-1}, x_{n-2} .. x1], rounded to the input dtype. */
+void orc_dct1(int dtype, int64_t n, const void *x, void *out) {
+    if (n == 1) {
+        memcpy(out, x, dtype == ORC_F64 ? sizeof(double) : sizeof(float));
+        return;
+    }
+    const int64_t m = 2 * (n - 1);
+    double *re = calloc((size_t)m, sizeof(double)), *im = calloc((size_t)m, sizeof(double));
+    for (int64_t k = 0; k < m; k++) {
+        const int64_t src = k < n ? k : m - k;
+        re[k] = dtype == ORC_F64 ? ((const double *)x)[src] : (double)((const float *)x)[src];
+    }
+    fft_line_f64(re, im, m, 0);
+    for (int64_t k = 0; k < n; k++) {
+        if (dtype == ORC_F64) ((double *)out)[k] = re[k];
+        else ((float *)out)[k] = (float)re[k];
+    }
+    free(re);
+    free(im);
+}

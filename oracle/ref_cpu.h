@@ -118,6 +118,12 @@ int orc_mlp_loss_f32(int num_layers, const int64_t *dims, int act,
 void orc_sweep_f32(const float *x, const float *y, int64_t rows, int64_t cols,
                    float *z, float *row_sum, int32_t *row_argmax);
 
+/* Fft (api/Fft.java): rank 1 or 3, power-of-two extents; in place for orc_fft. */
+void orc_fft(int dtype, int rank, const int64_t *dims, void *re, void *im, int inverse);
+void orc_rfft(int dtype, int rank, const int64_t *dims, const void *x, void *out_re, void *out_im);
+void orc_irfft(int dtype, int rank, const int64_t *dims, const void *re, const void *im, void *out);
+void orc_dct1(int dtype, int64_t n, const void *x, void *out);
+
 #ifdef __cplusplus
 }
 #endif

@@ -211,3 +211,91 @@ def test_oracle_permutation_is_a_permutation():
     assert sorted(p.tolist()) == list(range(1000))
     assert np.array_equal(p, orc.permutation(orc.split(7)[0], 1000))
     assert not np.array_equal(p, orc.permutation(orc.split(8)[0], 1000))
+
+
+# ---- Fft (T/FftTest.java): the oracle's restated radix-2 transform ----------------
+def _close(want, got, tol):
+    np.testing.assert_allclose(np.asarray(got, np.float64), np.asarray(want, np.float64), rtol=0, atol=tol)
+
+
+def test_oracle_fft_closed_forms():
+    # FftTest.java:35-70: [1, 2, 3, 4] -> [10, -2+2i, -2, -2-2i]; a constant is a delta of height n
+    re, im = o.fft(np.array([1, 2, 3, 4], np.float64), np.zeros(4))
+    _close([10, -2, -2, -2], re, 1e-12)
+    _close([0, 2, 0, -2], im, 1e-12)
+    re, im = o.fft(np.ones(16), np.zeros(16))
+    _close(np.r_[16.0, np.zeros(15)], re, 1e-10)
+    _close(np.zeros(16), im, 1e-10)
+
+
+def test_oracle_fft_round_trips_and_numpy():
+    r = np.random.default_rng(42)
+    # FftTest.java:72-110: fft -> ifft gives the signal back (FP64 1e-12, FP32 1e-4)
+    a, b = r.standard_normal(64), r.standard_normal(64)
+    _close(a, o.fft(*o.fft(a, b), inverse=True)[0], 1e-12)
+    a32, b32 = r.standard_normal(32).astype(np.float32), r.standard_normal(32).astype(np.float32)
+    back = o.fft(*o.fft(a32, b32), inverse=True)
+    _close(a32, back[0], 1e-4)
+    _close(b32, back[1], 1e-4)
+    # an independent check of the restatement: numpy's FFT in FP64
+    for n in (1, 2, 8, 1024):
+        x, y = r.standard_normal(n), r.standard_normal(n)
+        re, im = o.fft(x, y)
+        ref = np.fft.fft(x + 1j * y)
+        _close(ref.real, re, 1e-10 * n)
+        _close(ref.imag, im, 1e-10 * n)
+    g = r.standard_normal((4, 8, 16)) + 1j * r.standard_normal((4, 8, 16))
+    re, im = o.fft(g.real, g.imag)
+    ref = np.fft.fftn(g)
+    _close(ref.real, re, 1e-9)
+    _close(ref.imag, im, 1e-9)
+
+
+def test_oracle_dct1_direct_formula_and_self_inverse():
+    # FftTest.java:119-154: the direct DCT-I sum (n = 17) and DCT-I o DCT-I = 2 (n - 1) I (n = 33)
+    r = np.random.default_rng(11)
+    n = 17
+    x = r.standard_normal(n)
+    j = np.arange(1, n - 1)
+    want = np.array([x[0] + (1 if k % 2 == 0 else -1) * x[-1] + 2 * np.sum(x[1:-1] * np.cos(np.pi * j * k / (n - 1)))
+                     for k in range(n)])
+    _close(want, o.dct1(x), 1e-9)
+    x = r.standard_normal(33)
+    _close(2.0 * 32 * x, o.dct1(o.dct1(x)), 1e-9)
+    _close([3.14], o.dct1(np.array([3.14])), 1e-15)  # FftTest.java:223-229
+
+
+def test_oracle_rfft_irfft():
+    # FftTest.java:163-215: rfft equals the first n/2 + 1 bins of fft; irfft inverts it
+    r = np.random.default_rng(5)
+    x = r.standard_normal(64)
+    fr, fi = o.fft(x, np.zeros(64))
+    hr, hi = o.rfft(x)
+    assert hr.shape == (33,)
+    _close(fr[:33], hr, 1e-12)
+    _close(fi[:33], hi, 1e-12)
+    _close(x, o.irfft(hr, hi), 1e-12)
+    x32 = r.standard_normal(128).astype(np.float32)
+    _close(x32, o.irfft(*o.rfft(x32)), 1e-4)
+    # the imaginary parts of the DC and Nyquist bins do not reach the real signal
+    hr2, hi2 = hr.copy(), hi.copy()
+    hi2[0], hi2[-1] = 5.0, -7.0
+    _close(o.irfft(hr, hi), o.irfft(hr2, hi2), 1e-12)
+
+
+def test_oracle_3d_round_trips():
+    # FftTest.java:293-355: fft3 / ifft3 and rfft3 / irfft3 round trips
+    r = np.random.default_rng(9)
+    a, b = r.standard_normal((4, 8, 16)), r.standard_normal((4, 8, 16))
+    back = o.fft(*o.fft(a, b), inverse=True)
+    _close(a, back[0], 1e-10)
+    _close(b, back[1], 1e-10)
+    x = r.standard_normal((8, 4, 16))
+    hr, hi = o.rfft(x)
+    assert hr.shape == (8, 4, 9)
+    ref = np.fft.rfftn(x)
+    _close(ref.real, hr, 1e-9)
+    _close(ref.imag, hi, 1e-9)
+    _close(x, o.irfft(hr, hi), 1e-10)
+    x32 = r.standard_normal((4, 4, 8)).astype(np.float32)
+    _close(x32, o.irfft(*o.rfft(x32)), 1e-3)
