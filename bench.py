@@ -57,7 +57,7 @@ def parse():
     p.add_argument("--no-cpu-baseline", action="store_true")
     p.add_argument("--no-e2e", action="store_true")
     p.add_argument("--no-graph", action="store_true", help="time the eager step only (no CUDA graph)")
-    p.add_argument("--workload", default="dp_step", choices=["dp_step", "gemm", "sweep", "cfg0", "cfg2", "collectives", "fft"],
+    p.add_argument("--workload", default="dp_step", choices=["dp_step", "gemm", "sweep", "cfg0", "cfg2", "collectives", "fft", "linalg"],
                    help="dp_step is the headline; gemm/sweep are single-kernel measurements "
                         "used for profiling")
     p.add_argument("--m", type=int, default=8192)
@@ -685,6 +685,82 @@ def run_fft(args):
                                                  "for 256^3 scaled by N log N"}}), flush=True)
 
 
+B200_FP64_NOMINAL_TFLOPS = 40.0  # dense FP64 (tensor core) datasheet figure; no measured FP64 peak exists
+
+
+def run_linalg(args):
+    """Linalg on the device: Linalg.lu + LU.solve of an 8192 x 8192 FLOAT64
+    system (a 512 MB matrix, above the 126 MB L2), then Linalg.cond, eig and
+    svd at sizes the host algorithms take seconds on.  The factorisation is
+    FP64 tensor-bound: 2/3 n^3 flops against the nominal FP64 peak.  e2e
+    runs the same lu + solve from pinned host memory with the solution read
+    back.  The oracle's restatement of the reference's unblocked elimination
+    is timed beside it on n = 1024, one thread."""
+    import numpy as np
+    import torch
+    import jax4j_b200 as J
+    from oracle import oracle as orc
+    torch.cuda.set_device(0)
+    n = 8192
+    rng = np.random.default_rng(5)
+    a_host = torch.from_numpy(rng.standard_normal((n, n))).pin_memory()
+    b_host = torch.from_numpy(rng.standard_normal(n)).pin_memory()
+    A = J.ConcreteNDArray._wrap(a_host.view(-1).to("cuda"), J.Shape(n, n), J.DType.FLOAT64,
+                                J.Device.defaultDevice())
+    b = J.ConcreteNDArray._wrap(b_host.to("cuda"), J.Shape(n), J.DType.FLOAT64, J.Device.defaultDevice())
+
+    def step():
+        return J.Linalg.lu(A).solve(b)
+
+    flops = 2.0 / 3.0 * n ** 3 + 2.0 * n * n
+    ms = _timed(step, args.steps, args.warmup, 1)
+    x = step().numpy()
+    resid = float(np.abs(a_host.numpy() @ x - b_host.numpy()).max())
+
+    dev = torch.device("cuda")
+    x_host = torch.empty(n, dtype=torch.float64).pin_memory()
+
+    def e2e_step():
+        ad = a_host.view(-1).to(dev, non_blocking=True)
+        bd = b_host.to(dev, non_blocking=True)
+        Ad = J.ConcreteNDArray._wrap(ad, J.Shape(n, n), J.DType.FLOAT64, J.Device.defaultDevice())
+        bb = J.ConcreteNDArray._wrap(bd, J.Shape(n), J.DType.FLOAT64, J.Device.defaultDevice())
+        x_host.copy_(J.Linalg.lu(Ad).solve(bb).tensor(), non_blocking=True)
+
+    e2e_ms = _timed(e2e_step, args.steps, args.warmup, 1)
+    lu8 = J.Linalg.lu(A)
+    cond_ms = _timed(lambda: J.Linalg.cond(lu8), 3, 1, 1)
+    others = {"cond_hager_n8192_ms": cond_ms}
+    m1 = J.ConcreteNDArray.of(rng.standard_normal((1024, 1024)), J.Shape(1024, 1024), J.DType.FLOAT64)
+    others["eig_n1024_ms"] = _timed(lambda: J.Linalg.eig(m1), 2, 1, 1)
+    m2 = J.ConcreteNDArray.of(rng.standard_normal((2048, 1024)), J.Shape(2048, 1024), J.DType.FLOAT64)
+    others["svd_2048x1024_ms"] = _timed(lambda: J.Linalg.svd(m2), 2, 1, 1)
+
+    nc = 1024
+    ac = rng.standard_normal((nc, nc))
+    t0 = time.perf_counter()
+    st, lu_c, piv_c, _, _, _ = orc.lu_factor(ac)
+    orc.lu_solve(lu_c, piv_c, rng.standard_normal(nc))
+    cpu_s = time.perf_counter() - t0
+    cpu_gflops = (2.0 / 3.0 * nc ** 3 + 2.0 * nc * nc) / cpu_s / 1e9
+    achieved = flops / (ms / 1e3) / 1e12
+    print(json.dumps({
+        "metric": "lu + solve FP64 GFLOP/s (2/3 n^3 + 2 n^2)", "value": flops / (ms / 1e3) / 1e9, "unit": "GFLOP/s",
+        "n_gpus": 1, "steps": args.steps, "warmup": args.warmup, "ms_per_step": ms, "higher_is_better": True,
+        "dtype": "f64", "data": "synthetic N(0,1) matrix and right-hand side",
+        "config": {"workload": "Linalg.lu + LU.solve, n = 8192 FLOAT64 (512 MB matrix, above L2)"},
+        "max_abs_residual": resid,
+        "e2e": {"value": flops / (e2e_ms / 1e3) / 1e9, "unit": "GFLOP/s", "ms_per_step": e2e_ms,
+                "h2d_bytes_per_step": 8 * (n * n + n), "d2h_bytes_per_step": 8 * n},
+        "roofline": {"bound": "tensor", "achieved": achieved, "peak": B200_FP64_NOMINAL_TFLOPS,
+                     "unit": "TFLOP/s", "frac": achieved / B200_FP64_NOMINAL_TFLOPS,
+                     "peak_source": "nominal B200 dense FP64 (no measured FP64 peak)", "traffic": None},
+        "other_ops": others,
+        "cpu_baseline": {"value": cpu_gflops, "unit": "GFLOP/s", "cores": 1, "kind": "port",
+                         "sample": f"the reference's unblocked elimination + substitution (oracle) at n = {nc}: "
+                                   f"{cpu_s * 1e3:.0f} ms"}}), flush=True)
+
+
 # ---------------------------------------------------------------------------
 # the other configurations: their own measurements (parity is in tests/)
 # ---------------------------------------------------------------------------
@@ -955,6 +1031,8 @@ def main():
         run_collectives(args)
     elif args.workload == "fft":
         run_fft(args)
+    elif args.workload == "linalg":
+        run_linalg(args)
     else:
         run_ours(args)
 

@@ -350,6 +350,45 @@ J4C_API int j4c_irfft(int dtype, int rank, const int64_t *dims, const void *re, 
 J4C_API int j4c_dct1(int dtype, int64_t n, const void *x, void *out, j4c_stream stream);
 
 /* ------------------------------------------------------------------ */
+/* Dense linear algebra: replace api/Linalg.java's host LU, solves,     */
+/* Hager condition estimate, Francis-QR eigenvalues and Golub-Kahan-    */
+/* Reinsch SVD.  Matrices are row-major FLOAT32 or FLOAT64 on the       */
+/* device; everything is computed in FP64 as in the reference.          */
+/* ------------------------------------------------------------------ */
+/* The factorisation of Linalg.luFactorInPlace (Linalg.java:1021-1085):
+ * P A = L U of the n x n matrix a, into caller-allocated device arrays lu
+ * (n*n FP64, column-major, L's unit diagonal implied) and ipiv (n int64,
+ * 1-based row swaps in elimination order).  Host outputs: pivots[k] =
+ * |U_kk| for k = 0..n-1 (elimination order, so the first k that fails a
+ * singularity check is the step at which the reference throws), norms[0] =
+ * max |a_ij| and norms[1] = max_i sum_j |a_ij| of a.  Synchronous.  A zero
+ * pivot is not an error here: the caller applies the check. */
+J4C_API int j4c_lu_factor(int dtype, int64_t n, const void *a, double *lu, int64_t *ipiv, double *pivots,
+                          double *norms, j4c_stream stream);
+/* LU.solve / LU.solveTranspose (Linalg.java:141-233): A X = B
+ * (transpose = 0) or A^T X = B (transpose = 1) against a factorisation;
+ * b and x are row-major [n, nrhs] of `dtype` (a vector when nrhs = 1). */
+J4C_API int j4c_lu_solve(int64_t n, int64_t nrhs, const double *lu, const int64_t *ipiv, int transpose, int dtype,
+                         const void *b, void *x, j4c_stream stream);
+/* Linalg.reciprocalConditionNumber (Linalg.java:1102-1153): Hager's
+ * estimate of 1 / (||A||_inf ||A^-1||_inf), inf_norm = norms[1] of the
+ * factorisation; at most 5 iterations of two solves each.  *rcond (host)
+ * is 0 when inf_norm is 0 and +inf when the estimate of ||A^-1|| is 0.
+ * Synchronous. */
+J4C_API int j4c_lu_rcond(int64_t n, const double *lu, const int64_t *ipiv, double inf_norm, double *rcond,
+                         j4c_stream stream);
+/* Linalg.eig(A) (Linalg.java:768-800): the n eigenvalues of a real square
+ * matrix, real and imaginary parts in the input's dtype; complex ones in
+ * adjacent conjugate pairs.  The order may differ from the reference's
+ * Francis-QR deflation order.  Synchronous. */
+J4C_API int j4c_eig(int dtype, int64_t n, const void *a, void *wr, void *wi, j4c_stream stream);
+/* Linalg.svd (Linalg.java:411-460): thin SVD of an m x n matrix, m >= n:
+ * u [m, n], sigma [n] (descending, non-negative) and vt [n, n], row-major
+ * FP64 for both input dtypes, as the reference returns.  Synchronous. */
+J4C_API int j4c_svd(int dtype, int64_t m, int64_t n, const void *a, double *u, double *sigma, double *vt,
+                    j4c_stream stream);
+
+/* ------------------------------------------------------------------ */
 /* Fused elementwise programs: replace TornadoJitCompiler.compile       */
 /* (backend/TornadoJitCompiler.java:82-246), which runs one kernel per   */
 /* Jaxpr equation, with one generated kernel per chain.                  */

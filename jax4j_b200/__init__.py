@@ -8,12 +8,12 @@ from .core import (ConcreteNDArray, Device, DType, IllegalArgumentException, Ill
                    NDArray, PRNGKey, Primitive, Shape, UnsupportedOperationException)
 from .tracing import Equation, Jaxpr, Tracer, TracedNDArray, Var
 from .pytree import PyTree, PyTrees
-from .api import Fft, JAX, Lax, Nn, Numpy, Random
+from .api import Fft, JAX, Lax, Linalg, Nn, Numpy, Random, SingularityCheck, Svd
 from .pmap import CollectiveError, LocalShard, PmapContext
 from ._lib import J4CError, J4CTimeout
 
 __all__ = ["ConcreteNDArray", "Device", "DType", "NDArray", "PRNGKey", "Primitive", "Shape",
            "IllegalArgumentException", "IllegalStateException", "UnsupportedOperationException",
            "Equation", "Jaxpr", "Tracer", "TracedNDArray", "Var", "PyTree", "PyTrees", "JAX", "Lax",
-           "Nn", "Numpy", "Random", "Fft", "CollectiveError", "LocalShard", "PmapContext", "J4CError",
+           "Nn", "Numpy", "Random", "Fft", "Linalg", "SingularityCheck", "Svd", "CollectiveError", "LocalShard", "PmapContext", "J4CError",
            "J4CTimeout"]

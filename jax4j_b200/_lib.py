@@ -86,6 +86,11 @@ SIGNATURES = {
     "j4c_rfft": [I32, I32, PI64, P, P, P, P],
     "j4c_irfft": [I32, I32, PI64, P, P, P, P],
     "j4c_dct1": [I32, I64, P, P, P],
+    "j4c_lu_factor": [I32, I64, P, P, P, P, P, P],
+    "j4c_lu_solve": [I64, I64, P, P, I32, I32, P, P, P],
+    "j4c_lu_rcond": [I64, P, P, C.c_double, P, P],
+    "j4c_eig": [I32, I64, P, P, P, P],
+    "j4c_svd": [I32, I64, I64, P, P, P, P, P],
     "j4c_dot_split_batched": [P, P, P, P, P, I64, I64, I64, I64, I32, I32, I32, I32, P],
     "j4c_fused_compile": [P, C.POINTER(P)],
     "j4c_fused_source": [P, I32, P, C.c_size_t, C.POINTER(C.c_size_t)],

@@ -8,6 +8,9 @@ the extra argument (pmap of several sharded inputs, grad with argnum).
 """
 from __future__ import annotations
 
+import ctypes as C
+import decimal
+import enum
 import math
 import os
 from typing import Callable, List, Optional, Sequence
@@ -733,3 +736,287 @@ class Fft:
     def irfft3OnDevice(re: NDArray, im: NDArray, fullN2: int) -> ConcreteNDArray:
         """Fft.irfft3OnDevice (Fft.java:1072-1100): fullN2 is the last extent of the signal."""
         return _irfft(re, im, 3, fullN2)
+
+
+# ---- Linalg ---------------------------------------------------------------------------
+def _jdouble(x: float) -> str:
+    """java.lang.Double.toString of x (shortest digits; E notation outside
+    [1e-3, 1e7)), for the reference's exception messages."""
+    x = float(x)
+    if x != x:
+        return "NaN"
+    if math.isinf(x):
+        return "Infinity" if x > 0 else "-Infinity"
+    if x == 0.0:
+        return "-0.0" if math.copysign(1.0, x) < 0 else "0.0"
+    if 1e-3 <= abs(x) < 1e7:
+        r = repr(x)
+        return r if "e" not in r else format(x, "f")
+    _, digits, exponent = decimal.Decimal(repr(abs(x))).normalize().as_tuple()
+    ds = "".join(map(str, digits))
+    sign = "-" if x < 0 else ""
+    return f"{sign}{ds[0]}.{ds[1:] or '0'}E{len(ds) - 1 + exponent}"
+
+
+class SingularityCheck(enum.Enum):
+    """Linalg.SingularityCheck (Linalg.java:28-70): when lu / solve reject A.
+
+    SINGULARITY_CHECK_SUBMATRIX_MAX (the default): a pivot at or below
+    1e-14 x max|a_ij| of the original matrix.
+    SINGULARITY_CHECK_RECIPROCAL_CONDITION_EST: only exact-zero pivots in
+    the elimination, then Hager's estimate of 1 / kappa_inf below 1e-14."""
+    SINGULARITY_CHECK_SUBMATRIX_MAX = 0
+    SINGULARITY_CHECK_RECIPROCAL_CONDITION_EST = 1
+
+
+_RCOND_TOL = 1e-14  # Linalg.java:1096
+
+
+class LU:
+    """Linalg.LU (Linalg.java:116-233): P A = L U of a square matrix, held on
+    the device in FP64 (column-major packed factors and the row swaps), for
+    any number of O(n^2) solves.  solve(b) of an array returns an array of
+    b's dtype; solve of host doubles returns fresh host doubles."""
+
+    def __init__(self, lu: Optional[torch.Tensor], ipiv: Optional[torch.Tensor], n: int, inf_norm: float,
+                 device: Device):
+        self._lu, self._ipiv, self._n, self._inf_norm, self._device = lu, ipiv, n, inf_norm, device
+
+    def n(self) -> int:
+        """Order of the factored matrix (Linalg.java:133)."""
+        return self._n
+
+    def _stream(self) -> int:
+        return stream_of(self._lu.device.index) if self._lu is not None else 0
+
+    def _solve_tensor(self, b: torch.Tensor, dtype: DType, nrhs: int, transpose: bool) -> torch.Tensor:
+        """X = A^-1 B (or A^-T B) for B row-major [n, nrhs] of dtype on the device."""
+        x = torch.empty_like(b)
+        if self._n:
+            call("j4c_lu_solve", self._n, nrhs, self._lu.data_ptr(), self._ipiv.data_ptr(), int(transpose),
+                 dtype.ordinal, b.data_ptr(), x.data_ptr(), self._stream())
+        return x
+
+    def solve(self, b):
+        """LU.solve (Linalg.java:141-176): A x = b."""
+        if isinstance(b, NDArray):
+            if b.shape().rank() != 1 or b.shape().dimensions()[0] != self._n:
+                raise IllegalArgumentException(
+                    f"LU.solve: b must be length-{self._n} vector, got shape {b.shape()}")
+            if b.dtype() not in (DType.FLOAT32, DType.FLOAT64):
+                raise IllegalArgumentException(f"LU.solve requires FLOAT32 or FLOAT64 RHS, got {b.dtype()}")
+            if not isinstance(b, ConcreteNDArray):
+                raise IllegalArgumentException("LU.solve: a concrete right-hand side is required")
+            t = b.tensor()
+            if self._lu is not None and t.device != self._lu.device:
+                t = t.to(self._lu.device)
+            x = self._solve_tensor(t, b.dtype(), 1, False)
+            return ConcreteNDArray._wrap(x, Shape(self._n), b.dtype(), self._device)
+        return self._solve_host(b, False)
+
+    def _solve_host(self, b, transpose: bool) -> np.ndarray:
+        a = np.array(b, dtype=np.float64, copy=True).reshape(-1)
+        if a.shape[0] != self._n:
+            who = "LU.solveTranspose" if transpose else "LU.solve"
+            raise IllegalArgumentException(f"{who}: b length must be {self._n}, got {a.shape[0]}")
+        if not self._n:
+            return a
+        t = torch.from_numpy(a).to(self._lu.device)
+        return self._solve_tensor(t, DType.FLOAT64, 1, transpose).cpu().numpy()
+
+    def solveTranspose(self, b) -> np.ndarray:
+        """LU.solveTranspose (Linalg.java:206-233): A^T x = b on host doubles."""
+        return self._solve_host(b, True)
+
+    def _rcond(self) -> float:
+        """Linalg.reciprocalConditionNumber (Linalg.java:1102-1107)."""
+        if self._inf_norm == 0.0 or not self._n:
+            return 0.0
+        out = C.c_double(0.0)
+        call("j4c_lu_rcond", self._n, self._lu.data_ptr(), self._ipiv.data_ptr(), float(self._inf_norm),
+             C.addressof(out), self._stream())
+        return out.value
+
+
+def _la_concrete(A, who: str) -> ConcreteNDArray:
+    if not isinstance(A, ConcreteNDArray):
+        raise IllegalArgumentException(f"{who}: a concrete array is required (linear algebra is not traced)")
+    return A
+
+
+def _la_square(A, who: str) -> int:
+    if A.shape().rank() != 2:
+        raise IllegalArgumentException(f"{who}: A must be 2-D, got shape {A.shape()}")
+    n = A.shape().dimensions()[0]
+    if A.shape().dimensions()[1] != n:
+        raise IllegalArgumentException(f"{who}: A must be square, got shape {A.shape()}")
+    if A.dtype() not in (DType.FLOAT32, DType.FLOAT64):
+        raise IllegalArgumentException(f"{who} requires FLOAT32 or FLOAT64, got {A.dtype()}")
+    return n
+
+
+def _lu_factor(A, check: SingularityCheck) -> LU:
+    """Linalg.factorFromNDArray + luFactorInPlace (Linalg.java:313-333,
+    1021-1085): the factorisation on the device (j4c_lu_factor), then the
+    reference's per-step checks applied to the pivots in elimination order."""
+    n = _la_square(A, "lu")
+    A = _la_concrete(A, "lu")
+    if n == 0:
+        return LU(None, None, 0, 0.0, A.device())
+    dev = A.tensor().device
+    lu = torch.empty(n * n, dtype=torch.float64, device=dev)
+    ipiv = torch.empty(n, dtype=torch.int64, device=dev)
+    pivots = np.empty(n, np.float64)
+    norms = np.zeros(2, np.float64)
+    call("j4c_lu_factor", A.dtype().ordinal, n, A.data_ptr(), lu.data_ptr(), ipiv.data_ptr(),
+         pivots.ctypes.data, norms.ctypes.data, A._stream())
+    tol = 1e-14 * norms[0] if check is SingularityCheck.SINGULARITY_CHECK_SUBMATRIX_MAX else 0.0
+    bad = np.flatnonzero((pivots == 0.0) | (pivots <= tol))
+    if bad.size:
+        k = int(bad[0])
+        if pivots[k] == 0.0:
+            raise IllegalArgumentException(f"lu: matrix is singular (column {k} has zero pivot)")
+        raise IllegalArgumentException(
+            f"lu: matrix is singular under SUBMATRIX_MAX check (pivot {_jdouble(pivots[k])} \u2264 "
+            f"{_jdouble(tol)} = 1e-14 \u00d7 \u2016A\u2016_max)")
+    return LU(lu, ipiv, n, float(norms[1]), A.device())
+
+
+class Linalg:
+    """api/Linalg.java: dense real linear algebra on the device.  cuSOLVER
+    does the O(n^3) work in FP64 for both input dtypes (the reference's own
+    precision); the reference's argument checks, singularity rules and
+    exception messages are kept.  Linear algebra is not traced: inputs are
+    concrete arrays."""
+
+    SingularityCheck = SingularityCheck
+    LU = LU
+
+    @staticmethod
+    def solve(A: NDArray, b: NDArray,
+              check: SingularityCheck = SingularityCheck.SINGULARITY_CHECK_SUBMATRIX_MAX) -> ConcreteNDArray:
+        """Linalg.solve (Linalg.java:83-98): x with A x = b, in b's dtype."""
+        if A.dtype() != b.dtype():
+            raise IllegalArgumentException(f"solve requires matching dtypes: {A.dtype()} vs {b.dtype()}")
+        return Linalg.lu(A, check).solve(b)
+
+    @staticmethod
+    def lu(A: NDArray, check: SingularityCheck = SingularityCheck.SINGULARITY_CHECK_SUBMATRIX_MAX) -> LU:
+        """Linalg.lu (Linalg.java:244-265)."""
+        f = _lu_factor(A, check)
+        if check is SingularityCheck.SINGULARITY_CHECK_RECIPROCAL_CONDITION_EST:
+            rcond = f._rcond()
+            if rcond < _RCOND_TOL:
+                raise IllegalArgumentException(
+                    f"lu: matrix is ill-conditioned (rcond \u2248 {_jdouble(rcond)} < {_jdouble(_RCOND_TOL)}, "
+                    f"so \u03ba_\u221e \u2273 {_jdouble(1.0 / _RCOND_TOL)})")
+        return f
+
+    @staticmethod
+    def cond(A) -> float:
+        """Linalg.cond (Linalg.java:279-305): Hager's estimate of
+        kappa_inf = ||A||_inf ||A^-1||_inf; +inf for a matrix the
+        factorisation rejects.  Accepts an array or an LU."""
+        if not isinstance(A, LU):
+            try:
+                A = _lu_factor(A, SingularityCheck.SINGULARITY_CHECK_RECIPROCAL_CONDITION_EST)
+            except IllegalArgumentException:
+                return math.inf
+        rcond = A._rcond()
+        if rcond == 0.0 or not math.isfinite(rcond):
+            return math.inf
+        return 1.0 / rcond
+
+    @staticmethod
+    def eig(A: NDArray, B: Optional[NDArray] = None) -> List[ConcreteNDArray]:
+        """Linalg.eig(A) (Linalg.java:768-800): [real, imag] of the n
+        eigenvalues (input dtype), complex ones in adjacent conjugate pairs.
+        Linalg.eig(A, B) (Linalg.java:345-366): the generalized eigenvalues
+        of A x = lambda B x as the eigenvalues of C = B^-1 A, formed with
+        one factorisation of B (default check) and one multi-column solve;
+        FLOAT64 results, as the reference's."""
+        if B is not None:
+            return _eig_pair(A, B)
+        if A.shape().rank() != 2:
+            raise IllegalArgumentException(f"eig: A must be 2-D, got shape {A.shape()}")
+        n = A.shape().dimensions()[0]
+        if A.shape().dimensions()[1] != n:
+            raise IllegalArgumentException(f"eig: A must be square, got shape {A.shape()}")
+        if A.dtype() not in (DType.FLOAT32, DType.FLOAT64):
+            raise IllegalArgumentException(f"eig requires FLOAT32 or FLOAT64, got {A.dtype()}")
+        A = _la_concrete(A, "eig")
+        wr, wi = _fft_new(A, Shape(n)), _fft_new(A, Shape(n))
+        if n:
+            call("j4c_eig", A.dtype().ordinal, n, A.data_ptr(), wr.data_ptr(), wi.data_ptr(), A._stream())
+        return [wr, wi]
+
+    @staticmethod
+    def svd(A: NDArray) -> "Svd":
+        """Linalg.svd (Linalg.java:411-460): thin SVD A = U diag(sigma) Vt of
+        an m x n matrix, m >= n; U [m, n], sigma [n] descending and
+        non-negative, Vt [n, n]; FLOAT64 results for both input dtypes."""
+        if A.shape().rank() != 2:
+            raise IllegalArgumentException(f"svd: A must be 2-D, got shape {A.shape()}")
+        m, n = A.shape().dimensions()
+        if m < n:
+            raise IllegalArgumentException(f"svd currently requires m >= n (thin SVD), got shape {A.shape()}")
+        if A.dtype() not in (DType.FLOAT32, DType.FLOAT64):
+            raise IllegalArgumentException(f"svd requires FLOAT32 or FLOAT64, got {A.dtype()}")
+        A = _la_concrete(A, "svd")
+        dev = A.tensor().device
+
+        def new(*shape):
+            return ConcreteNDArray._wrap(torch.empty(math.prod(shape), dtype=torch.float64, device=dev),
+                                         Shape(shape), DType.FLOAT64, A.device())
+
+        U, sigma, Vt = new(m, n), new(n), new(n, n)
+        if n:
+            call("j4c_svd", A.dtype().ordinal, m, n, A.data_ptr(), U.data_ptr(), sigma.data_ptr(), Vt.data_ptr(),
+                 A._stream())
+        return Svd(U, sigma, Vt)
+
+
+class Svd:
+    """Linalg.Svd (Linalg.java:396): the record (U, sigma, Vt)."""
+    __slots__ = ("_U", "_sigma", "_Vt")
+
+    def __init__(self, U, sigma, Vt):
+        self._U, self._sigma, self._Vt = U, sigma, Vt
+
+    def U(self) -> ConcreteNDArray:
+        return self._U
+
+    def sigma(self) -> ConcreteNDArray:
+        return self._sigma
+
+    def Vt(self) -> ConcreteNDArray:
+        return self._Vt
+
+    def __iter__(self):
+        return iter((self._U, self._sigma, self._Vt))
+
+
+Linalg.Svd = Svd
+
+
+def _eig_pair(A, B) -> List[ConcreteNDArray]:
+    """Linalg.eig(A, B) (Linalg.java:345-381)."""
+    label = "eig(A, B)"
+    if A.shape().rank() != 2 or B.shape().rank() != 2:
+        raise IllegalArgumentException(f"{label}: inputs must be 2-D")
+    n = A.shape().dimensions()[0]
+    if A.shape().dimensions()[1] != n:
+        raise IllegalArgumentException(f"{label}: A must be square")
+    if B.shape().dimensions()[0] != n or B.shape().dimensions()[1] != n:
+        raise IllegalArgumentException(f"{label}: A and B must share shape")
+    if A.dtype() != B.dtype():
+        raise IllegalArgumentException(f"eig(A, B) requires matching dtypes: {A.dtype()} vs {B.dtype()}")
+    A = _la_concrete(A, label)
+    f = Linalg.lu(B)
+    if n == 0:
+        return Linalg.eig(ConcreteNDArray.of(np.zeros((0, 0)), Shape(0, 0), DType.FLOAT64, A.device()))
+    a = A.tensor()
+    if a.device != f._lu.device:
+        a = a.to(f._lu.device)
+    c = f._solve_tensor(a.to(torch.float64), DType.FLOAT64, n, False)  # C = B^-1 A, all n columns at once
+    return Linalg.eig(ConcreteNDArray._wrap(c, Shape(n, n), DType.FLOAT64, A.device()))

@@ -25,7 +25,7 @@ ARCH = ["-gencode", "arch=compute_100a,code=sm_100a"]
 CFLAGS = ARCH + ["-O3", "-lineinfo", "-std=c++17", "-Xcompiler", "-fPIC,-fvisibility=hidden",
                  "--expt-relaxed-constexpr", "-I", os.path.join(ROOT, "include"),
                  "-DJ4C_BUILDING_LIBRARY"]
-LDFLAGS = ARCH + ["-shared", "-Xlinker", "--no-undefined", "-lnccl", "-lnvrtc", "-lcufft", "-ldl",
+LDFLAGS = ARCH + ["-shared", "-Xlinker", "--no-undefined", "-lnccl", "-lnvrtc", "-lcufft", "-lcusolver", "-ldl",
                   "-L/usr/local/cuda/lib64/stubs", "-Xlinker", "-rpath,/usr/local/cuda/lib64"]
 
 

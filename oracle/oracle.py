@@ -55,6 +55,11 @@ def _declare(L):
     L.orc_rfft.argtypes = [C.c_int, C.c_int, P, P, P, P]
     L.orc_irfft.argtypes = [C.c_int, C.c_int, P, P, P, P]
     L.orc_dct1.argtypes = [C.c_int, CI64, P, P]
+    L.orc_lu_factor.argtypes = [P, CI64, C.c_int, P, P, P, P]
+    L.orc_lu_solve.argtypes = [P, P, CI64, P, P]
+    L.orc_lu_solve_t.argtypes = [P, P, CI64, P, P]
+    L.orc_lu_rcond.restype = C.c_double
+    L.orc_lu_rcond.argtypes = [P, P, CI64, C.c_double]
     L.orc_normal.argtypes = [C.c_uint64, CI64, P]
     L.orc_glorot_uniform.argtypes = [C.c_uint64, CI64, C.c_int, C.c_int, P]
     L.orc_broadcast_index.restype = CI64
@@ -416,3 +421,37 @@ def dct1(x):
     out = np.empty_like(x)
     lib().orc_dct1(_fft_dtype(x), x.shape[0], _p(x), _p(out))
     return out
+
+
+# ---- Linalg (api/Linalg.java) ----------------------------------------------------
+LU_ZERO_PIVOT, LU_SUBMATRIX = 1, 2
+
+
+def lu_factor(a, submatrix_check: bool = True):
+    """Linalg.luFactorInPlace (Linalg.java:1021-1085) on a copy of the n x n
+    matrix `a` (computed in FP64).  Returns (status, lu, piv, norms, fail_k,
+    fail_pivot): status 0, LU_ZERO_PIVOT or LU_SUBMATRIX; lu the packed
+    row-major factors; piv[i] the original row of factored row i; norms =
+    (max |a_ij|, max row sum)."""
+    lu = np.array(a, dtype=np.float64, copy=True, order="C")
+    n = lu.shape[0]
+    piv = np.empty(n, np.int64)
+    norms = np.zeros(2, np.float64)
+    fk = np.zeros(1, np.int64)
+    fp = np.zeros(1, np.float64)
+    st = lib().orc_lu_factor(_p(lu), n, int(bool(submatrix_check)), _p(piv), _p(norms), _p(fk), _p(fp))
+    return st, lu, piv, norms, int(fk[0]), float(fp[0])
+
+
+def lu_solve(lu, piv, b, transpose: bool = False):
+    """LU.substitute / LU.solveTranspose (Linalg.java:178-232)."""
+    b = np.ascontiguousarray(b, dtype=np.float64)
+    x = np.empty_like(b)
+    f = lib().orc_lu_solve_t if transpose else lib().orc_lu_solve
+    f(_p(lu), _p(piv), lu.shape[0], _p(b), _p(x))
+    return x
+
+
+def lu_rcond(lu, piv, inf_norm: float) -> float:
+    """Linalg.reciprocalConditionNumber (Linalg.java:1102-1153): Hager's estimate."""
+    return float(lib().orc_lu_rcond(_p(lu), _p(piv), lu.shape[0], float(inf_norm)))

@@ -880,3 +880,132 @@ void orc_dct1(int dtype, int64_t n, const void *x, void *out) {
     free(re);
     free(im);
 }
+
+/* ------------------------------------------------------------------ */
+/* api/Linalg.java: LU with partial pivoting, its solves and Hager's   */
+/* condition estimate, in FP64 on row-major arrays.                    */
+/* ------------------------------------------------------------------ */
+
+/* Linalg.luFactorInPlace (Linalg.java:1021-1085).  a (n x n, row-major) is
+ * overwritten by the packed Doolittle factors; piv[i] = the row of the
+ * original matrix that row i of the factors comes from; norms[0] =
+ * max |a_ij|, norms[1] = max_i sum_j |a_ij| of the input.  Returns 0, or
+ * ORC_LU_ZERO_PIVOT / ORC_LU_SUBMATRIX with *fail_k = the elimination step
+ * and *fail_piv = the pivot magnitude there (the reference's exceptions). */
+int orc_lu_factor(double *a, int64_t n, int submatrix_check, int64_t *piv, double *norms, int64_t *fail_k,
+                  double *fail_piv) {
+    double amax = 0.0, rmax = 0.0;
+    for (int64_t i = 0; i < n * n; i++) {
+        const double v = fabs(a[i]);
+        if (v > amax) amax = v;
+    }
+    for (int64_t i = 0; i < n; i++) {
+        double row = 0.0;
+        for (int64_t j = 0; j < n; j++) row += fabs(a[i * n + j]);
+        if (row > rmax) rmax = row;
+    }
+    norms[0] = amax;
+    norms[1] = rmax;
+    const double tol = submatrix_check ? 1e-14 * amax : 0.0;
+    for (int64_t i = 0; i < n; i++) piv[i] = i;
+    for (int64_t k = 0; k < n; k++) {
+        int64_t best = k;
+        double best_abs = fabs(a[k * n + k]);
+        for (int64_t i = k + 1; i < n; i++)
+            if (fabs(a[i * n + k]) > best_abs) {
+                best_abs = fabs(a[i * n + k]);
+                best = i;
+            }
+        if (best_abs == 0.0 || best_abs <= tol) {
+            *fail_k = k;
+            *fail_piv = best_abs;
+            return best_abs == 0.0 ? ORC_LU_ZERO_PIVOT : ORC_LU_SUBMATRIX;
+        }
+        if (best != k) {
+            for (int64_t j = 0; j < n; j++) {
+                const double t = a[k * n + j];
+                a[k * n + j] = a[best * n + j];
+                a[best * n + j] = t;
+            }
+            const int64_t t = piv[k];
+            piv[k] = piv[best];
+            piv[best] = t;
+        }
+        const double inv = 1.0 / a[k * n + k];
+        for (int64_t i = k + 1; i < n; i++) {
+            const double l = a[i * n + k] * inv;
+            a[i * n + k] = l;
+            if (l == 0.0) continue;
+            for (int64_t j = k + 1; j < n; j++) a[i * n + j] -= l * a[k * n + j];
+        }
+    }
+    return 0;
+}
+
+/* LU.substitute (Linalg.java:178-197): x = A^-1 b. */
+void orc_lu_solve(const double *lu, const int64_t *piv, int64_t n, const double *b, double *x) {
+    double *y = malloc(sizeof(double) * (size_t)n);
+    for (int64_t i = 0; i < n; i++) {
+        double acc = b[piv[i]];
+        for (int64_t j = 0; j < i; j++) acc -= lu[i * n + j] * y[j];
+        y[i] = acc;
+    }
+    for (int64_t i = n - 1; i >= 0; i--) {
+        double acc = y[i];
+        for (int64_t j = i + 1; j < n; j++) acc -= lu[i * n + j] * x[j];
+        x[i] = acc / lu[i * n + i];
+    }
+    free(y);
+}
+
+/* LU.solveTranspose (Linalg.java:206-232): x = A^-T b = P^-1 L^-T U^-T b. */
+void orc_lu_solve_t(const double *lu, const int64_t *piv, int64_t n, const double *b, double *x) {
+    double *y = malloc(sizeof(double) * (size_t)n), *w = malloc(sizeof(double) * (size_t)n);
+    for (int64_t i = 0; i < n; i++) {
+        double acc = b[i];
+        for (int64_t j = 0; j < i; j++) acc -= lu[j * n + i] * y[j];
+        y[i] = acc / lu[i * n + i];
+    }
+    for (int64_t i = n - 1; i >= 0; i--) {
+        double acc = y[i];
+        for (int64_t j = i + 1; j < n; j++) acc -= lu[j * n + i] * w[j];
+        w[i] = acc;
+    }
+    for (int64_t i = 0; i < n; i++) x[piv[i]] = w[i];
+    free(y);
+    free(w);
+}
+
+/* Linalg.reciprocalConditionNumber + hagerNormInvInf (Linalg.java:1102-1153). */
+double orc_lu_rcond(const double *lu, const int64_t *piv, int64_t n, double inf_norm) {
+    if (inf_norm == 0.0) return 0.0;
+    double *x = malloc(sizeof(double) * (size_t)n), *y = malloc(sizeof(double) * (size_t)n);
+    double *xi = malloc(sizeof(double) * (size_t)n), *z = malloc(sizeof(double) * (size_t)n);
+    for (int64_t i = 0; i < n; i++) x[i] = 1.0 / (double)n;
+    double estimate = 0.0;
+    for (int iter = 0; iter < 5; iter++) {
+        orc_lu_solve_t(lu, piv, n, x, y);
+        double y1 = 0.0;
+        for (int64_t i = 0; i < n; i++) y1 += fabs(y[i]);
+        if (iter > 0 && y1 <= estimate) break;
+        estimate = y1;
+        for (int64_t i = 0; i < n; i++) xi[i] = y[i] >= 0.0 ? 1.0 : -1.0;
+        orc_lu_solve(lu, piv, n, xi, z);
+        int64_t jstar = 0;
+        double zmax = fabs(z[0]), ztx = 0.0;
+        for (int64_t i = 1; i < n; i++)
+            if (fabs(z[i]) > zmax) {
+                zmax = fabs(z[i]);
+                jstar = i;
+            }
+        for (int64_t i = 0; i < n; i++) ztx += z[i] * x[i];
+        if (zmax <= fabs(ztx)) break;
+        for (int64_t i = 0; i < n; i++) x[i] = 0.0;
+        x[jstar] = 1.0;
+    }
+    free(x);
+    free(y);
+    free(xi);
+    free(z);
+    return estimate == 0.0 ? INFINITY : 1.0 / (inf_norm * estimate);
+}

@@ -124,6 +124,15 @@ void orc_rfft(int dtype, int rank, const int64_t *dims, const void *x, void *out
 void orc_irfft(int dtype, int rank, const int64_t *dims, const void *re, const void *im, void *out);
 void orc_dct1(int dtype, int64_t n, const void *x, void *out);
 
+/* Linalg (api/Linalg.java): FP64, row-major. */
+#define ORC_LU_ZERO_PIVOT 1
+#define ORC_LU_SUBMATRIX 2
+int orc_lu_factor(double *a, int64_t n, int submatrix_check, int64_t *piv, double *norms, int64_t *fail_k,
+                  double *fail_piv);
+void orc_lu_solve(const double *lu, const int64_t *piv, int64_t n, const double *b, double *x);
+void orc_lu_solve_t(const double *lu, const int64_t *piv, int64_t n, const double *b, double *x);
+double orc_lu_rcond(const double *lu, const int64_t *piv, int64_t n, double inf_norm);
+
 #ifdef __cplusplus
 }
 #endif
