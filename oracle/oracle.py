@@ -60,6 +60,8 @@ def _declare(L):
     L.orc_lu_solve_t.argtypes = [P, P, CI64, P, P]
     L.orc_lu_rcond.restype = C.c_double
     L.orc_lu_rcond.argtypes = [P, P, CI64, C.c_double]
+    L.orc_eig.argtypes = [C.c_int, CI64, P, P, P]
+    L.orc_svd.argtypes = [C.c_int, CI64, CI64, P, P, P, P]
     L.orc_normal.argtypes = [C.c_uint64, CI64, P]
     L.orc_glorot_uniform.argtypes = [C.c_uint64, CI64, C.c_int, C.c_int, P]
     L.orc_broadcast_index.restype = CI64
@@ -455,3 +457,27 @@ def lu_solve(lu, piv, b, transpose: bool = False):
 def lu_rcond(lu, piv, inf_norm: float) -> float:
     """Linalg.reciprocalConditionNumber (Linalg.java:1102-1153): Hager's estimate."""
     return float(lib().orc_lu_rcond(_p(lu), _p(piv), lu.shape[0], float(inf_norm)))
+
+
+def eig(a):
+    """Linalg.eig(A) (Linalg.java:768-800, 815-1005): Householder reduction to
+    Hessenberg form, then Francis double-shift QR; (wr, wi) in the order the
+    eigenvalues deflate, in a's dtype.  Raises if the iteration does not
+    converge (the reference's IllegalStateException)."""
+    a = np.ascontiguousarray(a)
+    n = a.shape[0]
+    wr, wi = np.empty(n, a.dtype), np.empty(n, a.dtype)
+    if lib().orc_eig(_fft_dtype(a), n, _p(a), _p(wr), _p(wi)):
+        raise RuntimeError("eig: Francis QR failed to converge")
+    return wr, wi
+
+
+def svd(a):
+    """Linalg.svd (Linalg.java:411-460, 485-749): Golub-Kahan bidiagonalisation
+    and Golub-Reinsch QR sweeps; (U [m, n], sigma [n], Vt [n, n]) in FP64."""
+    a = np.ascontiguousarray(a)
+    m, n = a.shape
+    u, s, vt = np.empty((m, n)), np.empty(n), np.empty((n, n))
+    if lib().orc_svd(_fft_dtype(a), m, n, _p(a), _p(u), _p(s), _p(vt)):
+        raise RuntimeError("svd: QR sweep failed to converge")
+    return u, s, vt

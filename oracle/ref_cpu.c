@@ -1009,3 +1009,456 @@ double orc_lu_rcond(const double *lu, const int64_t *piv, int64_t n, double inf_
     free(z);
     return estimate == 0.0 ? INFINITY : 1.0 / (inf_norm * estimate);
 }
+
+/* java.lang.Math.max(double, double): NaN if either argument is NaN. */
+static double jmax(double a, double b) {
+    if (a != a) return a;
+    if (b != b) return b;
+    return a >= b ? a : b;
+}
+
+#define RM(M, ld, i, j) (M)[(int64_t)(i) * (ld) + (j)]
+
+/* Linalg.reduceToHessenberg (Linalg.java:815-847): Householder similarity
+ * transforms zero column k below the subdiagonal, k = 0..n-3. */
+static void hessenberg(double *H, int64_t n) {
+    double *u = calloc((size_t)n + 1, sizeof(double));
+    for (int64_t k = 0; k + 2 < n; k++) {
+        double scale = 0.0;
+        for (int64_t i = k + 1; i < n; i++) scale = jmax(scale, fabs(RM(H, n, i, k)));
+        if (scale == 0.0) continue;
+        double h = 0.0;
+        for (int64_t i = k + 1; i < n; i++) {
+            u[i] = RM(H, n, i, k) / scale;
+            h += u[i] * u[i];
+        }
+        const double f = u[k + 1];
+        const double g = f >= 0 ? -sqrt(h) : sqrt(h);
+        h -= f * g;
+        u[k + 1] = f - g;
+        for (int64_t j = k; j < n; j++) { /* from the left, rows k+1.. */
+            double acc = 0.0;
+            for (int64_t i = k + 1; i < n; i++) acc += u[i] * RM(H, n, i, j);
+            acc /= h;
+            for (int64_t i = k + 1; i < n; i++) RM(H, n, i, j) -= acc * u[i];
+        }
+        for (int64_t i = 0; i < n; i++) { /* from the right, columns k+1.. */
+            double acc = 0.0;
+            for (int64_t j = k + 1; j < n; j++) acc += u[j] * RM(H, n, i, j);
+            acc /= h;
+            for (int64_t j = k + 1; j < n; j++) RM(H, n, i, j) -= acc * u[j];
+        }
+        RM(H, n, k + 1, k) = scale * g;
+        for (int64_t i = k + 2; i < n; i++) RM(H, n, i, k) = 0.0;
+    }
+    free(u);
+}
+
+/* Linalg.francisQR (Linalg.java:856-1005): the implicit double-shift QR
+ * iteration with deflation on an upper-Hessenberg matrix (EISPACK hqr's
+ * steps), eigenvalues in the order they deflate.  Returns 1 if an
+ * eigenvalue needs more than 300 n iterations (the reference throws). */
+static int francis_qr(double *H, int64_t nn, double *wr, double *wi) {
+    const double eps = ldexp(1.0, -52);
+    int64_t n = nn - 1, iter = 0;
+    double exshift = 0.0, p = 0, q = 0, r = 0, s = 0, z = 0, w, x, y;
+    double norm = 0.0;
+    for (int64_t i = 0; i < nn; i++)
+        for (int64_t j = i > 0 ? i - 1 : 0; j < nn; j++) norm += fabs(RM(H, nn, i, j));
+    while (n >= 0) {
+        int64_t l = n;
+        for (; l > 0; l--) { /* a negligible subdiagonal entry splits the matrix */
+            s = fabs(RM(H, nn, l - 1, l - 1)) + fabs(RM(H, nn, l, l));
+            if (s == 0.0) s = norm;
+            if (fabs(RM(H, nn, l, l - 1)) < eps * s) break;
+        }
+        if (l == n) { /* a 1 x 1 block: one real eigenvalue */
+            RM(H, nn, n, n) += exshift;
+            wr[n] = RM(H, nn, n, n);
+            wi[n] = 0.0;
+            n--;
+            iter = 0;
+            continue;
+        }
+        if (l == n - 1) { /* a 2 x 2 block: a real pair or a conjugate pair */
+            w = RM(H, nn, n, n - 1) * RM(H, nn, n - 1, n);
+            p = (RM(H, nn, n - 1, n - 1) - RM(H, nn, n, n)) / 2.0;
+            q = p * p + w;
+            z = sqrt(fabs(q));
+            RM(H, nn, n, n) += exshift;
+            RM(H, nn, n - 1, n - 1) += exshift;
+            x = RM(H, nn, n, n);
+            if (q >= 0) {
+                z = p >= 0 ? p + z : p - z;
+                wr[n - 1] = x + z;
+                wr[n] = z != 0.0 ? x - w / z : wr[n - 1];
+                wi[n - 1] = wi[n] = 0.0;
+            } else {
+                wr[n - 1] = wr[n] = x + p;
+                wi[n - 1] = z;
+                wi[n] = -z;
+            }
+            n -= 2;
+            iter = 0;
+            continue;
+        }
+        /* the shift: the trailing 2 x 2 block, or the exceptional one at
+         * iterations 10 and 20 */
+        x = RM(H, nn, n, n);
+        y = RM(H, nn, n - 1, n - 1);
+        w = RM(H, nn, n, n - 1) * RM(H, nn, n - 1, n);
+        if (iter == 10 || iter == 20) {
+            exshift += x;
+            for (int64_t i = 0; i <= n; i++) RM(H, nn, i, i) -= x;
+            s = fabs(RM(H, nn, n, n - 1)) + fabs(RM(H, nn, n - 1, n - 2));
+            x = y = 0.75 * s;
+            w = -0.4375 * s * s;
+        }
+        if (++iter > 300 * nn) return 1;
+        /* where two consecutive subdiagonal entries are small enough to start the sweep */
+        int64_t m = n - 2;
+        for (;; m--) {
+            z = RM(H, nn, m, m);
+            r = x - z;
+            s = y - z;
+            p = (r * s - w) / RM(H, nn, m + 1, m) + RM(H, nn, m, m + 1);
+            q = RM(H, nn, m + 1, m + 1) - z - r - s;
+            r = RM(H, nn, m + 2, m + 1);
+            s = fabs(p) + fabs(q) + fabs(r);
+            p /= s;
+            q /= s;
+            r /= s;
+            if (m == l) break;
+            if (fabs(RM(H, nn, m, m - 1)) * (fabs(q) + fabs(r)) <
+                eps * fabs(p) * (fabs(RM(H, nn, m - 1, m - 1)) + fabs(z) + fabs(RM(H, nn, m + 1, m + 1))))
+                break;
+        }
+        for (int64_t i = m + 2; i <= n; i++) {
+            RM(H, nn, i, i - 2) = 0.0;
+            if (i > m + 2) RM(H, nn, i, i - 3) = 0.0;
+        }
+        for (int64_t k = m; k <= n - 1; k++) { /* the double-shift bulge chase */
+            const int notlast = k != n - 1;
+            if (k != m) {
+                p = RM(H, nn, k, k - 1);
+                q = RM(H, nn, k + 1, k - 1);
+                r = notlast ? RM(H, nn, k + 2, k - 1) : 0.0;
+                x = fabs(p) + fabs(q) + fabs(r);
+                if (x == 0.0) continue;
+                p /= x;
+                q /= x;
+                r /= x;
+            }
+            s = sqrt(p * p + q * q + r * r);
+            if (p < 0) s = -s;
+            if (s == 0.0) continue;
+            if (k != m) RM(H, nn, k, k - 1) = -s * x;
+            else if (l != m) RM(H, nn, k, k - 1) = -RM(H, nn, k, k - 1);
+            p += s;
+            x = p / s;
+            y = q / s;
+            z = r / s;
+            q /= p;
+            r /= p;
+            for (int64_t j = k; j < nn; j++) { /* rows k..k+2 */
+                p = RM(H, nn, k, j) + q * RM(H, nn, k + 1, j);
+                if (notlast) {
+                    p += r * RM(H, nn, k + 2, j);
+                    RM(H, nn, k + 2, j) -= p * z;
+                }
+                RM(H, nn, k, j) -= p * x;
+                RM(H, nn, k + 1, j) -= p * y;
+            }
+            const int64_t imax = n < k + 3 ? n : k + 3;
+            for (int64_t i = 0; i <= imax; i++) { /* columns k..k+2 */
+                p = x * RM(H, nn, i, k) + y * RM(H, nn, i, k + 1);
+                if (notlast) {
+                    p += z * RM(H, nn, i, k + 2);
+                    RM(H, nn, i, k + 2) -= p * r;
+                }
+                RM(H, nn, i, k) -= p;
+                RM(H, nn, i, k + 1) -= p * q;
+            }
+        }
+    }
+    return 0;
+}
+
+/* Linalg.eig(A) (Linalg.java:768-800): FP64 for both dtypes; 0 or 1 (no convergence). */
+int orc_eig(int dtype, int64_t n, const void *a, void *wr, void *wi) {
+    double *H = malloc(sizeof(double) * (size_t)(n * n + 1));
+    double *r = malloc(sizeof(double) * (size_t)(n + 1)), *im = malloc(sizeof(double) * (size_t)(n + 1));
+    for (int64_t i = 0; i < n * n; i++)
+        H[i] = dtype == ORC_F64 ? ((const double *)a)[i] : (double)((const float *)a)[i];
+    hessenberg(H, n);
+    const int rc = francis_qr(H, n, r, im);
+    for (int64_t i = 0; i < n; i++) {
+        if (dtype == ORC_F64) {
+            ((double *)wr)[i] = r[i];
+            ((double *)wi)[i] = im[i];
+        } else {
+            ((float *)wr)[i] = (float)r[i];
+            ((float *)wi)[i] = (float)im[i];
+        }
+    }
+    free(H);
+    free(r);
+    free(im);
+    return rc;
+}
+
+/* Linalg.golubKahanBidiagonalize (Linalg.java:485-583): Householder
+ * reflections from both sides bring A (m x n, m >= n) to upper-bidiagonal
+ * form (diagonal s, superdiagonal e), and U (m x n), V (n x n) accumulate
+ * them.  The published Golub-Reinsch / LINPACK dsvdc first phase. */
+static void bidiagonalize(double *A, double *U, double *V, double *s, double *e, int64_t m, int64_t n) {
+    const int64_t nct = m - 1 < n ? m - 1 : n;
+    const int64_t nrt0 = n - 2 < m ? n - 2 : m, nrt = nrt0 > 0 ? nrt0 : 0;
+    double *work = malloc(sizeof(double) * (size_t)(m + 1));
+    for (int64_t k = 0; k < (nct > nrt ? nct : nrt); k++) {
+        if (k < nct) { /* the column reflector below the diagonal */
+            double nrm = 0.0;
+            for (int64_t i = k; i < m; i++) nrm = hypot(nrm, RM(A, n, i, k));
+            if (nrm != 0.0) {
+                if (RM(A, n, k, k) < 0.0) nrm = -nrm;
+                for (int64_t i = k; i < m; i++) RM(A, n, i, k) /= nrm;
+                RM(A, n, k, k) += 1.0;
+            }
+            s[k] = -nrm;
+        }
+        for (int64_t j = k + 1; j < n; j++) {
+            if (k < nct && s[k] != 0.0) {
+                double t = 0.0;
+                for (int64_t i = k; i < m; i++) t += RM(A, n, i, k) * RM(A, n, i, j);
+                t = -t / RM(A, n, k, k);
+                for (int64_t i = k; i < m; i++) RM(A, n, i, j) += t * RM(A, n, i, k);
+            }
+            e[j] = RM(A, n, k, j);
+        }
+        if (k < nrt) { /* the row reflector right of the superdiagonal */
+            double nrm = 0.0;
+            for (int64_t i = k + 1; i < n; i++) nrm = hypot(nrm, e[i]);
+            if (nrm != 0.0) {
+                if (e[k + 1] < 0.0) nrm = -nrm;
+                for (int64_t i = k + 1; i < n; i++) e[i] /= nrm;
+                e[k + 1] += 1.0;
+            }
+            e[k] = -nrm;
+            if (k + 1 < m && e[k] != 0.0) {
+                for (int64_t i = 0; i < m; i++) work[i] = 0.0;
+                for (int64_t j = k + 1; j < n; j++)
+                    for (int64_t i = k + 1; i < m; i++) work[i] += e[j] * RM(A, n, i, j);
+                for (int64_t j = k + 1; j < n; j++) {
+                    const double t = -e[j] / e[k + 1];
+                    for (int64_t i = k + 1; i < m; i++) RM(A, n, i, j) += t * work[i];
+                }
+            }
+            for (int64_t i = k + 1; i < n; i++) RM(V, n, i, k) = e[i];
+        }
+    }
+    const int64_t p = n < m + 1 ? n : m + 1;
+    if (nct < n) s[nct] = RM(A, n, nct, nct);
+    if (m < p) s[p - 1] = 0.0;
+    if (nrt + 1 < p) e[nrt] = RM(A, n, nrt, p - 1);
+    e[p - 1] = 0.0;
+    for (int64_t j = nct; j < n; j++) { /* U: the left reflectors applied to the identity */
+        for (int64_t i = 0; i < m; i++) RM(U, n, i, j) = 0.0;
+        RM(U, n, j, j) = 1.0;
+    }
+    for (int64_t k = nct - 1; k >= 0; k--) {
+        if (s[k] != 0.0) {
+            for (int64_t j = k + 1; j < n; j++) {
+                double t = 0.0;
+                for (int64_t i = k; i < m; i++) t += RM(A, n, i, k) * RM(U, n, i, j);
+                t = -t / RM(A, n, k, k);
+                for (int64_t i = k; i < m; i++) RM(U, n, i, j) += t * RM(A, n, i, k);
+            }
+            for (int64_t i = k; i < m; i++) RM(U, n, i, k) = -RM(A, n, i, k);
+            RM(U, n, k, k) = 1.0 + RM(U, n, k, k);
+            for (int64_t i = 0; i < k - 1; i++) RM(U, n, i, k) = 0.0;
+        } else {
+            for (int64_t i = 0; i < m; i++) RM(U, n, i, k) = 0.0;
+            RM(U, n, k, k) = 1.0;
+        }
+    }
+    for (int64_t k = n - 1; k >= 0; k--) { /* V: the right reflectors */
+        if (k < nrt && e[k] != 0.0) {
+            for (int64_t j = k + 1; j < n; j++) {
+                double t = 0.0;
+                for (int64_t i = k + 1; i < n; i++) t += RM(V, n, i, k) * RM(V, n, i, j);
+                t = -t / RM(V, n, k + 1, k);
+                for (int64_t i = k + 1; i < n; i++) RM(V, n, i, j) += t * RM(V, n, i, k);
+            }
+        }
+        for (int64_t i = 0; i < n; i++) RM(V, n, i, k) = 0.0;
+        RM(V, n, k, k) = 1.0;
+    }
+    free(work);
+}
+
+/* Rotate columns (j, k) of M (rows x ld): (Mj, Mk) <- (c Mj + s Mk, -s Mj + c Mk). */
+static void rotate_cols(double *M, int64_t rows, int64_t ld, int64_t j, int64_t k, double c, double s) {
+    for (int64_t i = 0; i < rows; i++) {
+        const double x = c * RM(M, ld, i, j) + s * RM(M, ld, i, k);
+        RM(M, ld, i, k) = -s * RM(M, ld, i, j) + c * RM(M, ld, i, k);
+        RM(M, ld, i, j) = x;
+    }
+}
+
+static void swap_cols(double *M, int64_t rows, int64_t ld, int64_t j, int64_t k) {
+    for (int64_t i = 0; i < rows; i++) {
+        const double t = RM(M, ld, i, j);
+        RM(M, ld, i, j) = RM(M, ld, i, k);
+        RM(M, ld, i, k) = t;
+    }
+}
+
+/* Linalg.golubReinschDiagonalize (Linalg.java:591-749): implicit-shift QR
+ * sweeps on the bidiagonal, the four cases of the published algorithm
+ * (negligible s[p-1]; a split at a negligible s[k]; a QR step; a converged
+ * value, made non-negative and moved into descending order).  Returns 1
+ * after more than 500 QR steps on one value (the reference throws). */
+static int golub_reinsch(double *U, double *V, double *s, double *e, int64_t m, int64_t n) {
+    int64_t p = n < m + 1 ? n : m + 1;
+    const double eps = ldexp(1.0, -52), tiny = ldexp(1.0, -966);
+    int iter = 0;
+    while (p > 0) {
+        int64_t k, kase;
+        for (k = p - 2; k >= 0; k--) {
+            const double thresh = tiny + eps * (fabs(s[k]) + fabs(s[k + 1]));
+            if (fabs(e[k]) <= thresh || e[k] != e[k]) {
+                e[k] = 0.0;
+                break;
+            }
+        }
+        if (k == p - 2) {
+            kase = 4;
+        } else {
+            int64_t ks;
+            for (ks = p - 1; ks > k; ks--) {
+                const double t = (ks != p ? fabs(e[ks]) : 0.0) + (ks != k + 1 ? fabs(e[ks - 1]) : 0.0);
+                if (fabs(s[ks]) <= tiny + eps * t) {
+                    s[ks] = 0.0;
+                    break;
+                }
+            }
+            if (ks == k) kase = 3;
+            else if (ks == p - 1) kase = 1;
+            else {
+                kase = 2;
+                k = ks;
+            }
+        }
+        k++;
+        if (kase == 1) { /* deflate the negligible s[p-1] */
+            double f = e[p - 2];
+            e[p - 2] = 0.0;
+            for (int64_t j = p - 2; j >= k; j--) {
+                const double t = hypot(s[j], f), cs = s[j] / t, sn = f / t;
+                s[j] = t;
+                if (j != k) {
+                    f = -sn * e[j - 1];
+                    e[j - 1] = cs * e[j - 1];
+                }
+                rotate_cols(V, n, n, j, p - 1, cs, sn);
+            }
+        } else if (kase == 2) { /* split at the negligible s[k-1] */
+            double f = e[k - 1];
+            e[k - 1] = 0.0;
+            for (int64_t j = k; j < p; j++) {
+                const double t = hypot(s[j], f), cs = s[j] / t, sn = f / t;
+                s[j] = t;
+                f = -sn * e[j];
+                e[j] = cs * e[j];
+                rotate_cols(U, m, n, j, k - 1, cs, sn);
+            }
+        } else if (kase == 3) { /* one implicit-shift QR step on [k, p-1] */
+            const double scale = jmax(jmax(jmax(jmax(fabs(s[p - 1]), fabs(s[p - 2])), fabs(e[p - 2])), fabs(s[k])),
+                                      fabs(e[k]));
+            const double sp = s[p - 1] / scale, spm1 = s[p - 2] / scale, epm1 = e[p - 2] / scale;
+            const double sk = s[k] / scale, ek = e[k] / scale;
+            const double b = ((spm1 + sp) * (spm1 - sp) + epm1 * epm1) / 2.0;
+            const double c = (sp * epm1) * (sp * epm1);
+            double shift = 0.0;
+            if (b != 0.0 || c != 0.0) {
+                shift = sqrt(b * b + c);
+                if (b < 0.0) shift = -shift;
+                shift = c / (b + shift);
+            }
+            double f = (sk + sp) * (sk - sp) + shift, g = sk * ek;
+            for (int64_t j = k; j < p - 1; j++) {
+                double t = hypot(f, g), cs = f / t, sn = g / t;
+                if (j != k) e[j - 1] = t;
+                f = cs * s[j] + sn * e[j];
+                e[j] = cs * e[j] - sn * s[j];
+                g = sn * s[j + 1];
+                s[j + 1] = cs * s[j + 1];
+                rotate_cols(V, n, n, j, j + 1, cs, sn);
+                t = hypot(f, g);
+                cs = f / t;
+                sn = g / t;
+                s[j] = t;
+                f = cs * e[j] + sn * s[j + 1];
+                s[j + 1] = -sn * e[j] + cs * s[j + 1];
+                g = sn * e[j + 1];
+                e[j + 1] = cs * e[j + 1];
+                if (j < m - 1) rotate_cols(U, m, n, j, j + 1, cs, sn);
+            }
+            e[p - 2] = f;
+            iter++;
+        } else { /* s[k] converged */
+            if (s[k] <= 0.0) {
+                s[k] = -s[k];
+                for (int64_t i = 0; i < n; i++) RM(V, n, i, k) = -RM(V, n, i, k);
+            }
+            for (; k < p - 1 && !(s[k] >= s[k + 1]); k++) {
+                const double t = s[k];
+                s[k] = s[k + 1];
+                s[k + 1] = t;
+                if (k < n - 1) swap_cols(V, n, n, k, k + 1);
+                if (k < m - 1) swap_cols(U, m, n, k, k + 1);
+            }
+            iter = 0;
+            p--;
+        }
+        if (iter > 500) return 1;
+    }
+    return 0;
+}
+
+/* Linalg.svd (Linalg.java:411-460): thin SVD of an m x n matrix (m >= n),
+ * FP64 outputs u [m, n], s [n] (descending, non-negative), vt [n, n].
+ * Returns 0, or 1 if the QR sweeps did not converge. */
+int orc_svd(int dtype, int64_t m, int64_t n, const void *a, double *u, double *s, double *vt) {
+    double *A = malloc(sizeof(double) * (size_t)(m * n + 1));
+    double *V = calloc((size_t)(n * n + 1), sizeof(double)), *e = calloc((size_t)n + 1, sizeof(double));
+    for (int64_t i = 0; i < m * n; i++)
+        A[i] = dtype == ORC_F64 ? ((const double *)a)[i] : (double)((const float *)a)[i];
+    for (int64_t i = 0; i < m * n; i++) u[i] = 0.0;
+    for (int64_t i = 0; i < n; i++) s[i] = 0.0;
+    bidiagonalize(A, u, V, s, e, m, n);
+    const int rc = golub_reinsch(u, V, s, e, m, n);
+    for (int64_t k = 0; k < n; k++) /* non-negative values, the sign moved into U */
+        if (s[k] < 0.0) {
+            s[k] = -s[k];
+            for (int64_t i = 0; i < m; i++) RM(u, n, i, k) = -RM(u, n, i, k);
+        }
+    for (int64_t k = 0; k + 1 < n; k++) { /* descending order */
+        int64_t best = k;
+        for (int64_t j = k + 1; j < n; j++)
+            if (s[j] > s[best]) best = j;
+        if (best != k) {
+            const double t = s[k];
+            s[k] = s[best];
+            s[best] = t;
+            swap_cols(u, m, n, k, best);
+            swap_cols(V, n, n, k, best);
+        }
+    }
+    for (int64_t i = 0; i < n; i++)
+        for (int64_t j = 0; j < n; j++) RM(vt, n, i, j) = RM(V, n, j, i);
+    free(A);
+    free(V);
+    free(e);
+    return rc;
+}

@@ -132,6 +132,9 @@ int orc_lu_factor(double *a, int64_t n, int submatrix_check, int64_t *piv, doubl
 void orc_lu_solve(const double *lu, const int64_t *piv, int64_t n, const double *b, double *x);
 void orc_lu_solve_t(const double *lu, const int64_t *piv, int64_t n, const double *b, double *x);
 double orc_lu_rcond(const double *lu, const int64_t *piv, int64_t n, double inf_norm);
+/* eigenvalues in deflation order (input dtype); thin SVD (FP64).  0, or 1 if the iteration did not converge. */
+int orc_eig(int dtype, int64_t n, const void *a, void *wr, void *wi);
+int orc_svd(int dtype, int64_t m, int64_t n, const void *a, double *u, double *s, double *vt);
 
 #ifdef __cplusplus
 }

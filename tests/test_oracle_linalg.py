@@ -88,3 +88,54 @@ def test_hager_matches_exact_norm_on_small_cases(n):
     est = 1.0 / (orc.lu_rcond(lu, piv, norms[1]) * norms[1])
     exact = np.abs(np.linalg.inv(a)).sum(axis=1).max()
     assert exact / 3 <= est <= exact * (1 + 1e-12)
+
+
+# ---- eig / svd: T/LinalgTest.java and T/LinalgSvdTest.java through the oracle --------
+def test_eig_reference_cases():
+    wr, wi = orc.eig(np.diag([3.0, -1.0, 7.0, 2.0]))
+    np.testing.assert_allclose(np.sort(wr), [-1, 2, 3, 7], atol=1e-12)
+    np.testing.assert_allclose(wi, 0, atol=1e-12)
+    np.testing.assert_allclose(np.sort(orc.eig(np.array([[2.0, 1.0], [1.0, 2.0]]))[0]), [1, 3], atol=1e-13)
+    wr, wi = orc.eig(np.array([[0.0, -1.0], [1.0, 0.0]]))
+    np.testing.assert_allclose(wr, 0, atol=1e-12)
+    np.testing.assert_allclose(np.abs(wi), 1, atol=1e-12)
+    assert abs(wi[0] + wi[1]) <= 1e-12
+    np.testing.assert_allclose(np.sort(orc.eig(np.array([[0, 0, 0], [1, 0, 1], [0, 1, 0.0]]))[0]), [-1, 0, 1],
+                               atol=1e-12)
+    a = JavaRandom(41).gaussians(36).reshape(6, 6)
+    assert abs(orc.eig(a)[0].sum() - np.trace(a)) <= 1e-10
+
+
+@pytest.mark.parametrize("n", [1, 2, 7, 40, 150])
+def test_eig_matches_lapack(n):
+    a = np.random.default_rng(n).standard_normal((n, n))
+    wr, wi = orc.eig(a)
+    got, want = np.sort_complex(wr + 1j * wi), np.sort_complex(np.linalg.eigvals(a))
+    np.testing.assert_allclose(got, want, atol=1e-10 * max(1.0, np.abs(want).max()))
+    wr32, _ = orc.eig(a.astype(np.float32))
+    assert wr32.dtype == np.float32
+
+
+def test_svd_reference_cases():
+    np.testing.assert_allclose(orc.svd(np.diag([3.0, 1.0, 2.0]))[1], [3, 2, 1], atol=1e-12)
+    a = JavaRandom(29).gaussians(12).reshape(4, 3)
+    u, s, vt = orc.svd(a)
+    np.testing.assert_allclose((u * s) @ vt, a, atol=1e-10)
+    for seed, tol in ((31, 1e-9), (37, 1e-11)):
+        a = JavaRandom(seed).gaussians(16).reshape(4, 4)
+        u, s, vt = orc.svd(a)
+        np.testing.assert_allclose(u.T @ u, np.eye(4), atol=tol)
+        np.testing.assert_allclose(vt @ vt.T, np.eye(4), atol=tol)
+    target = np.array([1.0, 1e-3, 1e-6, 1e-9, 1e-12])
+    s = orc.svd(np.diag(target))[1]
+    assert np.all(np.abs(s - target) / target <= 1e-13)
+    s = orc.svd(JavaRandom(43).gaussians(15).reshape(5, 3))[1]
+    assert np.all(s >= 0) and np.all(s[:-1] >= s[1:] - 1e-12)
+
+
+@pytest.mark.parametrize("m,n", [(1, 1), (3, 2), (30, 30), (120, 45)])
+def test_svd_matches_lapack(m, n):
+    a = np.random.default_rng(m + n).standard_normal((m, n))
+    u, s, vt = orc.svd(a)
+    np.testing.assert_allclose(s, np.linalg.svd(a, compute_uv=False), atol=1e-12 * s[0])
+    np.testing.assert_allclose((u * s) @ vt, a, atol=1e-12 * s[0])
