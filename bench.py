@@ -385,6 +385,11 @@ def run_ours(args):
     peaks = _measured_peaks()
     peak, peak_source = _tensor_peak(peaks, clk)
     achieved = (dot_flop / (dot_ms / 1e3)) / 1e12 if dot_ms > 0 else None
+    from jax4j_b200.core import split_kind
+    f16 = split_kind() == 1
+    # the three tensor-core products each FP32 product issues, against the dense rate of their kind
+    mma_peak = (peak if f16 else peak / 2) if peak else None
+    traffic = GEMM_DRAM_BYTES_PER_LAUNCH.get("fp16" if f16 else "tf32") if B == BATCH else None
     line = {
         "metric": METRIC, "value": value, "unit": "samples/s", "n_gpus": D, "steps": args.steps,
         "warmup": args.warmup, "ms_per_step": ms / args.steps, "higher_is_better": True,
@@ -393,17 +398,18 @@ def run_ours(args):
         "config": {"workload": WORKLOAD, "model": "mlp-1024-4096x3-1000-relu", "global_batch": D * B,
                    "per_gpu_batch": B, "parallelism": f"dp{D}",
                    "l2": "working set (167 MB params + >400 MB activations) exceeds the 126 MB L2"},
-        "roofline": {"bound": "tensor", "kernel": "dot (FP32 via 3xTF32 split)",
+        "roofline": {"bound": "tensor",
+                     "kernel": "dot (FP32 via 3xFP16 split, power-of-two scaled)" if f16
+                               else "dot (FP32 via 3xTF32 split)",
                      "achieved": achieved, "peak": peak, "unit": "TFLOP/s",
                      "frac": (achieved / peak) if (achieved and peak) else None,
                      "peak_source": peak_source,
                      "dot_share_of_step": dot_ms / eager_ms_local if eager_ms_local else None,
-                     # the three TF32 products each FP32 product issues, against the dense TF32 rate
-                     "tf32_issued": {"achieved": 3 * achieved if achieved else None,
-                                     "peak": peak / 2 if peak else None,
-                                     "frac": (6 * achieved / peak) if (achieved and peak) else None},
+                     "mma_issued": {"kind": "f16" if f16 else "tf32",
+                                    "achieved": 3 * achieved if achieved else None, "peak": mma_peak,
+                                    "frac": (3 * achieved / mma_peak) if (achieved and mma_peak) else None},
                      "algorithmic_bytes_per_launch": dot_bytes_per_launch,
-                     "traffic": GEMM_DRAM_BYTES_PER_LAUNCH if B == BATCH else None,
+                     "traffic": traffic,
                      "traffic_source": "ncu dram__bytes_read.sum + dram__bytes_write.sum over the 11 GEMM "
                                        "launches of one step at batch 8192, averaged per launch "
                                        "(single-pass capture, cold L2)"},
@@ -428,9 +434,10 @@ def run_ours(args):
         distributed.shutdown()
 
 
-# DRAM bytes per GEMM launch of the batch-8192 step, from an ncu capture of its
-# 11 GEMM launches (dram__bytes_read.sum + dram__bytes_write.sum, averaged).
-GEMM_DRAM_BYTES_PER_LAUNCH = 1.0663e9
+# DRAM bytes per GEMM launch of the batch-8192 step, from ncu captures of its
+# 11 GEMM launches (dram__bytes_read.sum + dram__bytes_write.sum, averaged),
+# per operand split kind.
+GEMM_DRAM_BYTES_PER_LAUNCH = {"tf32": 1.0663e9, "fp16": 5.573e8}
 
 
 def _tensor_peak(peaks: dict, clk: dict):
@@ -442,8 +449,8 @@ def _tensor_peak(peaks: dict, clk: dict):
     at_max = sm is not None and smax and sm >= 0.97 * smax
     src = peaks.get("source", "MEASURED_PEAKS.json")
     if sustained and not at_max:
-        return sustained, f"{src} bf16 sustained (SM clock below max during the run); TF32 dense rate is half"
-    return burst, f"{src} bf16 burst (SM clock at max during the run); TF32 dense rate is half"
+        return sustained, f"{src} bf16 sustained (SM clock below max during the run); FP16 dense rate equal, TF32 half"
+    return burst, f"{src} bf16 burst (SM clock at max during the run); FP16 dense rate equal, TF32 half"
 
 
 def _measured_peaks() -> dict:
@@ -567,7 +574,9 @@ def run_gemm(args):
     ms = timed(full)
     gemm_ms = timed(gemm_only)
     flop = 2.0 * M * N * K
-    print(json.dumps({"metric": "dot TFLOP/s (FP32 accuracy, 3xTF32)", "value": flop / (ms / 1e3) / 1e12,
+    from jax4j_b200.core import split_kind
+    print(json.dumps({"metric": "dot TFLOP/s (FP32 accuracy, %s)" % ("3xFP16" if split_kind() == 1 else "3xTF32"),
+                      "value": flop / (ms / 1e3) / 1e12,
                       "unit": "TFLOP/s", "ms_per_step": ms, "gemm_ms": gemm_ms,
                       "gemm_tflops": flop / (gemm_ms / 1e3) / 1e12,
                       "config": {"workload": f"dot {M}x{K}x{N} op(A){'T' if ta else ''} op(B){'T' if tb else ''}"},
@@ -956,8 +965,8 @@ def run_cfg2(args):
         flop = 2.0 * M * K * N * D
         print(json.dumps({"metric": "config-2 pmap dot + allGather TFLOP/s", "unit": "TFLOP/s",
                           "value": flop / (ms / 1e3) / 1e12, "ms_per_step": ms, "n_gpus": world,
-                          "config": {"workload": "per shard [4096,8192].[8192,4096] FP32 (3xTF32), "
-                                                 "allGather of the [4096,4096] results"},
+                          "config": {"workload": "per shard [4096,8192].[8192,4096] FP32 (tensor-core split "
+                                                 "GEMM), allGather of the [4096,4096] results"},
                           "allgather_bytes_per_rank": 4 * M * N}), flush=True)
     _finish(world)
 

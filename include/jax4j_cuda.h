@@ -278,16 +278,26 @@ J4C_API size_t j4c_dot_workspace_size(int dtype, int64_t M, int64_t K, int64_t N
 
 /* The FLOAT32 dot in two steps, so a tensor that takes part in several
  * products (a layer's input, weight and output gradient each appear in two
- * of the forward/VJP dots) is split once.  j4c_split_f32 writes
- * hi = tf32(x) and lo = tf32(x - hi) of x stored [rows, cols] as two arrays
- * [rows, j4c_split_pitch(cols)] (16-byte aligned, padding columns zero);
- * j4c_dot_split then computes C = op(A) . op(B) as j4c_dot does, from the
- * split arrays of A and B in their stored layouts (trans flags as for
- * j4c_dot).  The split of an unchanged tensor may be reused by any number of
- * j4c_dot_split calls. */
+ * of the forward/VJP dots) is split once.  j4c_split_f32 writes the hi and
+ * lo parts of x stored [rows, cols] into two caller-allocated arrays of
+ * rows * j4c_split_pitch(cols) floats each (16-byte aligned); j4c_dot_split
+ * then computes C = op(A) . op(B) as j4c_dot does, from the split arrays of
+ * A and B in their stored layouts (trans flags as for j4c_dot).  The split
+ * of an unchanged tensor may be reused by any number of j4c_dot_split calls.
+ * The split's format is the library's (j4c_dot_split_kind), fixed for the
+ * process:
+ *   1, 3xFP16 (default): with 2^e the power of two that brings max |x| over
+ *      the finite elements into [2^14, 2^15) (e in [-100, 100]), hi =
+ *      fp16(x 2^e) and lo = fp16(x 2^e - hi) as 2-byte halves in rows of
+ *      cols rounded up to 8 (padding zero), and in the hi array the 32-bit
+ *      bits of max |x| after the last row;
+ *   0, 3xTF32 (environment J4C_GEMM_SPLIT=tf32): hi = tf32(x), lo =
+ *      tf32(x - hi) as floats in rows of cols rounded up to 4 (padding zero),
+ *      j4c_split_pitch(cols) floats per row. */
+J4C_API int j4c_dot_split_kind(void);
 J4C_API int64_t j4c_split_pitch(int64_t cols);
 J4C_API int j4c_split_f32(const float *x, int64_t rows, int64_t cols, float *hi, float *lo, j4c_stream stream);
-/* The split of x^T: hi/lo arrays [cols, j4c_split_pitch(rows)].  A product
+/* The split of x^T: hi/lo arrays of cols * j4c_split_pitch(rows) floats.  A product
  * whose A and B are both stored with K as the leading (slow) dimension, such
  * as the weight gradient x^T . dy, runs fastest with one of them given in
  * this form (and its trans flag flipped). */

@@ -77,6 +77,7 @@ SIGNATURES = {
     "j4c_dot_ws": [I32, P, P, P, I64, I64, I64, I32, I32, P, C.c_size_t, P],
     "j4c_dot_workspace_size": [I32, I64, I64, I64],
     "j4c_split_pitch": [I64],
+    "j4c_dot_split_kind": [],
     "j4c_split_f32": [P, I64, I64, P, P, P],
     "j4c_split_f32_transposed": [P, I64, I64, P, P, P],
     "j4c_dot_split": [P, P, P, P, P, I64, I64, I64, I32, I32, P],

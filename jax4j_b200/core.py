@@ -740,9 +740,21 @@ def _dtype_of_numpy(arr: np.ndarray) -> DType:
 # When a list, every dot launch appends (start_event, end_event, flops, bytes):
 # CUDA events recorded on the launching stream around the kernel (used by the
 # benchmark to time the GEMM kernels inside its timed region) and the launch's
-# algorithmic HBM bytes: each FP32 operand read once as its hi/lo split (8 B per
-# element), every output written once, the epilogue's bias and mask read once.
+# algorithmic HBM bytes: each FP32 operand read once as its hi/lo split (4 B per
+# element for 3xFP16, 8 B for 3xTF32), every output written once, the
+# epilogue's bias and mask read once.
 DOT_TIMING = None
+
+
+def split_kind() -> int:
+    """The library's FLOAT32 dot split: 1 = 3xFP16 (power-of-two scaled FP16
+    hi/lo), 0 = 3xTF32 (J4C_GEMM_SPLIT=tf32)."""
+    return int(_lib.lib().j4c_dot_split_kind())
+
+
+def split_bytes_per_element() -> int:
+    """HBM bytes of one operand element's hi + lo split (read once by a GEMM)."""
+    return 4 if split_kind() == 1 else 8
 
 
 def _tf32_split(x: "ConcreteNDArray", transposed: bool = False):
@@ -857,8 +869,8 @@ def _dot_raw(a: "ConcreteNDArray", b: "ConcreteNDArray", trans_a: bool, trans_b:
     if timing is not None:
         ev1.record()
         if a._dtype == DType.FLOAT32:
-            nbytes = 8 * (M * K + K * N) + 4 * M * N * (1 + int(act) + int(mask is not None)) \
-                + (4 * N if bias is not None else 0)
+            nbytes = split_bytes_per_element() * (M * K + K * N) \
+                + 4 * M * N * (1 + int(act) + int(mask is not None)) + (4 * N if bias is not None else 0)
         else:
             nbytes = a._dtype.byteSize() * (M * K + K * N + M * N)
         timing.append((ev0, ev1, 2.0 * M * N * K, nbytes))

@@ -7,6 +7,8 @@ namespace j4c {
 int simt_gemm(int dtype, const void *a, const void *b, void *c, int64_t M, int64_t K, int64_t N,
               int trans_a, int trans_b, cudaStream_t s);
 int tc_gemm_workspace(int64_t M, int64_t K, int64_t N, size_t *bytes);
+int64_t tc_split_alloc_pitch(int64_t cols);
+int tc_split_kind();
 int tc_gemm_f32(const float *a, const float *b, float *c, int64_t M, int64_t K, int64_t N,
                 int trans_a, int trans_b, void *ws, size_t ws_bytes, cudaStream_t s);
 bool tc_gemm_supported(int64_t M, int64_t K, int64_t N);
@@ -66,7 +68,9 @@ int j4c_dot(int dtype, const void *a, const void *b, void *c, int64_t M, int64_t
     return rc;
 }
 
-int64_t j4c_split_pitch(int64_t cols) { return cols < 0 ? -1 : (cols + 3) / 4 * 4; }
+int64_t j4c_split_pitch(int64_t cols) { return cols < 0 ? -1 : tc_split_alloc_pitch(cols); }
+
+int j4c_dot_split_kind(void) { return tc_split_kind(); }
 
 int j4c_split_f32(const float *x, int64_t rows, int64_t cols, float *hi, float *lo, j4c_stream stream) {
     J4C_REQUIRE(rows >= 0 && cols >= 0, "j4c_split_f32: negative extent");

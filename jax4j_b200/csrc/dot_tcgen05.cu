@@ -30,10 +30,21 @@
 //  add it into FP32 registers with round-to-nearest while the MMA warp
 //  fills the other buffer.  The error then grows with sqrt(K) like an FP32
 //  sum.
+//  Split mode 3xFP16 (the default; J4C_GEMM_SPLIT=tf32 selects 3xTF32): the same three products from
+//  FP16 operands, at twice the tensor rate of TF32.  FP16 has TF32's 11-bit
+//  significand but a 5-bit exponent, so every operand is first scaled by a
+//  power of two 2^e chosen from its largest finite magnitude (max |x| 2^e in
+//  [2^14, 2^15)): hi = fp16(x 2^e), lo = fp16(x 2^e - hi), stored as 2-byte
+//  halves with the max in a word after the hi array, and the
+//  epilogue multiplies the accumulator by 2^-(e_a + e_b) (exact).  Elements
+//  below 2^-24 of the tensor's max lose digits (FP16 subnormals): an
+//  absolute error of at most ~2^-38 max |x| per element, on top of the
+//  2^-22 relative error of the split.
 //  Every mbarrier wait is bounded: after kWaitLimitNs without progress the
 //  kernel records J4C status kStatusTimeout, stops all roles, waits
 //  (bounded) for its own TMA and MMA work in flight, frees TMEM and returns.
 #include <cuda.h>
+#include <cuda_fp16.h>
 #include <cudaTypedefs.h>
 
 #include <algorithm>
@@ -47,8 +58,6 @@ namespace j4c {
 namespace tc {
 
 constexpr int BM = 128;           // rows of a CTA tile (TMEM lanes)
-constexpr int MNW = 32;           // MN-major tiles: floats per 128-byte swizzle row
-constexpr int UMMA_K = 8;         // K of one tf32 MMA instruction (32 bytes)
 constexpr int CHUNK_K = 256;      // K accumulated in TMEM before promotion to registers
 constexpr int kEpiWarps = 8;      // two warps per TMEM lane quadrant
 constexpr int kThreads = 64 + 32 * kEpiWarps;
@@ -56,15 +65,25 @@ constexpr int kStatusTimeout = 0x7C05;
 constexpr uint64_t kWaitLimitNs = 2000000000ull;  // 2 s without progress
 constexpr int kMaxTailSplits = 4; // parts along K of a tile of the last wave
 
-// BK = FP32 elements per smem row of a stage: 32 (128-byte swizzle) or 16
-// (64-byte swizzle, half the bytes per stage, so twice the stages fit).
-template <int BN, int STAGES, int BK>
+// Operand element of a split mode: 3xTF32 (4-byte tf32 values) or 3xFP16.
+template <bool F16>
+struct Elt {
+    static constexpr int SIZE = F16 ? 2 : 4;     // bytes per element
+    static constexpr int UMMA_K = F16 ? 16 : 8;  // K of one MMA instruction (32 bytes either way)
+    static constexpr int MNW = F16 ? 64 : 32;    // MN-major tiles: elements per 128-byte swizzle row
+};
+
+// BK = 32-bit words per smem row of a stage: 32 (128-byte swizzle) or 16
+// (64-byte swizzle, half the bytes per stage, so twice the stages fit);
+// BKE = the K elements those bytes hold.
+template <int BN, int STAGES, int BK, bool F16 = false>
 struct Cfg {
     static_assert(BK == 32 || BK == 16, "BK is 32 (SW128) or 16 (SW64)");
-    static constexpr int CHUNK_KB = CHUNK_K / BK;
+    static constexpr int BKE = BK * 4 / Elt<F16>::SIZE;
+    static constexpr int CHUNK_KB = CHUNK_K / BKE;
     static constexpr int A_BYTES = BM * BK * 4;
     static constexpr int B_BYTES = BN * BK * 4;
-    static constexpr int MN_BOX_BYTES = MNW * BK * 4;  // one MN-major column block (BK rows x 128 B)
+    static constexpr int MN_BOX_BYTES = 128 * BKE;  // one MN-major column block (BKE rows x 128 B)
     static constexpr int STAGE_BYTES = 2 * A_BYTES + 2 * B_BYTES;
     static constexpr int TMEM_COLS = 2 * BN;  // two partial-sum buffers
     static constexpr int COLS_PER_WARP = BN / 2;  // each epilogue warp owns half the columns
@@ -167,42 +186,68 @@ __device__ __forceinline__ uint64_t smem_desc(uint32_t addr) {
     return d;
 }
 
-// MN-major operand tile.  For 32-bit (tf32) operands the tensor core reads
-// MN-major data only in the "128-byte swizzle with 32-byte atoms" layout
-// (descriptor layout type 1; the TMA writes it with
-// CU_TENSOR_MAP_SWIZZLE_128B_ATOM_32B): 128-byte rows of 32 floats along M/N,
-// one row per k, whose four 32-byte pieces are permuted by (row mod 4).
-// Column blocks of 32 floats are stacked BK rows deep, MN_BOX_BYTES apart:
-// LBO = the distance between column blocks along M/N, SBO = the distance
-// between groups of 4 k-rows (one MMA's K = 8 reads two groups).
-template <int BK>
+// MN-major operand tile: 128-byte rows along M/N, one row per k, in column
+// blocks BKE rows deep and MN_BOX_BYTES apart (LBO = the distance between
+// column blocks along M/N; SBO = the distance between groups of k-rows).
+//   tf32: the tensor core reads 32-bit MN-major data only in the "128-byte
+//   swizzle with 32-byte atoms" layout (descriptor layout type 1; the TMA
+//   writes it with CU_TENSOR_MAP_SWIZZLE_128B_ATOM_32B): rows of 32 floats
+//   whose four 32-byte pieces are permuted by (row mod 4); SBO = 4 k-rows.
+//   fp16: the plain 128-byte swizzle (layout type 2, the TMA's
+//   CU_TENSOR_MAP_SWIZZLE_128B): rows of 64 halves; SBO = 8 k-rows.
+template <int BK, bool F16>
 __device__ __forceinline__ uint64_t smem_desc_mn(uint32_t addr) {
-    constexpr uint64_t box_bytes = MNW * BK * 4;
+    constexpr uint64_t box_bytes = 128 * (BK * 4 / Elt<F16>::SIZE);
+    constexpr uint64_t group_rows = F16 ? 8 : 4;
     uint64_t d = 0;
     d |= (uint64_t)((addr & 0x3FFFF) >> 4);
-    d |= (uint64_t)(box_bytes >> 4) << 16;       // LBO: next 32-float column block
-    d |= (uint64_t)((4 * 128) >> 4) << 32;       // SBO: next 4 k-rows
-    d |= (uint64_t)1 << 46;                      // descriptor version for sm_100
-    d |= (uint64_t)1 << 61;                      // 128-byte swizzle, 32-byte atoms
+    d |= (uint64_t)(box_bytes >> 4) << 16;           // LBO: next column block
+    d |= (uint64_t)((group_rows * 128) >> 4) << 32;  // SBO: next group of k-rows
+    d |= (uint64_t)1 << 46;                          // descriptor version for sm_100
+    d |= (uint64_t)(F16 ? 2 : 1) << 61;              // swizzle mode
     return d;
 }
 
-// kind::tf32 instruction descriptor: D f32, A/B tf32; a_mn / b_mn select the
-// MN-major operand layout (bits 15 / 16).
-__host__ __device__ constexpr uint32_t idesc_tf32(int m, int n, bool a_mn, bool b_mn) {
-    return (1u << 4) | (2u << 7) | (2u << 10) | ((a_mn ? 1u : 0u) << 15) | ((b_mn ? 1u : 0u) << 16) |
-           ((uint32_t)(n >> 3) << 17) | ((uint32_t)(m >> 4) << 24);
+// Instruction descriptor of kind::tf32 (A/B format 2) or kind::f16 with
+// fp16 A/B (format 0): D f32; a_mn / b_mn select the MN-major operand layout
+// (bits 15 / 16).
+template <bool F16>
+__host__ __device__ constexpr uint32_t idesc_mma(int m, int n, bool a_mn, bool b_mn) {
+    return (1u << 4) | ((F16 ? 0u : 2u) << 7) | ((F16 ? 0u : 2u) << 10) | ((a_mn ? 1u : 0u) << 15) |
+           ((b_mn ? 1u : 0u) << 16) | ((uint32_t)(n >> 3) << 17) | ((uint32_t)(m >> 4) << 24);
 }
 
-__device__ __forceinline__ void mma_tf32(uint32_t d_tmem, uint64_t a, uint64_t b, uint32_t idesc,
-                                         uint32_t accumulate) {
-    asm volatile(
-        "{\n\t.reg .pred p;\n\t"
-        "setp.ne.b32 p, %4, 0;\n\t"
-        "tcgen05.mma.cta_group::1.kind::tf32 [%0], %1, %2, %3, p;\n\t}" ::"r"(d_tmem),
-        "l"(a), "l"(b), "r"(idesc), "r"(accumulate)
-        : "memory");
+template <bool F16>
+__device__ __forceinline__ void mma_issue(uint32_t d_tmem, uint64_t a, uint64_t b, uint32_t idesc,
+                                          uint32_t accumulate) {
+    if constexpr (F16) {
+        asm volatile(
+            "{\n\t.reg .pred p;\n\t"
+            "setp.ne.b32 p, %4, 0;\n\t"
+            "tcgen05.mma.cta_group::1.kind::f16 [%0], %1, %2, %3, p;\n\t}" ::"r"(d_tmem),
+            "l"(a), "l"(b), "r"(idesc), "r"(accumulate)
+            : "memory");
+    } else {
+        asm volatile(
+            "{\n\t.reg .pred p;\n\t"
+            "setp.ne.b32 p, %4, 0;\n\t"
+            "tcgen05.mma.cta_group::1.kind::tf32 [%0], %1, %2, %3, p;\n\t}" ::"r"(d_tmem),
+            "l"(a), "l"(b), "r"(idesc), "r"(accumulate)
+            : "memory");
+    }
 }
+
+// The scale exponent e of an fp16 split from the bits of its max |x|
+// (finite, non-negative): max 2^e in [2^14, 2^15); 0 for a zero max;
+// clamped to [-100, 100] so that 2^-e is a normal float.
+__host__ __device__ __forceinline__ int split_exp(uint32_t maxbits) {
+    if (maxbits == 0) return 0;
+    const int e = 14 - ((int)((maxbits >> 23) & 0xFF) - 127);
+    return e < -100 ? -100 : (e > 100 ? 100 : e);
+}
+
+// 2^k as a float, |k| <= 100.
+__device__ __forceinline__ float pow2f(int k) { return __uint_as_float((uint32_t)(127 + k) << 23); }
 
 __device__ __forceinline__ void mma_commit(uint32_t bar) {
     asm volatile("tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];" ::"r"(bar)
@@ -264,27 +309,31 @@ struct Epilogue {
 
 __device__ __forceinline__ float ep_relu(float v) { return (0.0f >= v) ? 0.0f : v; }
 
-// Loads one operand's hi or lo tile (ROWS of M or N, BK of K) into smem.
-template <int ROWS, int BK, bool MN>
+// Loads one operand's hi or lo tile (ROWS of M or N, BKE of K) into smem.
+template <int ROWS, int BK, bool MN, bool F16>
 __device__ __forceinline__ void load_operand(uint32_t dst, const CUtensorMap *map, int kx, int row0, int z,
                                              uint32_t bar) {
     if constexpr (!MN) {
-        tma_load_3d(dst, map, kx, row0, z, bar);  // box {BK, ROWS, 1} of a [batch][rows, K] array
+        tma_load_3d(dst, map, kx, row0, z, bar);  // box {BKE, ROWS, 1} of a [batch][rows, K] array
     } else {
+        constexpr int W = Elt<F16>::MNW, BOX = 128 * (BK * 4 / Elt<F16>::SIZE);
 #pragma unroll
-        for (int i = 0; i < ROWS / MNW; i++)      // boxes {32, BK, 1} of a [batch][K, rows] array
-            tma_load_3d(dst + i * (MNW * BK * 4), map, row0 + i * MNW, kx, z, bar);
+        for (int i = 0; i < ROWS / W; i++)        // boxes {MNW, BKE, 1} of a [batch][K, rows] array
+            tma_load_3d(dst + i * BOX, map, row0 + i * W, kx, z, bar);
     }
 }
 
-template <int BN, int STAGES, int BK, bool A_MN, bool B_MN>
+// F16: the 3xFP16 split; amax / bmax are then the operands' max words.
+template <int BN, int STAGES, int BK, bool A_MN, bool B_MN, bool F16>
 __global__ void __launch_bounds__(kThreads, 1)
 gemm_3xtf32_kernel(const __grid_constant__ CUtensorMap tAh, const __grid_constant__ CUtensorMap tAl,
                    const __grid_constant__ CUtensorMap tBh, const __grid_constant__ CUtensorMap tBl,
                    float *__restrict__ C, int M, int N, int num_kb, int vec_store, int store_t,
                    Epilogue ep, int batch, int a_batched, int b_batched, int *status, int full_tiles,
-                   int splits, float *__restrict__ part, int *__restrict__ arrivals) {
-    using Q = Cfg<BN, STAGES, BK>;
+                   int splits, float *__restrict__ part, int *__restrict__ arrivals,
+                   const uint32_t *__restrict__ amax, const uint32_t *__restrict__ bmax) {
+    using Q = Cfg<BN, STAGES, BK, F16>;
+    constexpr int UMMA_K = Elt<F16>::UMMA_K;
     constexpr int CHUNK_KB = Q::CHUNK_KB;
     extern __shared__ uint8_t smem_raw[];
     uint8_t *smem = reinterpret_cast<uint8_t *>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
@@ -344,11 +393,11 @@ gemm_3xtf32_kernel(const __grid_constant__ CUtensorMap tAh, const __grid_constan
                     const uint32_t sb = smem_u32(smem + stage * Q::STAGE_BYTES);
                     const uint32_t fb = smem_u32(&ctl->full[stage]);
                     mbar_expect_tx(fb, Q::STAGE_BYTES);
-                    const int kx = kb * BK;
-                    load_operand<BM, BK, A_MN>(sb, &tAh, kx, mt * BM, za, fb);
-                    load_operand<BM, BK, A_MN>(sb + Q::A_BYTES, &tAl, kx, mt * BM, za, fb);
-                    load_operand<BN, BK, B_MN>(sb + 2 * Q::A_BYTES, &tBh, kx, nt * BN, zb, fb);
-                    load_operand<BN, BK, B_MN>(sb + 2 * Q::A_BYTES + Q::B_BYTES, &tBl, kx, nt * BN, zb, fb);
+                    const int kx = kb * Q::BKE;
+                    load_operand<BM, BK, A_MN, F16>(sb, &tAh, kx, mt * BM, za, fb);
+                    load_operand<BM, BK, A_MN, F16>(sb + Q::A_BYTES, &tAl, kx, mt * BM, za, fb);
+                    load_operand<BN, BK, B_MN, F16>(sb + 2 * Q::A_BYTES, &tBh, kx, nt * BN, zb, fb);
+                    load_operand<BN, BK, B_MN, F16>(sb + 2 * Q::A_BYTES + Q::B_BYTES, &tBl, kx, nt * BN, zb, fb);
                     issued++;
                     if (++stage == STAGES) {
                         stage = 0;
@@ -369,7 +418,7 @@ gemm_3xtf32_kernel(const __grid_constant__ CUtensorMap tAh, const __grid_constan
     } else if (warp == 1) {
         // ---------------- MMA issuer ----------------
         if (lane == 0) {
-            constexpr uint32_t idesc = idesc_tf32(BM, BN, A_MN, B_MN);
+            constexpr uint32_t idesc = idesc_mma<F16>(BM, BN, A_MN, B_MN);
             int stage = 0;
             uint32_t phase = 0;
             int ci = 0;  // chunk counter across tiles: selects the TMEM buffer
@@ -397,17 +446,17 @@ gemm_3xtf32_kernel(const __grid_constant__ CUtensorMap tAh, const __grid_constan
                         const uint32_t sb_hi = sa_hi + 2 * Q::A_BYTES;
                         const uint32_t sb_lo = sb_hi + Q::B_BYTES;
 #pragma unroll
-                        for (int kk = 0; kk < BK / UMMA_K; kk++) {
-                            // next K = 8: 32 bytes along a K-major row, 8 rows of 128 B in an MN-major block
-                            const uint32_t oa = A_MN ? kk * UMMA_K * 128 : kk * UMMA_K * 4;
-                            const uint32_t ob = B_MN ? kk * UMMA_K * 128 : kk * UMMA_K * 4;
-                            const uint64_t ah = A_MN ? smem_desc_mn<BK>(sa_hi + oa) : smem_desc<BK>(sa_hi + oa);
-                            const uint64_t al = A_MN ? smem_desc_mn<BK>(sa_lo + oa) : smem_desc<BK>(sa_lo + oa);
-                            const uint64_t bh = B_MN ? smem_desc_mn<BK>(sb_hi + ob) : smem_desc<BK>(sb_hi + ob);
-                            const uint64_t bl = B_MN ? smem_desc_mn<BK>(sb_lo + ob) : smem_desc<BK>(sb_lo + ob);
-                            mma_tf32(dcol, al, bh, idesc, (kb > kb0 || kk > 0) ? 1u : 0u);
-                            mma_tf32(dcol, ah, bl, idesc, 1u);
-                            mma_tf32(dcol, ah, bh, idesc, 1u);
+                        for (int kk = 0; kk < Q::BKE / UMMA_K; kk++) {
+                            // next UMMA_K: 32 bytes along a K-major row, UMMA_K rows of 128 B in an MN-major block
+                            const uint32_t oa = A_MN ? kk * UMMA_K * 128 : kk * 32;
+                            const uint32_t ob = B_MN ? kk * UMMA_K * 128 : kk * 32;
+                            const uint64_t ah = A_MN ? smem_desc_mn<BK, F16>(sa_hi + oa) : smem_desc<BK>(sa_hi + oa);
+                            const uint64_t al = A_MN ? smem_desc_mn<BK, F16>(sa_lo + oa) : smem_desc<BK>(sa_lo + oa);
+                            const uint64_t bh = B_MN ? smem_desc_mn<BK, F16>(sb_hi + ob) : smem_desc<BK>(sb_hi + ob);
+                            const uint64_t bl = B_MN ? smem_desc_mn<BK, F16>(sb_lo + ob) : smem_desc<BK>(sb_lo + ob);
+                            mma_issue<F16>(dcol, al, bh, idesc, (kb > kb0 || kk > 0) ? 1u : 0u);
+                            mma_issue<F16>(dcol, ah, bl, idesc, 1u);
+                            mma_issue<F16>(dcol, ah, bh, idesc, 1u);
                         }
                         mma_commit(smem_u32(&ctl->empty[stage]));
                         if (++stage == STAGES) {
@@ -494,6 +543,13 @@ gemm_3xtf32_kernel(const __grid_constant__ CUtensorMap tAh, const __grid_constan
                         if (p < splits) v = __fadd_rn(v, __ldcg(rp + (size_t)p * kEpiWarps * RF + (size_t)j * 32));
                     acc[j] = v;
                 }
+            }
+            if constexpr (F16) {
+                // the accumulator is in units of 2^(e_a + e_b): two exact power-of-two scalings
+                const int E = split_exp(__ldg(amax)) + split_exp(__ldg(bmax));
+                const float f1 = pow2f(-(E >> 1)), f2 = pow2f(-(E - (E >> 1)));
+#pragma unroll
+                for (int j = 0; j < Q::COLS_PER_WARP; j++) acc[j] = acc[j] * f1 * f2;
             }
             const int row = mt * BM + q * 32 + lane;
             const int col0 = nt * BN + cbase;
@@ -658,6 +714,163 @@ __global__ void __launch_bounds__(256) split_t_kernel(const float *__restrict__ 
     }
 }
 
+// ---- 3xFP16 operand split --------------------------------------------------------------
+// *word = the bits of max |x| over the finite elements of X [n] (zeroed beforehand):
+// non-negative floats order like their bits as unsigned integers.
+__global__ void __launch_bounds__(256) absmax_kernel(const float *__restrict__ src, int64_t n, int vec,
+                                                     uint32_t *__restrict__ word) {
+    uint32_t m = 0;
+    const int64_t stride = (int64_t)gridDim.x * blockDim.x;
+    const int64_t t0 = blockIdx.x * (int64_t)blockDim.x + threadIdx.x;
+    int64_t done = 0;
+    if (vec) {
+        // four independent 16-byte loads in flight per thread
+        const uint4 *s4 = reinterpret_cast<const uint4 *>(src);
+        const int64_t n4 = n / 4;
+        int64_t v = t0;
+        for (; v + 3 * stride < n4; v += 4 * stride) {
+            uint4 u[4];
+#pragma unroll
+            for (int i = 0; i < 4; i++) u[i] = __ldg(s4 + v + i * stride);
+#pragma unroll
+            for (int i = 0; i < 4; i++) {
+                const uint32_t b[4] = {u[i].x & 0x7FFFFFFFu, u[i].y & 0x7FFFFFFFu, u[i].z & 0x7FFFFFFFu,
+                                       u[i].w & 0x7FFFFFFFu};
+#pragma unroll
+                for (int j = 0; j < 4; j++)
+                    if (b[j] < 0x7F800000u && b[j] > m) m = b[j];
+            }
+        }
+        for (; v < n4; v += stride) {
+            const uint4 u = __ldg(s4 + v);
+            const uint32_t b[4] = {u.x & 0x7FFFFFFFu, u.y & 0x7FFFFFFFu, u.z & 0x7FFFFFFFu, u.w & 0x7FFFFFFFu};
+#pragma unroll
+            for (int j = 0; j < 4; j++)
+                if (b[j] < 0x7F800000u && b[j] > m) m = b[j];
+        }
+        done = n4 * 4;
+    }
+    for (int64_t i = done + t0; i < n; i += stride) {
+        const uint32_t b = __float_as_uint(src[i]) & 0x7FFFFFFFu;
+        if (b < 0x7F800000u && b > m) m = b;
+    }
+    for (int o = 16; o > 0; o >>= 1) m = max(m, __shfl_xor_sync(0xffffffffu, m, o));
+    if ((threadIdx.x & 31) == 0 && m) atomicMax(word, m);
+}
+
+// hi = fp16(x 2^e), lo = fp16(x 2^e - hi) of 8 consecutive values.
+__device__ __forceinline__ void split8_f16(const float (&x)[8], float sc, uint4 &h, uint4 &l) {
+    uint32_t hw[4], lw[4];
+#pragma unroll
+    for (int j = 0; j < 4; j++) {
+        const float a = x[2 * j] * sc, b = x[2 * j + 1] * sc;
+        const __half ha = __float2half_rn(a), hb = __float2half_rn(b);
+        const __half la = __float2half_rn(a - __half2float(ha)), lb = __float2half_rn(b - __half2float(hb));
+        hw[j] = (uint32_t)__half_as_ushort(ha) | ((uint32_t)__half_as_ushort(hb) << 16);
+        lw[j] = (uint32_t)__half_as_ushort(la) | ((uint32_t)__half_as_ushort(lb) << 16);
+    }
+    h = make_uint4(hw[0], hw[1], hw[2], hw[3]);
+    l = make_uint4(lw[0], lw[1], lw[2], lw[3]);
+}
+
+// X [rows, cols] -> fp16 hi/lo [rows, pitch] (pitch = cols rounded up to 8,
+// padding written as zero), scaled by 2^e from the max word.  8 columns per
+// thread step: 32-byte loads when the source allows, 16-byte stores.
+__global__ void __launch_bounds__(256) split16_kernel(const float *__restrict__ src, int64_t rows, int64_t cols,
+                                                      int64_t pitch, int vec, const uint32_t *__restrict__ word,
+                                                      __half *__restrict__ hi, __half *__restrict__ lo) {
+    const float sc = pow2f(split_exp(*word));
+    const int64_t q = pitch / 8;
+    const int64_t n = rows * q;
+    for (int64_t v = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; v < n;
+         v += (int64_t)gridDim.x * blockDim.x) {
+        const int64_t r = v / q, k = (v - r * q) * 8;
+        float x[8];
+        const float *p = src + r * cols + k;
+        if (vec && k + 8 <= cols) {
+            const float4 t0 = __ldg(reinterpret_cast<const float4 *>(p));
+            const float4 t1 = __ldg(reinterpret_cast<const float4 *>(p) + 1);
+            x[0] = t0.x; x[1] = t0.y; x[2] = t0.z; x[3] = t0.w;
+            x[4] = t1.x; x[5] = t1.y; x[6] = t1.z; x[7] = t1.w;
+        } else {
+#pragma unroll
+            for (int j = 0; j < 8; j++) x[j] = (k + j < cols) ? p[j] : 0.0f;
+        }
+        uint4 h, l;
+        split8_f16(x, sc, h, l);
+        *reinterpret_cast<uint4 *>(hi + r * pitch + k) = h;
+        *reinterpret_cast<uint4 *>(lo + r * pitch + k) = l;
+    }
+}
+
+// hi = fp16(x 2^e), lo = fp16(x 2^e - hi) of 4 consecutive values, packed.
+__device__ __forceinline__ void split4_f16(const float (&x)[4], float sc, uint2 &h, uint2 &l) {
+    uint32_t hw[2], lw[2];
+#pragma unroll
+    for (int j = 0; j < 2; j++) {
+        const float a = x[2 * j] * sc, b = x[2 * j + 1] * sc;
+        const __half ha = __float2half_rn(a), hb = __float2half_rn(b);
+        const __half la = __float2half_rn(a - __half2float(ha)), lb = __float2half_rn(b - __half2float(hb));
+        hw[j] = (uint32_t)__half_as_ushort(ha) | ((uint32_t)__half_as_ushort(hb) << 16);
+        lw[j] = (uint32_t)__half_as_ushort(la) | ((uint32_t)__half_as_ushort(lb) << 16);
+    }
+    h = make_uint2(hw[0], hw[1]);
+    l = make_uint2(lw[0], lw[1]);
+}
+
+// The fp16 split of X^T ([cols, pitch], pitch = rows rounded up to 8) and,
+// with phi / plo set, of X in its stored layout ([rows, ppitch], ppitch =
+// cols rounded up to 8) from the same loads; split_t_kernel's tiling, 8-byte
+// stores of 4 halves.  The first thread copies the max word to pword.
+__global__ void __launch_bounds__(256) split16_t_kernel(const float *__restrict__ src, int64_t rows, int64_t cols,
+                                                        int64_t pitch, int64_t tiles_c, int vec_in,
+                                                        const uint32_t *__restrict__ word, __half *__restrict__ hi,
+                                                        __half *__restrict__ lo, __half *__restrict__ phi,
+                                                        __half *__restrict__ plo, int64_t ppitch,
+                                                        uint32_t *__restrict__ pword) {
+    __shared__ float tile[64][65];
+    const uint32_t mw = *word;
+    const float sc = pow2f(split_exp(mw));
+    if (pword && blockIdx.x == 0 && threadIdx.x == 0) *pword = mw;
+    const int64_t c0 = (blockIdx.x % tiles_c) * 64, r0 = (blockIdx.x / tiles_c) * 64;
+    const int q = threadIdx.x & 15, w = threadIdx.x >> 4;
+#pragma unroll
+    for (int pass = 0; pass < 4; pass++) {
+        const int i = pass * 16 + w;
+        const int64_t r = r0 + i, c = c0 + 4 * q;
+        float v[4] = {0.0f, 0.0f, 0.0f, 0.0f};
+        if (r < rows) {
+            if (vec_in && c + 4 <= cols) {
+                const float4 t = __ldg(reinterpret_cast<const float4 *>(src + r * cols + c));
+                v[0] = t.x; v[1] = t.y; v[2] = t.z; v[3] = t.w;
+            } else {
+#pragma unroll
+                for (int k = 0; k < 4; k++) v[k] = (c + k < cols) ? src[r * cols + c + k] : 0.0f;
+            }
+        }
+#pragma unroll
+        for (int k = 0; k < 4; k++) tile[i][4 * q + k] = v[k];
+        if (phi && r < rows && c < ppitch) {  // columns past `cols` were loaded as zero
+            uint2 h, l;
+            split4_f16(v, sc, h, l);
+            *reinterpret_cast<uint2 *>(phi + r * ppitch + c) = h;
+            *reinterpret_cast<uint2 *>(plo + r * ppitch + c) = l;
+        }
+    }
+    __syncthreads();
+#pragma unroll
+    for (int pass = 0; pass < 4; pass++) {
+        const int j = pass * 16 + w;
+        const int64_t c = c0 + j, r = r0 + 4 * q;
+        if (c >= cols || r >= pitch) continue;
+        const float x[4] = {tile[4 * q][j], tile[4 * q + 1][j], tile[4 * q + 2][j], tile[4 * q + 3][j]};
+        uint2 h, l;
+        split4_f16(x, sc, h, l);
+        *reinterpret_cast<uint2 *>(hi + c * pitch + r) = h;
+        *reinterpret_cast<uint2 *>(lo + c * pitch + r) = l;
+    }
+}
+
 // ---- host side -------------------------------------------------------------------------
 static PFN_cuTensorMapEncodeTiled_v12000 encode_fn() {
     static PFN_cuTensorMapEncodeTiled_v12000 fn = nullptr;
@@ -672,33 +885,63 @@ static PFN_cuTensorMapEncodeTiled_v12000 encode_fn() {
     return fn;
 }
 
-inline int64_t split_pitch(int64_t cols) { return ceil_div(cols, 4) * 4; }
+// The operand split mode, fixed for the process: 3xFP16 unless
+// J4C_GEMM_SPLIT is "tf32" (3xTF32).  Splits and GEMMs must agree, so it is
+// read once.
+bool split_fp16() {
+    static const bool f16 = [] {
+        const char *v = getenv("J4C_GEMM_SPLIT");
+        return !(v && (v[0] == 't' || v[0] == 'T') && (v[1] == 'f' || v[1] == 'F') && v[2] == '3' && v[3] == '2');
+    }();
+    return f16;
+}
 
-// Tensor map of a hi or lo array [rows, pitch] (pitch * 4 bytes per row).
-//   K-major use (rows = M or N, cols = K): box {BK, box_rows}, BK*4-byte swizzle.
-//   MN-major use (rows = K, cols = M or N): box {32, BK}, 128-byte swizzle of 32-byte atoms.
+// Elements per row of a split array: cols rounded up to a 16-byte multiple.
+inline int64_t split_pitch(int64_t cols) { return split_fp16() ? ceil_div(cols, 8) * 8 : ceil_div(cols, 4) * 4; }
+inline int64_t split_esize() { return split_fp16() ? 2 : 4; }
+
+// Bytes of one hi or lo array of an operand [rows, cols]; an fp16 hi array is
+// followed by its 32-bit max word (16 bytes reserved).
+inline int64_t split_bytes(int64_t rows, int64_t cols) {
+    return rows * split_pitch(cols) * split_esize() + (split_fp16() ? 16 : 0);
+}
+
+// The max word of an fp16 hi array of an operand [rows, cols].
+inline uint32_t *split_word(const float *hi, int64_t rows, int64_t cols) {
+    return reinterpret_cast<uint32_t *>(reinterpret_cast<char *>(const_cast<float *>(hi)) +
+                                        rows * split_pitch(cols) * 2);
+}
+
+// Tensor map of a hi or lo array [rows, pitch] (pitch * esize bytes per row).
+//   K-major use (rows = M or N, cols = K): box {BKE, box_rows}, BK*4-byte swizzle.
+//   MN-major use (rows = K, cols = M or N): box {MNW, BKE}; tf32: 128-byte
+//   swizzle of 32-byte atoms, fp16: 128-byte swizzle.
 // Columns past `cols` and rows past `rows` read as zero (TMA fill).
 static int make_map(CUtensorMap *map, const float *base, int64_t rows, int64_t cols, bool mn, int box_rows,
                     int bk, int64_t batch) {
     auto fn = encode_fn();
     if (!fn) return set_error(J4C_E_CUDA, "cuTensorMapEncodeTiled is unavailable");
+    const bool f16 = split_fp16();
+    const int64_t es = split_esize();
+    const int bke = bk * 4 / (int)es;
     // [batch][rows, pitch]: batch entries back to back (batch = 1 for an operand shared by all)
     cuuint64_t dims[3] = {(cuuint64_t)cols, (cuuint64_t)rows, (cuuint64_t)batch};
-    cuuint64_t strides[2] = {(cuuint64_t)split_pitch(cols) * 4, (cuuint64_t)(rows * split_pitch(cols) * 4)};
+    cuuint64_t strides[2] = {(cuuint64_t)(split_pitch(cols) * es), (cuuint64_t)(rows * split_pitch(cols) * es)};
     cuuint32_t box[3];
     CUtensorMapSwizzle sw;
     if (mn) {
-        box[0] = MNW;
-        box[1] = (cuuint32_t)bk;
-        sw = CU_TENSOR_MAP_SWIZZLE_128B_ATOM_32B;
+        box[0] = f16 ? 64 : 32;
+        box[1] = (cuuint32_t)bke;
+        sw = f16 ? CU_TENSOR_MAP_SWIZZLE_128B : CU_TENSOR_MAP_SWIZZLE_128B_ATOM_32B;
     } else {
-        box[0] = (cuuint32_t)bk;
+        box[0] = (cuuint32_t)bke;
         box[1] = (cuuint32_t)box_rows;
         sw = bk == 32 ? CU_TENSOR_MAP_SWIZZLE_128B : CU_TENSOR_MAP_SWIZZLE_64B;
     }
     box[2] = 1;
     cuuint32_t estr[3] = {1, 1, 1};
-    CUresult r = fn(map, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 3, const_cast<float *>(base), dims, strides, box,
+    CUresult r = fn(map, f16 ? CU_TENSOR_MAP_DATA_TYPE_FLOAT16 : CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 3,
+                    const_cast<float *>(base), dims, strides, box,
                     estr, CU_TENSOR_MAP_INTERLEAVE_NONE, sw, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
                     CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
     if (r != CUDA_SUCCESS) return set_error(J4C_E_CUDA, "cuTensorMapEncodeTiled failed (%d)", (int)r);
@@ -740,12 +983,12 @@ size_t tail_scratch_bound(int64_t m, int64_t n, int64_t batch) {
     return most;
 }
 
-template <int BN, int STAGES, int BK, bool A_MN, bool B_MN>
+template <int BN, int STAGES, int BK, bool A_MN, bool B_MN, bool F16>
 static int launch_gemm(const float *ah, const float *al, const float *bh, const float *bl, float *c,
                        int64_t M, int64_t N, int64_t K, bool store_t, const Epilogue &ep, int64_t batch,
                        bool a_bat, bool b_bat, void *tail_ws, cudaStream_t s) {
-    using Q = Cfg<BN, STAGES, BK>;
-    auto kernel = gemm_3xtf32_kernel<BN, STAGES, BK, A_MN, B_MN>;
+    using Q = Cfg<BN, STAGES, BK, F16>;
+    auto kernel = gemm_3xtf32_kernel<BN, STAGES, BK, A_MN, B_MN, F16>;
     static std::mutex mu;
     static std::vector<char> configured;
     int dev = 0;
@@ -771,7 +1014,7 @@ static int launch_gemm(const float *ah, const float *al, const float *bh, const 
     if (!status) return set_error(J4C_E_OOM, "no device status word");
     const int64_t tiles = ceil_div(M, BM) * ceil_div(N, BN) * batch;
     if (tiles >= (1ll << 30)) return set_error(J4C_E_UNSUPPORTED, "dot: too many output tiles");
-    const int64_t num_kb = ceil_div(K, BK);
+    const int64_t num_kb = ceil_div(K, Q::BKE);
     const TailPlan tp = tail_plan(tiles, num_kb, Q::CHUNK_KB, sm_count());
     const int64_t units = tp.full_tiles + (tiles - tp.full_tiles) * tp.splits;
     const int grid = (int)std::min<int64_t>(units, sm_count());
@@ -790,29 +1033,41 @@ static int launch_gemm(const float *ah, const float *al, const float *bh, const 
         arrivals = reinterpret_cast<int *>(part + (tiles - tp.full_tiles) * tp.splits * BM * BN);
         J4C_CUDA(cudaMemsetAsync(arrivals, 0, (size_t)((tiles - tp.full_tiles) * kEpiWarps) * sizeof(int), s));
     }
+    const uint32_t *amax = F16 ? split_word(ah, ar * ab, ac) : nullptr;
+    const uint32_t *bmax = F16 ? split_word(bh, br * bb, bc) : nullptr;
     kernel<<<grid, kThreads, Q::SMEM_BYTES, s>>>(mAh, mAl, mBh, mBl, c, (int)M, (int)N, (int)num_kb,
                                                  store_t ? 0 : vec, store_t ? 1 : 0, ep, (int)batch, a_bat ? 1 : 0,
-                                                 b_bat ? 1 : 0, status, (int)tp.full_tiles, tp.splits, part, arrivals);
+                                                 b_bat ? 1 : 0, status, (int)tp.full_tiles, tp.splits, part, arrivals,
+                                                 amax, bmax);
     J4C_LAUNCH_CHECK("gemm_3xtf32_kernel");
     if (owned) return scratch_free(owned, s);
     return J4C_OK;
 }
 
-template <int BN, int STAGES, int BK>
+template <int BN, int STAGES, int BK, bool F16>
 static int launch_gemm_any(const float *ah, const float *al, const float *bh, const float *bl, float *c,
                            int64_t M, int64_t N, int64_t K, bool a_mn, bool b_mn, const Epilogue &ep,
                            int64_t batch, bool a_bat, bool b_bat, void *tail_ws, cudaStream_t s) {
     if (!a_mn && !b_mn)
-        return launch_gemm<BN, STAGES, BK, false, false>(ah, al, bh, bl, c, M, N, K, false, ep, batch, a_bat, b_bat, tail_ws, s);
+        return launch_gemm<BN, STAGES, BK, false, false, F16>(ah, al, bh, bl, c, M, N, K, false, ep, batch, a_bat, b_bat, tail_ws, s);
     if (a_mn && !b_mn)
-        return launch_gemm<BN, STAGES, BK, true, false>(ah, al, bh, bl, c, M, N, K, false, ep, batch, a_bat, b_bat, tail_ws, s);
+        return launch_gemm<BN, STAGES, BK, true, false, F16>(ah, al, bh, bl, c, M, N, K, false, ep, batch, a_bat, b_bat, tail_ws, s);
     // The wide (BN = 256) operand is read MN-major at a smem cost that
     // throttles the tensor pipe, so a K-major A with an MN-major B runs as
     // C^T = op(B)^T . op(A)^T: B's split becomes the (MN-major) A operand,
     // A's the (K-major) B operand, and the epilogue stores transposed.
     if (!a_mn && b_mn)
-        return launch_gemm<BN, STAGES, BK, true, false>(bh, bl, ah, al, c, N, M, K, true, ep, batch, b_bat, a_bat, tail_ws, s);
-    return launch_gemm<BN, STAGES, BK, true, true>(ah, al, bh, bl, c, M, N, K, false, ep, batch, a_bat, b_bat, tail_ws, s);
+        return launch_gemm<BN, STAGES, BK, true, false, F16>(bh, bl, ah, al, c, N, M, K, true, ep, batch, b_bat, a_bat, tail_ws, s);
+    return launch_gemm<BN, STAGES, BK, true, true, F16>(ah, al, bh, bl, c, M, N, K, false, ep, batch, a_bat, b_bat, tail_ws, s);
+}
+
+// *word = the bits of X's max finite |x| (n elements).
+static int absmax(const float *src, int64_t n, uint32_t *word, cudaStream_t s) {
+    J4C_CUDA(cudaMemsetAsync(word, 0, sizeof(uint32_t), s));
+    const int vec = aligned16(src);
+    absmax_kernel<<<grid_for(vec ? ceil_div(n, 16) : n, 256, 8), 256, 0, s>>>(src, n, vec, word);
+    J4C_LAUNCH_CHECK("absmax_kernel");
+    return J4C_OK;
 }
 
 // The split of X^T, and with phi / plo also X's own split, in one pass.
@@ -826,6 +1081,17 @@ int split_t(const float *src, int64_t rows, int64_t cols, float *hi, float *lo, 
     const int64_t tiles_c = ceil_div(cols, 64), tiles_r = ceil_div(pitch, 64);
     J4C_REQUIRE(tiles_c * tiles_r < (1ll << 31), "split: array too large");
     const int vec_in = (cols % 4 == 0) && aligned16(src);
+    if (split_fp16()) {
+        uint32_t *word = split_word(hi, cols, rows);
+        int rc = absmax(src, rows * cols, word, s);
+        if (rc) return rc;
+        split16_t_kernel<<<(unsigned)(tiles_c * tiles_r), 256, 0, s>>>(
+            src, rows, cols, pitch, tiles_c, vec_in, word, reinterpret_cast<__half *>(hi),
+            reinterpret_cast<__half *>(lo), reinterpret_cast<__half *>(phi), reinterpret_cast<__half *>(plo),
+            split_pitch(cols), phi ? split_word(phi, rows, cols) : nullptr);
+        J4C_LAUNCH_CHECK("split16_t_kernel");
+        return J4C_OK;
+    }
     split_t_kernel<<<(unsigned)(tiles_c * tiles_r), 256, 0, s>>>(src, rows, cols, pitch, tiles_c, vec_in, hi, lo,
                                                                  phi, plo, split_pitch(cols));
     J4C_LAUNCH_CHECK("split_t_kernel");
@@ -837,6 +1103,15 @@ int split(const float *src, int64_t rows, int64_t cols, float *hi, float *lo, cu
     J4C_REQUIRE(aligned16(hi) && aligned16(lo), "split: hi/lo must be 16-byte aligned");
     const int64_t pitch = split_pitch(cols);
     const int vec = (cols % 4 == 0) && aligned16(src);
+    if (split_fp16()) {
+        uint32_t *word = split_word(hi, rows, cols);
+        int rc = absmax(src, rows * cols, word, s);
+        if (rc) return rc;
+        split16_kernel<<<grid_for(rows * (pitch / 8), 256), 256, 0, s>>>(
+            src, rows, cols, pitch, vec, word, reinterpret_cast<__half *>(hi), reinterpret_cast<__half *>(lo));
+        J4C_LAUNCH_CHECK("split16_kernel");
+        return J4C_OK;
+    }
     split_kernel<<<grid_for(rows * (pitch / 4), 256), 256, 0, s>>>(src, rows, cols, pitch, vec, hi, lo);
     J4C_LAUNCH_CHECK("split_kernel");
     return J4C_OK;
@@ -849,15 +1124,25 @@ bool tc_gemm_supported(int64_t M, int64_t K, int64_t N) {
     return M >= 1 && N >= 1 && K >= 1 && M < (1ll << 31) && N < (1ll << 31) && K < (1ll << 31);
 }
 
-// hi + lo floats of one operand stored [rows, cols]
-static int64_t split_floats(int64_t rows, int64_t cols) { return 2 * rows * tc::split_pitch(cols); }
+// Bytes of one hi or lo array of an operand stored [rows, cols], 256-byte aligned.
+static int64_t split_buf(int64_t rows, int64_t cols) { return ceil_div(tc::split_bytes(rows, cols), 256) * 256; }
+
+// Floats per row that a caller allocates for one hi or lo array of an
+// operand with `cols` columns: rows * this floats hold split_bytes(rows, cols)
+// for every rows >= 1 (3xFP16: 2-byte halves plus the 16-byte max word).
+int64_t tc_split_alloc_pitch(int64_t cols) {
+    return tc::split_fp16() ? tc::split_pitch(cols) / 2 + 4 : tc::split_pitch(cols);
+}
+
+// 1 for the 3xFP16 split, 0 for 3xTF32.
+int tc_split_kind() { return tc::split_fp16() ? 1 : 0; }
 
 int tc_gemm_workspace(int64_t M, int64_t K, int64_t N, size_t *bytes) {
-    // the larger of the two storage orders of each operand, then the scratch
-    // of a tail split (256-byte aligned)
-    const int64_t a = std::max(split_floats(M, K), split_floats(K, M));
-    const int64_t b = std::max(split_floats(K, N), split_floats(N, K));
-    *bytes = ceil_div((int64_t)((a + b) * sizeof(float)), 256) * 256 + tc::tail_scratch_bound(M, N, 1);
+    // hi and lo of the larger of the two storage orders of each operand,
+    // then the scratch of a tail split
+    const int64_t a = 2 * std::max(split_buf(M, K), split_buf(K, M));
+    const int64_t b = 2 * std::max(split_buf(K, N), split_buf(N, K));
+    *bytes = (size_t)(a + b) + tc::tail_scratch_bound(M, N, 1);
     return J4C_OK;
 }
 
@@ -891,9 +1176,11 @@ static int gemm_presplit_ws(const float *ah, const float *al, const float *bh, c
     }();
     const tc::Epilogue ep{bias, mask, act};
     const bool ab = a_batched != 0, bb = b_batched != 0;
+    if (tc::split_fp16())
+        return tc::launch_gemm_any<256, 4, 16, true>(ah, al, bh, bl, c, M, N, K, a_mn, b_mn, ep, batch, ab, bb, tail_ws, s);
     if (variant == 0)
-        return tc::launch_gemm_any<256, 2, 32>(ah, al, bh, bl, c, M, N, K, a_mn, b_mn, ep, batch, ab, bb, tail_ws, s);
-    return tc::launch_gemm_any<256, 4, 16>(ah, al, bh, bl, c, M, N, K, a_mn, b_mn, ep, batch, ab, bb, tail_ws, s);
+        return tc::launch_gemm_any<256, 2, 32, false>(ah, al, bh, bl, c, M, N, K, a_mn, b_mn, ep, batch, ab, bb, tail_ws, s);
+    return tc::launch_gemm_any<256, 4, 16, false>(ah, al, bh, bl, c, M, N, K, a_mn, b_mn, ep, batch, ab, bb, tail_ws, s);
 }
 
 int tc_gemm_presplit(const float *ah, const float *al, const float *bh, const float *bl, float *c, int64_t M,
@@ -908,15 +1195,15 @@ int tc_gemm_f32(const float *a, const float *b, float *c, int64_t M, int64_t K, 
     J4C_REQUIRE(aligned16(ws), "dot: workspace must be 16-byte aligned");
     const int64_t ar = trans_a ? K : M, ac = trans_a ? M : K;  // A as stored
     const int64_t br = trans_b ? N : K, bc = trans_b ? K : N;  // B as stored
-    float *ah = static_cast<float *>(ws);
-    float *al = ah + ar * tc::split_pitch(ac);
-    float *bh = al + ar * tc::split_pitch(ac);
     const bool b_transposed = trans_a && !trans_b;  // B is split as B^T: [bc, pitch(br)]
-    float *bl = bh + (b_transposed ? bc * tc::split_pitch(br) : br * tc::split_pitch(bc));
+    char *w = static_cast<char *>(ws);
+    float *ah = reinterpret_cast<float *>(w);
+    float *al = reinterpret_cast<float *>(w + split_buf(ar, ac));
+    float *bh = reinterpret_cast<float *>(w + 2 * split_buf(ar, ac));
+    float *bl = reinterpret_cast<float *>(w + 2 * split_buf(ar, ac) +
+                                          (b_transposed ? split_buf(bc, br) : split_buf(br, bc)));
     // the tail-split scratch follows the largest layout of both splits
-    const int64_t a_fl = std::max(split_floats(M, K), split_floats(K, M));
-    const int64_t b_fl = std::max(split_floats(K, N), split_floats(N, K));
-    void *tail_ws = static_cast<char *>(ws) + ceil_div((int64_t)((a_fl + b_fl) * sizeof(float)), 256) * 256;
+    void *tail_ws = w + 2 * std::max(split_buf(M, K), split_buf(K, M)) + 2 * std::max(split_buf(K, N), split_buf(N, K));
     int rc;
     if ((rc = tc::split(a, ar, ac, ah, al, s))) return rc;
     if (b_transposed) {

@@ -280,26 +280,58 @@ def test_empty_and_single_element(J):
     assert e.exp().shape() == J.Shape(0, 3)
 
 
+def _split_parts(hi, lo, rows, cols):
+    """Decode split arrays of an operand [rows, cols] in the library's format:
+    (hi, lo) as float64 [rows, cols] in x's units, their padding columns, and
+    the quantum below which an element's split is exact to an absolute error
+    (3xFP16: the FP16 subnormal step in x's units; 3xTF32: 0)."""
+    from jax4j_b200.core import split_kind
+    if split_kind() == 1:
+        p = (cols + 7) // 8 * 8
+        hb = hi.cpu().numpy().view(np.uint8)
+        lb = lo.cpu().numpy().view(np.uint8)
+        h = hb[:rows * p * 2].view(np.float16).reshape(rows, p).astype(np.float64)
+        l = lb[:rows * p * 2].view(np.float16).reshape(rows, p).astype(np.float64)
+        mx = float(hb[rows * p * 2:rows * p * 2 + 4].view(np.float32)[0])
+        e = 0 if mx == 0 else int(np.clip(14 - (np.frexp(np.float32(mx))[1] - 1), -100, 100))
+        return h[:, :cols] * 2.0 ** -e, l[:, :cols] * 2.0 ** -e, (h[:, cols:], l[:, cols:]), 2.0 ** (-24 - e), mx
+    p = (cols + 3) // 4 * 4
+    h = hi.cpu().numpy()[:rows * p].reshape(rows, p)
+    l = lo.cpu().numpy()[:rows * p].reshape(rows, p)
+    assert np.all(h[:, :cols].view(np.uint32) & 0x1FFF == 0) and np.all(l[:, :cols].view(np.uint32) & 0x1FFF == 0)
+    return h[:, :cols].astype(np.float64), l[:, :cols].astype(np.float64), (h[:, cols:], l[:, cols:]), 0.0, None
+
+
+def _split_written_bytes(rows, cols):
+    """Bytes of a hi array that a split writes (the max word included) and of a lo array."""
+    from jax4j_b200.core import split_kind
+    if split_kind() == 1:
+        n = rows * ((cols + 7) // 8 * 8) * 2
+        return n + 4, n
+    n = rows * ((cols + 3) // 4 * 4) * 4
+    return n, n
+
+
 @pytest.mark.parametrize("rows,cols", [(1, 1), (3, 5), (37, 53), (64, 1000), (129, 4097)])
 def test_split_f32_layout(J, rows, cols):
-    """j4c_split_f32: hi is TF32 (low 13 mantissa bits clear), lo = tf32(x - hi),
-    rows padded to j4c_split_pitch(cols) with zeros."""
+    """j4c_split_f32 in the library's format (3xFP16: hi = fp16(x 2^e), lo =
+    fp16(x 2^e - hi), the max word after hi; 3xTF32: hi = tf32(x), lo =
+    tf32(x - hi)): hi + lo = x to 2^-21 relative (plus the FP16 subnormal
+    step for elements far below the array's max), padding zero."""
     import torch
     r = rng(rows * 31 + cols)
     x = (r.standard_normal((rows, cols)) * np.exp(r.uniform(-20, 20, (rows, cols)))).astype(np.float32)
     a = dev(J, x)
     pitch = _lib.lib().j4c_split_pitch(cols)
-    assert pitch % 4 == 0 and cols <= pitch < cols + 4
-    hi = torch.full((rows * pitch,), 7.0, dtype=torch.float32, device=a.tensor().device)
-    lo = torch.full((rows * pitch,), 7.0, dtype=torch.float32, device=a.tensor().device)
+    hi = torch.full((max(rows * pitch, 4),), 7.0, dtype=torch.float32, device=a.tensor().device)
+    lo = torch.full((max(rows * pitch, 4),), 7.0, dtype=torch.float32, device=a.tensor().device)
     _lib.call("j4c_split_f32", a.data_ptr(), rows, cols, hi.data_ptr(), lo.data_ptr(), a._stream())
-    h = hi.cpu().numpy().reshape(rows, pitch)
-    l = lo.cpu().numpy().reshape(rows, pitch)
-    assert np.all(h[:, cols:] == 0) and np.all(l[:, cols:] == 0)
-    h, l = h[:, :cols], l[:, :cols]
-    assert np.all(h.view(np.uint32) & 0x1FFF == 0) and np.all(l.view(np.uint32) & 0x1FFF == 0)
-    err = np.abs(h.astype(np.float64) + l - x)
-    assert np.all(err <= np.abs(x) * 2.0 ** -21)
+    h, l, pads, quantum, mx = _split_parts(hi, lo, rows, cols)
+    assert all(np.all(pd == 0) for pd in pads)
+    if mx is not None:
+        assert mx == np.abs(x).max()
+    err = np.abs(h + l - x)
+    assert np.all(err <= np.abs(x) * 2.0 ** -21 + quantum)
 
 
 @pytest.mark.parametrize("ta,tb", [(0, 0), (1, 0), (0, 1), (1, 1)])
@@ -346,16 +378,14 @@ def test_split_f32_transposed_layout(J, rows, cols):
     x = r.standard_normal((rows, cols)).astype(np.float32)
     a = dev(J, x)
     pitch = _lib.lib().j4c_split_pitch(rows)
-    hi = torch.full((cols * pitch,), 7.0, dtype=torch.float32, device=a.tensor().device)
-    lo = torch.full((cols * pitch,), 7.0, dtype=torch.float32, device=a.tensor().device)
+    hi = torch.full((max(cols * pitch, 4),), 7.0, dtype=torch.float32, device=a.tensor().device)
+    lo = torch.full((max(cols * pitch, 4),), 7.0, dtype=torch.float32, device=a.tensor().device)
     _lib.call("j4c_split_f32_transposed", a.data_ptr(), rows, cols, hi.data_ptr(), lo.data_ptr(), a._stream())
-    h = hi.cpu().numpy().reshape(cols, pitch)
-    l = lo.cpu().numpy().reshape(cols, pitch)
-    assert np.all(h[:, rows:] == 0) and np.all(l[:, rows:] == 0)
-    h, l = h[:, :rows], l[:, :rows]
-    assert np.all(h.view(np.uint32) & 0x1FFF == 0)
-    err = np.abs(h.astype(np.float64) + l - x.T)
-    assert np.all(err <= np.abs(x.T) * 2.0 ** -21)
+    h, l, pads, quantum, _ = _split_parts(hi, lo, cols, rows)
+    assert all(np.all(pd == 0) for pd in pads)
+    err = np.abs(h + l - x.T)
+    assert np.all(err <= np.abs(x.T) * 2.0 ** -21 + quantum)
+
 
 
 @pytest.mark.parametrize("ta,tb", [(0, 0), (1, 0), (0, 1), (1, 1)])
@@ -518,5 +548,6 @@ def test_split_f32_both_equals_the_two_passes(J, rows, cols):
     _lib.call("j4c_split_f32", a.data_ptr(), rows, cols, ref[0].data_ptr(), ref[1].data_ptr(), a._stream())
     _lib.call("j4c_split_f32_transposed", a.data_ptr(), rows, cols, ref[2].data_ptr(), ref[3].data_ptr(),
               a._stream())
-    for o, e in zip(out, ref):
-        assert torch.equal(o, e)
+    (hb, lb), (hbt, lbt) = _split_written_bytes(rows, cols), _split_written_bytes(cols, rows)
+    for o, e, nb in zip(out, ref, (hb, lb, hbt, lbt)):
+        assert torch.equal(o.view(torch.uint8)[:nb], e.view(torch.uint8)[:nb])
