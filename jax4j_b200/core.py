@@ -870,7 +870,7 @@ def _dot_raw(a: "ConcreteNDArray", b: "ConcreteNDArray", trans_a: bool, trans_b:
         ev1.record()
         if a._dtype == DType.FLOAT32:
             nbytes = split_bytes_per_element() * (M * K + K * N) \
-                + 4 * M * N * (1 + int(act) + int(mask is not None)) + (4 * N if bias is not None else 0)
+                + 4 * M * N * (int(store_c) + int(act) + int(mask is not None)) + (4 * N if bias is not None else 0)
         else:
             nbytes = a._dtype.byteSize() * (M * K + K * N + M * N)
         timing.append((ev0, ev1, 2.0 * M * N * K, nbytes))
