@@ -308,6 +308,14 @@ J4C_API int j4c_split_f32_transposed(const float *x, int64_t rows, int64_t cols,
  * the left operand of g . W^T and the right one of x^T . g). */
 J4C_API int j4c_split_f32_both(const float *x, int64_t rows, int64_t cols, float *hi, float *lo, float *hi_t,
                                float *lo_t, j4c_stream stream);
+/* Any of the three splits above -- hi/lo only (j4c_split_f32), hi_t/lo_t
+ * only (j4c_split_f32_transposed), or all four (j4c_split_f32_both) -- with
+ * x's max word computed already: max_word (device, may be NULL) holds the
+ * bits of x's largest finite |value| as j4c_dot_split_ep_max's out_max
+ * leaves them, and replaces the split's own max pass under 3xFP16 (ignored
+ * under 3xTF32). */
+J4C_API int j4c_split_f32_ex(const float *x, int64_t rows, int64_t cols, float *hi, float *lo, float *hi_t,
+                             float *lo_t, const uint32_t *max_word, j4c_stream stream);
 J4C_API int j4c_dot_split(const float *a_hi, const float *a_lo, const float *b_hi, const float *b_lo, float *c,
                           int64_t M, int64_t K, int64_t N, int trans_a, int trans_b, j4c_stream stream);
 /* j4c_dot_split with elementwise work fused into the store of C [M, N] (each
@@ -332,6 +340,14 @@ J4C_API int j4c_dot_split_batched(const float *a_hi, const float *a_lo, const fl
 J4C_API int j4c_dot_split_ep(const float *a_hi, const float *a_lo, const float *b_hi, const float *b_lo,
                              float *c, int64_t M, int64_t K, int64_t N, int trans_a, int trans_b,
                              const float *bias, const float *mask, float *act, j4c_stream stream);
+/* j4c_dot_split_ep that also leaves in *out_max (one device uint32) the bits
+ * of the largest finite |value| it writes to act (or to c when act is NULL):
+ * the max word a later j4c_split_f32_ex of that output takes instead of
+ * scanning it again. */
+J4C_API int j4c_dot_split_ep_max(const float *a_hi, const float *a_lo, const float *b_hi, const float *b_lo,
+                                 float *c, int64_t M, int64_t K, int64_t N, int trans_a, int trans_b,
+                                 const float *bias, const float *mask, float *act, uint32_t *out_max,
+                                 j4c_stream stream);
 
 /* ------------------------------------------------------------------ */
 /* Discrete Fourier transforms: replace api/Fft.java's radix-2 host     */

@@ -83,6 +83,8 @@ SIGNATURES = {
     "j4c_dot_split": [P, P, P, P, P, I64, I64, I64, I32, I32, P],
     "j4c_dot_split_ep": [P, P, P, P, P, I64, I64, I64, I32, I32, P, P, P, P],
     "j4c_split_f32_both": [P, I64, I64, P, P, P, P, P],
+    "j4c_split_f32_ex": [P, I64, I64, P, P, P, P, P, P],
+    "j4c_dot_split_ep_max": [P, P, P, P, P, I64, I64, I64, I32, I32, P, P, P, P, P],
     "j4c_fft": [I32, I32, PI64, P, P, P, P, I32, P],
     "j4c_rfft": [I32, I32, PI64, P, P, P, P],
     "j4c_irfft": [I32, I32, PI64, P, P, P, P],

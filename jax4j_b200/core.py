@@ -385,7 +385,7 @@ class ConcreteNDArray(NDArray):
     it has been a dot operand, for the other dots it takes part in.
     """
 
-    __slots__ = ("_t", "_shape", "_dtype", "_device", "_split", "_split_t", "_ready")
+    __slots__ = ("_t", "_shape", "_dtype", "_device", "_split", "_split_t", "_ready", "_absmax")
 
     def __init__(self, data, shape=None, dtype: DType = None, device: Device = None):
         if device is None:
@@ -422,6 +422,7 @@ class ConcreteNDArray(NDArray):
         self._split = None
         self._split_t = None
         self._ready = None  # CUDA event recorded once the value was produced, when tracked
+        self._absmax = None  # device word: bits of max finite |x|, left by the GEMM that wrote x
 
     # ---- construction helpers ----
     @staticmethod
@@ -453,6 +454,7 @@ class ConcreteNDArray(NDArray):
         obj._split = None
         obj._split_t = None
         obj._ready = None
+        obj._absmax = None
         return obj
 
     def _new(self, shape: Shape, dtype: DType) -> torch.Tensor:
@@ -766,8 +768,13 @@ def _tf32_split(x: "ConcreteNDArray", transposed: bool = False):
         n = (cols if transposed else rows) * _lib.lib().j4c_split_pitch(rows if transposed else cols)
         hi = torch.empty(max(n, 4), dtype=torch.float32, device=x._t.device)
         lo = torch.empty(max(n, 4), dtype=torch.float32, device=x._t.device)
-        call("j4c_split_f32_transposed" if transposed else "j4c_split_f32", x._t.data_ptr(), rows, cols,
-             hi.data_ptr(), lo.data_ptr(), x._stream())
+        mx = x._absmax.data_ptr() if x._absmax is not None else None
+        if transposed:
+            call("j4c_split_f32_ex", x._t.data_ptr(), rows, cols, None, None, hi.data_ptr(), lo.data_ptr(), mx,
+                 x._stream())
+        else:
+            call("j4c_split_f32_ex", x._t.data_ptr(), rows, cols, hi.data_ptr(), lo.data_ptr(), None, None, mx,
+                 x._stream())
         s = (hi, lo)
         if transposed:
             x._split_t = s
@@ -788,8 +795,8 @@ def _tf32_split_both(x: "ConcreteNDArray") -> None:
     n, n_t = rows * _lib.lib().j4c_split_pitch(cols), cols * _lib.lib().j4c_split_pitch(rows)
     hi, lo = (torch.empty(max(n, 4), dtype=torch.float32, device=x._t.device) for _ in range(2))
     hi_t, lo_t = (torch.empty(max(n_t, 4), dtype=torch.float32, device=x._t.device) for _ in range(2))
-    call("j4c_split_f32_both", x._t.data_ptr(), rows, cols, hi.data_ptr(), lo.data_ptr(), hi_t.data_ptr(),
-         lo_t.data_ptr(), x._stream())
+    call("j4c_split_f32_ex", x._t.data_ptr(), rows, cols, hi.data_ptr(), lo.data_ptr(), hi_t.data_ptr(),
+         lo_t.data_ptr(), x._absmax.data_ptr() if x._absmax is not None else None, x._stream())
     x._split, x._split_t = (hi, lo), (hi_t, lo_t)
 
 
@@ -827,6 +834,7 @@ def _dot_raw(a: "ConcreteNDArray", b: "ConcreteNDArray", trans_a: bool, trans_b:
     out = torch.empty(M * N if store_c else 0, dtype=a._dtype.torch, device=a._t.device)
     act_out = torch.empty(M * N, dtype=a._dtype.torch, device=a._t.device) if act else None
     timing = DOT_TIMING
+    out_max = None
     if a._dtype == DType.FLOAT32 and M and N and K:
         # tensor-core path: each operand's 3xTF32 split is made once per array.
         # With K the leading dimension of both stored operands (A^T . B, the
@@ -848,11 +856,15 @@ def _dot_raw(a: "ConcreteNDArray", b: "ConcreteNDArray", trans_a: bool, trans_b:
             ev1 = torch.cuda.Event(enable_timing=True)
             ev0.record()
         if epilogue:
-            call("j4c_dot_split_ep", ah.data_ptr(), al.data_ptr(), bh.data_ptr(), bl.data_ptr(),
+            # under 3xFP16 the epilogue also takes the max |value| of the output a later
+            # split will read (the relu output, or C), sparing that split its max pass
+            out_max = torch.empty(1, dtype=torch.int32, device=a._t.device) if split_kind() == 1 else None
+            call("j4c_dot_split_ep_max", ah.data_ptr(), al.data_ptr(), bh.data_ptr(), bl.data_ptr(),
                  out.data_ptr() if store_c else None,
                  M, K, N, int(ta), int(tb), bias.data_ptr() if bias is not None else None,
                  mask.data_ptr() if mask is not None else None,
-                 act_out.data_ptr() if act_out is not None else None, a._stream())
+                 act_out.data_ptr() if act_out is not None else None,
+                 out_max.data_ptr() if out_max is not None else None, a._stream())
         else:
             call("j4c_dot_split", ah.data_ptr(), al.data_ptr(), bh.data_ptr(), bl.data_ptr(), out.data_ptr(),
                  M, K, N, int(ta), int(tb), a._stream())
@@ -876,7 +888,12 @@ def _dot_raw(a: "ConcreteNDArray", b: "ConcreteNDArray", trans_a: bool, trans_b:
         timing.append((ev0, ev1, 2.0 * M * N * K, nbytes))
     c = ConcreteNDArray._wrap(out, Shape(M, N), a._dtype, device) if store_c else None
     if act:
-        return c, ConcreteNDArray._wrap(act_out, Shape(M, N), a._dtype, device)
+        h = ConcreteNDArray._wrap(act_out, Shape(M, N), a._dtype, device)
+        if out_max is not None:
+            h._absmax = out_max
+        return c, h
+    if out_max is not None:
+        c._absmax = out_max
     return c
 
 

@@ -18,7 +18,10 @@ int tc_split_f32_both(const float *x, int64_t rows, int64_t cols, float *hi, flo
                       cudaStream_t s);
 int tc_gemm_presplit(const float *ah, const float *al, const float *bh, const float *bl, float *c, int64_t M,
                      int64_t K, int64_t N, int trans_a, int trans_b, const float *bias, const float *mask,
-                     float *act, int64_t batch, int a_batched, int b_batched, cudaStream_t s);
+                     float *act, int64_t batch, int a_batched, int b_batched, cudaStream_t s,
+                     uint32_t *out_max = nullptr);
+int tc_split_f32_ex(const float *x, int64_t rows, int64_t cols, float *hi, float *lo, float *hi_t, float *lo_t,
+                    const uint32_t *max_in, cudaStream_t s);
 }  // namespace j4c
 
 using namespace j4c;
@@ -95,20 +98,40 @@ int j4c_split_f32_transposed(const float *x, int64_t rows, int64_t cols, float *
     return tc_split_f32_t(x, rows, cols, hi, lo, as_stream(stream));
 }
 
-int j4c_dot_split_ep(const float *a_hi, const float *a_lo, const float *b_hi, const float *b_lo, float *c,
-                     int64_t M, int64_t K, int64_t N, int trans_a, int trans_b, const float *bias,
-                     const float *mask, float *act, j4c_stream stream) {
+int j4c_dot_split_ep_max(const float *a_hi, const float *a_lo, const float *b_hi, const float *b_lo, float *c,
+                         int64_t M, int64_t K, int64_t N, int trans_a, int trans_b, const float *bias,
+                         const float *mask, float *act, uint32_t *out_max, j4c_stream stream) {
     J4C_REQUIRE(M >= 0 && K >= 0 && N >= 0, "j4c_dot_split: negative dimension");
-    if (M == 0 || N == 0) return J4C_OK;
+    if (M == 0 || N == 0) {
+        if (out_max) J4C_CUDA(cudaMemsetAsync(out_max, 0, sizeof(uint32_t), as_stream(stream)));
+        return J4C_OK;
+    }
     J4C_REQUIRE(c || act, "j4c_dot_split: NULL output");
     J4C_REQUIRE(K > 0 || (!bias && !mask && !act), "j4c_dot_split_ep: K = 0 with an epilogue");
-    if (K == 0) return j4c_fill(J4C_FLOAT32, c, M * N, 0.0, stream);
+    if (K == 0) {
+        if (out_max) J4C_CUDA(cudaMemsetAsync(out_max, 0, sizeof(uint32_t), as_stream(stream)));
+        return j4c_fill(J4C_FLOAT32, c, M * N, 0.0, stream);
+    }
     J4C_REQUIRE(a_hi && a_lo && b_hi && b_lo, "j4c_dot_split: NULL operand");
     if (!tc_gemm_supported(M, K, N))
         return set_error(J4C_E_UNSUPPORTED, "j4c_dot_split: shape %lld x %lld x %lld is too large", (long long)M,
                          (long long)K, (long long)N);
     return tc_gemm_presplit(a_hi, a_lo, b_hi, b_lo, c, M, K, N, trans_a, trans_b, bias, mask, act, 1, 0, 0,
-                            as_stream(stream));
+                            as_stream(stream), out_max);
+}
+
+int j4c_dot_split_ep(const float *a_hi, const float *a_lo, const float *b_hi, const float *b_lo, float *c,
+                     int64_t M, int64_t K, int64_t N, int trans_a, int trans_b, const float *bias,
+                     const float *mask, float *act, j4c_stream stream) {
+    return j4c_dot_split_ep_max(a_hi, a_lo, b_hi, b_lo, c, M, K, N, trans_a, trans_b, bias, mask, act, nullptr,
+                                stream);
+}
+
+int j4c_split_f32_ex(const float *x, int64_t rows, int64_t cols, float *hi, float *lo, float *hi_t, float *lo_t,
+                     const uint32_t *max_word, j4c_stream stream) {
+    J4C_REQUIRE(rows >= 0 && cols >= 0, "j4c_split_f32_ex: negative dimension");
+    J4C_REQUIRE(x && (hi || hi_t) && !hi == !lo && !hi_t == !lo_t, "j4c_split_f32_ex: NULL argument");
+    return tc_split_f32_ex(x, rows, cols, hi, lo, hi_t, lo_t, max_word, as_stream(stream));
 }
 
 int j4c_dot_split_batched(const float *a_hi, const float *a_lo, const float *b_hi, const float *b_lo, float *c,

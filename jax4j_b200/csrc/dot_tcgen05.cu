@@ -301,11 +301,21 @@ __device__ __forceinline__ Unit unit_of(int u, int full_tiles, int splits, int n
 //   v = acc + bias[col]            (a bias add broadcast along rows)
 //   v = mask[row][col] > 0 ? v : 0 (relu' given the saved pre-activation)
 //   C[row][col] = v,  act[row][col] = max(0, v)  (Java Math.max rules)
+// and, with out_max set (zeroed by the launch), the bits of the largest
+// finite |value| written to act (or to C when there is no act): the max word
+// a later 3xFP16 split of that output takes instead of its own max pass.
 struct Epilogue {
     const float *bias;
     const float *mask;
     float *act;
+    uint32_t *out_max;
 };
+
+// m = the bits of max(m, |v|) over finite v.
+__device__ __forceinline__ void track_max(uint32_t &m, float v) {
+    const uint32_t b = __float_as_uint(v) & 0x7FFFFFFFu;
+    if (b < 0x7F800000u && b > m) m = b;
+}
 
 __device__ __forceinline__ float ep_relu(float v) { return (0.0f >= v) ? 0.0f : v; }
 
@@ -553,6 +563,7 @@ gemm_3xtf32_kernel(const __grid_constant__ CUtensorMap tAh, const __grid_constan
             }
             const int row = mt * BM + q * 32 + lane;
             const int col0 = nt * BN + cbase;
+            uint32_t mloc = 0;  // max of the values this lane stores (ep.out_max)
             if (store_t) {
                 // C holds the transpose of this product ([N, M]): for each
                 // column the warp's 32 lanes write 32 consecutive floats.
@@ -567,6 +578,7 @@ gemm_3xtf32_kernel(const __grid_constant__ CUtensorMap tAh, const __grid_constan
                             if (mask_b) v = __ldg(mask_b + idx) > 0.0f ? v : 0.0f;
                             if (Cb) Cb[idx] = v;
                             if (act_b) act_b[idx] = ep_relu(v);
+                            if (ep.out_max) track_max(mloc, act_b ? ep_relu(v) : v);
                         }
                     }
                 }
@@ -590,6 +602,10 @@ gemm_3xtf32_kernel(const __grid_constant__ CUtensorMap tAh, const __grid_constan
                         if (act_b)
                             reinterpret_cast<float4 *>(act_b + base)[v4] =
                                 make_float4(ep_relu(x[0]), ep_relu(x[1]), ep_relu(x[2]), ep_relu(x[3]));
+                        if (ep.out_max) {
+#pragma unroll
+                            for (int i = 0; i < 4; i++) track_max(mloc, act_b ? ep_relu(x[i]) : x[i]);
+                        }
                     }
                 } else {
 #pragma unroll
@@ -599,9 +615,14 @@ gemm_3xtf32_kernel(const __grid_constant__ CUtensorMap tAh, const __grid_constan
                             if (mask_b) v = __ldg(mask_b + base + j) > 0.0f ? v : 0.0f;
                             if (Cb) Cb[base + j] = v;
                             if (act_b) act_b[base + j] = ep_relu(v);
+                            if (ep.out_max) track_max(mloc, act_b ? ep_relu(v) : v);
                         }
                     }
                 }
+            }
+            if (ep.out_max) {  // uniform: every lane of the warp gets here
+                for (int o = 16; o > 0; o >>= 1) mloc = max(mloc, __shfl_xor_sync(0xffffffffu, mloc, o));
+                if (lane == 0 && mloc) atomicMax(ep.out_max, mloc);
             }
         }
     }
@@ -1033,6 +1054,7 @@ static int launch_gemm(const float *ah, const float *al, const float *bh, const 
         arrivals = reinterpret_cast<int *>(part + (tiles - tp.full_tiles) * tp.splits * BM * BN);
         J4C_CUDA(cudaMemsetAsync(arrivals, 0, (size_t)((tiles - tp.full_tiles) * kEpiWarps) * sizeof(int), s));
     }
+    if (ep.out_max) J4C_CUDA(cudaMemsetAsync(ep.out_max, 0, sizeof(uint32_t), s));
     const uint32_t *amax = F16 ? split_word(ah, ar * ab, ac) : nullptr;
     const uint32_t *bmax = F16 ? split_word(bh, br * bb, bc) : nullptr;
     kernel<<<grid, kThreads, Q::SMEM_BYTES, s>>>(mAh, mAl, mBh, mBl, c, (int)M, (int)N, (int)num_kb,
@@ -1071,8 +1093,10 @@ static int absmax(const float *src, int64_t n, uint32_t *word, cudaStream_t s) {
 }
 
 // The split of X^T, and with phi / plo also X's own split, in one pass.
+// max_in (3xFP16 only): X's max word computed already (a GEMM epilogue's
+// out_max), copied instead of a max pass.
 int split_t(const float *src, int64_t rows, int64_t cols, float *hi, float *lo, cudaStream_t s,
-            float *phi = nullptr, float *plo = nullptr) {
+            float *phi = nullptr, float *plo = nullptr, const uint32_t *max_in = nullptr) {
     if (rows == 0 || cols == 0) return J4C_OK;
     J4C_REQUIRE(aligned16(hi) && aligned16(lo), "split: hi/lo must be 16-byte aligned");
     J4C_REQUIRE(!phi == !plo && (!phi || (aligned16(phi) && aligned16(plo))),
@@ -1083,8 +1107,12 @@ int split_t(const float *src, int64_t rows, int64_t cols, float *hi, float *lo, 
     const int vec_in = (cols % 4 == 0) && aligned16(src);
     if (split_fp16()) {
         uint32_t *word = split_word(hi, cols, rows);
-        int rc = absmax(src, rows * cols, word, s);
-        if (rc) return rc;
+        if (max_in) {
+            J4C_CUDA(cudaMemcpyAsync(word, max_in, sizeof(uint32_t), cudaMemcpyDeviceToDevice, s));
+        } else {
+            const int rc = absmax(src, rows * cols, word, s);
+            if (rc) return rc;
+        }
         split16_t_kernel<<<(unsigned)(tiles_c * tiles_r), 256, 0, s>>>(
             src, rows, cols, pitch, tiles_c, vec_in, word, reinterpret_cast<__half *>(hi),
             reinterpret_cast<__half *>(lo), reinterpret_cast<__half *>(phi), reinterpret_cast<__half *>(plo),
@@ -1098,15 +1126,20 @@ int split_t(const float *src, int64_t rows, int64_t cols, float *hi, float *lo, 
     return J4C_OK;
 }
 
-int split(const float *src, int64_t rows, int64_t cols, float *hi, float *lo, cudaStream_t s) {
+int split(const float *src, int64_t rows, int64_t cols, float *hi, float *lo, cudaStream_t s,
+          const uint32_t *max_in = nullptr) {
     if (rows == 0 || cols == 0) return J4C_OK;
     J4C_REQUIRE(aligned16(hi) && aligned16(lo), "split: hi/lo must be 16-byte aligned");
     const int64_t pitch = split_pitch(cols);
     const int vec = (cols % 4 == 0) && aligned16(src);
     if (split_fp16()) {
         uint32_t *word = split_word(hi, rows, cols);
-        int rc = absmax(src, rows * cols, word, s);
-        if (rc) return rc;
+        if (max_in) {
+            J4C_CUDA(cudaMemcpyAsync(word, max_in, sizeof(uint32_t), cudaMemcpyDeviceToDevice, s));
+        } else {
+            const int rc = absmax(src, rows * cols, word, s);
+            if (rc) return rc;
+        }
         split16_kernel<<<grid_for(rows * (pitch / 8), 256), 256, 0, s>>>(
             src, rows, cols, pitch, vec, word, reinterpret_cast<__half *>(hi), reinterpret_cast<__half *>(lo));
         J4C_LAUNCH_CHECK("split16_kernel");
@@ -1159,12 +1192,20 @@ int tc_split_f32_both(const float *x, int64_t rows, int64_t cols, float *hi, flo
     return tc::split_t(x, rows, cols, hi_t, lo_t, s, hi, lo);
 }
 
+// Any of the splits (stored layout: hi/lo; transposed: hi_t/lo_t; both in
+// one pass), with X's max word given (3xFP16) or NULL.
+int tc_split_f32_ex(const float *x, int64_t rows, int64_t cols, float *hi, float *lo, float *hi_t, float *lo_t,
+                    const uint32_t *max_in, cudaStream_t s) {
+    if (hi_t) return tc::split_t(x, rows, cols, hi_t, lo_t, s, hi, lo, max_in);
+    return tc::split(x, rows, cols, hi, lo, s, max_in);
+}
+
 // tail_ws: scratch of at least tc::tail_scratch_bound bytes, or NULL to take it
 // from the library's pool when the product splits its last wave.
 static int gemm_presplit_ws(const float *ah, const float *al, const float *bh, const float *bl, float *c, int64_t M,
                             int64_t K, int64_t N, int trans_a, int trans_b, const float *bias, const float *mask,
                             float *act, int64_t batch, int a_batched, int b_batched, void *tail_ws,
-                            cudaStream_t s) {
+                            cudaStream_t s, uint32_t *out_max = nullptr) {
     J4C_REQUIRE(aligned16(ah) && aligned16(al) && aligned16(bh) && aligned16(bl),
                 "dot: split operands must be 16-byte aligned");
     // op(A) = A [M,K] is read K-major; A^T (A stored [K,M]) MN-major.
@@ -1174,7 +1215,7 @@ static int gemm_presplit_ws(const float *ah, const float *al, const float *bh, c
         const char *v = getenv("J4C_GEMM_VARIANT");
         return v ? atoi(v) : 1;
     }();
-    const tc::Epilogue ep{bias, mask, act};
+    const tc::Epilogue ep{bias, mask, act, out_max};
     const bool ab = a_batched != 0, bb = b_batched != 0;
     if (tc::split_fp16())
         return tc::launch_gemm_any<256, 4, 16, true>(ah, al, bh, bl, c, M, N, K, a_mn, b_mn, ep, batch, ab, bb, tail_ws, s);
@@ -1185,9 +1226,10 @@ static int gemm_presplit_ws(const float *ah, const float *al, const float *bh, c
 
 int tc_gemm_presplit(const float *ah, const float *al, const float *bh, const float *bl, float *c, int64_t M,
                      int64_t K, int64_t N, int trans_a, int trans_b, const float *bias, const float *mask,
-                     float *act, int64_t batch, int a_batched, int b_batched, cudaStream_t s) {
+                     float *act, int64_t batch, int a_batched, int b_batched, cudaStream_t s,
+                     uint32_t *out_max) {
     return gemm_presplit_ws(ah, al, bh, bl, c, M, K, N, trans_a, trans_b, bias, mask, act, batch, a_batched,
-                            b_batched, nullptr, s);
+                            b_batched, nullptr, s, out_max);
 }
 
 int tc_gemm_f32(const float *a, const float *b, float *c, int64_t M, int64_t K, int64_t N,

@@ -551,3 +551,41 @@ def test_split_f32_both_equals_the_two_passes(J, rows, cols):
     (hb, lb), (hbt, lbt) = _split_written_bytes(rows, cols), _split_written_bytes(cols, rows)
     for o, e, nb in zip(out, ref, (hb, lb, hbt, lbt)):
         assert torch.equal(o.view(torch.uint8)[:nb], e.view(torch.uint8)[:nb])
+
+
+@pytest.mark.parametrize("ta,tb,act,masked", [(0, 0, True, False), (1, 0, True, False), (0, 1, False, True),
+                                              (0, 0, False, True), (1, 1, True, False)])
+def test_epilogue_max_word_and_split_from_it(J, ta, tb, act, masked):
+    """Under 3xFP16 an epilogue GEMM leaves the max finite |value| of the output
+    a later split reads (the relu output, or the masked C) in a device word;
+    the split that takes the word is byte-identical to one that scans the
+    output itself, in both layouts and in one pass."""
+    import torch
+    from jax4j_b200.core import _dot_raw, split_kind
+    if split_kind() != 1:
+        pytest.skip("the max word belongs to the 3xFP16 split")
+    r = rng(ta * 8 + tb * 4 + act * 2 + masked)
+    M, K, N = 333, 257, 1030  # ragged edges, several tiles, the transposed store for (0, 1)
+    A = (r.standard_normal((M, K)) * 3).astype(np.float32)
+    B = r.standard_normal((K, N)).astype(np.float32)
+    a = dev(J, A.T.copy() if ta else A)
+    b = dev(J, B.T.copy() if tb else B)
+    bias = dev(J, r.standard_normal(N).astype(np.float32)) if act else None
+    mask = dev(J, r.standard_normal((M, N)).astype(np.float32)) if masked else None
+    res = _dot_raw(a, b, bool(ta), bool(tb), a.device(), bias=bias, mask=mask, act=act)
+    out = res[1] if act else res
+    assert out._absmax is not None
+    got = int(out._absmax.cpu().numpy()[0]) & 0xFFFFFFFF
+    want = int(np.abs(out.numpy()).max().view(np.uint32))
+    assert got == want, (hex(got), hex(want))
+    rows, cols = M, N
+    pc, pr = _lib.lib().j4c_split_pitch(cols), _lib.lib().j4c_split_pitch(rows)
+    d = out.tensor().device
+    given = [torch.full((n,), 7.0, dtype=torch.float32, device=d) for n in (rows * pc, rows * pc, cols * pr, cols * pr)]
+    scan = [torch.full((n,), 9.0, dtype=torch.float32, device=d) for n in (rows * pc, rows * pc, cols * pr, cols * pr)]
+    _lib.call("j4c_split_f32_ex", out.data_ptr(), rows, cols, *[t.data_ptr() for t in given],
+              out._absmax.data_ptr(), out._stream())
+    _lib.call("j4c_split_f32_ex", out.data_ptr(), rows, cols, *[t.data_ptr() for t in scan], None, out._stream())
+    (hb, lb), (hbt, lbt) = _split_written_bytes(rows, cols), _split_written_bytes(cols, rows)
+    for o, e, nb in zip(given, scan, (hb, lb, hbt, lbt)):
+        assert torch.equal(o.view(torch.uint8)[:nb], e.view(torch.uint8)[:nb])
