@@ -748,10 +748,16 @@ def _dtype_of_numpy(arr: np.ndarray) -> DType:
 DOT_TIMING = None
 
 
+_SPLIT_KIND = None
+
+
 def split_kind() -> int:
     """The library's FLOAT32 dot split: 1 = 3xFP16 (power-of-two scaled FP16
-    hi/lo), 0 = 3xTF32 (J4C_GEMM_SPLIT=tf32)."""
-    return int(_lib.lib().j4c_dot_split_kind())
+    hi/lo), 0 = 3xTF32 (J4C_GEMM_SPLIT=tf32); fixed for the process."""
+    global _SPLIT_KIND
+    if _SPLIT_KIND is None:
+        _SPLIT_KIND = int(_lib.lib().j4c_dot_split_kind())
+    return _SPLIT_KIND
 
 
 def split_bytes_per_element() -> int:
