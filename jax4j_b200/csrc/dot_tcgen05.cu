@@ -58,7 +58,7 @@ namespace j4c {
 namespace tc {
 
 constexpr int BM = 128;           // rows of a CTA tile (TMEM lanes)
-constexpr int CHUNK_K = 256;      // K accumulated in TMEM before promotion to registers
+constexpr int CHUNK_K = 256;      // K accumulated in TMEM before promotion (3xTF32; 512 for 3xFP16)
 constexpr int kEpiWarps = 8;      // two warps per TMEM lane quadrant
 constexpr int kThreads = 64 + 32 * kEpiWarps;
 constexpr int kStatusTimeout = 0x7C05;
@@ -80,7 +80,10 @@ template <int BN, int STAGES, int BK, bool F16 = false>
 struct Cfg {
     static_assert(BK == 32 || BK == 16, "BK is 32 (SW128) or 16 (SW64)");
     static constexpr int BKE = BK * 4 / Elt<F16>::SIZE;
-    static constexpr int CHUNK_KB = CHUNK_K / BKE;
+    // FP16 MMAs take half the time of TF32 ones per K, so the FP16 chunk is
+    // twice as deep: the same number of MMAs accumulate in TMEM either way,
+    // and the epilogue keeps a chunk's worth of MMA time to store a tile.
+    static constexpr int CHUNK_KB = (F16 ? 2 * CHUNK_K : CHUNK_K) / BKE;
     static constexpr int A_BYTES = BM * BK * 4;
     static constexpr int B_BYTES = BN * BK * 4;
     static constexpr int MN_BOX_BYTES = 128 * BKE;  // one MN-major column block (BKE rows x 128 B)
