@@ -199,7 +199,11 @@ J4C_API int j4c_reduce_axis(int prim, int dtype, const void *in, int64_t outer, 
  * J4C_REDUCE_NOALLOC_SCRATCH_BYTES that every GPU loading the library holds
  * until the process exits; a reduction needing more is rejected with
  * J4C_E_INVALID (use j4c_reduce_axis).  The first call on each device looks
- * the array's address up (cudaGetSymbolAddress) and should come before any
+ * the array's address up (cudaGetSymbolAddress).  Under CUDA's lazy module
+ * loading (the default on current drivers) that lookup may be what loads the
+ * library's device image onto the device, and the driver then reserves the
+ * image's memory, this array included: make the first call at start-up,
+ * before the host hands the device's memory to its arena and before any
  * stream capture on that device.  All calls share the one array: calls
  * whose work overlaps on the GPU (other streams, other threads) race on it;
  * nothing needs clearing between calls. */

@@ -447,7 +447,9 @@ int reduce_all_any(int dtype, const void *in, int64_t n, void *out, int mean, cu
 static __device__ __align__(256) unsigned char g_reduce_noalloc_scratch[J4C_REDUCE_NOALLOC_SCRATCH_BYTES];
 
 // Device address of the array on the current device, looked up once per
-// device (the first call on a device does this; no allocation happens).
+// device (the first call on a device does this; it allocates nothing itself,
+// but under lazy module loading the lookup may load the library's device
+// image, whose memory -- this array included -- the driver then reserves).
 static int noalloc_scratch(void **out) {
     static std::mutex mu;
     static std::vector<void *> ptrs;
