@@ -40,7 +40,7 @@
 extern "C" {
 #endif
 
-#define J4C_ABI_VERSION 1
+#define J4C_ABI_VERSION 2
 
 #if defined(__GNUC__)
 #define J4C_API __attribute__((visibility("default")))
@@ -269,8 +269,10 @@ J4C_API int j4c_scatter_add_rows(int dtype, const void *g, int64_t rows, int64_t
  *   op(A) = A stored [M,K] (trans_a = 0) or A stored [K,M] (trans_a = 1)
  *   op(B) = B stored [K,N] (trans_b = 0) or B stored [N,K] (trans_b = 1)
  * FLOAT32 runs on the 5th-generation tensor cores (tcgen05, TMA-fed) with a
- * 3xTF32 split (a = hi + lo; a.b ~ hi.hi + hi.lo + lo.hi) so the result has
- * FP32 accuracy; FLOAT64 runs a CUDA-core kernel.  Scratch for the split
+ * three-product split (a = hi + lo; a.b ~ hi.hi + hi.lo + lo.hi, in FP16 with
+ * per-line power-of-two scales or in TF32; see j4c_dot_split_kind) so the
+ * result has FP32 accuracy, and operands holding a NaN or an infinity get the
+ * reference's sequential FP32 sum exactly; FLOAT64 runs a CUDA-core kernel.  Scratch for the split
  * operands comes from the library's stream-ordered pool. */
 J4C_API int j4c_dot(int dtype, const void *a, const void *b, void *c, int64_t M, int64_t K, int64_t N,
             int trans_a, int trans_b, j4c_stream stream);
@@ -282,44 +284,75 @@ J4C_API size_t j4c_dot_workspace_size(int dtype, int64_t M, int64_t K, int64_t N
 
 /* The FLOAT32 dot in two steps, so a tensor that takes part in several
  * products (a layer's input, weight and output gradient each appear in two
- * of the forward/VJP dots) is split once.  j4c_split_f32 writes the hi and
- * lo parts of x stored [rows, cols] into two caller-allocated arrays of
- * rows * j4c_split_pitch(cols) floats each (16-byte aligned); j4c_dot_split
- * then computes C = op(A) . op(B) as j4c_dot does, from the split arrays of
- * A and B in their stored layouts (trans flags as for j4c_dot).  The split
- * of an unchanged tensor may be reused by any number of j4c_dot_split calls.
- * The split's format is the library's (j4c_dot_split_kind), fixed for the
- * process:
- *   1, 3xFP16 (default): with 2^e the power of two that brings max |x| over
- *      the finite elements into [2^14, 2^15) (e in [-100, 100]), hi =
- *      fp16(x 2^e) and lo = fp16(x 2^e - hi) as 2-byte halves in rows of
- *      cols rounded up to 8 (padding zero), and in the hi array the 32-bit
- *      bits of max |x| after the last row;
- *   0, 3xTF32 (environment J4C_GEMM_SPLIT=tf32): hi = tf32(x), lo =
- *      tf32(x - hi) as floats in rows of cols rounded up to 4 (padding zero),
- *      j4c_split_pitch(cols) floats per row. */
+ * of the forward/VJP dots) is split once per use.  A split of x stored
+ * [rows, cols] is two caller-allocated device arrays, hi and lo, of
+ * j4c_split_floats(rows, cols) floats each (16-byte aligned; for the
+ * transposed split j4c_split_floats(cols, rows)); j4c_dot_split then
+ * computes C = op(A) . op(B) as j4c_dot does, from the splits of A and B
+ * (trans flags as for j4c_dot).  Which split an operand takes follows from
+ * how the GEMM reads it:
+ *   op(A) = A, A stored [M, K]     (trans_a = 0): j4c_split_f32(A)
+ *   op(A) = A^T, A stored [K, M]   (trans_a = 1): j4c_split_f32_cols(A), or
+ *                                  j4c_split_f32_transposed(A) with trans_a = 0
+ *   op(B) = B, B stored [K, N]     (trans_b = 0): j4c_split_f32_cols(B), or
+ *                                  j4c_split_f32_transposed(B) with trans_b = 1
+ *   op(B) = B^T, B stored [N, K]   (trans_b = 1): j4c_split_f32(B)
+ * i.e. a split read K-major (K along its rows) has one line per row, one read
+ * MN-major one line per column.  A GEMM given a split of the wrong kind
+ * computes nothing and records device status 0x7C06 (j4c_device_status).
+ * The split of an unchanged tensor may be reused by any number of products;
+ * the tensor itself must stay allocated and unchanged while its splits are
+ * used (a product whose operand holds a NaN or an infinity reads it).
+ * The format is the library's (j4c_dot_split_kind), fixed for the process:
+ *   1, 3xFP16 (default): each line (a row or a column of the data) is scaled
+ *      by the power of two 2^e that brings its largest finite |x| into
+ *      [2^14, 2^15) (e in [-113, 127]), hi = fp16(x 2^e) and lo =
+ *      fp16(x 2^e - hi) as 2-byte halves in rows of j4c_split_pitch(cols)
+ *      elements (padding zero); the hi array then holds a 32-byte header and
+ *      the line maxima the epilogue scales by;
+ *   0, 3xTF32 (environment J4C_GEMM_SPLIT=tf32): the same line scales (they
+ *      keep FP32 subnormals, which TF32 products flush, exact), hi =
+ *      tf32(x 2^e), lo = tf32(x 2^e - hi) as floats in rows of
+ *      j4c_split_pitch(cols) elements, then the header and line maxima.
+ * Special values: a split records whether x holds a NaN or an infinity (it
+ * stores them as zero); a product either of whose operands does is computed
+ * on the CUDA cores as the reference's sequential FP32 sum of x's own values
+ * (core/ConcreteNDArray.java:452-459), bit for bit, NaN/Inf rules included. */
 J4C_API int j4c_dot_split_kind(void);
+/* Elements per row of a split's data with `cols` columns (halves under
+ * 3xFP16, floats under 3xTF32); -1 for a negative extent. */
 J4C_API int64_t j4c_split_pitch(int64_t cols);
+/* Floats to allocate for each of hi and lo of a split whose data is
+ * [rows, cols]; -1 for a negative extent. */
+J4C_API int64_t j4c_split_floats(int64_t rows, int64_t cols);
+/* The stored-layout split with one line per row (read K-major). */
 J4C_API int j4c_split_f32(const float *x, int64_t rows, int64_t cols, float *hi, float *lo, j4c_stream stream);
-/* The split of x^T: hi/lo arrays of cols * j4c_split_pitch(rows) floats.  A product
- * whose A and B are both stored with K as the leading (slow) dimension, such
- * as the weight gradient x^T . dy, runs fastest with one of them given in
- * this form (and its trans flag flipped). */
+/* The stored-layout split with one line per column (read MN-major). */
+J4C_API int j4c_split_f32_cols(const float *x, int64_t rows, int64_t cols, float *hi, float *lo,
+                               j4c_stream stream);
+/* The split of x^T (data [cols, rows], its rows -- x's columns -- as lines;
+ * read K-major).  A product whose A and B are both stored with K as the
+ * leading (slow) dimension, such as the weight gradient x^T . dy, runs
+ * fastest with one of them given in this form (and its trans flag flipped). */
 J4C_API int j4c_split_f32_transposed(const float *x, int64_t rows, int64_t cols, float *hi, float *lo,
                                      j4c_stream stream);
-/* Both splits of x in one pass over it: hi/lo exactly as j4c_split_f32 and
- * hi_t/lo_t exactly as j4c_split_f32_transposed (an output gradient that is
- * the left operand of g . W^T and the right one of x^T . g). */
+/* Both j4c_split_f32 (hi/lo) and j4c_split_f32_transposed (hi_t/lo_t) in
+ * one pass over x (an output gradient that is the left operand of g . W^T
+ * and the right one of x^T . g). */
 J4C_API int j4c_split_f32_both(const float *x, int64_t rows, int64_t cols, float *hi, float *lo, float *hi_t,
                                float *lo_t, j4c_stream stream);
-/* Any of the three splits above -- hi/lo only (j4c_split_f32), hi_t/lo_t
- * only (j4c_split_f32_transposed), or all four (j4c_split_f32_both) -- with
- * x's max word computed already: max_word (device, may be NULL) holds the
- * bits of x's largest finite |value| as j4c_dot_split_ep_max's out_max
- * leaves them, and replaces the split's own max pass under 3xFP16 (ignored
- * under 3xTF32). */
-J4C_API int j4c_split_f32_ex(const float *x, int64_t rows, int64_t cols, float *hi, float *lo, float *hi_t,
-                             float *lo_t, const uint32_t *max_word, j4c_stream stream);
+/* Any of the splits above in one pass -- hi/lo (row lines), hi_c/lo_c
+ * (column lines) or hi_t/lo_t (transposed), each pair optional, hi_c and
+ * hi_t not both -- with x's line maxima computed already: lines (device, may
+ * be NULL) holds rows + cols words, the bits of the largest finite |x| of
+ * each row and then of each column, as j4c_split_lines or
+ * j4c_dot_split_ep_max's out_lines leave them; it replaces the split's own
+ * max pass. */
+J4C_API int j4c_split_f32_ex(const float *x, int64_t rows, int64_t cols, float *hi, float *lo, float *hi_c,
+                             float *lo_c, float *hi_t, float *lo_t, const uint32_t *lines, j4c_stream stream);
+/* lines [rows + cols] (device): the line maxima of x (rows, then columns)
+ * in one pass, for several later j4c_split_f32_ex calls. */
+J4C_API int j4c_split_lines(const float *x, int64_t rows, int64_t cols, uint32_t *lines, j4c_stream stream);
 J4C_API int j4c_dot_split(const float *a_hi, const float *a_lo, const float *b_hi, const float *b_lo, float *c,
                           int64_t M, int64_t K, int64_t N, int trans_a, int trans_b, j4c_stream stream);
 /* j4c_dot_split with elementwise work fused into the store of C [M, N] (each
@@ -335,22 +368,24 @@ J4C_API int j4c_dot_split(const float *a_hi, const float *a_lo, const float *b_h
 /* Strided-batched j4c_dot_split (vmap's batched dot, api/Vmap.java:269-297):
  * for b < batch, C[b] = op(A[b]) . op(B[b]) with C [batch, M, N].  An operand
  * flagged batched holds `batch` split matrices back to back (the split of its
- * [batch * rows, cols] storage); an unbatched one is shared by every b.  One
- * persistent launch covers every (b, tile).  trans_a && !trans_b is rejected
- * (pass one operand's transposed split instead, as for j4c_dot_split). */
+ * [batch * rows, cols] storage, of the kind its use needs as above); an
+ * unbatched one is shared by every b.  One persistent launch covers every
+ * (b, tile).  trans_a && !trans_b is rejected (pass one operand's transposed
+ * split instead, as for j4c_dot_split). */
 J4C_API int j4c_dot_split_batched(const float *a_hi, const float *a_lo, const float *b_hi, const float *b_lo,
                                   float *c, int64_t batch, int64_t M, int64_t K, int64_t N, int trans_a,
                                   int trans_b, int a_batched, int b_batched, j4c_stream stream);
 J4C_API int j4c_dot_split_ep(const float *a_hi, const float *a_lo, const float *b_hi, const float *b_lo,
                              float *c, int64_t M, int64_t K, int64_t N, int trans_a, int trans_b,
                              const float *bias, const float *mask, float *act, j4c_stream stream);
-/* j4c_dot_split_ep that also leaves in *out_max (one device uint32) the bits
- * of the largest finite |value| it writes to act (or to c when act is NULL):
- * the max word a later j4c_split_f32_ex of that output takes instead of
- * scanning it again. */
+/* j4c_dot_split_ep that also leaves in out_lines (M + N device uint32
+ * words) the line maxima of what it writes to act (or to c when act is
+ * NULL): the bits of the largest finite |value| of each of the M rows, then
+ * of each of the N columns -- what a later j4c_split_f32_ex of that output
+ * takes instead of scanning it again. */
 J4C_API int j4c_dot_split_ep_max(const float *a_hi, const float *a_lo, const float *b_hi, const float *b_lo,
                                  float *c, int64_t M, int64_t K, int64_t N, int trans_a, int trans_b,
-                                 const float *bias, const float *mask, float *act, uint32_t *out_max,
+                                 const float *bias, const float *mask, float *act, uint32_t *out_lines,
                                  j4c_stream stream);
 
 /* ------------------------------------------------------------------ */

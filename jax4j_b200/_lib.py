@@ -83,7 +83,10 @@ SIGNATURES = {
     "j4c_dot_split": [P, P, P, P, P, I64, I64, I64, I32, I32, P],
     "j4c_dot_split_ep": [P, P, P, P, P, I64, I64, I64, I32, I32, P, P, P, P],
     "j4c_split_f32_both": [P, I64, I64, P, P, P, P, P],
-    "j4c_split_f32_ex": [P, I64, I64, P, P, P, P, P, P],
+    "j4c_split_f32_ex": [P, I64, I64, P, P, P, P, P, P, P, P],
+    "j4c_split_f32_cols": [P, I64, I64, P, P, P],
+    "j4c_split_lines": [P, I64, I64, P, P],
+    "j4c_split_floats": [I64, I64],
     "j4c_dot_split_ep_max": [P, P, P, P, P, I64, I64, I64, I32, I32, P, P, P, P, P],
     "j4c_fft": [I32, I32, PI64, P, P, P, P, I32, P],
     "j4c_rfft": [I32, I32, PI64, P, P, P, P],
@@ -114,7 +117,7 @@ SIGNATURES = {
     "j4c_psum_slots": [I32, C.POINTER(P), I32, P, I64, P],
 }
 _RESTYPES = {"j4c_last_error": C.c_char_p, "j4c_dot_workspace_size": C.c_size_t,
-             "j4c_split_pitch": C.c_int64}
+             "j4c_split_pitch": C.c_int64, "j4c_split_floats": C.c_int64}
 
 
 def lib() -> C.CDLL:

@@ -381,11 +381,11 @@ class ConcreteNDArray(NDArray):
 
     Storage is a flat, contiguous HBM buffer of shape.size() elements of the
     dtype (BOOL as one byte 0/1).  Instances are immutable, which is what
-    lets a FLOAT32 array keep the hi/lo split of its values (`_split`) once
-    it has been a dot operand, for the other dots it takes part in.
+    lets a FLOAT32 array keep the hi/lo splits of its values (`_split`, by
+    kind) once it has been a dot operand, for the other dots it takes part in.
     """
 
-    __slots__ = ("_t", "_shape", "_dtype", "_device", "_split", "_split_t", "_ready", "_absmax")
+    __slots__ = ("_t", "_shape", "_dtype", "_device", "_split", "_ready", "_lines")
 
     def __init__(self, data, shape=None, dtype: DType = None, device: Device = None):
         if device is None:
@@ -419,10 +419,9 @@ class ConcreteNDArray(NDArray):
         self._shape = shape
         self._dtype = dtype
         self._device = device
-        self._split = None
-        self._split_t = None
+        self._split = None  # {kind: (hi, lo)}: "r" row lines, "c" column lines, "t" transposed
         self._ready = None  # CUDA event recorded once the value was produced, when tracked
-        self._absmax = None  # device word: bits of max finite |x|, left by the GEMM that wrote x
+        self._lines = None  # device words [rows + cols]: line maxima (bits of max finite |x|)
 
     # ---- construction helpers ----
     @staticmethod
@@ -452,9 +451,8 @@ class ConcreteNDArray(NDArray):
         obj._dtype = dtype
         obj._device = device
         obj._split = None
-        obj._split_t = None
         obj._ready = None
-        obj._absmax = None
+        obj._lines = None
         return obj
 
     def _new(self, shape: Shape, dtype: DType) -> torch.Tensor:
@@ -765,45 +763,59 @@ def split_bytes_per_element() -> int:
     return 4 if split_kind() == 1 else 8
 
 
-def _tf32_split(x: "ConcreteNDArray", transposed: bool = False):
-    """hi/lo split of a 2-D FLOAT32 array -- in its stored layout, or of its
-    transpose -- made on first use and kept on the (immutable) array."""
-    s = x._split_t if transposed else x._split
-    if s is None:
+# Split kinds of a 2-D FLOAT32 array x [rows, cols] (j4c_split_f32_ex):
+#   "r": x's layout, one line per row -- read K-major (x is A [M, K] or B^T [N, K])
+#   "c": x's layout, one line per column -- read MN-major (x is A^T [K, M] or B [K, N])
+#   "t": x^T, its rows (x's columns) as lines -- read K-major with the trans flag flipped
+def _kind(kind: str) -> str:
+    return kind
+
+
+def _split_lines(x: "ConcreteNDArray"):
+    """x's line maxima (rows then columns), from the GEMM that wrote x or one
+    max pass, kept on the array for every split of it."""
+    if x._lines is None:
         rows, cols = x._shape.dimensions()
-        n = (cols if transposed else rows) * _lib.lib().j4c_split_pitch(rows if transposed else cols)
-        hi = torch.empty(max(n, 4), dtype=torch.float32, device=x._t.device)
-        lo = torch.empty(max(n, 4), dtype=torch.float32, device=x._t.device)
-        mx = x._absmax.data_ptr() if x._absmax is not None else None
-        if transposed:
-            call("j4c_split_f32_ex", x._t.data_ptr(), rows, cols, None, None, hi.data_ptr(), lo.data_ptr(), mx,
-                 x._stream())
-        else:
-            call("j4c_split_f32_ex", x._t.data_ptr(), rows, cols, hi.data_ptr(), lo.data_ptr(), None, None, mx,
-                 x._stream())
-        s = (hi, lo)
-        if transposed:
-            x._split_t = s
-        else:
-            x._split = s
-    return s
+        lines = torch.empty(rows + cols, dtype=torch.int32, device=x._t.device)
+        call("j4c_split_lines", x._t.data_ptr(), rows, cols, lines.data_ptr(), x._stream())
+        x._lines = lines
+    return x._lines
 
 
-def _tf32_split_both(x: "ConcreteNDArray") -> None:
-    """Both splits of a 2-D FLOAT32 array (stored layout and transpose) in one
-    pass over it, kept on the array; for an output gradient that is the left
-    operand of g . W^T and, transposed, the right operand of x^T . g."""
-    if x._dtype != DType.FLOAT32 or x._shape.rank() != 2 or x._split is not None or x._split_t is not None:
+def _make_splits(x: "ConcreteNDArray", kinds) -> None:
+    """The splits of x of the given kinds that it lacks, in one pass ("c" and
+    "t" are alternatives: not both in one pass)."""
+    kinds = [k for k in dict.fromkeys(_kind(k) for k in kinds) if not (x._split and k in x._split)]
+    if not kinds:
         return
+    if "c" in kinds and "t" in kinds:
+        _make_splits(x, ["t"])
+        kinds.remove("t")
     rows, cols = x._shape.dimensions()
-    if not rows or not cols:
-        return
-    n, n_t = rows * _lib.lib().j4c_split_pitch(cols), cols * _lib.lib().j4c_split_pitch(rows)
-    hi, lo = (torch.empty(max(n, 4), dtype=torch.float32, device=x._t.device) for _ in range(2))
-    hi_t, lo_t = (torch.empty(max(n_t, 4), dtype=torch.float32, device=x._t.device) for _ in range(2))
-    call("j4c_split_f32_ex", x._t.data_ptr(), rows, cols, hi.data_ptr(), lo.data_ptr(), hi_t.data_ptr(),
-         lo_t.data_ptr(), x._absmax.data_ptr() if x._absmax is not None else None, x._stream())
-    x._split, x._split_t = (hi, lo), (hi_t, lo_t)
+    L = _lib.lib()
+    out = {}
+    for k in kinds:
+        n = L.j4c_split_floats(cols, rows) if k == "t" else L.j4c_split_floats(rows, cols)
+        out[k] = (torch.empty(n, dtype=torch.float32, device=x._t.device),
+                  torch.empty(n, dtype=torch.float32, device=x._t.device))
+    ptrs = []
+    for k in ("r", "c", "t"):
+        ptrs += [out[k][0].data_ptr(), out[k][1].data_ptr()] if k in out else [None, None]
+    lines = _split_lines(x)
+    call("j4c_split_f32_ex", x._t.data_ptr(), rows, cols, *ptrs,
+         lines.data_ptr() if lines is not None else None, x._stream())
+    if x._split is None:
+        x._split = {}
+    x._split.update(out)
+
+
+def _split_of(x: "ConcreteNDArray", kind: str):
+    """The (hi, lo) split of a 2-D FLOAT32 array of the given kind, made on
+    first use and kept on the (immutable) array."""
+    kind = _kind(kind)
+    if x._split is None or kind not in x._split:
+        _make_splits(x, [kind])
+    return x._split[kind]
 
 
 def dot_supports_epilogue(a: "ConcreteNDArray") -> bool:
@@ -846,25 +858,28 @@ def _dot_raw(a: "ConcreteNDArray", b: "ConcreteNDArray", trans_a: bool, trans_b:
         # With K the leading dimension of both stored operands (A^T . B, the
         # weight gradient) one of them goes in transposed (K-major) form: the
         # smaller one, so the extra split pass is as short as possible.
+        # The split kind follows how the GEMM reads an operand: op(A) = A and
+        # op(B) = B^T K-major (row lines), op(A) = A^T and op(B) = B MN-major
+        # (column lines).
         ta, tb = trans_a, trans_b
         if ta and not tb:
             if a._shape.size() < b._shape.size():
-                (ah, al), ta = _tf32_split(a, True), False
-                bh, bl = _tf32_split(b)
+                (ah, al), ta = _split_of(a, "t"), False
+                bh, bl = _split_of(b, "c")
             else:
-                ah, al = _tf32_split(a)
-                (bh, bl), tb = _tf32_split(b, True), True
+                ah, al = _split_of(a, "c")
+                (bh, bl), tb = _split_of(b, "t"), True
         else:
-            ah, al = _tf32_split(a)
-            bh, bl = _tf32_split(b)
+            ah, al = _split_of(a, "c" if ta else "r")
+            bh, bl = _split_of(b, "r" if tb else "c")
         if timing is not None:
             ev0 = torch.cuda.Event(enable_timing=True)
             ev1 = torch.cuda.Event(enable_timing=True)
             ev0.record()
         if epilogue:
-            # under 3xFP16 the epilogue also takes the max |value| of the output a later
-            # split will read (the relu output, or C), sparing that split its max pass
-            out_max = torch.empty(1, dtype=torch.int32, device=a._t.device) if split_kind() == 1 else None
+            # the epilogue also takes the line maxima of the output a later split
+            # will read (the relu output, or C), sparing it a max pass
+            out_max = torch.empty(M + N, dtype=torch.int32, device=a._t.device)
             call("j4c_dot_split_ep_max", ah.data_ptr(), al.data_ptr(), bh.data_ptr(), bl.data_ptr(),
                  out.data_ptr() if store_c else None,
                  M, K, N, int(ta), int(tb), bias.data_ptr() if bias is not None else None,
@@ -896,10 +911,10 @@ def _dot_raw(a: "ConcreteNDArray", b: "ConcreteNDArray", trans_a: bool, trans_b:
     if act:
         h = ConcreteNDArray._wrap(act_out, Shape(M, N), a._dtype, device)
         if out_max is not None:
-            h._absmax = out_max
+            h._lines = out_max
         return c, h
     if out_max is not None:
-        c._absmax = out_max
+        c._lines = out_max
     return c
 
 

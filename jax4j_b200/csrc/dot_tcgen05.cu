@@ -30,19 +30,28 @@
 //  add it into FP32 registers with round-to-nearest while the MMA warp
 //  fills the other buffer.  The error then grows with sqrt(K) like an FP32
 //  sum.
-//  Split mode 3xFP16 (the default; J4C_GEMM_SPLIT=tf32 selects 3xTF32): the same three products from
-//  FP16 operands, at twice the tensor rate of TF32.  FP16 has TF32's 11-bit
-//  significand but a 5-bit exponent, so every operand is first scaled by a
-//  power of two 2^e chosen from its largest finite magnitude (max |x| 2^e in
-//  [2^14, 2^15)): hi = fp16(x 2^e), lo = fp16(x 2^e - hi), stored as 2-byte
-//  halves with the max in a word after the hi array, and the
-//  epilogue multiplies the accumulator by 2^-(e_a + e_b) (exact).  Elements
-//  below 2^-24 of the tensor's max lose digits (FP16 subnormals): an
-//  absolute error of at most ~2^-38 max |x| per element, on top of the
-//  2^-22 relative error of the split.
-//  Every mbarrier wait is bounded: after kWaitLimitNs without progress the
-//  kernel records J4C status kStatusTimeout, stops all roles, waits
-//  (bounded) for its own TMA and MMA work in flight, frees TMEM and returns.
+//  Split mode 3xFP16 (the default; J4C_GEMM_SPLIT=tf32 selects 3xTF32): the
+//  same three products from FP16 operands, at twice the tensor rate of TF32.
+//  FP16 has TF32's 11-bit significand but a 5-bit exponent, so every line of
+//  an operand -- a row of op(A) (one of the M rows) or a column of op(B) (one
+//  of the N columns) -- is scaled by its own power of two 2^e, chosen from
+//  the line's largest finite magnitude m so that m 2^e lies in [2^14, 2^15):
+//  hi = fp16(x 2^e), lo = fp16(x 2^e - hi).  The scale of a line is constant
+//  along K, so it factors out of the line's dot products, and the epilogue
+//  multiplies C[i][j] by 2^-(e_i + e_j) (exact, one rounding at most when the
+//  result is subnormal).  e spans [-113, 127]: every finite FP32 line is
+//  brought into FP16's normal range, whatever the line's magnitude or how far
+//  it lies below the rest of the tensor.  Within a line, elements more than
+//  2^24 below the line's max fall into FP16 subnormals: their split carries
+//  an absolute error of at most ~2^-39 of the line's max.
+//  Special values.  The hi/lo decomposition cannot carry an infinity (inf -
+//  inf = NaN in lo, 0 * inf = NaN against a partner whose lo is zero), so a
+//  split records whether its source holds a NaN or an infinity, and where the
+//  source is.  A GEMM either of whose operands does runs its exact path: every
+//  output is the reference's sequential FP32 sum (float products added from
+//  k = 0 in order, no fused multiply-add, core/ConcreteNDArray.java:452-459)
+//  of the FP32 sources, on the CUDA cores -- slow, but the reference's result
+//  bit for bit, special values included.
 #include <cuda.h>
 #include <cuda_fp16.h>
 #include <cudaTypedefs.h>
@@ -64,6 +73,32 @@ constexpr int kThreads = 64 + 32 * kEpiWarps;
 constexpr int kStatusTimeout = 0x7C05;
 constexpr uint64_t kWaitLimitNs = 2000000000ull;  // 2 s without progress
 constexpr int kMaxTailSplits = 4; // parts along K of a tile of the last wave
+constexpr int kStatusBadSplit = 0x7C06;  // an operand is not a split of the layout its use needs
+
+// ---- split format ----------------------------------------------------------------
+// A split of a FLOAT32 array X is two device arrays, hi and lo.  Each holds a
+// data matrix [rd, cd] -- X as stored, or X^T for a transposed split -- in
+// rows of split_pitch(cd) elements (2-byte halves under 3xFP16, 4-byte tf32
+// values under 3xTF32; padding columns zero).  The hi array continues after
+// its data (a multiple of 16 bytes) with a SplitHeader and the line words:
+// one per data row (a split read K-major, whose rows are M or N) or one per
+// data column (read MN-major), each the bits of the largest finite |x| of
+// its line, from which the line's scale follows (split_exp).  Both split
+// kinds scale: FP16 needs it for range, TF32 for FP32 subnormals, which its
+// products do not keep.
+constexpr uint32_t kLayoutT = 1;      // the data is X^T
+constexpr uint32_t kLayoutCols = 2;   // one line word per data column (MN-major use)
+constexpr uint32_t kSplitMagic = 0x53433449u;
+
+struct SplitHeader {
+    unsigned long long src;  // X as stored (FP32): what the exact path reads
+    unsigned int nonfinite;  // nonzero: X holds a NaN or an infinity
+    unsigned int layout;     // kLayoutT | kLayoutCols
+    unsigned int lines;      // line words after the header
+    unsigned int magic;      // kSplitMagic once a split has been written
+    unsigned long long reserved;
+};
+static_assert(sizeof(SplitHeader) == 32, "split header size");
 
 // Operand element of a split mode: 3xTF32 (4-byte tf32 values) or 3xFP16.
 template <bool F16>
@@ -240,17 +275,34 @@ __device__ __forceinline__ void mma_issue(uint32_t d_tmem, uint64_t a, uint64_t 
     }
 }
 
-// The scale exponent e of an fp16 split from the bits of its max |x|
-// (finite, non-negative): max 2^e in [2^14, 2^15); 0 for a zero max;
-// clamped to [-100, 100] so that 2^-e is a normal float.
+// The scale exponent e of a line of an fp16 split from the bits of its
+// largest finite |x|: max 2^e in [2^14, 2^15); 0 for a zero line.  A finite
+// max is below 2^128, so e >= -113; a max below 2^-112 takes e = 126, which
+// still keeps the line's values to 22 significant bits in hi + lo (and
+// represents an FP32 subnormal, at most 23 bits above 2^-149, exactly).
+// 2^e and 2^-e are then normal floats.
 __host__ __device__ __forceinline__ int split_exp(uint32_t maxbits) {
     if (maxbits == 0) return 0;
     const int e = 14 - ((int)((maxbits >> 23) & 0xFF) - 127);
-    return e < -100 ? -100 : (e > 100 ? 100 : e);
+    return e > 126 ? 126 : e;
 }
 
-// 2^k as a float, |k| <= 100.
-__device__ __forceinline__ float pow2f(int k) { return __uint_as_float((uint32_t)(127 + k) << 23); }
+// 2^k as a float, -149 <= k <= 127 (a subnormal below -126).
+__device__ __forceinline__ float pow2f(int k) {
+    return __uint_as_float(k >= -126 ? (uint32_t)(127 + k) << 23 : 1u << (k + 149));
+}
+
+// v 2^k for k in [-252, 226] (the sum of two negated line exponents, each
+// in [-126, 113]) as two multiplies by 2^(k >> 1) and 2^(k - (k >> 1)): both
+// exponents lie in [-126, 113], so both factors are normal floats (two
+// integer operations each), and as they share k's sign the intermediate lies
+// between v and the result -- it overflows only when the result does, and
+// both steps are exact whenever the result is a normal float (a result in the
+// subnormal range is rounded once or twice at its 2^-149 step).
+__device__ __forceinline__ float unscale(float v, int k) {
+    const int k1 = k >> 1;
+    return v * __uint_as_float((uint32_t)(127 + k1) << 23) * __uint_as_float((uint32_t)(127 + k - k1) << 23);
+}
 
 __device__ __forceinline__ void mma_commit(uint32_t bar) {
     asm volatile("tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];" ::"r"(bar)
@@ -304,23 +356,73 @@ __device__ __forceinline__ Unit unit_of(int u, int full_tiles, int splits, int n
 //   v = acc + bias[col]            (a bias add broadcast along rows)
 //   v = mask[row][col] > 0 ? v : 0 (relu' given the saved pre-activation)
 //   C[row][col] = v,  act[row][col] = max(0, v)  (Java Math.max rules)
-// and, with out_max set (zeroed by the launch), the bits of the largest
-// finite |value| written to act (or to C when there is no act): the max word
-// a later 3xFP16 split of that output takes instead of its own max pass.
+// and, with out_lines set (zeroed by the launch), the line words of the
+// stored output: out_lines[r] (r < out_rows) the bits of the largest finite
+// |value| of stored row r, out_lines[out_rows + c] of stored column c, taken
+// over what is written to act (or to C when there is no act) -- the line
+// maxima a later 3xFP16 split of that output takes instead of its own pass.
 struct Epilogue {
     const float *bias;
     const float *mask;
     float *act;
-    uint32_t *out_max;
+    uint32_t *out_lines;
+    int out_rows;
 };
 
-// m = the bits of max(m, |v|) over finite v.
-__device__ __forceinline__ void track_max(uint32_t &m, float v) {
+// The bits of |v| for finite v, else 0.
+__device__ __forceinline__ uint32_t finite_bits(float v) {
     const uint32_t b = __float_as_uint(v) & 0x7FFFFFFFu;
-    if (b < 0x7F800000u && b > m) m = b;
+    return b < 0x7F800000u ? b : 0u;
 }
 
 __device__ __forceinline__ float ep_relu(float v) { return (0.0f >= v) ? 0.0f : v; }
+
+// The exact path, for operands one of which holds a NaN or an infinity: each
+// output of this CTA's tiles is the reference's dot -- float products of the
+// FP32 sources added in k order from 0.0f, no fused multiply-add
+// (core/ConcreteNDArray.java:452-459) -- then the epilogue, one element per
+// thread step.  A source element (line l, k) of an operand whose data rows
+// are its lines (read K-major, not transposed) is src[(z * L + l) * K + k];
+// otherwise (MN-major, or a transposed split) src[(z * K + k) * L + l], with
+// z the batch entry of a batched operand and L = M for A, N for B.
+template <int BN>
+__device__ void exact_tiles(const float *__restrict__ A, bool a_col, const float *__restrict__ B, bool b_col,
+                            float *__restrict__ C, int M, int N, int K, int store_t, const Epilogue &ep,
+                            int batch, int a_batched, int b_batched) {
+    const int num_m = (M + BM - 1) / BM, num_n = (N + BN - 1) / BN;
+    const int tiles_per_batch = num_m * num_n, num_tiles = tiles_per_batch * batch;
+    for (int t = blockIdx.x; t < num_tiles; t += gridDim.x) {
+        const int bidx = t / tiles_per_batch;
+        int mt, nt;
+        tile_coords(t - bidx * tiles_per_batch, num_m, num_n, mt, nt);
+        const float *Ab = A + (a_batched ? (size_t)bidx * M * K : 0);
+        const float *Bb = B + (b_batched ? (size_t)bidx * N * K : 0);
+        const size_t boff = (size_t)bidx * (size_t)M * (size_t)N;
+        for (int e = threadIdx.x; e < BM * BN; e += blockDim.x) {
+            const int i = mt * BM + e / BN, j = nt * BN + e % BN;
+            if (i >= M || j >= N) continue;
+            float s = 0.0f;
+            for (int k = 0; k < K; k++) {
+                const float a = a_col ? Ab[(size_t)k * M + i] : Ab[(size_t)i * K + k];
+                const float b = b_col ? Bb[(size_t)k * N + j] : Bb[(size_t)j * K + k];
+                s = __fadd_rn(s, __fmul_rn(a, b));
+            }
+            const size_t idx = boff + (store_t ? (size_t)j * M + i : (size_t)i * N + j);
+            float v = ep.bias ? __fadd_rn(s, __ldg(ep.bias + (store_t ? i : j))) : s;
+            if (ep.mask) v = __ldg(ep.mask + idx) > 0.0f ? v : 0.0f;
+            if (C) C[idx] = v;
+            if (ep.act) ep.act[idx] = ep_relu(v);
+            if (ep.out_lines) {
+                const uint32_t m = finite_bits(ep.act ? ep_relu(v) : v);
+                const int sr = store_t ? j : i, sc = store_t ? i : j;
+                if (m) {
+                    atomicMax(ep.out_lines + sr, m);
+                    atomicMax(ep.out_lines + ep.out_rows + sc, m);
+                }
+            }
+        }
+    }
+}
 
 // Loads one operand's hi or lo tile (ROWS of M or N, BKE of K) into smem.
 template <int ROWS, int BK, bool MN, bool F16>
@@ -336,18 +438,38 @@ __device__ __forceinline__ void load_operand(uint32_t dst, const CUtensorMap *ma
     }
 }
 
-// F16: the 3xFP16 split; amax / bmax are then the operands' max words.
+// F16: the 3xFP16 split (else 3xTF32).  ahdr / bhdr: the headers of the
+// operands' hi arrays, whose line words give the scales.
 template <int BN, int STAGES, int BK, bool A_MN, bool B_MN, bool F16>
 __global__ void __launch_bounds__(kThreads, 1)
 gemm_3xtf32_kernel(const __grid_constant__ CUtensorMap tAh, const __grid_constant__ CUtensorMap tAl,
                    const __grid_constant__ CUtensorMap tBh, const __grid_constant__ CUtensorMap tBl,
-                   float *__restrict__ C, int M, int N, int num_kb, int vec_store, int store_t,
+                   float *__restrict__ C, int M, int N, int K, int num_kb, int vec_store, int store_t,
                    Epilogue ep, int batch, int a_batched, int b_batched, int *status, int full_tiles,
                    int splits, float *__restrict__ part, int *__restrict__ arrivals,
-                   const uint32_t *__restrict__ amax, const uint32_t *__restrict__ bmax) {
+                   const SplitHeader *__restrict__ ahdr, const SplitHeader *__restrict__ bhdr) {
     using Q = Cfg<BN, STAGES, BK, F16>;
     constexpr int UMMA_K = Elt<F16>::UMMA_K;
     constexpr int CHUNK_KB = Q::CHUNK_KB;
+    {
+        // What the operands' splits say, the same for every thread: a split
+        // must match its use (under 3xFP16 its lines are the rows of a
+        // K-major operand, the columns of an MN-major one), and a source
+        // with a NaN or an infinity sends the whole product down the exact path.
+        const uint32_t a_layout = ahdr->layout, b_layout = bhdr->layout;
+        const bool bad = ahdr->magic != kSplitMagic || bhdr->magic != kSplitMagic ||
+                         ((a_layout & kLayoutCols) != 0) != A_MN || ((b_layout & kLayoutCols) != 0) != B_MN;
+        if (bad) {
+            if (threadIdx.x == 0 && status) atomicCAS(status, 0, kStatusBadSplit);
+            return;
+        }
+        if (ahdr->nonfinite | bhdr->nonfinite) {
+            exact_tiles<BN>(reinterpret_cast<const float *>(ahdr->src), A_MN || (a_layout & kLayoutT),
+                            reinterpret_cast<const float *>(bhdr->src), B_MN || (b_layout & kLayoutT), C, M, N, K,
+                            store_t, ep, batch, a_batched, b_batched);
+            return;
+        }
+    }
     extern __shared__ uint8_t smem_raw[];
     uint8_t *smem = reinterpret_cast<uint8_t *>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
     Ctl<STAGES> *ctl = reinterpret_cast<Ctl<STAGES> *>(smem + STAGES * Q::STAGE_BYTES);
@@ -557,76 +679,120 @@ gemm_3xtf32_kernel(const __grid_constant__ CUtensorMap tAh, const __grid_constan
                     acc[j] = v;
                 }
             }
-            if constexpr (F16) {
-                // the accumulator is in units of 2^(e_a + e_b): two exact power-of-two scalings
-                const int E = split_exp(__ldg(amax)) + split_exp(__ldg(bmax));
-                const float f1 = pow2f(-(E >> 1)), f2 = pow2f(-(E - (E >> 1)));
-#pragma unroll
-                for (int j = 0; j < Q::COLS_PER_WARP; j++) acc[j] = acc[j] * f1 * f2;
-            }
             const int row = mt * BM + q * 32 + lane;
             const int col0 = nt * BN + cbase;
-            uint32_t mloc = 0;  // max of the values this lane stores (ep.out_max)
-            if (store_t) {
-                // C holds the transpose of this product ([N, M]): for each
-                // column the warp's 32 lanes write 32 consecutive floats.
-                // Stored C's column index is `row`, so the bias is one value.
-                if (row < M) {
-                    const float b = ep.bias ? __ldg(ep.bias + row) : 0.0f;
+            const bool row_ok = row < M;
+            // The accumulator of C[row][col] is in units of
+            // 2^(e_a(row) + e_b(col)), the scales of op(A)'s row line and op(B)'s
+            // column line.  A K-major batched operand has lines per batch entry; an
+            // MN-major one shares its column lines (taken over all entries).
+            const uint32_t *al = reinterpret_cast<const uint32_t *>(ahdr + 1) +
+                                 ((!A_MN && a_batched) ? (size_t)bidx * M : 0);
+            const uint32_t *bl = reinterpret_cast<const uint32_t *>(bhdr + 1) +
+                                 ((!B_MN && b_batched) ? (size_t)bidx * N : 0);
+            const int ea = row_ok ? split_exp(__ldg(al + row)) : 0;
+            const bool vec_full = row_ok && !store_t && vec_store && col0 + Q::COLS_PER_WARP <= N;
+            const float bias_t = (store_t && ep.bias && row_ok) ? __ldg(ep.bias + row) : 0.0f;
+            {
+                // lane l reads the line word of column g*32 + l; the warp shares it
+                const int nea = -ea;
 #pragma unroll
-                    for (int j = 0; j < Q::COLS_PER_WARP; j++) {
-                        if (col0 + j < N) {
-                            const size_t idx = (size_t)(col0 + j) * (size_t)M + row;
-                            float v = ep.bias ? __fadd_rn(acc[j], b) : acc[j];
-                            if (mask_b) v = __ldg(mask_b + idx) > 0.0f ? v : 0.0f;
-                            if (Cb) Cb[idx] = v;
-                            if (act_b) act_b[idx] = ep_relu(v);
-                            if (ep.out_max) track_max(mloc, act_b ? ep_relu(v) : v);
-                        }
-                    }
+                for (int g = 0; g < Q::COLS_PER_WARP / 32; g++) {
+                    const int mycol = col0 + g * 32 + lane;
+                    const int eb_l = mycol < N ? split_exp(__ldg(bl + mycol)) : 0;
+#pragma unroll
+                    for (int jj = 0; jj < 32; jj++)
+                        acc[g * 32 + jj] = unscale(acc[g * 32 + jj], nea - __shfl_sync(0xffffffffu, eb_l, jj));
                 }
-            } else if (row < M && col0 < N) {
+            }
+            // Store; afterwards acc[j] holds the bits of the stored |v| (the relu
+            // output when act is written; finite values only, 0 outside C), from
+            // which the line maxima are taken.
+            if (vec_full) {
                 const size_t base = (size_t)row * (size_t)N + col0;
-                if (vec_store && col0 + Q::COLS_PER_WARP <= N) {
 #pragma unroll
-                    for (int v4 = 0; v4 < Q::COLS_PER_WARP / 4; v4++) {
-                        float x[4] = {acc[4 * v4], acc[4 * v4 + 1], acc[4 * v4 + 2], acc[4 * v4 + 3]};
-                        if (ep.bias) {
-                            const float4 b = __ldg(reinterpret_cast<const float4 *>(ep.bias + col0) + v4);
-                            x[0] = __fadd_rn(x[0], b.x); x[1] = __fadd_rn(x[1], b.y);
-                            x[2] = __fadd_rn(x[2], b.z); x[3] = __fadd_rn(x[3], b.w);
-                        }
-                        if (mask_b) {
-                            const float4 m = __ldg(reinterpret_cast<const float4 *>(mask_b + base) + v4);
-                            x[0] = m.x > 0.0f ? x[0] : 0.0f; x[1] = m.y > 0.0f ? x[1] : 0.0f;
-                            x[2] = m.z > 0.0f ? x[2] : 0.0f; x[3] = m.w > 0.0f ? x[3] : 0.0f;
-                        }
-                        if (Cb) reinterpret_cast<float4 *>(Cb + base)[v4] = make_float4(x[0], x[1], x[2], x[3]);
-                        if (act_b)
-                            reinterpret_cast<float4 *>(act_b + base)[v4] =
-                                make_float4(ep_relu(x[0]), ep_relu(x[1]), ep_relu(x[2]), ep_relu(x[3]));
-                        if (ep.out_max) {
+                for (int v4 = 0; v4 < Q::COLS_PER_WARP / 4; v4++) {
+                    float x[4] = {acc[4 * v4], acc[4 * v4 + 1], acc[4 * v4 + 2], acc[4 * v4 + 3]};
+                    if (ep.bias) {
+                        const float4 b = __ldg(reinterpret_cast<const float4 *>(ep.bias + col0) + v4);
+                        x[0] = __fadd_rn(x[0], b.x); x[1] = __fadd_rn(x[1], b.y);
+                        x[2] = __fadd_rn(x[2], b.z); x[3] = __fadd_rn(x[3], b.w);
+                    }
+                    if (mask_b) {
+                        const float4 m = __ldg(reinterpret_cast<const float4 *>(mask_b + base) + v4);
+                        x[0] = m.x > 0.0f ? x[0] : 0.0f; x[1] = m.y > 0.0f ? x[1] : 0.0f;
+                        x[2] = m.z > 0.0f ? x[2] : 0.0f; x[3] = m.w > 0.0f ? x[3] : 0.0f;
+                    }
+                    if (Cb) reinterpret_cast<float4 *>(Cb + base)[v4] = make_float4(x[0], x[1], x[2], x[3]);
+                    if (act_b) {
 #pragma unroll
-                            for (int i = 0; i < 4; i++) track_max(mloc, act_b ? ep_relu(x[i]) : x[i]);
+                        for (int e = 0; e < 4; e++) x[e] = ep_relu(x[e]);
+                        reinterpret_cast<float4 *>(act_b + base)[v4] = make_float4(x[0], x[1], x[2], x[3]);
+                    }
+#pragma unroll
+                    for (int e = 0; e < 4; e++) acc[4 * v4 + e] = __uint_as_float(finite_bits(x[e]));
+                }
+            } else if (store_t) {
+                // C holds the transpose of this product ([N, M]): for each
+                // column the warp's 32 lanes write 32 consecutive floats, and
+                // stored C's column index is `row`, so the bias is one value.
+#pragma unroll
+                for (int j = 0; j < Q::COLS_PER_WARP; j++) {
+                    float v = 0.0f;
+                    if (row_ok && col0 + j < N) {
+                        const size_t idx = (size_t)(col0 + j) * (size_t)M + row;
+                        v = ep.bias ? __fadd_rn(acc[j], bias_t) : acc[j];
+                        if (mask_b) v = __ldg(mask_b + idx) > 0.0f ? v : 0.0f;
+                        if (Cb) Cb[idx] = v;
+                        if (act_b) {
+                            v = ep_relu(v);
+                            act_b[idx] = v;
                         }
                     }
-                } else {
+                    acc[j] = __uint_as_float(finite_bits(v));
+                }
+            } else {
+                const size_t base = (size_t)row * (size_t)N + col0;
 #pragma unroll
-                    for (int j = 0; j < Q::COLS_PER_WARP; j++) {
-                        if (col0 + j < N) {
-                            float v = ep.bias ? __fadd_rn(acc[j], __ldg(ep.bias + col0 + j)) : acc[j];
-                            if (mask_b) v = __ldg(mask_b + base + j) > 0.0f ? v : 0.0f;
-                            if (Cb) Cb[base + j] = v;
-                            if (act_b) act_b[base + j] = ep_relu(v);
-                            if (ep.out_max) track_max(mloc, act_b ? ep_relu(v) : v);
+                for (int j = 0; j < Q::COLS_PER_WARP; j++) {
+                    float v = 0.0f;
+                    if (row_ok && col0 + j < N) {
+                        v = ep.bias ? __fadd_rn(acc[j], __ldg(ep.bias + col0 + j)) : acc[j];
+                        if (mask_b) v = __ldg(mask_b + base + j) > 0.0f ? v : 0.0f;
+                        if (Cb) Cb[base + j] = v;
+                        if (act_b) {
+                            v = ep_relu(v);
+                            act_b[base + j] = v;
                         }
                     }
+                    acc[j] = __uint_as_float(finite_bits(v));
                 }
             }
-            if (ep.out_max) {  // uniform: every lane of the warp gets here
-                for (int o = 16; o > 0; o >>= 1) mloc = max(mloc, __shfl_xor_sync(0xffffffffu, mloc, o));
-                if (lane == 0 && mloc) atomicMax(ep.out_max, mloc);
+            uint32_t rmax = 0;  // over this lane's values: a stored row (a stored column when store_t)
+            if (ep.out_lines) {  // uniform: every lane of the warp gets here
+#pragma unroll
+                for (int j = 0; j < Q::COLS_PER_WARP; j++) rmax = max(rmax, __float_as_uint(acc[j]));
+#pragma unroll
+                for (int g = 0; g < Q::COLS_PER_WARP / 32; g++) {
+                    // Column maxima over the warp's 32 rows: a butterfly that halves
+                    // the group each step, after which lane l holds column g*32 + l.
+#pragma unroll
+                    for (int off = 16; off >= 1; off >>= 1) {
+                        const bool up = (lane & off) != 0;
+#pragma unroll
+                        for (int i = 0; i < off; i++) {
+                            const uint32_t lo_v = __float_as_uint(acc[g * 32 + i]);
+                            const uint32_t hi_v = __float_as_uint(acc[g * 32 + i + off]);
+                            const uint32_t got = __shfl_xor_sync(0xffffffffu, up ? lo_v : hi_v, off);
+                            acc[g * 32 + i] = __uint_as_float(max(up ? hi_v : lo_v, got));
+                        }
+                    }
+                    const int col = col0 + g * 32 + lane;
+                    const uint32_t m = __float_as_uint(acc[g * 32]);
+                    if (col < N && m) atomicMax(ep.out_lines + (store_t ? col : ep.out_rows + col), m);
+                }
             }
+            if (ep.out_lines && row_ok && rmax) atomicMax(ep.out_lines + (store_t ? ep.out_rows + row : row), rmax);
         }
     }
 
@@ -640,22 +806,135 @@ gemm_3xtf32_kernel(const __grid_constant__ CUtensorMap tAh, const __grid_constan
     }
 }
 
-// ---- operand split: X [rows, cols] -> hi/lo [rows, pitch], pitch = cols rounded up to 4 ----
+// ---- operand splits ---------------------------------------------------------------------
 __device__ __forceinline__ float tf32_round(float x) {
     uint32_t r;
     asm("cvt.rna.tf32.f32 %0, %1;" : "=r"(r) : "f"(x));
     return __uint_as_float(r & 0xFFFFE000u);
 }
 
-// 4 consecutive columns per thread step: 16-byte loads when the source
-// allows, 16-byte stores of hi and lo; padding columns are written as zero.
+__device__ __forceinline__ bool is_finite_f(float x) { return (__float_as_uint(x) & 0x7F800000u) != 0x7F800000u; }
+
+// A non-finite source element is split as zero (the exact path computes
+// every output of a product whose operand holds one); `bad` records it.
+__device__ __forceinline__ float finite_or_zero(float x, bool &bad) {
+    if (is_finite_f(x)) return x;
+    bad = true;
+    return 0.0f;
+}
+
+// Block 0 thread 0 writes a split's header (its nonfinite word is zeroed
+// beforehand and only ever OR-ed).
+__device__ __forceinline__ void write_header(SplitHeader *h, const float *src, uint32_t layout, uint32_t lines) {
+    h->src = reinterpret_cast<unsigned long long>(src);
+    h->layout = layout;
+    h->lines = lines;
+    h->magic = kSplitMagic;
+}
+
+// Every warp ORs `bad` into the headers' nonfinite words.
+__device__ __forceinline__ void flag_nonfinite(bool bad, SplitHeader *h0, SplitHeader *h1) {
+    if (__any_sync(0xffffffffu, bad) && (threadIdx.x & 31) == 0) {
+        if (h0) atomicOr(&h0->nonfinite, 1u);
+        if (h1) atomicOr(&h1->nonfinite, 1u);
+    }
+}
+
+// Line maxima of X [R, C]: rowmax[r] / colmax[c] = the bits of the largest
+// finite |x| of row r / column c (each array optional, zeroed beforehand;
+// non-negative floats order like their bits as unsigned integers).  Tiles of
+// 64 rows x 512 columns: warp w takes rows w, w + 8, ...; lane l the four
+// columns 4l.. of each 128-column quarter (16-byte loads when X allows).  A
+// row's max is reduced over the warp and added with one atomic per tile, a
+// column's over the 8 warps in shared memory, one atomic per tile.
+template <bool ROWS, bool COLS>
+__global__ void __launch_bounds__(256) lines_max_kernel(const float *__restrict__ src, int64_t R, int64_t C, int vec,
+                                                        uint32_t *__restrict__ rowmax, uint32_t *__restrict__ colmax) {
+    constexpr int TR = 64, TC = 512;
+    __shared__ uint32_t cm[COLS ? 8 : 1][COLS ? TC : 1];
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    const int64_t tiles_c = (C + TC - 1) / TC, tiles = ((R + TR - 1) / TR) * tiles_c;
+    for (int64_t t = blockIdx.x; t < tiles; t += gridDim.x) {
+        const int64_t r0 = (t / tiles_c) * TR, c0 = (t % tiles_c) * TC;
+        uint32_t cmx[16];
+#pragma unroll
+        for (int k = 0; k < 16; k++) cmx[k] = 0;
+#pragma unroll 2
+        for (int i = 0; i < TR / 8; i++) {
+            const int64_t r = r0 + warp + 8 * i;
+            uint32_t rmx = 0;
+            if (r < R) {
+                const float *p = src + r * C;
+#pragma unroll
+                for (int qq = 0; qq < 4; qq++) {
+                    const int64_t c = c0 + qq * 128 + 4 * lane;
+                    uint32_t b[4];
+                    if (vec && c + 4 <= C) {
+                        const uint4 u = __ldg(reinterpret_cast<const uint4 *>(p + c));
+                        b[0] = u.x; b[1] = u.y; b[2] = u.z; b[3] = u.w;
+                    } else {
+#pragma unroll
+                        for (int e = 0; e < 4; e++) b[e] = c + e < C ? __float_as_uint(p[c + e]) : 0u;
+                    }
+#pragma unroll
+                    for (int e = 0; e < 4; e++) {
+                        const uint32_t m = finite_bits(__uint_as_float(b[e]));
+                        rmx = max(rmx, m);
+                        cmx[qq * 4 + e] = max(cmx[qq * 4 + e], m);
+                    }
+                }
+            }
+            if (ROWS) {
+#pragma unroll
+                for (int o = 16; o > 0; o >>= 1) rmx = max(rmx, __shfl_xor_sync(0xffffffffu, rmx, o));
+                if (lane == 0 && r < R && rmx) atomicMax(rowmax + r, rmx);
+            }
+        }
+        if (COLS) {
+#pragma unroll
+            for (int k = 0; k < 16; k++) cm[warp][(k >> 2) * 128 + 4 * lane + (k & 3)] = cmx[k];
+            __syncthreads();
+            for (int cc = threadIdx.x; cc < TC; cc += blockDim.x) {
+                uint32_t m = 0;
+#pragma unroll
+                for (int w = 0; w < 8; w++) m = max(m, cm[w][cc]);
+                if (m && c0 + cc < C) atomicMax(colmax + c0 + cc, m);
+            }
+            __syncthreads();
+        }
+    }
+}
+
+// The scale 2^e of a line from its max word.
+__device__ __forceinline__ float line_scale(const uint32_t *lines, int64_t i) {
+    return pow2f(split_exp(__ldg(lines + i)));
+}
+
+// 3xTF32 split of X [rows, cols] in its stored layout -> hi/lo [rows, pitch]
+// (pitch = cols rounded up to 4): with row scales from rmax into hr/lr (a
+// split for K-major use) and/or column scales from cmax into hc/lc (for
+// MN-major use).  The scales keep FP32 subnormals, which TF32 products do
+// not, exact.  4 consecutive columns per thread step: 16-byte loads when the
+// source allows, 16-byte stores; padding columns are written as zero.
 __global__ void __launch_bounds__(256) split_kernel(const float *__restrict__ src, int64_t rows, int64_t cols,
-                                                    int64_t pitch, int vec, float *__restrict__ hi,
-                                                    float *__restrict__ lo) {
+                                                    int64_t pitch, int vec, const uint32_t *__restrict__ rmax,
+                                                    const uint32_t *__restrict__ cmax, float *__restrict__ hr,
+                                                    float *__restrict__ lr, float *__restrict__ hc,
+                                                    float *__restrict__ lc, SplitHeader *hdr_r, SplitHeader *hdr_c,
+                                                    uint32_t *__restrict__ copy_r, uint32_t *__restrict__ copy_c) {
     const int64_t q = pitch / 4;
     const int64_t n = rows * q;
-    for (int64_t v = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; v < n;
-         v += (int64_t)gridDim.x * blockDim.x) {
+    const int64_t t0 = blockIdx.x * (int64_t)blockDim.x + threadIdx.x, stride = (int64_t)gridDim.x * blockDim.x;
+    if (t0 == 0) {
+        if (hdr_r) write_header(hdr_r, src, 0, (uint32_t)rows);
+        if (hdr_c) write_header(hdr_c, src, kLayoutCols, (uint32_t)cols);
+    }
+    if (copy_r)
+        for (int64_t i = t0; i < rows; i += stride) copy_r[i] = rmax[i];
+    if (copy_c)
+        for (int64_t i = t0; i < cols; i += stride) copy_c[i] = cmax[i];
+    bool bad = false;
+    for (int64_t v = t0; v < n; v += stride) {
         const int64_t r = v / q, k = (v - r * q) * 4;
         float x[4];
         const float *p = src + r * cols + k;
@@ -666,18 +945,34 @@ __global__ void __launch_bounds__(256) split_kernel(const float *__restrict__ sr
 #pragma unroll
             for (int j = 0; j < 4; j++) x[j] = (k + j < cols) ? p[j] : 0.0f;
         }
-        float h[4], l[4];
 #pragma unroll
-        for (int j = 0; j < 4; j++) {
-            h[j] = tf32_round(x[j]);
-            l[j] = tf32_round(x[j] - h[j]);
+        for (int j = 0; j < 4; j++) x[j] = finite_or_zero(x[j], bad);
+        float h[4], l[4];
+        if (hr) {
+            const float sc = line_scale(rmax, r);
+#pragma unroll
+            for (int j = 0; j < 4; j++) {
+                h[j] = tf32_round(x[j] * sc);
+                l[j] = tf32_round(x[j] * sc - h[j]);
+            }
+            *reinterpret_cast<float4 *>(hr + r * pitch + k) = make_float4(h[0], h[1], h[2], h[3]);
+            *reinterpret_cast<float4 *>(lr + r * pitch + k) = make_float4(l[0], l[1], l[2], l[3]);
         }
-        *reinterpret_cast<float4 *>(hi + r * pitch + k) = make_float4(h[0], h[1], h[2], h[3]);
-        *reinterpret_cast<float4 *>(lo + r * pitch + k) = make_float4(l[0], l[1], l[2], l[3]);
+        if (hc) {
+#pragma unroll
+            for (int j = 0; j < 4; j++) {
+                const float sc = k + j < cols ? line_scale(cmax, k + j) : 1.0f;
+                h[j] = tf32_round(x[j] * sc);
+                l[j] = tf32_round(x[j] * sc - h[j]);
+            }
+            *reinterpret_cast<float4 *>(hc + r * pitch + k) = make_float4(h[0], h[1], h[2], h[3]);
+            *reinterpret_cast<float4 *>(lc + r * pitch + k) = make_float4(l[0], l[1], l[2], l[3]);
+        }
     }
+    flag_nonfinite(bad, hdr_r, hdr_c);
 }
 
-// Transposed split: X [rows, cols] -> hi/lo of X^T, [cols, pitch] with
+// Transposed 3xTF32 split: X [rows, cols] -> hi/lo of X^T, [cols, pitch] with
 // pitch = rows rounded up to 4.  64 x 64 tiles through shared memory; each
 // lane reads 4 consecutive floats of an X row (16 bytes when X's rows allow)
 // and writes 4 consecutive floats of an X^T row to hi and to lo (16 bytes;
@@ -687,12 +982,25 @@ __global__ void __launch_bounds__(256) split_kernel(const float *__restrict__ sr
 // an operand for one read of it.
 __global__ void __launch_bounds__(256) split_t_kernel(const float *__restrict__ src, int64_t rows, int64_t cols,
                                                       int64_t pitch, int64_t tiles_c, int vec_in,
-                                                      float *__restrict__ hi, float *__restrict__ lo,
-                                                      float *__restrict__ phi, float *__restrict__ plo,
-                                                      int64_t ppitch) {
+                                                      const uint32_t *__restrict__ rmax,
+                                                      const uint32_t *__restrict__ cmax, float *__restrict__ hi,
+                                                      float *__restrict__ lo, float *__restrict__ phi,
+                                                      float *__restrict__ plo, int64_t ppitch, SplitHeader *ht,
+                                                      SplitHeader *hp, uint32_t *__restrict__ copy_t,
+                                                      uint32_t *__restrict__ copy_p) {
     __shared__ float tile[64][65];
+    const int64_t t0 = blockIdx.x * (int64_t)blockDim.x + threadIdx.x, stride = (int64_t)gridDim.x * blockDim.x;
+    if (t0 == 0) {
+        write_header(ht, src, kLayoutT, (uint32_t)cols);
+        if (hp) write_header(hp, src, 0, (uint32_t)rows);
+    }
+    if (copy_t)
+        for (int64_t i = t0; i < cols; i += stride) copy_t[i] = cmax[i];
+    if (copy_p)
+        for (int64_t i = t0; i < rows; i += stride) copy_p[i] = rmax[i];
     const int64_t c0 = (blockIdx.x % tiles_c) * 64, r0 = (blockIdx.x / tiles_c) * 64;
     const int q = threadIdx.x & 15, w = threadIdx.x >> 4;  // 16 lanes per 64-float row, 16 rows per pass
+    bool bad = false;
 #pragma unroll
     for (int pass = 0; pass < 4; pass++) {  // tile[i][4q..4q+3] = X[r0 + i][c0 + 4q ..]
         const int i = pass * 16 + w;
@@ -708,13 +1016,17 @@ __global__ void __launch_bounds__(256) split_t_kernel(const float *__restrict__ 
             }
         }
 #pragma unroll
-        for (int k = 0; k < 4; k++) tile[i][4 * q + k] = v[k];
+        for (int k = 0; k < 4; k++) {
+            v[k] = finite_or_zero(v[k], bad);
+            tile[i][4 * q + k] = v[k];
+        }
         if (phi && r < rows && c < ppitch) {  // columns past `cols` were loaded as zero
+            const float sc = line_scale(rmax, r);
             float h[4], l[4];
 #pragma unroll
             for (int k = 0; k < 4; k++) {
-                h[k] = tf32_round(v[k]);
-                l[k] = tf32_round(v[k] - h[k]);
+                h[k] = tf32_round(v[k] * sc);
+                l[k] = tf32_round(v[k] * sc - h[k]);
             }
             *reinterpret_cast<float4 *>(phi + r * ppitch + c) = make_float4(h[0], h[1], h[2], h[3]);
             *reinterpret_cast<float4 *>(plo + r * ppitch + c) = make_float4(l[0], l[1], l[2], l[3]);
@@ -726,138 +1038,119 @@ __global__ void __launch_bounds__(256) split_t_kernel(const float *__restrict__ 
         const int j = pass * 16 + w;
         const int64_t c = c0 + j, r = r0 + 4 * q;
         if (c >= cols || r >= pitch) continue;
+        const float sc = line_scale(cmax, c);
         float h[4], l[4];
 #pragma unroll
         for (int k = 0; k < 4; k++) {
-            const float x = tile[4 * q + k][j];  // rows >= `rows` were loaded as zero
+            const float x = tile[4 * q + k][j] * sc;  // rows >= `rows` were loaded as zero
             h[k] = tf32_round(x);
             l[k] = tf32_round(x - h[k]);
         }
         *reinterpret_cast<float4 *>(hi + c * pitch + r) = make_float4(h[0], h[1], h[2], h[3]);
         *reinterpret_cast<float4 *>(lo + c * pitch + r) = make_float4(l[0], l[1], l[2], l[3]);
     }
+    flag_nonfinite(bad, ht, hp);
 }
 
-// ---- 3xFP16 operand split --------------------------------------------------------------
-// *word = the bits of max |x| over the finite elements of X [n] (zeroed beforehand):
-// non-negative floats order like their bits as unsigned integers.
-__global__ void __launch_bounds__(256) absmax_kernel(const float *__restrict__ src, int64_t n, int vec,
-                                                     uint32_t *__restrict__ word) {
-    uint32_t m = 0;
-    const int64_t stride = (int64_t)gridDim.x * blockDim.x;
-    const int64_t t0 = blockIdx.x * (int64_t)blockDim.x + threadIdx.x;
-    int64_t done = 0;
-    if (vec) {
-        // four independent 16-byte loads in flight per thread
-        const uint4 *s4 = reinterpret_cast<const uint4 *>(src);
-        const int64_t n4 = n / 4;
-        int64_t v = t0;
-        for (; v + 3 * stride < n4; v += 4 * stride) {
-            uint4 u[4];
-#pragma unroll
-            for (int i = 0; i < 4; i++) u[i] = __ldg(s4 + v + i * stride);
-#pragma unroll
-            for (int i = 0; i < 4; i++) {
-                const uint32_t b[4] = {u[i].x & 0x7FFFFFFFu, u[i].y & 0x7FFFFFFFu, u[i].z & 0x7FFFFFFFu,
-                                       u[i].w & 0x7FFFFFFFu};
-#pragma unroll
-                for (int j = 0; j < 4; j++)
-                    if (b[j] < 0x7F800000u && b[j] > m) m = b[j];
-            }
-        }
-        for (; v < n4; v += stride) {
-            const uint4 u = __ldg(s4 + v);
-            const uint32_t b[4] = {u.x & 0x7FFFFFFFu, u.y & 0x7FFFFFFFu, u.z & 0x7FFFFFFFu, u.w & 0x7FFFFFFFu};
-#pragma unroll
-            for (int j = 0; j < 4; j++)
-                if (b[j] < 0x7F800000u && b[j] > m) m = b[j];
-        }
-        done = n4 * 4;
-    }
-    for (int64_t i = done + t0; i < n; i += stride) {
-        const uint32_t b = __float_as_uint(src[i]) & 0x7FFFFFFFu;
-        if (b < 0x7F800000u && b > m) m = b;
-    }
-    for (int o = 16; o > 0; o >>= 1) m = max(m, __shfl_xor_sync(0xffffffffu, m, o));
-    if ((threadIdx.x & 31) == 0 && m) atomicMax(word, m);
-}
-
-// hi = fp16(x 2^e), lo = fp16(x 2^e - hi) of 8 consecutive values.
-__device__ __forceinline__ void split8_f16(const float (&x)[8], float sc, uint4 &h, uint4 &l) {
-    uint32_t hw[4], lw[4];
-#pragma unroll
-    for (int j = 0; j < 4; j++) {
-        const float a = x[2 * j] * sc, b = x[2 * j + 1] * sc;
-        const __half ha = __float2half_rn(a), hb = __float2half_rn(b);
-        const __half la = __float2half_rn(a - __half2float(ha)), lb = __float2half_rn(b - __half2float(hb));
-        hw[j] = (uint32_t)__half_as_ushort(ha) | ((uint32_t)__half_as_ushort(hb) << 16);
-        lw[j] = (uint32_t)__half_as_ushort(la) | ((uint32_t)__half_as_ushort(lb) << 16);
-    }
-    h = make_uint4(hw[0], hw[1], hw[2], hw[3]);
-    l = make_uint4(lw[0], lw[1], lw[2], lw[3]);
+// ---- 3xFP16 splits ----------------------------------------------------------------------
+// hi = fp16(x s), lo = fp16(x s - hi) of a finite x (x s - hi is exact in FP32).
+__device__ __forceinline__ uint32_t split2_f16(float a, float b, float sa, float sb, uint32_t &lw) {
+    const float xa = a * sa, xb = b * sb;
+    const __half ha = __float2half_rn(xa), hb = __float2half_rn(xb);
+    const __half la = __float2half_rn(xa - __half2float(ha)), lb = __float2half_rn(xb - __half2float(hb));
+    lw = (uint32_t)__half_as_ushort(la) | ((uint32_t)__half_as_ushort(lb) << 16);
+    return (uint32_t)__half_as_ushort(ha) | ((uint32_t)__half_as_ushort(hb) << 16);
 }
 
 // X [rows, cols] -> fp16 hi/lo [rows, pitch] (pitch = cols rounded up to 8,
-// padding written as zero), scaled by 2^e from the max word.  8 columns per
-// thread step: 32-byte loads when the source allows, 16-byte stores.
+// padding written as zero) in the stored layout: with row scales from rmax
+// into hr/lr (a split for K-major use) and/or with column scales from cmax
+// into hc/lc (for MN-major use).  8 columns per thread step: 32-byte loads
+// when the source allows, 16-byte stores.  copy_r / copy_c, when given,
+// receive rmax / cmax (the outputs' own line words, when the maxima came
+// from elsewhere).
 __global__ void __launch_bounds__(256) split16_kernel(const float *__restrict__ src, int64_t rows, int64_t cols,
-                                                      int64_t pitch, int vec, const uint32_t *__restrict__ word,
-                                                      __half *__restrict__ hi, __half *__restrict__ lo) {
-    const float sc = pow2f(split_exp(*word));
+                                                      int64_t pitch, int vec, const uint32_t *__restrict__ rmax,
+                                                      const uint32_t *__restrict__ cmax, __half *__restrict__ hr,
+                                                      __half *__restrict__ lr, __half *__restrict__ hc,
+                                                      __half *__restrict__ lc, SplitHeader *hdr_r,
+                                                      SplitHeader *hdr_c, uint32_t *__restrict__ copy_r,
+                                                      uint32_t *__restrict__ copy_c) {
     const int64_t q = pitch / 8;
     const int64_t n = rows * q;
-    for (int64_t v = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; v < n;
-         v += (int64_t)gridDim.x * blockDim.x) {
+    const int64_t t0 = blockIdx.x * (int64_t)blockDim.x + threadIdx.x, stride = (int64_t)gridDim.x * blockDim.x;
+    if (t0 == 0) {
+        if (hdr_r) write_header(hdr_r, src, 0, (uint32_t)rows);
+        if (hdr_c) write_header(hdr_c, src, kLayoutCols, (uint32_t)cols);
+    }
+    if (copy_r)
+        for (int64_t i = t0; i < rows; i += stride) copy_r[i] = rmax[i];
+    if (copy_c)
+        for (int64_t i = t0; i < cols; i += stride) copy_c[i] = cmax[i];
+    bool bad = false;
+    for (int64_t v = t0; v < n; v += stride) {
         const int64_t r = v / q, k = (v - r * q) * 8;
         float x[8];
         const float *p = src + r * cols + k;
         if (vec && k + 8 <= cols) {
-            const float4 t0 = __ldg(reinterpret_cast<const float4 *>(p));
-            const float4 t1 = __ldg(reinterpret_cast<const float4 *>(p) + 1);
-            x[0] = t0.x; x[1] = t0.y; x[2] = t0.z; x[3] = t0.w;
-            x[4] = t1.x; x[5] = t1.y; x[6] = t1.z; x[7] = t1.w;
+            const float4 t0v = __ldg(reinterpret_cast<const float4 *>(p));
+            const float4 t1v = __ldg(reinterpret_cast<const float4 *>(p) + 1);
+            x[0] = t0v.x; x[1] = t0v.y; x[2] = t0v.z; x[3] = t0v.w;
+            x[4] = t1v.x; x[5] = t1v.y; x[6] = t1v.z; x[7] = t1v.w;
         } else {
 #pragma unroll
             for (int j = 0; j < 8; j++) x[j] = (k + j < cols) ? p[j] : 0.0f;
         }
-        uint4 h, l;
-        split8_f16(x, sc, h, l);
-        *reinterpret_cast<uint4 *>(hi + r * pitch + k) = h;
-        *reinterpret_cast<uint4 *>(lo + r * pitch + k) = l;
-    }
-}
-
-// hi = fp16(x 2^e), lo = fp16(x 2^e - hi) of 4 consecutive values, packed.
-__device__ __forceinline__ void split4_f16(const float (&x)[4], float sc, uint2 &h, uint2 &l) {
-    uint32_t hw[2], lw[2];
 #pragma unroll
-    for (int j = 0; j < 2; j++) {
-        const float a = x[2 * j] * sc, b = x[2 * j + 1] * sc;
-        const __half ha = __float2half_rn(a), hb = __float2half_rn(b);
-        const __half la = __float2half_rn(a - __half2float(ha)), lb = __float2half_rn(b - __half2float(hb));
-        hw[j] = (uint32_t)__half_as_ushort(ha) | ((uint32_t)__half_as_ushort(hb) << 16);
-        lw[j] = (uint32_t)__half_as_ushort(la) | ((uint32_t)__half_as_ushort(lb) << 16);
+        for (int j = 0; j < 8; j++) x[j] = finite_or_zero(x[j], bad);
+        if (hr) {
+            const float sc = line_scale(rmax, r);
+            uint32_t hw[4], lw[4];
+#pragma unroll
+            for (int j = 0; j < 4; j++) hw[j] = split2_f16(x[2 * j], x[2 * j + 1], sc, sc, lw[j]);
+            *reinterpret_cast<uint4 *>(hr + r * pitch + k) = make_uint4(hw[0], hw[1], hw[2], hw[3]);
+            *reinterpret_cast<uint4 *>(lr + r * pitch + k) = make_uint4(lw[0], lw[1], lw[2], lw[3]);
+        }
+        if (hc) {
+            float sc[8];
+#pragma unroll
+            for (int j = 0; j < 8; j++) sc[j] = k + j < cols ? line_scale(cmax, k + j) : 1.0f;
+            uint32_t hw[4], lw[4];
+#pragma unroll
+            for (int j = 0; j < 4; j++) hw[j] = split2_f16(x[2 * j], x[2 * j + 1], sc[2 * j], sc[2 * j + 1], lw[j]);
+            *reinterpret_cast<uint4 *>(hc + r * pitch + k) = make_uint4(hw[0], hw[1], hw[2], hw[3]);
+            *reinterpret_cast<uint4 *>(lc + r * pitch + k) = make_uint4(lw[0], lw[1], lw[2], lw[3]);
+        }
     }
-    h = make_uint2(hw[0], hw[1]);
-    l = make_uint2(lw[0], lw[1]);
+    flag_nonfinite(bad, hdr_r, hdr_c);
 }
 
-// The fp16 split of X^T ([cols, pitch], pitch = rows rounded up to 8) and,
-// with phi / plo set, of X in its stored layout ([rows, ppitch], ppitch =
-// cols rounded up to 8) from the same loads; split_t_kernel's tiling, 8-byte
-// stores of 4 halves.  The first thread copies the max word to pword.
+// The fp16 split of X^T ([cols, pitch], pitch = rows rounded up to 8; its
+// rows are X's columns, scaled by cmax) and, with phi / plo set, the
+// row-scaled split of X in its stored layout ([rows, ppitch], ppitch = cols
+// rounded up to 8, scaled by rmax) from the same loads; split_t_kernel's
+// tiling, 8-byte stores of 4 halves.
 __global__ void __launch_bounds__(256) split16_t_kernel(const float *__restrict__ src, int64_t rows, int64_t cols,
                                                         int64_t pitch, int64_t tiles_c, int vec_in,
-                                                        const uint32_t *__restrict__ word, __half *__restrict__ hi,
+                                                        const uint32_t *__restrict__ rmax,
+                                                        const uint32_t *__restrict__ cmax, __half *__restrict__ hi,
                                                         __half *__restrict__ lo, __half *__restrict__ phi,
-                                                        __half *__restrict__ plo, int64_t ppitch,
-                                                        uint32_t *__restrict__ pword) {
+                                                        __half *__restrict__ plo, int64_t ppitch, SplitHeader *ht,
+                                                        SplitHeader *hp, uint32_t *__restrict__ copy_t,
+                                                        uint32_t *__restrict__ copy_p) {
     __shared__ float tile[64][65];
-    const uint32_t mw = *word;
-    const float sc = pow2f(split_exp(mw));
-    if (pword && blockIdx.x == 0 && threadIdx.x == 0) *pword = mw;
+    const int64_t t0 = blockIdx.x * (int64_t)blockDim.x + threadIdx.x, stride = (int64_t)gridDim.x * blockDim.x;
+    if (t0 == 0) {
+        write_header(ht, src, kLayoutT, (uint32_t)cols);
+        if (hp) write_header(hp, src, 0, (uint32_t)rows);
+    }
+    if (copy_t)
+        for (int64_t i = t0; i < cols; i += stride) copy_t[i] = cmax[i];
+    if (copy_p)
+        for (int64_t i = t0; i < rows; i += stride) copy_p[i] = rmax[i];
     const int64_t c0 = (blockIdx.x % tiles_c) * 64, r0 = (blockIdx.x / tiles_c) * 64;
     const int q = threadIdx.x & 15, w = threadIdx.x >> 4;
+    bool bad = false;
 #pragma unroll
     for (int pass = 0; pass < 4; pass++) {
         const int i = pass * 16 + w;
@@ -873,12 +1166,16 @@ __global__ void __launch_bounds__(256) split16_t_kernel(const float *__restrict_
             }
         }
 #pragma unroll
-        for (int k = 0; k < 4; k++) tile[i][4 * q + k] = v[k];
+        for (int k = 0; k < 4; k++) {
+            v[k] = finite_or_zero(v[k], bad);
+            tile[i][4 * q + k] = v[k];
+        }
         if (phi && r < rows && c < ppitch) {  // columns past `cols` were loaded as zero
-            uint2 h, l;
-            split4_f16(v, sc, h, l);
-            *reinterpret_cast<uint2 *>(phi + r * ppitch + c) = h;
-            *reinterpret_cast<uint2 *>(plo + r * ppitch + c) = l;
+            const float sc = line_scale(rmax, r);
+            uint32_t lw0, lw1;
+            const uint32_t h0 = split2_f16(v[0], v[1], sc, sc, lw0), h1 = split2_f16(v[2], v[3], sc, sc, lw1);
+            *reinterpret_cast<uint2 *>(phi + r * ppitch + c) = make_uint2(h0, h1);
+            *reinterpret_cast<uint2 *>(plo + r * ppitch + c) = make_uint2(lw0, lw1);
         }
     }
     __syncthreads();
@@ -887,12 +1184,14 @@ __global__ void __launch_bounds__(256) split16_t_kernel(const float *__restrict_
         const int j = pass * 16 + w;
         const int64_t c = c0 + j, r = r0 + 4 * q;
         if (c >= cols || r >= pitch) continue;
-        const float x[4] = {tile[4 * q][j], tile[4 * q + 1][j], tile[4 * q + 2][j], tile[4 * q + 3][j]};
-        uint2 h, l;
-        split4_f16(x, sc, h, l);
-        *reinterpret_cast<uint2 *>(hi + c * pitch + r) = h;
-        *reinterpret_cast<uint2 *>(lo + c * pitch + r) = l;
+        const float sc = line_scale(cmax, c);
+        uint32_t lw0, lw1;
+        const uint32_t h0 = split2_f16(tile[4 * q][j], tile[4 * q + 1][j], sc, sc, lw0);
+        const uint32_t h1 = split2_f16(tile[4 * q + 2][j], tile[4 * q + 3][j], sc, sc, lw1);
+        *reinterpret_cast<uint2 *>(hi + c * pitch + r) = make_uint2(h0, h1);
+        *reinterpret_cast<uint2 *>(lo + c * pitch + r) = make_uint2(lw0, lw1);
     }
+    flag_nonfinite(bad, ht, hp);
 }
 
 // ---- host side -------------------------------------------------------------------------
@@ -920,20 +1219,25 @@ bool split_fp16() {
     return f16;
 }
 
-// Elements per row of a split array: cols rounded up to a 16-byte multiple.
+// Elements per row of a split's data: cols rounded up to a 16-byte multiple.
 inline int64_t split_pitch(int64_t cols) { return split_fp16() ? ceil_div(cols, 8) * 8 : ceil_div(cols, 4) * 4; }
 inline int64_t split_esize() { return split_fp16() ? 2 : 4; }
 
-// Bytes of one hi or lo array of an operand [rows, cols]; an fp16 hi array is
-// followed by its 32-bit max word (16 bytes reserved).
-inline int64_t split_bytes(int64_t rows, int64_t cols) {
-    return rows * split_pitch(cols) * split_esize() + (split_fp16() ? 16 : 0);
+// Bytes of a split's data [rd, cd] (a multiple of 16).
+inline int64_t split_data_bytes(int64_t rd, int64_t cd) { return rd * split_pitch(cd) * split_esize(); }
+
+// Bytes of one hi or lo array of a split whose data is [rd, cd], for either
+// line axis: the data, the header and max(rd, cd) line words.
+inline int64_t split_bytes(int64_t rd, int64_t cd) {
+    return ceil_div(split_data_bytes(rd, cd) + (int64_t)sizeof(SplitHeader) + 4 * std::max(rd, cd), 16) * 16;
 }
 
-// The max word of an fp16 hi array of an operand [rows, cols].
-inline uint32_t *split_word(const float *hi, int64_t rows, int64_t cols) {
-    return reinterpret_cast<uint32_t *>(reinterpret_cast<char *>(const_cast<float *>(hi)) +
-                                        rows * split_pitch(cols) * 2);
+// The header of a hi array whose data is [rd, cd], and its line words.
+inline SplitHeader *split_header(const float *hi, int64_t rd, int64_t cd) {
+    return reinterpret_cast<SplitHeader *>(reinterpret_cast<char *>(const_cast<float *>(hi)) + split_data_bytes(rd, cd));
+}
+inline uint32_t *split_lines(const float *hi, int64_t rd, int64_t cd) {
+    return reinterpret_cast<uint32_t *>(split_header(hi, rd, cd) + 1);
 }
 
 // Tensor map of a hi or lo array [rows, pitch] (pitch * esize bytes per row).
@@ -1057,13 +1361,13 @@ static int launch_gemm(const float *ah, const float *al, const float *bh, const 
         arrivals = reinterpret_cast<int *>(part + (tiles - tp.full_tiles) * tp.splits * BM * BN);
         J4C_CUDA(cudaMemsetAsync(arrivals, 0, (size_t)((tiles - tp.full_tiles) * kEpiWarps) * sizeof(int), s));
     }
-    if (ep.out_max) J4C_CUDA(cudaMemsetAsync(ep.out_max, 0, sizeof(uint32_t), s));
-    const uint32_t *amax = F16 ? split_word(ah, ar * ab, ac) : nullptr;
-    const uint32_t *bmax = F16 ? split_word(bh, br * bb, bc) : nullptr;
-    kernel<<<grid, kThreads, Q::SMEM_BYTES, s>>>(mAh, mAl, mBh, mBl, c, (int)M, (int)N, (int)num_kb,
+    if (ep.out_lines) J4C_CUDA(cudaMemsetAsync(ep.out_lines, 0, (size_t)(M + N) * sizeof(uint32_t), s));
+    const SplitHeader *ahdr = split_header(ah, ar * ab, ac);
+    const SplitHeader *bhdr = split_header(bh, br * bb, bc);
+    kernel<<<grid, kThreads, Q::SMEM_BYTES, s>>>(mAh, mAl, mBh, mBl, c, (int)M, (int)N, (int)K, (int)num_kb,
                                                  store_t ? 0 : vec, store_t ? 1 : 0, ep, (int)batch, a_bat ? 1 : 0,
                                                  b_bat ? 1 : 0, status, (int)tp.full_tiles, tp.splits, part, arrivals,
-                                                 amax, bmax);
+                                                 ahdr, bhdr);
     J4C_LAUNCH_CHECK("gemm_3xtf32_kernel");
     if (owned) return scratch_free(owned, s);
     return J4C_OK;
@@ -1086,69 +1390,93 @@ static int launch_gemm_any(const float *ah, const float *al, const float *bh, co
     return launch_gemm<BN, STAGES, BK, true, true, F16>(ah, al, bh, bl, c, M, N, K, false, ep, batch, a_bat, b_bat, tail_ws, s);
 }
 
-// *word = the bits of X's max finite |x| (n elements).
-static int absmax(const float *src, int64_t n, uint32_t *word, cudaStream_t s) {
-    J4C_CUDA(cudaMemsetAsync(word, 0, sizeof(uint32_t), s));
-    const int vec = aligned16(src);
-    absmax_kernel<<<grid_for(vec ? ceil_div(n, 16) : n, 256, 8), 256, 0, s>>>(src, n, vec, word);
-    J4C_LAUNCH_CHECK("absmax_kernel");
+// rowmax[r] / colmax[c] (either may be NULL): the bits of the largest finite
+// |x| of each row / column of X [rows, cols]; zeroed here first.
+static int lines_max(const float *src, int64_t rows, int64_t cols, uint32_t *rowmax, uint32_t *colmax,
+                     cudaStream_t s) {
+    if (rowmax) J4C_CUDA(cudaMemsetAsync(rowmax, 0, (size_t)rows * sizeof(uint32_t), s));
+    if (colmax) J4C_CUDA(cudaMemsetAsync(colmax, 0, (size_t)cols * sizeof(uint32_t), s));
+    if (!rowmax && !colmax) return J4C_OK;
+    const int vec = (cols % 4 == 0) && aligned16(src);
+    const int64_t tiles = ceil_div(rows, 64) * ceil_div(cols, 512);
+    const unsigned grid = (unsigned)std::min<int64_t>(tiles, (int64_t)sm_count() * 8);
+    if (rowmax && colmax) lines_max_kernel<true, true><<<grid, 256, 0, s>>>(src, rows, cols, vec, rowmax, colmax);
+    else if (rowmax) lines_max_kernel<true, false><<<grid, 256, 0, s>>>(src, rows, cols, vec, rowmax, colmax);
+    else lines_max_kernel<false, true><<<grid, 256, 0, s>>>(src, rows, cols, vec, rowmax, colmax);
+    J4C_LAUNCH_CHECK("lines_max_kernel");
     return J4C_OK;
 }
 
-// The split of X^T, and with phi / plo also X's own split, in one pass.
-// max_in (3xFP16 only): X's max word computed already (a GEMM epilogue's
-// out_max), copied instead of a max pass.
-int split_t(const float *src, int64_t rows, int64_t cols, float *hi, float *lo, cudaStream_t s,
-            float *phi = nullptr, float *plo = nullptr, const uint32_t *max_in = nullptr) {
+// Any of the splits of X [rows, cols] in one pass over it:
+//   r: the stored layout with row lines (read K-major),
+//   c: the stored layout with column lines (read MN-major),
+//   t: X^T with its rows (X's columns) as lines (read K-major),
+// r alone, c alone, t alone, r + c or r + t.  lines_in (may be NULL):
+// X's line maxima computed already, rows then columns, as a GEMM epilogue's
+// out_lines leaves them; otherwise a max pass over X computes those needed.
+int split_any(const float *src, int64_t rows, int64_t cols, float *hr, float *lr, float *hc, float *lc, float *ht,
+              float *lt, const uint32_t *lines_in, cudaStream_t s) {
     if (rows == 0 || cols == 0) return J4C_OK;
-    J4C_REQUIRE(aligned16(hi) && aligned16(lo), "split: hi/lo must be 16-byte aligned");
-    J4C_REQUIRE(!phi == !plo && (!phi || (aligned16(phi) && aligned16(plo))),
-                "split: both stored-layout outputs, 16-byte aligned");
-    const int64_t pitch = split_pitch(rows);
-    const int64_t tiles_c = ceil_div(cols, 64), tiles_r = ceil_div(pitch, 64);
-    J4C_REQUIRE(tiles_c * tiles_r < (1ll << 31), "split: array too large");
-    const int vec_in = (cols % 4 == 0) && aligned16(src);
-    if (split_fp16()) {
-        uint32_t *word = split_word(hi, cols, rows);
-        if (max_in) {
-            J4C_CUDA(cudaMemcpyAsync(word, max_in, sizeof(uint32_t), cudaMemcpyDeviceToDevice, s));
+    J4C_REQUIRE(!hr == !lr && !hc == !lc && !ht == !lt, "split: hi and lo come in pairs");
+    J4C_REQUIRE(hr || hc || ht, "split: no output");
+    J4C_REQUIRE(!(hc && ht), "split: the column-line and the transposed split are alternatives, not one pass");
+    for (const float *p : {hr, lr, hc, lc, ht, lt})
+        J4C_REQUIRE(!p || aligned16(p), "split: hi/lo must be 16-byte aligned");
+    J4C_REQUIRE(rows < (1ll << 31) && cols < (1ll << 31), "split: extent too large");
+    const bool f16 = split_fp16();
+    SplitHeader *hdr_r = hr ? split_header(hr, rows, cols) : nullptr;
+    SplitHeader *hdr_c = hc ? split_header(hc, rows, cols) : nullptr;
+    SplitHeader *hdr_t = ht ? split_header(ht, cols, rows) : nullptr;
+    // headers start at zero (their line words are written whole below)
+    if (hdr_r) J4C_CUDA(cudaMemsetAsync(hdr_r, 0, sizeof(SplitHeader), s));
+    if (hdr_c) J4C_CUDA(cudaMemsetAsync(hdr_c, 0, sizeof(SplitHeader), s));
+    if (hdr_t) J4C_CUDA(cudaMemsetAsync(hdr_t, 0, sizeof(SplitHeader), s));
+    uint32_t *own_r = hdr_r ? reinterpret_cast<uint32_t *>(hdr_r + 1) : nullptr;
+    uint32_t *own_c = hdr_c ? reinterpret_cast<uint32_t *>(hdr_c + 1)
+                            : (hdr_t ? reinterpret_cast<uint32_t *>(hdr_t + 1) : nullptr);
+    const uint32_t *rmax = nullptr, *cmax = nullptr;
+    uint32_t *copy_r = nullptr, *copy_c = nullptr;
+    if (lines_in) {
+        rmax = lines_in;
+        cmax = lines_in + rows;
+        copy_r = own_r;
+        copy_c = own_c;
+    } else {
+        int rc = lines_max(src, rows, cols, own_r, own_c, s);
+        if (rc) return rc;
+        rmax = own_r;
+        cmax = own_c;
+    }
+    if (ht) {
+        const int64_t pitch = split_pitch(rows);
+        const int64_t tiles_c = ceil_div(cols, 64), tiles_r = ceil_div(pitch, 64);
+        J4C_REQUIRE(tiles_c * tiles_r < (1ll << 31), "split: array too large");
+        const int vec_in = (cols % 4 == 0) && aligned16(src);
+        if (f16) {
+            split16_t_kernel<<<(unsigned)(tiles_c * tiles_r), 256, 0, s>>>(
+                src, rows, cols, pitch, tiles_c, vec_in, rmax, cmax, reinterpret_cast<__half *>(ht),
+                reinterpret_cast<__half *>(lt), reinterpret_cast<__half *>(hr), reinterpret_cast<__half *>(lr),
+                split_pitch(cols), hdr_t, hdr_r, copy_c, copy_r);
+            J4C_LAUNCH_CHECK("split16_t_kernel");
         } else {
-            const int rc = absmax(src, rows * cols, word, s);
-            if (rc) return rc;
+            split_t_kernel<<<(unsigned)(tiles_c * tiles_r), 256, 0, s>>>(src, rows, cols, pitch, tiles_c, vec_in, rmax,
+                                                                         cmax, ht, lt, hr, lr, split_pitch(cols), hdr_t,
+                                                                         hdr_r, copy_c, copy_r);
+            J4C_LAUNCH_CHECK("split_t_kernel");
         }
-        split16_t_kernel<<<(unsigned)(tiles_c * tiles_r), 256, 0, s>>>(
-            src, rows, cols, pitch, tiles_c, vec_in, word, reinterpret_cast<__half *>(hi),
-            reinterpret_cast<__half *>(lo), reinterpret_cast<__half *>(phi), reinterpret_cast<__half *>(plo),
-            split_pitch(cols), phi ? split_word(phi, rows, cols) : nullptr);
-        J4C_LAUNCH_CHECK("split16_t_kernel");
         return J4C_OK;
     }
-    split_t_kernel<<<(unsigned)(tiles_c * tiles_r), 256, 0, s>>>(src, rows, cols, pitch, tiles_c, vec_in, hi, lo,
-                                                                 phi, plo, split_pitch(cols));
-    J4C_LAUNCH_CHECK("split_t_kernel");
-    return J4C_OK;
-}
-
-int split(const float *src, int64_t rows, int64_t cols, float *hi, float *lo, cudaStream_t s,
-          const uint32_t *max_in = nullptr) {
-    if (rows == 0 || cols == 0) return J4C_OK;
-    J4C_REQUIRE(aligned16(hi) && aligned16(lo), "split: hi/lo must be 16-byte aligned");
     const int64_t pitch = split_pitch(cols);
     const int vec = (cols % 4 == 0) && aligned16(src);
-    if (split_fp16()) {
-        uint32_t *word = split_word(hi, rows, cols);
-        if (max_in) {
-            J4C_CUDA(cudaMemcpyAsync(word, max_in, sizeof(uint32_t), cudaMemcpyDeviceToDevice, s));
-        } else {
-            const int rc = absmax(src, rows * cols, word, s);
-            if (rc) return rc;
-        }
+    if (f16) {
         split16_kernel<<<grid_for(rows * (pitch / 8), 256), 256, 0, s>>>(
-            src, rows, cols, pitch, vec, word, reinterpret_cast<__half *>(hi), reinterpret_cast<__half *>(lo));
+            src, rows, cols, pitch, vec, rmax, cmax, reinterpret_cast<__half *>(hr), reinterpret_cast<__half *>(lr),
+            reinterpret_cast<__half *>(hc), reinterpret_cast<__half *>(lc), hdr_r, hdr_c, copy_r, copy_c);
         J4C_LAUNCH_CHECK("split16_kernel");
         return J4C_OK;
     }
-    split_kernel<<<grid_for(rows * (pitch / 4), 256), 256, 0, s>>>(src, rows, cols, pitch, vec, hi, lo);
+    split_kernel<<<grid_for(rows * (pitch / 4), 256), 256, 0, s>>>(src, rows, cols, pitch, vec, rmax, cmax, hr, lr, hc,
+                                                                   lc, hdr_r, hdr_c, copy_r, copy_c);
     J4C_LAUNCH_CHECK("split_kernel");
     return J4C_OK;
 }
@@ -1160,15 +1488,15 @@ bool tc_gemm_supported(int64_t M, int64_t K, int64_t N) {
     return M >= 1 && N >= 1 && K >= 1 && M < (1ll << 31) && N < (1ll << 31) && K < (1ll << 31);
 }
 
-// Bytes of one hi or lo array of an operand stored [rows, cols], 256-byte aligned.
+// Bytes of one hi or lo array of a split whose data is [rows, cols], 256-byte aligned.
 static int64_t split_buf(int64_t rows, int64_t cols) { return ceil_div(tc::split_bytes(rows, cols), 256) * 256; }
 
-// Floats per row that a caller allocates for one hi or lo array of an
-// operand with `cols` columns: rows * this floats hold split_bytes(rows, cols)
-// for every rows >= 1 (3xFP16: 2-byte halves plus the 16-byte max word).
-int64_t tc_split_alloc_pitch(int64_t cols) {
-    return tc::split_fp16() ? tc::split_pitch(cols) / 2 + 4 : tc::split_pitch(cols);
-}
+// Floats of one hi or lo array of a split whose data is [rows, cols] (either
+// line axis): what a caller allocates for each of the two.
+int64_t tc_split_floats(int64_t rows, int64_t cols) { return tc::split_bytes(rows, cols) / 4; }
+
+// Elements per row of a split's data with `cols` columns.
+int64_t tc_split_pitch(int64_t cols) { return tc::split_pitch(cols); }
 
 // 1 for the 3xFP16 split, 0 for 3xTF32.
 int tc_split_kind() { return tc::split_fp16() ? 1 : 0; }
@@ -1182,25 +1510,16 @@ int tc_gemm_workspace(int64_t M, int64_t K, int64_t N, size_t *bytes) {
     return J4C_OK;
 }
 
-int tc_split_f32(const float *x, int64_t rows, int64_t cols, float *hi, float *lo, cudaStream_t s) {
-    return tc::split(x, rows, cols, hi, lo, s);
+int tc_split_any(const float *x, int64_t rows, int64_t cols, float *hr, float *lr, float *hc, float *lc, float *ht,
+                 float *lt, const uint32_t *lines_in, cudaStream_t s) {
+    return tc::split_any(x, rows, cols, hr, lr, hc, lc, ht, lt, lines_in, s);
 }
 
-int tc_split_f32_t(const float *x, int64_t rows, int64_t cols, float *hi, float *lo, cudaStream_t s) {
-    return tc::split_t(x, rows, cols, hi, lo, s);
-}
-
-int tc_split_f32_both(const float *x, int64_t rows, int64_t cols, float *hi, float *lo, float *hi_t, float *lo_t,
-                      cudaStream_t s) {
-    return tc::split_t(x, rows, cols, hi_t, lo_t, s, hi, lo);
-}
-
-// Any of the splits (stored layout: hi/lo; transposed: hi_t/lo_t; both in
-// one pass), with X's max word given (3xFP16) or NULL.
-int tc_split_f32_ex(const float *x, int64_t rows, int64_t cols, float *hi, float *lo, float *hi_t, float *lo_t,
-                    const uint32_t *max_in, cudaStream_t s) {
-    if (hi_t) return tc::split_t(x, rows, cols, hi_t, lo_t, s, hi, lo, max_in);
-    return tc::split(x, rows, cols, hi, lo, s, max_in);
+// lines [rows + cols]: X's row maxima, then its column maxima (bits of the
+// largest finite |x| of each line), as a GEMM epilogue's out_lines.
+int tc_split_lines(const float *x, int64_t rows, int64_t cols, uint32_t *lines, cudaStream_t s) {
+    if (rows == 0 || cols == 0) return J4C_OK;
+    return tc::lines_max(x, rows, cols, lines, lines + rows, s);
 }
 
 // tail_ws: scratch of at least tc::tail_scratch_bound bytes, or NULL to take it
@@ -1208,9 +1527,10 @@ int tc_split_f32_ex(const float *x, int64_t rows, int64_t cols, float *hi, float
 static int gemm_presplit_ws(const float *ah, const float *al, const float *bh, const float *bl, float *c, int64_t M,
                             int64_t K, int64_t N, int trans_a, int trans_b, const float *bias, const float *mask,
                             float *act, int64_t batch, int a_batched, int b_batched, void *tail_ws,
-                            cudaStream_t s, uint32_t *out_max = nullptr) {
+                            cudaStream_t s, uint32_t *out_lines = nullptr) {
     J4C_REQUIRE(aligned16(ah) && aligned16(al) && aligned16(bh) && aligned16(bl),
                 "dot: split operands must be 16-byte aligned");
+    J4C_REQUIRE(!out_lines || batch == 1, "dot: line maxima of a batched product");
     // op(A) = A [M,K] is read K-major; A^T (A stored [K,M]) MN-major.
     // op(B) = B [K,N] is read MN-major; B^T (B stored [N,K]) K-major.
     const bool a_mn = trans_a != 0, b_mn = trans_b == 0;
@@ -1218,7 +1538,7 @@ static int gemm_presplit_ws(const float *ah, const float *al, const float *bh, c
         const char *v = getenv("J4C_GEMM_VARIANT");
         return v ? atoi(v) : 1;
     }();
-    const tc::Epilogue ep{bias, mask, act, out_max};
+    const tc::Epilogue ep{bias, mask, act, out_lines, (int)M};
     const bool ab = a_batched != 0, bb = b_batched != 0;
     if (tc::split_fp16())
         return tc::launch_gemm_any<256, 4, 16, true>(ah, al, bh, bl, c, M, N, K, a_mn, b_mn, ep, batch, ab, bb, tail_ws, s);
@@ -1230,9 +1550,9 @@ static int gemm_presplit_ws(const float *ah, const float *al, const float *bh, c
 int tc_gemm_presplit(const float *ah, const float *al, const float *bh, const float *bl, float *c, int64_t M,
                      int64_t K, int64_t N, int trans_a, int trans_b, const float *bias, const float *mask,
                      float *act, int64_t batch, int a_batched, int b_batched, cudaStream_t s,
-                     uint32_t *out_max) {
+                     uint32_t *out_lines) {
     return gemm_presplit_ws(ah, al, bh, bl, c, M, K, N, trans_a, trans_b, bias, mask, act, batch, a_batched,
-                            b_batched, nullptr, s, out_max);
+                            b_batched, nullptr, s, out_lines);
 }
 
 int tc_gemm_f32(const float *a, const float *b, float *c, int64_t M, int64_t K, int64_t N,
@@ -1250,13 +1570,19 @@ int tc_gemm_f32(const float *a, const float *b, float *c, int64_t M, int64_t K, 
     // the tail-split scratch follows the largest layout of both splits
     void *tail_ws = w + 2 * std::max(split_buf(M, K), split_buf(K, M)) + 2 * std::max(split_buf(K, N), split_buf(N, K));
     int rc;
-    if ((rc = tc::split(a, ar, ac, ah, al, s))) return rc;
+    // A read K-major (trans_a = 0) takes row lines, MN-major column lines
+    if ((rc = trans_a ? tc::split_any(a, ar, ac, nullptr, nullptr, ah, al, nullptr, nullptr, nullptr, s)
+                      : tc::split_any(a, ar, ac, ah, al, nullptr, nullptr, nullptr, nullptr, nullptr, s)))
+        return rc;
     if (b_transposed) {
         // both stored K-leading: B goes in as the split of B^T (K-major)
-        if ((rc = tc::split_t(b, br, bc, bh, bl, s))) return rc;
+        if ((rc = tc::split_any(b, br, bc, nullptr, nullptr, nullptr, nullptr, bh, bl, nullptr, s))) return rc;
         return gemm_presplit_ws(ah, al, bh, bl, c, M, K, N, trans_a, 1, nullptr, nullptr, nullptr, 1, 0, 0, tail_ws, s);
     }
-    if ((rc = tc::split(b, br, bc, bh, bl, s))) return rc;
+    // B read MN-major (trans_b = 0) takes column lines, K-major row lines
+    if ((rc = trans_b ? tc::split_any(b, br, bc, bh, bl, nullptr, nullptr, nullptr, nullptr, nullptr, s)
+                      : tc::split_any(b, br, bc, nullptr, nullptr, bh, bl, nullptr, nullptr, nullptr, s)))
+        return rc;
     return gemm_presplit_ws(ah, al, bh, bl, c, M, K, N, trans_a, trans_b, nullptr, nullptr, nullptr, 1, 0, 0, tail_ws,
                             s);
 }

@@ -197,6 +197,38 @@ def _needs_grad(jaxpr: Jaxpr) -> set:
 FUSION = os.environ.get("J4C_FUSION", "1") != "0"
 
 
+def _dot_split_kinds(jaxpr: Jaxpr, eq) -> tuple:
+    """The operand splits a DOT equation's forward and, for the cotangents the
+    backward will compute, its VJP read (Grad.java:385-390), as split kinds of
+    core._split_of: the forward reads A with row lines and B with column
+    lines; dA = g . B^T reads B with row lines; dB = A^T . g reads A with
+    column lines, or transposed when A is the smaller operand."""
+    need = _needs_grad(jaxpr)
+    a, b = eq.inputs
+    ka, kb = ["r"], ["c"]
+    if b.id in need:
+        ka.append("t" if a.shape.size() < eq.outputs[0].shape.size() else "c")
+    if a.id in need:
+        kb.append("r")
+    return ka, kb
+
+
+def _presplit_dot(jaxpr: Jaxpr, eq, values) -> None:
+    """Makes every split a DOT's operands will take, each operand's in one
+    pass over it, before the forward product (the backward then finds them)."""
+    from .core import _make_splits
+    a, b = values.get(eq.inputs[0].id), values.get(eq.inputs[1].id)
+    if not (isinstance(a, ConcreteNDArray) and isinstance(b, ConcreteNDArray)):
+        return
+    if a.dtype() != DType.FLOAT32 or b.dtype() != DType.FLOAT32 or a.shape().rank() != 2 or b.shape().rank() != 2:
+        return
+    if not (a.shape().size() and b.shape().size()):
+        return
+    ka, kb = _dot_split_kinds(jaxpr, eq)
+    _make_splits(a, ka)
+    _make_splits(b, kb)
+
+
 def _evaluate(jaxpr: Jaxpr, args: List[NDArray], keep_for_vjp: bool) -> Dict[int, NDArray]:
     values: Dict[int, NDArray] = dict(jaxpr.consts)
     if len(args) != len(jaxpr.inVars):
@@ -207,13 +239,19 @@ def _evaluate(jaxpr: Jaxpr, args: List[NDArray], keep_for_vjp: bool) -> Dict[int
         from . import fusion
         for kind, item in fusion.plan_for(jaxpr, keep_for_vjp).steps:
             if kind == "eq":
+                if keep_for_vjp and item.primitive == Primitive.DOT:
+                    _presplit_dot(jaxpr, item, values)
                 _run_equation(item, values)
             elif kind == "dot_ep":
+                if keep_for_vjp:
+                    _presplit_dot(jaxpr, item.dot, values)
                 fusion.run_dot_epilogue(item, values)
             else:
                 fusion.run_group(item, values)
         return values
     for eq in jaxpr.equations:
+        if keep_for_vjp and eq.primitive == Primitive.DOT:
+            _presplit_dot(jaxpr, eq, values)
         _run_equation(eq, values)
     return values
 
@@ -431,14 +469,14 @@ def _merge(grads: Dict[int, NDArray], vid: int, g: NDArray) -> None:
 
 
 def _split_g_both(g, a, want_a: bool, want_b: bool) -> None:
-    """A DOT VJP reads its output gradient g in the stored layout (g . B^T)
-    and, when A is at least as large as g, transposed (A^T . g takes the
-    smaller operand's transposed split): then both splits of g are made in
-    one pass."""
-    from .core import _tf32_split_both
+    """A DOT VJP reads its output gradient g with row lines (g . B^T) and,
+    for A^T . g, transposed when A is at least as large as g (the smaller
+    operand goes in transposed) or else with column lines: both splits of g
+    are made in one pass."""
+    from .core import _make_splits
     if (want_a and want_b and isinstance(g, ConcreteNDArray) and isinstance(a, ConcreteNDArray)
-            and a.shape().size() >= g.shape().size()):
-        _tf32_split_both(g)
+            and g.dtype() == DType.FLOAT32 and g.shape().rank() == 2 and g.shape().size()):
+        _make_splits(g, ["r", "t" if a.shape().size() >= g.shape().size() else "c"])
 
 
 def _relu_fed_dots(jaxpr: Jaxpr, need) -> Dict[int, object]:

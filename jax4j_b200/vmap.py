@@ -96,12 +96,12 @@ def _strided_batched_dot(a, a_batched, b, b_batched, batch, M, K, N) -> Concrete
     """One launch of the strided-batched tcgen05 GEMM (j4c_dot_split_batched):
     each operand is split once as its [entries * rows, cols] storage."""
     import torch
-    from .core import _tf32_split
+    from .core import _split_of
     dev = a._check_devices(b)
     a2 = a.reshape(Shape(batch * M, K)) if a_batched else a
     b2 = b.reshape(Shape(batch * K, N)) if b_batched else b
-    ah, al = _tf32_split(a2)
-    bh, bl = _tf32_split(b2)
+    ah, al = _split_of(a2, "r")  # read K-major: one line per row (per entry)
+    bh, bl = _split_of(b2, "c")  # read MN-major: one line per column, shared by the entries
     out = torch.empty(batch * M * N, dtype=torch.float32, device=a.tensor().device)
     call("j4c_dot_split_batched", ah.data_ptr(), al.data_ptr(), bh.data_ptr(), bl.data_ptr(), out.data_ptr(),
          batch, M, K, N, 0, 0, int(a_batched), int(b_batched), a._stream())

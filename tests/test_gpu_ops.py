@@ -280,65 +280,82 @@ def test_empty_and_single_element(J):
     assert e.exp().shape() == J.Shape(0, 3)
 
 
-def _split_parts(hi, lo, rows, cols):
-    """Decode split arrays of an operand [rows, cols] in the library's format:
-    (hi, lo) as float64 [rows, cols] in x's units, their padding columns, and
-    the quantum below which an element's split is exact to an absolute error
-    (3xFP16: the FP16 subnormal step in x's units; 3xTF32: 0)."""
-    from jax4j_b200.core import split_kind
-    if split_kind() == 1:
-        p = (cols + 7) // 8 * 8
-        hb = hi.cpu().numpy().view(np.uint8)
-        lb = lo.cpu().numpy().view(np.uint8)
-        h = hb[:rows * p * 2].view(np.float16).reshape(rows, p).astype(np.float64)
-        l = lb[:rows * p * 2].view(np.float16).reshape(rows, p).astype(np.float64)
-        mx = float(hb[rows * p * 2:rows * p * 2 + 4].view(np.float32)[0])
-        e = 0 if mx == 0 else int(np.clip(14 - (np.frexp(np.float32(mx))[1] - 1), -100, 100))
-        return h[:, :cols] * 2.0 ** -e, l[:, :cols] * 2.0 ** -e, (h[:, cols:], l[:, cols:]), 2.0 ** (-24 - e), mx
-    p = (cols + 3) // 4 * 4
-    h = hi.cpu().numpy()[:rows * p].reshape(rows, p)
-    l = lo.cpu().numpy()[:rows * p].reshape(rows, p)
-    assert np.all(h[:, :cols].view(np.uint32) & 0x1FFF == 0) and np.all(l[:, :cols].view(np.uint32) & 0x1FFF == 0)
-    return h[:, :cols].astype(np.float64), l[:, :cols].astype(np.float64), (h[:, cols:], l[:, cols:]), 0.0, None
-
-
-def _split_written_bytes(rows, cols):
-    """Bytes of a hi array that a split writes (the max word included) and of a lo array."""
-    from jax4j_b200.core import split_kind
-    if split_kind() == 1:
-        n = rows * ((cols + 7) // 8 * 8) * 2
-        return n + 4, n
-    n = rows * ((cols + 3) // 4 * 4) * 4
-    return n, n
-
-
-@pytest.mark.parametrize("rows,cols", [(1, 1), (3, 5), (37, 53), (64, 1000), (129, 4097)])
-def test_split_f32_layout(J, rows, cols):
-    """j4c_split_f32 in the library's format (3xFP16: hi = fp16(x 2^e), lo =
-    fp16(x 2^e - hi), the max word after hi; 3xTF32: hi = tf32(x), lo =
-    tf32(x - hi)): hi + lo = x to 2^-21 relative (plus the FP16 subnormal
-    step for elements far below the array's max), padding zero."""
+def _split_alloc(J, x_dev, rd, cd, fill):
+    """hi and lo arrays for a split whose data is [rd, cd], pre-filled."""
     import torch
+    n = _lib.lib().j4c_split_floats(rd, cd)
+    return [torch.full((n,), fill, dtype=torch.float32, device=x_dev) for _ in range(2)]
+
+
+def _split_parts(hi, lo, rd, cd, axis):
+    """Decode split arrays whose data is [rd, cd] in the library's format:
+    (hi, lo) as float64 [rd, cd] in x's units, their padding columns, the
+    per-element quantum below which an element's split is exact to an
+    absolute error (3xFP16: the FP16 subnormal step of its line in x's
+    units; 3xTF32: 0), and the line words (3xFP16; `axis` "rows" or "cols")."""
+    from jax4j_b200.core import split_kind
+    hb = hi.cpu().numpy().view(np.uint8)
+    lb = lo.cpu().numpy().view(np.uint8)
+    f16 = split_kind() == 1
+    p = (cd + 7) // 8 * 8 if f16 else (cd + 3) // 4 * 4
+    nb = rd * p * (2 if f16 else 4)
+    n_lines = rd if axis == "rows" else cd
+    words = hb[nb + 32:nb + 32 + 4 * n_lines].view(np.uint32)
+    mx = words.view(np.float32).astype(np.float64)
+    e = np.where(words == 0, 0, np.minimum(14 - (np.frexp(mx)[1] - 1), 126))
+    sc = 2.0 ** -e.astype(np.float64)
+    sc = sc[:, None] if axis == "rows" else sc[None, :]
+    if f16:
+        h = hb[:nb].view(np.float16).reshape(rd, p).astype(np.float64)
+        l = lb[:nb].view(np.float16).reshape(rd, p).astype(np.float64)
+        return h[:, :cd] * sc, l[:, :cd] * sc, (h[:, cd:], l[:, cd:]), 2.0 ** -24 * sc, words
+    h = hb[:nb].view(np.float32).reshape(rd, p)
+    l = lb[:nb].view(np.float32).reshape(rd, p)
+    assert np.all(h[:, :cd].view(np.uint32) & 0x1FFF == 0) and np.all(l[:, :cd].view(np.uint32) & 0x1FFF == 0)
+    return (h[:, :cd].astype(np.float64) * sc, l[:, :cd].astype(np.float64) * sc, (h[:, cd:], l[:, cd:]),
+            2.0 ** -149 * sc, words)
+
+
+def _split_written_bytes(rd, cd, n_lines):
+    """Bytes of a hi array that a split writes (data, header, line words) and of a lo array."""
+    from jax4j_b200.core import split_kind
+    n = rd * ((cd + 7) // 8 * 8) * 2 if split_kind() == 1 else rd * ((cd + 3) // 4 * 4) * 4
+    return n + 32 + 4 * n_lines, n
+
+
+def _line_max_bits(x, axis):
+    a = np.abs(np.where(np.isfinite(x), x, 0)).astype(np.float32)
+    return a.max(axis=1 if axis == "rows" else 0).view(np.uint32)
+
+
+@pytest.mark.parametrize("entry,axis", [("j4c_split_f32", "rows"), ("j4c_split_f32_cols", "cols")])
+@pytest.mark.parametrize("rows,cols", [(1, 1), (3, 5), (37, 53), (64, 1000), (129, 4097)])
+def test_split_f32_layout(J, rows, cols, entry, axis):
+    """j4c_split_f32 (a line per row) and j4c_split_f32_cols (a line per
+    column) in the library's format (3xFP16: each line scaled by 2^e with its
+    max |x| 2^e in [2^14, 2^15), hi = fp16(x 2^e), lo = fp16(x 2^e - hi), the
+    line maxima after the header; 3xTF32: hi = tf32(x), lo = tf32(x - hi)):
+    hi + lo = x to 2^-21 relative (plus the FP16 subnormal step of the line
+    for elements far below its max), padding zero.  The values span 2^+-29
+    around 1, so lines differ in magnitude by many powers of two."""
     r = rng(rows * 31 + cols)
     x = (r.standard_normal((rows, cols)) * np.exp(r.uniform(-20, 20, (rows, cols)))).astype(np.float32)
     a = dev(J, x)
-    pitch = _lib.lib().j4c_split_pitch(cols)
-    hi = torch.full((max(rows * pitch, 4),), 7.0, dtype=torch.float32, device=a.tensor().device)
-    lo = torch.full((max(rows * pitch, 4),), 7.0, dtype=torch.float32, device=a.tensor().device)
-    _lib.call("j4c_split_f32", a.data_ptr(), rows, cols, hi.data_ptr(), lo.data_ptr(), a._stream())
-    h, l, pads, quantum, mx = _split_parts(hi, lo, rows, cols)
+    hi, lo = _split_alloc(J, a.tensor().device, rows, cols, 7.0)
+    _lib.call(entry, a.data_ptr(), rows, cols, hi.data_ptr(), lo.data_ptr(), a._stream())
+    h, l, pads, quantum, words = _split_parts(hi, lo, rows, cols, axis)
     assert all(np.all(pd == 0) for pd in pads)
-    if mx is not None:
-        assert mx == np.abs(x).max()
+    np.testing.assert_array_equal(words, _line_max_bits(x, axis))
     err = np.abs(h + l - x)
     assert np.all(err <= np.abs(x) * 2.0 ** -21 + quantum)
 
 
 @pytest.mark.parametrize("ta,tb", [(0, 0), (1, 0), (0, 1), (1, 1)])
 def test_dot_ws_and_split_reuse(J, ta, tb):
-    """j4c_dot_ws (split inside) and j4c_dot_split reusing one split of A
-    for two products with different layouts of A."""
+    """j4c_dot_ws (splits inside) and j4c_dot_split reusing the split of A
+    that its layout takes in a second product with another operand."""
     import torch
+    from jax4j_b200.core import _split_of
     M, K, N = 200, 300, 150
     r = rng(ta * 2 + tb + 5)
     A = r.uniform(-1, 1, (M, K)).astype(np.float32)
@@ -352,40 +369,60 @@ def test_dot_ws_and_split_reuse(J, ta, tb):
               ws_bytes, a._stream())
     ref = orc.dot(A, B, threads=8)
     assert_rel(out.cpu().numpy().reshape(M, N), ref, TOL_REDUCTION, "dot_ws")
-    # the split of `a` used again, now as the transposed operand of a second product
-    from jax4j_b200.core import _tf32_split
-    ah, al = _tf32_split(a)
-    C2 = r.uniform(-1, 1, (M, 70)).astype(np.float32) if not ta else r.uniform(-1, 1, (K, 70)).astype(np.float32)
-    c2 = dev(J, C2)
-    ch, cl = _tf32_split(c2)
-    out2 = torch.empty(K * 70 if not ta else M * 70, dtype=torch.float32, device=a.tensor().device)
-    if not ta:   # a stored [M, K]: a^T . c2 = [K, M] . [M, 70]
+    # op(A) . C2 twice with A's one split of the kind its layout needs
+    ah, al = _split_of(a, "c" if ta else "r")
+    for n2 in (70, 33):
+        C2 = r.uniform(-1, 1, (K, n2)).astype(np.float32)
+        c2 = dev(J, C2)
+        ch, cl = _split_of(c2, "c")
+        out2 = torch.empty(M * n2, dtype=torch.float32, device=a.tensor().device)
         _lib.call("j4c_dot_split", ah.data_ptr(), al.data_ptr(), ch.data_ptr(), cl.data_ptr(), out2.data_ptr(),
-                  K, M, 70, 1, 0, a._stream())
-        ref2 = orc.dot(np.ascontiguousarray(A.T), C2, threads=8)
-    else:        # a stored [K, M]: a^T . c2 = [M, K] . [K, 70]
-        _lib.call("j4c_dot_split", ah.data_ptr(), al.data_ptr(), ch.data_ptr(), cl.data_ptr(), out2.data_ptr(),
-                  M, K, 70, 1, 0, a._stream())
-        ref2 = orc.dot(A, C2, threads=8)
-    assert_rel(out2.cpu().numpy().reshape(ref2.shape), ref2, TOL_REDUCTION, "split reuse")
+                  M, K, n2, ta, 0, a._stream())
+        assert_rel(out2.cpu().numpy().reshape(M, n2), orc.dot(A, C2, threads=8), TOL_REDUCTION, "split reuse")
+
+
+def test_dot_rejects_a_split_of_the_wrong_kind(J):
+    """A K-major operand needs a split with row lines and an MN-major one
+    column lines; a GEMM given the other kind computes nothing and records
+    device status 0x7C06, and the library keeps working afterwards."""
+    import ctypes as C
+    import torch
+    from jax4j_b200.core import _split_of
+    M, K, N = 64, 96, 80
+    r = rng(99)
+    A = r.uniform(-1, 1, (M, K)).astype(np.float32)
+    B = r.uniform(-1, 1, (K, N)).astype(np.float32)
+    a, b = dev(J, A), dev(J, B)
+    out = torch.full((M * N,), 5.0, dtype=torch.float32, device=a.tensor().device)
+    (ah, al), (bh, bl) = _split_of(a, "c"), _split_of(b, "c")  # A wants row lines here
+    _lib.call("j4c_dot_split", ah.data_ptr(), al.data_ptr(), bh.data_ptr(), bl.data_ptr(), out.data_ptr(),
+              M, K, N, 0, 0, a._stream())
+    torch.cuda.synchronize()
+    code = C.c_int(0)
+    assert _lib.lib().j4c_device_status(C.byref(code)) == 0
+    assert code.value == 0x7C06
+    assert torch.all(out == 5.0)  # nothing written
+    ah, al = _split_of(a, "r")
+    _lib.call("j4c_dot_split", ah.data_ptr(), al.data_ptr(), bh.data_ptr(), bl.data_ptr(), out.data_ptr(),
+              M, K, N, 0, 0, a._stream())
+    assert_rel(out.cpu().numpy().reshape(M, N), orc.dot(A, B), TOL_REDUCTION, "after the rejected call")
+    assert _lib.lib().j4c_device_status(C.byref(code)) == 0 and code.value == 0
 
 
 @pytest.mark.parametrize("rows,cols", [(1, 1), (3, 5), (37, 53), (64, 1000), (130, 67)])
 def test_split_f32_transposed_layout(J, rows, cols):
-    """j4c_split_f32_transposed: the split of x^T as [cols, pitch(rows)], padding zero."""
-    import torch
+    """j4c_split_f32_transposed: the split of x^T as [cols, pitch(rows)],
+    padding zero, a line per data row (x's columns)."""
     r = rng(rows * 17 + cols)
-    x = r.standard_normal((rows, cols)).astype(np.float32)
+    x = (r.standard_normal((rows, cols)) * np.exp(r.uniform(-10, 10, (1, cols)))).astype(np.float32)
     a = dev(J, x)
-    pitch = _lib.lib().j4c_split_pitch(rows)
-    hi = torch.full((max(cols * pitch, 4),), 7.0, dtype=torch.float32, device=a.tensor().device)
-    lo = torch.full((max(cols * pitch, 4),), 7.0, dtype=torch.float32, device=a.tensor().device)
+    hi, lo = _split_alloc(J, a.tensor().device, cols, rows, 7.0)
     _lib.call("j4c_split_f32_transposed", a.data_ptr(), rows, cols, hi.data_ptr(), lo.data_ptr(), a._stream())
-    h, l, pads, quantum, _ = _split_parts(hi, lo, cols, rows)
+    h, l, pads, quantum, words = _split_parts(hi, lo, cols, rows, "rows")
     assert all(np.all(pd == 0) for pd in pads)
+    np.testing.assert_array_equal(words, _line_max_bits(x, "cols"))
     err = np.abs(h + l - x.T)
     assert np.all(err <= np.abs(x.T) * 2.0 ** -21 + quantum)
-
 
 
 @pytest.mark.parametrize("ta,tb", [(0, 0), (1, 0), (0, 1), (1, 1)])
@@ -536,81 +573,188 @@ def test_dot_tail_split_shapes(J, ta, tb, M, K, N):
 @pytest.mark.parametrize("rows,cols", [(1, 1), (3, 5), (64, 64), (130, 257), (8192, 1000), (1000, 4096)])
 def test_split_f32_both_equals_the_two_passes(J, rows, cols):
     """j4c_split_f32_both writes exactly what j4c_split_f32 and
-    j4c_split_f32_transposed write, padding included."""
-    import torch
+    j4c_split_f32_transposed write (data, padding, header, line words), and
+    j4c_split_f32_ex with row and column lines exactly what j4c_split_f32
+    and j4c_split_f32_cols write."""
     r = rng(rows * 5 + cols)
     a = dev(J, r.standard_normal((rows, cols)).astype(np.float32))
-    pc, pr = _lib.lib().j4c_split_pitch(cols), _lib.lib().j4c_split_pitch(rows)
     d = a.tensor().device
-    out = [torch.full((n,), 7.0, dtype=torch.float32, device=d) for n in (rows * pc, rows * pc, cols * pr, cols * pr)]
-    ref = [torch.full((n,), 9.0, dtype=torch.float32, device=d) for n in (rows * pc, rows * pc, cols * pr, cols * pr)]
+    out = _split_alloc(J, d, rows, cols, 7.0) + _split_alloc(J, d, cols, rows, 7.0)
+    ref = _split_alloc(J, d, rows, cols, 9.0) + _split_alloc(J, d, cols, rows, 9.0)
     _lib.call("j4c_split_f32_both", a.data_ptr(), rows, cols, *[t.data_ptr() for t in out], a._stream())
     _lib.call("j4c_split_f32", a.data_ptr(), rows, cols, ref[0].data_ptr(), ref[1].data_ptr(), a._stream())
     _lib.call("j4c_split_f32_transposed", a.data_ptr(), rows, cols, ref[2].data_ptr(), ref[3].data_ptr(),
               a._stream())
-    (hb, lb), (hbt, lbt) = _split_written_bytes(rows, cols), _split_written_bytes(cols, rows)
+    (hb, lb), (hbt, lbt) = _split_written_bytes(rows, cols, rows), _split_written_bytes(cols, rows, cols)
     for o, e, nb in zip(out, ref, (hb, lb, hbt, lbt)):
-        assert torch.equal(o.view(torch.uint8)[:nb], e.view(torch.uint8)[:nb])
+        assert torch_equal_bytes(o, e, nb)
+    rc = _split_alloc(J, d, rows, cols, 7.0) + _split_alloc(J, d, rows, cols, 7.0)
+    _lib.call("j4c_split_f32_ex", a.data_ptr(), rows, cols, *[t.data_ptr() for t in rc], None, None, None,
+              a._stream())
+    cref = _split_alloc(J, d, rows, cols, 9.0)
+    _lib.call("j4c_split_f32_cols", a.data_ptr(), rows, cols, cref[0].data_ptr(), cref[1].data_ptr(), a._stream())
+    hbc, lbc = _split_written_bytes(rows, cols, cols)
+    for o, e, nb in zip(rc, ref[:2] + cref, (hb, lb, hbc, lbc)):
+        assert torch_equal_bytes(o, e, nb)
+
+
+def torch_equal_bytes(a, b, nbytes):
+    import torch
+    return torch.equal(a.view(torch.uint8)[:nbytes], b.view(torch.uint8)[:nbytes])
 
 
 @pytest.mark.parametrize("ta,tb,act,masked", [(0, 0, True, False), (1, 0, True, False), (0, 1, False, True),
                                               (0, 0, False, True), (1, 1, True, False)])
-def test_epilogue_max_word_and_split_from_it(J, ta, tb, act, masked):
-    """Under 3xFP16 an epilogue GEMM leaves the max finite |value| of the output
-    a later split reads (the relu output, or the masked C) in a device word;
-    the split that takes the word is byte-identical to one that scans the
-    output itself, in both layouts and in one pass."""
-    import torch
-    from jax4j_b200.core import _dot_raw, split_kind
-    if split_kind() != 1:
-        pytest.skip("the max word belongs to the 3xFP16 split")
+def test_epilogue_line_maxima_and_split_from_them(J, ta, tb, act, masked):
+    """An epilogue GEMM leaves the line maxima (rows, then columns) of the
+    output a later split reads (the relu output, or the masked C); the splits
+    that take them are byte-identical to ones that scan the output
+    themselves, for every kind and in one pass."""
+    from jax4j_b200.core import _dot_raw
     r = rng(ta * 8 + tb * 4 + act * 2 + masked)
-    M, K, N = 333, 257, 1030  # ragged edges, several tiles, the transposed store for (0, 1)
+    M, K, N = 333, 257, 1030  # ragged edges, several tiles, the transposed store for (0, 0)
     A = (r.standard_normal((M, K)) * 3).astype(np.float32)
+    A[5] *= np.float32(2.0 ** -40)  # a row far below the others
     B = r.standard_normal((K, N)).astype(np.float32)
     a = dev(J, A.T.copy() if ta else A)
     b = dev(J, B.T.copy() if tb else B)
-    bias = dev(J, r.standard_normal(N).astype(np.float32)) if act else None
+    bias = dev(J, r.standard_normal(N).astype(np.float32) * 1e-12) if act else None
     mask = dev(J, r.standard_normal((M, N)).astype(np.float32)) if masked else None
     res = _dot_raw(a, b, bool(ta), bool(tb), a.device(), bias=bias, mask=mask, act=act)
     out = res[1] if act else res
-    assert out._absmax is not None
-    got = int(out._absmax.cpu().numpy()[0]) & 0xFFFFFFFF
-    want = int(np.abs(out.numpy()).max().view(np.uint32))
-    assert got == want, (hex(got), hex(want))
-    rows, cols = M, N
-    pc, pr = _lib.lib().j4c_split_pitch(cols), _lib.lib().j4c_split_pitch(rows)
+    assert out._lines is not None
+    got = out._lines.cpu().numpy().view(np.uint32)
+    o = out.numpy()
+    np.testing.assert_array_equal(got[:M], _line_max_bits(o, "rows"))
+    np.testing.assert_array_equal(got[M:], _line_max_bits(o, "cols"))
     d = out.tensor().device
-    given = [torch.full((n,), 7.0, dtype=torch.float32, device=d) for n in (rows * pc, rows * pc, cols * pr, cols * pr)]
-    scan = [torch.full((n,), 9.0, dtype=torch.float32, device=d) for n in (rows * pc, rows * pc, cols * pr, cols * pr)]
-    _lib.call("j4c_split_f32_ex", out.data_ptr(), rows, cols, *[t.data_ptr() for t in given],
-              out._absmax.data_ptr(), out._stream())
-    _lib.call("j4c_split_f32_ex", out.data_ptr(), rows, cols, *[t.data_ptr() for t in scan], None, out._stream())
-    (hb, lb), (hbt, lbt) = _split_written_bytes(rows, cols), _split_written_bytes(cols, rows)
-    for o, e, nb in zip(given, scan, (hb, lb, hbt, lbt)):
-        assert torch.equal(o.view(torch.uint8)[:nb], e.view(torch.uint8)[:nb])
+    for pair in (("r", "t"), ("r", "c"), ("c",)):
+        given, scan = [], []
+        for k in ("r", "c", "t"):
+            if k in pair:
+                rd, cd = (N, M) if k == "t" else (M, N)
+                given += _split_alloc(J, d, rd, cd, 7.0)
+                scan += _split_alloc(J, d, rd, cd, 9.0)
+            else:
+                given += [None, None]
+                scan += [None, None]
+        ptr = lambda t: t.data_ptr() if t is not None else None  # noqa: E731
+        _lib.call("j4c_split_f32_ex", out.data_ptr(), M, N, *[ptr(t) for t in given], out._lines.data_ptr(),
+                  out._stream())
+        _lib.call("j4c_split_f32_ex", out.data_ptr(), M, N, *[ptr(t) for t in scan], None, out._stream())
+        for i, k in enumerate(("r", "c", "t")):
+            if k in pair:
+                rd, cd, nl = (N, M, N) if k == "t" else (M, N, M if k == "r" else N)
+                hb, lb = _split_written_bytes(rd, cd, nl)
+                assert torch_equal_bytes(given[2 * i], scan[2 * i], hb), (pair, k)
+                assert torch_equal_bytes(given[2 * i + 1], scan[2 * i + 1], lb), (pair, k)
+
+
+def _rel_err_vs_fp64(got, A, B):
+    """Per-element error of a product against an FP64 one, relative to
+    sum_k |a_ik b_kj| (the scale of a dot's own rounding), and numpy's FP32
+    product's error measured the same way."""
+    exact = A.astype(np.float64) @ B.astype(np.float64)
+    scale = np.abs(A).astype(np.float64) @ np.abs(B).astype(np.float64)
+    scale = np.where(scale == 0, 1.0, scale)
+    fp32 = np.abs((A @ B).astype(np.float64) - exact) / scale
+    return np.abs(got.astype(np.float64) - exact) / scale, fp32
 
 
 @pytest.mark.parametrize("K", [256, 4096])
 def test_dot_accuracy_against_fp64(J, K):
-    """The split GEMM's error per element, relative to sum_k |a_ik b_kj| (the
-    scale of a dot's own rounding), against an FP64 product: within a few
-    times numpy's FP32 product on N(0, 1) rows, and rows 2^-20 below the
-    tensor's max (3xFP16's per-tensor scale) within 1e-5.  Measured on a
-    B200 with 3xFP16: 5.7e-7 / 1.1e-7 (K = 256 / 4096) against numpy's
-    2.9e-7 / 5.4e-8, and 2.0e-6 / 4.6e-7 on the scaled-down rows."""
+    """The split GEMM's error per element, relative to sum_k |a_ik b_kj|,
+    against an FP64 product: within a few times numpy's FP32 product on
+    N(0, 1) rows and on rows 2^-20 and 2^-30 below the tensor's max (each
+    line of a 3xFP16 operand carries its own scale), in every operand layout."""
     from jax4j_b200.core import _dot_raw
     r = rng(K)
     M, N = 256, 384
     A = r.standard_normal((M, K)).astype(np.float32)
-    A[::7] *= np.float32(2.0 ** -20)  # every 7th row far below the tensor's max
+    A[::7] *= np.float32(2.0 ** -20)   # rows far below the tensor's max
+    A[3::11] *= np.float32(2.0 ** -30)
     B = r.standard_normal((K, N)).astype(np.float32)
-    a = dev(J, A)
-    got = _dot_raw(a, dev(J, B), False, False, a.device()).numpy().astype(np.float64)
-    exact = A.astype(np.float64) @ B.astype(np.float64)
-    scale = np.abs(A).astype(np.float64) @ np.abs(B).astype(np.float64)
-    err = np.abs(got - exact) / scale
-    fp32 = np.abs((A @ B).astype(np.float64) - exact) / scale
-    normal = np.delete(err, np.s_[::7], axis=0)
-    assert normal.max() <= max(4 * fp32.max(), 1e-6), (normal.max(), fp32.max())
-    assert err[::7].max() <= 1e-5, err[::7].max()
+    B[:, ::5] *= np.float32(2.0 ** -25)  # columns far below the max
+    for ta, tb in ((0, 0), (1, 0), (0, 1), (1, 1)):
+        a, b = dev(J, A.T.copy() if ta else A), dev(J, B.T.copy() if tb else B)
+        got = _dot_raw(a, b, bool(ta), bool(tb), a.device()).numpy()
+        err, fp32 = _rel_err_vs_fp64(got, A, B)
+        assert err.max() <= max(4 * fp32.max(), 1e-6), ((ta, tb), err.max(), fp32.max())
+
+
+@pytest.mark.parametrize("a_max,b_max", [(1e-30, 1e30), (1e-20, 1e20), (1e30, 1e-30), (3e38, 3e-39),
+                                         (1e-38, 1e-3), (2e-40, 1e35)])
+def test_dot_extreme_magnitudes(J, a_max, b_max):
+    """Operands whose whole range sits at either end of FP32's exponent range
+    (down to FP32 subnormals, up to 3e38), paired so that the products stay
+    finite and normal: per element within a few times numpy's FP32 error
+    against FP64 (every line is scaled into the split format's range, which
+    also keeps FP32 subnormals exact)."""
+    from jax4j_b200.core import _dot_raw
+    r = rng(int(abs(np.log10(a_max))) + 3)
+    M, K, N = 192, 512, 160
+    A = (r.uniform(-1, 1, (M, K)) * a_max).astype(np.float32)
+    B = (r.uniform(-1, 1, (K, N)) * b_max).astype(np.float32)
+    a, b = dev(J, A), dev(J, B)
+    got = _dot_raw(a, b, False, False, a.device()).numpy()
+    assert np.all(np.isfinite(got))
+    err, fp32 = _rel_err_vs_fp64(got, A, B)
+    assert err.max() <= max(4 * fp32.max(), 2e-6), (err.max(), fp32.max())
+
+
+def _with_specials(r, shape, kinds):
+    x = r.uniform(-1, 1, shape).astype(np.float32)
+    x[r.uniform(size=shape) < 0.05] = 0.0  # exact zeros: 0 * inf = NaN
+    flat = x.reshape(-1)
+    for k in kinds:
+        idx = r.choice(flat.size, size=3, replace=False)
+        flat[idx] = {"inf": np.inf, "-inf": -np.inf, "nan": np.nan}[k]
+    return x
+
+
+@pytest.mark.parametrize("ta,tb", [(0, 0), (1, 0), (0, 1), (1, 1)])
+@pytest.mark.parametrize("where", ["a", "b", "both"])
+def test_dot_special_values_equal_the_reference(J, ta, tb, where):
+    """An operand holding +-Inf or NaN: the product is the reference's
+    sequential FP32 sum (core/ConcreteNDArray.java:452-459) bit for bit --
+    Inf rows and columns, 0 * Inf = NaN, +Inf + -Inf = NaN, NaN spreading --
+    in every layout, as the oracle computes it."""
+    from jax4j_b200.core import _dot_raw
+    r = rng(ta * 4 + tb * 2 + len(where))
+    M, K, N = 150, 200, 170
+    A = _with_specials(r, (M, K), ["inf", "-inf", "nan"] if where in ("a", "both") else [])
+    B = _with_specials(r, (K, N), ["-inf", "inf"] if where in ("b", "both") else [])
+    a, b = dev(J, A.T.copy() if ta else A), dev(J, B.T.copy() if tb else B)
+    got = _dot_raw(a, b, bool(ta), bool(tb), a.device()).numpy()
+    ref = orc.dot(A, B)
+    assert np.any(~np.isfinite(ref))
+    assert np.array_equal(got, ref, equal_nan=True), int(np.sum(~((got == ref) | (np.isnan(got) & np.isnan(ref)))))
+
+
+def test_dot_special_values_through_the_epilogue_and_vmap(J):
+    """The exact path under a bias + relu epilogue (the relu output stored),
+    with its line maxima for the next split, and in the strided-batched
+    GEMM of vmap."""
+    from jax4j_b200.core import _dot_raw
+    r = rng(1234)
+    M, K, N = 130, 96, 140
+    A = _with_specials(r, (M, K), ["inf", "nan"])
+    B = r.uniform(-1, 1, (K, N)).astype(np.float32)
+    bias = r.uniform(-1, 1, N).astype(np.float32)
+    a, b, bi = dev(J, A), dev(J, B), dev(J, bias)
+    _, h = _dot_raw(a, b, False, False, a.device(), bias=bi, act=True, store_c=False)
+    z = (orc.dot(A, B) + bias).astype(np.float32)
+    want = np.where(np.isnan(z), z, np.maximum(z, np.float32(0)))
+    assert np.array_equal(h.numpy(), want, equal_nan=True)
+    lines = h._lines.cpu().numpy().view(np.uint32) if h._lines is not None else None
+    if lines is not None:
+        np.testing.assert_array_equal(lines[:M], _line_max_bits(want, "rows"))
+        np.testing.assert_array_equal(lines[M:], _line_max_bits(want, "cols"))
+    # vmap's strided-batched dot: [3, M, K] . [3, K, N] with a special in one entry
+    A3 = np.stack([r.uniform(-1, 1, (M, K)).astype(np.float32) for _ in range(3)])
+    B3 = np.stack([r.uniform(-1, 1, (K, N)).astype(np.float32) for _ in range(3)])
+    A3[1, 7, 9] = np.inf
+    B3[2, 4, 11] = np.nan
+    got = J.JAX.vmap(lambda x, w: x.dot(w), in_axes=[0, 0])(dev(J, A3), dev(J, B3)).numpy()
+    for i in range(3):
+        assert np.array_equal(got[i], orc.dot(A3[i], B3[i]), equal_nan=True), i

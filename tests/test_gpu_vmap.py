@@ -140,9 +140,8 @@ def test_strided_batched_gemm_one_launch(J, a_b, b_b, B, M, K, N):
     n0 = _lib.kernel_launches()
     out = f(J.ConcreteNDArray.of(A), J.ConcreteNDArray.of(W))
     launched = _lib.kernel_launches() - n0
-    from jax4j_b200.core import split_kind
-    # two operand splits (each an abs-max pass and the split under 3xFP16) and one GEMM
-    assert launched <= (5 if split_kind() == 1 else 3), launched
+    # two operand splits (each a line-max pass and the split) and one GEMM
+    assert launched <= 5, launched
     o = out.numpy()
     for i in range(B):
         assert_rel(o[i], orc.dot(A[i] if a_b else A, W[i] if b_b else W), TOL_REDUCTION, f"example {i}")
