@@ -123,6 +123,15 @@ J4C_API int j4c_stream_destroy(j4c_stream stream);
 /* Reads and clears the library's device status word on the current device:
  * non-zero after a kernel gave up a bounded wait or rejected its input. */
 J4C_API int j4c_device_status(int *out_code);
+/* No counterpart in the reference (its collectives and kernels wait without
+ * limit).  Sets, for kernels launched afterwards in this process, how long
+ * a pipeline wait of the persistent GEMM may see no progress before the
+ * kernel gives up: it records device status 0x7C05, stops its pipeline,
+ * waits (always up to 2 s) for its own copies and tensor-core work in flight,
+ * releases its tensor memory and returns, leaving C unspecified.  ns > 0;
+ * the previous limit goes to *previous (may be NULL).  Default 2 s; below
+ * 1 ms the waits poll without suspending (a limit for testing this path). */
+J4C_API int j4c_set_wait_limit_ns(uint64_t ns, uint64_t *previous);
 
 /* ------------------------------------------------------------------ */
 /* Storage: replaces ConcreteNDArray's host Storage records             */
@@ -344,14 +353,15 @@ J4C_API int j4c_split_f32_both(const float *x, int64_t rows, int64_t cols, float
 /* Any of the splits above in one pass -- hi/lo (row lines), hi_c/lo_c
  * (column lines) or hi_t/lo_t (transposed), each pair optional, hi_c and
  * hi_t not both -- with x's line maxima computed already: lines (device, may
- * be NULL) holds rows + cols words, the bits of the largest finite |x| of
- * each row and then of each column, as j4c_split_lines or
- * j4c_dot_split_ep_max's out_lines leave them; it replaces the split's own
- * max pass. */
+ * be NULL) holds rows + cols + 1 words, the bits of the largest finite |x| of
+ * each row and then of each column, then a word nonzero when x holds a NaN
+ * or an infinity, as j4c_split_lines or j4c_dot_split_ep_max's out_lines
+ * leave them; it replaces the split's own max pass. */
 J4C_API int j4c_split_f32_ex(const float *x, int64_t rows, int64_t cols, float *hi, float *lo, float *hi_c,
                              float *lo_c, float *hi_t, float *lo_t, const uint32_t *lines, j4c_stream stream);
-/* lines [rows + cols] (device): the line maxima of x (rows, then columns)
- * in one pass, for several later j4c_split_f32_ex calls. */
+/* lines [rows + cols + 1] (device): the line maxima of x (rows, then
+ * columns) and its NaN/Inf flag in one pass, for several later
+ * j4c_split_f32_ex calls. */
 J4C_API int j4c_split_lines(const float *x, int64_t rows, int64_t cols, uint32_t *lines, j4c_stream stream);
 J4C_API int j4c_dot_split(const float *a_hi, const float *a_lo, const float *b_hi, const float *b_lo, float *c,
                           int64_t M, int64_t K, int64_t N, int trans_a, int trans_b, j4c_stream stream);
@@ -378,11 +388,12 @@ J4C_API int j4c_dot_split_batched(const float *a_hi, const float *a_lo, const fl
 J4C_API int j4c_dot_split_ep(const float *a_hi, const float *a_lo, const float *b_hi, const float *b_lo,
                              float *c, int64_t M, int64_t K, int64_t N, int trans_a, int trans_b,
                              const float *bias, const float *mask, float *act, j4c_stream stream);
-/* j4c_dot_split_ep that also leaves in out_lines (M + N device uint32
+/* j4c_dot_split_ep that also leaves in out_lines (M + N + 1 device uint32
  * words) the line maxima of what it writes to act (or to c when act is
  * NULL): the bits of the largest finite |value| of each of the M rows, then
- * of each of the N columns -- what a later j4c_split_f32_ex of that output
- * takes instead of scanning it again. */
+ * of each of the N columns, then a word nonzero when a written value is a
+ * NaN or an infinity -- what a later j4c_split_f32_ex of that output takes
+ * instead of scanning it again. */
 J4C_API int j4c_dot_split_ep_max(const float *a_hi, const float *a_lo, const float *b_hi, const float *b_lo,
                                  float *c, int64_t M, int64_t K, int64_t N, int trans_a, int trans_b,
                                  const float *bias, const float *mask, float *act, uint32_t *out_lines,

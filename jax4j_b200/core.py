@@ -421,7 +421,7 @@ class ConcreteNDArray(NDArray):
         self._device = device
         self._split = None  # {kind: (hi, lo)}: "r" row lines, "c" column lines, "t" transposed
         self._ready = None  # CUDA event recorded once the value was produced, when tracked
-        self._lines = None  # device words [rows + cols]: line maxima (bits of max finite |x|)
+        self._lines = None  # device words [rows + cols + 1]: line maxima (bits of max finite |x|), NaN/Inf flag
 
     # ---- construction helpers ----
     @staticmethod
@@ -776,7 +776,7 @@ def _split_lines(x: "ConcreteNDArray"):
     max pass, kept on the array for every split of it."""
     if x._lines is None:
         rows, cols = x._shape.dimensions()
-        lines = torch.empty(rows + cols, dtype=torch.int32, device=x._t.device)
+        lines = torch.empty(rows + cols + 1, dtype=torch.int32, device=x._t.device)
         call("j4c_split_lines", x._t.data_ptr(), rows, cols, lines.data_ptr(), x._stream())
         x._lines = lines
     return x._lines
@@ -879,7 +879,7 @@ def _dot_raw(a: "ConcreteNDArray", b: "ConcreteNDArray", trans_a: bool, trans_b:
         if epilogue:
             # the epilogue also takes the line maxima of the output a later split
             # will read (the relu output, or C), sparing it a max pass
-            out_max = torch.empty(M + N, dtype=torch.int32, device=a._t.device)
+            out_max = torch.empty(M + N + 1, dtype=torch.int32, device=a._t.device)
             call("j4c_dot_split_ep_max", ah.data_ptr(), al.data_ptr(), bh.data_ptr(), bl.data_ptr(),
                  out.data_ptr() if store_c else None,
                  M, K, N, int(ta), int(tb), bias.data_ptr() if bias is not None else None,

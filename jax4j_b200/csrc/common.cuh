@@ -56,6 +56,11 @@ int scratch_free(void *p, cudaStream_t s);
 // if the word cannot be allocated.
 int *device_status_ptr();
 
+// The limit, in ns without progress, after which a pipeline wait of a
+// persistent kernel gives up and records its status (j4c_set_wait_limit_ns;
+// 2 s unless set).
+uint64_t wait_limit_ns();
+
 inline size_t dtype_size(int dtype) {
     switch (dtype) {
     case J4C_FLOAT32: return 4;

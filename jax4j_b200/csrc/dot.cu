@@ -115,8 +115,7 @@ int j4c_split_f32_ex(const float *x, int64_t rows, int64_t cols, float *hi, floa
 
 int j4c_split_lines(const float *x, int64_t rows, int64_t cols, uint32_t *lines, j4c_stream stream) {
     J4C_REQUIRE(rows >= 0 && cols >= 0, "j4c_split_lines: negative extent");
-    if (rows == 0 || cols == 0) return J4C_OK;
-    J4C_REQUIRE(x && lines, "j4c_split_lines: NULL pointer");
+    J4C_REQUIRE(lines && (x || rows == 0 || cols == 0), "j4c_split_lines: NULL pointer");
     return tc_split_lines(x, rows, cols, lines, as_stream(stream));
 }
 
@@ -126,13 +125,13 @@ int j4c_dot_split_ep_max(const float *a_hi, const float *a_lo, const float *b_hi
     J4C_REQUIRE(M >= 0 && K >= 0 && N >= 0, "j4c_dot_split: negative dimension");
     cudaStream_t s = as_stream(stream);
     if (M == 0 || N == 0) {
-        if (out_lines && M + N) J4C_CUDA(cudaMemsetAsync(out_lines, 0, (size_t)(M + N) * sizeof(uint32_t), s));
+        if (out_lines) J4C_CUDA(cudaMemsetAsync(out_lines, 0, (size_t)(M + N + 1) * sizeof(uint32_t), s));
         return J4C_OK;
     }
     J4C_REQUIRE(c || act, "j4c_dot_split: NULL output");
     J4C_REQUIRE(K > 0 || (!bias && !mask && !act), "j4c_dot_split_ep: K = 0 with an epilogue");
     if (K == 0) {
-        if (out_lines) J4C_CUDA(cudaMemsetAsync(out_lines, 0, (size_t)(M + N) * sizeof(uint32_t), s));
+        if (out_lines) J4C_CUDA(cudaMemsetAsync(out_lines, 0, (size_t)(M + N + 1) * sizeof(uint32_t), s));
         return j4c_fill(J4C_FLOAT32, c, M * N, 0.0, stream);
     }
     J4C_REQUIRE(a_hi && a_lo && b_hi && b_lo, "j4c_dot_split: NULL operand");

@@ -172,17 +172,51 @@ __device__ __forceinline__ bool mbar_try_wait(uint32_t bar, uint32_t parity) {
     return ok != 0;
 }
 
+// Non-blocking probe of the phase with the given parity.
+__device__ __forceinline__ bool mbar_test_wait(uint32_t bar, uint32_t parity) {
+    uint32_t ok;
+    asm volatile(
+        "{\n\t.reg .pred p;\n\t"
+        "mbarrier.test_wait.parity.shared::cta.b64 p, [%1], %2;\n\t"
+        "selp.u32 %0, 1, 0, p;\n\t}"
+        : "=r"(ok)
+        : "r"(bar), "r"(parity)
+        : "memory");
+    return ok != 0;
+}
+
+constexpr uint64_t kShortLimitNs = 1000000ull;  // below this a wait polls without suspending
+
 // Waits for the phase with the given parity; false if the CTA is aborting or
-// no progress was seen for kWaitLimitNs (then records the status and aborts).
+// no progress was seen for limit_ns (then records the status and aborts).
+// The pipeline's waits take the launch's limit (j4c_set_wait_limit_ns); the
+// drains before exit (honour_abort false) always take kWaitLimitNs, so
+// every load and MMA a CTA issued lands before it releases its memory.
 __device__ __forceinline__ bool wait_bar(uint32_t bar, uint32_t parity, volatile int *abort,
-                                         int *status, bool honour_abort = true) {
+                                         int *status, bool honour_abort = true,
+                                         uint64_t limit_ns = kWaitLimitNs) {
+    if (limit_ns < kShortLimitNs) {
+        // A short limit (set for a test of this path): try_wait may suspend
+        // the thread until the phase completes, so probe without suspending
+        // and read the clock at every probe.
+        const uint64_t t0 = now_ns();
+        for (;;) {
+            if (mbar_test_wait(bar, parity)) return true;
+            if (honour_abort && *abort) return false;
+            if (now_ns() - t0 > limit_ns) {
+                *abort = 1;
+                if (status) atomicCAS(status, 0, kStatusTimeout);
+                return false;
+            }
+        }
+    }
     if (mbar_try_wait(bar, parity)) return true;
     const uint64_t t0 = now_ns();
     for (uint32_t it = 1;; ++it) {
         if (mbar_try_wait(bar, parity)) return true;
         if ((it & 63) == 0) {
             if (honour_abort && *abort) return false;
-            if (now_ns() - t0 > kWaitLimitNs) {
+            if (now_ns() - t0 > limit_ns) {
                 *abort = 1;
                 if (status) atomicCAS(status, 0, kStatusTimeout);
                 return false;
@@ -292,18 +326,6 @@ __device__ __forceinline__ float pow2f(int k) {
     return __uint_as_float(k >= -126 ? (uint32_t)(127 + k) << 23 : 1u << (k + 149));
 }
 
-// v 2^k for k in [-252, 226] (the sum of two negated line exponents, each
-// in [-126, 113]) as two multiplies by 2^(k >> 1) and 2^(k - (k >> 1)): both
-// exponents lie in [-126, 113], so both factors are normal floats (two
-// integer operations each), and as they share k's sign the intermediate lies
-// between v and the result -- it overflows only when the result does, and
-// both steps are exact whenever the result is a normal float (a result in the
-// subnormal range is rounded once or twice at its 2^-149 step).
-__device__ __forceinline__ float unscale(float v, int k) {
-    const int k1 = k >> 1;
-    return v * __uint_as_float((uint32_t)(127 + k1) << 23) * __uint_as_float((uint32_t)(127 + k - k1) << 23);
-}
-
 __device__ __forceinline__ void mma_commit(uint32_t bar) {
     asm volatile("tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];" ::"r"(bar)
                  : "memory");
@@ -359,14 +381,16 @@ __device__ __forceinline__ Unit unit_of(int u, int full_tiles, int splits, int n
 // and, with out_lines set (zeroed by the launch), the line words of the
 // stored output: out_lines[r] (r < out_rows) the bits of the largest finite
 // |value| of stored row r, out_lines[out_rows + c] of stored column c, taken
-// over what is written to act (or to C when there is no act) -- the line
-// maxima a later 3xFP16 split of that output takes instead of its own pass.
+// over what is written to act (or to C when there is no act), and *out_flag
+// nonzero when a written value is a NaN or an infinity -- what a later split
+// of that output takes instead of its own max pass.
 struct Epilogue {
     const float *bias;
     const float *mask;
     float *act;
     uint32_t *out_lines;
     int out_rows;
+    uint32_t *out_flag;
 };
 
 // The bits of |v| for finite v, else 0.
@@ -413,12 +437,14 @@ __device__ void exact_tiles(const float *__restrict__ A, bool a_col, const float
             if (C) C[idx] = v;
             if (ep.act) ep.act[idx] = ep_relu(v);
             if (ep.out_lines) {
-                const uint32_t m = finite_bits(ep.act ? ep_relu(v) : v);
+                const float tv = ep.act ? ep_relu(v) : v;
+                const uint32_t m = finite_bits(tv);
                 const int sr = store_t ? j : i, sc = store_t ? i : j;
                 if (m) {
                     atomicMax(ep.out_lines + sr, m);
                     atomicMax(ep.out_lines + ep.out_rows + sc, m);
                 }
+                if ((__float_as_uint(tv) & 0x7F800000u) == 0x7F800000u) atomicOr(ep.out_flag, 1u);
             }
         }
     }
@@ -445,7 +471,7 @@ __global__ void __launch_bounds__(kThreads, 1)
 gemm_3xtf32_kernel(const __grid_constant__ CUtensorMap tAh, const __grid_constant__ CUtensorMap tAl,
                    const __grid_constant__ CUtensorMap tBh, const __grid_constant__ CUtensorMap tBl,
                    float *__restrict__ C, int M, int N, int K, int num_kb, int vec_store, int store_t,
-                   Epilogue ep, int batch, int a_batched, int b_batched, int *status, int full_tiles,
+                   Epilogue ep, int batch, int a_batched, int b_batched, int *status, uint64_t wait_ns, int full_tiles,
                    int splits, float *__restrict__ part, int *__restrict__ arrivals,
                    const SplitHeader *__restrict__ ahdr, const SplitHeader *__restrict__ bhdr) {
     using Q = Cfg<BN, STAGES, BK, F16>;
@@ -521,7 +547,7 @@ gemm_3xtf32_kernel(const __grid_constant__ CUtensorMap tAh, const __grid_constan
                 tile_coords(t - bidx * tiles_per_batch, num_m, num_n, mt, nt);
                 const int za = a_batched ? bidx : 0, zb = b_batched ? bidx : 0;
                 for (int kb = w.kb0; kb < w.kb1; kb++) {
-                    if (!wait_bar(smem_u32(&ctl->empty[stage]), phase ^ 1, abort, status)) {
+                    if (!wait_bar(smem_u32(&ctl->empty[stage]), phase ^ 1, abort, status, true, wait_ns)) {
                         ok = false;
                         break;
                     }
@@ -563,7 +589,7 @@ gemm_3xtf32_kernel(const __grid_constant__ CUtensorMap tAh, const __grid_constan
                 for (int kb0 = w.kb0; ok && kb0 < w.kb1; kb0 += CHUNK_KB, ci++) {
                     const int buf = ci & 1;
                     const uint32_t bph = (ci >> 1) & 1;
-                    if (!wait_bar(smem_u32(&ctl->tempty[buf]), bph ^ 1, abort, status)) {
+                    if (!wait_bar(smem_u32(&ctl->tempty[buf]), bph ^ 1, abort, status, true, wait_ns)) {
                         ok = false;
                         break;
                     }
@@ -571,7 +597,7 @@ gemm_3xtf32_kernel(const __grid_constant__ CUtensorMap tAh, const __grid_constan
                     const uint32_t dcol = tmem + buf * BN;
                     const int kb1 = min(w.kb1, kb0 + CHUNK_KB);
                     for (int kb = kb0; kb < kb1; kb++) {
-                        if (!wait_bar(smem_u32(&ctl->full[stage]), phase, abort, status)) {
+                        if (!wait_bar(smem_u32(&ctl->full[stage]), phase, abort, status, true, wait_ns)) {
                             ok = false;
                             break;
                         }
@@ -633,7 +659,7 @@ gemm_3xtf32_kernel(const __grid_constant__ CUtensorMap tAh, const __grid_constan
             for (int kb0 = w.kb0; kb0 < w.kb1; kb0 += CHUNK_KB, ci++) {
                 const int buf = ci & 1;
                 const uint32_t bph = (ci >> 1) & 1;
-                if (!wait_bar(smem_u32(&ctl->tfull[buf]), bph, abort, status)) {
+                if (!wait_bar(smem_u32(&ctl->tfull[buf]), bph, abort, status, true, wait_ns)) {
                     ok = false;
                     break;
                 }
@@ -695,14 +721,25 @@ gemm_3xtf32_kernel(const __grid_constant__ CUtensorMap tAh, const __grid_constan
             const float bias_t = (store_t && ep.bias && row_ok) ? __ldg(ep.bias + row) : 0.0f;
             {
                 // lane l reads the line word of column g*32 + l; the warp shares it
-                const int nea = -ea;
+                // 2^-(ea + eb) as (2^(nea1) 2^(neb1)) (2^(nea - nea1) 2^(neb - neb1)) with
+                // nea = -ea, neb = -eb (each in [-126, 113]) and x1 = x >> 1: every
+                // factor and both products are normal floats (exponents in [-126, 114]),
+                // the two products differ by at most a factor 4, so the intermediate
+                // lies within a factor 4 of the path from v to the result -- exact
+                // whenever the result is a normal float.
+                const int nea = -ea, nea1 = nea >> 1;
+                const float pa1 = __uint_as_float((uint32_t)(127 + nea1) << 23);
+                const float pa2 = __uint_as_float((uint32_t)(127 + nea - nea1) << 23);
 #pragma unroll
                 for (int g = 0; g < Q::COLS_PER_WARP / 32; g++) {
                     const int mycol = col0 + g * 32 + lane;
-                    const int eb_l = mycol < N ? split_exp(__ldg(bl + mycol)) : 0;
+                    const int neb = mycol < N ? -split_exp(__ldg(bl + mycol)) : 0, neb1 = neb >> 1;
+                    const float pb1 = __uint_as_float((uint32_t)(127 + neb1) << 23);
+                    const float pb2 = __uint_as_float((uint32_t)(127 + neb - neb1) << 23);
 #pragma unroll
                     for (int jj = 0; jj < 32; jj++)
-                        acc[g * 32 + jj] = unscale(acc[g * 32 + jj], nea - __shfl_sync(0xffffffffu, eb_l, jj));
+                        acc[g * 32 + jj] = acc[g * 32 + jj] * (pa1 * __shfl_sync(0xffffffffu, pb1, jj)) *
+                                           (pa2 * __shfl_sync(0xffffffffu, pb2, jj));
                 }
             }
             // Store; afterwards acc[j] holds the bits of the stored |v| (the relu
@@ -730,26 +767,24 @@ gemm_3xtf32_kernel(const __grid_constant__ CUtensorMap tAh, const __grid_constan
                         reinterpret_cast<float4 *>(act_b + base)[v4] = make_float4(x[0], x[1], x[2], x[3]);
                     }
 #pragma unroll
-                    for (int e = 0; e < 4; e++) acc[4 * v4 + e] = __uint_as_float(finite_bits(x[e]));
+                    for (int e = 0; e < 4; e++) acc[4 * v4 + e] = x[e];
                 }
             } else if (store_t) {
-                // C holds the transpose of this product ([N, M]): for each
-                // column the warp's 32 lanes write 32 consecutive floats, and
-                // stored C's column index is `row`, so the bias is one value.
+                if (row_ok) {
 #pragma unroll
-                for (int j = 0; j < Q::COLS_PER_WARP; j++) {
-                    float v = 0.0f;
-                    if (row_ok && col0 + j < N) {
-                        const size_t idx = (size_t)(col0 + j) * (size_t)M + row;
-                        v = ep.bias ? __fadd_rn(acc[j], bias_t) : acc[j];
-                        if (mask_b) v = __ldg(mask_b + idx) > 0.0f ? v : 0.0f;
-                        if (Cb) Cb[idx] = v;
-                        if (act_b) {
-                            v = ep_relu(v);
-                            act_b[idx] = v;
+                    for (int j = 0; j < Q::COLS_PER_WARP; j++) {
+                        if (col0 + j < N) {
+                            const size_t idx = (size_t)(col0 + j) * (size_t)M + row;
+                            float v = ep.bias ? __fadd_rn(acc[j], bias_t) : acc[j];
+                            if (mask_b) v = __ldg(mask_b + idx) > 0.0f ? v : 0.0f;
+                            if (Cb) Cb[idx] = v;
+                            if (act_b) {
+                                v = ep_relu(v);
+                                act_b[idx] = v;
+                            }
+                            acc[j] = v;
                         }
                     }
-                    acc[j] = __uint_as_float(finite_bits(v));
                 }
             } else {
                 const size_t base = (size_t)row * (size_t)N + col0;
@@ -765,13 +800,21 @@ gemm_3xtf32_kernel(const __grid_constant__ CUtensorMap tAh, const __grid_constan
                             act_b[base + j] = v;
                         }
                     }
-                    acc[j] = __uint_as_float(finite_bits(v));
+                    acc[j] = v;
                 }
             }
             uint32_t rmax = 0;  // over this lane's values: a stored row (a stored column when store_t)
             if (ep.out_lines) {  // uniform: every lane of the warp gets here
+                bool nonfinite = false;
 #pragma unroll
-                for (int j = 0; j < Q::COLS_PER_WARP; j++) rmax = max(rmax, __float_as_uint(acc[j]));
+                for (int j = 0; j < Q::COLS_PER_WARP; j++) {
+                    const bool in_c = row_ok && col0 + j < N;
+                    nonfinite |= in_c && (__float_as_uint(acc[j]) & 0x7F800000u) == 0x7F800000u;
+                    const uint32_t b = in_c ? finite_bits(acc[j]) : 0u;
+                    rmax = max(rmax, b);
+                    acc[j] = __uint_as_float(b);
+                }
+                if (__any_sync(0xffffffffu, nonfinite) && lane == 0) atomicOr(ep.out_flag, 1u);
 #pragma unroll
                 for (int g = 0; g < Q::COLS_PER_WARP / 32; g++) {
                     // Column maxima over the warp's 32 rows: a butterfly that halves
@@ -823,18 +866,26 @@ __device__ __forceinline__ float finite_or_zero(float x, bool &bad) {
     return 0.0f;
 }
 
-// Block 0 thread 0 writes a split's header (its nonfinite word is zeroed
-// beforehand and only ever OR-ed).
-__device__ __forceinline__ void write_header(SplitHeader *h, const float *src, uint32_t layout, uint32_t lines) {
+// Block 0 thread 0 writes a split's header.  nf: the source's NaN/Inf flag
+// as the pass that computed its line maxima left it, written here; or NULL
+// when the header was zeroed beforehand and the split's own threads OR in
+// what they see (flag_nonfinite).
+__device__ __forceinline__ void write_header(SplitHeader *h, const float *src, uint32_t layout, uint32_t lines,
+                                             const uint32_t *nf) {
     h->src = reinterpret_cast<unsigned long long>(src);
+    if (nf) {
+        h->nonfinite = *nf;
+        h->reserved = 0;
+    }
     h->layout = layout;
     h->lines = lines;
     h->magic = kSplitMagic;
 }
 
-// Every warp ORs `bad` into the headers' nonfinite words.
-__device__ __forceinline__ void flag_nonfinite(bool bad, SplitHeader *h0, SplitHeader *h1) {
-    if (__any_sync(0xffffffffu, bad) && (threadIdx.x & 31) == 0) {
+// Every warp ORs `bad` into the headers' nonfinite words (when no flag came
+// with the line maxima).
+__device__ __forceinline__ void flag_nonfinite(bool bad, SplitHeader *h0, SplitHeader *h1, const uint32_t *nf) {
+    if (!nf && __any_sync(0xffffffffu, bad) && (threadIdx.x & 31) == 0) {
         if (h0) atomicOr(&h0->nonfinite, 1u);
         if (h1) atomicOr(&h1->nonfinite, 1u);
     }
@@ -842,52 +893,63 @@ __device__ __forceinline__ void flag_nonfinite(bool bad, SplitHeader *h0, SplitH
 
 // Line maxima of X [R, C]: rowmax[r] / colmax[c] = the bits of the largest
 // finite |x| of row r / column c (each array optional, zeroed beforehand;
-// non-negative floats order like their bits as unsigned integers).  Tiles of
-// 64 rows x 512 columns: warp w takes rows w, w + 8, ...; lane l the four
-// columns 4l.. of each 128-column quarter (16-byte loads when X allows).  A
-// row's max is reduced over the warp and added with one atomic per tile, a
-// column's over the 8 warps in shared memory, one atomic per tile.
+// non-negative floats order like their bits as unsigned integers).  Work
+// unit (s, g): the 512-column strip s of the rows [g R / G, (g + 1) R / G);
+// lane l reads the four columns 4l.. of each 128-column quarter of the strip
+// (16-byte loads when X allows), warp w every 8th row from w, four rows per
+// step (16 independent loads in flight per thread).  A row's max over the
+// strip is reduced over the warp (redux.sync) and added with one atomic; a
+// column's over the unit's rows is kept in registers, reduced over the 8
+// warps in shared memory and added with one atomic per unit.
 template <bool ROWS, bool COLS>
 __global__ void __launch_bounds__(256) lines_max_kernel(const float *__restrict__ src, int64_t R, int64_t C, int vec,
-                                                        uint32_t *__restrict__ rowmax, uint32_t *__restrict__ colmax) {
-    constexpr int TR = 64, TC = 512;
+                                                        int64_t groups, uint32_t *__restrict__ rowmax,
+                                                        uint32_t *__restrict__ colmax, uint32_t *__restrict__ flag) {
+    constexpr int TC = 512, RW = 4;
     __shared__ uint32_t cm[COLS ? 8 : 1][COLS ? TC : 1];
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-    const int64_t tiles_c = (C + TC - 1) / TC, tiles = ((R + TR - 1) / TR) * tiles_c;
-    for (int64_t t = blockIdx.x; t < tiles; t += gridDim.x) {
-        const int64_t r0 = (t / tiles_c) * TR, c0 = (t % tiles_c) * TC;
+    const int64_t strips = (C + TC - 1) / TC;
+    bool bad = false;
+    for (int64_t unit = blockIdx.x; unit < strips * groups; unit += gridDim.x) {
+        const int64_t s = unit % strips, g = unit / strips;
+        const int64_t c0 = s * TC, r_begin = g * R / groups, r_end = (g + 1) * R / groups;
         uint32_t cmx[16];
 #pragma unroll
         for (int k = 0; k < 16; k++) cmx[k] = 0;
-#pragma unroll 2
-        for (int i = 0; i < TR / 8; i++) {
-            const int64_t r = r0 + warp + 8 * i;
-            uint32_t rmx = 0;
-            if (r < R) {
+        for (int64_t rb = r_begin + warp; rb < r_end; rb += 8 * RW) {
+            uint32_t b[RW][16];
+#pragma unroll
+            for (int i = 0; i < RW; i++) {
+                const int64_t r = rb + 8 * i;
                 const float *p = src + r * C;
 #pragma unroll
                 for (int qq = 0; qq < 4; qq++) {
                     const int64_t c = c0 + qq * 128 + 4 * lane;
-                    uint32_t b[4];
-                    if (vec && c + 4 <= C) {
+                    if (r < r_end && vec && c + 4 <= C) {
                         const uint4 u = __ldg(reinterpret_cast<const uint4 *>(p + c));
-                        b[0] = u.x; b[1] = u.y; b[2] = u.z; b[3] = u.w;
+                        b[i][4 * qq] = u.x; b[i][4 * qq + 1] = u.y; b[i][4 * qq + 2] = u.z; b[i][4 * qq + 3] = u.w;
                     } else {
 #pragma unroll
-                        for (int e = 0; e < 4; e++) b[e] = c + e < C ? __float_as_uint(p[c + e]) : 0u;
-                    }
-#pragma unroll
-                    for (int e = 0; e < 4; e++) {
-                        const uint32_t m = finite_bits(__uint_as_float(b[e]));
-                        rmx = max(rmx, m);
-                        cmx[qq * 4 + e] = max(cmx[qq * 4 + e], m);
+                        for (int e = 0; e < 4; e++)
+                            b[i][4 * qq + e] = (r < r_end && c + e < C) ? __float_as_uint(p[c + e]) : 0u;
                     }
                 }
             }
-            if (ROWS) {
 #pragma unroll
-                for (int o = 16; o > 0; o >>= 1) rmx = max(rmx, __shfl_xor_sync(0xffffffffu, rmx, o));
-                if (lane == 0 && r < R && rmx) atomicMax(rowmax + r, rmx);
+            for (int i = 0; i < RW; i++) {
+                uint32_t rmx = 0;
+#pragma unroll
+                for (int k = 0; k < 16; k++) {
+                    bad |= (b[i][k] & 0x7F800000u) == 0x7F800000u;
+                    const uint32_t m = finite_bits(__uint_as_float(b[i][k]));
+                    rmx = max(rmx, m);
+                    cmx[k] = max(cmx[k], m);
+                }
+                if (ROWS) {
+                    rmx = __reduce_max_sync(0xffffffffu, rmx);
+                    const int64_t r = rb + 8 * i;
+                    if (lane == 0 && r < r_end && rmx) atomicMax(rowmax + r, rmx);
+                }
             }
         }
         if (COLS) {
@@ -903,6 +965,7 @@ __global__ void __launch_bounds__(256) lines_max_kernel(const float *__restrict_
             __syncthreads();
         }
     }
+    if (flag && __any_sync(0xffffffffu, bad) && lane == 0) atomicOr(flag, 1u);
 }
 
 // The scale 2^e of a line from its max word.
@@ -921,13 +984,14 @@ __global__ void __launch_bounds__(256) split_kernel(const float *__restrict__ sr
                                                     const uint32_t *__restrict__ cmax, float *__restrict__ hr,
                                                     float *__restrict__ lr, float *__restrict__ hc,
                                                     float *__restrict__ lc, SplitHeader *hdr_r, SplitHeader *hdr_c,
-                                                    uint32_t *__restrict__ copy_r, uint32_t *__restrict__ copy_c) {
+                                                    uint32_t *__restrict__ copy_r, uint32_t *__restrict__ copy_c,
+                                                    const uint32_t *nf) {
     const int64_t q = pitch / 4;
     const int64_t n = rows * q;
     const int64_t t0 = blockIdx.x * (int64_t)blockDim.x + threadIdx.x, stride = (int64_t)gridDim.x * blockDim.x;
     if (t0 == 0) {
-        if (hdr_r) write_header(hdr_r, src, 0, (uint32_t)rows);
-        if (hdr_c) write_header(hdr_c, src, kLayoutCols, (uint32_t)cols);
+        if (hdr_r) write_header(hdr_r, src, 0, (uint32_t)rows, nf);
+        if (hdr_c) write_header(hdr_c, src, kLayoutCols, (uint32_t)cols, nf);
     }
     if (copy_r)
         for (int64_t i = t0; i < rows; i += stride) copy_r[i] = rmax[i];
@@ -969,7 +1033,7 @@ __global__ void __launch_bounds__(256) split_kernel(const float *__restrict__ sr
             *reinterpret_cast<float4 *>(lc + r * pitch + k) = make_float4(l[0], l[1], l[2], l[3]);
         }
     }
-    flag_nonfinite(bad, hdr_r, hdr_c);
+    flag_nonfinite(bad, hdr_r, hdr_c, nf);
 }
 
 // Transposed 3xTF32 split: X [rows, cols] -> hi/lo of X^T, [cols, pitch] with
@@ -987,12 +1051,12 @@ __global__ void __launch_bounds__(256) split_t_kernel(const float *__restrict__ 
                                                       float *__restrict__ lo, float *__restrict__ phi,
                                                       float *__restrict__ plo, int64_t ppitch, SplitHeader *ht,
                                                       SplitHeader *hp, uint32_t *__restrict__ copy_t,
-                                                      uint32_t *__restrict__ copy_p) {
+                                                      uint32_t *__restrict__ copy_p, const uint32_t *nf) {
     __shared__ float tile[64][65];
     const int64_t t0 = blockIdx.x * (int64_t)blockDim.x + threadIdx.x, stride = (int64_t)gridDim.x * blockDim.x;
     if (t0 == 0) {
-        write_header(ht, src, kLayoutT, (uint32_t)cols);
-        if (hp) write_header(hp, src, 0, (uint32_t)rows);
+        write_header(ht, src, kLayoutT, (uint32_t)cols, nf);
+        if (hp) write_header(hp, src, 0, (uint32_t)rows, nf);
     }
     if (copy_t)
         for (int64_t i = t0; i < cols; i += stride) copy_t[i] = cmax[i];
@@ -1049,7 +1113,7 @@ __global__ void __launch_bounds__(256) split_t_kernel(const float *__restrict__ 
         *reinterpret_cast<float4 *>(hi + c * pitch + r) = make_float4(h[0], h[1], h[2], h[3]);
         *reinterpret_cast<float4 *>(lo + c * pitch + r) = make_float4(l[0], l[1], l[2], l[3]);
     }
-    flag_nonfinite(bad, ht, hp);
+    flag_nonfinite(bad, ht, hp, nf);
 }
 
 // ---- 3xFP16 splits ----------------------------------------------------------------------
@@ -1075,13 +1139,13 @@ __global__ void __launch_bounds__(256) split16_kernel(const float *__restrict__ 
                                                       __half *__restrict__ lr, __half *__restrict__ hc,
                                                       __half *__restrict__ lc, SplitHeader *hdr_r,
                                                       SplitHeader *hdr_c, uint32_t *__restrict__ copy_r,
-                                                      uint32_t *__restrict__ copy_c) {
+                                                      uint32_t *__restrict__ copy_c, const uint32_t *nf) {
     const int64_t q = pitch / 8;
     const int64_t n = rows * q;
     const int64_t t0 = blockIdx.x * (int64_t)blockDim.x + threadIdx.x, stride = (int64_t)gridDim.x * blockDim.x;
     if (t0 == 0) {
-        if (hdr_r) write_header(hdr_r, src, 0, (uint32_t)rows);
-        if (hdr_c) write_header(hdr_c, src, kLayoutCols, (uint32_t)cols);
+        if (hdr_r) write_header(hdr_r, src, 0, (uint32_t)rows, nf);
+        if (hdr_c) write_header(hdr_c, src, kLayoutCols, (uint32_t)cols, nf);
     }
     if (copy_r)
         for (int64_t i = t0; i < rows; i += stride) copy_r[i] = rmax[i];
@@ -1122,7 +1186,7 @@ __global__ void __launch_bounds__(256) split16_kernel(const float *__restrict__ 
             *reinterpret_cast<uint4 *>(lc + r * pitch + k) = make_uint4(lw[0], lw[1], lw[2], lw[3]);
         }
     }
-    flag_nonfinite(bad, hdr_r, hdr_c);
+    flag_nonfinite(bad, hdr_r, hdr_c, nf);
 }
 
 // The fp16 split of X^T ([cols, pitch], pitch = rows rounded up to 8; its
@@ -1137,12 +1201,12 @@ __global__ void __launch_bounds__(256) split16_t_kernel(const float *__restrict_
                                                         __half *__restrict__ lo, __half *__restrict__ phi,
                                                         __half *__restrict__ plo, int64_t ppitch, SplitHeader *ht,
                                                         SplitHeader *hp, uint32_t *__restrict__ copy_t,
-                                                        uint32_t *__restrict__ copy_p) {
+                                                        uint32_t *__restrict__ copy_p, const uint32_t *nf) {
     __shared__ float tile[64][65];
     const int64_t t0 = blockIdx.x * (int64_t)blockDim.x + threadIdx.x, stride = (int64_t)gridDim.x * blockDim.x;
     if (t0 == 0) {
-        write_header(ht, src, kLayoutT, (uint32_t)cols);
-        if (hp) write_header(hp, src, 0, (uint32_t)rows);
+        write_header(ht, src, kLayoutT, (uint32_t)cols, nf);
+        if (hp) write_header(hp, src, 0, (uint32_t)rows, nf);
     }
     if (copy_t)
         for (int64_t i = t0; i < cols; i += stride) copy_t[i] = cmax[i];
@@ -1191,7 +1255,7 @@ __global__ void __launch_bounds__(256) split16_t_kernel(const float *__restrict_
         *reinterpret_cast<uint2 *>(hi + c * pitch + r) = make_uint2(h0, h1);
         *reinterpret_cast<uint2 *>(lo + c * pitch + r) = make_uint2(lw0, lw1);
     }
-    flag_nonfinite(bad, ht, hp);
+    flag_nonfinite(bad, ht, hp, nf);
 }
 
 // ---- host side -------------------------------------------------------------------------
@@ -1361,12 +1425,13 @@ static int launch_gemm(const float *ah, const float *al, const float *bh, const 
         arrivals = reinterpret_cast<int *>(part + (tiles - tp.full_tiles) * tp.splits * BM * BN);
         J4C_CUDA(cudaMemsetAsync(arrivals, 0, (size_t)((tiles - tp.full_tiles) * kEpiWarps) * sizeof(int), s));
     }
-    if (ep.out_lines) J4C_CUDA(cudaMemsetAsync(ep.out_lines, 0, (size_t)(M + N) * sizeof(uint32_t), s));
+    if (ep.out_lines) J4C_CUDA(cudaMemsetAsync(ep.out_lines, 0, (size_t)(M + N + 1) * sizeof(uint32_t), s));
     const SplitHeader *ahdr = split_header(ah, ar * ab, ac);
     const SplitHeader *bhdr = split_header(bh, br * bb, bc);
     kernel<<<grid, kThreads, Q::SMEM_BYTES, s>>>(mAh, mAl, mBh, mBl, c, (int)M, (int)N, (int)K, (int)num_kb,
                                                  store_t ? 0 : vec, store_t ? 1 : 0, ep, (int)batch, a_bat ? 1 : 0,
-                                                 b_bat ? 1 : 0, status, (int)tp.full_tiles, tp.splits, part, arrivals,
+                                                 b_bat ? 1 : 0, status, wait_limit_ns(), (int)tp.full_tiles, tp.splits,
+                                                 part, arrivals,
                                                  ahdr, bhdr);
     J4C_LAUNCH_CHECK("gemm_3xtf32_kernel");
     if (owned) return scratch_free(owned, s);
@@ -1391,18 +1456,25 @@ static int launch_gemm_any(const float *ah, const float *al, const float *bh, co
 }
 
 // rowmax[r] / colmax[c] (either may be NULL): the bits of the largest finite
-// |x| of each row / column of X [rows, cols]; zeroed here first.
+// |x| of each row / column of X [rows, cols]; *flag (may be NULL) nonzero
+// when X holds a NaN or an infinity.  All three start at zero: the caller
+// zeroes them (one memset when they lie back to back).
 static int lines_max(const float *src, int64_t rows, int64_t cols, uint32_t *rowmax, uint32_t *colmax,
-                     cudaStream_t s) {
-    if (rowmax) J4C_CUDA(cudaMemsetAsync(rowmax, 0, (size_t)rows * sizeof(uint32_t), s));
-    if (colmax) J4C_CUDA(cudaMemsetAsync(colmax, 0, (size_t)cols * sizeof(uint32_t), s));
-    if (!rowmax && !colmax) return J4C_OK;
+                     uint32_t *flag, cudaStream_t s) {
+    if (!rowmax && !colmax && !flag) return J4C_OK;
     const int vec = (cols % 4 == 0) && aligned16(src);
-    const int64_t tiles = ceil_div(rows, 64) * ceil_div(cols, 512);
-    const unsigned grid = (unsigned)std::min<int64_t>(tiles, (int64_t)sm_count() * 8);
-    if (rowmax && colmax) lines_max_kernel<true, true><<<grid, 256, 0, s>>>(src, rows, cols, vec, rowmax, colmax);
-    else if (rowmax) lines_max_kernel<true, false><<<grid, 256, 0, s>>>(src, rows, cols, vec, rowmax, colmax);
-    else lines_max_kernel<false, true><<<grid, 256, 0, s>>>(src, rows, cols, vec, rowmax, colmax);
+    // units: 512-column strips times row groups of at least 32 rows, about
+    // four per SM
+    const int64_t strips = ceil_div(cols, 512);
+    const int64_t groups = std::max<int64_t>(1, std::min<int64_t>(ceil_div(rows, 32),
+                                                                  ceil_div((int64_t)sm_count() * 4, strips)));
+    const unsigned grid = (unsigned)std::min<int64_t>(strips * groups, (int64_t)sm_count() * 8);
+    if (rowmax && colmax)
+        lines_max_kernel<true, true><<<grid, 256, 0, s>>>(src, rows, cols, vec, groups, rowmax, colmax, flag);
+    else if (rowmax)
+        lines_max_kernel<true, false><<<grid, 256, 0, s>>>(src, rows, cols, vec, groups, rowmax, colmax, flag);
+    else
+        lines_max_kernel<false, true><<<grid, 256, 0, s>>>(src, rows, cols, vec, groups, rowmax, colmax, flag);
     J4C_LAUNCH_CHECK("lines_max_kernel");
     return J4C_OK;
 }
@@ -1413,7 +1485,8 @@ static int lines_max(const float *src, int64_t rows, int64_t cols, uint32_t *row
 //   t: X^T with its rows (X's columns) as lines (read K-major),
 // r alone, c alone, t alone, r + c or r + t.  lines_in (may be NULL):
 // X's line maxima computed already, rows then columns, as a GEMM epilogue's
-// out_lines leaves them; otherwise a max pass over X computes those needed.
+// out_lines leaves them (rows, then columns, then the NaN/Inf flag word);
+// otherwise a max pass over X computes those needed.
 int split_any(const float *src, int64_t rows, int64_t cols, float *hr, float *lr, float *hc, float *lc, float *ht,
               float *lt, const uint32_t *lines_in, cudaStream_t s) {
     if (rows == 0 || cols == 0) return J4C_OK;
@@ -1427,26 +1500,31 @@ int split_any(const float *src, int64_t rows, int64_t cols, float *hr, float *lr
     SplitHeader *hdr_r = hr ? split_header(hr, rows, cols) : nullptr;
     SplitHeader *hdr_c = hc ? split_header(hc, rows, cols) : nullptr;
     SplitHeader *hdr_t = ht ? split_header(ht, cols, rows) : nullptr;
-    // headers start at zero (their line words are written whole below)
-    if (hdr_r) J4C_CUDA(cudaMemsetAsync(hdr_r, 0, sizeof(SplitHeader), s));
-    if (hdr_c) J4C_CUDA(cudaMemsetAsync(hdr_c, 0, sizeof(SplitHeader), s));
-    if (hdr_t) J4C_CUDA(cudaMemsetAsync(hdr_t, 0, sizeof(SplitHeader), s));
     uint32_t *own_r = hdr_r ? reinterpret_cast<uint32_t *>(hdr_r + 1) : nullptr;
     uint32_t *own_c = hdr_c ? reinterpret_cast<uint32_t *>(hdr_c + 1)
                             : (hdr_t ? reinterpret_cast<uint32_t *>(hdr_t + 1) : nullptr);
-    const uint32_t *rmax = nullptr, *cmax = nullptr;
+    const uint32_t *rmax = nullptr, *cmax = nullptr, *nf = nullptr;
     uint32_t *copy_r = nullptr, *copy_c = nullptr;
     if (lines_in) {
+        // the maxima and the NaN/Inf flag came with the call: the kernels
+        // copy them into the outputs and write whole headers, nothing to zero
         rmax = lines_in;
         cmax = lines_in + rows;
+        nf = lines_in + rows + cols;
         copy_r = own_r;
         copy_c = own_c;
     } else {
-        int rc = lines_max(src, rows, cols, own_r, own_c, s);
+        // headers and line words start at zero; the max pass fills the line
+        // words and the split kernel ORs the flag into the headers
+        if (hdr_r) J4C_CUDA(cudaMemsetAsync(hdr_r, 0, sizeof(SplitHeader) + 4 * rows, s));
+        if (hdr_c) J4C_CUDA(cudaMemsetAsync(hdr_c, 0, sizeof(SplitHeader) + 4 * cols, s));
+        if (hdr_t) J4C_CUDA(cudaMemsetAsync(hdr_t, 0, sizeof(SplitHeader) + 4 * cols, s));
+        int rc = lines_max(src, rows, cols, own_r, own_c, nullptr, s);
         if (rc) return rc;
         rmax = own_r;
         cmax = own_c;
     }
+    (void)f16;
     if (ht) {
         const int64_t pitch = split_pitch(rows);
         const int64_t tiles_c = ceil_div(cols, 64), tiles_r = ceil_div(pitch, 64);
@@ -1456,12 +1534,12 @@ int split_any(const float *src, int64_t rows, int64_t cols, float *hr, float *lr
             split16_t_kernel<<<(unsigned)(tiles_c * tiles_r), 256, 0, s>>>(
                 src, rows, cols, pitch, tiles_c, vec_in, rmax, cmax, reinterpret_cast<__half *>(ht),
                 reinterpret_cast<__half *>(lt), reinterpret_cast<__half *>(hr), reinterpret_cast<__half *>(lr),
-                split_pitch(cols), hdr_t, hdr_r, copy_c, copy_r);
+                split_pitch(cols), hdr_t, hdr_r, copy_c, copy_r, nf);
             J4C_LAUNCH_CHECK("split16_t_kernel");
         } else {
             split_t_kernel<<<(unsigned)(tiles_c * tiles_r), 256, 0, s>>>(src, rows, cols, pitch, tiles_c, vec_in, rmax,
                                                                          cmax, ht, lt, hr, lr, split_pitch(cols), hdr_t,
-                                                                         hdr_r, copy_c, copy_r);
+                                                                         hdr_r, copy_c, copy_r, nf);
             J4C_LAUNCH_CHECK("split_t_kernel");
         }
         return J4C_OK;
@@ -1471,12 +1549,12 @@ int split_any(const float *src, int64_t rows, int64_t cols, float *hr, float *lr
     if (f16) {
         split16_kernel<<<grid_for(rows * (pitch / 8), 256), 256, 0, s>>>(
             src, rows, cols, pitch, vec, rmax, cmax, reinterpret_cast<__half *>(hr), reinterpret_cast<__half *>(lr),
-            reinterpret_cast<__half *>(hc), reinterpret_cast<__half *>(lc), hdr_r, hdr_c, copy_r, copy_c);
+            reinterpret_cast<__half *>(hc), reinterpret_cast<__half *>(lc), hdr_r, hdr_c, copy_r, copy_c, nf);
         J4C_LAUNCH_CHECK("split16_kernel");
         return J4C_OK;
     }
     split_kernel<<<grid_for(rows * (pitch / 4), 256), 256, 0, s>>>(src, rows, cols, pitch, vec, rmax, cmax, hr, lr, hc,
-                                                                   lc, hdr_r, hdr_c, copy_r, copy_c);
+                                                                   lc, hdr_r, hdr_c, copy_r, copy_c, nf);
     J4C_LAUNCH_CHECK("split_kernel");
     return J4C_OK;
 }
@@ -1515,11 +1593,13 @@ int tc_split_any(const float *x, int64_t rows, int64_t cols, float *hr, float *l
     return tc::split_any(x, rows, cols, hr, lr, hc, lc, ht, lt, lines_in, s);
 }
 
-// lines [rows + cols]: X's row maxima, then its column maxima (bits of the
-// largest finite |x| of each line), as a GEMM epilogue's out_lines.
+// lines [rows + cols + 1]: X's row maxima, then its column maxima (bits of
+// the largest finite |x| of each line), then the NaN/Inf flag, as a GEMM
+// epilogue's out_lines.
 int tc_split_lines(const float *x, int64_t rows, int64_t cols, uint32_t *lines, cudaStream_t s) {
+    J4C_CUDA(cudaMemsetAsync(lines, 0, (size_t)(rows + cols + 1) * sizeof(uint32_t), s));
     if (rows == 0 || cols == 0) return J4C_OK;
-    return tc::lines_max(x, rows, cols, lines, lines + rows, s);
+    return tc::lines_max(x, rows, cols, lines, lines + rows, lines + rows + cols, s);
 }
 
 // tail_ws: scratch of at least tc::tail_scratch_bound bytes, or NULL to take it
@@ -1538,7 +1618,7 @@ static int gemm_presplit_ws(const float *ah, const float *al, const float *bh, c
         const char *v = getenv("J4C_GEMM_VARIANT");
         return v ? atoi(v) : 1;
     }();
-    const tc::Epilogue ep{bias, mask, act, out_lines, (int)M};
+    const tc::Epilogue ep{bias, mask, act, out_lines, (int)M, out_lines ? out_lines + M + N : nullptr};
     const bool ab = a_batched != 0, bb = b_batched != 0;
     if (tc::split_fp16())
         return tc::launch_gemm_any<256, 4, 16, true>(ah, al, bh, bl, c, M, N, K, a_mn, b_mn, ep, batch, ab, bb, tail_ws, s);

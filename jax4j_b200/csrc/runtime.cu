@@ -50,6 +50,10 @@ int sm_count() {
     return cache[dev];
 }
 
+std::atomic<uint64_t> g_wait_limit_ns{2000000000ull};
+
+uint64_t wait_limit_ns() { return g_wait_limit_ns.load(std::memory_order_relaxed); }
+
 int *device_status_ptr() {
     static std::mutex mu;
     static std::vector<int *> words;
@@ -210,6 +214,13 @@ int j4c_enable_peer_access(int device, int peer) {
     }
     cudaSetDevice(cur);
     if (e != cudaSuccess) return cuda_status(e, "cudaDeviceEnablePeerAccess");
+    return J4C_OK;
+}
+
+int j4c_set_wait_limit_ns(uint64_t ns, uint64_t *previous) {
+    J4C_REQUIRE(ns > 0, "j4c_set_wait_limit_ns: the limit must be positive");
+    const uint64_t old = j4c::g_wait_limit_ns.exchange(ns);
+    if (previous) *previous = old;
     return J4C_OK;
 }
 

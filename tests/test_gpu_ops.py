@@ -625,8 +625,10 @@ def test_epilogue_line_maxima_and_split_from_them(J, ta, tb, act, masked):
     assert out._lines is not None
     got = out._lines.cpu().numpy().view(np.uint32)
     o = out.numpy()
+    assert got.size == M + N + 1
     np.testing.assert_array_equal(got[:M], _line_max_bits(o, "rows"))
-    np.testing.assert_array_equal(got[M:], _line_max_bits(o, "cols"))
+    np.testing.assert_array_equal(got[M:M + N], _line_max_bits(o, "cols"))
+    assert got[M + N] == 0  # no NaN or infinity written
     d = out.tensor().device
     for pair in (("r", "t"), ("r", "c"), ("c",)):
         given, scan = [], []
@@ -746,10 +748,15 @@ def test_dot_special_values_through_the_epilogue_and_vmap(J):
     z = (orc.dot(A, B) + bias).astype(np.float32)
     want = np.where(np.isnan(z), z, np.maximum(z, np.float32(0)))
     assert np.array_equal(h.numpy(), want, equal_nan=True)
-    lines = h._lines.cpu().numpy().view(np.uint32) if h._lines is not None else None
-    if lines is not None:
-        np.testing.assert_array_equal(lines[:M], _line_max_bits(want, "rows"))
-        np.testing.assert_array_equal(lines[M:], _line_max_bits(want, "cols"))
+    lines = h._lines.cpu().numpy().view(np.uint32)
+    np.testing.assert_array_equal(lines[:M], _line_max_bits(want, "rows"))
+    np.testing.assert_array_equal(lines[M:M + N], _line_max_bits(want, "cols"))
+    assert lines[M + N] != 0  # the relu output holds NaN and infinity
+    # ... and a product taking it as an operand runs the exact path too
+    from jax4j_b200.core import _dot_raw as dr
+    C2 = r.uniform(-1, 1, (N, 20)).astype(np.float32)
+    got2 = dr(h, dev(J, C2), False, False, a.device()).numpy()
+    assert np.array_equal(got2, orc.dot(h.numpy(), C2), equal_nan=True)
     # vmap's strided-batched dot: [3, M, K] . [3, K, N] with a special in one entry
     A3 = np.stack([r.uniform(-1, 1, (M, K)).astype(np.float32) for _ in range(3)])
     B3 = np.stack([r.uniform(-1, 1, (K, N)).astype(np.float32) for _ in range(3)])
