@@ -57,6 +57,8 @@ def parse():
     p.add_argument("--no-cpu-baseline", action="store_true")
     p.add_argument("--no-e2e", action="store_true")
     p.add_argument("--no-graph", action="store_true", help="time the eager step only (no CUDA graph)")
+    p.add_argument("--no-secondary", action="store_true",
+                   help="skip the configuration 0-3 measurements that ride along in the headline line")
     p.add_argument("--workload", default="dp_step", choices=["dp_step", "gemm", "sweep", "cfg0", "cfg2", "collectives", "fft", "linalg"],
                    help="dp_step is the headline; gemm/sweep are single-kernel measurements "
                         "used for profiling")
@@ -375,15 +377,22 @@ def run_ours(args):
         for g in slot_graphs:
             g.release()
 
+    replayed = bool(graphs)
     for g in graphs:
         g.release()  # before the process group goes away (a graph may hold NCCL work)
+    graphs = []
+    secondary = None
+    if not args.no_secondary:
+        # configurations 0-3, a few seconds each, on the same ranks (every rank
+        # takes the same collective steps; rank 0 keeps the results)
+        secondary = measure_secondary(args)
     if rank != 0:
         if world > 1:
             distributed.barrier()
             distributed.shutdown()
         return
     peaks = _measured_peaks()
-    peak, peak_source = _tensor_peak(peaks, clk)
+    peak, peak_source = _tensor_peak(peaks, ms / 1e3)
     achieved = (dot_flop / (dot_ms / 1e3)) / 1e12 if dot_ms > 0 else None
     from jax4j_b200.core import split_kind
     f16 = split_kind() == 1
@@ -414,12 +423,13 @@ def run_ours(args):
                                        "launches of one step at batch 8192, averaged per launch "
                                        "(single-pass capture, cold L2)"},
         "gpu_launches": launches,
-        "execution": ("CUDA graph replay of the recorded step (%d kernels per step)" % per_replay) if graphs
+        "execution": ("CUDA graph replay of the recorded step (%d kernels per step)" % per_replay) if replayed
                      else "eager",
         "eager": {"ms_per_step": eager_ms / args.steps, "value": D * B * args.steps / (eager_ms / 1e3),
                   "gpu_launches": eager_launches},
         "host_enqueue_ms_per_step": host_ms,
         "clocks": clk,
+        "timed_region_s": ms / 1e3,
         "flops_per_sample": flops_per_sample(),
     }
     if graph_note:
@@ -427,7 +437,9 @@ def run_ours(args):
     if e2e:
         line["e2e"] = e2e
     if D == 1 and not args.no_cpu_baseline:
-        line["cpu_baseline"] = cpu_baseline(10.0)
+        line["cpu_baseline"] = cpu_baseline()
+    if secondary is not None:
+        line["secondary"] = secondary
     print(json.dumps(line), flush=True)
     if world > 1:
         distributed.barrier()
@@ -440,17 +452,21 @@ def run_ours(args):
 GEMM_DRAM_BYTES_PER_LAUNCH = {"tf32": 1.0663e9, "fp16": 5.573e8}
 
 
-def _tensor_peak(peaks: dict, clk: dict):
-    """The bf16 denominator for a tensor-bound kernel: the sustained (power
-    capped) figure when the sampled SM clock sat below its maximum, else the
-    burst figure (the kernel ran at full clock, as the burst GEMM did)."""
+SUSTAINED_AFTER_S = 1.0  # timed regions at least this long are compared with the sustained peak
+
+
+def _tensor_peak(peaks: dict, timed_s: float):
+    """The bf16 denominator for a tensor-bound kernel, chosen by the length of
+    the timed region: the burst figure (a short run, as the burst cuBLAS GEMM
+    was timed) below SUSTAINED_AFTER_S, the sustained (seconds-long, power
+    capped) figure above it."""
     burst, sustained = peaks.get("bf16_tflops"), peaks.get("bf16_tflops_sustained")
-    sm, smax = (clk or {}).get("sm_mhz"), (clk or {}).get("sm_max_mhz")
-    at_max = sm is not None and smax and sm >= 0.97 * smax
     src = peaks.get("source", "MEASURED_PEAKS.json")
-    if sustained and not at_max:
-        return sustained, f"{src} bf16 sustained (SM clock below max during the run); FP16 dense rate equal, TF32 half"
-    return burst, f"{src} bf16 burst (SM clock at max during the run); FP16 dense rate equal, TF32 half"
+    if sustained and timed_s >= SUSTAINED_AFTER_S:
+        return sustained, (f"{src} bf16 sustained (timed region {timed_s:.2f} s >= {SUSTAINED_AFTER_S} s); "
+                           "FP16 dense rate equal, TF32 half")
+    return burst, (f"{src} bf16 burst (timed region {timed_s:.2f} s < {SUSTAINED_AFTER_S} s); "
+                   "FP16 dense rate equal, TF32 half")
 
 
 def _measured_peaks() -> dict:
@@ -478,57 +494,72 @@ def _cpu_case(samples: int):
     return ws, bs, x, t
 
 
-def cpu_baseline(target_s: float) -> dict:
-    """The oracle's restatement of the reference's host grad step, on a
-    sample of the batch sized to ~target_s of CPU work, all host threads."""
+CPU_SLICE = 512        # samples of the batch the CPU arms time (CPU-N: all host threads)
+CPU_SLICE_SERIAL = 32  # samples the reference's own threading (one-thread dot) is timed on
+
+
+def _cpu_step(samples: int, threads: int) -> float:
+    """Seconds of one grad step of the oracle's restatement of the
+    reference's host path on `samples` samples of the batch."""
+    from oracle import oracle as orc
+    ws, bs, x, t = _cpu_case(samples)
+    t0 = time.perf_counter()
+    orc.mlp_loss_grad(ws, bs, x, t, act="relu", threads=threads)
+    return time.perf_counter() - t0
+
+
+def cpu_baseline() -> dict:
+    """The oracle's restatement of the reference's host grad step on a fixed
+    slice of the batch (CPU_SLICE samples) with its dot row-parallel over
+    all host threads (the reference's CPU-N mode, BackendBenchmark.java:
+    281-291, bit-identical to its serial loop), and beside it the
+    reference's own threading -- the dot on one thread (ConcreteNDArray.java:
+    452-459), elementwise work parallel -- on CPU_SLICE_SERIAL samples."""
     from oracle import oracle as orc
     threads = orc.nproc()
-    n = 16
-    ws, bs, x, t = _cpu_case(n)
-    t0 = time.perf_counter()
-    orc.mlp_loss_grad(ws, bs, x, t, act="relu", threads=threads)
-    dt = time.perf_counter() - t0
-    n2 = int(max(16, min(1024, n * target_s / max(dt, 1e-3))))
-    ws, bs, x, t = _cpu_case(n2)
-    t0 = time.perf_counter()
-    orc.mlp_loss_grad(ws, bs, x, t, act="relu", threads=threads)
-    dt = time.perf_counter() - t0
-    return {"value": n2 / dt, "unit": "samples/s", "cores": threads, "kind": "port",
-            "sample": f"{n2} samples of the same model, one grad step (sequential-k float dot, "
-                      f"row-parallel over {threads} threads)"}
+    dt = _cpu_step(CPU_SLICE, threads)
+    dt1 = _cpu_step(CPU_SLICE_SERIAL, 1)
+    return {"value": CPU_SLICE / dt, "unit": "samples/s", "cores": threads, "kind": "port",
+            "sample": f"{CPU_SLICE} samples of the batch, one grad step of the same model (sequential-k "
+                      f"float dot, row-parallel over {threads} threads: the reference's CPU-N mode)",
+            "reference_threading": {"value": CPU_SLICE_SERIAL / dt1, "unit": "samples/s", "cores": 1,
+                                    "sample": f"{CPU_SLICE_SERIAL} samples, dot on one thread as the "
+                                              "reference's ConcreteNDArray.dot runs it"}}
 
 
 def run_reference(args):
+    """The reference's CPU algorithm (the oracle's C restatement of its host
+    path) with all host threads, each step one grad step on the fixed
+    CPU_SLICE samples of the headline batch; rank 0 alone under torchrun."""
     world = int(os.environ.get("WORLD_SIZE", "1"))
     rank = int(os.environ.get("RANK", "0"))
     if rank != 0:
         return
     from oracle import oracle as orc
     threads = orc.nproc()
-    n = 16
-    ws, bs, x, t = _cpu_case(n)
-    t0 = time.perf_counter()
-    orc.mlp_loss_grad(ws, bs, x, t, act="relu", threads=threads)
-    dt = time.perf_counter() - t0
-    per_step_s = 60.0 / max(1, args.steps + args.warmup)
-    n = int(max(8, min(1024, n * per_step_s / max(dt, 1e-3))))
-    ws, bs, x, t = _cpu_case(n)
+    ws, bs, x, t = _cpu_case(CPU_SLICE)
     for _ in range(args.warmup):
         orc.mlp_loss_grad(ws, bs, x, t, act="relu", threads=threads)
     t0 = time.perf_counter()
     for _ in range(args.steps):
         orc.mlp_loss_grad(ws, bs, x, t, act="relu", threads=threads)
     el = time.perf_counter() - t0
-    value = n * args.steps / el
+    value = CPU_SLICE * args.steps / el
+    dt1 = _cpu_step(CPU_SLICE_SERIAL, 1)
     line = {"metric": METRIC, "value": value, "unit": "samples/s", "n_gpus": world,
             "steps": args.steps, "warmup": args.warmup, "ms_per_step": el * 1e3 / args.steps,
             "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "f32",
             "data": "synthetic", "impl": "reference",
             "config": {"workload": WORKLOAD, "model": "mlp-1024-4096x3-1000-relu",
-                       "global_batch": BATCH * world, "parallelism": f"dp{world}"},
+                       "global_batch": BATCH * world, "parallelism": f"dp{world}",
+                       "cpu_slice": f"{CPU_SLICE} samples of the batch per step"},
             "cpu_baseline": {"value": value, "unit": "samples/s", "cores": threads, "kind": "port",
-                             "sample": f"{n} samples per step (the reference's host algorithm, "
-                                       f"C restatement, row-parallel dot over {threads} threads)"},
+                             "sample": f"{CPU_SLICE} samples per step (the reference's host algorithm, "
+                                       f"C restatement, row-parallel dot over {threads} threads)",
+                             "reference_threading": {"value": CPU_SLICE_SERIAL / dt1, "unit": "samples/s",
+                                                     "cores": 1,
+                                                     "sample": f"{CPU_SLICE_SERIAL} samples, dot on one "
+                                                               "thread"}},
             "e2e": {"value": value, "unit": "samples/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}
     print(json.dumps(line), flush=True)
 
@@ -583,14 +614,37 @@ def run_gemm(args):
                       "algorithmic_bytes": 4 * (M * K + K * N + M * N)}), flush=True)
 
 
-def run_sweep(args):
-    """where(x.gt(0), tanh(x)*sigmoid(y), relu(y).clip(-1,1)), sum(-1,keep), argmax(-1)."""
+SWEEP_ROWS, SWEEP_COLS = 4096, 16384
+
+
+def _sweep_cpu(rows: int = 64) -> dict:
+    """The oracle's restatement of the sweep (one thread) on `rows` rows."""
+    from oracle import oracle as orc
+    x = orc.normal(1, (rows * SWEEP_COLS,)).reshape(rows, SWEEP_COLS)
+    y = orc.uniform(11, (rows * SWEEP_COLS,), -3.0, 3.0).reshape(rows, SWEEP_COLS)
+    t0 = time.perf_counter()
+    orc.sweep(x, y)
+    dt = time.perf_counter() - t0
+    n = rows * SWEEP_COLS
+    return {"value": n / dt, "unit": "elements/s", "cores": 1, "kind": "port",
+            "sample": f"{rows} rows x {SWEEP_COLS} of the sweep (where/tanh/sigmoid/clip + row sum + argmax), "
+                      "one thread"}
+
+
+def measure_sweep(args, quick: bool = False):
+    """Config 1: z = where(x.gt(0), tanh(x)*sigmoid(y), relu(y).clip(-1,1)),
+    z.sum(-1, keep) and z.argmax(-1) over this rank's [rows, cols] shard
+    (x ~ N(0,1), y ~ U(-3,3)), one fused generated kernel via JAX.jit; no
+    collective (each rank its own rows).  Returns rank 0's result."""
     import torch
     import jax4j_b200 as J
-    torch.cuda.set_device(0)
-    R, Cc = args.rows, args.cols
-    x = J.Random.normal(J.PRNGKey.key(1), J.Shape(R, Cc))
-    y = J.Random.uniform(J.PRNGKey.key(11), J.Shape(R, Cc), -3.0, 3.0)
+    from jax4j_b200 import grad as _g
+    rank, world, _ = _spmd_setup()
+    R, Cc = (SWEEP_ROWS, SWEEP_COLS) if quick else (args.rows, args.cols)
+    x = J.Random.normal(J.PRNGKey.key(1), J.Shape(world * R, Cc), offset=rank * R * Cc,
+                        count=R * Cc).reshape(J.Shape(R, Cc))
+    y = J.Random.uniform(J.PRNGKey.key(11), J.Shape(world * R, Cc), -3.0, 3.0, offset=rank * R * Cc,
+                         count=R * Cc).reshape(J.Shape(R, Cc))
     zero, lo, hi = (J.ConcreteNDArray.scalar(v) for v in (0.0, -1.0, 1.0))
 
     def sweep(xx, yy):
@@ -598,49 +652,50 @@ def run_sweep(args):
         return z.sum(-1, True), z.argmax(-1)
 
     jitted = J.JAX.jit(sweep)
-
-    def step():
-        return jitted(x, y)
-
-    from jax4j_b200 import grad as _g
+    steps = 10 if quick else args.steps
 
     def timed(fused: bool) -> float:
         _g.FUSION = fused
-        for _ in range(args.warmup):
-            step()
-        torch.cuda.synchronize()
-        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-        e0.record()
-        for _ in range(args.steps):
-            step()
-        e1.record()
-        torch.cuda.synchronize()
-        return e0.elapsed_time(e1) / args.steps
+        try:
+            return _timed(lambda: jitted(x, y), steps, max(3, args.warmup), world)
+        finally:
+            _g.FUSION = True
 
     ms_unfused = timed(False)
     ms = timed(True)
-    # the same fused launch replayed from a CUDA graph: device time without
-    # the Python interpreter's per-call cost
+    # the fused launch replayed from a CUDA graph: device time without the
+    # Python interpreter's per-call cost
     graph = torch.cuda.CUDAGraph()
     with torch.cuda.graph(graph):
-        step()
-    for _ in range(args.warmup):
-        graph.replay()
-    torch.cuda.synchronize()
-    g0, g1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-    g0.record()
-    for _ in range(args.steps):
-        graph.replay()
-    g1.record()
-    torch.cuda.synchronize()
-    ms_graph = g0.elapsed_time(g1) / args.steps
+        jitted(x, y)
+    ms_graph = _timed(graph.replay, 5 * steps, 3, world)
+    del graph
     n = R * Cc
-    print(json.dumps({"metric": "elements/s", "value": n / (ms / 1e3), "unit": "elements/s",
-                      "ms_per_step": ms, "ms_per_step_unfused": ms_unfused, "ms_per_step_graph": ms_graph,
-                      "graph_GBps": (8 * n + 8 * R) / (ms_graph / 1e3) / 1e9,
-                      "config": {"workload": f"sweep {R}x{Cc} via JAX.jit"},
-                      "min_bytes_per_step": 8 * n + 8 * R,
-                      "effective_GBps": (8 * n + 8 * R) / (ms / 1e3) / 1e9}), flush=True)
+    min_bytes = 8 * n + 8 * R  # x, y read once; a sum and an argmax per row written
+    if rank != 0:
+        return None
+    peaks = _measured_peaks()
+    gbs = min_bytes / (ms_graph / 1e3) / 1e9
+    out = {"metric": "config-1 sweep elements/s", "value": world * n / (ms_graph / 1e3), "unit": "elements/s",
+           "n_gpus": world, "scaling": "weak", "ms_per_step": ms_graph, "ms_per_step_eager": ms,
+           "ms_per_step_unfused": ms_unfused,
+           "config": {"workload": f"where/tanh/sigmoid/clip + sum(-1) + argmax(-1), [{R},{Cc}] per GPU, "
+                                  "fused (JAX.jit), CUDA graph replay"},
+           "roofline": {"bound": "hbm", "kernel": "generated fused row kernel (fused.cu)", "achieved": gbs,
+                        "peak": peaks.get("hbm_gbs"), "unit": "GB/s",
+                        "frac": gbs / peaks["hbm_gbs"] if peaks.get("hbm_gbs") else None,
+                        "traffic": None, "algorithmic_bytes_per_launch": min_bytes,
+                        "peak_source": f"{peaks.get('source', 'MEASURED_PEAKS.json')} hbm_gbs (copy)"}}
+    if world == 1 and not args.no_cpu_baseline:
+        out["cpu_baseline"] = _sweep_cpu()
+    return out
+
+
+def run_sweep(args):
+    r = measure_sweep(args)
+    if r is not None:
+        print(json.dumps(r), flush=True)
+    _finish(int(os.environ.get("WORLD_SIZE", "1")))
 
 
 def run_fft(args):
@@ -820,17 +875,22 @@ def _finish(world: int):
         distributed.shutdown()
 
 
-def run_cfg0(args):
+def measure_cfg0(args, quick: bool = False):
     """Config 0: 2-layer tanh MLP 784-512-10, x [2,256,784] ~ N(0,1) sharded
     over D = 2 pmap devices (two ranks, or two shards on one GPU).  (i) grad of
-    pmap w.r.t. x; (ii) pmap of gradTree over {W1,b1,W2,b2} + psumTree."""
+    pmap w.r.t. x; (ii) pmap of gradTree over {W1,b1,W2,b2} + psumTree.
+    Each recorded as a CUDA graph and replayed; returns rank 0's result."""
     import torch
     import jax4j_b200 as J
+    from jax4j_b200.graphs import CapturedStep
     rank, world, devices = _spmd_setup()
     if world == 1:
         devices = [J.Device.defaultDevice(), J.Device(None, "shard1")]
+    elif world != 2:
+        return {"note": "config 0 is defined on D = 2 pmap devices; it runs at 1 GPU (two shards) and 2 GPUs"} \
+            if rank == 0 else None
     D = len(devices)
-    dims, B = [784, 512, 10], 256
+    B = 256
     keys = J.Random.split(J.PRNGKey.key(0), 3)
     params = {"w1": J.Random.glorotUniform(keys[0], J.Shape(784, 512), 784, 512),
               "b1": J.ConcreteNDArray.full(J.Shape(512), 0.0),
@@ -842,41 +902,18 @@ def run_cfg0(args):
     t_t.view(2 * B, 10).scatter_(1, lab.view(-1, 1), 1.0)
     t_all = J.ConcreteNDArray._wrap(t_t, J.Shape(2, B, 10), J.DType.FLOAT32, J.Device.defaultDevice())
     if world > 1:
-        x_in = J.LocalShard(J.ConcreteNDArray._wrap(x_all.tensor().view(2, -1)[rank].clone(),
-                                                    J.Shape(B, 784), J.DType.FLOAT32, J.Device.defaultDevice()), D)
-        t_in = J.LocalShard(J.ConcreteNDArray._wrap(t_t.view(2, -1)[rank].clone(), J.Shape(B, 10),
-                                                    J.DType.FLOAT32, J.Device.defaultDevice()), D)
+        xa = J.ConcreteNDArray._wrap(x_all.tensor().view(2, -1)[rank].clone(), J.Shape(B, 784),
+                                     J.DType.FLOAT32, J.Device.defaultDevice())
+        ta = J.ConcreteNDArray._wrap(t_t.view(2, -1)[rank].clone(), J.Shape(B, 10), J.DType.FLOAT32,
+                                     J.Device.defaultDevice())
     else:
-        x_in, t_in = x_all, t_all
+        xa, ta = x_all, t_all
     neg = J.ConcreteNDArray.scalar(-1.0)
 
     def loss_fn(p, xs, ts):
         h = xs.dot(p["w1"]).add(p["b1"]).tanh()
         logits = h.dot(p["w2"]).add(p["b2"])
         return J.Nn.softmax(logits).log().mul(ts).sum(-1).mean().mul(neg)
-
-    def part_i():
-        return J.JAX.grad(lambda xx: J.JAX.pmap(lambda xs, ts: loss_fn(params, xs, ts), devices)(xx, t_in).sum())(
-            x_in)
-
-    def body_ii(xs, ts):
-        v, g = J.JAX.valueAndGradTree(
-            lambda tr: loss_fn({k: tr.children[k].value for k in params}, xs, ts))(J.PyTree.dictOf(params))
-        J.Lax.psumTree(g)
-        return v
-
-    pm = J.JAX.pmap(body_ii, devices)
-
-    def part_ii():
-        return pm(x_in, t_in)
-
-    ms_i = _timed(part_i, args.steps, args.warmup, world)
-    ms_ii = _timed(part_ii, args.steps, args.warmup, world)
-
-    # the same two computations recorded as CUDA graphs and replayed
-    from jax4j_b200.graphs import CapturedStep
-    xa = x_in.local if world > 1 else x_in
-    ta = t_in.local if world > 1 else t_in
 
     def wrap(a, b):
         return (J.LocalShard(a, D), J.LocalShard(b, D)) if world > 1 else (a, b)
@@ -897,30 +934,47 @@ def run_cfg0(args):
 
         return [J.JAX.pmap(body, devices)(xi, ti)] + outs
 
+    steps = 10 if quick else args.steps
+    ms_i = _timed(lambda: fn_i(xa, ta), steps, max(3, args.warmup), world)
+    ms_ii = _timed(lambda: fn_ii(xa, ta), steps, max(3, args.warmup), world)
     cs_i = CapturedStep(fn_i, [xa, ta])
-    gms_i = _timed(cs_i, args.steps * 10, args.warmup, world)
+    gms_i = _timed(cs_i, steps * 10, max(3, args.warmup), world)
     cs_i.release()
     cs_ii = CapturedStep(fn_ii, [xa, ta])
-    gms_ii = _timed(cs_ii, args.steps * 10, args.warmup, world)
+    gms_ii = _timed(cs_ii, steps * 10, max(3, args.warmup), world)
     cs_ii.release()
-    if rank == 0:
-        samples = 2 * B
-        line = {"metric": "config-0 grad-step samples/s", "unit": "samples/s", "n_gpus": world,
-                "config": {"workload": "2-layer tanh MLP 784-512-10, x [2,256,784], D=2 pmap devices"},
-                "grad_wrt_x": {"value": samples / (gms_i / 1e3), "ms_per_step": gms_i,
-                               "eager_ms_per_step": ms_i, "flop_per_sample": 1626112},
-                "grad_tree_psum": {"value": samples / (gms_ii / 1e3), "ms_per_step": gms_ii,
-                                   "eager_ms_per_step": ms_ii, "flop_per_sample": 1636352,
-                                   "psum_floats": 407050},
-                "execution": "CUDA graph replay of the recorded step (eager times beside)",
-                "bound": "latency (launches); eager: host dispatch"}
-        if world == 1 and not args.no_cpu_baseline:
-            line["cpu_baseline"] = _cfg0_cpu()
-        print(json.dumps(line), flush=True)
-    _finish(world)
+    if rank != 0:
+        return None
+    samples = 2 * B
+    peaks = _measured_peaks()
+    flop_ii = 1636352 * samples / (gms_ii / 1e3) / 1e12
+    out = {"metric": "config-0 grad-step samples/s", "value": samples / (gms_ii / 1e3), "unit": "samples/s",
+           "n_gpus": world,
+           "config": {"workload": "2-layer tanh MLP 784-512-10, x [2,256,784], D=2 pmap devices; value = "
+                                  "part (ii) gradTree + psumTree"},
+           "grad_wrt_x": {"value": samples / (gms_i / 1e3), "ms_per_step": gms_i,
+                          "eager_ms_per_step": ms_i, "flop_per_sample": 1626112},
+           "grad_tree_psum": {"value": samples / (gms_ii / 1e3), "ms_per_step": gms_ii,
+                              "eager_ms_per_step": ms_ii, "flop_per_sample": 1636352, "psum_floats": 407050},
+           "execution": "CUDA graph replay of the recorded step (eager times beside)",
+           "roofline": {"bound": "latency", "achieved": flop_ii, "peak": peaks.get("bf16_tflops"),
+                        "unit": "TFLOP/s",
+                        "frac": flop_ii / peaks["bf16_tflops"] if peaks.get("bf16_tflops") else None,
+                        "note": "a 0.8 GFLOP step of 20-odd launches: bound by launch and kernel latency; "
+                                "the tensor fraction is for information"}}
+    if world == 1 and not args.no_cpu_baseline:
+        out["cpu_baseline"] = _cfg0_cpu(reps=2)
+    return out
 
 
-def _cfg0_cpu() -> dict:
+def run_cfg0(args):
+    r = measure_cfg0(args)
+    if r is not None:
+        print(json.dumps(r), flush=True)
+    _finish(int(os.environ.get("WORLD_SIZE", "1")))
+
+
+def _cfg0_cpu(reps: int = 10) -> dict:
     import numpy as np
     from oracle import oracle as orc
     keys = orc.split(0, 3)
@@ -932,22 +986,37 @@ def _cfg0_cpu() -> dict:
     t[np.arange(512), lab] = 1
     t = t.reshape(2, 256, 10)
     threads = orc.nproc()
-    reps = 0
     t0 = time.perf_counter()
-    while time.perf_counter() - t0 < 10.0:
+    for _ in range(reps):
         for d in range(2):  # the two shards, as the reference's pmap runs them
             orc.mlp_loss_grad(ws, bs, x[d], t[d], act="tanh", threads=threads)
-        reps += 1
     dt = time.perf_counter() - t0
     return {"value": 512 * reps / dt, "unit": "samples/s", "cores": threads, "kind": "port",
-            "sample": f"{reps} full steps (both shards, grad over the params)"}
+            "sample": f"{reps} full steps (both shards, grad over the params), row-parallel dot"}
 
 
-def run_cfg2(args):
+def _cfg2_cpu(rows: int = 16) -> dict:
+    """The oracle's sequential-k dot on `rows` rows of a shard's product,
+    row-parallel over all host threads (the reference's CPU-N matmul)."""
+    from oracle import oracle as orc
+    K, N = 8192, 4096
+    a = orc.uniform(2, (rows * K,), -1.0, 1.0).reshape(rows, K)
+    b = orc.uniform(orc.split(2, 2)[1], (K * N,), -1.0, 1.0).reshape(K, N)
+    threads = orc.nproc()
+    t0 = time.perf_counter()
+    orc.dot(a, b, threads=threads)
+    dt = time.perf_counter() - t0
+    return {"value": 2.0 * rows * K * N / dt / 1e12, "unit": "TFLOP/s", "cores": threads, "kind": "port",
+            "sample": f"{rows} rows of a shard's [4096,8192].[8192,4096] product, row-parallel dot"}
+
+
+def measure_cfg2(args, quick: bool = False):
     """Config 2: each shard computes A_i [4096,8192] . B [8192,4096]
     (A ~ U(-1,1) sharded on the leading axis, B replicated, seed 2) and the
-    results are gathered with Lax.allGather."""
+    results are gathered with Lax.allGather.  Returns rank 0's result."""
     import jax4j_b200 as J
+    from jax4j_b200 import core
+    from jax4j_b200.core import split_kind
     rank, world, devices = _spmd_setup()
     D = len(devices)
     M, K, N = 4096, 8192, 4096
@@ -956,41 +1025,87 @@ def run_cfg2(args):
     B = J.Random.uniform(J.Random.split(J.PRNGKey.key(2), 2)[1], J.Shape(K, N), -1.0, 1.0)
     a_in = J.LocalShard(A, D) if world > 1 else A.reshape(J.Shape(1, M, K))
     pm = J.JAX.pmap(lambda a: J.Lax.allGather(a.dot(B), D), devices)
+    steps = 10 if quick else args.steps
+    core.DOT_TIMING = []
+    ms = _timed(lambda: pm(a_in), steps, max(3, args.warmup), world)
+    dots = core.DOT_TIMING[-steps:]
+    core.DOT_TIMING = None
+    gemm_ms = sum(a.elapsed_time(b) for a, b, _, _ in dots) / max(1, len(dots))
+    if rank != 0:
+        return None
+    flop = 2.0 * M * K * N
+    peaks = _measured_peaks()
+    f16 = split_kind() == 1
+    peak, src = _tensor_peak(peaks, ms * steps / 1e3)
+    ach = flop / (gemm_ms / 1e3) / 1e12
+    mma_peak = peak if f16 else peak / 2
+    out = {"metric": "config-2 pmap dot + allGather TFLOP/s", "unit": "TFLOP/s",
+           "value": D * flop / (ms / 1e3) / 1e12, "ms_per_step": ms, "n_gpus": world, "scaling": "weak",
+           "config": {"workload": "per shard [4096,8192].[8192,4096] FP32 (tensor-core split GEMM, "
+                                  + ("3xFP16" if f16 else "3xTF32") + "), allGather of the [4096,4096] results"},
+           "allgather_bytes_per_rank": 4 * M * N,
+           "roofline": {"bound": "tensor", "kernel": "dot (gemm_3xtf32_kernel)", "achieved": ach, "peak": peak,
+                        "unit": "TFLOP/s", "frac": ach / peak, "peak_source": src, "gemm_ms": gemm_ms,
+                        "mma_issued": {"kind": "f16" if f16 else "tf32", "achieved": 3 * ach, "peak": mma_peak,
+                                       "frac": 3 * ach / mma_peak}}}
+    if world == 1 and not args.no_cpu_baseline:
+        out["cpu_baseline"] = _cfg2_cpu()
+    return out
 
-    def step():
-        return pm(a_in)
 
-    ms = _timed(step, args.steps, args.warmup, world)
-    if rank == 0:
-        flop = 2.0 * M * K * N * D
-        print(json.dumps({"metric": "config-2 pmap dot + allGather TFLOP/s", "unit": "TFLOP/s",
-                          "value": flop / (ms / 1e3) / 1e12, "ms_per_step": ms, "n_gpus": world,
-                          "config": {"workload": "per shard [4096,8192].[8192,4096] FP32 (tensor-core split "
-                                                 "GEMM), allGather of the [4096,4096] results"},
-                          "allgather_bytes_per_rank": 4 * M * N}), flush=True)
-    _finish(world)
+def run_cfg2(args):
+    r = measure_cfg2(args)
+    if r is not None:
+        print(json.dumps(r), flush=True)
+    _finish(int(os.environ.get("WORLD_SIZE", "1")))
 
 
-def run_collectives(args):
-    """Config 3: Lax.psum / Lax.allGather of float32 vectors ~ N(0,1), 4 KB to
-    1 GB per rank.  Reports NCCL-convention bus GB/s for the raw device
-    collective (back-to-back on the stream) and per call through JAX.pmap,
-    plus grad through psum (its VJP is a psum) at 64 MB."""
+PEER_COPY_GBS = 770.0  # measured NVLink peer copy per direction on this pool's B200s
+
+
+def _collective_cpu(mb: int = 64, D: int = 8) -> dict:
+    """The reference's in-process psum (SharedCollective.psum: each of the D
+    shard threads sums all D slots in slot order) restated by the oracle,
+    on D slots of `mb` MB."""
+    import numpy as np
+    from oracle import oracle as orc
+    n = (mb << 20) // 4
+    slots = [np.full(n, float(i + 1), np.float32) for i in range(D)]
+    t0 = time.perf_counter()
+    orc.psum(slots)
+    dt = time.perf_counter() - t0
+    return {"value": (n * 4) / dt * 2 * (D - 1) / D / 1e9, "unit": "GB/s", "cores": 1, "kind": "port",
+            "sample": f"psum over {D} slots of {mb} MB (one shard's thread), reported in the NCCL bus-bandwidth "
+                      "convention"}
+
+
+def measure_collectives(args, sizes=None):
+    """Config 3: Lax.psum / Lax.allGather of float32 vectors ~ N(0,1) per
+    rank.  Reports NCCL-convention bus GB/s for the raw device collective
+    (back-to-back on the stream) and per call through JAX.pmap, plus grad
+    through psum (its VJP is a psum) at 64 MB.  Returns rank 0's result."""
     import torch
     import jax4j_b200 as J
     from jax4j_b200 import _lib, distributed
     rank, world, devices = _spmd_setup()
     D = len(devices)
     if D == 1:
-        if rank == 0:
-            print(json.dumps({"metric": "psum bus GB/s", "n_gpus": 1,
-                              "note": "a collective over one device moves no data; run with --gpus >= 2"}))
-        return
+        if rank != 0:
+            return None
+        out = {"metric": "psum bus GB/s", "n_gpus": 1,
+               "note": "a collective over one device moves no data; measured at N >= 2"}
+        if not args.no_cpu_baseline:
+            out["cpu_baseline"] = _collective_cpu()
+        return out
     comm = distributed.state().comm
     stream = torch.cuda.current_stream().cuda_stream
+    if sizes is None:
+        sizes, size = [], 4096
+        while size <= args.max_bytes:
+            sizes.append(size)
+            size *= 4
     rows = []
-    size = 4096
-    while size <= args.max_bytes:
+    for size in sizes:
         n = size // 4
         x = J.Random.normal(J.PRNGKey.key(4), J.Shape(n), offset=rank * n, count=n)
         out = torch.empty(n, dtype=torch.float32, device="cuda")
@@ -1008,20 +1123,49 @@ def run_collectives(args):
                      "allgather_busbw_GBps": size * D / (ag_ms / 1e3) * (D - 1) / D / 1e9,
                      "pmap_psum_ms": api_ms})
         del x, out, gat
-        size *= 4
     n = (64 << 20) // 4
     x = J.Random.normal(J.PRNGKey.key(5), J.Shape(n), offset=rank * n, count=n)
     gpm = J.JAX.pmap(lambda s: J.JAX.grad(lambda v: J.Lax.psum(v.mul(v)).sum())(s), devices)
     grad_ms = _timed(lambda: gpm(J.LocalShard(x, D)), 5, 2, world)
-    if rank == 0:
-        peak = max(r["allreduce_busbw_GBps"] for r in rows)
-        print(json.dumps({"metric": "psum bus GB/s", "value": peak, "unit": "GB/s", "n_gpus": D,
-                          "config": {"workload": "Lax.psum / Lax.allGather, float32, 4 KB..%d MB per rank"
-                                                 % (args.max_bytes >> 20)},
-                          "sizes": rows, "grad_through_psum_64MB_ms": grad_ms,
-                          "peak_source": "NCCL busBW convention: allreduce (S/t)*2(D-1)/D, "
-                                         "allgather (D*S/t)*(D-1)/D"}), flush=True)
-    _finish(world)
+    del x
+    if rank != 0:
+        return None
+    at64 = next((r for r in rows if r["bytes"] == 64 << 20), rows[-1])
+    return {"metric": "psum bus GB/s", "value": at64["allreduce_busbw_GBps"], "unit": "GB/s", "n_gpus": D,
+            "config": {"workload": "Lax.psum / Lax.allGather, float32, per rank: "
+                                   + ", ".join(f"{r['bytes'] >> 20} MB" if r["bytes"] >= 1 << 20
+                                               else f"{r['bytes'] >> 10} KB" for r in rows)
+                                   + "; value = all-reduce bus GB/s at %d MB" % (at64["bytes"] >> 20)},
+            "sizes": rows, "grad_through_psum_64MB_ms": grad_ms,
+            "roofline": {"bound": "nvlink", "achieved": at64["allreduce_busbw_GBps"], "peak": PEER_COPY_GBS,
+                         "unit": "GB/s", "frac": at64["allreduce_busbw_GBps"] / PEER_COPY_GBS,
+                         "peak_source": "measured NVLink peer copy per direction on this pool's B200s "
+                                        "(NCCL bus-bandwidth convention: allreduce (S/t)*2(D-1)/D, "
+                                        "allgather (D*S/t)*(D-1)/D)"}}
+
+
+def run_collectives(args):
+    r = measure_collectives(args)
+    if r is not None:
+        print(json.dumps(r), flush=True)
+    _finish(int(os.environ.get("WORLD_SIZE", "1")))
+
+
+def measure_secondary(args) -> dict:
+    """Configurations 0-3 beside the headline, a few seconds each: config 0
+    samples/s, the config-1 fused sweep against HBM, the config-2 dot against
+    the tensor peak, and at N >= 2 psum / allGather bus GB/s at 64 MB,
+    256 MB and 1 GB.  Every rank runs them; rank 0 gets the results."""
+    out = {}
+    for name, fn in (("cfg0", lambda: measure_cfg0(args, quick=True)),
+                     ("cfg1_sweep", lambda: measure_sweep(args, quick=True)),
+                     ("cfg2", lambda: measure_cfg2(args, quick=True)),
+                     ("cfg3_collectives", lambda: measure_collectives(args, sizes=[64 << 20, 256 << 20, 1 << 30]))):
+        try:
+            out[name] = fn()
+        except Exception as e:  # noqa: BLE001 - one failed side measurement must not lose the headline
+            out[name] = {"error": f"{type(e).__name__}: {str(e)[:300]}"}
+    return out
 
 
 def main():
