@@ -23,13 +23,14 @@
 //     shared-memory ring; warp 1 lane 0 issues
 //     tcgen05.mma.kind::tf32 (M=128, N=BN, K=8) and tcgen05.commit's the
 //     ring slots back; warps 2..9 accumulate and store C.
-//  Promotion: the tensor core's FP32 accumulation does not round to nearest,
-//  so its error grows linearly with the number of accumulating MMAs.  The
-//  K loop is therefore cut into chunks of CHUNK_KB k-blocks; each chunk's
-//  partial product goes to one of two TMEM buffers, and the epilogue warps
-//  add it into FP32 registers with round-to-nearest while the MMA warp
-//  fills the other buffer.  The error then grows with sqrt(K) like an FP32
-//  sum.
+//  Promotion: the tensor core's FP32 accumulation does not round to nearest
+//  (it truncates), so its error grows linearly with the number of
+//  accumulating MMAs and is biased toward zero.  The K loop is therefore cut
+//  into chunks (Cfg::CHUNK_KB, CHUNK2_KB); each chunk's partial product goes
+//  to one of two TMEM buffers, and the epilogue warps add it into FP32
+//  registers with round-to-nearest while the MMA warp fills the other
+//  buffer.  The error then grows with sqrt(K) like an FP32 sum, plus a
+//  relative bias of about 3.6e-8 per MMA of a chunk (-1.6e-6 for 3xFP16).
 //  Split mode 3xFP16 (the default; J4C_GEMM_SPLIT=tf32 selects 3xTF32): the
 //  same three products from FP16 operands, at twice the tensor rate of TF32.
 //  FP16 has TF32's 11-bit significand but a 5-bit exponent, so every line of
@@ -67,7 +68,14 @@ namespace j4c {
 namespace tc {
 
 constexpr int BM = 128;           // rows of a CTA tile (TMEM lanes)
-constexpr int CHUNK_K = 256;      // K accumulated in TMEM before promotion (3xTF32; 512 for 3xFP16)
+// K accumulated in TMEM before promotion: the first two chunks of a work
+// unit, then the rest (see Cfg).
+// Measured on a B200 (positive operands, where the truncation bias cannot
+// cancel): 3xFP16 with 512-deep chunks -3.4e-6 relative at 448 TFLOP/s
+// (4096^3), 256-deep -1.6e-6 at 431, 128-deep -0.7e-6 at 400; 3xTF32 at K =
+// 8192 -2.3e-6 (256 throughout) and -1.4e-6 (256 then 128) at the same speed.
+constexpr int CHUNK_F16_FIRST = 256, CHUNK_F16_REST = 256;
+constexpr int CHUNK_TF32_FIRST = 256, CHUNK_TF32_REST = 128;
 constexpr int kEpiWarps = 8;      // two warps per TMEM lane quadrant
 constexpr int kThreads = 64 + 32 * kEpiWarps;
 constexpr int kStatusTimeout = 0x7C05;
@@ -115,10 +123,13 @@ template <int BN, int STAGES, int BK, bool F16 = false>
 struct Cfg {
     static_assert(BK == 32 || BK == 16, "BK is 32 (SW128) or 16 (SW64)");
     static constexpr int BKE = BK * 4 / Elt<F16>::SIZE;
-    // FP16 MMAs take half the time of TF32 ones per K, so the FP16 chunk is
-    // twice as deep: the same number of MMAs accumulate in TMEM either way,
-    // and the epilogue keeps a chunk's worth of MMA time to store a tile.
-    static constexpr int CHUNK_KB = (F16 ? 2 * CHUNK_K : CHUNK_K) / BKE;
+    // Promotion chunks: the first two of a work unit are CHUNK_KB k-blocks
+    // deep -- while the MMAs fill them the epilogue warps are still storing
+    // the previous tile, so they must last as long as that store -- and the
+    // rest CHUNK2_KB, shorter, since the tensor core's truncating accumulation
+    // biases a partial sum toward zero by about 3.6e-8 per MMA it adds.
+    static constexpr int CHUNK_KB = (F16 ? CHUNK_F16_FIRST : CHUNK_TF32_FIRST) / BKE;
+    static constexpr int CHUNK2_KB = (F16 ? CHUNK_F16_REST : CHUNK_TF32_REST) / BKE;
     static constexpr int A_BYTES = BM * BK * 4;
     static constexpr int B_BYTES = BN * BK * 4;
     static constexpr int MN_BOX_BYTES = 128 * BKE;  // one MN-major column block (BKE rows x 128 B)
@@ -476,7 +487,8 @@ gemm_3xtf32_kernel(const __grid_constant__ CUtensorMap tAh, const __grid_constan
                    const SplitHeader *__restrict__ ahdr, const SplitHeader *__restrict__ bhdr) {
     using Q = Cfg<BN, STAGES, BK, F16>;
     constexpr int UMMA_K = Elt<F16>::UMMA_K;
-    constexpr int CHUNK_KB = Q::CHUNK_KB;
+    // end of chunk n of a unit that starts at k-block kb0 and ends at end
+    auto chunk_end = [](int kb0, int n, int end) { return min(end, kb0 + (n < 2 ? Q::CHUNK_KB : Q::CHUNK2_KB)); };
     {
         // What the operands' splits say, the same for every thread: a split
         // must match its use (under 3xFP16 its lines are the rows of a
@@ -586,7 +598,7 @@ gemm_3xtf32_kernel(const __grid_constant__ CUtensorMap tAh, const __grid_constan
             bool ok = true;
             for (int u = blockIdx.x; ok && u < num_units; u += gridDim.x) {
                 const Unit w = unit_of(u, full_tiles, splits, num_kb);
-                for (int kb0 = w.kb0; ok && kb0 < w.kb1; kb0 += CHUNK_KB, ci++) {
+                for (int kb0 = w.kb0, n = 0; ok && kb0 < w.kb1; kb0 = chunk_end(kb0, n, w.kb1), n++, ci++) {
                     const int buf = ci & 1;
                     const uint32_t bph = (ci >> 1) & 1;
                     if (!wait_bar(smem_u32(&ctl->tempty[buf]), bph ^ 1, abort, status, true, wait_ns)) {
@@ -595,7 +607,7 @@ gemm_3xtf32_kernel(const __grid_constant__ CUtensorMap tAh, const __grid_constan
                     }
                     tc_fence_after();
                     const uint32_t dcol = tmem + buf * BN;
-                    const int kb1 = min(w.kb1, kb0 + CHUNK_KB);
+                    const int kb1 = chunk_end(kb0, n, w.kb1);
                     for (int kb = kb0; kb < kb1; kb++) {
                         if (!wait_bar(smem_u32(&ctl->full[stage]), phase, abort, status, true, wait_ns)) {
                             ok = false;
@@ -656,7 +668,7 @@ gemm_3xtf32_kernel(const __grid_constant__ CUtensorMap tAh, const __grid_constan
             float acc[Q::COLS_PER_WARP];
 #pragma unroll
             for (int j = 0; j < Q::COLS_PER_WARP; j++) acc[j] = 0.0f;
-            for (int kb0 = w.kb0; kb0 < w.kb1; kb0 += CHUNK_KB, ci++) {
+            for (int kb0 = w.kb0, n = 0; kb0 < w.kb1; kb0 = chunk_end(kb0, n, w.kb1), n++, ci++) {
                 const int buf = ci & 1;
                 const uint32_t bph = (ci >> 1) & 1;
                 if (!wait_bar(smem_u32(&ctl->tfull[buf]), bph, abort, status, true, wait_ns)) {

@@ -205,3 +205,136 @@ def test_all_gather_vjp_modes(J, mode, factor):
     finally:
         P.ALLGATHER_VJP = old
     np.testing.assert_allclose(g, factor * c, rtol=1e-6)
+
+
+def test_headline_grad_step_full_batch_8192(J):
+    """Config 4 at the size the benchmark times: one data-parallel grad step
+    of the 1024-4096-4096-4096-1000 relu MLP at batch 8192 on one GPU, with
+    the benchmark's seeds (Glorot weights from key 3, x ~ N(0,1) from key 1,
+    labels from key 2).  The loss, every bias gradient and every weight
+    gradient in full against the oracle's restatement of the reference's
+    host step (all host threads; about a minute of CPU), and against an FP64
+    computation of the same step."""
+    import torch
+    dims, B, D = [1024, 4096, 4096, 4096, 1000], 8192, 1
+    params = make_mlp(J, dims, 3)
+    x = J.Random.normal(J.PRNGKey.key(1), J.Shape(D, B, dims[0]))
+    u = J.Random.uniform(J.PRNGKey.key(2), J.Shape(D * B))
+    labels = np.minimum((u.numpy() * dims[-1]).astype(np.int64), dims[-1] - 1)
+    t_host = onehot(labels, dims[-1]).reshape(D, B, dims[-1])
+    t = J.ConcreteNDArray.of(t_host)
+    loss = mlp_loss(J, "relu")
+    out = {}
+
+    def body(xs, ts):
+        v, g = J.JAX.valueAndGradTree(lambda p: loss(p, xs, ts))(params)
+        out["g"] = J.Lax.psumTree(g)
+        return v
+
+    losses = J.JAX.pmap(body, [J.Device.defaultDevice()])(x, t).toFloatArray()
+    torch.cuda.synchronize()
+    ws, bs = host_params(params)
+    xh = x.numpy()[0]
+    masks = relu_masks(J, params, J.ConcreteNDArray.of(xh), xh, "relu")
+    ref_loss, ref_gw, ref_gb, _ = orc.mlp_loss_grad(ws, bs, xh, t_host[0], act="relu", threads=orc.nproc(),
+                                                    relu_masks=masks)
+    assert abs(losses[0] - ref_loss) <= TOL_REDUCTION * abs(ref_loss), (losses[0], ref_loss)
+    g = out["g"].children
+    exact_w, exact_b = _mlp_grads_fp64(ws, bs, xh, t_host[0], masks)
+    for l in range(len(ws)):
+        _assert_grad(g[f"b{l + 1}"].value.numpy(), ref_gb[l], exact_b[l], f"db{l + 1}")
+        _assert_grad(g[f"w{l + 1}"].value.numpy(), ref_gw[l], exact_w[l], f"dW{l + 1}")
+
+
+def _mlp_grads_fp64(ws, bs, x, onehot_t, masks):
+    """The relu MLP's softmax cross-entropy gradients in FP64 (numpy), with
+    the given relu masks: the exact values the FP32 computations round."""
+    W = [w.astype(np.float64) for w in ws]
+    acts, a = [], x.astype(np.float64)
+    for l in range(len(W) - 1):
+        acts.append(a)
+        a = (a @ W[l] + bs[l]) * masks[l]
+    acts.append(a)
+    logits = a @ W[-1] + bs[-1]
+    e = np.exp(logits)
+    g = (e / e.sum(-1, keepdims=True) - onehot_t) / x.shape[0]
+    gw, gb = [None] * len(W), [None] * len(W)
+    for l in range(len(W) - 1, -1, -1):
+        gw[l] = acts[l].T @ g
+        gb[l] = g.sum(0)
+        if l:
+            g = (g @ W[l].T) * masks[l - 1]
+    return gw, gb
+
+
+def _assert_grad(got, ref, exact, what):
+    """The device gradient against the oracle's at the reductions tolerance
+    (per tensor) on all but at most one element in a million -- at a batch
+    of 8192 the reference's own sequential FP32 sums carry errors of the
+    order of the tolerance on a few elements of heavy cancellation -- and
+    the device's worst error against the exact (FP64) gradient within 4
+    times the reference's own worst error, or 10 times inside the tolerance,
+    both relative to the gradient's rms."""
+    got, ref, exact = (np.asarray(v, np.float64) for v in (got, ref, exact))
+    rms = float(np.sqrt(np.mean(ref * ref)))
+    beyond = np.abs(got - ref) > TOL_REDUCTION * np.maximum(np.abs(ref), rms)
+    assert beyond.sum() <= max(1, got.size // 1_000_000), (what, int(beyond.sum()))
+    e_dev = float(np.max(np.abs(got - exact))) / rms
+    e_ref = float(np.max(np.abs(ref - exact))) / rms
+    assert e_dev <= max(4 * e_ref, TOL_REDUCTION / 10), (what, e_dev, e_ref)
+
+
+def _config0_inputs(J):
+    """Config 0 exactly as the benchmark builds it: W1 [784,512], W2 [512,10]
+    Glorot from keys split from key 0, zero biases, x [2,256,784] ~ N(0,1)
+    from key 0, labels (int)(u * 10) from the third split key."""
+    keys = J.Random.split(J.PRNGKey.key(0), 3)
+    params = {"w1": J.Random.glorotUniform(keys[0], J.Shape(784, 512), 784, 512),
+              "b1": J.ConcreteNDArray.full(J.Shape(512), 0.0),
+              "w2": J.Random.glorotUniform(keys[1], J.Shape(512, 10), 512, 10),
+              "b2": J.ConcreteNDArray.full(J.Shape(10), 0.0)}
+    x = J.Random.normal(J.PRNGKey.key(0), J.Shape(2, 256, 784))
+    labels = np.minimum((J.Random.uniform(keys[2], J.Shape(512)).numpy() * 10).astype(np.int64), 9)
+    t_host = onehot(labels, 10).reshape(2, 256, 10)
+    return params, x, t_host
+
+
+def test_config0_full_size_both_parts(J):
+    """Config 0 at its full size, x [2,256,784] over two pmap shards on one
+    GPU: (i) the gradient of pmap(loss).sum() w.r.t. x, per shard; (ii) pmap
+    of gradTree over {W1,b1,W2,b2} with psumTree -- against the oracle."""
+    params, x, t_host = _config0_inputs(J)
+    t = J.ConcreteNDArray.of(t_host)
+    devices = [J.Device.defaultDevice(), J.Device(None, "shard1")]
+    neg = J.ConcreteNDArray.scalar(-1.0)
+
+    def loss_fn(p, xs, ts):
+        h = xs.dot(p["w1"]).add(p["b1"]).tanh()
+        logits = h.dot(p["w2"]).add(p["b2"])
+        return J.Nn.softmax(logits).log().mul(ts).sum(-1).mean().mul(neg)
+
+    gx = J.JAX.grad(lambda xx: J.JAX.pmap(lambda xs, ts: loss_fn(params, xs, ts), devices)(xx, t).sum())(x)
+    out = {}
+
+    def body(xs, ts):
+        v, g = J.JAX.valueAndGradTree(
+            lambda tr: loss_fn({k: tr.children[k].value for k in params}, xs, ts))(J.PyTree.dictOf(params))
+        out[id(xs.device())] = J.Lax.psumTree(g)
+        return v
+
+    losses = J.JAX.pmap(body, devices)(x, t).toFloatArray()
+    ws = [params["w1"].numpy(), params["w2"].numpy()]
+    bs = [params["b1"].numpy(), params["b2"].numpy()]
+    xh = x.numpy()
+    per = [orc.mlp_loss_grad(ws, bs, xh[i], t_host[i], act="tanh", want_gx=True, threads=orc.nproc())
+           for i in range(2)]
+    gxh = gx.numpy()
+    for i in range(2):
+        assert abs(losses[i] - per[i][0]) <= TOL_REDUCTION * abs(per[i][0])
+        assert_rel(gxh[i], per[i][3], TOL_REDUCTION, f"(i) dL/dx shard {i}")
+    for g in out.values():  # every shard holds the same psum
+        c = g.children
+        for l, k in enumerate(("w1", "w2")):
+            assert_rel(c[k].value.numpy(), orc.psum([per[0][1][l], per[1][1][l]]), TOL_REDUCTION, f"(ii) d{k}")
+        for l, k in enumerate(("b1", "b2")):
+            assert_rel(c[k].value.numpy(), orc.psum([per[0][2][l], per[1][2][l]]), TOL_REDUCTION, f"(ii) d{k}")
