@@ -398,6 +398,19 @@ J4C_API int j4c_dot_split_ep_max(const float *a_hi, const float *a_lo, const flo
                                  float *c, int64_t M, int64_t K, int64_t N, int trans_a, int trans_b,
                                  const float *bias, const float *mask, float *act, uint32_t *out_lines,
                                  j4c_stream stream);
+/* j4c_dot_split_ep_max with relu bits (Grad.reluGrad, api/Grad.java:585-598,
+ * fed by bits instead of a float array): act_bits (may be NULL; needs act)
+ * receives one bit per element of act, set where act > 0 -- bit c & 31 of
+ * word c / 32 of each of the M rows of ceil(N / 32) uint32 words -- and
+ * mask_bits (may be NULL; not with mask) masks C by such bits (C = bit ?
+ * C : 0, as mask > 0 does).  1/32 of the bytes of the float mask.  Bits need
+ * the form that stores C untransposed: trans_b = 1 (for A . B, pass B's
+ * transposed split) or trans_a = 1; with trans_a = trans_b = 0 they are
+ * rejected (J4C_E_INVALID). */
+J4C_API int j4c_dot_split_ep_bits(const float *a_hi, const float *a_lo, const float *b_hi, const float *b_lo,
+                                  float *c, int64_t M, int64_t K, int64_t N, int trans_a, int trans_b,
+                                  const float *bias, const float *mask, const uint32_t *mask_bits, float *act,
+                                  uint32_t *act_bits, uint32_t *out_lines, j4c_stream stream);
 
 /* ------------------------------------------------------------------ */
 /* Discrete Fourier transforms: replace api/Fft.java's radix-2 host     */

@@ -89,6 +89,7 @@ SIGNATURES = {
     "j4c_split_floats": [I64, I64],
     "j4c_set_wait_limit_ns": [C.c_uint64, C.POINTER(C.c_uint64)],
     "j4c_dot_split_ep_max": [P, P, P, P, P, I64, I64, I64, I32, I32, P, P, P, P, P],
+    "j4c_dot_split_ep_bits": [P, P, P, P, P, I64, I64, I64, I32, I32, P, P, P, P, P, P, P],
     "j4c_fft": [I32, I32, PI64, P, P, P, P, I32, P],
     "j4c_rfft": [I32, I32, PI64, P, P, P, P],
     "j4c_irfft": [I32, I32, PI64, P, P, P, P],

@@ -385,7 +385,7 @@ class ConcreteNDArray(NDArray):
     kind) once it has been a dot operand, for the other dots it takes part in.
     """
 
-    __slots__ = ("_t", "_shape", "_dtype", "_device", "_split", "_ready", "_lines")
+    __slots__ = ("_t", "_shape", "_dtype", "_device", "_split", "_ready", "_lines", "_relu_bits")
 
     def __init__(self, data, shape=None, dtype: DType = None, device: Device = None):
         if device is None:
@@ -422,6 +422,7 @@ class ConcreteNDArray(NDArray):
         self._split = None  # {kind: (hi, lo)}: "r" row lines, "c" column lines, "t" transposed
         self._ready = None  # CUDA event recorded once the value was produced, when tracked
         self._lines = None  # device words [rows + cols + 1]: line maxima (bits of max finite |x|), NaN/Inf flag
+        self._relu_bits = None  # a relu output's x > 0 as bits (rows of ceil(cols / 32) words), from its GEMM
 
     # ---- construction helpers ----
     @staticmethod
@@ -453,6 +454,7 @@ class ConcreteNDArray(NDArray):
         obj._split = None
         obj._ready = None
         obj._lines = None
+        obj._relu_bits = None
         return obj
 
     def _new(self, shape: Shape, dtype: DType) -> torch.Tensor:
@@ -745,6 +747,10 @@ def _dtype_of_numpy(arr: np.ndarray) -> DType:
 # epilogue's bias and mask read once.
 DOT_TIMING = None
 
+# The relu' mask of an input gradient read as the bits the forward GEMM left
+# (1/32 of the bytes of the float relu output).
+RELU_BITS = True
+
 
 _SPLIT_KIND = None
 
@@ -853,6 +859,7 @@ def _dot_raw(a: "ConcreteNDArray", b: "ConcreteNDArray", trans_a: bool, trans_b:
     act_out = torch.empty(M * N, dtype=a._dtype.torch, device=a._t.device) if act else None
     timing = DOT_TIMING
     out_max = None
+    act_bits = None
     if a._dtype == DType.FLOAT32 and M and N and K:
         # tensor-core path: each operand's 3xTF32 split is made once per array.
         # With K the leading dimension of both stored operands (A^T . B, the
@@ -860,7 +867,10 @@ def _dot_raw(a: "ConcreteNDArray", b: "ConcreteNDArray", trans_a: bool, trans_b:
         # smaller one, so the extra split pass is as short as possible.
         # The split kind follows how the GEMM reads an operand: op(A) = A and
         # op(B) = B^T K-major (row lines), op(A) = A^T and op(B) = B MN-major
-        # (column lines).
+        # (column lines), or a transposed split read K-major.  Both operands
+        # K-major is the fastest form, so B [K, N] goes in transposed for
+        # A . B; with K leading in both stored operands (A^T . B, the weight
+        # gradient) the smaller one goes in transposed.
         ta, tb = trans_a, trans_b
         if ta and not tb:
             if a._shape.size() < b._shape.size():
@@ -869,6 +879,9 @@ def _dot_raw(a: "ConcreteNDArray", b: "ConcreteNDArray", trans_a: bool, trans_b:
             else:
                 ah, al = _split_of(a, "c")
                 (bh, bl), tb = _split_of(b, "t"), True
+        elif not ta and not tb:
+            ah, al = _split_of(a, "r")
+            (bh, bl), tb = _split_of(b, "t"), True
         else:
             ah, al = _split_of(a, "c" if ta else "r")
             bh, bl = _split_of(b, "r" if tb else "c")
@@ -878,14 +891,22 @@ def _dot_raw(a: "ConcreteNDArray", b: "ConcreteNDArray", trans_a: bool, trans_b:
             ev0.record()
         if epilogue:
             # the epilogue also takes the line maxima of the output a later split
-            # will read (the relu output, or C), sparing it a max pass
+            # will read (the relu output, or C), sparing it a max pass; a relu
+            # output leaves its x > 0 bits, and a mask that has them is read as
+            # bits (C stored untransposed: not the K-major A . MN-major B form)
             out_max = torch.empty(M + N + 1, dtype=torch.int32, device=a._t.device)
-            call("j4c_dot_split_ep_max", ah.data_ptr(), al.data_ptr(), bh.data_ptr(), bl.data_ptr(),
+            bits_ok = bool(ta or tb) and RELU_BITS
+            mask_bits = mask._relu_bits if (mask is not None and bits_ok) else None
+            act_bits = (torch.empty(M * ((N + 31) // 32), dtype=torch.int32, device=a._t.device)
+                        if act and bits_ok else None)
+            call("j4c_dot_split_ep_bits", ah.data_ptr(), al.data_ptr(), bh.data_ptr(), bl.data_ptr(),
                  out.data_ptr() if store_c else None,
                  M, K, N, int(ta), int(tb), bias.data_ptr() if bias is not None else None,
-                 mask.data_ptr() if mask is not None else None,
+                 mask.data_ptr() if (mask is not None and mask_bits is None) else None,
+                 mask_bits.data_ptr() if mask_bits is not None else None,
                  act_out.data_ptr() if act_out is not None else None,
-                 out_max.data_ptr() if out_max is not None else None, a._stream())
+                 act_bits.data_ptr() if act_bits is not None else None,
+                 out_max.data_ptr(), a._stream())
         else:
             call("j4c_dot_split", ah.data_ptr(), al.data_ptr(), bh.data_ptr(), bl.data_ptr(), out.data_ptr(),
                  M, K, N, int(ta), int(tb), a._stream())
@@ -912,6 +933,8 @@ def _dot_raw(a: "ConcreteNDArray", b: "ConcreteNDArray", trans_a: bool, trans_b:
         h = ConcreteNDArray._wrap(act_out, Shape(M, N), a._dtype, device)
         if out_max is not None:
             h._lines = out_max
+        if act_bits is not None:
+            h._relu_bits = act_bits
         return c, h
     if out_max is not None:
         c._lines = out_max

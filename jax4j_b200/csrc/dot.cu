@@ -21,7 +21,8 @@ int tc_split_lines(const float *x, int64_t rows, int64_t cols, uint32_t *lines, 
 int tc_gemm_presplit(const float *ah, const float *al, const float *bh, const float *bl, float *c, int64_t M,
                      int64_t K, int64_t N, int trans_a, int trans_b, const float *bias, const float *mask,
                      float *act, int64_t batch, int a_batched, int b_batched, cudaStream_t s,
-                     uint32_t *out_lines = nullptr);
+                     uint32_t *out_lines = nullptr, const uint32_t *mask_bits = nullptr,
+                     uint32_t *act_bits = nullptr);
 }  // namespace j4c
 
 using namespace j4c;
@@ -119,17 +120,19 @@ int j4c_split_lines(const float *x, int64_t rows, int64_t cols, uint32_t *lines,
     return tc_split_lines(x, rows, cols, lines, as_stream(stream));
 }
 
-int j4c_dot_split_ep_max(const float *a_hi, const float *a_lo, const float *b_hi, const float *b_lo, float *c,
-                         int64_t M, int64_t K, int64_t N, int trans_a, int trans_b, const float *bias,
-                         const float *mask, float *act, uint32_t *out_lines, j4c_stream stream) {
+int j4c_dot_split_ep_bits(const float *a_hi, const float *a_lo, const float *b_hi, const float *b_lo, float *c,
+                          int64_t M, int64_t K, int64_t N, int trans_a, int trans_b, const float *bias,
+                          const float *mask, const uint32_t *mask_bits, float *act, uint32_t *act_bits,
+                          uint32_t *out_lines, j4c_stream stream) {
     J4C_REQUIRE(M >= 0 && K >= 0 && N >= 0, "j4c_dot_split: negative dimension");
+    J4C_REQUIRE(!(mask && mask_bits), "j4c_dot_split_ep_bits: the mask as floats or as bits, not both");
     cudaStream_t s = as_stream(stream);
     if (M == 0 || N == 0) {
         if (out_lines) J4C_CUDA(cudaMemsetAsync(out_lines, 0, (size_t)(M + N + 1) * sizeof(uint32_t), s));
         return J4C_OK;
     }
     J4C_REQUIRE(c || act, "j4c_dot_split: NULL output");
-    J4C_REQUIRE(K > 0 || (!bias && !mask && !act), "j4c_dot_split_ep: K = 0 with an epilogue");
+    J4C_REQUIRE(K > 0 || (!bias && !mask && !mask_bits && !act), "j4c_dot_split_ep: K = 0 with an epilogue");
     if (K == 0) {
         if (out_lines) J4C_CUDA(cudaMemsetAsync(out_lines, 0, (size_t)(M + N + 1) * sizeof(uint32_t), s));
         return j4c_fill(J4C_FLOAT32, c, M * N, 0.0, stream);
@@ -139,7 +142,14 @@ int j4c_dot_split_ep_max(const float *a_hi, const float *a_lo, const float *b_hi
         return set_error(J4C_E_UNSUPPORTED, "j4c_dot_split: shape %lld x %lld x %lld is too large", (long long)M,
                          (long long)K, (long long)N);
     return tc_gemm_presplit(a_hi, a_lo, b_hi, b_lo, c, M, K, N, trans_a, trans_b, bias, mask, act, 1, 0, 0, s,
-                            out_lines);
+                            out_lines, mask_bits, act_bits);
+}
+
+int j4c_dot_split_ep_max(const float *a_hi, const float *a_lo, const float *b_hi, const float *b_lo, float *c,
+                         int64_t M, int64_t K, int64_t N, int trans_a, int trans_b, const float *bias,
+                         const float *mask, float *act, uint32_t *out_lines, j4c_stream stream) {
+    return j4c_dot_split_ep_bits(a_hi, a_lo, b_hi, b_lo, c, M, K, N, trans_a, trans_b, bias, mask, nullptr, act,
+                                 nullptr, out_lines, stream);
 }
 
 int j4c_dot_split_ep(const float *a_hi, const float *a_lo, const float *b_hi, const float *b_lo, float *c,

@@ -342,16 +342,14 @@ __device__ __forceinline__ void mma_commit(uint32_t bar) {
                  : "memory");
 }
 
-__device__ __forceinline__ void tmem_ld32(uint32_t taddr, uint32_t (&r)[32]) {
+// 16 consecutive TMEM columns of this warp's 32 lanes (tcgen05.ld 32x32b.x16).
+__device__ __forceinline__ void tmem_ld16(uint32_t taddr, uint32_t (&r)[16]) {
     asm volatile(
-        "tcgen05.ld.sync.aligned.32x32b.x32.b32 "
-        "{%0,%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15,"
-        "%16,%17,%18,%19,%20,%21,%22,%23,%24,%25,%26,%27,%28,%29,%30,%31}, [%32];"
+        "tcgen05.ld.sync.aligned.32x32b.x16.b32 "
+        "{%0,%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15}, [%16];"
         : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]),
           "=r"(r[7]), "=r"(r[8]), "=r"(r[9]), "=r"(r[10]), "=r"(r[11]), "=r"(r[12]), "=r"(r[13]),
-          "=r"(r[14]), "=r"(r[15]), "=r"(r[16]), "=r"(r[17]), "=r"(r[18]), "=r"(r[19]),
-          "=r"(r[20]), "=r"(r[21]), "=r"(r[22]), "=r"(r[23]), "=r"(r[24]), "=r"(r[25]),
-          "=r"(r[26]), "=r"(r[27]), "=r"(r[28]), "=r"(r[29]), "=r"(r[30]), "=r"(r[31])
+          "=r"(r[14]), "=r"(r[15])
         : "r"(taddr));
     asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
 }
@@ -395,6 +393,10 @@ __device__ __forceinline__ Unit unit_of(int u, int full_tiles, int splits, int n
 // over what is written to act (or to C when there is no act), and *out_flag
 // nonzero when a written value is a NaN or an infinity -- what a later split
 // of that output takes instead of its own max pass.
+// The relu' mask may come as bits instead (mask_bits, one bit per element:
+// bit c & 31 of word c / 32 of a row of bits_words words, set where the
+// mask is > 0), and the relu output's bits (act > 0) may be written the same
+// way (act_bits): 1/32 of the bytes.  Bits need C stored untransposed.
 struct Epilogue {
     const float *bias;
     const float *mask;
@@ -402,6 +404,9 @@ struct Epilogue {
     uint32_t *out_lines;
     int out_rows;
     uint32_t *out_flag;
+    const uint32_t *mask_bits;
+    uint32_t *act_bits;
+    int bits_words;
 };
 
 // The bits of |v| for finite v, else 0.
@@ -433,6 +438,13 @@ __device__ void exact_tiles(const float *__restrict__ A, bool a_col, const float
         const float *Ab = A + (a_batched ? (size_t)bidx * M * K : 0);
         const float *Bb = B + (b_batched ? (size_t)bidx * N * K : 0);
         const size_t boff = (size_t)bidx * (size_t)M * (size_t)N;
+        if (ep.act_bits) {  // this tile's words start at zero, then take each element's bit
+            for (int e = threadIdx.x; e < BM * (BN / 32); e += blockDim.x) {
+                const int i = mt * BM + e / (BN / 32), wd = nt * (BN / 32) + e % (BN / 32);
+                if (i < M && wd < ep.bits_words) ep.act_bits[(size_t)i * ep.bits_words + wd] = 0u;
+            }
+            __syncthreads();
+        }
         for (int e = threadIdx.x; e < BM * BN; e += blockDim.x) {
             const int i = mt * BM + e / BN, j = nt * BN + e % BN;
             if (i >= M || j >= N) continue;
@@ -444,9 +456,14 @@ __device__ void exact_tiles(const float *__restrict__ A, bool a_col, const float
             }
             const size_t idx = boff + (store_t ? (size_t)j * M + i : (size_t)i * N + j);
             float v = ep.bias ? __fadd_rn(s, __ldg(ep.bias + (store_t ? i : j))) : s;
-            if (ep.mask) v = __ldg(ep.mask + idx) > 0.0f ? v : 0.0f;
+            if (ep.mask_bits)
+                v = (__ldg(ep.mask_bits + (size_t)i * ep.bits_words + (j >> 5)) >> (j & 31)) & 1u ? v : 0.0f;
+            else if (ep.mask)
+                v = __ldg(ep.mask + idx) > 0.0f ? v : 0.0f;
             if (C) C[idx] = v;
             if (ep.act) ep.act[idx] = ep_relu(v);
+            if (ep.act_bits && ep_relu(v) > 0.0f)
+                atomicOr(ep.act_bits + (size_t)i * ep.bits_words + (j >> 5), 1u << (j & 31));
             if (ep.out_lines) {
                 const float tv = ep.act ? ep_relu(v) : v;
                 const uint32_t m = finite_bits(tv);
@@ -458,6 +475,7 @@ __device__ void exact_tiles(const float *__restrict__ A, bool a_col, const float
                 if ((__float_as_uint(tv) & 0x7F800000u) == 0x7F800000u) atomicOr(ep.out_flag, 1u);
             }
         }
+        if (ep.act_bits) __syncthreads();  // the tile's bits are settled before the next tile zeroes its own
     }
 }
 
@@ -677,11 +695,12 @@ gemm_3xtf32_kernel(const __grid_constant__ CUtensorMap tAh, const __grid_constan
                 }
                 tc_fence_after();
 #pragma unroll
-                for (int c = 0; c < Q::COLS_PER_WARP / 32; c++) {
-                    uint32_t r[32];
-                    tmem_ld32(tmem + (uint32_t)(buf * BN + cbase + c * 32) + lane_off, r);
+                for (int c = 0; c < Q::COLS_PER_WARP / 16; c++) {
+                    // 16 columns at a time: fewer registers live beside the 128 accumulators
+                    uint32_t r[16];
+                    tmem_ld16(tmem + (uint32_t)(buf * BN + cbase + c * 16) + lane_off, r);
 #pragma unroll
-                    for (int j = 0; j < 32; j++) acc[c * 32 + j] = __fadd_rn(acc[c * 32 + j], __uint_as_float(r[j]));
+                    for (int j = 0; j < 16; j++) acc[c * 16 + j] = __fadd_rn(acc[c * 16 + j], __uint_as_float(r[j]));
                 }
                 tc_fence_before();
                 __syncwarp();
@@ -730,6 +749,11 @@ gemm_3xtf32_kernel(const __grid_constant__ CUtensorMap tAh, const __grid_constan
                                  ((!B_MN && b_batched) ? (size_t)bidx * N : 0);
             const int ea = row_ok ? split_exp(__ldg(al + row)) : 0;
             const bool vec_full = row_ok && !store_t && vec_store && col0 + Q::COLS_PER_WARP <= N;
+            // relu' mask bits and the relu output's bits of this lane's row, one
+            // 32-column word at a time (C stored untransposed): word j / 32 of
+            // the lane's columns is at bits + row * bits_words + col0 / 32 + j / 32
+            const size_t bits_row = (size_t)row * ep.bits_words + (col0 >> 5);
+            uint32_t mword = 0u, aword = 0u;
             const float bias_t = (store_t && ep.bias && row_ok) ? __ldg(ep.bias + row) : 0.0f;
             {
                 // lane l reads the line word of column g*32 + l; the warp shares it
@@ -754,20 +778,27 @@ gemm_3xtf32_kernel(const __grid_constant__ CUtensorMap tAh, const __grid_constan
                                            (pa2 * __shfl_sync(0xffffffffu, pb2, jj));
                 }
             }
-            // Store; afterwards acc[j] holds the bits of the stored |v| (the relu
-            // output when act is written; finite values only, 0 outside C), from
-            // which the line maxima are taken.
+            // Store; afterwards acc[j] holds the stored value (the relu output
+            // when act is written; 0 outside C), from which the line maxima are
+            // taken.
             if (vec_full) {
                 const size_t base = (size_t)row * (size_t)N + col0;
 #pragma unroll
                 for (int v4 = 0; v4 < Q::COLS_PER_WARP / 4; v4++) {
                     float x[4] = {acc[4 * v4], acc[4 * v4 + 1], acc[4 * v4 + 2], acc[4 * v4 + 3]};
+                    if ((v4 & 7) == 0) {  // a new 32-column word
+                        mword = ep.mask_bits ? __ldg(ep.mask_bits + bits_row + (v4 >> 3)) : 0u;
+                        aword = 0u;
+                    }
                     if (ep.bias) {
                         const float4 b = __ldg(reinterpret_cast<const float4 *>(ep.bias + col0) + v4);
                         x[0] = __fadd_rn(x[0], b.x); x[1] = __fadd_rn(x[1], b.y);
                         x[2] = __fadd_rn(x[2], b.z); x[3] = __fadd_rn(x[3], b.w);
                     }
-                    if (mask_b) {
+                    if (ep.mask_bits) {
+#pragma unroll
+                        for (int e = 0; e < 4; e++) x[e] = (mword >> ((4 * v4 + e) & 31)) & 1u ? x[e] : 0.0f;
+                    } else if (mask_b) {
                         const float4 m = __ldg(reinterpret_cast<const float4 *>(mask_b + base) + v4);
                         x[0] = m.x > 0.0f ? x[0] : 0.0f; x[1] = m.y > 0.0f ? x[1] : 0.0f;
                         x[2] = m.z > 0.0f ? x[2] : 0.0f; x[3] = m.w > 0.0f ? x[3] : 0.0f;
@@ -775,9 +806,13 @@ gemm_3xtf32_kernel(const __grid_constant__ CUtensorMap tAh, const __grid_constan
                     if (Cb) reinterpret_cast<float4 *>(Cb + base)[v4] = make_float4(x[0], x[1], x[2], x[3]);
                     if (act_b) {
 #pragma unroll
-                        for (int e = 0; e < 4; e++) x[e] = ep_relu(x[e]);
+                        for (int e = 0; e < 4; e++) {
+                            x[e] = ep_relu(x[e]);
+                            if (x[e] > 0.0f) aword |= 1u << ((4 * v4 + e) & 31);
+                        }
                         reinterpret_cast<float4 *>(act_b + base)[v4] = make_float4(x[0], x[1], x[2], x[3]);
                     }
+                    if ((v4 & 7) == 7 && ep.act_bits) ep.act_bits[bits_row + (v4 >> 3)] = aword;
 #pragma unroll
                     for (int e = 0; e < 4; e++) acc[4 * v4 + e] = x[e];
                 }
@@ -803,16 +838,26 @@ gemm_3xtf32_kernel(const __grid_constant__ CUtensorMap tAh, const __grid_constan
 #pragma unroll
                 for (int j = 0; j < Q::COLS_PER_WARP; j++) {
                     float v = 0.0f;
+                    const bool word_in = row_ok && (col0 >> 5) + (j >> 5) < ep.bits_words;
+                    if ((j & 31) == 0) {
+                        mword = (ep.mask_bits && word_in) ? __ldg(ep.mask_bits + bits_row + (j >> 5)) : 0u;
+                        aword = 0u;
+                    }
                     if (row_ok && col0 + j < N) {
                         v = ep.bias ? __fadd_rn(acc[j], __ldg(ep.bias + col0 + j)) : acc[j];
-                        if (mask_b) v = __ldg(mask_b + base + j) > 0.0f ? v : 0.0f;
+                        if (ep.mask_bits)
+                            v = (mword >> (j & 31)) & 1u ? v : 0.0f;
+                        else if (mask_b)
+                            v = __ldg(mask_b + base + j) > 0.0f ? v : 0.0f;
                         if (Cb) Cb[base + j] = v;
                         if (act_b) {
                             v = ep_relu(v);
                             act_b[base + j] = v;
+                            if (v > 0.0f) aword |= 1u << (j & 31);
                         }
                     }
                     acc[j] = v;
+                    if ((j & 31) == 31 && ep.act_bits && word_in) ep.act_bits[bits_row + (j >> 5)] = aword;
                 }
             }
             uint32_t rmax = 0;  // over this lane's values: a stored row (a stored column when store_t)
@@ -1619,7 +1664,8 @@ int tc_split_lines(const float *x, int64_t rows, int64_t cols, uint32_t *lines, 
 static int gemm_presplit_ws(const float *ah, const float *al, const float *bh, const float *bl, float *c, int64_t M,
                             int64_t K, int64_t N, int trans_a, int trans_b, const float *bias, const float *mask,
                             float *act, int64_t batch, int a_batched, int b_batched, void *tail_ws,
-                            cudaStream_t s, uint32_t *out_lines = nullptr) {
+                            cudaStream_t s, uint32_t *out_lines = nullptr, const uint32_t *mask_bits = nullptr,
+                            uint32_t *act_bits = nullptr) {
     J4C_REQUIRE(aligned16(ah) && aligned16(al) && aligned16(bh) && aligned16(bl),
                 "dot: split operands must be 16-byte aligned");
     J4C_REQUIRE(!out_lines || batch == 1, "dot: line maxima of a batched product");
@@ -1630,7 +1676,14 @@ static int gemm_presplit_ws(const float *ah, const float *al, const float *bh, c
         const char *v = getenv("J4C_GEMM_VARIANT");
         return v ? atoi(v) : 1;
     }();
-    const tc::Epilogue ep{bias, mask, act, out_lines, (int)M, out_lines ? out_lines + M + N : nullptr};
+    // bits need C stored untransposed: not the K-major A . MN-major B form,
+    // which runs as C^T = op(B)^T . op(A)^T
+    J4C_REQUIRE(!(mask_bits || act_bits) || trans_a || trans_b,
+                "dot: mask bits need B given as its transposed split (trans_b = 1) or A^T");
+    J4C_REQUIRE(!act_bits || act, "dot: relu bits need the relu output");
+    J4C_REQUIRE(!(mask_bits || act_bits) || batch == 1, "dot: mask bits of a batched product");
+    const tc::Epilogue ep{bias,      mask,     act, out_lines, (int)M, out_lines ? out_lines + M + N : nullptr,
+                          mask_bits, act_bits, (int)ceil_div(N, 32)};
     const bool ab = a_batched != 0, bb = b_batched != 0;
     if (tc::split_fp16())
         return tc::launch_gemm_any<256, 4, 16, true>(ah, al, bh, bl, c, M, N, K, a_mn, b_mn, ep, batch, ab, bb, tail_ws, s);
@@ -1642,9 +1695,9 @@ static int gemm_presplit_ws(const float *ah, const float *al, const float *bh, c
 int tc_gemm_presplit(const float *ah, const float *al, const float *bh, const float *bl, float *c, int64_t M,
                      int64_t K, int64_t N, int trans_a, int trans_b, const float *bias, const float *mask,
                      float *act, int64_t batch, int a_batched, int b_batched, cudaStream_t s,
-                     uint32_t *out_lines) {
+                     uint32_t *out_lines, const uint32_t *mask_bits, uint32_t *act_bits) {
     return gemm_presplit_ws(ah, al, bh, bl, c, M, K, N, trans_a, trans_b, bias, mask, act, batch, a_batched,
-                            b_batched, nullptr, s, out_lines);
+                            b_batched, nullptr, s, out_lines, mask_bits, act_bits);
 }
 
 int tc_gemm_f32(const float *a, const float *b, float *c, int64_t M, int64_t K, int64_t N,
@@ -1652,7 +1705,9 @@ int tc_gemm_f32(const float *a, const float *b, float *c, int64_t M, int64_t K, 
     J4C_REQUIRE(aligned16(ws), "dot: workspace must be 16-byte aligned");
     const int64_t ar = trans_a ? K : M, ac = trans_a ? M : K;  // A as stored
     const int64_t br = trans_b ? N : K, bc = trans_b ? K : N;  // B as stored
-    const bool b_transposed = trans_a && !trans_b;  // B is split as B^T: [bc, pitch(br)]
+    // B stored [K, N] is split as B^T ([bc, pitch(br)], read K-major): both
+    // operands K-major is the fastest form
+    const bool b_transposed = !trans_b;
     char *w = static_cast<char *>(ws);
     float *ah = reinterpret_cast<float *>(w);
     float *al = reinterpret_cast<float *>(w + split_buf(ar, ac));
@@ -1667,14 +1722,11 @@ int tc_gemm_f32(const float *a, const float *b, float *c, int64_t M, int64_t K, 
                       : tc::split_any(a, ar, ac, ah, al, nullptr, nullptr, nullptr, nullptr, nullptr, s)))
         return rc;
     if (b_transposed) {
-        // both stored K-leading: B goes in as the split of B^T (K-major)
         if ((rc = tc::split_any(b, br, bc, nullptr, nullptr, nullptr, nullptr, bh, bl, nullptr, s))) return rc;
         return gemm_presplit_ws(ah, al, bh, bl, c, M, K, N, trans_a, 1, nullptr, nullptr, nullptr, 1, 0, 0, tail_ws, s);
     }
-    // B read MN-major (trans_b = 0) takes column lines, K-major row lines
-    if ((rc = trans_b ? tc::split_any(b, br, bc, bh, bl, nullptr, nullptr, nullptr, nullptr, nullptr, s)
-                      : tc::split_any(b, br, bc, nullptr, nullptr, bh, bl, nullptr, nullptr, nullptr, s)))
-        return rc;
+    // B stored [N, K] is read K-major with row lines
+    if ((rc = tc::split_any(b, br, bc, bh, bl, nullptr, nullptr, nullptr, nullptr, nullptr, s))) return rc;
     return gemm_presplit_ws(ah, al, bh, bl, c, M, K, N, trans_a, trans_b, nullptr, nullptr, nullptr, 1, 0, 0, tail_ws,
                             s);
 }

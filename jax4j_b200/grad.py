@@ -200,12 +200,12 @@ FUSION = os.environ.get("J4C_FUSION", "1") != "0"
 def _dot_split_kinds(jaxpr: Jaxpr, eq) -> tuple:
     """The operand splits a DOT equation's forward and, for the cotangents the
     backward will compute, its VJP read (Grad.java:385-390), as split kinds of
-    core._split_of: the forward reads A with row lines and B with column
-    lines; dA = g . B^T reads B with row lines; dB = A^T . g reads A with
-    column lines, or transposed when A is the smaller operand."""
+    core._split_of: the forward reads A with row lines and B transposed;
+    dA = g . B^T reads B with row lines; dB = A^T . g reads A with column
+    lines, or transposed when A is the smaller operand."""
     need = _needs_grad(jaxpr)
     a, b = eq.inputs
-    ka, kb = ["r"], ["c"]
+    ka, kb = ["r"], ["t"]
     if b.id in need:
         ka.append("t" if a.shape.size() < eq.outputs[0].shape.size() else "c")
     if a.id in need:

@@ -765,3 +765,60 @@ def test_dot_special_values_through_the_epilogue_and_vmap(J):
     got = J.JAX.vmap(lambda x, w: x.dot(w), in_axes=[0, 0])(dev(J, A3), dev(J, B3)).numpy()
     for i in range(3):
         assert np.array_equal(got[i], orc.dot(A3[i], B3[i]), equal_nan=True), i
+
+
+def _pack_bits(m):
+    """x > 0 of a [rows, cols] array as rows of ceil(cols / 32) uint32 words."""
+    rows, cols = m.shape
+    w = (cols + 31) // 32
+    padded = np.zeros((rows, w * 32), dtype=bool)
+    padded[:, :cols] = m
+    return np.packbits(padded.reshape(rows, w, 4, 8)[:, :, ::-1, ::-1].reshape(rows, w * 32),
+                       axis=1).view(">u4").astype(np.uint32).reshape(rows, w)
+
+
+@pytest.mark.parametrize("M,K,N,special", [(333, 257, 1030, False), (256, 512, 4096, False), (130, 96, 70, True)])
+def test_relu_bits_equal_the_float_mask(J, M, K, N, special):
+    """A forward epilogue (bias + relu) leaves h > 0 as bits; an input
+    gradient masked by those bits equals the one masked by the float relu
+    output bit for bit -- in the tensor-core path and in the exact path of
+    operands holding NaN/Inf."""
+    from jax4j_b200 import core
+    from jax4j_b200.core import _dot_raw
+    r = rng(M + N)
+    A = r.standard_normal((M, K)).astype(np.float32)
+    if special:
+        A[3, 5], A[7, 1] = np.inf, np.nan
+    W = (r.standard_normal((K, N)) * 0.05).astype(np.float32)
+    bias = r.standard_normal(N).astype(np.float32) * 0.1
+    a, w, b = dev(J, A), dev(J, W), dev(J, bias)
+    _, h = _dot_raw(a, w, False, False, a.device(), bias=b, act=True, store_c=False)
+    assert h._relu_bits is not None
+    hh = h.numpy()
+    np.testing.assert_array_equal(h._relu_bits.cpu().numpy().view(np.uint32).reshape(M, -1), _pack_bits(hh > 0))
+    G = r.standard_normal((M, 64)).astype(np.float32)
+    W2 = r.standard_normal((N, 64)).astype(np.float32)  # dX = G . W2^T, masked by h > 0
+    g, w2 = dev(J, G), dev(J, W2)
+    with_bits = _dot_raw(g, w2, False, True, a.device(), mask=h).numpy()
+    bits, h._relu_bits = h._relu_bits, None
+    with_floats = _dot_raw(g, w2, False, True, a.device(), mask=h).numpy()
+    h._relu_bits = bits
+    assert np.array_equal(with_bits, with_floats, equal_nan=True)
+
+
+def test_relu_bits_rejected_where_c_is_stored_transposed(J):
+    """The K-major A . MN-major B form stores C transposed, so it cannot
+    take relu bits: j4c_dot_split_ep_bits rejects them there."""
+    import torch
+    from jax4j_b200.core import _split_of
+    M, K, N = 64, 32, 96
+    r = rng(3)
+    a, b = dev(J, r.standard_normal((M, K)).astype(np.float32)), dev(J, r.standard_normal((K, N)).astype(np.float32))
+    (ah, al), (bh, bl) = _split_of(a, "r"), _split_of(b, "c")
+    act = torch.empty(M * N, dtype=torch.float32, device=a.tensor().device)
+    bits = torch.empty(M * 3, dtype=torch.int32, device=a.tensor().device)
+    rc = _lib.lib().j4c_dot_split_ep_bits(ah.data_ptr(), al.data_ptr(), bh.data_ptr(), bl.data_ptr(), None, M, K, N,
+                                          0, 0, None, None, None, act.data_ptr(), bits.data_ptr(), None,
+                                          a._stream())
+    assert rc == _lib.E_INVALID
+    assert "transposed split" in _lib.lib().j4c_last_error().decode()
