@@ -343,6 +343,7 @@ class Lax:
         first = leaves[0]
         if any(l.dtype() != first.dtype() or l.tensor().device != first.tensor().device for l in leaves):
             return PyTrees.map(Lax.psum, tree)
+        _pm.verify_signature(ctx, "psumTree", first.dtype(), [l.shape().size() for l in leaves])
         if isinstance(ctx.collective, _pm.NcclCollective) and PSUM_BUCKET_BYTES > 0:
             return PyTrees.unflatten(tree, _psum_overlapped(ctx, leaves))
         total = sum(l.shape().size() for l in leaves)

@@ -16,8 +16,8 @@ from __future__ import annotations
 import ctypes as C
 import datetime
 import os
-from dataclasses import dataclass
-from typing import List, Optional
+from dataclasses import dataclass, field
+from typing import List, Optional, Tuple
 
 import torch
 import torch.distributed as dist
@@ -35,6 +35,7 @@ class SpmdState:
     comm: int
     collective: NcclCollective
     devices: List[Device]
+    verified: set = field(default_factory=set)
 
 
 _state: Optional[SpmdState] = None
@@ -101,6 +102,41 @@ def heartbeat() -> None:
         dist.monitored_barrier(timeout=datetime.timedelta(seconds=HEARTBEAT_S))
     except RuntimeError as e:
         raise CollectiveError(f"pmap: a peer rank did not reach the step within {HEARTBEAT_S} s: {e}") from e
+
+
+# Collective signature check.  NCCL matches collectives by call order alone: a
+# rank that all-reduces 100 floats while its peer all-reduces 200 hangs or
+# reads past the smaller buffer.  The reference's SharedCollective.psum has
+# the same hazard (api/SharedCollective.java:44-54: the sum loop runs over the
+# caller's length and indexes every peer's deposit with it, so a shorter
+# deposit throws on the longer caller while its peers wait at the barrier).
+# Before a collective signature (kind, dtype, element counts) is used for the
+# first time, every rank exchanges it over the host process group; ranks that
+# disagree all raise CollectiveError naming each rank's signature, and no
+# device work is enqueued.  A signature seen before is not exchanged again, so
+# the steady state (and a step recorded as a CUDA graph) pays nothing.
+CHECK_SIGNATURES = os.environ.get("J4C_CHECK_COLLECTIVES", "1") != "0"
+
+
+def verify_collective(kind: str, dtype: str, counts: Tuple[int, ...]) -> None:
+    """Raises CollectiveError on every rank when the ranks' collectives differ
+    in kind, dtype or element counts (first use of each signature only)."""
+    from .pmap import CollectiveError
+    st = _state
+    if st is None or st.world_size == 1 or not CHECK_SIGNATURES or not dist.is_initialized():
+        return
+    key = (kind, dtype, tuple(int(c) for c in counts))
+    if key in st.verified:
+        return
+    sigs: list = [None] * st.world_size
+    try:
+        dist.all_gather_object(sigs, key)
+    except RuntimeError as e:
+        raise CollectiveError(f"{kind}: a peer rank did not reach the signature check: {e}") from e
+    if any(s != key for s in sigs):
+        desc = "; ".join(f"rank {r}: {s[0]} of {s[1]} {list(s[2])}" for r, s in enumerate(sigs))
+        raise CollectiveError(f"{kind}: ranks issued different collectives ({desc})")
+    st.verified.add(key)
 
 
 def global_devices() -> List[Device]:

@@ -250,11 +250,23 @@ def _nccl_for(ordinals: tuple) -> NcclCollective:
 # ---------------------------------------------------------------------------
 # eager collective entry points used by Lax and the Grad interpreter
 # ---------------------------------------------------------------------------
+def verify_signature(ctx: "PmapContext", kind: str, dtype: DType, counts) -> None:
+    """One-process-per-GPU runs: checks that every rank issues this collective
+    with the same dtype and element counts before any rank enqueues it
+    (distributed.verify_collective).  Shards sharing a process compare their
+    deposits in the collective itself."""
+    from . import distributed
+    st = distributed.state()
+    if st is not None and ctx.collective is st.collective:
+        distributed.verify_collective(kind, dtype.name, counts)
+
+
 def psum_value(x: NDArray) -> NDArray:
     """Lax.psum eager branch (Lax.java:184-186): identity outside pmap."""
     ctx = PmapContext.current()
     if ctx is None or ctx.numDevices == 1:
         return x  # a sum over one shard is the shard itself (arrays are immutable)
+    verify_signature(ctx, "psum", x.dtype(), (x.shape().size(),))
     return ctx.collective.psum(ctx.deviceIndex, x)
 
 
@@ -263,6 +275,7 @@ def all_gather_value(x: NDArray) -> NDArray:
     ctx = PmapContext.current()
     if ctx is None:
         return stack([x])
+    verify_signature(ctx, "allGather", x.dtype(), (x.shape().size(),))
     return ctx.collective.allGather(ctx.deviceIndex, x)
 
 
@@ -287,6 +300,7 @@ def all_gather_vjp(g: ConcreteNDArray) -> ConcreteNDArray:
     if ctx is None:
         return g
     if ALLGATHER_VJP == "reduce_scatter" and ctx.numDevices > 1:
+        verify_signature(ctx, "reduceScatter", g.dtype(), (g.shape().size(),))
         return ctx.collective.reduceScatter(ctx.deviceIndex, g)
     return split(g, ctx.numDevices)[ctx.deviceIndex]
 
@@ -417,6 +431,8 @@ def _local_inputs(inputs: Sequence[NDArray], D: int, rank: int) -> List[Concrete
 
 def _gather_stack(st, local: ConcreteNDArray) -> ConcreteNDArray:
     """Stacks every rank's result: an all-gather across the processes."""
+    from . import distributed
+    distributed.verify_collective("pmap output allGather", local.dtype().name, (local.shape().size(),))
     return st.collective.allGather(0, local)
 
 

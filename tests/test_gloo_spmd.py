@@ -101,6 +101,33 @@ def _worker(rank, world, port, scenario, q):
                 q.put((rank, "no error", None, time.time() - t0))
             except Exception as e:  # noqa: BLE001
                 q.put((rank, type(e).__name__, str(e)[:200], time.time() - t0))
+        elif scenario == "mismatched_psum":
+            # rank r all-reduces 2 + r elements: every rank must get an error
+            # naming both signatures, before any collective is enqueued
+            from jax4j_b200 import ConcreteNDArray, Device, DType, Shape, distributed as dd
+            n = 2 + rank
+            local = _cpu_array([1.0] * n, [n])
+            t0 = time.time()
+            try:
+                JAX.pmap(lambda s: Lax.psum(s), devices)(LocalShard(local, world))
+                q.put((rank, "no error", None, time.time() - t0))
+            except Exception as e:  # noqa: BLE001
+                q.put((rank, type(e).__name__, str(e)[:300], time.time() - t0))
+        elif scenario == "matched_psum_checked_once":
+            from jax4j_b200 import distributed as dd
+            calls = []
+            real = dist.all_gather_object
+
+            def counting(*a, **k):
+                calls.append(1)
+                return real(*a, **k)
+
+            dist.all_gather_object = counting
+            local = _cpu_array([float(rank)] * 3, [3])
+            outs = [JAX.pmap(lambda s: Lax.psum(s), devices)(LocalShard(local, world)) for _ in range(3)]
+            dist.all_gather_object = real
+            sig = ("psum", "FLOAT32", (3,))
+            q.put((rank, "ok", [o.tensor().tolist() for o in outs], (len(calls), sig in dd.state().verified)))
         elif scenario == "max_over_ranks":
             t = torch.tensor([float(rank + 1)], dtype=torch.float64)
             dist.all_reduce(t, op=dist.ReduceOp.MAX)
@@ -171,6 +198,26 @@ def test_spmd_peer_that_left_is_detected_before_the_next_collective():
     status, msg, elapsed = res[0]
     assert status == "CollectiveError", (status, msg)
     assert elapsed < 30
+
+
+def test_spmd_mismatched_collective_sizes_raise_on_every_rank():
+    res = _run("mismatched_psum")
+    assert set(res) == {0, 1}
+    for r in (0, 1):
+        status, msg, elapsed = res[r]
+        assert status == "CollectiveError", (r, status, msg)
+        assert "different collectives" in msg and "[2]" in msg and "[3]" in msg, msg
+        assert elapsed < 30
+
+
+def test_spmd_collective_signature_is_exchanged_once():
+    res = _run("matched_psum_checked_once")
+    for r in (0, 1):
+        status, values, (n_exchanges, recorded) = res[r]
+        assert status == "ok", values
+        assert values == [[1.0] * 6] * 3  # stacked [psum, psum] of ranks 0 and 1
+        # the psum's signature once, the pmap output's all-gather once
+        assert n_exchanges == 2 and recorded
 
 
 def test_spmd_timing_is_max_over_ranks():
