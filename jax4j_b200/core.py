@@ -385,7 +385,7 @@ class ConcreteNDArray(NDArray):
     kind) once it has been a dot operand, for the other dots it takes part in.
     """
 
-    __slots__ = ("_t", "_shape", "_dtype", "_device", "_split", "_ready", "_lines", "_relu_bits")
+    __slots__ = ("_t", "_shape", "_dtype", "_device", "_split", "_ready", "_lines", "_relu_bits", "_scalar")
 
     def __init__(self, data, shape=None, dtype: DType = None, device: Device = None):
         if device is None:
@@ -423,6 +423,7 @@ class ConcreteNDArray(NDArray):
         self._ready = None  # CUDA event recorded once the value was produced, when tracked
         self._lines = None  # device words [rows + cols + 1]: line maxima (bits of max finite |x|), NaN/Inf flag
         self._relu_bits = None  # a relu output's x > 0 as bits (rows of ceil(cols / 32) words), from its GEMM
+        self._scalar = None  # host copy of a one-element floating array made by full() / scalar()
 
     # ---- construction helpers ----
     @staticmethod
@@ -442,7 +443,12 @@ class ConcreteNDArray(NDArray):
         device = device or Device.defaultDevice()
         t = torch.empty(shape.size(), dtype=dtype.torch, device=device.torch_device())
         call("j4c_fill", dtype.ordinal, t.data_ptr(), t.numel(), float(value), stream_of(device.ordinal()))
-        return ConcreteNDArray._wrap(t, shape, dtype, device)
+        out = ConcreteNDArray._wrap(t, shape, dtype, device)
+        if shape.size() == 1 and dtype in (DType.FLOAT32, DType.FLOAT64):
+            # the value the fill kernel stored ((float) value for FLOAT32), so
+            # a fused program can take it as a literal
+            out._scalar = float(np.float32(value)) if dtype == DType.FLOAT32 else float(value)
+        return out
 
     @staticmethod
     def _wrap(t: torch.Tensor, shape: Shape, dtype: DType, device: Device) -> "ConcreteNDArray":
@@ -455,6 +461,7 @@ class ConcreteNDArray(NDArray):
         obj._ready = None
         obj._lines = None
         obj._relu_bits = None
+        obj._scalar = None
         return obj
 
     def _new(self, shape: Shape, dtype: DType) -> torch.Tensor:

@@ -8,6 +8,7 @@
 #include <type_traits>
 
 #include "common.cuh"
+#include "jmath.cuh"
 
 namespace j4c {
 
@@ -32,17 +33,21 @@ __device__ __forceinline__ uint8_t compare_op(T a, T b) {
     else return a != b;
 }
 
+J4C_MATH_DEFS
+
 // ConcreteNDArray.unary (core/ConcreteNDArray.java:657-664).  FP32 uses the
-// CUDA single-precision functions (<= 2 ulp), FP64 the double ones.
+// CUDA single-precision functions (<= 2 ulp) for exp/log/sin/cos and the
+// one-exponential tanh and sigmoid of jmath.cuh (<= 1.6e-6 relative for
+// |x| <= 10); FP64 the double functions.
 template <int OP>
 __device__ __forceinline__ float unary_op(float x) {
     if constexpr (OP == J4C_EXP) return expf(x);
     else if constexpr (OP == J4C_LOG) return logf(x);
     else if constexpr (OP == J4C_SIN) return sinf(x);
     else if constexpr (OP == J4C_COS) return cosf(x);
-    else if constexpr (OP == J4C_TANH) return tanhf(x);
+    else if constexpr (OP == J4C_TANH) return j_tanh(x);
     else if constexpr (OP == J4C_RELU) return java_max(0.0f, x);
-    else return __frcp_rn(__fadd_rn(1.0f, expf(-x)));  // SIGMOID: correctly rounded 1 / (1 + e^-x)
+    else return j_sigmoid(x);  // SIGMOID: 1 / (1 + e^-x)
 }
 template <int OP>
 __device__ __forceinline__ double unary_op(double x) {

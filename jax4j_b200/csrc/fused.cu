@@ -26,6 +26,7 @@
 #include <vector>
 
 #include "common.cuh"
+#include "jmath.cuh"
 
 namespace j4c {
 namespace fused {
@@ -90,6 +91,31 @@ template <> __device__ __forceinline__ float j_min<float>(float a, float b) {
     float m;
     asm("min.NaN.f32 %0, %1, %2;" : "=f"(m) : "f"(a), "f"(b));
     return a == b ? __int_as_float(__float_as_int(a) | __float_as_int(b)) : m;
+}
+// Per-thread asynchronous copies into shared memory (cp.async, 16 bytes):
+// a thread stages its own future vectors and reads back only what it
+// staged, so the wait_group on its own copies is the only ordering needed.
+__device__ __forceinline__ void j_cp16(void *smem, const void *g) {
+    const unsigned s = (unsigned)__cvta_generic_to_shared(smem);
+    asm volatile("cp.async.cg.shared.global [%0], [%1], 16;" ::"r"(s), "l"(g) : "memory");
+}
+__device__ __forceinline__ void j_cp_commit() { asm volatile("cp.async.commit_group;" ::: "memory"); }
+template <int N> __device__ __forceinline__ void j_cp_wait() {
+    asm volatile("cp.async.wait_group %0;" ::"n"(N) : "memory");
+}
+__device__ __forceinline__ float j_max_nz(float a, float b) {
+    float m;
+    asm("max.NaN.f32 %0, %1, %2;" : "=f"(m) : "f"(a), "f"(b));
+    return m;
+}
+__device__ __forceinline__ float j_min_nz(float a, float b) {
+    float m;
+    asm("min.NaN.f32 %0, %1, %2;" : "=f"(m) : "f"(a), "f"(b));
+    return m;
+}
+__device__ __forceinline__ float j_where(unsigned char c, float x, float y) {
+    const float s = c ? x : y, t = c ? y : x;
+    return __fadd_rn(s, __fmul_rn(0.0f, t));
 }
 template <class T> __device__ __forceinline__ T j_relu(T x) { return (T(0) >= x) ? T(0) : x; }
 __device__ __forceinline__ int j_d2i(double v) {
@@ -210,6 +236,58 @@ static int validate(const j4c_program *p) {
     return J4C_OK;
 }
 
+// Numpy.where's blend (api/Numpy.java:39-44): ADD(MUL(c, x), MUL(SUB(1, c), y))
+// with c a BOOL cast to FLOAT32, so c is exactly 0 or 1.  With c = 1 the
+// blend is x + (+0 * y), with c = 0 it is (+0 * x) + y; as IEEE addition
+// commutes (signed zeros and NaN included) both are s + (+0 * t) with
+// s = the selected operand and t = the other -- two selects, one multiply
+// and one add instead of the cast, three multiplies/adds and a subtract,
+// bit for bit the arithmetic blend (NaN and Inf in the unselected operand
+// still make the result NaN).  Returns the BOOL insn and x, y.
+static bool where_blend(const j4c_program *p, int i, int *cond, int *x, int *y) {
+    const j4c_insn &q = p->insns[i];
+    if (q.op != J4C_ADD || q.dtype != J4C_FLOAT32) return false;
+    auto mul_of = [&](int k, int want, int *other) {
+        const j4c_insn &m = p->insns[k];
+        if (m.op != J4C_MUL || m.dtype != J4C_FLOAT32) return -1;
+        const j4c_insn &a = p->insns[m.a], &b = p->insns[m.b];
+        auto is_c = [&](const j4c_insn &c, int idx) {
+            return want < 0 ? (c.op == J4C_CAST && p->insns[c.a].dtype == J4C_BOOL) : idx == want;
+        };
+        if (is_c(a, m.a)) { *other = m.b; return m.a; }
+        if (is_c(b, m.b)) { *other = m.a; return m.b; }
+        return -1;
+    };
+    for (int order = 0; order < 2; order++) {
+        const int t1 = order ? q.b : q.a, t2 = order ? q.a : q.b;
+        int xv, yv;
+        const int c = mul_of(t1, -1, &xv);
+        if (c < 0) continue;
+        // the other term multiplies SUB(CONST 1, c)
+        for (int k = 0; k < i; k++) {
+            const j4c_insn &sb = p->insns[k];
+            if (sb.op != J4C_SUB || sb.dtype != J4C_FLOAT32 || sb.b != c) continue;
+            const j4c_insn &one = p->insns[sb.a];
+            if (one.op != J4C_OP_CONST || one.value != 1.0) continue;
+            if (mul_of(t2, k, &yv) == k) {
+                *cond = p->insns[c].a;
+                *x = xv;
+                *y = yv;
+                return true;
+            }
+        }
+    }
+    return false;
+}
+
+// A float MAX / MIN with a constant operand other than +-0: Java's Math.max /
+// Math.min differ from max.NaN / min.NaN only on a +0 / -0 pair, which a
+// non-zero constant rules out, so the single instruction is exact.
+static bool nonzero_const(const j4c_program *p, int k) {
+    const j4c_insn &c = p->insns[k];
+    return c.op == J4C_OP_CONST && c.dtype == J4C_FLOAT32 && (float)c.value != 0.0f;
+}
+
 // Code for one element.  The element's inputs are read from `ld<k>` (a
 // register array filled before the lane loop) and its outputs go to
 // `st<k>`; lane `l` is the element's position inside the thread's group of V.
@@ -219,6 +297,16 @@ static std::string gen_element(const j4c_program *p) {
         const j4c_insn &q = p->insns[i];
         const char *T = ctype(q.dtype);
         o << "        const " << T << " v" << i << " = ";
+        int wc, wx, wy;
+        if (where_blend(p, i, &wc, &wx, &wy)) {
+            o << "j_where(v" << wc << ", v" << wx << ", v" << wy << ");\n";
+            continue;
+        }
+        if ((q.op == J4C_MAX || q.op == J4C_MIN) && q.dtype == J4C_FLOAT32 &&
+            (nonzero_const(p, q.a) || nonzero_const(p, q.b))) {
+            o << (q.op == J4C_MAX ? "j_max_nz(v" : "j_min_nz(v") << q.a << ", v" << q.b << ");\n";
+            continue;
+        }
         switch (q.op) {
         case J4C_OP_INPUT: o << "ld" << q.a << "[l];\n"; continue;
         case J4C_OP_CONST: o << const_literal(q.dtype, q.value) << ";\n"; continue;
@@ -244,10 +332,11 @@ static std::string gen_element(const j4c_program *p) {
         case J4C_LOG: o << (f ? "logf(" : "log(") << x << ");\n"; break;
         case J4C_SIN: o << (f ? "sinf(" : "sin(") << x << ");\n"; break;
         case J4C_COS: o << (f ? "cosf(" : "cos(") << x << ");\n"; break;
-        case J4C_TANH: o << (f ? "tanhf(" : "tanh(") << x << ");\n"; break;
+        case J4C_TANH: o << (f ? "j_tanh(" : "tanh(") << x << ");\n"; break;
         case J4C_RELU: o << "j_relu(" << x << ");\n"; break;
-        case J4C_SIGMOID:  // 1 / (1 + e^-x); a correctly rounded reciprocal equals the correctly rounded 1.0 / d
-            o << (f ? "__frcp_rn(__fadd_rn(1.0f, expf(-" : "__drcp_rn(__dadd_rn(1.0, exp(-") << x << ")));\n";
+        case J4C_SIGMOID:  // 1 / (1 + e^-x): jmath.cuh's j_sigmoid for FP32, as the eager kernel
+            if (f) o << "j_sigmoid(" << x << ");\n";
+            else o << "__drcp_rn(__dadd_rn(1.0, exp(-" << x << ")));\n";
             break;
         case J4C_CAST: {
             int src = p->insns[q.a].dtype, dst = q.dtype;
@@ -268,16 +357,45 @@ static std::string gen_element(const j4c_program *p) {
 
 static int dsize(int dt) { return dt == J4C_FLOAT64 || dt == J4C_INT64 ? 8 : dt == J4C_BOOL ? 1 : 4; }
 
+// Row kernels with 4 elements per thread stage their full-size FP32 inputs
+// through shared memory S iterations ahead (cp.async): the loads in flight
+// no longer depend on how many registers the chain leaves for them (a
+// thread's S - 1 future vectors per input wait in shared memory, not in
+// registers), which is what keeps HBM busy while the chain computes.
+// Returns the staged slot of input i, or -1.
+static int staged_slot(const j4c_program *p, int i) {
+    if (p->input_bcast[i] != J4C_BCAST_FULL || p->input_dtype[i] != J4C_FLOAT32) return -1;
+    int k = 0;
+    for (int q = 0; q < i; q++)
+        if (p->input_bcast[q] == J4C_BCAST_FULL && p->input_dtype[q] == J4C_FLOAT32) k++;
+    return k;
+}
+static int n_staged(const j4c_program *p) {
+    int n = 0;
+    for (int i = 0; i < p->n_inputs; i++) n += staged_slot(p, i) >= 0;
+    return n;
+}
+// Stages in flight: S * NS * 256 threads * 16 bytes stays <= 32 KB.
+static int stage_depth(const j4c_program *p) {
+    const int n = n_staged(p);
+    return n == 0 ? 0 : n <= 2 ? 4 : n <= 4 ? 2 : 0;
+}
+
 // Loads the V consecutive elements starting at element `base` (row/flat
 // position) into ld<k>, and declares st<k>.  4-byte types move as one
 // 128-bit access when V == 4; the launcher only picks V == 4 when every
 // such pointer is 16-byte aligned and the extent is a multiple of 4.
-static std::string gen_loads(const j4c_program *p, bool flat, int V) {
+static std::string gen_loads(const j4c_program *p, bool flat, int V, bool staged = false) {
     std::ostringstream o;
     for (int i = 0; i < p->n_inputs; i++) {
         const char *T = ctype(p->input_dtype[i]);
         const int b = p->input_bcast[i];
         o << "      " << T << " ld" << i << "[" << V << "];\n";
+        if (staged && staged_slot(p, i) >= 0) {
+            o << "      { const float4 t = s_stage[sc][" << staged_slot(p, i) << "][threadIdx.x]; ld" << i
+              << "[0] = t.x; ld" << i << "[1] = t.y; ld" << i << "[2] = t.z; ld" << i << "[3] = t.w; }\n";
+            continue;
+        }
         std::string ptr = std::string("((const ") + T + " *)a.in[" + std::to_string(i) + "])";
         if (b == J4C_BCAST_SCALAR || b == J4C_BCAST_COL) {
             const char *at = b == J4C_BCAST_SCALAR ? "0" : "r";
@@ -328,15 +446,46 @@ static std::string gen_source(const j4c_program *p, bool *needs_rows) {
     *needs_rows = rows;
     const std::string element = gen_element(p);
     std::ostringstream o;
-    o << kPreamble;
+    o << kPreamble << J4C_MATH_SRC << "\n";
     if (!rows) {
         for (int V : {1, 4}) {
+            const int S = V == 4 ? stage_depth(p) : 0;
             o << "extern \"C\" __global__ void __launch_bounds__(256) k_flat" << (V == 4 ? "4" : "")
-              << "(i64 N, Args a) {\n"
-              << "    for (i64 e = (blockIdx.x * (i64)blockDim.x + threadIdx.x) * " << V << "; e < N;\n"
-              << "         e += (i64)gridDim.x * blockDim.x * " << V << ") {\n"
-              << gen_loads(p, true, V) << "      #pragma unroll\n      for (int l = 0; l < " << V
-              << "; l++) {\n"
+              << "(i64 N, Args a) {\n";
+            if (S > 0) {
+                // the grid-stride sequence of a thread, staged S - 1 vectors ahead
+                auto issue = [&](const char *eexpr, const char *slot) {
+                    std::ostringstream c;
+                    for (int i = 0; i < p->n_inputs; i++) {
+                        const int k = staged_slot(p, i);
+                        if (k < 0) continue;
+                        c << "j_cp16(&s_stage[" << slot << "][" << k << "][threadIdx.x], (const float *)a.in[" << i
+                          << "] + " << eexpr << "); ";
+                    }
+                    return c.str();
+                };
+                o << "    __shared__ float4 s_stage[" << S << "][" << n_staged(p) << "][256];\n"
+                  << "    const i64 G4 = (i64)gridDim.x * blockDim.x * 4;\n"
+                  << "    const i64 e0 = (blockIdx.x * (i64)blockDim.x + threadIdx.x) * 4;\n"
+                  << "    #pragma unroll\n    for (int s = 0; s < " << S - 1 << "; s++) {\n"
+                  << "      const i64 ee = e0 + (i64)s * G4;\n"
+                  << "      if (ee < N) { " << issue("ee", "s") << "}\n"
+                  << "      j_cp_commit();\n    }\n"
+                  << "    int it = 0;\n"
+                  << "    for (i64 e = e0; e < N; e += G4, it++) {\n"
+                  << "      { const i64 en = e + " << S - 1 << " * G4; const int sn = (it + " << S - 1 << ") & "
+                  << S - 1 << ";\n"
+                  << "        if (en < N) { " << issue("en", "sn") << "}\n"
+                  << "        j_cp_commit(); }\n"
+                  << "      j_cp_wait<" << S - 1 << ">();\n"
+                  << "      const int sc = it & " << S - 1 << ";\n"
+                  << gen_loads(p, true, V, true);
+            } else {
+                o << "    for (i64 e = (blockIdx.x * (i64)blockDim.x + threadIdx.x) * " << V << "; e < N;\n"
+                  << "         e += (i64)gridDim.x * blockDim.x * " << V << ") {\n"
+                  << gen_loads(p, true, V);
+            }
+            o << "      #pragma unroll\n      for (int l = 0; l < " << V << "; l++) {\n"
               << element << "      }\n"
               << gen_stores(p, true, V) << "    }\n}\n";
         }
@@ -349,6 +498,8 @@ static std::string gen_source(const j4c_program *p, bool *needs_rows) {
         std::string name = std::string(tpr == 32 ? "k_rows_warp" : "k_rows_block") + (V == 4 ? "4" : "");
         o << "extern \"C\" __global__ void __launch_bounds__(256) " << name << "(i64 R, i64 C, Args a) {\n";
         if (tpr == 256) o << "    __shared__ double s_d[8]; __shared__ float s_f[8]; __shared__ int s_i[8];\n";
+        if (V == 4 && stage_depth(p) > 0)
+            o << "    __shared__ float4 s_stage[" << stage_depth(p) << "][" << n_staged(p) << "][256];\n";
         o << "    const int sub = threadIdx.x % " << tpr << ";\n"
           << "    const int rows_per_cta = 256 / " << tpr << ";\n"
           << "    for (i64 r0 = (i64)blockIdx.x * rows_per_cta; r0 < R; r0 += (i64)gridDim.x * rows_per_cta) {\n"
@@ -364,9 +515,38 @@ static std::string gen_source(const j4c_program *p, bool *needs_rows) {
                   << "      int bi" << k << " = -1; int nan" << k << " = 0;\n";
             }
         }
-        o << "      if (r < R) {\n"
-          << "      for (i64 j = (i64)sub * " << V << "; j < C; j += " << tpr * V << ") {\n"
-          << gen_loads(p, false, V);
+        const int S = V == 4 ? stage_depth(p) : 0;
+        o << "      if (r < R) {\n";
+        if (S > 0) {
+            // each thread's vector j lands in slot (iteration % S); the copy
+            // for iteration it + S - 1 is issued before iteration it waits
+            auto issue = [&](const char *jexpr, const char *slot) {
+                std::ostringstream c;
+                for (int i = 0; i < p->n_inputs; i++) {
+                    const int k = staged_slot(p, i);
+                    if (k < 0) continue;
+                    c << "j_cp16(&s_stage[" << slot << "][" << k << "][threadIdx.x], (const float *)a.in[" << i
+                      << "] + r * C + " << jexpr << "); ";
+                }
+                return c.str();
+            };
+            o << "      #pragma unroll\n      for (int s = 0; s < " << S - 1 << "; s++) {\n"
+              << "        const i64 jj = (i64)sub * 4 + (i64)s * " << tpr * 4 << ";\n"
+              << "        if (jj < C) { " << issue("jj", "s") << "}\n"
+              << "        j_cp_commit();\n      }\n"
+              << "      int it = 0;\n"
+              << "      for (i64 j = (i64)sub * 4; j < C; j += " << tpr * 4 << ", it++) {\n"
+              << "      { const i64 jn = j + " << (S - 1) * tpr * 4 << "; const int sn = (it + " << S - 1 << ") & "
+              << S - 1 << ";\n"
+              << "        if (jn < C) { " << issue("jn", "sn") << "}\n"
+              << "        j_cp_commit(); }\n"
+              << "      j_cp_wait<" << S - 1 << ">();\n"
+              << "      const int sc = it & " << S - 1 << ";\n"
+              << gen_loads(p, false, V, true);
+        } else {
+            o << "      for (i64 j = (i64)sub * " << V << "; j < C; j += " << tpr * V << ") {\n"
+              << gen_loads(p, false, V);
+        }
         // a lane's sum takes its V consecutive elements as ((x0 + x1) + (x2 + x3)),
         // the order of the row reduction kernel, so fused and eager sums agree
         for (int k = 0; k < p->n_tails; k++)

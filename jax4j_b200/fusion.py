@@ -38,6 +38,7 @@ TAILS = {P.SUM_AXIS, P.MEAN_AXIS, P.ARGMAX, P.ARGMIN}
 FUSED_DTYPES = {DType.FLOAT32, DType.FLOAT64, DType.INT32, DType.BOOL}
 BCAST_FULL, BCAST_ROW, BCAST_COL, BCAST_SCALAR = 0, 1, 2, 3
 OP_INPUT = -1
+OP_CONST = -2
 
 # which operands each primitive's VJP rule reads (api/Grad.java:341-472);
 # "out" = the equation's own output
@@ -104,6 +105,7 @@ class Group:
         self.tail_values = set()   # var ids produced by the tails
         self.input_ids = set()     # var ids read from outside the group
         self.inputs: List[tuple] = []  # (var, kind) in slot order
+        self.consts: Dict[int, float] = {}  # var id -> value of a one-element constant taken as a literal
         self.outputs: List = []        # vars written to memory
         self.handle = None
 
@@ -282,6 +284,18 @@ def plan(jaxpr: Jaxpr, keep_for_vjp: bool) -> Plan:
                 if v.id not in g.values and v.id not in seen:
                     seen[v.id] = (v, bcast_kind(v.shape, g.shape))
         g.inputs = list(seen.values())
+        # one-element floating constants of the Jaxpr (Numpy.where's 1, clip's
+        # bounds, ...) become literals of the generated kernel, as long as the
+        # group keeps an input to read
+        lit = {}
+        for v, k in g.inputs:
+            c = jaxpr.consts.get(v.id)
+            val = getattr(c, "_scalar", None) if isinstance(c, ConcreteNDArray) else None
+            if k == BCAST_SCALAR and val is not None and c.dtype() == v.dtype:
+                lit[v.id] = val
+        if lit and len(lit) < len(g.inputs):
+            g.consts = lit
+            g.inputs = [(v, k) for v, k in g.inputs if v.id not in lit]
     # drop groups that write nothing (all dead) by turning them into no-ops
     return Plan(steps, groups)
 
@@ -294,7 +308,10 @@ def _program(g: Group):
     def operand(v):
         if v.id in index:
             return index[v.id]
-        insns.append((OP_INPUT, v.dtype.ordinal, slot[v.id], -1, 0.0))
+        if v.id in g.consts:
+            insns.append((OP_CONST, v.dtype.ordinal, -1, -1, g.consts[v.id]))
+        else:
+            insns.append((OP_INPUT, v.dtype.ordinal, slot[v.id], -1, 0.0))
         index[v.id] = len(insns) - 1
         return index[v.id]
 

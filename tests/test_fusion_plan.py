@@ -241,3 +241,48 @@ def test_deferred_values_refuse_what_a_kernel_cannot_broadcast():
     assert lazy.row_sum(a, Shape(16)) is None             # a column sum: not a last-axis tail
     assert lazy.row_sum(a, Shape(8)).meta.keepDims is False
     assert lazy.row_sum(a, Shape(8, 1)).meta.keepDims is True
+
+
+def _host_scalar(v):
+    """A one-element constant as ConcreteNDArray.full makes it (value kept on
+    the host), without a device."""
+    import numpy as np
+    import torch
+    from jax4j_b200.core import ConcreteNDArray, Device
+    a = ConcreteNDArray._wrap(torch.tensor([v], dtype=torch.float32), Shape(1), DType.FLOAT32, Device.host())
+    a._scalar = float(np.float32(v))
+    return a
+
+
+def test_scalar_constants_become_literals_and_where_and_clip_specialise():
+    zero, lo, hi, one = _host_scalar(0.0), _host_scalar(-1.0), _host_scalar(1.0), _host_scalar(1.0)
+
+    def f(x, y):
+        # Numpy.where's equations (api.py Numpy.where; a device scalar there)
+        c = x.gt(zero).astype(DType.FLOAT32)
+        z = c.mul(x.tanh().mul(y.sigmoid())).add(one.sub(c).mul(y.relu().clip(lo, hi)))
+        return z.sum(-1, True), z.argmax(-1)
+
+    jp = G.make_jaxpr(f, Spec(16, 64), Spec(16, 64))
+    plan = fusion.plan(jp, keep_for_vjp=False)
+    assert len(plan.groups) == 1
+    g = plan.groups[0]
+    # x and y stay inputs; 0, -1, 1 and the blend's 1 are literals
+    assert [v.shape for v, _ in g.inputs] == [Shape(16, 64), Shape(16, 64)]
+    assert sorted(g.consts.values()) == [-1.0, 0.0, 1.0, 1.0]
+    src = fusion.group_source(g, compile=True)
+    assert "= j_where(v" in src                      # the blend as select + one multiply-add pair
+    assert "= j_max_nz(v" in src and "= j_min_nz(v" in src  # clip against non-zero literal bounds
+    assert "= j_tanh(v" in src and "= j_sigmoid(v" in src
+
+
+def test_zero_literal_keeps_java_max():
+    zero = _host_scalar(0.0)
+
+    def f(x):
+        return x.max(zero).min(zero)  # +0 / -0 pairs need Math.max / Math.min's rule
+
+    g = fusion.plan(G.make_jaxpr(f, Spec(4, 8)), keep_for_vjp=False).groups[0]
+    src = fusion.group_source(g, compile=True)
+    assert "= j_max_nz(v" not in src and "= j_min_nz(v" not in src
+    assert "= j_max(v" in src and "= j_min(v" in src

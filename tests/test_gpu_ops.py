@@ -92,6 +92,44 @@ def test_unary(J, op, n):
         assert_rel(got, ref, TOL_ELEMENTWISE, op)
 
 
+def test_tanh_sigmoid_per_element_error_bounds(J):
+    """The one-exponential tanh and sigmoid (jmath.cuh) against FP64, per
+    element, with the bounds derived beside them: tanh within 13 units of
+    2^-23 relative (1.6e-6) everywhere; sigmoid within (3.5 + 1.2|x|)
+    units while its value is normal, below 1.2e-38 in absolute terms past
+    x < -87.3; special values and signed zeros as the reference's
+    (float) Math.tanh / 1 / (1 + Math.exp(-x))."""
+    u = 2.0 ** -23
+    r = rng(9)
+    x = np.concatenate([np.linspace(-30, 30, 400001), r.standard_normal(200000) * 4,
+                        np.linspace(-0.3, 0.3, 100001), np.geomspace(1e-38, 1e-2, 4000),
+                        -np.geomspace(1e-38, 1e-2, 4000), np.linspace(-100, 100, 20001)]).astype(np.float32)
+    xd = x.astype(np.float64)
+    th = np.asarray(dev(J, x).tanh().toFloatArray(), np.float64)
+    ref_t = np.tanh(xd)
+    err_t = np.abs(th - ref_t) / np.maximum(np.abs(ref_t), 1e-300)
+    assert err_t.max() <= 13 * u, f"tanh: worst {err_t.max() / u:.2f} u at x = {x[np.argmax(err_t)]!r}"
+    sg = np.asarray(dev(J, x).sigmoid().toFloatArray(), np.float64)
+    with np.errstate(over="ignore"):
+        ref_s = 1.0 / (1.0 + np.exp(-xd))
+    normal = ref_s >= 2.0 ** -126
+    bound = (3.5 + 1.2 * np.abs(xd)) * u
+    err_s = np.abs(sg - ref_s) / np.maximum(ref_s, 1e-300)
+    assert np.all(err_s[normal] <= bound[normal]), \
+        f"sigmoid: worst {np.max(err_s[normal] / bound[normal]):.3f} of the bound at x = {x[normal][np.argmax(err_s[normal] / bound[normal])]!r}"
+    assert np.all(np.abs(sg - ref_s)[~normal] <= 2.0 ** -126)
+    sp = np.array([np.nan, np.inf, -np.inf, 0.0, -0.0, 1e-45, -1e-45, 44.5, -44.5, 88.0, -88.0], np.float32)
+    t = np.asarray(dev(J, sp).tanh().toFloatArray())
+    s_ = np.asarray(dev(J, sp).sigmoid().toFloatArray())
+    assert np.isnan(t[0]) and np.isnan(s_[0])
+    assert t[1] == 1.0 and t[2] == -1.0 and s_[1] == 1.0 and s_[2] == 0.0
+    assert t[3] == 0.0 and not np.signbit(t[3]) and t[4] == 0.0 and np.signbit(t[4])
+    assert s_[3] == 0.5 and s_[4] == 0.5
+    assert t[5] == np.float32(1e-45) and t[6] == np.float32(-1e-45)
+    assert t[7] == 1.0 and t[8] == -1.0 and t[9] == 1.0 and t[10] == -1.0
+    assert s_[9] == 1.0 and 0.0 <= s_[10] <= 2.0 ** -126
+
+
 CASTS = [("float32", "int32"), ("float32", "bool"), ("float32", "float64"), ("float32", "int64"),
          ("int32", "float32"), ("int32", "bool"), ("bool", "float32"), ("bool", "int32"),
          ("float64", "float32"), ("float64", "int32"), ("int64", "int32"), ("int64", "float32")]
