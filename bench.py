@@ -59,7 +59,8 @@ def parse():
     p.add_argument("--no-graph", action="store_true", help="time the eager step only (no CUDA graph)")
     p.add_argument("--no-secondary", action="store_true",
                    help="skip the configuration 0-3 measurements that ride along in the headline line")
-    p.add_argument("--workload", default="dp_step", choices=["dp_step", "gemm", "sweep", "cfg0", "cfg2", "collectives", "fft", "linalg"],
+    p.add_argument("--workload", default="dp_step", choices=["dp_step", "gemm", "sweep", "cfg0", "cfg2", "collectives", "psum_sgd", "fft",
+                                                   "linalg"],
                    help="dp_step is the headline; gemm/sweep are single-kernel measurements "
                         "used for profiling")
     p.add_argument("--m", type=int, default=8192)
@@ -174,8 +175,6 @@ def run_ours(args):
     t_loc = J.ConcreteNDArray._wrap(t_t, J.Shape(B, DIMS[-1]), J.DType.FLOAT32, dev)
 
     neg = J.ConcreteNDArray.scalar(-1.0)
-    inv_d = J.ConcreteNDArray.scalar(1.0 / D)
-    lr = J.ConcreteNDArray.scalar(LR)
     names = list(params)
 
     def loss(p, x, t):
@@ -187,9 +186,6 @@ def run_ours(args):
         logits = a.dot(c[f"w{L}"].value).add(c[f"b{L}"].value)
         return J.Nn.softmax(logits).log().mul(t).sum(-1).mean().mul(neg)
 
-    # SGD update, jitted: one fused kernel per parameter (w - g * (1/D) * lr)
-    sgd = J.JAX.jit(lambda w, g: w.sub(g.mul(inv_d).mul(lr)))
-
     def step_fn(xs_arr, ts_arr, *ps):
         """One training step as a function of its buffers:
         (x, one-hot targets, *params) -> [per-shard losses, *updated params]."""
@@ -198,9 +194,12 @@ def run_ours(args):
 
         def body(xs, ts):
             value, grads = J.JAX.valueAndGradTree(lambda tr: loss(tr, xs, ts))(J.PyTree.dictOf(p))
-            g = J.Lax.psumTree(grads).children
-            for k in names:  # psum-averaged gradient, SGD update
-                new[k] = sgd(p[k], g[k].value)
+            # psum-averaged gradient and SGD update, w - (psum(g) * (1/D)) * lr:
+            # fused over peer memory at N > 1 (j4c_psum_sgd), psumTree + one
+            # update kernel per parameter otherwise
+            upd = J.Lax.psumSgdTree(J.PyTree.dictOf(p), grads, 1.0 / D, LR).children
+            for k in names:
+                new[k] = upd[k].value
             return value
 
         if world > 1:
@@ -406,6 +405,7 @@ def run_ours(args):
         "data": "synthetic: seeded SplitMix64 streams (Random.normal/uniform), Glorot weights",
         "config": {"workload": WORKLOAD, "model": "mlp-1024-4096x3-1000-relu", "global_batch": D * B,
                    "per_gpu_batch": B, "parallelism": f"dp{D}",
+                   "gradient_update": update_path(D),
                    "l2": "working set (167 MB params + >400 MB activations) exceeds the 126 MB L2"},
         "roofline": {"bound": "tensor",
                      "kernel": "dot (FP32 via 3xFP16 split, power-of-two scaled)" if f16
@@ -1144,11 +1144,99 @@ def measure_collectives(args, sizes=None):
                                         "allgather (D*S/t)*(D-1)/D)"}}
 
 
+def measure_psum_sgd(args):
+    """The headline's gradient exchange alone: Lax.psumSgdTree over the
+    parameter tree of the 1024-4096x3-1000 MLP (167 MB of FLOAT32 per rank),
+    fused over peer memory (j4c_psum_sgd) against psumTree (NCCL, per
+    bucket) followed by one update kernel per parameter.  Each call is timed
+    on the device, not overlapped with anything; bus GB/s in NCCL's
+    all-reduce convention (2 (D - 1) / D x bytes / time).  Returns rank 0's
+    result."""
+    import numpy as np
+    import torch
+    import jax4j_b200 as J
+    from jax4j_b200 import api as A, psum_sgd
+    rank, world, devices = _spmd_setup()
+    D = len(devices)
+    if D == 1:
+        return None if rank else {"metric": "psumSgdTree bus GB/s", "n_gpus": 1,
+                                  "note": "the exchange moves no data on one device; measured at N >= 2"}
+    shapes = []
+    for i in range(1, len(DIMS)):
+        shapes += [(DIMS[i - 1], DIMS[i]), (DIMS[i],)]
+    r = np.random.default_rng(10 + rank)
+    params = J.PyTree.list(*[J.PyTree.leaf(J.ConcreteNDArray.of(np.zeros(sh, np.float32))) for sh in shapes])
+    grads = J.PyTree.list(*[J.PyTree.leaf(J.ConcreteNDArray.of(r.standard_normal(sh).astype(np.float32)))
+                            for sh in shapes])
+    nbytes = 4 * sum(int(np.prod(sh)) for sh in shapes)
+    one = J.LocalShard(J.ConcreteNDArray.of(np.zeros(4, np.float32)), D)
+    upd = A._sgd_update(1.0 / D, LR)
+
+    def fused(dummy):
+        J.Lax.psumSgdTree(params, grads, 1.0 / D, LR)
+        return dummy
+
+    def unfused(dummy):
+        g = J.PyTrees.flatten(J.Lax.psumTree(grads))
+        [upd(w, gg) for w, gg in zip(J.PyTrees.flatten(params), g)]
+        return dummy
+
+    pf, pu = J.JAX.pmap(fused, devices), J.JAX.pmap(unfused, devices)
+    steps = max(5, args.steps)
+
+    def graphed(fn):
+        # device time of one call: recorded as a CUDA graph after eager
+        # warm-up calls (peer buffers, communicators, kernels), then replayed
+        for _ in range(2):
+            fn(one)
+        torch.cuda.synchronize()
+        g = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(g):
+            fn(one)
+        ms = _timed(g.replay, steps, 3, world)
+        torch.cuda.synchronize()
+        del g
+        return ms
+
+    ms_f = graphed(pf) if psum_sgd.ENABLED else None
+    ms_u = graphed(pu)
+    if rank != 0:
+        return None
+    bus = lambda ms: nbytes / (ms / 1e3) * 2 * (D - 1) / D / 1e9
+    out = {"metric": "psumSgdTree bus GB/s", "value": bus(ms_f) if ms_f else None, "unit": "GB/s", "n_gpus": D,
+           "config": {"workload": f"gradient all-reduce + SGD update of the headline's 8 parameters "
+                                  f"({nbytes / 1e6:.0f} MB per rank), one call per step recorded as a CUDA "
+                                  "graph, not overlapped with compute"},
+           "fused_ms": ms_f, "nccl_then_update_ms": ms_u, "nccl_then_update_busbw_GBps": bus(ms_u),
+           "roofline": {"bound": "nvlink", "achieved": bus(ms_f) if ms_f else None, "peak": PEER_COPY_GBS,
+                        "unit": "GB/s", "frac": bus(ms_f) / PEER_COPY_GBS if ms_f else None,
+                        "peak_source": "measured NVLink peer copy per direction on this pool's B200s"}}
+    return out
+
+
+def run_psum_sgd(args):
+    r = measure_psum_sgd(args)
+    if r is not None:
+        print(json.dumps(r), flush=True)
+    _finish(int(os.environ.get("WORLD_SIZE", "1")))
+
+
 def run_collectives(args):
     r = measure_collectives(args)
     if r is not None:
         print(json.dumps(r), flush=True)
     _finish(int(os.environ.get("WORLD_SIZE", "1")))
+
+
+def update_path(D: int) -> str:
+    """Which path Lax.psumSgdTree takes for the headline's parameters."""
+    from jax4j_b200 import psum_sgd
+    if D == 1:
+        return "one elementwise update kernel per parameter (no collective at N = 1)"
+    if psum_sgd.ENABLED:
+        return ("gradient all-reduce fused with the SGD update over peer memory (j4c_psum_sgd), "
+                "bucketed and overlapped with the backward")
+    return "NCCL all-reduce per bucket (psumTree), then one update kernel per parameter"
 
 
 def measure_secondary(args) -> dict:
@@ -1182,6 +1270,8 @@ def main():
         run_cfg2(args)
     elif args.workload == "collectives":
         run_collectives(args)
+    elif args.workload == "psum_sgd":
+        run_psum_sgd(args)
     elif args.workload == "fft":
         run_fft(args)
     elif args.workload == "linalg":

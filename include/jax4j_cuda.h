@@ -595,6 +595,44 @@ J4C_API int j4c_comm_wait(j4c_comm comm, j4c_stream stream);
 J4C_API int j4c_psum_slots(int dtype, const void *const *slots, int nslots, void *out, int64_t n,
                    j4c_stream stream);
 
+/* ---- gradient all-reduce fused with the SGD update (one process per GPU) ----
+ * Replaces, for a data-parallel step, Lax.psum of every gradient
+ * (api/SharedCollective.java:44-54) followed by the elementwise update
+ * w - g * scale * lr on each parameter.  Buffers a peer must read live in
+ * peer buffers: device memory allocated with j4c_peer_alloc, whose handle
+ * (J4C_PEER_HANDLE_BYTES) the caller sends to every other rank, which maps it
+ * with j4c_peer_open (CUDA IPC; the ranks' GPUs must reach one another over
+ * NVLink).  j4c_peer_close unmaps a peer's buffer, j4c_peer_free releases
+ * one's own.  Peer buffers start zeroed. */
+#define J4C_PEER_HANDLE_BYTES 64
+J4C_API int j4c_peer_alloc(size_t bytes, void **ptr, void *handle, size_t handle_len);
+J4C_API int j4c_peer_open(const void *handle, size_t handle_len, void **ptr);
+J4C_API int j4c_peer_close(void *ptr);
+J4C_API int j4c_peer_free(void *ptr);
+/* Bytes of the flag block each rank keeps in a peer buffer (16-byte
+ * aligned, zeroed at allocation, one per group of ranks; a group's calls
+ * are issued in the same order on every rank, on one stream per rank). */
+J4C_API size_t j4c_psum_sgd_flag_bytes(void);
+/* One bucket of n floats (a multiple of 4, at least 4 per rank): grads[p],
+ * upd[p] and flags[p] are rank p's packed gradients, exchange buffer (n
+ * floats) and flag block, as mapped in this process (this rank's own
+ * pointers at index rank); all are HOST arrays of nranks device pointers,
+ * nranks <= 8.  This rank's parameters of the bucket are nsegs <= 16
+ * segments (params[i], seg_len[i] floats each, multiples of 4, 16-byte
+ * aligned) in bucket order.  stage is local scratch of n + 4 * nranks
+ * floats.  out (n floats) receives
+ *     w - ((sum over ranks p = 0..nranks-1, in order, of grads[p]) * scale) * lr
+ * for every element, the same bits on every rank: rank r reduces and updates
+ * the r-th slice (the peers' gradients of it copied over NVLink by the copy
+ * engines into stage), and gathers the other slices from the peers'
+ * exchange buffers the same way; no rank writes another rank's memory but
+ * its flag words.  Every cross-rank wait is bounded (j4c_set_wait_limit_ns):
+ * on expiry the waiting kernel records device status 0x7C05 and returns;
+ * the group is then unusable. */
+J4C_API int j4c_psum_sgd(const float *const *grads, const float *const *upd, uint32_t *const *flags, int nranks,
+                         int rank, int64_t n, int nsegs, const int64_t *seg_len, const float *const *params,
+                         float scale, float lr, float *stage, float *out, j4c_stream stream);
+
 #ifdef __cplusplus
 }
 #endif

@@ -201,6 +201,18 @@ public final class J4C {
     static final MethodHandle PSUM_SLOTS = h("j4c_psum_slots", FunctionDescriptor.of(
         JAVA_INT, JAVA_INT, ADDRESS, JAVA_INT, ADDRESS, JAVA_LONG, ADDRESS));
 
+    // ---- gradient all-reduce fused with the SGD update over peer memory (psum_sgd.cu) ----
+    static final MethodHandle PEER_ALLOC = h("j4c_peer_alloc", FunctionDescriptor.of(
+        JAVA_INT, JAVA_LONG, ADDRESS, ADDRESS, JAVA_LONG));
+    static final MethodHandle PEER_OPEN = h("j4c_peer_open", FunctionDescriptor.of(
+        JAVA_INT, ADDRESS, JAVA_LONG, ADDRESS));
+    static final MethodHandle PEER_CLOSE = h("j4c_peer_close", FunctionDescriptor.of(JAVA_INT, ADDRESS));
+    static final MethodHandle PEER_FREE = h("j4c_peer_free", FunctionDescriptor.of(JAVA_INT, ADDRESS));
+    static final MethodHandle PSUM_SGD_FLAG_BYTES = h("j4c_psum_sgd_flag_bytes", FunctionDescriptor.of(JAVA_LONG));
+    static final MethodHandle PSUM_SGD = h("j4c_psum_sgd", FunctionDescriptor.of(
+        JAVA_INT, ADDRESS, ADDRESS, ADDRESS, JAVA_INT, JAVA_INT, JAVA_LONG, JAVA_INT, ADDRESS, ADDRESS,
+        JAVA_FLOAT, JAVA_FLOAT, ADDRESS, ADDRESS, ADDRESS));
+
     /** The library's message for the last failed call on this thread. */
     public static String lastError() {
         try {

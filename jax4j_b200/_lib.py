@@ -117,9 +117,17 @@ SIGNATURES = {
     "j4c_reduce_scatter": [P, I32, P, P, I64, P],
     "j4c_comm_wait": [P, P],
     "j4c_psum_slots": [I32, C.POINTER(P), I32, P, I64, P],
+    "j4c_peer_alloc": [C.c_size_t, C.POINTER(P), P, C.c_size_t],
+    "j4c_peer_open": [P, C.c_size_t, C.POINTER(P)],
+    "j4c_peer_close": [P],
+    "j4c_peer_free": [P],
+    "j4c_psum_sgd_flag_bytes": [],
+    "j4c_psum_sgd": [C.POINTER(P), C.POINTER(P), C.POINTER(P), I32, I32, I64, I32, C.POINTER(I64), C.POINTER(P),
+                     C.c_float, C.c_float, P, P, P],
 }
 _RESTYPES = {"j4c_last_error": C.c_char_p, "j4c_dot_workspace_size": C.c_size_t,
-             "j4c_split_pitch": C.c_int64, "j4c_split_floats": C.c_int64}
+             "j4c_split_pitch": C.c_int64, "j4c_split_floats": C.c_int64,
+             "j4c_psum_sgd_flag_bytes": C.c_size_t}
 
 
 def lib() -> C.CDLL:

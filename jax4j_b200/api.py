@@ -366,6 +366,45 @@ class Lax:
         return PyTrees.unflatten(tree, out)
 
 
+    @staticmethod
+    def psumSgdTree(params: PyTree, grads: PyTree, scale: float, lr: float) -> PyTree:
+        """The SGD update of a data-parallel step with its gradient all-reduce:
+        every leaf w of `params` becomes w - ((psum(g) * scale) * lr) for the
+        matching leaf g of `grads` -- the reference's psum of the gradients
+        (api/Lax.java:184-186) followed by the elementwise update
+        w.sub(g.mul(scale).mul(lr)), e.g. scale = 1/D for the mean gradient.
+
+        In one-process-per-GPU runs with FLOAT32 leaves, the all-reduce and
+        the update are one pair of kernels per bucket over peer memory
+        (j4c_psum_sgd), overlapped with the rest of the backward like
+        psumTree's buckets; the sum over ranks is taken in rank order, so every
+        rank holds the same bits.  Elsewhere (one shard, shards sharing a
+        process, other dtypes) it is psumTree followed by the elementwise
+        update.  The new parameters are fresh arrays."""
+        pl, gl = PyTrees.flatten(params), PyTrees.flatten(grads)
+        if len(pl) != len(gl):
+            raise IllegalArgumentException(f"psumSgdTree: {len(pl)} parameters but {len(gl)} gradients")
+        for w, g in zip(pl, gl):
+            if w.shape() != g.shape() or w.dtype() != g.dtype():
+                raise IllegalArgumentException(f"psumSgdTree: parameter {w.shape()} {w.dtype()} does not match "
+                                               f"gradient {g.shape()} {g.dtype()}")
+        ctx = _pm.PmapContext.current()
+        from . import distributed, psum_sgd
+        st = distributed.state()
+        if (ctx is not None and ctx.numDevices > 1 and Tracer.current() is None and st is not None
+                and ctx.collective is st.collective and isinstance(st.collective, _pm.NcclCollective)
+                and all(isinstance(x, ConcreteNDArray) for x in pl + gl)
+                and psum_sgd.eligible(pl, gl, st.world_size)):
+            _pm.verify_signature(ctx, "psumSgdTree", pl[0].dtype(), [w.shape().size() for w in pl])
+            dev = pl[0].tensor().device
+            bucket = max(4, PSUM_BUCKET_BYTES // 4) if PSUM_BUCKET_BYTES > 0 else 1 << 62
+            return PyTrees.unflatten(params, psum_sgd.fused(ctx, st, pl, gl, float(scale), float(lr),
+                                                            _comm_stream(dev), bucket))
+        summed = PyTrees.flatten(Lax.psumTree(grads))
+        update = _sgd_update(float(scale), float(lr))
+        return PyTrees.unflatten(params, [update(w, g) for w, g in zip(pl, summed)])
+
+
 # Gradient all-reduce overlapped with the backward pass.  The backward records
 # a CUDA event on each gradient when it is complete; psumTree groups the leaves
 # into buckets (last leaves first, the order the backward completes them) and
@@ -381,6 +420,19 @@ def _comm_stream(device) -> "torch.cuda.Stream":
     if s is None:
         s = _comm_streams[device] = torch.cuda.Stream(device=device)
     return s
+
+
+_sgd_updates = {}
+
+
+def _sgd_update(scale: float, lr: float):
+    """w - ((g * scale) * lr) as one jitted elementwise chain (cached per
+    scale and lr, which become literals of the generated kernel)."""
+    f = _sgd_updates.get((scale, lr))
+    if f is None:
+        s_arr, lr_arr = ConcreteNDArray.scalar(scale), ConcreteNDArray.scalar(lr)
+        f = _sgd_updates[(scale, lr)] = JAX.jit(lambda w, g: w.sub(g.mul(s_arr).mul(lr_arr)))
+    return f
 
 
 def _psum_overlapped(ctx, leaves: List[ConcreteNDArray]) -> List[ConcreteNDArray]:

@@ -154,6 +154,9 @@ def shutdown() -> None:
     """Destroys the communicator and the process group."""
     global _state
     if _state is not None:
+        from . import psum_sgd
+        psum_sgd.close_all()  # peers' buffers unmapped while every rank is still here
+        barrier()
         if _state.comm:
             call("j4c_comm_destroy", _state.comm)
         _state = None

@@ -81,6 +81,77 @@ def main():
         gx = J.JAX.grad(lambda xx: J.JAX.pmap(loss, devices)(xx, tl).sum())(J.LocalShard(x, D))
         np.savez(args.out + f".rank{rank}", gx=gx.numpy(), x=x.numpy(), t=t,
                  **{k: params[k].numpy() for k in params})
+    elif args.scenario == "psum_sgd":
+        # Lax.psumSgdTree's fused path (peer memory) against psumTree + the
+        # elementwise update, over three steps; leaves sized to make several
+        # buckets, one of them cut by the 16-segment limit
+        import torch
+        from jax4j_b200 import api as A
+        old_bucket = A.PSUM_BUCKET_BYTES
+        A.PSUM_BUCKET_BYTES = 1 << 20
+        r = np.random.default_rng(100 + rank)
+        shapes = [(512, 384), (384,), (384, 260), (260,)] + [(4 * (k + 1),) for k in range(18)] + [(1024, 300)]
+        base = np.random.default_rng(7)
+        params = J.PyTree.list(*[J.PyTree.leaf(J.ConcreteNDArray.of(base.standard_normal(s).astype(np.float32)))
+                                 for s in shapes])
+        scale, lr = 1.0 / D, 0.05
+        p_fused, p_ref = params, params
+        for step in range(3):
+            grads = J.PyTree.list(*[J.PyTree.leaf(J.ConcreteNDArray.of(r.standard_normal(s).astype(np.float32)))
+                                    for s in shapes])
+            res = {}
+
+            def fused_body(dummy):
+                res["fused"] = J.Lax.psumSgdTree(p_fused, grads, scale, lr)
+                return dummy
+
+            def ref_body(dummy):
+                g = J.Lax.psumTree(grads)
+                upd = A._sgd_update(scale, lr)
+                res["ref"] = J.PyTrees.unflatten(p_ref, [upd(w, gg) for w, gg in zip(J.PyTrees.flatten(p_ref),
+                                                                                    J.PyTrees.flatten(g))])
+                return dummy
+
+            one = J.LocalShard(J.ConcreteNDArray.of(np.zeros(4, np.float32)), D)
+            J.JAX.pmap(fused_body, devices)(one)
+            J.JAX.pmap(ref_body, devices)(one)
+            p_fused, p_ref = res["fused"], res["ref"]
+        torch.cuda.synchronize()
+        fl = [x.numpy() for x in J.PyTrees.flatten(p_fused)]
+        rl = [x.numpy() for x in J.PyTrees.flatten(p_ref)]
+        import ctypes as C
+        from jax4j_b200 import _lib
+        code = C.c_int(0)
+        _lib.lib().j4c_device_status(C.byref(code))
+        np.savez(args.out + f".rank{rank}", status=code.value, **{f"f{i}": a for i, a in enumerate(fl)},
+                 **{f"r{i}": a for i, a in enumerate(rl)})
+        A.PSUM_BUCKET_BYTES = old_bucket
+    elif args.scenario == "psum_sgd_timeout":
+        # rank 0 runs the fused update alone with a 1 ms wait limit: its waits
+        # on rank 1's flags (which nothing sets) run out, the kernels record
+        # status 0x7C05 and return; rank 1 stays alive (its buffer stays
+        # mapped) and joins the host barrier afterwards
+        import ctypes as C
+        import torch
+        from jax4j_b200 import _lib, psum_sgd
+        shapes = [(256, 64), (64,)]
+        w = [J.ConcreteNDArray.of(np.ones(s, np.float32)) for s in shapes]
+        g = [J.ConcreteNDArray.of(np.ones(s, np.float32)) for s in shapes]
+        psum_sgd._plan_for(st, tuple(x.shape().size() for x in w), 1 << 30)  # both ranks map the buffers
+        distributed.barrier()
+        if rank == 0:
+            prev = C.c_uint64(0)
+            _lib.lib().j4c_set_wait_limit_ns(1000000, C.byref(prev))
+            from jax4j_b200 import api as A
+            ctx_stream = A._comm_stream(w[0].tensor().device)
+            out = psum_sgd.fused(None, st, w, g, 0.5, 0.1, ctx_stream, 1 << 30)
+            torch.cuda.synchronize()
+            _lib.lib().j4c_set_wait_limit_ns(prev.value, None)
+            code = C.c_int(0)
+            _lib.lib().j4c_device_status(C.byref(code))
+            with open(args.out, "w") as f:
+                f.write(str(code.value))
+        distributed.barrier()
     elif args.scenario == "leave":
         x = J.ConcreteNDArray.of(np.ones((D, 8), np.float32))
         J.JAX.pmap(lambda s: J.Lax.psum(s), devices)(x).toFloatArray()

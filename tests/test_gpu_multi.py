@@ -97,3 +97,34 @@ def test_rank_leaving_between_steps_is_reported_on_the_host(tmp_path):
     r = _torchrun("leave", out, {"J4C_HEARTBEAT_S": "5", "NCCL_NVLS_ENABLE": "0"})
     assert os.path.exists(out), r.stderr[-2000:]
     assert open(out).read().startswith("CollectiveError")
+
+
+@needs2
+def test_psum_sgd_tree_fused_over_peer_memory_equals_psum_then_update(tmp_path):
+    """Lax.psumSgdTree over two processes takes the fused path (the
+    gradients summed out of the peer's memory, the update applied to each
+    rank's slice, the slices gathered back) and, over three steps with three
+    buckets (one cut at 16 leaves), gives the same bits as psumTree followed
+    by the elementwise update: with two ranks the sum g0 + g1 is NCCL's too."""
+    out = str(tmp_path / "psgd")
+    r = _torchrun("psum_sgd", out)
+    assert r.returncode == 0, r.stderr[-2000:]
+    z = [np.load(out + f".rank{k}.npz") for k in range(2)]
+    for k in range(2):
+        assert int(z[k]["status"]) == 0
+        n = len([f for f in z[k].files if f.startswith("f")])
+        assert n == 23
+        for i in range(n):
+            np.testing.assert_array_equal(z[k][f"f{i}"], z[k][f"r{i}"], err_msg=f"rank {k} leaf {i}")
+            np.testing.assert_array_equal(z[k][f"f{i}"], z[0][f"f{i}"], err_msg=f"rank {k} leaf {i} vs rank 0")
+
+
+@needs2
+def test_psum_sgd_wait_runs_out_with_a_status(tmp_path):
+    """Rank 0 runs the fused update while rank 1 stays on the host: rank 0's
+    waits on flags that nothing sets run out after the 1 ms limit, and the
+    kernels record status 0x7C05 and return (no fault, no hang)."""
+    out = str(tmp_path / "ps_timeout.txt")
+    r = _torchrun("psum_sgd_timeout", out, {"NCCL_NVLS_ENABLE": "0"})
+    assert r.returncode == 0, r.stderr[-2000:]
+    assert int(open(out).read()) == 0x7C05
