@@ -195,8 +195,9 @@ def run_ours(args):
         def body(xs, ts):
             value, grads = J.JAX.valueAndGradTree(lambda tr: loss(tr, xs, ts))(J.PyTree.dictOf(p))
             # psum-averaged gradient and SGD update, w - (psum(g) * (1/D)) * lr:
-            # fused over peer memory at N > 1 (j4c_psum_sgd), psumTree + one
-            # update kernel per parameter otherwise
+            # psumTree (NCCL, bucketed, overlapped) + one update kernel per
+            # parameter, or with J4C_PSUM_SGD=1 the exchange fused with the
+            # update over peer memory (j4c_psum_sgd)
             upd = J.Lax.psumSgdTree(J.PyTree.dictOf(p), grads, 1.0 / D, LR).children
             for k in names:
                 new[k] = upd[k].value
@@ -1117,8 +1118,20 @@ def measure_collectives(args, sizes=None):
                        iters, 3, world)
         pm = J.JAX.pmap(lambda s: J.Lax.psum(s), devices)
         api_ms = _timed(lambda: pm(J.LocalShard(x, D)), max(3, iters // 10), 2, world)
+        # the same all-reduce recorded as a CUDA graph of 10 calls: device
+        # time without the host's per-call enqueue (as inside a recorded step)
+        g = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(g):
+            gs = torch.cuda.current_stream().cuda_stream
+            for _ in range(10):
+                _lib.call("j4c_psum", comm, 0, x.data_ptr(), out.data_ptr(), n, gs)
+        graph_ms = _timed(g.replay, max(3, iters // 10), 2, world) / 10
+        torch.cuda.synchronize()
+        del g
         rows.append({"bytes": size, "allreduce_ms": ar_ms,
                      "allreduce_busbw_GBps": size / (ar_ms / 1e3) * 2 * (D - 1) / D / 1e9,
+                     "allreduce_graph_ms": graph_ms,
+                     "allreduce_graph_busbw_GBps": size / (graph_ms / 1e3) * 2 * (D - 1) / D / 1e9,
                      "allgather_ms": ag_ms,
                      "allgather_busbw_GBps": size * D / (ag_ms / 1e3) * (D - 1) / D / 1e9,
                      "pmap_psum_ms": api_ms})
@@ -1198,8 +1211,14 @@ def measure_psum_sgd(args):
         del g
         return ms
 
-    ms_f = graphed(pf) if psum_sgd.ENABLED else None
-    ms_u = graphed(pu)
+    was = psum_sgd.ENABLED
+    try:
+        psum_sgd.ENABLED = True   # the fused exchange, whatever the default
+        ms_f = graphed(pf)
+        psum_sgd.ENABLED = False  # psumTree (NCCL) + update kernels
+        ms_u = graphed(pu)
+    finally:
+        psum_sgd.ENABLED = was
     if rank != 0:
         return None
     bus = lambda ms: nbytes / (ms / 1e3) * 2 * (D - 1) / D / 1e9

@@ -374,13 +374,14 @@ class Lax:
         (api/Lax.java:184-186) followed by the elementwise update
         w.sub(g.mul(scale).mul(lr)), e.g. scale = 1/D for the mean gradient.
 
-        In one-process-per-GPU runs with FLOAT32 leaves, the all-reduce and
-        the update are one pair of kernels per bucket over peer memory
-        (j4c_psum_sgd), overlapped with the rest of the backward like
+        With J4C_PSUM_SGD=1, in one-process-per-GPU runs with FLOAT32 leaves,
+        the all-reduce and the update are one j4c_psum_sgd call per bucket
+        over peer memory, overlapped with the rest of the backward like
         psumTree's buckets; the sum over ranks is taken in rank order, so every
-        rank holds the same bits.  Elsewhere (one shard, shards sharing a
-        process, other dtypes) it is psumTree followed by the elementwise
-        update.  The new parameters are fresh arrays."""
+        rank holds the same bits.  Otherwise (the default: NCCL measured as
+        fast or faster; one shard; shards sharing a process; other dtypes) it
+        is psumTree followed by the elementwise update.  The new parameters
+        are fresh arrays."""
         pl, gl = PyTrees.flatten(params), PyTrees.flatten(grads)
         if len(pl) != len(gl):
             raise IllegalArgumentException(f"psumSgdTree: {len(pl)} parameters but {len(gl)} gradients")

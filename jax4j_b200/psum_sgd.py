@@ -35,7 +35,10 @@ from .core import ConcreteNDArray, DType
 HANDLE_BYTES = 64          # J4C_PEER_HANDLE_BYTES
 MAX_RANKS, MAX_SEGS = 8, 16
 FLAG_AREA = 256            # bytes reserved for the flag block at the start of the buffer
-ENABLED = os.environ.get("J4C_PSUM_SGD", "1") != "0"
+# Off unless J4C_PSUM_SGD=1: measured on B200s, NCCL's all-reduce (NVLS from
+# 4 MB at 8 GPUs) plus one update kernel per parameter is as fast at 2 GPUs
+# and faster at 8, where the copy engines pull from 7 peers per bucket.
+ENABLED = os.environ.get("J4C_PSUM_SGD", "0") == "1"
 
 
 def plan_buckets(sizes: Sequence[int], bucket_floats: int, max_segs: int = MAX_SEGS) -> List[List[int]]:

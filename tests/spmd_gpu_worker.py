@@ -86,7 +86,8 @@ def main():
         # elementwise update, over three steps; leaves sized to make several
         # buckets, one of them cut by the 16-segment limit
         import torch
-        from jax4j_b200 import api as A
+        from jax4j_b200 import api as A, psum_sgd
+        assert psum_sgd.ENABLED, "run with J4C_PSUM_SGD=1"
         old_bucket = A.PSUM_BUCKET_BYTES
         A.PSUM_BUCKET_BYTES = 1 << 20
         r = np.random.default_rng(100 + rank)

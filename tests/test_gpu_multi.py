@@ -107,7 +107,7 @@ def test_psum_sgd_tree_fused_over_peer_memory_equals_psum_then_update(tmp_path):
     buckets (one cut at 16 leaves), gives the same bits as psumTree followed
     by the elementwise update: with two ranks the sum g0 + g1 is NCCL's too."""
     out = str(tmp_path / "psgd")
-    r = _torchrun("psum_sgd", out)
+    r = _torchrun("psum_sgd", out, {"J4C_PSUM_SGD": "1"})
     assert r.returncode == 0, r.stderr[-2000:]
     z = [np.load(out + f".rank{k}.npz") for k in range(2)]
     for k in range(2):
