@@ -119,7 +119,11 @@ struct Elt {
 // BK = 32-bit words per smem row of a stage: 32 (128-byte swizzle) or 16
 // (64-byte swizzle, half the bytes per stage, so twice the stages fit);
 // BKE = the K elements those bytes hold.
-template <int BN, int STAGES, int BK, bool F16 = false>
+// PAIR: a CTA pair (cluster of 2) computes a 256 x BN tile with
+// tcgen05.mma.cta_group::2: each CTA holds 128 rows of op(A) and BN / 2 rows
+// of op(B)^T in its shared memory and 128 rows x BN columns of the result in
+// its tensor memory, so each SM reads half of B's tile per MMA.
+template <int BN, int STAGES, int BK, bool F16 = false, bool PAIR = false>
 struct Cfg {
     static_assert(BK == 32 || BK == 16, "BK is 32 (SW128) or 16 (SW64)");
     static constexpr int BKE = BK * 4 / Elt<F16>::SIZE;
@@ -130,8 +134,10 @@ struct Cfg {
     // biases a partial sum toward zero by about 3.6e-8 per MMA it adds.
     static constexpr int CHUNK_KB = (F16 ? CHUNK_F16_FIRST : CHUNK_TF32_FIRST) / BKE;
     static constexpr int CHUNK2_KB = (F16 ? CHUNK_F16_REST : CHUNK_TF32_REST) / BKE;
+    static constexpr int TM = PAIR ? 2 * BM : BM;  // rows of an output tile
+    static constexpr int BROWS = PAIR ? BN / 2 : BN;  // rows of op(B)^T in one CTA's stage
     static constexpr int A_BYTES = BM * BK * 4;
-    static constexpr int B_BYTES = BN * BK * 4;
+    static constexpr int B_BYTES = BROWS * BK * 4;
     static constexpr int MN_BOX_BYTES = 128 * BKE;  // one MN-major column block (BKE rows x 128 B)
     static constexpr int STAGE_BYTES = 2 * A_BYTES + 2 * B_BYTES;
     static constexpr int TMEM_COLS = 2 * BN;  // two partial-sum buffers
@@ -246,6 +252,37 @@ __device__ __forceinline__ void tma_load_3d(uint32_t dst, const CUtensorMap *map
         : "memory");
 }
 
+// The CTA pair's TMA load: data into this CTA's shared memory, completion
+// bytes to the barrier at `bar`, a shared::cluster address (the pair
+// leader's barrier).  No multicast.
+__device__ __forceinline__ void tma_load_3d_pair(uint32_t dst, const CUtensorMap *map, int x, int y, int z,
+                                                 uint32_t bar) {
+    asm volatile(
+        "cp.async.bulk.tensor.3d.cta_group::2.shared::cluster.global.mbarrier::complete_tx::bytes"
+        " [%0], [%1, {%2, %3, %4}], [%5];" ::"r"(dst),
+        "l"(reinterpret_cast<uint64_t>(map)), "r"(x), "r"(y), "r"(z), "r"(bar)
+        : "memory");
+}
+__device__ __forceinline__ uint32_t cluster_ctarank() {
+    uint32_t r;
+    asm volatile("mov.u32 %0, %%cluster_ctarank;" : "=r"(r));
+    return r;
+}
+// The shared::cluster address of the same shared-memory offset in CTA `rank` of the cluster.
+__device__ __forceinline__ uint32_t mapa_shared(uint32_t addr, uint32_t rank) {
+    uint32_t r;
+    asm volatile("mapa.shared::cluster.u32 %0, %1, %2;" : "=r"(r) : "r"(addr), "r"(rank));
+    return r;
+}
+// Every thread of both CTAs of the pair: nothing is left to wait for here
+// (the pair's CTAs run together), so the hardware barrier cannot stall.
+__device__ __forceinline__ void cluster_sync() {
+    asm volatile("barrier.cluster.arrive.release.aligned;\n\tbarrier.cluster.wait.acquire.aligned;" ::: "memory");
+}
+__device__ __forceinline__ void mbar_arrive_cluster(uint32_t cluster_addr) {
+    asm volatile("mbarrier.arrive.release.cluster.shared::cluster.b64 _, [%0];" ::"r"(cluster_addr) : "memory");
+}
+
 __device__ __forceinline__ void tc_fence_before() {
     asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory");
 }
@@ -339,6 +376,38 @@ __device__ __forceinline__ float pow2f(int k) {
 
 __device__ __forceinline__ void mma_commit(uint32_t bar) {
     asm volatile("tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];" ::"r"(bar)
+                 : "memory");
+}
+
+// The pair's MMA (issued by the leader CTA for both) and its commits: to the
+// barrier at the same offset in both CTAs, or to the leader's alone.
+template <bool F16>
+__device__ __forceinline__ void mma_issue_pair(uint32_t d_tmem, uint64_t a, uint64_t b, uint32_t idesc,
+                                               uint32_t accumulate) {
+    if constexpr (F16) {
+        asm volatile(
+            "{\n\t.reg .pred p;\n\t"
+            "setp.ne.b32 p, %4, 0;\n\t"
+            "tcgen05.mma.cta_group::2.kind::f16 [%0], %1, %2, %3, p;\n\t}" ::"r"(d_tmem),
+            "l"(a), "l"(b), "r"(idesc), "r"(accumulate)
+            : "memory");
+    } else {
+        asm volatile(
+            "{\n\t.reg .pred p;\n\t"
+            "setp.ne.b32 p, %4, 0;\n\t"
+            "tcgen05.mma.cta_group::2.kind::tf32 [%0], %1, %2, %3, p;\n\t}" ::"r"(d_tmem),
+            "l"(a), "l"(b), "r"(idesc), "r"(accumulate)
+            : "memory");
+    }
+}
+__device__ __forceinline__ void mma_commit_pair_both(uint32_t bar) {
+    asm volatile(
+        "tcgen05.commit.cta_group::2.mbarrier::arrive::one.shared::cluster.multicast::cluster.b64 [%0], %1;" ::"r"(bar),
+        "h"((uint16_t)3)
+        : "memory");
+}
+__device__ __forceinline__ void mma_commit_pair_leader(uint32_t bar) {
+    asm volatile("tcgen05.commit.cta_group::2.mbarrier::arrive::one.shared::cluster.b64 [%0];" ::"r"(bar)
                  : "memory");
 }
 
@@ -480,22 +549,26 @@ __device__ void exact_tiles(const float *__restrict__ A, bool a_col, const float
 }
 
 // Loads one operand's hi or lo tile (ROWS of M or N, BKE of K) into smem.
-template <int ROWS, int BK, bool MN, bool F16>
+template <int ROWS, int BK, bool MN, bool F16, bool PAIR = false>
 __device__ __forceinline__ void load_operand(uint32_t dst, const CUtensorMap *map, int kx, int row0, int z,
                                              uint32_t bar) {
+    auto load = [&](uint32_t d, int x, int y) {
+        if constexpr (PAIR) tma_load_3d_pair(d, map, x, y, z, bar);
+        else tma_load_3d(d, map, x, y, z, bar);
+    };
     if constexpr (!MN) {
-        tma_load_3d(dst, map, kx, row0, z, bar);  // box {BKE, ROWS, 1} of a [batch][rows, K] array
+        load(dst, kx, row0);  // box {BKE, ROWS, 1} of a [batch][rows, K] array
     } else {
         constexpr int W = Elt<F16>::MNW, BOX = 128 * (BK * 4 / Elt<F16>::SIZE);
 #pragma unroll
         for (int i = 0; i < ROWS / W; i++)        // boxes {MNW, BKE, 1} of a [batch][K, rows] array
-            tma_load_3d(dst + i * BOX, map, row0 + i * W, kx, z, bar);
+            load(dst + i * BOX, row0 + i * W, kx);
     }
 }
 
 // F16: the 3xFP16 split (else 3xTF32).  ahdr / bhdr: the headers of the
 // operands' hi arrays, whose line words give the scales.
-template <int BN, int STAGES, int BK, bool A_MN, bool B_MN, bool F16>
+template <int BN, int STAGES, int BK, bool A_MN, bool B_MN, bool F16, bool PAIR>
 __global__ void __launch_bounds__(kThreads, 1)
 gemm_3xtf32_kernel(const __grid_constant__ CUtensorMap tAh, const __grid_constant__ CUtensorMap tAl,
                    const __grid_constant__ CUtensorMap tBh, const __grid_constant__ CUtensorMap tBl,
@@ -503,8 +576,9 @@ gemm_3xtf32_kernel(const __grid_constant__ CUtensorMap tAh, const __grid_constan
                    Epilogue ep, int batch, int a_batched, int b_batched, int *status, uint64_t wait_ns, int full_tiles,
                    int splits, float *__restrict__ part, int *__restrict__ arrivals,
                    const SplitHeader *__restrict__ ahdr, const SplitHeader *__restrict__ bhdr) {
-    using Q = Cfg<BN, STAGES, BK, F16>;
+    using Q = Cfg<BN, STAGES, BK, F16, PAIR>;
     constexpr int UMMA_K = Elt<F16>::UMMA_K;
+    constexpr int NPAIR = PAIR ? 2 : 1;
     // end of chunk n of a unit that starts at k-block kb0 and ends at end
     auto chunk_end = [](int kb0, int n, int end) { return min(end, kb0 + (n < 2 ? Q::CHUNK_KB : Q::CHUNK2_KB)); };
     {
@@ -531,7 +605,13 @@ gemm_3xtf32_kernel(const __grid_constant__ CUtensorMap tAh, const __grid_constan
     Ctl<STAGES> *ctl = reinterpret_cast<Ctl<STAGES> *>(smem + STAGES * Q::STAGE_BYTES);
     volatile int *abort = &ctl->abort;
     const int warp = threadIdx.x / 32, lane = threadIdx.x % 32;
-    const int num_m = (M + BM - 1) / BM, num_n = (N + BN - 1) / BN;
+    // A pair shares its work units: unit u goes to pair u mod (pairs); this
+    // CTA holds rows crank * 128.. of each tile and of B's tile rows.
+    const uint32_t crank = PAIR ? cluster_ctarank() : 0u;
+    const bool leader = crank == 0;
+    const int u0 = PAIR ? (int)(blockIdx.x >> 1) : (int)blockIdx.x;
+    const int ustep = PAIR ? (int)(gridDim.x >> 1) : (int)gridDim.x;
+    const int num_m = (M + Q::TM - 1) / Q::TM, num_n = (N + BN - 1) / BN;
     const int tiles_per_batch = num_m * num_n;
     const int num_tiles = tiles_per_batch * batch;  // batch entries one after another
     const int num_units = full_tiles + (num_tiles - full_tiles) * splits;
@@ -543,7 +623,7 @@ gemm_3xtf32_kernel(const __grid_constant__ CUtensorMap tAh, const __grid_constan
         }
         for (int b = 0; b < 2; b++) {
             mbar_init(smem_u32(&ctl->tfull[b]), 1);
-            mbar_init(smem_u32(&ctl->tempty[b]), kEpiWarps);
+            mbar_init(smem_u32(&ctl->tempty[b]), NPAIR * kEpiWarps);  // the leader's counts both CTAs' warps
         }
         mbar_init(smem_u32(&ctl->drain), 1);
         ctl->abort = 0;
@@ -551,14 +631,24 @@ gemm_3xtf32_kernel(const __grid_constant__ CUtensorMap tAh, const __grid_constan
         asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
     }
     if (warp == 1) {
-        asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(
-                         smem_u32(&ctl->tmem_base)),
-                     "r"(Q::TMEM_COLS)
-                     : "memory");
-        asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;" ::: "memory");
+        if constexpr (PAIR) {
+            // both CTAs' warp 1, the same destination offset
+            asm volatile("tcgen05.alloc.cta_group::2.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(
+                             smem_u32(&ctl->tmem_base)),
+                         "r"(Q::TMEM_COLS)
+                         : "memory");
+            asm volatile("tcgen05.relinquish_alloc_permit.cta_group::2.sync.aligned;" ::: "memory");
+        } else {
+            asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(
+                             smem_u32(&ctl->tmem_base)),
+                         "r"(Q::TMEM_COLS)
+                         : "memory");
+            asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;" ::: "memory");
+        }
     }
     tc_fence_before();
-    __syncthreads();
+    if constexpr (PAIR) cluster_sync();  // both CTAs' barriers exist before either signals the other's
+    else __syncthreads();
     tc_fence_after();
     const uint32_t tmem = ctl->tmem_base;
 
@@ -569,26 +659,31 @@ gemm_3xtf32_kernel(const __grid_constant__ CUtensorMap tAh, const __grid_constan
             uint32_t phase = 0;
             int issued = 0;
             bool ok = true;
-            for (int u = blockIdx.x; ok && u < num_units; u += gridDim.x) {
+            for (int u = u0; ok && u < num_units; u += ustep) {
                 const Unit w = unit_of(u, full_tiles, splits, num_kb);
                 const int t = w.tile;
                 int mt, nt;
                 const int bidx = t / tiles_per_batch;
                 tile_coords(t - bidx * tiles_per_batch, num_m, num_n, mt, nt);
                 const int za = a_batched ? bidx : 0, zb = b_batched ? bidx : 0;
+                const int arow = mt * Q::TM + (int)crank * BM, brow = nt * BN + (int)crank * Q::BROWS;
                 for (int kb = w.kb0; kb < w.kb1; kb++) {
                     if (!wait_bar(smem_u32(&ctl->empty[stage]), phase ^ 1, abort, status, true, wait_ns)) {
                         ok = false;
                         break;
                     }
                     const uint32_t sb = smem_u32(smem + stage * Q::STAGE_BYTES);
-                    const uint32_t fb = smem_u32(&ctl->full[stage]);
-                    mbar_expect_tx(fb, Q::STAGE_BYTES);
+                    // both CTAs' bytes complete the leader's full barrier, which
+                    // the leader alone arms with the pair's total
+                    const uint32_t fb_local = smem_u32(&ctl->full[stage]);
+                    const uint32_t fb = PAIR ? mapa_shared(fb_local, 0) : fb_local;
+                    if (leader) mbar_expect_tx(fb_local, NPAIR * Q::STAGE_BYTES);
                     const int kx = kb * Q::BKE;
-                    load_operand<BM, BK, A_MN, F16>(sb, &tAh, kx, mt * BM, za, fb);
-                    load_operand<BM, BK, A_MN, F16>(sb + Q::A_BYTES, &tAl, kx, mt * BM, za, fb);
-                    load_operand<BN, BK, B_MN, F16>(sb + 2 * Q::A_BYTES, &tBh, kx, nt * BN, zb, fb);
-                    load_operand<BN, BK, B_MN, F16>(sb + 2 * Q::A_BYTES + Q::B_BYTES, &tBl, kx, nt * BN, zb, fb);
+                    load_operand<BM, BK, A_MN, F16, PAIR>(sb, &tAh, kx, arow, za, fb);
+                    load_operand<BM, BK, A_MN, F16, PAIR>(sb + Q::A_BYTES, &tAl, kx, arow, za, fb);
+                    load_operand<Q::BROWS, BK, B_MN, F16, PAIR>(sb + 2 * Q::A_BYTES, &tBh, kx, brow, zb, fb);
+                    load_operand<Q::BROWS, BK, B_MN, F16, PAIR>(sb + 2 * Q::A_BYTES + Q::B_BYTES, &tBl, kx, brow, zb,
+                                                                fb);
                     issued++;
                     if (++stage == STAGES) {
                         stage = 0;
@@ -597,8 +692,10 @@ gemm_3xtf32_kernel(const __grid_constant__ CUtensorMap tAh, const __grid_constan
                 }
             }
             // Every load this thread issued must land before the CTA exits:
-            // wait (bounded, even when aborting) on the last STAGES slots.
-            for (int i = 0; i < STAGES && i < issued; i++) {
+            // wait (bounded, even when aborting) on the last STAGES slots.  In
+            // a pair the leader's full barriers count both CTAs' loads; the
+            // follower's land before the pair's final barrier.
+            for (int i = 0; leader && i < STAGES && i < issued; i++) {
                 if (--stage < 0) {
                     stage = STAGES - 1;
                     phase ^= 1;
@@ -608,13 +705,13 @@ gemm_3xtf32_kernel(const __grid_constant__ CUtensorMap tAh, const __grid_constan
         }
     } else if (warp == 1) {
         // ---------------- MMA issuer ----------------
-        if (lane == 0) {
-            constexpr uint32_t idesc = idesc_mma<F16>(BM, BN, A_MN, B_MN);
+        if (lane == 0 && leader) {
+            constexpr uint32_t idesc = idesc_mma<F16>(Q::TM, BN, A_MN, B_MN);
             int stage = 0;
             uint32_t phase = 0;
             int ci = 0;  // chunk counter across tiles: selects the TMEM buffer
             bool ok = true;
-            for (int u = blockIdx.x; ok && u < num_units; u += gridDim.x) {
+            for (int u = u0; ok && u < num_units; u += ustep) {
                 const Unit w = unit_of(u, full_tiles, splits, num_kb);
                 for (int kb0 = w.kb0, n = 0; ok && kb0 < w.kb1; kb0 = chunk_end(kb0, n, w.kb1), n++, ci++) {
                     const int buf = ci & 1;
@@ -645,22 +742,32 @@ gemm_3xtf32_kernel(const __grid_constant__ CUtensorMap tAh, const __grid_constan
                             const uint64_t al = A_MN ? smem_desc_mn<BK, F16>(sa_lo + oa) : smem_desc<BK>(sa_lo + oa);
                             const uint64_t bh = B_MN ? smem_desc_mn<BK, F16>(sb_hi + ob) : smem_desc<BK>(sb_hi + ob);
                             const uint64_t bl = B_MN ? smem_desc_mn<BK, F16>(sb_lo + ob) : smem_desc<BK>(sb_lo + ob);
-                            mma_issue<F16>(dcol, al, bh, idesc, (kb > kb0 || kk > 0) ? 1u : 0u);
-                            mma_issue<F16>(dcol, ah, bl, idesc, 1u);
-                            mma_issue<F16>(dcol, ah, bh, idesc, 1u);
+                            if constexpr (PAIR) {
+                                mma_issue_pair<F16>(dcol, al, bh, idesc, (kb > kb0 || kk > 0) ? 1u : 0u);
+                                mma_issue_pair<F16>(dcol, ah, bl, idesc, 1u);
+                                mma_issue_pair<F16>(dcol, ah, bh, idesc, 1u);
+                            } else {
+                                mma_issue<F16>(dcol, al, bh, idesc, (kb > kb0 || kk > 0) ? 1u : 0u);
+                                mma_issue<F16>(dcol, ah, bl, idesc, 1u);
+                                mma_issue<F16>(dcol, ah, bh, idesc, 1u);
+                            }
                         }
-                        mma_commit(smem_u32(&ctl->empty[stage]));
+                        if constexpr (PAIR) mma_commit_pair_both(smem_u32(&ctl->empty[stage]));
+                        else mma_commit(smem_u32(&ctl->empty[stage]));
                         if (++stage == STAGES) {
                             stage = 0;
                             phase ^= 1;
                         }
                     }
                     if (!ok) break;
-                    mma_commit(smem_u32(&ctl->tfull[buf]));
+                    if constexpr (PAIR) mma_commit_pair_both(smem_u32(&ctl->tfull[buf]));
+                    else mma_commit(smem_u32(&ctl->tfull[buf]));
                 }
             }
-            // All MMAs this thread issued complete before TMEM is released.
-            mma_commit(smem_u32(&ctl->drain));
+            // All MMAs this thread issued complete before TMEM is released (in
+            // a pair, before the pair's final barrier releases the follower).
+            if constexpr (PAIR) mma_commit_pair_leader(smem_u32(&ctl->drain));
+            else mma_commit(smem_u32(&ctl->drain));
             wait_bar(smem_u32(&ctl->drain), 0, abort, status, false);
         }
     } else {
@@ -672,7 +779,11 @@ gemm_3xtf32_kernel(const __grid_constant__ CUtensorMap tAh, const __grid_constan
         const uint32_t lane_off = (uint32_t)(q * 32) << 16;
         int ci = 0;
         bool ok = true;
-        for (int u = blockIdx.x; ok && u < num_units; u += gridDim.x) {
+        // the leader's tempty barrier counts both CTAs' epilogue warps
+        const uint32_t tempty_addr[2] = {
+            PAIR && !leader ? mapa_shared(smem_u32(&ctl->tempty[0]), 0) : smem_u32(&ctl->tempty[0]),
+            PAIR && !leader ? mapa_shared(smem_u32(&ctl->tempty[1]), 0) : smem_u32(&ctl->tempty[1])};
+        for (int u = u0; ok && u < num_units; u += ustep) {
             const Unit w = unit_of(u, full_tiles, splits, num_kb);
             const int t = w.tile;
             int mt, nt;
@@ -704,7 +815,10 @@ gemm_3xtf32_kernel(const __grid_constant__ CUtensorMap tAh, const __grid_constan
                 }
                 tc_fence_before();
                 __syncwarp();
-                if (lane == 0) mbar_arrive(smem_u32(&ctl->tempty[buf]));
+                if (lane == 0) {
+                    if (PAIR && !leader) mbar_arrive_cluster(tempty_addr[buf]);
+                    else mbar_arrive(tempty_addr[buf]);
+                }
             }
             if (!ok) break;
             if (w.part >= 0) {
@@ -715,28 +829,29 @@ gemm_3xtf32_kernel(const __grid_constant__ CUtensorMap tAh, const __grid_constan
                 // warp of the last part to arrive adds all partials in part order.
                 constexpr int RF = 32 * Q::COLS_PER_WARP;  // floats of one warp's region
                 const size_t tix = (size_t)(t - full_tiles);
-                float *mine = part + ((tix * splits + w.part) * kEpiWarps + ew) * (size_t)RF + lane;
+                float *mine = part + (((tix * splits + w.part) * NPAIR + crank) * kEpiWarps + ew) * (size_t)RF + lane;
 #pragma unroll
                 for (int j = 0; j < Q::COLS_PER_WARP; j++) mine[(size_t)j * 32] = acc[j];
                 __threadfence();
                 __syncwarp();
                 int before = 0;
-                if (lane == 0) before = atomicAdd(arrivals + tix * kEpiWarps + ew, 1);
+                if (lane == 0) before = atomicAdd(arrivals + (tix * NPAIR + crank) * kEpiWarps + ew, 1);
                 before = __shfl_sync(0xffffffffu, before, 0);
                 if (before != splits - 1) continue;  // a later part settles the region
                 __threadfence();
                 // every partial (this part's too) is read back through L2
-                const float *rp = part + (tix * splits * kEpiWarps + ew) * (size_t)RF + lane;
+                const float *rp = part + ((tix * splits * NPAIR + crank) * kEpiWarps + ew) * (size_t)RF + lane;
 #pragma unroll
                 for (int j = 0; j < Q::COLS_PER_WARP; j++) {
                     float v = __ldcg(rp + (size_t)j * 32);
 #pragma unroll
                     for (int p = 1; p < kMaxTailSplits; p++)
-                        if (p < splits) v = __fadd_rn(v, __ldcg(rp + (size_t)p * kEpiWarps * RF + (size_t)j * 32));
+                        if (p < splits)
+                            v = __fadd_rn(v, __ldcg(rp + (size_t)p * NPAIR * kEpiWarps * RF + (size_t)j * 32));
                     acc[j] = v;
                 }
             }
-            const int row = mt * BM + q * 32 + lane;
+            const int row = mt * Q::TM + (int)crank * BM + q * 32 + lane;
             const int col0 = nt * BN + cbase;
             const bool row_ok = row < M;
             // The accumulator of C[row][col] is in units of
@@ -897,12 +1012,20 @@ gemm_3xtf32_kernel(const __grid_constant__ CUtensorMap tAh, const __grid_constan
     }
 
     tc_fence_before();
-    __syncthreads();
+    // a pair: the leader's MMAs (which write the follower's tensor memory and
+    // read its shared memory) are drained, and neither CTA signals the other
+    // any more, before either releases its memory
+    if constexpr (PAIR) cluster_sync();
+    else __syncthreads();
     tc_fence_after();
     if (warp == 1) {
         __syncwarp();
-        asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem), "r"(Q::TMEM_COLS)
-                     : "memory");
+        if constexpr (PAIR)
+            asm volatile("tcgen05.dealloc.cta_group::2.sync.aligned.b32 %0, %1;" ::"r"(tmem), "r"(Q::TMEM_COLS)
+                         : "memory");
+        else
+            asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem), "r"(Q::TMEM_COLS)
+                         : "memory");
     }
 }
 
@@ -1405,39 +1528,42 @@ struct TailPlan {
     int splits;
 };
 
-static TailPlan tail_plan(int64_t tiles, int64_t num_kb, int64_t chunk_kb, int64_t sms) {
-    const int64_t full = tiles / sms * sms, rem = tiles - full;
+// slots: the work units that run at once (one per SM, one per pair of SMs).
+static TailPlan tail_plan(int64_t tiles, int64_t num_kb, int64_t chunk_kb, int64_t slots) {
+    const int64_t full = tiles / slots * slots, rem = tiles - full;
     if (rem == 0) return TailPlan{tiles, 1};
-    int64_t sp = std::min<int64_t>(kMaxTailSplits, sms / rem);
+    int64_t sp = std::min<int64_t>(kMaxTailSplits, slots / rem);
     while (sp > 1 && num_kb / sp < chunk_kb) sp--;
     return sp < 2 ? TailPlan{tiles, 1} : TailPlan{full, (int)sp};
 }
 
-// Scratch of a tail split: the parts' FP32 partial tiles, then one arrival
-// counter per (split tile, epilogue warp).
-static size_t tail_scratch_bytes(int64_t tiles, const TailPlan &p, int bn) {
+// Scratch of a tail split: the parts' FP32 partial tiles (tm x bn each), then
+// one arrival counter per (split tile, CTA of the tile, epilogue warp).
+static size_t tail_scratch_bytes(int64_t tiles, const TailPlan &p, int tm, int bn) {
     if (p.splits < 2) return 0;
     const int64_t rem = tiles - p.full_tiles;
-    return (size_t)(rem * p.splits * BM * bn) * sizeof(float) + (size_t)(rem * kEpiWarps) * sizeof(int);
+    return (size_t)(rem * p.splits * tm * bn) * sizeof(float) + (size_t)(rem * (tm / BM) * kEpiWarps) * sizeof(int);
 }
 
 // An upper bound of tail_scratch_bytes for an [m, n] product in either
 // orientation (the K condition only lowers the number of parts).
 size_t tail_scratch_bound(int64_t m, int64_t n, int64_t batch) {
     size_t most = 0;
-    for (int o = 0; o < 2; o++) {
-        const int64_t tiles = ceil_div(o ? n : m, BM) * ceil_div(o ? m : n, 256) * batch;
-        most = std::max(most, tail_scratch_bytes(tiles, tail_plan(tiles, 1ll << 40, 1, sm_count()), 256));
-    }
+    for (int o = 0; o < 2; o++)
+        for (int tm : {BM, 2 * BM}) {
+            const int64_t tiles = ceil_div(o ? n : m, tm) * ceil_div(o ? m : n, 256) * batch;
+            const int64_t slots = tm == BM ? sm_count() : sm_count() / 2;
+            most = std::max(most, tail_scratch_bytes(tiles, tail_plan(tiles, 1ll << 40, 1, slots), tm, 256));
+        }
     return most;
 }
 
-template <int BN, int STAGES, int BK, bool A_MN, bool B_MN, bool F16>
+template <int BN, int STAGES, int BK, bool A_MN, bool B_MN, bool F16, bool PAIR>
 static int launch_gemm(const float *ah, const float *al, const float *bh, const float *bl, float *c,
                        int64_t M, int64_t N, int64_t K, bool store_t, const Epilogue &ep, int64_t batch,
                        bool a_bat, bool b_bat, void *tail_ws, cudaStream_t s) {
-    using Q = Cfg<BN, STAGES, BK, F16>;
-    auto kernel = gemm_3xtf32_kernel<BN, STAGES, BK, A_MN, B_MN, F16>;
+    using Q = Cfg<BN, STAGES, BK, F16, PAIR>;
+    auto kernel = gemm_3xtf32_kernel<BN, STAGES, BK, A_MN, B_MN, F16, PAIR>;
     static std::mutex mu;
     static std::vector<char> configured;
     int dev = 0;
@@ -1457,59 +1583,82 @@ static int launch_gemm(const float *ah, const float *al, const float *bh, const 
     const int64_t br = B_MN ? K : N, bc = B_MN ? N : K;
     const int64_t ab = a_bat ? batch : 1, bb = b_bat ? batch : 1;
     if ((rc = make_map(&mAh, ah, ar, ac, A_MN, BM, BK, ab)) || (rc = make_map(&mAl, al, ar, ac, A_MN, BM, BK, ab)) ||
-        (rc = make_map(&mBh, bh, br, bc, B_MN, BN, BK, bb)) || (rc = make_map(&mBl, bl, br, bc, B_MN, BN, BK, bb)))
+        (rc = make_map(&mBh, bh, br, bc, B_MN, Q::BROWS, BK, bb)) ||
+        (rc = make_map(&mBl, bl, br, bc, B_MN, Q::BROWS, BK, bb)))
         return rc;
     int *status = device_status_ptr();
     if (!status) return set_error(J4C_E_OOM, "no device status word");
-    const int64_t tiles = ceil_div(M, BM) * ceil_div(N, BN) * batch;
+    const int64_t tiles = ceil_div(M, Q::TM) * ceil_div(N, BN) * batch;
     if (tiles >= (1ll << 30)) return set_error(J4C_E_UNSUPPORTED, "dot: too many output tiles");
     const int64_t num_kb = ceil_div(K, Q::BKE);
-    const TailPlan tp = tail_plan(tiles, num_kb, Q::CHUNK_KB, sm_count());
+    const int64_t slots = PAIR ? sm_count() / 2 : sm_count();
+    const TailPlan tp = tail_plan(tiles, num_kb, Q::CHUNK_KB, slots);
     const int64_t units = tp.full_tiles + (tiles - tp.full_tiles) * tp.splits;
-    const int grid = (int)std::min<int64_t>(units, sm_count());
+    const int grid = (int)std::min<int64_t>(units, slots) * (PAIR ? 2 : 1);
     const int vec = (N % 4 == 0) && aligned16(c) && (!ep.bias || aligned16(ep.bias)) &&
                     (!ep.mask || aligned16(ep.mask)) && (!ep.act || aligned16(ep.act));
     float *part = nullptr;
     int *arrivals = nullptr;
     void *owned = nullptr;
     if (tp.splits > 1) {
-        const size_t bytes = tail_scratch_bytes(tiles, tp, BN);
+        const size_t bytes = tail_scratch_bytes(tiles, tp, Q::TM, BN);
         if (!tail_ws) {
             if ((rc = scratch_alloc(bytes, &owned, s))) return rc;
             tail_ws = owned;
         }
         part = static_cast<float *>(tail_ws);
-        arrivals = reinterpret_cast<int *>(part + (tiles - tp.full_tiles) * tp.splits * BM * BN);
-        J4C_CUDA(cudaMemsetAsync(arrivals, 0, (size_t)((tiles - tp.full_tiles) * kEpiWarps) * sizeof(int), s));
+        arrivals = reinterpret_cast<int *>(part + (tiles - tp.full_tiles) * tp.splits * Q::TM * BN);
+        J4C_CUDA(cudaMemsetAsync(arrivals, 0,
+                                 (size_t)((tiles - tp.full_tiles) * (Q::TM / BM) * kEpiWarps) * sizeof(int), s));
     }
     if (ep.out_lines) J4C_CUDA(cudaMemsetAsync(ep.out_lines, 0, (size_t)(M + N + 1) * sizeof(uint32_t), s));
     const SplitHeader *ahdr = split_header(ah, ar * ab, ac);
     const SplitHeader *bhdr = split_header(bh, br * bb, bc);
-    kernel<<<grid, kThreads, Q::SMEM_BYTES, s>>>(mAh, mAl, mBh, mBl, c, (int)M, (int)N, (int)K, (int)num_kb,
-                                                 store_t ? 0 : vec, store_t ? 1 : 0, ep, (int)batch, a_bat ? 1 : 0,
-                                                 b_bat ? 1 : 0, status, wait_limit_ns(), (int)tp.full_tiles, tp.splits,
-                                                 part, arrivals,
-                                                 ahdr, bhdr);
-    J4C_LAUNCH_CHECK("gemm_3xtf32_kernel");
+    if constexpr (PAIR) {
+        cudaLaunchConfig_t cfg = {};
+        cfg.gridDim = dim3((unsigned)grid);
+        cfg.blockDim = dim3(kThreads);
+        cfg.dynamicSmemBytes = Q::SMEM_BYTES;
+        cfg.stream = s;
+        cudaLaunchAttribute attr[1];
+        attr[0].id = cudaLaunchAttributeClusterDimension;
+        attr[0].val.clusterDim.x = 2;
+        attr[0].val.clusterDim.y = 1;
+        attr[0].val.clusterDim.z = 1;
+        cfg.attrs = attr;
+        cfg.numAttrs = 1;
+        const int mi = (int)M, ni = (int)N, ki = (int)K, kbi = (int)num_kb, vs = store_t ? 0 : vec,
+                  st = store_t ? 1 : 0, bt = (int)batch, abi = a_bat ? 1 : 0, bbi = b_bat ? 1 : 0,
+                  ft = (int)tp.full_tiles;
+        J4C_CUDA(cudaLaunchKernelEx(&cfg, kernel, mAh, mAl, mBh, mBl, c, mi, ni, ki, kbi, vs, st, ep, bt, abi, bbi,
+                                    status, wait_limit_ns(), ft, tp.splits, part, arrivals, ahdr, bhdr));
+        count_launch();
+    } else {
+        kernel<<<grid, kThreads, Q::SMEM_BYTES, s>>>(mAh, mAl, mBh, mBl, c, (int)M, (int)N, (int)K, (int)num_kb,
+                                                     store_t ? 0 : vec, store_t ? 1 : 0, ep, (int)batch,
+                                                     a_bat ? 1 : 0, b_bat ? 1 : 0, status, wait_limit_ns(),
+                                                     (int)tp.full_tiles, tp.splits, part, arrivals, ahdr, bhdr);
+        J4C_LAUNCH_CHECK("gemm_3xtf32_kernel");
+    }
     if (owned) return scratch_free(owned, s);
     return J4C_OK;
 }
 
-template <int BN, int STAGES, int BK, bool F16>
+template <int BN, int STAGES, int BK, bool F16, bool PAIR = false>
 static int launch_gemm_any(const float *ah, const float *al, const float *bh, const float *bl, float *c,
                            int64_t M, int64_t N, int64_t K, bool a_mn, bool b_mn, const Epilogue &ep,
                            int64_t batch, bool a_bat, bool b_bat, void *tail_ws, cudaStream_t s) {
     if (!a_mn && !b_mn)
-        return launch_gemm<BN, STAGES, BK, false, false, F16>(ah, al, bh, bl, c, M, N, K, false, ep, batch, a_bat, b_bat, tail_ws, s);
+        return launch_gemm<BN, STAGES, BK, false, false, F16, PAIR>(ah, al, bh, bl, c, M, N, K, false, ep, batch, a_bat, b_bat, tail_ws, s);
     if (a_mn && !b_mn)
-        return launch_gemm<BN, STAGES, BK, true, false, F16>(ah, al, bh, bl, c, M, N, K, false, ep, batch, a_bat, b_bat, tail_ws, s);
+        return launch_gemm<BN, STAGES, BK, true, false, F16, PAIR>(ah, al, bh, bl, c, M, N, K, false, ep, batch, a_bat, b_bat, tail_ws, s);
     // The wide (BN = 256) operand is read MN-major at a smem cost that
     // throttles the tensor pipe, so a K-major A with an MN-major B runs as
     // C^T = op(B)^T . op(A)^T: B's split becomes the (MN-major) A operand,
     // A's the (K-major) B operand, and the epilogue stores transposed.
     if (!a_mn && b_mn)
-        return launch_gemm<BN, STAGES, BK, true, false, F16>(bh, bl, ah, al, c, N, M, K, true, ep, batch, b_bat, a_bat, tail_ws, s);
-    return launch_gemm<BN, STAGES, BK, true, true, F16>(ah, al, bh, bl, c, M, N, K, false, ep, batch, a_bat, b_bat, tail_ws, s);
+        return launch_gemm<BN, STAGES, BK, true, false, F16, PAIR>(bh, bl, ah, al, c, N, M, K, true, ep, batch, b_bat, a_bat, tail_ws, s);
+    return launch_gemm<BN, STAGES, BK, true, true, F16, PAIR>(ah, al, bh, bl, c, M, N, K, false, ep, batch, a_bat, b_bat, tail_ws, s);
 }
 
 // rowmax[r] / colmax[c] (either may be NULL): the bits of the largest finite
@@ -1685,6 +1834,16 @@ static int gemm_presplit_ws(const float *ah, const float *al, const float *bh, c
     const tc::Epilogue ep{bias,      mask,     act, out_lines, (int)M, out_lines ? out_lines + M + N : nullptr,
                           mask_bits, act_bits, (int)ceil_div(N, 32)};
     const bool ab = a_batched != 0, bb = b_batched != 0;
+    // CTA pairs (256-row tiles, cta_group::2) for 3xFP16 products whose
+    // stored rows (the kernel's M: N when C is stored transposed) fill them
+    static const bool pair = [] {
+        const char *v = getenv("J4C_GEMM_PAIR");
+        return !(v && v[0] == '0');
+    }();
+    const int64_t kernel_m = (!a_mn && b_mn) ? N : M;
+    if (tc::split_fp16() && pair && kernel_m >= 2 * tc::BM)
+        return tc::launch_gemm_any<256, 6, 16, true, true>(ah, al, bh, bl, c, M, N, K, a_mn, b_mn, ep, batch, ab, bb,
+                                                           tail_ws, s);
     if (tc::split_fp16())
         return tc::launch_gemm_any<256, 4, 16, true>(ah, al, bh, bl, c, M, N, K, a_mn, b_mn, ep, batch, ab, bb, tail_ws, s);
     if (variant == 0)
