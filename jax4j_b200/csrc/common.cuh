@@ -116,7 +116,16 @@ __device__ __forceinline__ T java_min(T a, T b) {
 __device__ __forceinline__ float r_add(float a, float b) { return __fadd_rn(a, b); }
 __device__ __forceinline__ float r_sub(float a, float b) { return __fsub_rn(a, b); }
 __device__ __forceinline__ float r_mul(float a, float b) { return __fmul_rn(a, b); }
-__device__ __forceinline__ float r_div(float a, float b) { return __fdiv_rn(a, b); }
+// IEEE division.  A zero dividend over a non-zero, non-NaN divisor (an
+// infinity included) is a zero whose sign is the XOR of the operands' signs;
+// that case is answered directly (gradients through a division are mostly
+// zeros, e.g. a one-hot target's log-softmax VJP), everything else is the
+// correctly rounded quotient.
+__device__ __forceinline__ float r_div(float a, float b) {
+    if (a == 0.0f && b == b && b != 0.0f)
+        return __int_as_float((__float_as_int(a) ^ __float_as_int(b)) & (int)0x80000000);
+    return __fdiv_rn(a, b);
+}
 __device__ __forceinline__ double r_add(double a, double b) { return __dadd_rn(a, b); }
 __device__ __forceinline__ double r_sub(double a, double b) { return __dsub_rn(a, b); }
 __device__ __forceinline__ double r_mul(double a, double b) { return __dmul_rn(a, b); }

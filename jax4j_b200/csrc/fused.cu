@@ -61,7 +61,13 @@ struct Args { const void *in[16]; void *out[16]; void *tail[8]; };
 __device__ __forceinline__ float j_add(float a, float b) { return __fadd_rn(a, b); }
 __device__ __forceinline__ float j_sub(float a, float b) { return __fsub_rn(a, b); }
 __device__ __forceinline__ float j_mul(float a, float b) { return __fmul_rn(a, b); }
-__device__ __forceinline__ float j_div(float a, float b) { return __fdiv_rn(a, b); }
+// A zero dividend over a non-zero, non-NaN divisor: the signed zero IEEE
+// division defines, answered directly (as the eager kernels do).
+__device__ __forceinline__ float j_div(float a, float b) {
+    if (a == 0.0f && b == b && b != 0.0f)
+        return __int_as_float((__float_as_int(a) ^ __float_as_int(b)) & (int)0x80000000);
+    return __fdiv_rn(a, b);
+}
 __device__ __forceinline__ double j_add(double a, double b) { return __dadd_rn(a, b); }
 __device__ __forceinline__ double j_sub(double a, double b) { return __dsub_rn(a, b); }
 __device__ __forceinline__ double j_mul(double a, double b) { return __dmul_rn(a, b); }

@@ -23,6 +23,7 @@ Everything else runs equation by equation, as before.
 from __future__ import annotations
 
 import ctypes as C
+import os
 from typing import Dict, List, Optional
 
 import torch
@@ -339,7 +340,32 @@ def _c_program(g: Group):
     return prog, (arr, in_dt, in_bc, out_i, t_op, t_in)
 
 
+# J4C_FUSED_LOG=1 prints each group's program to stderr when it is compiled:
+# shape, inputs (broadcast kind), instructions, outputs and tails.
+FUSED_LOG = os.environ.get("J4C_FUSED_LOG", "0") == "1"
+_KINDS = {BCAST_FULL: "full", BCAST_ROW: "row", BCAST_COL: "col", BCAST_SCALAR: "scalar"}
+
+
+def describe(g: Group) -> str:
+    insns, outs, tail_ops, tail_insn = _program(g)
+    names = {int(p): p.name for p in P}
+    body = []
+    for i, (op, dt, a, b, val) in enumerate(insns):
+        if op == OP_INPUT:
+            v, k = g.inputs[a]
+            body.append(f"v{i}=in{a}[{_KINDS.get(k, k)}]")
+        elif op == OP_CONST:
+            body.append(f"v{i}={val:g}")
+        else:
+            body.append(f"v{i}={names.get(op, op)}(v{a}{', v%d' % b if b >= 0 else ''})")
+    tails = [f"{names.get(o, o)}(v{t})" for o, t in zip(tail_ops, tail_insn)]
+    return (f"fused group {g.shape}: {'; '.join(body)} | out {['v%d' % o for o in outs]} | tails {tails}")
+
+
 def compile_group(g: Group) -> None:
+    if FUSED_LOG:
+        import sys
+        print(describe(g), file=sys.stderr, flush=True)
     prog, _keep = _c_program(g)
     handle = C.c_void_p()
     _lib.check(_lib.lib().j4c_fused_compile(C.cast(C.pointer(prog), C.c_void_p), C.byref(handle)),

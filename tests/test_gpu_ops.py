@@ -52,8 +52,11 @@ def test_binary_bit_exact(J, op, sa, sb):
 
 
 def test_binary_java_special_values(J):
-    a = np.float32([np.nan, 1, -0.0, 0.0, np.inf, -np.inf, 3, 0])
-    b = np.float32([1, np.nan, 0.0, -0.0, np.inf, 2, 0, 0])
+    # zero dividends over every kind of divisor (division answers them directly)
+    a = np.float32([np.nan, 1, -0.0, 0.0, np.inf, -np.inf, 3, 0,
+                    0.0, -0.0, 0.0, -0.0, 0.0, -0.0, 0.0, -0.0, 0.0, -0.0])
+    b = np.float32([1, np.nan, 0.0, -0.0, np.inf, 2, 0, 0,
+                    3, 3, -3, -3, np.inf, -np.inf, 1e-45, -1e-45, np.nan, 3e38])
     for op in BIN:
         got = getattr(dev(J, a), op)(dev(J, b)).numpy()
         ref = orc.binary(getattr(orc, op.upper()), a, b)
