@@ -449,8 +449,9 @@ def run_ours(args):
 
 # DRAM bytes per GEMM launch of the batch-8192 step, from ncu captures of its
 # 11 GEMM launches (dram__bytes_read.sum + dram__bytes_write.sum, averaged),
-# per operand split kind.
-GEMM_DRAM_BYTES_PER_LAUNCH = {"tf32": 1.0663e9, "fp16": 5.573e8}
+# per operand split kind: 3xFP16 with CTA-pair tiles (the default), 3xTF32
+# with single-CTA tiles (profiles/dp_step_launches_mlp_b8192.md).
+GEMM_DRAM_BYTES_PER_LAUNCH = {"tf32": 1.0663e9, "fp16": 4.747e8}
 
 
 SUSTAINED_AFTER_S = 1.0  # timed regions at least this long are compared with the sustained peak
