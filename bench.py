@@ -59,8 +59,8 @@ def parse():
     p.add_argument("--no-graph", action="store_true", help="time the eager step only (no CUDA graph)")
     p.add_argument("--no-secondary", action="store_true",
                    help="skip the configuration 0-3 measurements that ride along in the headline line")
-    p.add_argument("--workload", default="dp_step", choices=["dp_step", "gemm", "sweep", "cfg0", "cfg2", "collectives", "psum_sgd", "fft",
-                                                   "linalg"],
+    p.add_argument("--workload", default="dp_step", choices=["dp_step", "gemm", "dot64", "sweep", "cfg0", "cfg2", "collectives", "psum_sgd",
+                                                   "fft", "linalg"],
                    help="dp_step is the headline; gemm/sweep are single-kernel measurements "
                         "used for profiling")
     p.add_argument("--m", type=int, default=8192)
@@ -564,6 +564,45 @@ def run_reference(args):
                                                                "thread"}},
             "e2e": {"value": value, "unit": "samples/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}
     print(json.dumps(line), flush=True)
+
+
+def run_dot64(args):
+    """One FLOAT64 dot C[M,N] = op(A)[M,K].op(B)[K,N] per step through j4c_dot
+    (the DMMA kernel; J4C_DOT64=simt selects the CUDA-core kernel), A and B
+    ~ U(-1, 1), inputs resident.  Reported against the B200's nominal dense
+    FP64 rate (no measured FP64 peak exists on this pool)."""
+    import torch
+    import jax4j_b200 as J
+    from jax4j_b200._lib import call
+    torch.cuda.set_device(0)
+    M, K, N = args.m, args.k, args.n
+    ta, tb = args.trans[0] == "t", args.trans[1] == "t"
+    g = torch.Generator(device="cuda").manual_seed(5)
+    A = torch.rand((K, M) if ta else (M, K), dtype=torch.float64, device="cuda", generator=g) * 2 - 1
+    B = torch.rand((N, K) if tb else (K, N), dtype=torch.float64, device="cuda", generator=g) * 2 - 1
+    out = torch.empty(M * N, dtype=torch.float64, device="cuda")
+    stream = torch.cuda.current_stream().cuda_stream
+    fn = lambda: call("j4c_dot", 1, A.data_ptr(), B.data_ptr(), out.data_ptr(), M, K, N, int(ta), int(tb), stream)
+    for _ in range(args.warmup):
+        fn()
+    torch.cuda.synchronize()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record()
+    for _ in range(args.steps):
+        fn()
+    e1.record()
+    torch.cuda.synchronize()
+    ms = e0.elapsed_time(e1) / args.steps
+    ref = (A.t() if ta else A) @ (B.t() if tb else B)
+    err = float((out.view(M, N) - ref).abs().max() / ref.abs().max())
+    tf = 2.0 * M * N * K / (ms / 1e3) / 1e12
+    kernel = "simt" if os.environ.get("J4C_DOT64", "").startswith("s") else "dmma"
+    print(json.dumps({"metric": "FLOAT64 dot TFLOP/s", "value": tf, "unit": "TFLOP/s", "ms_per_step": ms,
+                      "kernel": kernel, "max_rel_diff_vs_torch": err, "dtype": "f64",
+                      "config": {"workload": f"dot {M}x{K}x{N} op(A) op(B) = {args.trans}"},
+                      "roofline": {"bound": "fp64", "achieved": tf, "peak": 40.0, "unit": "TFLOP/s",
+                                   "frac": tf / 40.0, "peak_source": "nominal B200 dense FP64 (fallback)"}}),
+          flush=True)
 
 
 def run_gemm(args):
@@ -1282,6 +1321,8 @@ def main():
         run_reference(args)
     elif args.workload == "gemm":
         run_gemm(args)
+    elif args.workload == "dot64":
+        run_dot64(args)
     elif args.workload == "sweep":
         run_sweep(args)
     elif args.workload == "cfg0":

@@ -2,12 +2,15 @@
 // core/ConcreteNDArray.java:406-461; ExecutionBackend.matmul,
 // backend/ExecutionBackend.java:19).  Chooses the kernel for a shape/dtype.
 #include <algorithm>
+#include <cstdlib>
 
 #include "common.cuh"
 
 namespace j4c {
 int simt_gemm(int dtype, const void *a, const void *b, void *c, int64_t M, int64_t K, int64_t N,
               int trans_a, int trans_b, cudaStream_t s);
+int dmma_gemm(const double *a, const double *b, double *c, int64_t M, int64_t K, int64_t N, int trans_a,
+              int trans_b, cudaStream_t s);
 int tc_gemm_workspace(int64_t M, int64_t K, int64_t N, size_t *bytes);
 int64_t tc_split_floats(int64_t rows, int64_t cols);
 int64_t tc_split_pitch(int64_t cols);
@@ -55,6 +58,14 @@ int j4c_dot_ws(int dtype, const void *a, const void *b, void *c, int64_t M, int6
         return tc_gemm_f32((const float *)a, (const float *)b, (float *)c, M, K, N, trans_a,
                            trans_b, workspace, workspace_bytes, s);
     }
+    // FLOAT64 on the FP64 tensor path (DMMA) unless J4C_DOT64=simt asks for
+    // the CUDA-core kernel (kept for comparison)
+    static const bool simt64 = [] {
+        const char *v = getenv("J4C_DOT64");
+        return v && v[0] == 's';
+    }();
+    if (dtype == J4C_FLOAT64 && !simt64)
+        return dmma_gemm((const double *)a, (const double *)b, (double *)c, M, K, N, trans_a, trans_b, s);
     return simt_gemm(dtype, a, b, c, M, K, N, trans_a, trans_b, s);
 }
 

@@ -284,21 +284,35 @@ __global__ void __launch_bounds__(256) row_arg_kernel(const T *__restrict__ in, 
             const T *p = in + row * len;
             first_nan = p[0] != p[0];
             // VEC consecutive elements per step (one 16-byte load when VEC > 1;
-            // the launcher checks alignment and len % VEC); each lane still
-            // visits its elements in increasing index order.
-            for (int64_t j0 = (int64_t)sub * VEC; j0 < len; j0 += (int64_t)TPR * VEC) {
-                T v[VEC];
-                if constexpr (VEC == 4 && sizeof(T) == 4) {
-                    const float4 q = __ldg(reinterpret_cast<const float4 *>(p + j0));
-                    v[0] = q.x; v[1] = q.y; v[2] = q.z; v[3] = q.w;
-                } else {
-                    v[0] = p[j0];
+            // the launcher checks alignment and len % VEC), U steps' loads
+            // issued before any is compared (more bytes in flight per thread);
+            // each lane still visits its elements in increasing index order.
+            constexpr int U = 4;
+            constexpr int64_t STEP = (int64_t)TPR * VEC;
+            for (int64_t j00 = (int64_t)sub * VEC; j00 < len; j00 += U * STEP) {
+                T v[U][VEC];
+#pragma unroll
+                for (int u = 0; u < U; u++) {
+                    const int64_t j0 = j00 + u * STEP;
+                    if (j0 < len) {
+                        if constexpr (VEC == 4 && sizeof(T) == 4) {
+                            const float4 q = __ldg(reinterpret_cast<const float4 *>(p + j0));
+                            v[u][0] = q.x; v[u][1] = q.y; v[u][2] = q.z; v[u][3] = q.w;
+                        } else {
+                            v[u][0] = p[j0];
+                        }
+                    }
                 }
 #pragma unroll
-                for (int k = 0; k < VEC; k++) {
-                    if (v[k] == v[k] && arg_better<T, MAX>(v[k], (int32_t)(j0 + k), best, bi)) {
-                        best = v[k];
-                        bi = (int32_t)(j0 + k);
+                for (int u = 0; u < U; u++) {
+                    const int64_t j0 = j00 + u * STEP;
+                    if (j0 >= len) break;
+#pragma unroll
+                    for (int k = 0; k < VEC; k++) {
+                        if (v[u][k] == v[u][k] && arg_better<T, MAX>(v[u][k], (int32_t)(j0 + k), best, bi)) {
+                            best = v[u][k];
+                            bi = (int32_t)(j0 + k);
+                        }
                     }
                 }
             }
