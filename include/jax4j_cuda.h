@@ -363,6 +363,13 @@ J4C_API int j4c_split_f32_ex(const float *x, int64_t rows, int64_t cols, float *
  * columns) and its NaN/Inf flag in one pass, for several later
  * j4c_split_f32_ex calls. */
 J4C_API int j4c_split_lines(const float *x, int64_t rows, int64_t cols, uint32_t *lines, j4c_stream stream);
+/* The SGD update of a [rows, cols] FLOAT32 weight, out = w - ((g * scale) * lr)
+ * elementwise (the reference's update, w.sub(g.mul(scale).mul(lr)), bit for
+ * bit), with out's line words in lines (rows + cols + 1 words: row maxima,
+ * column maxima, NaN/Inf flag, as j4c_split_lines leaves them; zeroed by the
+ * call) so that out's next splits need no max pass.  out must not alias w or g. */
+J4C_API int j4c_sgd_update_lines(const float *w, const float *g, int64_t rows, int64_t cols, float scale, float lr,
+                                 float *out, uint32_t *lines, j4c_stream stream);
 J4C_API int j4c_dot_split(const float *a_hi, const float *a_lo, const float *b_hi, const float *b_lo, float *c,
                           int64_t M, int64_t K, int64_t N, int trans_a, int trans_b, j4c_stream stream);
 /* j4c_dot_split with elementwise work fused into the store of C [M, N] (each

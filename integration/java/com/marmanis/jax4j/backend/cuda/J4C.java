@@ -128,6 +128,8 @@ public final class J4C {
         ADDRESS));
     static final MethodHandle SPLIT_LINES = h("j4c_split_lines", FunctionDescriptor.of(
         JAVA_INT, ADDRESS, JAVA_LONG, JAVA_LONG, ADDRESS, ADDRESS));
+    static final MethodHandle SGD_UPDATE_LINES = h("j4c_sgd_update_lines", FunctionDescriptor.of(
+        JAVA_INT, ADDRESS, ADDRESS, JAVA_LONG, JAVA_LONG, JAVA_FLOAT, JAVA_FLOAT, ADDRESS, ADDRESS, ADDRESS));
     static final MethodHandle DOT_SPLIT = h("j4c_dot_split", FunctionDescriptor.of(
         JAVA_INT, ADDRESS, ADDRESS, ADDRESS, ADDRESS, ADDRESS, JAVA_LONG, JAVA_LONG, JAVA_LONG, JAVA_INT,
         JAVA_INT, ADDRESS));

@@ -117,6 +117,7 @@ SIGNATURES = {
     "j4c_reduce_scatter": [P, I32, P, P, I64, P],
     "j4c_comm_wait": [P, P],
     "j4c_psum_slots": [I32, C.POINTER(P), I32, P, I64, P],
+    "j4c_sgd_update_lines": [P, P, I64, I64, C.c_float, C.c_float, P, P, P],
     "j4c_peer_alloc": [C.c_size_t, C.POINTER(P), P, C.c_size_t],
     "j4c_peer_open": [P, C.c_size_t, C.POINTER(P)],
     "j4c_peer_close": [P],

@@ -403,7 +403,8 @@ class Lax:
                                                             _comm_stream(dev), bucket))
         summed = PyTrees.flatten(Lax.psumTree(grads))
         update = _sgd_update(float(scale), float(lr))
-        return PyTrees.unflatten(params, [update(w, g) for w, g in zip(pl, summed)])
+        return PyTrees.unflatten(params, [_sgd_leaf(w, g, float(scale), float(lr), update)
+                                          for w, g in zip(pl, summed)])
 
 
 # Gradient all-reduce overlapped with the backward pass.  The backward records
@@ -424,6 +425,30 @@ def _comm_stream(device) -> "torch.cuda.Stream":
 
 
 _sgd_updates = {}
+
+# Weights at least this large are updated by j4c_sgd_update_lines, which also
+# leaves the new weight's line maxima for its next splits (no max pass).
+SGD_LINES_MIN = 1 << 16
+
+
+def _sgd_leaf(w, g, scale: float, lr: float, update):
+    """One leaf's w - ((g * scale) * lr): a 2-D FLOAT32 weight on the GPU
+    through j4c_sgd_update_lines (the same bits as the elementwise chain, plus
+    the result's line maxima kept on it), anything else through `update`."""
+    if (isinstance(w, ConcreteNDArray) and isinstance(g, ConcreteNDArray) and Tracer.current() is None
+            and w.dtype() == DType.FLOAT32 and g.dtype() == DType.FLOAT32 and w.shape() == g.shape()
+            and w.shape().rank() == 2 and w.shape().size() >= SGD_LINES_MIN
+            and w.tensor().device.type == "cuda" and g.tensor().device == w.tensor().device):
+        rows, cols = w.shape().dimensions()
+        t = torch.empty(rows * cols, dtype=torch.float32, device=w.tensor().device)
+        lines = torch.empty(rows + cols + 1, dtype=torch.int32, device=t.device)
+        wt, gt = w.tensor().contiguous(), g.tensor().contiguous()
+        call("j4c_sgd_update_lines", wt.data_ptr(), gt.data_ptr(), rows, cols, C.c_float(scale), C.c_float(lr),
+             t.data_ptr(), lines.data_ptr(), w._stream())
+        out = ConcreteNDArray._wrap(t, w.shape(), DType.FLOAT32, w.device())
+        out._lines = lines
+        return out
+    return update(w, g)
 
 
 def _sgd_update(scale: float, lr: float):

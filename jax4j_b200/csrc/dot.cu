@@ -21,6 +21,8 @@ bool tc_gemm_supported(int64_t M, int64_t K, int64_t N);
 int tc_split_any(const float *x, int64_t rows, int64_t cols, float *hr, float *lr, float *hc, float *lc, float *ht,
                  float *lt, const uint32_t *lines_in, cudaStream_t s);
 int tc_split_lines(const float *x, int64_t rows, int64_t cols, uint32_t *lines, cudaStream_t s);
+int tc_sgd_update_lines(const float *w, const float *g, int64_t rows, int64_t cols, float scale, float lr, float *out,
+                        uint32_t *lines, cudaStream_t s);
 int tc_gemm_presplit(const float *ah, const float *al, const float *bh, const float *bl, float *c, int64_t M,
                      int64_t K, int64_t N, int trans_a, int trans_b, const float *bias, const float *mask,
                      float *act, int64_t batch, int a_batched, int b_batched, cudaStream_t s,
@@ -129,6 +131,12 @@ int j4c_split_lines(const float *x, int64_t rows, int64_t cols, uint32_t *lines,
     J4C_REQUIRE(rows >= 0 && cols >= 0, "j4c_split_lines: negative extent");
     J4C_REQUIRE(lines && (x || rows == 0 || cols == 0), "j4c_split_lines: NULL pointer");
     return tc_split_lines(x, rows, cols, lines, as_stream(stream));
+}
+
+int j4c_sgd_update_lines(const float *w, const float *g, int64_t rows, int64_t cols, float scale, float lr,
+                         float *out, uint32_t *lines, j4c_stream stream) {
+    if (rows == 0 || cols == 0) return J4C_OK;
+    return tc_sgd_update_lines(w, g, rows, cols, scale, lr, out, lines, as_stream(stream));
 }
 
 int j4c_dot_split_ep_bits(const float *a_hi, const float *a_lo, const float *b_hi, const float *b_lo, float *c,

@@ -1081,10 +1081,15 @@ __device__ __forceinline__ void flag_nonfinite(bool bad, SplitHeader *h0, SplitH
 // strip is reduced over the warp (redux.sync) and added with one atomic; a
 // column's over the unit's rows is kept in registers, reduced over the 8
 // warps in shared memory and added with one atomic per unit.
-template <bool ROWS, bool COLS>
+// SGD: src is a parameter w and each element first becomes
+// w - ((gsrc * scale) * lr), written to out; the maxima are those of the result
+// (the SGD update of a weight leaving the line words its next splits take).
+template <bool ROWS, bool COLS, bool SGD = false>
 __global__ void __launch_bounds__(256) lines_max_kernel(const float *__restrict__ src, int64_t R, int64_t C, int vec,
                                                         int64_t groups, uint32_t *__restrict__ rowmax,
-                                                        uint32_t *__restrict__ colmax, uint32_t *__restrict__ flag) {
+                                                        uint32_t *__restrict__ colmax, uint32_t *__restrict__ flag,
+                                                        const float *__restrict__ gsrc = nullptr, float scale = 0.0f,
+                                                        float lr = 0.0f, float *__restrict__ out = nullptr) {
     constexpr int TC = 512, RW = 4;
     __shared__ uint32_t cm[COLS ? 8 : 1][COLS ? TC : 1];
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
@@ -1108,10 +1113,32 @@ __global__ void __launch_bounds__(256) lines_max_kernel(const float *__restrict_
                     if (r < r_end && vec && c + 4 <= C) {
                         const uint4 u = __ldg(reinterpret_cast<const uint4 *>(p + c));
                         b[i][4 * qq] = u.x; b[i][4 * qq + 1] = u.y; b[i][4 * qq + 2] = u.z; b[i][4 * qq + 3] = u.w;
+                        if constexpr (SGD) {
+                            const float4 gv = __ldg(reinterpret_cast<const float4 *>(gsrc + r * C + c));
+                            const float gg[4] = {gv.x, gv.y, gv.z, gv.w};
+                            float o[4];
+#pragma unroll
+                            for (int e = 0; e < 4; e++) {
+                                o[e] = __fsub_rn(__uint_as_float(b[i][4 * qq + e]),
+                                                 __fmul_rn(__fmul_rn(gg[e], scale), lr));
+                                b[i][4 * qq + e] = __float_as_uint(o[e]);
+                            }
+                            *reinterpret_cast<float4 *>(out + r * C + c) = make_float4(o[0], o[1], o[2], o[3]);
+                        }
                     } else {
 #pragma unroll
-                        for (int e = 0; e < 4; e++)
-                            b[i][4 * qq + e] = (r < r_end && c + e < C) ? __float_as_uint(p[c + e]) : 0u;
+                        for (int e = 0; e < 4; e++) {
+                            const bool in = r < r_end && c + e < C;
+                            b[i][4 * qq + e] = in ? __float_as_uint(p[c + e]) : 0u;
+                            if constexpr (SGD) {
+                                if (in) {
+                                    const float o = __fsub_rn(__uint_as_float(b[i][4 * qq + e]),
+                                                              __fmul_rn(__fmul_rn(gsrc[r * C + c + e], scale), lr));
+                                    out[r * C + c + e] = o;
+                                    b[i][4 * qq + e] = __float_as_uint(o);
+                                }
+                            }
+                        }
                     }
                 }
             }
@@ -1685,6 +1712,25 @@ static int lines_max(const float *src, int64_t rows, int64_t cols, uint32_t *row
     return J4C_OK;
 }
 
+// out = w - ((g * scale) * lr) over W [rows, cols], with out's line words
+// (rows, columns, NaN/Inf flag) in lines, zeroed here: the SGD update of a
+// weight that leaves what its next splits take instead of a max pass.
+int sgd_update_lines(const float *w, const float *g, int64_t rows, int64_t cols, float scale, float lr, float *out,
+                     uint32_t *lines, cudaStream_t s) {
+    J4C_REQUIRE(w && g && out && lines, "j4c_sgd_update_lines: NULL argument");
+    J4C_REQUIRE(rows > 0 && cols > 0 && rows < (1ll << 31) && cols < (1ll << 31), "j4c_sgd_update_lines: bad extent");
+    J4C_CUDA(cudaMemsetAsync(lines, 0, (size_t)(rows + cols + 1) * sizeof(uint32_t), s));
+    const int vec = (cols % 4 == 0) && aligned16(w) && aligned16(g) && aligned16(out);
+    const int64_t strips = ceil_div(cols, 512);
+    const int64_t groups = std::max<int64_t>(1, std::min<int64_t>(ceil_div(rows, 32),
+                                                                  ceil_div((int64_t)sm_count() * 4, strips)));
+    const unsigned grid = (unsigned)std::min<int64_t>(strips * groups, (int64_t)sm_count() * 8);
+    lines_max_kernel<true, true, true><<<grid, 256, 0, s>>>(w, rows, cols, vec, groups, lines, lines + rows,
+                                                            lines + rows + cols, g, scale, lr, out);
+    J4C_LAUNCH_CHECK("lines_max_kernel (sgd)");
+    return J4C_OK;
+}
+
 // Any of the splits of X [rows, cols] in one pass over it:
 //   r: the stored layout with row lines (read K-major),
 //   c: the stored layout with column lines (read MN-major),
@@ -1802,6 +1848,11 @@ int tc_split_any(const float *x, int64_t rows, int64_t cols, float *hr, float *l
 // lines [rows + cols + 1]: X's row maxima, then its column maxima (bits of
 // the largest finite |x| of each line), then the NaN/Inf flag, as a GEMM
 // epilogue's out_lines.
+int tc_sgd_update_lines(const float *w, const float *g, int64_t rows, int64_t cols, float scale, float lr, float *out,
+                        uint32_t *lines, cudaStream_t s) {
+    return tc::sgd_update_lines(w, g, rows, cols, scale, lr, out, lines, s);
+}
+
 int tc_split_lines(const float *x, int64_t rows, int64_t cols, uint32_t *lines, cudaStream_t s) {
     J4C_CUDA(cudaMemsetAsync(lines, 0, (size_t)(rows + cols + 1) * sizeof(uint32_t), s));
     if (rows == 0 || cols == 0) return J4C_OK;

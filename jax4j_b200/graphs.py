@@ -48,12 +48,27 @@ class CapturedStep:
         # inputs are not updated).
         side = torch.cuda.Stream(device=dev)
         side.wait_stream(torch.cuda.current_stream(dev))
+        self._lines = {}  # input index -> static line-word buffer carried with a donated output's
         with torch.cuda.stream(side):
             for _ in range(max(1, warmup)):
-                self._check(self.fn(*self._fresh_inputs()))
+                warm = self._check(self.fn(*self._fresh_inputs()))
+        # A donated output that carries its line maxima (an SGD-updated weight)
+        # hands them to its input too: the recorded step's splits of that input
+        # then take them instead of a max pass.  They start as the max pass of
+        # the input's current contents.
+        for o, i in self.donate.items():
+            x = self.inputs[i]
+            if getattr(warm[o], "_lines", None) is not None and x.shape().rank() == 2:
+                rows, cols = x.shape().dimensions()
+                buf = torch.empty(rows + cols + 1, dtype=torch.int32, device=dev)
+                call("j4c_split_lines", x.data_ptr(), rows, cols, buf.data_ptr(), stream_of(dev.index))
+                self._lines[i] = buf
+        del warm
         torch.cuda.current_stream(dev).wait_stream(side)
         torch.cuda.synchronize(dev)
         self.graph = torch.cuda.CUDAGraph()
+        from ._lib import kernel_launches
+        k0 = kernel_launches()
         with torch.cuda.graph(self.graph):
             outs = self._check(self.fn(*self._fresh_inputs()))
             s = torch.cuda.current_stream(dev).cuda_stream
@@ -63,6 +78,12 @@ class CapturedStep:
                     raise ValueError(f"CapturedStep: output {o} does not match input {i}")
                 call("j4c_memcpy_d2d", dst.data_ptr(), src.data_ptr(),
                      dst.tensor().numel() * dst.tensor().element_size(), s)
+                if i in self._lines:
+                    if getattr(src, "_lines", None) is None:
+                        raise ValueError(f"CapturedStep: output {o} lost its line maxima during capture")
+                    call("j4c_memcpy_d2d", self._lines[i].data_ptr(), src._lines.data_ptr(),
+                         self._lines[i].numel() * 4, s)
+        self.kernels = kernel_launches() - k0  # this library's kernels recorded in the graph
         self.outputs: List[ConcreteNDArray] = outs
         self.device = dev
 
@@ -82,7 +103,10 @@ class CapturedStep:
     def _fresh_inputs(self) -> List[ConcreteNDArray]:
         # New wrappers around the static buffers: arrays are immutable and may
         # cache derived data (dot splits), while these buffers are refilled.
-        return [ConcreteNDArray._wrap(x.tensor(), x.shape(), x.dtype(), x.device()) for x in self.inputs]
+        out = [ConcreteNDArray._wrap(x.tensor(), x.shape(), x.dtype(), x.device()) for x in self.inputs]
+        for i, buf in getattr(self, "_lines", {}).items():
+            out[i]._lines = buf
+        return out
 
     def set_input(self, index: int, src: ConcreteNDArray, stream: Optional[int] = None) -> None:
         """Copies `src` into static input `index` (device to device) on `stream`
@@ -94,6 +118,9 @@ class CapturedStep:
             return
         s = stream if stream is not None else stream_of(self.device.index)
         call("j4c_memcpy_d2d", dst.data_ptr(), src.data_ptr(), dst.tensor().numel() * dst.tensor().element_size(), s)
+        if index in self._lines:  # the new contents' line maxima
+            rows, cols = dst.shape().dimensions()
+            call("j4c_split_lines", dst.data_ptr(), rows, cols, self._lines[index].data_ptr(), s)
 
     def __call__(self) -> List[ConcreteNDArray]:
         """Replays the step on the current stream.  In one-process-per-GPU

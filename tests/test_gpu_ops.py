@@ -274,6 +274,35 @@ def test_dot_f64_tensor_path(J, ta, tb, M, K, N):
     np.testing.assert_allclose(out.cpu().numpy().reshape(M, N), ref, rtol=1e-12, atol=1e-12 * max(1.0, np.sqrt(K)))
 
 
+@pytest.mark.parametrize("rows,cols,special", [(300, 1000, False), (517, 130, True), (64, 4097, False)])
+def test_sgd_update_lines_equals_update_then_max_pass(J, rows, cols, special):
+    """j4c_sgd_update_lines (psumSgdTree's update of a 2-D weight) gives the
+    elementwise chain's bits and the line words a max pass over the result
+    would, NaN/Inf flag included."""
+    import torch
+    from jax4j_b200 import api as A, _lib
+    r = rng(rows + cols)
+    w = r.standard_normal((rows, cols)).astype(np.float32)
+    g = (r.standard_normal((rows, cols)) * 10).astype(np.float32)
+    if special:
+        g[3, 5] = np.inf
+        w[7, 1] = np.nan
+    W, G = dev(J, w), dev(J, g)
+    old = A.SGD_LINES_MIN
+    try:
+        A.SGD_LINES_MIN = 1
+        got = A._sgd_leaf(W, G, 0.125, 0.01, A._sgd_update(0.125, 0.01))
+    finally:
+        A.SGD_LINES_MIN = old
+    ref = A._sgd_update(0.125, 0.01)(W, G)
+    np.testing.assert_array_equal(got.numpy().view(np.uint32), ref.numpy().view(np.uint32))
+    assert got._lines is not None
+    lines = torch.empty(rows + cols + 1, dtype=torch.int32, device="cuda")
+    _lib.call("j4c_split_lines", ref.data_ptr(), rows, cols, lines.data_ptr(), torch.cuda.current_stream().cuda_stream)
+    np.testing.assert_array_equal(got._lines.cpu().numpy(), lines.cpu().numpy())
+    assert bool(got._lines[-1].item()) == special
+
+
 def test_transpose(J):
     from jax4j_b200 import _lib
     import torch
