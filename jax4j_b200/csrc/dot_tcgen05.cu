@@ -1359,19 +1359,35 @@ __global__ void __launch_bounds__(256) split16_kernel(const float *__restrict__ 
     if (copy_c)
         for (int64_t i = t0; i < cols; i += stride) copy_c[i] = cmax[i];
     bool bad = false;
-    for (int64_t v = t0; v < n; v += stride) {
-        const int64_t r = v / q, k = (v - r * q) * 8;
-        float x[8];
-        const float *p = src + r * cols + k;
-        if (vec && k + 8 <= cols) {
-            const float4 t0v = __ldg(reinterpret_cast<const float4 *>(p));
-            const float4 t1v = __ldg(reinterpret_cast<const float4 *>(p) + 1);
-            x[0] = t0v.x; x[1] = t0v.y; x[2] = t0v.z; x[3] = t0v.w;
-            x[4] = t1v.x; x[5] = t1v.y; x[6] = t1v.z; x[7] = t1v.w;
-        } else {
+    // the column scales of a thread's 8 columns, kept while its columns stay
+    // the same (the grid stride is usually a multiple of a row's vectors)
+    int64_t sc_k = -1;
+    float csc[8];
+    // two vectors per thread per step, both loaded before either is split
+    for (int64_t v0 = t0; v0 < n; v0 += 2 * stride) {
+        float xx[2][8];
 #pragma unroll
-            for (int j = 0; j < 8; j++) x[j] = (k + j < cols) ? p[j] : 0.0f;
+        for (int u = 0; u < 2; u++) {
+            const int64_t v = v0 + u * stride;
+            if (v >= n) break;
+            const int64_t r = v / q, k = (v - r * q) * 8;
+            const float *p = src + r * cols + k;
+            if (vec && k + 8 <= cols) {
+                const float4 t0v = __ldg(reinterpret_cast<const float4 *>(p));
+                const float4 t1v = __ldg(reinterpret_cast<const float4 *>(p) + 1);
+                xx[u][0] = t0v.x; xx[u][1] = t0v.y; xx[u][2] = t0v.z; xx[u][3] = t0v.w;
+                xx[u][4] = t1v.x; xx[u][5] = t1v.y; xx[u][6] = t1v.z; xx[u][7] = t1v.w;
+            } else {
+#pragma unroll
+                for (int j = 0; j < 8; j++) xx[u][j] = (k + j < cols) ? p[j] : 0.0f;
+            }
         }
+#pragma unroll
+        for (int u = 0; u < 2; u++) {
+        const int64_t v = v0 + u * stride;
+        if (v >= n) break;
+        const int64_t r = v / q, k = (v - r * q) * 8;
+        float *x = xx[u];
 #pragma unroll
         for (int j = 0; j < 8; j++) x[j] = finite_or_zero(x[j], bad);
         if (hr) {
@@ -1383,14 +1399,18 @@ __global__ void __launch_bounds__(256) split16_kernel(const float *__restrict__ 
             *reinterpret_cast<uint4 *>(lr + r * pitch + k) = make_uint4(lw[0], lw[1], lw[2], lw[3]);
         }
         if (hc) {
-            float sc[8];
+            if (k != sc_k) {
 #pragma unroll
-            for (int j = 0; j < 8; j++) sc[j] = k + j < cols ? line_scale(cmax, k + j) : 1.0f;
+                for (int j = 0; j < 8; j++) csc[j] = k + j < cols ? line_scale(cmax, k + j) : 1.0f;
+                sc_k = k;
+            }
             uint32_t hw[4], lw[4];
 #pragma unroll
-            for (int j = 0; j < 4; j++) hw[j] = split2_f16(x[2 * j], x[2 * j + 1], sc[2 * j], sc[2 * j + 1], lw[j]);
+            for (int j = 0; j < 4; j++)
+                hw[j] = split2_f16(x[2 * j], x[2 * j + 1], csc[2 * j], csc[2 * j + 1], lw[j]);
             *reinterpret_cast<uint4 *>(hc + r * pitch + k) = make_uint4(hw[0], hw[1], hw[2], hw[3]);
             *reinterpret_cast<uint4 *>(lc + r * pitch + k) = make_uint4(lw[0], lw[1], lw[2], lw[3]);
+        }
         }
     }
     flag_nonfinite(bad, hdr_r, hdr_c, nf);
@@ -1422,20 +1442,28 @@ __global__ void __launch_bounds__(256) split16_t_kernel(const float *__restrict_
     const int64_t c0 = (blockIdx.x % tiles_c) * 64, r0 = (blockIdx.x / tiles_c) * 64;
     const int q = threadIdx.x & 15, w = threadIdx.x >> 4;
     bool bad = false;
+    // all four rows' loads in flight before any of them is used
+    float vv[4][4];
+#pragma unroll
+    for (int pass = 0; pass < 4; pass++) {
+        const int64_t r = r0 + pass * 16 + w, c = c0 + 4 * q;
+#pragma unroll
+        for (int k = 0; k < 4; k++) vv[pass][k] = 0.0f;
+        if (r < rows) {
+            if (vec_in && c + 4 <= cols) {
+                const float4 t = __ldg(reinterpret_cast<const float4 *>(src + r * cols + c));
+                vv[pass][0] = t.x; vv[pass][1] = t.y; vv[pass][2] = t.z; vv[pass][3] = t.w;
+            } else {
+#pragma unroll
+                for (int k = 0; k < 4; k++) vv[pass][k] = (c + k < cols) ? src[r * cols + c + k] : 0.0f;
+            }
+        }
+    }
 #pragma unroll
     for (int pass = 0; pass < 4; pass++) {
         const int i = pass * 16 + w;
         const int64_t r = r0 + i, c = c0 + 4 * q;
-        float v[4] = {0.0f, 0.0f, 0.0f, 0.0f};
-        if (r < rows) {
-            if (vec_in && c + 4 <= cols) {
-                const float4 t = __ldg(reinterpret_cast<const float4 *>(src + r * cols + c));
-                v[0] = t.x; v[1] = t.y; v[2] = t.z; v[3] = t.w;
-            } else {
-#pragma unroll
-                for (int k = 0; k < 4; k++) v[k] = (c + k < cols) ? src[r * cols + c + k] : 0.0f;
-            }
-        }
+        float *v = vv[pass];
 #pragma unroll
         for (int k = 0; k < 4; k++) {
             v[k] = finite_or_zero(v[k], bad);
