@@ -448,7 +448,7 @@ def run_ours(args):
 # DRAM bytes per GEMM launch of the batch-8192 step, from ncu captures of its
 # 11 GEMM launches (dram__bytes_read.sum + dram__bytes_write.sum, averaged),
 # per operand split kind: 3xFP16 with CTA-pair tiles (the default), 3xTF32
-# with single-CTA tiles (profiles/dp_step_launches_mlp_b8192.md).
+# with single-CTA tiles.
 GEMM_DRAM_BYTES_PER_LAUNCH = {"tf32": 1.0663e9, "fp16": 4.747e8}
 
 
