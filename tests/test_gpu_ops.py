@@ -805,14 +805,14 @@ def _with_specials(r, shape, kinds):
 
 @pytest.mark.parametrize("ta,tb", [(0, 0), (1, 0), (0, 1), (1, 1)])
 @pytest.mark.parametrize("where", ["a", "b", "both"])
-def test_dot_special_values_equal_the_reference(J, ta, tb, where):
+@pytest.mark.parametrize("M,K,N", [(150, 200, 170), (300, 96, 280)])  # single CTAs; CTA pairs (>= 256 rows)
+def test_dot_special_values_equal_the_reference(J, ta, tb, where, M, K, N):
     """An operand holding +-Inf or NaN: the product is the reference's
     sequential FP32 sum (core/ConcreteNDArray.java:452-459) bit for bit --
     Inf rows and columns, 0 * Inf = NaN, +Inf + -Inf = NaN, NaN spreading --
     in every layout, as the oracle computes it."""
     from jax4j_b200.core import _dot_raw
-    r = rng(ta * 4 + tb * 2 + len(where))
-    M, K, N = 150, 200, 170
+    r = rng(ta * 4 + tb * 2 + len(where) + M)
     A = _with_specials(r, (M, K), ["inf", "-inf", "nan"] if where in ("a", "both") else [])
     B = _with_specials(r, (K, N), ["-inf", "inf"] if where in ("b", "both") else [])
     a, b = dev(J, A.T.copy() if ta else A), dev(J, B.T.copy() if tb else B)
