@@ -118,3 +118,22 @@ def test_collective_replacement_mirrors_shared_collective():
     assert re.search(r"public float\[\] psum\(int deviceIndex, float\[\] data\)", src)
     assert re.search(r"public DeviceStorage allGather\(int deviceIndex, DeviceStorage shard\)", src)
     assert "barrier.await(timeoutMs" in src  # bounded, unlike CyclicBarrier.await()
+
+
+def test_fused_program_struct_offsets_match_the_c_layout():
+    """CudaFusedProgram writes j4c_insn / j4c_program at the offsets the C
+    struct has (natural alignment: the ctypes mirror in fusion.py, which
+    fused.cu's static_asserts pin to the header)."""
+    import ctypes
+    from jax4j_b200 import fusion
+    src = (JAVA / "CudaFusedProgram.java").read_text()
+    prog_sets = re.findall(r"prog\.set\((JAVA_INT|ADDRESS), (\d+),", src)
+    fields = [f for f, _ in fusion._Program._fields_]
+    want = [getattr(fusion._Program, f).offset for f in fields]
+    assert [int(o) for _, o in prog_sets] == want, (prog_sets, list(zip(fields, want)))
+    kinds = ["JAVA_INT" if t is ctypes.c_int32 else "ADDRESS" for _, t in fusion._Program._fields_]
+    assert [k for k, _ in prog_sets] == kinds
+    assert ctypes.sizeof(fusion._Program) == 80
+    insn_sets = re.findall(r"e\.set\((JAVA_INT|JAVA_DOUBLE), (\d+),", src)
+    assert [int(o) for _, o in insn_sets] == [getattr(fusion._Insn, f).offset for f, _ in fusion._Insn._fields_]
+    assert ctypes.sizeof(fusion._Insn) == 24
